@@ -1,0 +1,171 @@
+/*
+ * lfm3attn — B200 (sm_100a) KV-cache attention path for the LFM3-1.7B engine of
+ * jwyjohn/lfm3-1.7b-mi50, as a plain C ABI.
+ *
+ * The reference engine (Go, internal/model) drives its HIP kernels through internal/kfd
+ * dispatch packets with packed argument structs. This header is what its cgo shim binds in
+ * their place: every entry point takes raw device pointers and sizes the caller owns, never
+ * allocates, returns 0 or a negative LFM3A_E* code, and never throws. Each declaration names the
+ * reference interface it replaces (paths inside the reference project).
+ *
+ * Streams are cudaStream_t values passed as void* (NULL = the legacy default stream).
+ * fp16 data is IEEE binary16. All device buffers must be 16-byte aligned.
+ */
+#ifndef LFM3ATTN_H
+#define LFM3ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LFM3A_VERSION 1
+
+/* Return codes. */
+enum {
+  LFM3A_OK = 0,
+  LFM3A_EINVAL = -1,      /* bad argument: size, geometry, null or misaligned pointer */
+  LFM3A_ELAUNCH = -2,     /* a kernel launch was rejected */
+  LFM3A_ETIMEOUT = -3,    /* lfm3a_sync gave up waiting */
+  LFM3A_ECUDA = -4,       /* a CUDA runtime call failed; lfm3a_last_error() has the detail */
+  LFM3A_ENOTSUP = -5,     /* geometry or cache mode this entry point does not implement */
+  LFM3A_EWORKSPACE = -6,  /* the workspace is smaller than the *_workspace_bytes figure */
+  LFM3A_EDEVICE = -7      /* a kernel gave up a bounded wait and raised the device error word */
+};
+
+/* Cache modes. */
+enum {
+  /* B200 layout: per (block, kv head) a section holding K and V in fp16 and an int8 copy of V
+   * (per 64-token block absmax scale), each in the tensor-core operand tile order. */
+  LFM3A_MODE_F16 = 0,
+  /* The reference's int8 records: per (slot, kv head) K int8[D] | K scale f32 | V int8[D] |
+   * V scale f32 (kernels/ops.hip:226-251, internal/model/engine.go:28-32). */
+  LFM3A_MODE_I8REC = 1
+};
+
+/* Geometry and strides of one layer's paged pool. */
+typedef struct lfm3a_kv_layout {
+  int32_t mode;          /* LFM3A_MODE_* */
+  int32_t kv_heads;      /* 8 (benchmark geometry) or 4 (the reference model) */
+  int32_t head_dim;      /* 64 or 128 */
+  int32_t block_tokens;  /* tokens per block: 32, as engine.go:31 (BlockTokens) */
+  int64_t head_bytes;    /* MODE_F16: bytes of one (block, kv head) section; MODE_I8REC: record bytes */
+  int64_t block_bytes;   /* bytes of one block, all kv heads (engine.go:32 KVBlock for MODE_I8REC) */
+} lfm3a_kv_layout;
+
+/* One layer's pool as a kernel sees it; the counterpart of the kv / kv_block / kv_head / kv_slot /
+ * block_table / block_size fields of KvArgs (kernels/ops.hip:226-234) and Params
+ * (kernels/prefill_attn.hip:99-115). Block-table entries at or past pool_blocks are clamped. */
+typedef struct lfm3a_kv_view {
+  void* pool;                  /* device: this layer's block pool */
+  const int32_t* block_table;  /* device: logical block -> physical block (engine.go:682-685 SetBlock) */
+  int64_t pool_blocks;         /* physical blocks in the pool */
+  lfm3a_kv_layout layout;
+} lfm3a_kv_view;
+
+/* ---------------------------------------------------------------- housekeeping */
+int lfm3a_version(void);
+const char* lfm3a_strerror(int code);
+/* Detail of the last failure on the calling thread (a CUDA error string, the failed check). */
+const char* lfm3a_last_error(void);
+
+/* Fills *out for a mode and geometry (replaces the Rec/KVBlock constants, engine.go:28-32).
+ * block_tokens must be 32. */
+int lfm3a_kv_layout_init(int mode, int kv_heads, int head_dim, int block_tokens, lfm3a_kv_layout* out);
+
+/* Host: the cos | sin table per position, fp16 bits, [positions][head_dim]
+ * (internal/model/engine.go:428-461 buildRope; theta 1e6 factor 0.5 for full layers and theta 1e4
+ * factor 1 for sliding layers of the reference model, engine.go:333-338). */
+int lfm3a_rope_table(double theta, double factor, int head_dim, int positions, uint16_t* out_host);
+
+/* Waits for the stream with a limit (internal/kfd/queue.go:292-310 Wait, wrapped by
+ * internal/model/prefill.go:350-355 drain). Returns LFM3A_ETIMEOUT after timeout_ms, and
+ * LFM3A_EDEVICE (clearing the word) when a kernel gave up a bounded wait since the last call. */
+int lfm3a_sync(void* stream, int timeout_ms);
+
+/* ---------------------------------------------------------------- KV cache */
+/* Append n tokens at positions pos0 .. pos0 + n - 1 of one layer (kernels/ops.hip:236-251 kv_write,
+ * Go call internal/model/prefill.go:469-475; the verify-side append dspark.hip:1050-1060).
+ * k, v: device fp16, token t head h at k + t * token_stride + h * head_dim (token_stride 0 means
+ * kv_heads * head_dim; the reference reads them out of the fused projection with f_stride).
+ * rope: device fp16 table [positions][head_dim] (lfm3a_rope_table) applied to K at each position,
+ * or NULL. k_norm: device fp16 RMS-norm weights [head_dim] applied to K first (eps 1e-5), or NULL.
+ * MODE_F16 also re-quantises the int8 V of every 64-token block the append touches, over the
+ * tokens below pos0 + n. The block-table entries of all positions written must be in place. */
+int lfm3a_kv_append(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride, int pos0, int n,
+                    const void* rope, const void* k_norm, void* stream);
+
+/* Roll the cache back to new_len tokens after DSpark rejects drafts (the reference never writes
+ * rejected tokens and keeps the length in State.a, dspark.hip:2848-2895; here the drafts were
+ * appended, and bytes past the length are dead). MODE_F16 re-quantises the int8 V of the block that
+ * now ends the sequence so that it covers only live tokens. MODE_I8REC has no device work. */
+int lfm3a_kv_truncate(const lfm3a_kv_view* kv, int new_len, void* stream);
+
+/* Acceptance of one verify round on the device (dspark.hip:2848-2895): accepted = longest prefix with
+ * best[t] == tokens[t + 1], commit = accepted + 1. state[0] (the sequence length before the round's
+ * drafts) advances by commit; state[1] += accepted; state[2] += m; state[3] = commit. All device. */
+int lfm3a_accept(const int32_t* best, const int32_t* tokens, int m, int32_t* state, void* stream);
+
+/* ---------------------------------------------------------------- verify attention */
+/* Workspace for the split-KV partials of a verify call: m * q_heads * splits * (head_dim + 2) floats. */
+size_t lfm3a_verify_workspace_bytes(int m, int q_heads, int head_dim, int splits);
+
+/* The split count verify attention uses when called with splits <= 0. */
+int lfm3a_verify_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int window, int sm_count);
+
+/* DSpark verify attention of m tokens (dspark.hip:1809-2131 attention_v3 / verify_attention_paged and
+ * the combine, dspark.hip:2134-2185, launched by internal/model/dspark.go:541-621 draftLaunch).
+ * The m draft tokens' K/V must already be appended at ctx_len .. ctx_len + m - 1. Token t attends the
+ * context keys [start, ctx_len) (start = window > 0 ? ctx_len - window + 1 : 0, and kpos > qpos - window)
+ * and the drafts ctx_len .. ctx_len + t. q: device fp16 [m][q_heads][head_dim]. gate: device fp16
+ * [m][q_heads] logits (out *= sigmoid) or NULL. out: device fp16 [m][q_heads][head_dim].
+ * workspace: lfm3a_verify_workspace_bytes bytes when splits > 1 (may be NULL for one split).
+ * MODE_F16, head_dim 64, q_heads = 4 * kv_heads, 1 <= m <= 32. */
+int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
+                           const void* gate, void* out, void* workspace, size_t workspace_bytes, int splits,
+                           void* stream);
+
+/* The same pass over the keys a cache shard holds, for verify attention split across GPUs by sequence
+ * blocks: the cache holds positions [kv_begin, kv_end) of the sequence (its block table is indexed by
+ * global position); the queries sit at ctx_len + t as above, and the drafts count only where the shard
+ * holds them. partial: device f32 [m * q_heads][head_dim + 2] = this shard's log-sum-exp partial
+ * (acc relative to max, max in log2 units, sum), to be merged by lfm3a_combine with the other shards'
+ * (dspark.hip:2100-2120 partial rows, merged by combine_phase :2134-2185). */
+int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int kv_begin, int kv_end,
+                         int ctx_len, int window, float* partial, void* workspace, size_t workspace_bytes, int splits,
+                         void* stream);
+
+/* Log-sum-exp merge of split partials (dspark.hip:2134-2185 combine_phase; kernels/prefill_attn.hip:489-505).
+ * Partial s of row r: head_dim + 2 floats at partials + r * row_stride + s * split_stride = (unnormalised
+ * acc[head_dim], max (log2 units), sum); strides 0 mean [rows][splits][head_dim + 2]. out: device fp16
+ * [rows][head_dim] = gate-scaled sum_s 2^(m_s - M) acc_s / sum_s 2^(m_s - M) l_s. gate: device fp16 [rows]
+ * logits or NULL. Merges the partials of one GPU's splits and the partials gathered from several GPUs. */
+int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
+                  const void* gate, void* out, void* stream);
+
+/* ---------------------------------------------------------------- prefill attention */
+size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim);
+
+/* Causal (optionally sliding-window) prefill attention of tokens query tokens at positions
+ * context .. context + tokens - 1 over the cache [0, context + tokens) (kernels/prefill_attn.hip:373-486
+ * with combine :489-505, and kernels/prefill_attn_exact.hip:173-344 for exact != 0; Go call
+ * internal/model/prefill.go:476-511). The chunk's K/V must already be appended.
+ * exact = 0: u8 softmax probabilities per row and 64-key tile times the int8 V copy (tcgen05 kind::i8);
+ * exact = 1: fp16 probabilities times fp16 V (tcgen05 kind::f16). q, out: device fp16
+ * [tokens][q_heads][head_dim]. MODE_F16, head_dim 64, q_heads = 4 * kv_heads. */
+int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
+                            int exact, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- test hooks */
+/* The device u8 quantiser of softmax rows (kernels/prefill_attn.hip:305-331): for each row of 64 P'
+ * values, q = rne_sat_u8(P' * (255 / max(rowmax, 1e-30))), sc = rowmax * (1/255). p: device f32
+ * [rows][64]; q: device u8 [rows][64]; sc: device f32 [rows]. Same device function as the prefill kernel. */
+int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LFM3ATTN_H */

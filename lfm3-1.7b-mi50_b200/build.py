@@ -1,0 +1,50 @@
+"""Builds liblfm3attn.so in this directory from csrc/ for sm_100a (nvcc cross-compiles without a GPU)."""
+from __future__ import annotations
+
+import os
+import pathlib
+import subprocess
+import sys
+
+HERE = pathlib.Path(__file__).resolve().parent
+SRC = HERE / "csrc" / "lfm3attn.cu"
+OUT = HERE / "liblfm3attn.so"
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared",
+]
+
+
+def nvcc() -> str:
+    home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    path = pathlib.Path(home) / "bin" / "nvcc"
+    return str(path) if path.exists() else "nvcc"
+
+
+def needs_build() -> bool:
+    if not OUT.exists():
+        return True
+    newest = max(p.stat().st_mtime for p in (HERE / "csrc").iterdir())
+    header = HERE.parent / "include" / "lfm3attn.h"
+    newest = max(newest, header.stat().st_mtime)
+    return newest > OUT.stat().st_mtime
+
+
+def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
+    if force or needs_build():
+        cmd = [nvcc(), *NVCC_FLAGS, "-o", str(OUT), str(SRC)]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            sys.stderr.write(res.stdout + res.stderr)
+            raise RuntimeError(f"nvcc failed ({res.returncode})")
+        if verbose:
+            sys.stderr.write(res.stderr)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -1,0 +1,392 @@
+// The C ABI of include/lfm3attn.h: argument checks, launch geometry and error reporting around the
+// sm_100a kernels. One translation unit, so every kernel reaches the module's device error word.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <string>
+#include <thread>
+
+#include "../../include/lfm3attn.h"
+#include "common.cuh"
+#include "kv.cuh"
+#include "prefill.cuh"
+#include "verify.cuh"
+
+using namespace lfm3a;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& what) {
+  g_last_error = what;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return e == cudaErrorLaunchFailure || e == cudaErrorInvalidConfiguration || e == cudaErrorLaunchOutOfResources
+             ? LFM3A_ELAUNCH
+             : LFM3A_ECUDA;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, what);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int current_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+// Sets a kernel's dynamic shared-memory limit once per device.
+template <typename K>
+int ensure_smem(K kernel, int bytes, bool* done_per_device) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(LFM3A_EINVAL, "device index out of range");
+  if (!done_per_device[dev]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    done_per_device[dev] = true;
+  }
+  return LFM3A_OK;
+}
+
+int check_view(const lfm3a_kv_view* kv) {
+  if (!kv || !kv->pool || !kv->block_table) return fail(LFM3A_EINVAL, "null kv view, pool or block table");
+  if (kv->pool_blocks <= 0) return fail(LFM3A_EINVAL, "pool_blocks must be positive");
+  const lfm3a_kv_layout& L = kv->layout;
+  lfm3a_kv_layout want;
+  const int rc = lfm3a_kv_layout_init(L.mode, L.kv_heads, L.head_dim, L.block_tokens, &want);
+  if (rc != LFM3A_OK) return rc;
+  if (want.head_bytes != L.head_bytes || want.block_bytes != L.block_bytes)
+    return fail(LFM3A_EINVAL, "layout strides do not match lfm3a_kv_layout_init");
+  if (!aligned16(kv->pool)) return fail(LFM3A_EINVAL, "pool must be 16-byte aligned");
+  return LFM3A_OK;
+}
+
+KvGeom geom_of(const lfm3a_kv_view* kv) {
+  KvGeom g;
+  g.pool = static_cast<char*>(kv->pool);
+  g.table = kv->block_table;
+  g.pool_blocks = kv->pool_blocks;
+  g.block_bytes = kv->layout.block_bytes;
+  g.head_bytes = kv->layout.head_bytes;
+  g.kv_heads = kv->layout.kv_heads;
+  return g;
+}
+
+int launch_v8(const lfm3a_kv_view* kv, int qb0, int qb1, int len, cudaStream_t st) {
+  if (qb1 <= qb0) return LFM3A_OK;
+  V8Args a;
+  a.g = geom_of(kv);
+  a.qb0 = qb0;
+  a.len = len;
+  const dim3 grid(qb1 - qb0, kv->layout.kv_heads);
+  if (kv->layout.head_dim == 64) v8_quant_kernel<64><<<grid, 256, 0, st>>>(a);
+  else v8_quant_kernel<128><<<grid, 256, 0, st>>>(a);
+  return check_launch("v8_quant_kernel");
+}
+
+int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count) {
+  const int start = window > 0 ? std::max(0, ctx_len - window + 1) : 0;
+  const int p_total = (ctx_len + m - 1) / kBlockTokens - start / kBlockTokens + 1;
+  // Two resident blocks per SM, at least two pages per split.
+  int splits = (2 * sm_count + kv_heads - 1) / kv_heads;
+  splits = std::min(splits, std::max(1, p_total / 2));
+  return std::max(1, splits);
+}
+
+int launch_combine(const float* part, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
+                   const __half* gate, __half* out16, float* out32, cudaStream_t st) {
+  const int blocks = (rows + 3) / 4;
+  if (head_dim == 64)
+    combine_kernel<64><<<blocks, 128, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
+  else
+    combine_kernel<128><<<blocks, 128, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
+  return check_launch("combine_kernel");
+}
+
+// Shared body of lfm3a_verify_attention (out16 set) and lfm3a_verify_partial (out32 set).
+int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int kv_begin, int kv_end, int ctx_len,
+               int window, const void* gate, __half* out16, float* out32, void* workspace, size_t workspace_bytes,
+               int splits, cudaStream_t st) {
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  const lfm3a_kv_layout& L = kv->layout;
+  if (L.mode != LFM3A_MODE_F16 || L.head_dim != 64) return fail(LFM3A_ENOTSUP, "verify attention needs MODE_F16, head_dim 64");
+  if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "verify attention needs 4 query heads per kv head");
+  if (!q || (!out16 && !out32) || m < 1 || m > 32 || ctx_len < 0 || window < 0) return fail(LFM3A_EINVAL, "bad verify arguments");
+  if (kv_begin < 0 || kv_end <= kv_begin || kv_end > ctx_len + m) return fail(LFM3A_EINVAL, "bad key range");
+  if (!aligned16(q) || !aligned16(out16 ? (const void*)out16 : (const void*)out32)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
+  if (window > 0 && window < m) return fail(LFM3A_EINVAL, "window shorter than the verified tokens");
+  VerifyArgs a;
+  a.g = geom_of(kv);
+  a.q = static_cast<const __half*>(q);
+  a.gate = static_cast<const __half*>(gate);
+  a.out = out16;
+  a.m = m;
+  a.q_heads = q_heads;
+  a.ctx_len = ctx_len;
+  a.window = window;
+  a.start = std::max(kv_begin, window > 0 ? std::max(0, ctx_len - window + 1) : 0);
+  a.kv_end = kv_end;
+  // A shard wholly below the window start still runs its last page, with every key masked.
+  a.p_begin = std::min(a.start, kv_end - 1) / kBlockTokens;
+  a.p_total = (kv_end - 1) / kBlockTokens - a.p_begin + 1;
+  if (splits <= 0) splits = verify_splits_for(L.kv_heads, a.p_total * kBlockTokens, 1, 0, current_sm_count());
+  a.splits = std::min(splits, a.p_total);
+  a.qk_scale = 0.125f * kLog2e;
+  const int rows = m * q_heads;
+  // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
+  if (a.splits == 1 && out32) {
+    a.part = out32;
+  } else if (a.splits > 1) {
+    if (!workspace || !aligned16(workspace)) return fail(LFM3A_EINVAL, "verify needs a 16-byte aligned workspace");
+    if (workspace_bytes < lfm3a_verify_workspace_bytes(m, q_heads, 64, a.splits))
+      return fail(LFM3A_EWORKSPACE, "verify workspace too small");
+    a.part = static_cast<float*>(workspace);
+  } else {
+    a.part = nullptr;
+  }
+  const bool direct = a.splits == 1 && out16;
+  if (!direct) a.out = nullptr;
+  const dim3 grid(a.splits, L.kv_heads);
+  const int smem = kVerifyStages * kVerifyStageBytes + 2 * kVerifyStages * 8;
+  const int wpg = (m + 7) / 8;
+  static bool done[4][64];
+  switch (wpg) {
+#define LFM3A_VERIFY_CASE(W)                                               \
+  case W:                                                                  \
+    rc = ensure_smem(verify_kernel<W>, smem, done[W - 1]);                 \
+    if (rc != LFM3A_OK) return rc;                                         \
+    verify_kernel<W><<<grid, (2 * W + 1) * 32, smem, st>>>(a);             \
+    break;
+    LFM3A_VERIFY_CASE(1)
+    LFM3A_VERIFY_CASE(2)
+    LFM3A_VERIFY_CASE(3)
+    LFM3A_VERIFY_CASE(4)
+#undef LFM3A_VERIFY_CASE
+    default: return fail(LFM3A_EINVAL, "m out of range");
+  }
+  rc = check_launch("verify_kernel");
+  if (rc != LFM3A_OK || a.splits == 1) return rc;
+  return launch_combine(a.part, rows, a.splits, 64, kVerifyPart, (int64_t)a.splits * kVerifyPart,
+                        static_cast<const __half*>(gate), out16, out32, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lfm3a_version(void) { return LFM3A_VERSION; }
+
+const char* lfm3a_strerror(int code) {
+  switch (code) {
+    case LFM3A_OK: return "ok";
+    case LFM3A_EINVAL: return "invalid argument";
+    case LFM3A_ELAUNCH: return "kernel launch failed";
+    case LFM3A_ETIMEOUT: return "timed out";
+    case LFM3A_ECUDA: return "CUDA runtime error";
+    case LFM3A_ENOTSUP: return "not supported";
+    case LFM3A_EWORKSPACE: return "workspace too small";
+    case LFM3A_EDEVICE: return "a kernel gave up a bounded wait";
+    default: return "unknown error";
+  }
+}
+
+const char* lfm3a_last_error(void) { return g_last_error.c_str(); }
+
+int lfm3a_kv_layout_init(int mode, int kv_heads, int head_dim, int block_tokens, lfm3a_kv_layout* out) {
+  if (!out) return fail(LFM3A_EINVAL, "null layout");
+  if (block_tokens != kBlockTokens) return fail(LFM3A_ENOTSUP, "block_tokens must be 32");
+  if (head_dim != 64 && head_dim != 128) return fail(LFM3A_ENOTSUP, "head_dim must be 64 or 128");
+  if (kv_heads <= 0 || kv_heads > 64) return fail(LFM3A_EINVAL, "kv_heads out of range");
+  out->mode = mode;
+  out->kv_heads = kv_heads;
+  out->head_dim = head_dim;
+  out->block_tokens = block_tokens;
+  if (mode == LFM3A_MODE_F16) {
+    out->head_bytes = 160 * head_dim + 128;
+    out->block_bytes = out->head_bytes * kv_heads;
+  } else if (mode == LFM3A_MODE_I8REC) {
+    out->head_bytes = 2 * head_dim + 8;
+    out->block_bytes = out->head_bytes * kv_heads * block_tokens;
+  } else {
+    return fail(LFM3A_EINVAL, "unknown cache mode");
+  }
+  return LFM3A_OK;
+}
+
+int lfm3a_rope_table(double theta, double factor, int head_dim, int positions, uint16_t* out_host) {
+  if (!out_host || positions <= 0 || head_dim <= 0 || (head_dim & 1)) return fail(LFM3A_EINVAL, "bad rope table arguments");
+  const int half = head_dim / 2;
+  int angles = (int)(factor * head_dim) / 2;
+  angles = std::max(0, std::min(angles, half));
+  // Frequencies in fp32 as engine.go:432-436: inv[i] = 1 / float32(theta ^ float32(2i / D)).
+  float inv[512] = {0};
+  if (half > 512) return fail(LFM3A_EINVAL, "head_dim too large");
+  for (int i = 0; i < angles; ++i) {
+    const float e = (float)(2 * i) / (float)head_dim;
+    inv[i] = 1.f / (float)std::pow(theta, (double)e);
+  }
+  for (int p = 0; p < positions; ++p) {
+    const float t = (float)p;
+    uint16_t* row = out_host + (size_t)p * head_dim;
+    for (int i = 0; i < half; ++i) {
+      const double f = (double)(t * inv[i]);   // fp32 product, widened (engine.go:449)
+      const __half c = __float2half_rn((float)std::cos(f)), s = __float2half_rn((float)std::sin(f));
+      row[i] = *reinterpret_cast<const uint16_t*>(&c);
+      row[half + i] = *reinterpret_cast<const uint16_t*>(&s);
+    }
+  }
+  return LFM3A_OK;
+}
+
+int lfm3a_sync(void* stream, int timeout_ms) {
+  const cudaStream_t st = as_stream(stream);
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms < 0 ? 0 : timeout_ms);
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
+    if (std::chrono::steady_clock::now() > deadline) return fail(LFM3A_ETIMEOUT, "stream still busy at the deadline");
+    std::this_thread::yield();
+  }
+  int word = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&word, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  if (word != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return fail(LFM3A_EDEVICE, "device error word " + std::to_string(word));
+  }
+  return LFM3A_OK;
+}
+
+int lfm3a_kv_append(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride, int pos0, int n,
+                    const void* rope, const void* k_norm, void* stream) {
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  if (n == 0) return LFM3A_OK;
+  if (!k || !v || n < 0 || pos0 < 0) return fail(LFM3A_EINVAL, "bad append arguments");
+  const int D = kv->layout.head_dim, H = kv->layout.kv_heads;
+  if (token_stride == 0) token_stride = (int64_t)H * D;
+  if (token_stride < (int64_t)H * D) return fail(LFM3A_EINVAL, "token_stride smaller than kv_heads * head_dim");
+  AppendArgs a;
+  a.g = geom_of(kv);
+  a.k = static_cast<const __half*>(k);
+  a.v = static_cast<const __half*>(v);
+  a.rope = static_cast<const __half*>(rope);
+  a.knorm = static_cast<const __half*>(k_norm);
+  a.stride = token_stride;
+  a.pos0 = pos0;
+  a.n = n;
+  const cudaStream_t st = as_stream(stream);
+  const int blocks = (n * H + 3) / 4;
+  if (kv->layout.mode == LFM3A_MODE_F16) {
+    if (D == 64) kv_append_f16_kernel<64><<<blocks, 128, 0, st>>>(a);
+    else kv_append_f16_kernel<128><<<blocks, 128, 0, st>>>(a);
+    rc = check_launch("kv_append_f16_kernel");
+    if (rc != LFM3A_OK) return rc;
+    const int len = pos0 + n;
+    return launch_v8(kv, pos0 / kQuantBlock, (len - 1) / kQuantBlock + 1, len, st);
+  }
+  if (D == 64) kv_append_i8rec_kernel<64><<<blocks, 128, 0, st>>>(a);
+  else kv_append_i8rec_kernel<128><<<blocks, 128, 0, st>>>(a);
+  return check_launch("kv_append_i8rec_kernel");
+}
+
+int lfm3a_kv_truncate(const lfm3a_kv_view* kv, int new_len, void* stream) {
+  const int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  if (new_len < 0) return fail(LFM3A_EINVAL, "negative length");
+  if (kv->layout.mode != LFM3A_MODE_F16 || new_len % kQuantBlock == 0) return LFM3A_OK;
+  const int qb = new_len / kQuantBlock;
+  return launch_v8(kv, qb, qb + 1, new_len, as_stream(stream));
+}
+
+int lfm3a_accept(const int32_t* best, const int32_t* tokens, int m, int32_t* state, void* stream) {
+  if (!best || !tokens || !state || m < 1) return fail(LFM3A_EINVAL, "bad accept arguments");
+  accept_kernel<<<1, 32, 0, as_stream(stream)>>>(best, tokens, m, state);
+  return check_launch("accept_kernel");
+}
+
+size_t lfm3a_verify_workspace_bytes(int m, int q_heads, int head_dim, int splits) {
+  if (m <= 0 || q_heads <= 0 || head_dim <= 0 || splits <= 0) return 0;
+  return (size_t)m * q_heads * splits * (head_dim + 2) * sizeof(float);
+}
+
+int lfm3a_verify_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int window, int sm_count) {
+  if (!layout || ctx_len < 0 || m < 1) return fail(LFM3A_EINVAL, "bad verify split arguments");
+  return verify_splits_for(layout->kv_heads, ctx_len, m, window, sm_count > 0 ? sm_count : current_sm_count());
+}
+
+int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
+                  const void* gate, void* out, void* stream) {
+  if (!partials || !out || rows <= 0 || splits <= 0) return fail(LFM3A_EINVAL, "bad combine arguments");
+  if (head_dim != 64 && head_dim != 128) return fail(LFM3A_ENOTSUP, "combine head_dim must be 64 or 128");
+  if (split_stride == 0) split_stride = head_dim + 2;
+  if (row_stride == 0) row_stride = split_stride * splits;
+  return launch_combine(partials, rows, splits, head_dim, split_stride, row_stride, static_cast<const __half*>(gate),
+                        static_cast<__half*>(out), nullptr, as_stream(stream));
+}
+
+int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
+                           const void* gate, void* out, void* workspace, size_t workspace_bytes, int splits,
+                           void* stream) {
+  if (splits <= 0 && kv) splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count());
+  return run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, static_cast<__half*>(out), nullptr,
+                    workspace, workspace_bytes, splits, as_stream(stream));
+}
+
+int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int kv_begin, int kv_end,
+                         int ctx_len, int window, float* partial, void* workspace, size_t workspace_bytes, int splits,
+                         void* stream) {
+  return run_verify(kv, q, m, q_heads, kv_begin, kv_end, ctx_len, window, nullptr, nullptr, partial, workspace,
+                    workspace_bytes, splits, as_stream(stream));
+}
+
+size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim) {
+  (void)tokens;
+  (void)q_heads;
+  (void)head_dim;
+  return 0;
+}
+
+int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
+                            int exact, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  const lfm3a_kv_layout& L = kv->layout;
+  if (L.mode != LFM3A_MODE_F16 || L.head_dim != 64) return fail(LFM3A_ENOTSUP, "prefill attention needs MODE_F16, head_dim 64");
+  if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "prefill attention needs 4 query heads per kv head");
+  if (!q || !out || tokens < 0 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill arguments");
+  if (tokens == 0) return LFM3A_OK;
+  if (!aligned16(q) || !aligned16(out)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
+  return launch_prefill(geom_of(kv), static_cast<const __half*>(q), tokens, q_heads, context, window, exact != 0,
+                        static_cast<__half*>(out), as_stream(stream));
+}
+
+int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* stream) {
+  if (!p || !q || !sc || rows < 0) return fail(LFM3A_EINVAL, "bad quantize_p arguments");
+  if (rows == 0) return LFM3A_OK;
+  quantize_p_rows_kernel<<<(rows + 127) / 128, 128, 0, as_stream(stream)>>>(p, rows, q, sc);
+  return check_launch("quantize_p_rows_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,339 @@
+"""Host side of the B200 KV-cache attention path: ctypes bindings of include/lfm3attn.h and a
+per-layer cache object that mirrors how the reference engine owns its KV pools.
+
+The reference engine (Go, internal/model) allocates each layer's paged pool and block table
+(engine.go:474-512 allocRuntime), maps logical to physical blocks (engine.go:682-685 SetBlock,
+generate.go:281-295 ensureBlock) and passes raw device addresses to its kernels
+(prefill.go:464-511, dspark.go:541-621). `LayerCache` does the same with torch-owned device memory;
+the library itself never allocates. Every call raises `LFM3AError` on a non-zero return code.
+
+There is no CPU fallback: importing this module loads liblfm3attn.so and fails loudly without it.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import pathlib
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _HERE / "liblfm3attn.so"
+
+MODE_F16 = 0
+MODE_I8REC = 1
+BLOCK_TOKENS = 32
+QUANT_BLOCK = 64
+
+OK, EINVAL, ELAUNCH, ETIMEOUT, ECUDA, ENOTSUP, EWORKSPACE, EDEVICE = 0, -1, -2, -3, -4, -5, -6, -7
+
+
+class LFM3AError(RuntimeError):
+    def __init__(self, code: int, what: str):
+        super().__init__(f"lfm3attn error {code} ({what})")
+        self.code = code
+
+
+class KvLayout(ctypes.Structure):
+    _fields_ = [
+        ("mode", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("block_tokens", ctypes.c_int32),
+        ("head_bytes", ctypes.c_int64),
+        ("block_bytes", ctypes.c_int64),
+    ]
+
+
+class KvView(ctypes.Structure):
+    _fields_ = [
+        ("pool", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("pool_blocks", ctypes.c_int64),
+        ("layout", KvLayout),
+    ]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); the exported surface of include/lfm3attn.h.
+SIGNATURES = {
+    "lfm3a_version": (_I, []),
+    "lfm3a_strerror": (ctypes.c_char_p, [_I]),
+    "lfm3a_last_error": (ctypes.c_char_p, []),
+    "lfm3a_kv_layout_init": (_I, [_I, _I, _I, _I, ctypes.POINTER(KvLayout)]),
+    "lfm3a_rope_table": (_I, [ctypes.c_double, ctypes.c_double, _I, _I, _P]),
+    "lfm3a_sync": (_I, [_P, _I]),
+    "lfm3a_kv_append": (_I, [ctypes.POINTER(KvView), _P, _P, _I64, _I, _I, _P, _P, _P]),
+    "lfm3a_kv_truncate": (_I, [ctypes.POINTER(KvView), _I, _P]),
+    "lfm3a_accept": (_I, [_P, _P, _I, _P, _P]),
+    "lfm3a_verify_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "lfm3a_verify_splits": (_I, [ctypes.POINTER(KvLayout), _I, _I, _I, _I]),
+    "lfm3a_verify_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _P, _SZ, _I, _P]),
+    "lfm3a_verify_partial": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
+    "lfm3a_combine": (_I, [_P, _I, _I, _I, _I64, _I64, _P, _P, _P]),
+    "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "lfm3a_prefill_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "lfm3a_quantize_p_u8": (_I, [_P, _I, _P, _P, _P]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C-ABI library (loaded on first use; raises when it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise LFM3AError(ECUDA, f"{LIB_PATH} is missing: run __graft_entry__.build()")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != OK:
+        detail = lib().lfm3a_last_error().decode(errors="replace")
+        raise LFM3AError(rc, f"{lib().lfm3a_strerror(rc).decode()}: {detail}")
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def layout(mode: int, kv_heads: int, head_dim: int, block_tokens: int = BLOCK_TOKENS) -> KvLayout:
+    out = KvLayout()
+    _check(lib().lfm3a_kv_layout_init(mode, kv_heads, head_dim, block_tokens, ctypes.byref(out)))
+    return out
+
+
+def rope_table(theta: float, factor: float, head_dim: int, positions: int) -> np.ndarray:
+    """cos | sin rows per position as fp16 bits (engine.go:428-461 buildRope), computed by the library."""
+    out = np.empty((positions, head_dim), dtype=np.uint16)
+    _check(lib().lfm3a_rope_table(theta, factor, head_dim, positions, out.ctypes.data))
+    return out
+
+
+def sync(stream=None, timeout_ms: int = 120000) -> None:
+    """Bounded wait for the stream plus the device error word (queue.go:292-310 Wait)."""
+    _check(lib().lfm3a_sync(_stream(stream), timeout_ms))
+
+
+class LayerCache:
+    """One layer's paged pool and block table in device memory (engine.go:474-512, 682-685)."""
+
+    def __init__(self, mode: int, kv_heads: int, head_dim: int, capacity_tokens: int, device="cuda",
+                 block_table=None, pool_blocks: int | None = None):
+        import torch
+
+        self.layout = layout(mode, kv_heads, head_dim)
+        self.mode, self.kv_heads, self.head_dim = mode, kv_heads, head_dim
+        self.capacity = capacity_tokens
+        logical = (capacity_tokens + BLOCK_TOKENS - 1) // BLOCK_TOKENS
+        self.pool_blocks = pool_blocks if pool_blocks is not None else logical
+        self.pool = torch.zeros(self.pool_blocks * self.layout.block_bytes, dtype=torch.uint8, device=device)
+        if block_table is None:
+            block_table = torch.arange(logical, dtype=torch.int32, device=device)
+        self.table = block_table
+        self.length = 0
+        self.view = KvView(self.pool.data_ptr(), self.table.data_ptr(), self.pool_blocks, self.layout)
+
+    def set_block(self, logical: int, physical: int) -> None:
+        self.table[logical] = physical
+
+    def append(self, k, v, pos0: int | None = None, rope=None, k_norm=None, token_stride: int = 0, stream=None) -> None:
+        """Stores k, v ([n][kv_heads][head_dim] fp16 device tensors) at positions pos0.. (default: the end)."""
+        pos0 = self.length if pos0 is None else pos0
+        n = k.shape[0]
+        if pos0 + n > self.capacity:
+            raise LFM3AError(EINVAL, "append past the cache capacity")
+        _check(lib().lfm3a_kv_append(ctypes.byref(self.view), _ptr(k), _ptr(v), token_stride, pos0, n, _ptr(rope),
+                                     _ptr(k_norm), _stream(stream)))
+        self.length = max(self.length, pos0 + n)
+
+    def truncate(self, new_len: int, stream=None) -> None:
+        """Rollback after rejected drafts: the length drops, the tail block's int8 V is re-quantised."""
+        _check(lib().lfm3a_kv_truncate(ctypes.byref(self.view), new_len, _stream(stream)))
+        self.length = new_len
+
+    def verify(self, q, ctx_len: int, window: int = 0, gate=None, out=None, workspace=None, splits: int = 0,
+               stream=None):
+        """DSpark verify attention of q ([m][q_heads][head_dim] fp16) over the cache; drafts appended."""
+        import torch
+
+        m, qh, d = q.shape
+        if out is None:
+            out = torch.empty_like(q)
+        if splits <= 0:
+            splits = verify_splits(self.layout, ctx_len, m, window)
+        need = lib().lfm3a_verify_workspace_bytes(m, qh, d, splits)
+        if workspace is None and splits > 1:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib().lfm3a_verify_attention(ctypes.byref(self.view), _ptr(q), m, qh, ctx_len, window, _ptr(gate),
+                                            _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
+        return out
+
+    def verify_partial(self, q, kv_begin: int, kv_end: int, ctx_len: int, window: int = 0, out=None, workspace=None,
+                       splits: int = 0, stream=None):
+        """This cache shard's log-sum-exp partial [m * q_heads][head_dim + 2] over positions [kv_begin, kv_end)."""
+        import torch
+
+        m, qh, d = q.shape
+        if out is None:
+            out = torch.empty((m * qh, d + 2), dtype=torch.float32, device=q.device)
+        if splits <= 0:
+            splits = verify_splits(self.layout, kv_end - kv_begin, 1, 0)
+        need = lib().lfm3a_verify_workspace_bytes(m, qh, d, splits)
+        if workspace is None and splits > 1:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib().lfm3a_verify_partial(ctypes.byref(self.view), _ptr(q), m, qh, kv_begin, kv_end, ctx_len, window,
+                                          _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
+        return out
+
+    def prefill(self, q, context: int, window: int = 0, exact: bool = False, out=None, workspace=None, stream=None):
+        """Causal prefill attention of q ([T][q_heads][head_dim] fp16) at positions context.."""
+        import torch
+
+        t, qh, d = q.shape
+        if out is None:
+            out = torch.empty_like(q)
+        need = lib().lfm3a_prefill_workspace_bytes(t, qh, d)
+        if workspace is None and need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib().lfm3a_prefill_attention(ctypes.byref(self.view), _ptr(q), t, qh, context, window, int(exact),
+                                             _ptr(out), _ptr(workspace), ws_bytes, _stream(stream)))
+        return out
+
+    # -------------------------------------------------------------- host-side inspection
+    def logical(self, length: int | None = None) -> dict:
+        """Decodes the pool into logical arrays (for checks): see decode_pool."""
+        length = self.length if length is None else length
+        pool = self.pool.cpu().numpy()
+        table = self.table.cpu().numpy()
+        return decode_pool(pool, table, self.layout, length)
+
+
+def verify_splits(lay: KvLayout, ctx_len: int, m: int, window: int = 0, sm_count: int = 0) -> int:
+    rc = lib().lfm3a_verify_splits(ctypes.byref(lay), ctx_len, m, window, sm_count)
+    if rc < 0:
+        _check(rc)
+    return rc
+
+
+def combine(partials, rows: int, splits: int, head_dim: int, split_stride: int = 0, row_stride: int = 0, gate=None,
+            out=None, stream=None):
+    """Log-sum-exp merge of f32 partials (strides in floats; 0 = [rows][splits][head_dim + 2])."""
+    import torch
+
+    if out is None:
+        out = torch.empty((rows, head_dim), dtype=torch.float16, device=partials.device)
+    _check(lib().lfm3a_combine(_ptr(partials), rows, splits, head_dim, split_stride, row_stride, _ptr(gate), _ptr(out),
+                               _stream(stream)))
+    return out
+
+
+def accept(best, tokens, state, stream=None) -> None:
+    m = tokens.numel()
+    _check(lib().lfm3a_accept(_ptr(best), _ptr(tokens), m, _ptr(state), _stream(stream)))
+
+
+def quantize_p_u8(p, stream=None):
+    import torch
+
+    rows = p.shape[0]
+    q = torch.empty((rows, 64), dtype=torch.uint8, device=p.device)
+    sc = torch.empty((rows,), dtype=torch.float32, device=p.device)
+    _check(lib().lfm3a_quantize_p_u8(_ptr(p), rows, _ptr(q), _ptr(sc), _stream(stream)))
+    return q, sc
+
+
+# ------------------------------------------------------------------ page layout (host decoding)
+def _f16_section_index(d: int):
+    """Index arrays of the MODE_F16 section for s in 0..31, dim in 0..d-1 (see csrc/kv.cuh)."""
+    s = np.arange(BLOCK_TOKENS)[:, None]
+    dim = np.arange(d)[None, :]
+    k_idx = ((s >> 3) * (d // 8) + (dim >> 3)) * 64 + (s & 7) * 8 + (dim & 7)
+    v_idx = ((dim >> 3) * 4 + (s >> 3)) * 64 + (dim & 7) * 8 + (s & 7)
+    v8_idx = ((dim >> 3) * 2 + (s >> 4)) * 128 + (dim & 7) * 16 + (s & 15)
+    return k_idx, v_idx, v8_idx
+
+
+def decode_pool(pool: np.ndarray, table: np.ndarray, lay: KvLayout, length: int) -> dict:
+    """Logical view of `length` tokens of a pool (uint8 bytes).
+
+    MODE_F16 -> K, V [length][kv_heads][head_dim] uint16 (fp16 bits), V8 [64-rounded][kv_heads][head_dim]
+    int8 and vscale [blocks of 64][kv_heads] f32. MODE_I8REC -> rec [length][kv_heads][2 * head_dim + 8] uint8.
+    """
+    h, d = lay.kv_heads, lay.head_dim
+    pages = (length + BLOCK_TOKENS - 1) // BLOCK_TOKENS
+    if lay.mode == MODE_I8REC:
+        rec_bytes = 2 * d + 8
+        out = np.zeros((pages * BLOCK_TOKENS, h, rec_bytes), dtype=np.uint8)
+        for p in range(pages):
+            blk = int(table[p])
+            raw = pool[blk * lay.block_bytes:(blk + 1) * lay.block_bytes].reshape(BLOCK_TOKENS, h, rec_bytes)
+            out[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS] = raw
+        return {"rec": out[:length]}
+    k_idx, v_idx, v8_idx = _f16_section_index(d)
+    K = np.zeros((pages * BLOCK_TOKENS, h, d), dtype=np.uint16)
+    V = np.zeros_like(K)
+    V8 = np.zeros((pages * BLOCK_TOKENS, h, d), dtype=np.int8)
+    page_scale = np.zeros((pages, h), dtype=np.float32)
+    for p in range(pages):
+        blk = int(table[p])
+        for hh in range(h):
+            base = blk * lay.block_bytes + hh * lay.head_bytes
+            sec = pool[base:base + lay.head_bytes]
+            kk = sec[:64 * d].view(np.uint16)
+            vv = sec[64 * d:128 * d].view(np.uint16)
+            v8 = sec[128 * d:160 * d].view(np.int8)
+            K[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS, hh] = kk[k_idx]
+            V[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS, hh] = vv[v_idx]
+            V8[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS, hh] = v8[v8_idx]
+            page_scale[p, hh] = sec[160 * d:160 * d + 4].view(np.float32)[0]
+    qblocks = (length + QUANT_BLOCK - 1) // QUANT_BLOCK
+    vscale = page_scale[0::2][:qblocks]
+    v8_len = min(V8.shape[0], qblocks * QUANT_BLOCK)
+    V8_out = np.zeros((qblocks * QUANT_BLOCK, h, d), dtype=np.int8)
+    V8_out[:v8_len] = V8[:v8_len]
+    return {"K": K[:length], "V": V[:length], "V8": V8_out, "vscale": vscale, "page_scale": page_scale}
+
+
+@dataclass
+class Geometry:
+    """Attention geometry: the benchmark's 32/8/64 or the reference model's 16/4/128."""
+
+    q_heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 64
+
+    @property
+    def group(self) -> int:
+        return self.q_heads // self.kv_heads
+
+    @property
+    def qk_scale(self) -> float:
+        return 1.0 / math.sqrt(self.head_dim)

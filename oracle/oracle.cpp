@@ -1,0 +1,449 @@
+// CPU restatement of the reference KV-cache attention arithmetic. TEST INFRASTRUCTURE ONLY:
+// the parity tests, the smoke check and the benchmark's CPU-baseline leg call it as the checker.
+// Parity status: UNPINNED against the reference itself (no runnable reference and no reference
+// golden vectors); cross-checked against tests/golden (an independent numpy restatement) and fp64.
+// Build: oracle/Makefile (g++ -O3 -fopenmp -ffp-contract=off, so every a*b+c rounds twice as the
+// restated source lines do).
+#include "oracle.h"
+
+#include <math.h>
+#include <omp.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+namespace {
+
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LAZY = 8.f;   // prefill_attn.hip:33: rescale only when a tile beats the max by 2^8
+constexpr int BS = 32;        // KV block tokens (engine.go:31)
+constexpr int QB = 64;        // prefill key tile and int8 V block (prefill_attn.hip:29)
+
+inline float r16(float x) { return orc_f16_to_f32(orc_f32_to_f16(x)); }
+
+// Butterfly sum over 32 lanes, the order the append kernel's warp reduction uses: for o = 16..1,
+// v[l] = v[l] + v[l ^ o]. Every lane ends with the same bits; lane 0's value is returned.
+float lane_tree_sum(float* v) {
+  float t[32];
+  for (int o = 16; o >= 1; o >>= 1) {
+    for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
+    memcpy(v, t, sizeof(t));
+  }
+  return v[0];
+}
+
+// RMS k-norm + RoPE of one head, ops.hip:193-200. x: [D] fp32 values of fp16 inputs, out: [D] fp32
+// values of the stored fp16 results. Lane l of the kernel holds pairs (l + 32 j, l + 32 j + D/2).
+void norm_rope_head(const float* x, int D, const uint16_t* rope_row, const uint16_t* knorm, float* out) {
+  const int half = D / 2, J = D / 64;
+  float a1[128], b1[128];
+  if (knorm) {
+    float lanes[32];
+    for (int l = 0; l < 32; ++l) {
+      float acc = 0.f;
+      for (int j = 0; j < J; ++j) {
+        const float a = x[l + 32 * j], b = x[l + 32 * j + half];
+        const float term = a * a + b * b;   // two products, one sum (no contraction)
+        acc = j == 0 ? term : acc + term;
+      }
+      lanes[l] = acc;
+    }
+    const float ss = lane_tree_sum(lanes);
+    const float inv = 1.f / sqrtf(ss / (float)D + 1e-5f);
+    for (int i = 0; i < half; ++i) {
+      a1[i] = r16(x[i] * inv * orc_f16_to_f32(knorm[i]));
+      b1[i] = r16(x[i + half] * inv * orc_f16_to_f32(knorm[i + half]));
+    }
+  } else {
+    for (int i = 0; i < half; ++i) {
+      a1[i] = x[i];
+      b1[i] = x[i + half];
+    }
+  }
+  for (int i = 0; i < half; ++i) {
+    if (rope_row) {
+      const float c = orc_f16_to_f32(rope_row[i]), s = orc_f16_to_f32(rope_row[i + half]);
+      const float t1 = a1[i] * c, t2 = b1[i] * s, t3 = b1[i] * c, t4 = a1[i] * s;
+      out[i] = r16(t1 - t2);
+      out[i + half] = r16(t3 + t4);
+    } else {
+      out[i] = a1[i];
+      out[i + half] = b1[i];
+    }
+  }
+}
+
+// The cache quantiser of ops.hip:213-224: scale = max(amax/127, 1e-6), round half away from zero.
+inline int8_t quant_half_away(float x, float inv) {
+  float q = x * inv;
+  q = q >= 0.f ? q + 0.5f : q - 0.5f;
+  return (int8_t)truncf(fminf(fmaxf(q, -128.f), 127.f));
+}
+
+inline float cache_scale(float amax) { return fmaxf(amax / 127.f, 1e-6f); }
+
+inline uint8_t rne_sat_u8(float x) {
+  float r = nearbyintf(x);   // default rounding: to nearest, ties to even
+  r = fminf(fmaxf(r, 0.f), 255.f);
+  return (uint8_t)r;
+}
+
+inline int kv_start(int ctx_len, int window) { return window > 0 ? std::max(0, ctx_len - window + 1) : 0; }
+
+}  // namespace
+
+extern "C" {
+
+uint16_t orc_f32_to_f16(float f) {
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  const uint16_t sign = (uint16_t)((b >> 16) & 0x8000u);
+  const int32_t biased = (int32_t)((b >> 23) & 0xffu);
+  uint32_t man = b & 0x7fffffu;
+  if (biased == 0xff) return man ? (uint16_t)(sign | 0x7e00u) : (uint16_t)(sign | 0x7c00u);
+  const int32_t exp = biased - 127 + 15;
+  if (exp >= 31) return (uint16_t)(sign | 0x7c00u);
+  if (exp <= 0) {
+    if (exp < -10) return sign;
+    man |= 0x800000u;
+    const uint32_t shift = (uint32_t)(14 - exp);
+    uint32_t m = man >> shift;
+    const uint32_t rem = man & ((1u << shift) - 1u), half = 1u << (shift - 1u);
+    if (rem > half || (rem == half && (m & 1u))) ++m;
+    return (uint16_t)(sign | m);
+  }
+  const uint32_t m = man >> 13, rem = man & 0x1fffu;
+  uint16_t out = (uint16_t)(sign | ((uint32_t)exp << 10) | m);
+  if (rem > 0x1000u || (rem == 0x1000u && (m & 1u))) ++out;
+  return out;
+}
+
+float orc_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu, bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {
+      uint32_t e = 127 - 15 + 1;
+      while (!(man & 0x400u)) {
+        man <<= 1;
+        --e;
+      }
+      bits = sign | (e << 23) | ((man & 0x3ffu) << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | (0xffu << 23) | (man << 13);
+  } else {
+    bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+void orc_set_threads(int n) { omp_set_num_threads(n > 0 ? n : 1); }
+int orc_get_threads(void) { return omp_get_max_threads(); }
+
+void orc_rope_table(double theta, double factor, int head_dim, int positions, uint16_t* out) {
+  const int half = head_dim / 2, angles = (int)(factor * head_dim) / 2;
+  std::vector<float> inv(half, 0.f);
+  for (int i = 0; i < angles; ++i) {
+    const float e = (float)(2 * i) / (float)head_dim;
+    inv[i] = 1.f / (float)pow(theta, (double)e);
+  }
+#pragma omp parallel for schedule(static)
+  for (int p = 0; p < positions; ++p) {
+    const float t = (float)p;
+    for (int i = 0; i < half; ++i) {
+      const double f = (double)(t * inv[i]);
+      out[(size_t)p * head_dim + i] = orc_f32_to_f16((float)cos(f));
+      out[(size_t)p * head_dim + half + i] = orc_f32_to_f16((float)sin(f));
+    }
+  }
+}
+
+void orc_kv_append_f16(const uint16_t* k, const uint16_t* v, int n, int kv_heads, int head_dim, int pos0,
+                       const uint16_t* rope, const uint16_t* knorm, uint16_t* k_out, uint16_t* v_out) {
+  const int D = head_dim;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < n * kv_heads; ++r) {
+    const int t = r / kv_heads;
+    float x[128], o[128];
+    for (int d = 0; d < D; ++d) x[d] = orc_f16_to_f32(k[(size_t)r * D + d]);
+    norm_rope_head(x, D, rope ? rope + (size_t)(pos0 + t) * D : nullptr, knorm, o);
+    for (int d = 0; d < D; ++d) {
+      k_out[(size_t)r * D + d] = orc_f32_to_f16(o[d]);
+      v_out[(size_t)r * D + d] = v[(size_t)r * D + d];
+    }
+  }
+}
+
+void orc_kv_append_i8rec(const uint16_t* k, const uint16_t* v, int n, int kv_heads, int head_dim, int pos0,
+                         const uint16_t* rope, const uint16_t* knorm, uint8_t* rec) {
+  const int D = head_dim, R = 2 * D + 8;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < n * kv_heads; ++r) {
+    const int t = r / kv_heads;
+    float x[128], kk[128], vv[128];
+    for (int d = 0; d < D; ++d) {
+      x[d] = orc_f16_to_f32(k[(size_t)r * D + d]);
+      vv[d] = orc_f16_to_f32(v[(size_t)r * D + d]);
+    }
+    norm_rope_head(x, D, rope ? rope + (size_t)(pos0 + t) * D : nullptr, knorm, kk);
+    uint8_t* out = rec + (size_t)r * R;
+    const float* src[2] = {kk, vv};
+    for (int part = 0; part < 2; ++part) {
+      float amax = 0.f;
+      for (int d = 0; d < D; ++d) amax = fmaxf(amax, fabsf(src[part][d]));
+      const float scale = cache_scale(amax), inv = 1.f / scale;
+      uint8_t* dst = out + part * (D + 4);
+      for (int d = 0; d < D; ++d) dst[d] = (uint8_t)quant_half_away(src[part][d], inv);
+      memcpy(dst + D, &scale, 4);
+    }
+  }
+}
+
+void orc_quantize_v8(const uint16_t* v, int len, int kv_heads, int head_dim, int8_t* v8, float* scale) {
+  const int D = head_dim, nblk = (len + QB - 1) / QB;
+  memset(v8, 0, (size_t)nblk * QB * kv_heads * D);
+#pragma omp parallel for schedule(static)
+  for (int bh = 0; bh < nblk * kv_heads; ++bh) {
+    const int b = bh / kv_heads, h = bh % kv_heads;
+    const int t0 = b * QB, t1 = std::min(len, t0 + QB);
+    float amax = 0.f;
+    for (int t = t0; t < t1; ++t)
+      for (int d = 0; d < D; ++d) amax = fmaxf(amax, fabsf(orc_f16_to_f32(v[((size_t)t * kv_heads + h) * D + d])));
+    const float sc = cache_scale(amax), inv = 1.f / sc;
+    scale[bh] = sc;
+    for (int t = t0; t < t1; ++t)
+      for (int d = 0; d < D; ++d) {
+        const size_t i = ((size_t)t * kv_heads + h) * D + d;
+        v8[i] = quant_half_away(orc_f16_to_f32(v[i]), inv);
+      }
+  }
+}
+
+void orc_quantize_p_u8(const float* p, int rows, int cols, uint8_t* q, float* sc) {
+  for (int r = 0; r < rows; ++r) {
+    float pm = 0.f;
+    for (int c = 0; c < cols; ++c) pm = fmaxf(pm, p[(size_t)r * cols + c]);
+    const float inv = 255.f / fmaxf(pm, 1e-30f);
+    for (int c = 0; c < cols; ++c) q[(size_t)r * cols + c] = rne_sat_u8(p[(size_t)r * cols + c] * inv);
+    sc[r] = pm * (1.f / 255.f);
+  }
+}
+
+void orc_verify(const uint16_t* q, int m, int q_heads, int kv_heads, int head_dim, const uint16_t* K,
+                const uint16_t* V, int ctx_len, int window, const uint16_t* gate, int splits, float* out) {
+  const int D = head_dim, G = q_heads / kv_heads;
+  const int start = kv_start(ctx_len, window), kv_end = ctx_len + m;
+  const int p_begin = start / BS, p_total = (kv_end - 1) / BS - p_begin + 1;
+  const int S = std::max(1, std::min(splits, p_total));
+  const float qk_scale = (1.f / sqrtf((float)D)) * LOG2E;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int row = 0; row < m * q_heads; ++row) {
+    const int t = row / q_heads, qh = row % q_heads, h = qh / G, qpos = ctx_len + t;
+    float qf[128];
+    for (int d = 0; d < D; ++d) qf[d] = orc_f16_to_f32(q[(size_t)row * D + d]);
+    std::vector<float> pacc((size_t)S * D, 0.f), pm(S, -1e30f), pl(S, 0.f);
+    for (int s = 0; s < S; ++s) {
+      const int g0 = p_begin + (int)((int64_t)p_total * s / S), g1 = p_begin + (int)((int64_t)p_total * (s + 1) / S);
+      float m_run = -1e30f, l_run = 0.f, acc[128] = {0};
+      for (int pg = g0; pg < g1; ++pg) {
+        float sc[BS];
+        float mx = -INFINITY;
+        for (int kk = 0; kk < BS; ++kk) {
+          const int kpos = pg * BS + kk;
+          bool valid;
+          if (kpos < ctx_len) valid = kpos >= start && (window == 0 || kpos > qpos - window);
+          else valid = kpos <= qpos;
+          if (!valid) {
+            sc[kk] = -INFINITY;
+            continue;
+          }
+          const uint16_t* kr = K + ((size_t)kpos * kv_heads + h) * D;
+          float dot = 0.f;
+#pragma omp simd reduction(+ : dot)
+          for (int d = 0; d < D; ++d) dot += qf[d] * orc_f16_to_f32(kr[d]);
+          sc[kk] = dot * qk_scale;
+          mx = fmaxf(mx, sc[kk]);
+        }
+        if (mx > m_run) {
+          const float corr = exp2f(m_run - mx);
+          m_run = mx;
+          l_run *= corr;
+          for (int d = 0; d < D; ++d) acc[d] *= corr;
+        }
+        for (int kk = 0; kk < BS; ++kk) {
+          if (sc[kk] == -INFINITY) continue;
+          const int kpos = pg * BS + kk;
+          const float p = exp2f(sc[kk] - m_run);
+          l_run += p;
+          const float p16 = r16(p);
+          const uint16_t* vr = V + ((size_t)kpos * kv_heads + h) * D;
+          for (int d = 0; d < D; ++d) acc[d] += p16 * orc_f16_to_f32(vr[d]);
+        }
+      }
+      for (int d = 0; d < D; ++d) pacc[(size_t)s * D + d] = acc[d];
+      pm[s] = m_run;
+      pl[s] = l_run;
+    }
+    float M = -INFINITY;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, pm[s]);
+    float L = 0.f, o[128] = {0};
+    for (int s = 0; s < S; ++s) {
+      const float f = exp2f(pm[s] - M);
+      L += f * pl[s];
+      for (int d = 0; d < D; ++d) o[d] += f * pacc[(size_t)s * D + d];
+    }
+    float g = 1.f;
+    if (gate) g = 1.f / (1.f + exp2f(-orc_f16_to_f32(gate[row]) * LOG2E));
+    for (int d = 0; d < D; ++d) out[(size_t)row * D + d] = (L > 0.f ? o[d] / L : 0.f) * g;
+  }
+}
+
+void orc_attention_f64(const uint16_t* q, int nq, int qpos0, int q_heads, int kv_heads, int head_dim,
+                       const uint16_t* K, const uint16_t* V, int kv_len, int window, int row_step, float* out) {
+  const int D = head_dim, G = q_heads / kv_heads;
+  const int rows = (nq + row_step - 1) / row_step;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int ri = 0; ri < rows * q_heads; ++ri) {
+    const int t = (ri / q_heads) * row_step, qh = ri % q_heads, h = qh / G, qpos = qpos0 + t;
+    const size_t row = (size_t)t * q_heads + qh;
+    double qd[128];
+    for (int d = 0; d < D; ++d) qd[d] = orc_f16_to_f32(q[row * D + d]);
+    const int kb = window > 0 ? std::max(0, qpos - window + 1) : 0, ke = std::min(qpos + 1, kv_len);
+    const double scale = 1.0 / sqrt((double)D);
+    std::vector<double> s(std::max(0, ke - kb));
+    double mx = -INFINITY;
+    for (int kpos = kb; kpos < ke; ++kpos) {
+      const uint16_t* kr = K + ((size_t)kpos * kv_heads + h) * D;
+      double dot = 0.0;
+      for (int d = 0; d < D; ++d) dot += qd[d] * (double)orc_f16_to_f32(kr[d]);
+      s[kpos - kb] = dot * scale;
+      mx = std::max(mx, s[kpos - kb]);
+    }
+    double l = 0.0, o[128] = {0};
+    for (int kpos = kb; kpos < ke; ++kpos) {
+      const double p = exp(s[kpos - kb] - mx);
+      l += p;
+      const uint16_t* vr = V + ((size_t)kpos * kv_heads + h) * D;
+      for (int d = 0; d < D; ++d) o[d] += p * (double)orc_f16_to_f32(vr[d]);
+    }
+    for (int d = 0; d < D; ++d) out[row * D + d] = l > 0.0 ? (float)(o[d] / l) : 0.f;
+  }
+}
+
+}  // extern "C"
+
+namespace {
+
+// One query row of the prefill kernels: CTA of 32 query tokens (t0 = t & ~31), 64-key tiles from the
+// CTA's first key rounded down to 64, lazy running max with the first tile of the CTA setting it
+// (prefill_attn.hip:212-332,373-486).
+template <bool I8>
+void prefill_row(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int D, const uint16_t* K,
+                 const uint16_t* V, const int8_t* V8, const float* vscale, int window, int t, int qh, float* o) {
+  const int G = q_heads / kv_heads, h = qh / G;
+  const int t0 = t & ~31, ntok = std::min(32, T - t0);
+  const int qpos = context + t, qfirst = context + t0, kend = context + t0 + ntok;
+  const int kbegin = window > 0 ? std::max(0, qfirst - window + 1) : 0;
+  const int kt_begin = kbegin / QB * QB;
+  const float qk_scale = (1.f / sqrtf((float)D)) * LOG2E;
+  float qf[128];
+  for (int d = 0; d < D; ++d) qf[d] = orc_f16_to_f32(q[((size_t)t * q_heads + qh) * D + d]);
+  float m = 0.f, l = 0.f, acc[128] = {0};
+  bool first = true;
+  for (int k0 = kt_begin; k0 < kend; k0 += QB, first = false) {
+    float s[QB];
+    float tm = -INFINITY;
+    for (int kk = 0; kk < QB; ++kk) {
+      const int kpos = k0 + kk;
+      const bool valid = kpos <= qpos && kpos >= kbegin && (window == 0 || kpos > qpos - window);
+      if (!valid) {
+        s[kk] = -INFINITY;
+        continue;
+      }
+      const uint16_t* kr = K + ((size_t)kpos * kv_heads + h) * D;
+      float dot = 0.f;
+#pragma omp simd reduction(+ : dot)
+      for (int d = 0; d < D; ++d) dot += qf[d] * orc_f16_to_f32(kr[d]);
+      s[kk] = dot * qk_scale;
+      tm = fmaxf(tm, s[kk]);
+    }
+    if (tm > -INFINITY && (first || tm > m + LAZY)) {
+      const float corr = exp2f(m - tm);
+      m = tm;
+      l *= corr;
+      for (int d = 0; d < D; ++d) acc[d] *= corr;
+    }
+    float p[QB];
+    for (int kk = 0; kk < QB; ++kk) {
+      p[kk] = s[kk] == -INFINITY ? 0.f : exp2f(s[kk] - m);
+      l += p[kk];
+    }
+    if (I8) {
+      const float vs = vscale[(size_t)(k0 / QB) * kv_heads + h];
+      float pp[QB];
+      for (int kk = 0; kk < QB; ++kk) pp[kk] = p[kk] * vs;
+      uint8_t q8[QB];
+      float sc;
+      orc_quantize_p_u8(pp, 1, QB, q8, &sc);
+      for (int d = 0; d < D; ++d) {
+        int32_t sum = 0;
+        for (int kk = 0; kk < QB; ++kk) {
+          if (!q8[kk]) continue;
+          sum += (int32_t)q8[kk] * (int32_t)V8[((size_t)(k0 + kk) * kv_heads + h) * D + d];
+        }
+        acc[d] += sc * (float)sum;
+      }
+    } else {
+      for (int kk = 0; kk < QB; ++kk) {
+        if (p[kk] == 0.f) continue;
+        const float p16 = r16(p[kk]);
+        const uint16_t* vr = V + ((size_t)(k0 + kk) * kv_heads + h) * D;
+        for (int d = 0; d < D; ++d) acc[d] += p16 * orc_f16_to_f32(vr[d]);
+      }
+    }
+  }
+  for (int d = 0; d < D; ++d) o[d] = l > 0.f ? acc[d] / l : 0.f;
+}
+
+template <bool I8>
+void prefill_all(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int D, const uint16_t* K,
+                 const uint16_t* V, const int8_t* V8, const float* vscale, int window, int row_step, float* out) {
+  const int rows = (T + row_step - 1) / row_step;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int ri = 0; ri < rows * q_heads; ++ri) {
+    const int t = (ri / q_heads) * row_step, qh = ri % q_heads;
+    prefill_row<I8>(q, T, context, q_heads, kv_heads, D, K, V, V8, vscale, window, t, qh,
+                    out + ((size_t)t * q_heads + qh) * D);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+void orc_prefill_i8pv(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
+                      const uint16_t* K, const int8_t* V8, const float* vscale, int window, int row_step, float* out) {
+  prefill_all<true>(q, T, context, q_heads, kv_heads, head_dim, K, nullptr, V8, vscale, window, row_step, out);
+}
+
+void orc_prefill_exact(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
+                       const uint16_t* K, const uint16_t* V, int window, int row_step, float* out) {
+  prefill_all<false>(q, T, context, q_heads, kv_heads, head_dim, K, V, nullptr, nullptr, window, row_step, out);
+}
+
+int orc_accept(const int32_t* best, const int32_t* tokens, int m) {
+  int acc = 0;
+  for (int t = 0; t < m - 1; ++t) {
+    if (best[t] != tokens[t + 1]) break;
+    ++acc;
+  }
+  return acc + 1;
+}
+
+}  // extern "C"

@@ -1,0 +1,91 @@
+/*
+ * CPU restatement of the reference KV-cache attention arithmetic (jwyjohn/lfm3-1.7b-mi50).
+ *
+ * TEST INFRASTRUCTURE ONLY. The parity tests, the smoke check and the CPU-baseline leg of the
+ * benchmark call these functions as the checker; the product library never links them.
+ *
+ * Parity status: UNPINNED against the reference itself. The reference is Go + HIP for gfx906:
+ * no Go toolchain, no ROCm and no AMD GPU exist here, its compiled code objects are off limits,
+ * and its repository ships no golden vectors or known-answer tests for any attention kernel.
+ * The restatement is cross-checked instead against an independent numpy restatement of the
+ * same source lines (tests/golden) and against exact fp64 attention.
+ *
+ * Every function names the reference lines it restates (paths inside the reference project).
+ * Arrays are row-major; fp16 values travel as uint16_t bit patterns.
+ *
+ * Logical cache arrays used throughout:
+ *   K, V    [tokens][kv_heads][head_dim] fp16 (K after k-norm/RoPE, as stored by the append)
+ *   V8      [tokens][kv_heads][head_dim] int8, the int8 copy of V quantised per (kv head,
+ *           64-token block); tokens past the cache length hold 0
+ *   vscale  [blocks of 64][kv_heads] f32
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* fp16 <-> fp32, round to nearest even: internal/fp16/fp16.go:8-64. */
+uint16_t orc_f32_to_f16(float f);
+float orc_f16_to_f32(uint16_t h);
+
+/* cos | sin rows per position: internal/model/engine.go:428-461 (buildRope). out [positions][head_dim]. */
+void orc_rope_table(double theta, double factor, int head_dim, int positions, uint16_t* out);
+
+/* K/V append of n tokens at positions pos0.. (kernels/ops.hip:193-200,236-251; dspark.hip:1050-1060):
+ * optional RMS k-norm (weights knorm[head_dim], eps 1e-5), optional RoPE from the table, fp16 rounding
+ * after each step. k, v: [n][kv_heads][head_dim] fp16. k_out, v_out: the values the cache stores. */
+void orc_kv_append_f16(const uint16_t* k, const uint16_t* v, int n, int kv_heads, int head_dim, int pos0,
+                       const uint16_t* rope, const uint16_t* knorm, uint16_t* k_out, uint16_t* v_out);
+
+/* The same append into the reference's int8 264-byte records (head_dim 128) or (2*head_dim+8)-byte
+ * records in general: K int8[D] | K scale f32 | V int8[D] | V scale f32 (ops.hip:213-251).
+ * rec: [n][kv_heads][2*head_dim+8] bytes. */
+void orc_kv_append_i8rec(const uint16_t* k, const uint16_t* v, int n, int kv_heads, int head_dim, int pos0,
+                         const uint16_t* rope, const uint16_t* knorm, uint8_t* rec);
+
+/* int8 V per (kv head, 64-token block), absmax/127 with the cache quantiser's rounding (ops.hip:213-224
+ * applied per block instead of per token). v: [len][kv_heads][head_dim]. v8: [ceil64(len)][kv_heads][head_dim],
+ * scale: [ceil(len/64)][kv_heads]. */
+void orc_quantize_v8(const uint16_t* v, int len, int kv_heads, int head_dim, int8_t* v8, float* scale);
+
+/* u8 quantisation of P' rows against the row maximum (prefill_attn.hip:305-331):
+ * q = rne_sat_u8(p * (255 / max(pm, 1e-30))), sc = pm * (1/255). p: [rows][cols]. */
+void orc_quantize_p_u8(const float* p, int rows, int cols, uint8_t* q, float* sc);
+
+/* Verify attention over the cache (drafts already appended at ctx_len..ctx_len+m-1), restating the
+ * split-KV page partition, exact running max, fp16 P and the log-sum-exp combine with the optional
+ * sigmoid gate (dspark.hip:975-979,1809-2121,2134-2185). q: [m][q_heads][head_dim] fp16, gate: [m][q_heads]
+ * fp16 logits or NULL, out: [m][q_heads][head_dim] f32. */
+void orc_verify(const uint16_t* q, int m, int q_heads, int kv_heads, int head_dim, const uint16_t* K,
+                const uint16_t* V, int ctx_len, int window, const uint16_t* gate, int splits, float* out);
+
+/* Exact fp64 attention for query tokens at positions qpos0 + t (t < nq) over keys [0, kv_len), causal,
+ * optional sliding window; rows t = 0, row_step, 2*row_step, ... only. out [nq][q_heads][head_dim] f32
+ * (rows not computed are left untouched). */
+void orc_attention_f64(const uint16_t* q, int nq, int qpos0, int q_heads, int kv_heads, int head_dim,
+                       const uint16_t* K, const uint16_t* V, int kv_len, int window, int row_step, float* out);
+
+/* Prefill attention with u8 P and int8 V (prefill_attn.hip:212-367,373-486): 64-key tiles aligned to 64,
+ * lazy running max (threshold 2^8), P' = p * vscale quantised per row and tile, PV in exact integers.
+ * Query tokens t < T at positions context + t; keys [0, context + T). Rows t % row_step == 0 only. */
+void orc_prefill_i8pv(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
+                      const uint16_t* K, const int8_t* V8, const float* vscale, int window, int row_step, float* out);
+
+/* The same with fp16 P and fp16 V (prefill_attn_exact.hip:173-344 with fp16 V). */
+void orc_prefill_exact(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
+                       const uint16_t* K, const uint16_t* V, int window, int row_step, float* out);
+
+/* Acceptance of a verify round (dspark.hip:2848-2895): the longest prefix t with best[t] == tokens[t+1],
+ * then commit = accepted + 1 positions. Returns commit. */
+int orc_accept(const int32_t* best, const int32_t* tokens, int m);
+
+/* Threads the oracle may use (OpenMP). */
+void orc_set_threads(int n);
+int orc_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif

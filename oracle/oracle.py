@@ -1,0 +1,174 @@
+"""ctypes wrapper of the CPU restatement in oracle.cpp.
+
+TEST INFRASTRUCTURE ONLY: tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it as
+the checker. Parity status: unpinned against the reference itself (see oracle.h).
+fp16 arrays travel as numpy float16 (bit-identical to the uint16 patterns the C side takes).
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "liboracle.so"
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_lib = None
+
+_SIGS = {
+    "orc_f32_to_f16": (ctypes.c_uint16, [ctypes.c_float]),
+    "orc_f16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
+    "orc_rope_table": (None, [ctypes.c_double, ctypes.c_double, _I, _I, _P]),
+    "orc_kv_append_f16": (None, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "orc_kv_append_i8rec": (None, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "orc_quantize_v8": (None, [_P, _I, _I, _I, _P, _P]),
+    "orc_quantize_p_u8": (None, [_P, _I, _I, _P, _P]),
+    "orc_verify": (None, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _P]),
+    "orc_attention_f64": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
+    "orc_prefill_i8pv": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
+    "orc_prefill_exact": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _P]),
+    "orc_accept": (_I, [_P, _P, _I]),
+    "orc_set_threads": (None, [_I]),
+    "orc_get_threads": (_I, []),
+}
+
+
+def build() -> pathlib.Path:
+    res = subprocess.run(["make", "-C", str(HERE)], capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + res.stdout + res.stderr)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        h = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def _c(a: np.ndarray | None, dtype=None):
+    if a is None:
+        return None, None
+    a = np.ascontiguousarray(a, dtype=dtype) if dtype is not None else np.ascontiguousarray(a)
+    return a, a.ctypes.data
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(n)
+
+
+def get_threads() -> int:
+    return lib().orc_get_threads()
+
+
+def rope_table(theta: float, factor: float, head_dim: int, positions: int) -> np.ndarray:
+    out = np.empty((positions, head_dim), dtype=np.float16)
+    lib().orc_rope_table(theta, factor, head_dim, positions, out.ctypes.data)
+    return out
+
+
+def kv_append_f16(k, v, pos0: int, rope=None, knorm=None):
+    n, h, d = k.shape
+    k, kp = _c(k, np.float16)
+    v, vp = _c(v, np.float16)
+    rope, rp = _c(rope, np.float16)
+    knorm, np_ = _c(knorm, np.float16)
+    ko = np.empty_like(k)
+    vo = np.empty_like(v)
+    lib().orc_kv_append_f16(kp, vp, n, h, d, pos0, rp, np_, ko.ctypes.data, vo.ctypes.data)
+    return ko, vo
+
+
+def kv_append_i8rec(k, v, pos0: int, rope=None, knorm=None) -> np.ndarray:
+    n, h, d = k.shape
+    k, kp = _c(k, np.float16)
+    v, vp = _c(v, np.float16)
+    rope, rp = _c(rope, np.float16)
+    knorm, np_ = _c(knorm, np.float16)
+    rec = np.empty((n, h, 2 * d + 8), dtype=np.uint8)
+    lib().orc_kv_append_i8rec(kp, vp, n, h, d, pos0, rp, np_, rec.ctypes.data)
+    return rec
+
+
+def quantize_v8(v, length: int | None = None):
+    length = v.shape[0] if length is None else length
+    _, h, d = v.shape
+    v, vp = _c(v[:length], np.float16)
+    nblk = (length + 63) // 64
+    v8 = np.empty((nblk * 64, h, d), dtype=np.int8)
+    sc = np.empty((nblk, h), dtype=np.float32)
+    lib().orc_quantize_v8(vp, length, h, d, v8.ctypes.data, sc.ctypes.data)
+    return v8, sc
+
+
+def quantize_p_u8(p):
+    p, pp = _c(p, np.float32)
+    rows, cols = p.shape
+    q = np.empty((rows, cols), dtype=np.uint8)
+    sc = np.empty((rows,), dtype=np.float32)
+    lib().orc_quantize_p_u8(pp, rows, cols, q.ctypes.data, sc.ctypes.data)
+    return q, sc
+
+
+def verify(q, K, V, ctx_len: int, window: int = 0, gate=None, splits: int = 1) -> np.ndarray:
+    m, qh, d = q.shape
+    kvh = K.shape[1]
+    q, qp = _c(q, np.float16)
+    K, kp = _c(K, np.float16)
+    V, vp = _c(V, np.float16)
+    gate, gp = _c(gate, np.float16)
+    out = np.empty((m, qh, d), dtype=np.float32)
+    lib().orc_verify(qp, m, qh, kvh, d, kp, vp, ctx_len, window, gp, splits, out.ctypes.data)
+    return out
+
+
+def attention_f64(q, qpos0: int, K, V, kv_len: int, window: int = 0, row_step: int = 1) -> np.ndarray:
+    nq, qh, d = q.shape
+    kvh = K.shape[1]
+    q, qp = _c(q, np.float16)
+    K, kp = _c(K, np.float16)
+    V, vp = _c(V, np.float16)
+    out = np.zeros((nq, qh, d), dtype=np.float32)
+    lib().orc_attention_f64(qp, nq, qpos0, qh, kvh, d, kp, vp, kv_len, window, row_step, out.ctypes.data)
+    return out
+
+
+def prefill_i8pv(q, context: int, K, V8, vscale, window: int = 0, row_step: int = 1) -> np.ndarray:
+    t, qh, d = q.shape
+    kvh = K.shape[1]
+    q, qp = _c(q, np.float16)
+    K, kp = _c(K, np.float16)
+    V8, v8p = _c(V8, np.int8)
+    vscale, sp = _c(vscale, np.float32)
+    out = np.zeros((t, qh, d), dtype=np.float32)
+    lib().orc_prefill_i8pv(qp, t, context, qh, kvh, d, kp, v8p, sp, window, row_step, out.ctypes.data)
+    return out
+
+
+def prefill_exact(q, context: int, K, V, window: int = 0, row_step: int = 1) -> np.ndarray:
+    t, qh, d = q.shape
+    kvh = K.shape[1]
+    q, qp = _c(q, np.float16)
+    K, kp = _c(K, np.float16)
+    V, vp = _c(V, np.float16)
+    out = np.zeros((t, qh, d), dtype=np.float32)
+    lib().orc_prefill_exact(qp, t, context, qh, kvh, d, kp, vp, window, row_step, out.ctypes.data)
+    return out
+
+
+def accept(best, tokens) -> int:
+    best, bp = _c(best, np.int32)
+    tokens, tp = _c(tokens, np.int32)
+    return lib().orc_accept(bp, tp, tokens.shape[0])

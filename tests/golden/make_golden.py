@@ -1,0 +1,194 @@
+"""Writes tests/golden/golden.npz: known-answer vectors for the bit-exact parts of the path, computed by
+an independent numpy restatement of the reference lines (not by the C++ oracle they check).
+
+The reference repository ships no golden vectors for these kernels, so these fixtures pin the oracle
+to a second, separately written restatement of the same source lines:
+  rope table       internal/model/engine.go:428-461 (buildRope)
+  fp16 append      kernels/ops.hip:186-200 (norm_rotate), :236-251 (kv_write) into fp16 K/V
+  int8 records     kernels/ops.hip:213-251 (quantize_pair, kv_write), 264-byte records at head_dim 128
+  int8 V blocks    the same quantiser per (kv head, 64-token block)
+  u8 P             kernels/prefill_attn.hip:305-331 (IEEE division in place of v_rcp_f32)
+  accept           kernels/dspark.hip:2851-2860
+Run: python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import math
+import pathlib
+import sys
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1] / "lfm3-1.7b-mi50_b200"))
+import synth  # noqa: E402  (the seeded generator of the benchmark inputs)
+
+f32 = np.float32
+
+
+def f16(x):
+    return np.asarray(x, dtype=f32).astype(np.float16)
+
+
+def rope_rows(theta, factor, d, positions):
+    half, angles = d // 2, int(factor * d) // 2
+    inv = np.zeros(half, dtype=f32)
+    for i in range(angles):
+        e = f32(2 * i) / f32(d)
+        inv[i] = f32(1.0) / f32(math.pow(theta, float(e)))
+    out = np.zeros((len(positions), d), dtype=np.float16)
+    for r, p in enumerate(positions):
+        t = f32(p)
+        for i in range(half):
+            f = float(f32(t * inv[i]))
+            out[r, i] = np.float16(f32(math.cos(f)))
+            out[r, half + i] = np.float16(f32(math.sin(f)))
+    return out
+
+
+def norm_rope(k, pos0, rope, knorm):
+    """k: [n][h][d] float16 -> stored fp16; rope: full table [positions][d] or None; knorm [d] or None."""
+    n, h, d = k.shape
+    half, J = d // 2, d // 64
+    x = k.astype(f32)
+    a = np.stack([x[..., 32 * j:32 * j + 32] for j in range(J)], axis=-2)                 # [n][h][J][32]
+    b = np.stack([x[..., half + 32 * j:half + 32 * j + 32] for j in range(J)], axis=-2)
+    if knorm is not None:
+        lanes = a[..., 0, :] * a[..., 0, :] + b[..., 0, :] * b[..., 0, :]
+        for j in range(1, J):
+            lanes = lanes + (a[..., j, :] * a[..., j, :] + b[..., j, :] * b[..., j, :])
+        for o in (16, 8, 4, 2, 1):
+            lanes = lanes + lanes[..., np.arange(32) ^ o]
+        ss = lanes[..., 0]
+        inv = f32(1.0) / np.sqrt(ss / f32(d) + f32(1e-5))
+        w = knorm.astype(f32)
+        wa = np.stack([w[32 * j:32 * j + 32] for j in range(J)])
+        wb = np.stack([w[half + 32 * j:half + 32 * j + 32] for j in range(J)])
+        a = f16((a * inv[..., None, None]) * wa).astype(f32)
+        b = f16((b * inv[..., None, None]) * wb).astype(f32)
+    if rope is not None:
+        rows = rope[pos0:pos0 + n].astype(f32)                                             # [n][d]
+        c = np.stack([rows[:, 32 * j:32 * j + 32] for j in range(J)], axis=-2)[:, None]    # [n][1][J][32]
+        s = np.stack([rows[:, half + 32 * j:half + 32 * j + 32] for j in range(J)], axis=-2)[:, None]
+        ra = f16(a * c - b * s).astype(f32)
+        rb = f16(b * c + a * s).astype(f32)
+        a, b = ra, rb
+    out = np.zeros((n, h, d), dtype=np.float16)
+    for j in range(J):
+        out[..., 32 * j:32 * j + 32] = f16(a[..., j, :])
+        out[..., half + 32 * j:half + 32 * j + 32] = f16(b[..., j, :])
+    return out
+
+
+def quant_half_away(x, inv):
+    q = x.astype(f32) * inv
+    q = np.where(q >= 0, q + f32(0.5), q - f32(0.5)).astype(f32)
+    return np.trunc(np.clip(q, f32(-128), f32(127))).astype(np.int8)
+
+
+def i8_records(kst, v):
+    n, h, d = kst.shape
+    rec = np.zeros((n, h, 2 * d + 8), dtype=np.uint8)
+    for part, src in enumerate((kst.astype(f32), v.astype(f32))):
+        amax = np.abs(src).max(axis=-1)
+        scale = np.maximum(amax / f32(127), f32(1e-6)).astype(f32)
+        inv = (f32(1) / scale).astype(f32)
+        q = quant_half_away(src, inv[..., None])
+        off = part * (d + 4)
+        rec[..., off:off + d] = q.view(np.uint8)
+        rec[..., off + d:off + d + 4] = scale[..., None].view(np.uint8).reshape(n, h, 4)
+    return rec
+
+
+def v8_blocks(v, length):
+    _, h, d = v.shape
+    nblk = (length + 63) // 64
+    v8 = np.zeros((nblk * 64, h, d), dtype=np.int8)
+    sc = np.zeros((nblk, h), dtype=f32)
+    for b in range(nblk):
+        t0, t1 = 64 * b, min(length, 64 * b + 64)
+        blk = v[t0:t1].astype(f32)
+        amax = np.abs(blk).max(axis=(0, 2))
+        scale = np.maximum(amax / f32(127), f32(1e-6)).astype(f32)
+        inv = (f32(1) / scale).astype(f32)
+        sc[b] = scale
+        v8[t0:t1] = quant_half_away(blk, inv[None, :, None])
+    return v8, sc
+
+
+def p_u8(p):
+    pm = p.max(axis=1).astype(f32)
+    inv = (f32(255) / np.maximum(pm, f32(1e-30))).astype(f32)
+    x = (p * inv[:, None]).astype(f32)
+    q = np.clip(np.rint(x), 0, 255).astype(np.uint8)
+    return q, (pm * f32(1.0 / 255.0)).astype(f32)
+
+
+def accept(best, tokens):
+    acc = 0
+    for t in range(len(tokens) - 1):
+        if best[t] != tokens[t + 1]:
+            break
+        acc += 1
+    return acc + 1
+
+
+def main():
+    g = {}
+    # RoPE tables: the benchmark's (theta 1e6, all 32 pairs, D 64) and the reference model's two.
+    pos = np.array([0, 1, 2, 31, 1023, 1024, 1031, 32767, 32783, 131071, 131087])
+    g["rope_1e6_f1_d64_pos"] = pos
+    g["rope_1e6_f1_d64"] = rope_rows(1e6, 1.0, 64, pos)
+    g["rope_1e6_f05_d128"] = rope_rows(1e6, 0.5, 128, pos)
+    g["rope_1e4_f1_d128"] = rope_rows(1e4, 1.0, 128, pos)
+
+    # fp16 append, config 1 (seed 0): 8 drafts at positions 1024.. with RoPE theta 1e6.
+    case = synth.verify_case(0, 1024, 8)
+    table = rope_rows(1e6, 1.0, 64, np.arange(1032))
+    g["c1_newK"], g["c1_newV"] = case["newK"], case["newV"]
+    g["c1_K_rope"] = norm_rope(case["newK"], 1024, table, None)
+    # Same drafts with a k-norm weight vector.
+    s = synth.Stream(100)
+    knorm64 = f16(1.0 + 0.25 * s.normal(64))
+    g["knorm64"] = knorm64
+    g["c1_K_norm_rope"] = norm_rope(case["newK"], 1024, table, knorm64)
+
+    # Reference-geometry int8 records: 16/4/128, theta 1e6 factor 0.5, 5 tokens at position 40.
+    s = synth.Stream(101)
+    k128 = s.normal_f16((5, 4, 128))
+    v128 = s.normal_f16((5, 4, 128))
+    knorm128 = f16(1.0 + 0.25 * s.normal(128))
+    table128 = rope_rows(1e6, 0.5, 128, np.arange(48))
+    g["rec_k"], g["rec_v"], g["knorm128"] = k128, v128, knorm128
+    g["rec"] = i8_records(norm_rope(k128, 40, table128, knorm128), v128)
+
+    # int8 V per 64-token block: 100 tokens (one full block, one partial), a zero head to hit the floor.
+    s = synth.Stream(102)
+    vq = s.normal_f16((100, 8, 64))
+    vq[:, 3, :] = 0
+    g["v8_in"] = vq
+    g["v8"], g["v8_scale"] = v8_blocks(vq, 100)
+
+    # u8 P rows: random, exact ties at .5 after scaling, an all-zero row, a single spike.
+    s = synth.Stream(103)
+    p = np.abs(s.normal(16 * 64)).astype(f32).reshape(16, 64)
+    p[3] = 0
+    p[4] = 0
+    p[4, 7] = 1.0
+    p[5] = np.arange(64, dtype=f32) / f32(2.0)       # pm = 31.5, inv = 255/31.5
+    p[6] = f32(2.0) ** -40 * (np.arange(64, dtype=f32) + 1)
+    g["p_in"] = p
+    g["p_q"], g["p_sc"] = p_u8(p)
+
+    # accept
+    best = np.array([5, 6, 7, 9, 1, 2, 3, 4], dtype=np.int32)
+    toks = np.array([4, 5, 6, 7, 8, 9, 9, 9], dtype=np.int32)
+    g["acc_best"], g["acc_tokens"] = best, toks
+    g["acc_commit"] = np.array([accept(best, toks), accept(best[:1], toks[:1]), accept(best, np.array([4, 0, 0, 0, 0, 0, 0, 0]))])
+
+    np.savez_compressed(HERE / "golden.npz", **g)
+    print("wrote", HERE / "golden.npz", sum(v.nbytes for v in g.values()), "bytes raw")
+
+
+if __name__ == "__main__":
+    main()

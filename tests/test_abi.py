@@ -1,0 +1,101 @@
+"""The C-ABI library on CPU: it loads, exports every symbol include/lfm3attn.h declares, and its host-side
+logic (layouts, RoPE table, argument checks) behaves. No kernel runs here."""
+import ctypes
+import pathlib
+import re
+
+import numpy as np
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "lfm3attn.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(lfm3a_\w+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported(la):
+    names = declared_functions()
+    assert len(names) >= 15
+    handle = ctypes.CDLL(str(la.LIB_PATH))
+    missing = [n for n in names if not hasattr(handle, n)]
+    assert not missing, missing
+    assert set(names) <= set(la.SIGNATURES), set(names) - set(la.SIGNATURES)
+
+
+def test_version_and_strings(la):
+    assert la.lib().lfm3a_version() == 1
+    assert la.lib().lfm3a_strerror(-1) == b"invalid argument"
+    assert la.lib().lfm3a_strerror(-7).startswith(b"a kernel gave up")
+
+
+@pytest.mark.parametrize("mode,h,d,head,block", [(0, 8, 64, 10368, 82944), (0, 4, 128, 20608, 82432),
+                                                 (1, 4, 128, 264, 33792), (1, 8, 64, 136, 34816)])
+def test_layouts(la, mode, h, d, head, block):
+    lay = la.layout(mode, h, d)
+    assert (lay.head_bytes, lay.block_bytes) == (head, block)
+    assert lay.head_bytes % 128 == 0 or mode == 1
+
+
+def test_layout_rejects(la):
+    with pytest.raises(la.LFM3AError) as e:
+        la.layout(0, 8, 96)
+    assert e.value.code == la.ENOTSUP
+    with pytest.raises(la.LFM3AError):
+        la.layout(0, 8, 64, block_tokens=16)
+    with pytest.raises(la.LFM3AError):
+        la.layout(7, 8, 64)
+
+
+@pytest.mark.parametrize("theta,factor,d", [(1e6, 1.0, 64), (1e6, 0.5, 128), (1e4, 1.0, 128)])
+def test_rope_table_matches_oracle(la, orc, theta, factor, d):
+    n = 4096
+    got = la.rope_table(theta, factor, d, n)
+    want = orc.rope_table(theta, factor, d, n).view(np.uint16)
+    assert np.array_equal(got, want)
+
+
+def test_argument_checks_without_device(la):
+    lib = la.lib()
+    view = la.KvView(None, None, 0, la.layout(0, 8, 64))
+    assert lib.lfm3a_kv_append(ctypes.byref(view), None, None, 0, 0, 1, None, None, None) == la.EINVAL
+    good = la.KvView(64, 64, 10, la.layout(0, 8, 64))
+    bad_geom = la.KvView(64, 64, 10, la.layout(0, 4, 128))
+    assert lib.lfm3a_verify_attention(ctypes.byref(bad_geom), 64, 16, 16, 100, 0, None, 64, None, 0, 1, None) == la.ENOTSUP
+    assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 16, 100, 0, None, 64, None, 0, 1, None) == la.ENOTSUP
+    assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 40, 32, 100, 0, None, 64, None, 0, 1, None) == la.EINVAL
+    assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 32, 100, 0, None, 64, None, 0, 4, None) == la.EINVAL
+    assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 32, 1000, 0, None, 64, 64, 16, 4, None) == la.EWORKSPACE
+    assert lib.lfm3a_verify_partial(ctypes.byref(good), 64, 16, 32, 500, 400, 1000, 0, 64, None, 0, 1, None) == la.EINVAL
+    assert lib.lfm3a_combine(None, 4, 2, 64, 0, 0, None, 64, None) == la.EINVAL
+    assert lib.lfm3a_kv_truncate(ctypes.byref(good), -1, None) == la.EINVAL
+    assert b"negative" in lib.lfm3a_last_error()
+    lay = la.layout(0, 8, 64)
+    view_bad_stride = la.KvView(64, 64, 10, la.KvLayout(0, 8, 64, 32, 10000, 80000))
+    assert lib.lfm3a_kv_truncate(ctypes.byref(view_bad_stride), 5, None) == la.EINVAL
+    assert lay.head_bytes == 10368
+
+
+def test_split_choice(la):
+    lay = la.layout(0, 8, 64)
+    assert la.verify_splits(lay, 32768, 16, 0, 148) == 37
+    assert la.verify_splits(lay, 131072, 16, 0, 148) == 37
+    assert la.verify_splits(lay, 100, 8, 0, 148) == 2
+    assert la.verify_splits(lay, 20, 8, 0, 148) == 1
+    assert la.verify_splits(lay, 1024, 8, 0, 148) == 16
+    ws = la.lib().lfm3a_verify_workspace_bytes(16, 32, 64, 37)
+    assert ws == 16 * 32 * 37 * 66 * 4
+
+
+def test_synth_generator_is_deterministic(synth):
+    a = synth.Stream(3).normal_f16((1000,))
+    s = synth.Stream(3)
+    b = np.concatenate([s.normal_f16((400,)), s.normal_f16((600,))])
+    assert np.array_equal(a.view(np.uint16), b.view(np.uint16))
+    z = synth.Stream(0).normal(200000)
+    assert abs(z.mean()) < 0.01 and abs(z.std() - 1) < 0.01
+    keep = synth.geometric_keep(4, 256)
+    assert keep.min() >= 1 and keep.max() <= 16 and 2.5 < keep.mean() < 4.0

@@ -1,0 +1,115 @@
+"""DSpark verify attention on the GPU against the oracle (same arithmetic) and exact fp64 attention.
+Tolerance: max |gpu - reference| <= 2e-3 x RMS(reference) (fp16 probabilities, fp32 accumulation)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def dev(a, cuda):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def rel_err(got, want):
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    return float(np.max(np.abs(got.astype(np.float64) - want))) / rms
+
+
+def setup(la, orc, synth, cuda, seed, ctx_len, m, window=0, theta=1e6):
+    case = synth.verify_case(seed, ctx_len, m)
+    cache = la.LayerCache(la.MODE_F16, 8, 64, ctx_len + m + 64, device=cuda)
+    rope_np = la.rope_table(theta, 1.0, 64, ctx_len + m + 1)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    cache.append(dev(case["newK"], cuda), dev(case["newV"], cuda), ctx_len, rope=dev(rope_np.view(np.float16), cuda))
+    k_new, v_new = orc.kv_append_f16(case["newK"], case["newV"], ctx_len, rope=rope_np.view(np.float16))
+    K = np.concatenate([case["K"], k_new])
+    V = np.concatenate([case["V"], v_new])
+    return case, cache, K, V
+
+
+@pytest.mark.parametrize("splits", [1, 0, 7])
+def test_verify_c1(la, orc, synth, cuda, splits):
+    case, cache, K, V = setup(la, orc, synth, cuda, 0, 1024, 8)
+    out = cache.verify(dev(case["Q"], cuda), 1024, splits=splits)
+    la.sync()
+    got = out.float().cpu().numpy()
+    assert rel_err(got, orc.verify(case["Q"], K, V, 1024, splits=max(splits, 1))) < TOL
+    assert rel_err(got, orc.attention_f64(case["Q"], 1024, K, V, 1032)) < TOL
+
+
+@pytest.mark.parametrize("m", [1, 3, 9, 16, 17, 32])
+def test_verify_token_counts(la, orc, synth, cuda, m):
+    case, cache, K, V = setup(la, orc, synth, cuda, 20 + m, 2000, m)
+    out = cache.verify(dev(case["Q"], cuda), 2000)
+    la.sync()
+    got = out.float().cpu().numpy()
+    assert rel_err(got, orc.attention_f64(case["Q"], 2000, K, V, 2000 + m)) < TOL
+
+
+def test_verify_window_gate(la, orc, synth, cuda):
+    case, cache, K, V = setup(la, orc, synth, cuda, 30, 5000, 16)
+    gate = synth.Stream(31).normal_f16((16, 32))
+    out = cache.verify(dev(case["Q"], cuda), 5000, window=256, gate=dev(gate, cuda))
+    la.sync()
+    got = out.float().cpu().numpy()
+    want = orc.attention_f64(case["Q"], 5000, K, V, 5016, window=256)
+    sig = 1.0 / (1.0 + np.exp(-gate.astype(np.float64)))
+    assert rel_err(got, want * sig[..., None]) < TOL
+
+
+@pytest.mark.parametrize("ctx_len", [0, 5, 31, 32, 33, 100])
+def test_verify_short_contexts(la, orc, synth, cuda, ctx_len):
+    case, cache, K, V = setup(la, orc, synth, cuda, 40 + ctx_len, ctx_len, 16)
+    out = cache.verify(dev(case["Q"], cuda), ctx_len)
+    la.sync()
+    got = out.float().cpu().numpy()
+    assert rel_err(got, orc.attention_f64(case["Q"], ctx_len, K, V, ctx_len + 16)) < TOL
+
+
+def test_verify_c2_full_size(la, orc, synth, cuda):
+    """Config 2 at full size: 32768 cached tokens, 16 drafts (seed 1)."""
+    case, cache, K, V = setup(la, orc, synth, cuda, 1, 32768, 16)
+    out = cache.verify(dev(case["Q"], cuda), 32768)
+    la.sync()
+    got = out.float().cpu().numpy()
+    assert rel_err(got, orc.attention_f64(case["Q"], 32768, K, V, 32784)) < TOL
+
+
+def test_verify_lifecycle_small(la, orc, synth, cuda):
+    """Append 16 drafts, verify, keep n and roll back the rest, 12 times; the cache matches the oracle's."""
+    s = synth.Stream(50)
+    ctx = 700
+    k0 = s.normal_f16((ctx, 8, 64))
+    v0 = s.normal_f16((ctx, 8, 64))
+    cache = la.LayerCache(la.MODE_F16, 8, 64, ctx + 16 * 13, device=cuda)
+    rope_np = la.rope_table(1e6, 1.0, 64, ctx + 16 * 13)
+    rope = dev(rope_np.view(np.float16), cuda)
+    cache.append(dev(k0, cuda), dev(v0, cuda), 0)
+    K, V = k0.copy(), v0.copy()
+    keep = synth.geometric_keep(4, 12)
+    for step in range(12):
+        nk = s.normal_f16((16, 8, 64))
+        nv = s.normal_f16((16, 8, 64))
+        q = s.normal_f16((16, 32, 64))
+        L = cache.length
+        cache.append(dev(nk, cuda), dev(nv, cuda), L, rope=rope)
+        out = cache.verify(dev(q, cuda), L)
+        ko, vo = orc.kv_append_f16(nk, nv, L, rope=rope_np.view(np.float16))
+        Kf, Vf = np.concatenate([K, ko]), np.concatenate([V, vo])
+        la.sync()
+        assert rel_err(out.float().cpu().numpy(), orc.attention_f64(q, L, Kf, Vf, L + 16)) < TOL
+        n = int(keep[step])
+        cache.truncate(L + n)
+        K, V = Kf[:L + n], Vf[:L + n]
+    la.sync()
+    got = cache.logical()
+    assert got["K"].shape[0] == ctx + int(keep.sum())
+    assert np.array_equal(got["K"].view(np.uint16), K.view(np.uint16))
+    assert np.array_equal(got["V"].view(np.uint16), V.view(np.uint16))
+    v8, sc = orc.quantize_v8(V, V.shape[0])
+    assert np.array_equal(got["V8"], v8)
+    assert np.array_equal(got["vscale"].view(np.uint32), sc.view(np.uint32))

@@ -1,0 +1,77 @@
+"""The C++ oracle against the golden vectors of tests/golden (an independent numpy restatement)."""
+import pathlib
+
+import numpy as np
+import pytest
+
+GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "golden.npz"
+
+
+@pytest.fixture(scope="module")
+def g():
+    return np.load(GOLDEN)
+
+
+def bits(a):
+    return np.asarray(a).view(np.uint16)
+
+
+def test_fp16_rounding(orc):
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.normal(size=20000).astype(np.float32) * 10.0 ** rng.integers(-9, 6, 20000),
+                        np.float32([0.0, -0.0, 65504.0, 65520.0, 1e-8, -6e-8, 2.0 ** -24, 3 * 2.0 ** -25, np.inf, -np.inf])])
+    want = x.astype(np.float16).view(np.uint16)
+    got = np.array([orc.lib().orc_f32_to_f16(float(v)) for v in x], dtype=np.uint16)
+    assert np.array_equal(got, want)
+    back = np.array([orc.lib().orc_f16_to_f32(int(b)) for b in want[:2000]], dtype=np.float32)
+    assert np.array_equal(back, want[:2000].view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("name,theta,factor,d", [("rope_1e6_f1_d64", 1e6, 1.0, 64), ("rope_1e6_f05_d128", 1e6, 0.5, 128),
+                                                 ("rope_1e4_f1_d128", 1e4, 1.0, 128)])
+def test_rope_table(orc, g, name, theta, factor, d):
+    pos = g["rope_1e6_f1_d64_pos"]
+    table = orc.rope_table(theta, factor, d, int(pos.max()) + 1)
+    assert np.array_equal(bits(table[pos]), bits(g[name]))
+
+
+def test_append_f16_rope(orc, g):
+    table = orc.rope_table(1e6, 1.0, 64, 1032)
+    k, v = orc.kv_append_f16(g["c1_newK"], g["c1_newV"], 1024, rope=table)
+    assert np.array_equal(bits(k), bits(g["c1_K_rope"]))
+    assert np.array_equal(bits(v), bits(g["c1_newV"]))
+
+
+def test_append_f16_norm_rope(orc, g):
+    table = orc.rope_table(1e6, 1.0, 64, 1032)
+    k, _ = orc.kv_append_f16(g["c1_newK"], g["c1_newV"], 1024, rope=table, knorm=g["knorm64"])
+    assert np.array_equal(bits(k), bits(g["c1_K_norm_rope"]))
+
+
+def test_append_i8_records(orc, g):
+    table = orc.rope_table(1e6, 0.5, 128, 48)
+    rec = orc.kv_append_i8rec(g["rec_k"], g["rec_v"], 40, rope=table, knorm=g["knorm128"])
+    assert rec.shape[-1] == 264
+    assert np.array_equal(rec, g["rec"])
+
+
+def test_v8_blocks(orc, g):
+    v8, sc = orc.quantize_v8(g["v8_in"], 100)
+    assert np.array_equal(v8, g["v8"])
+    assert np.array_equal(sc.view(np.uint32), g["v8_scale"].view(np.uint32))
+    assert np.all(sc[:, 3] == np.float32(1e-6))
+
+
+def test_p_u8(orc, g):
+    q, sc = orc.quantize_p_u8(g["p_in"])
+    assert np.array_equal(q, g["p_q"])
+    assert np.array_equal(sc.view(np.uint32), g["p_sc"].view(np.uint32))
+    assert q[3].max() == 0 and q[4, 7] == 255
+
+
+def test_accept(orc, g):
+    best, toks = g["acc_best"], g["acc_tokens"]
+    want = g["acc_commit"]
+    assert orc.accept(best, toks) == want[0]
+    assert orc.accept(best[:1], toks[:1]) == want[1]
+    assert orc.accept(best, np.array([4, 0, 0, 0, 0, 0, 0, 0], dtype=np.int32)) == want[2]

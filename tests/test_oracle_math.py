@@ -1,0 +1,73 @@
+"""The oracle's restated attention arithmetic against exact fp64 attention, at sizes it finishes in seconds."""
+import numpy as np
+import pytest
+
+
+def rel_err(got, want):
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    return float(np.max(np.abs(got.astype(np.float64) - want))) / rms
+
+
+def build_cache(orc, case, ctx_len, m, theta=1e6):
+    table = orc.rope_table(theta, 1.0, 64, ctx_len + m)
+    k_new, v_new = orc.kv_append_f16(case["newK"], case["newV"], ctx_len, rope=table)
+    K = np.concatenate([case["K"], k_new])
+    V = np.concatenate([case["V"], v_new])
+    return K, V
+
+
+@pytest.mark.parametrize("splits", [1, 3, 16])
+def test_verify_c1_matches_fp64(orc, synth, splits):
+    case = synth.verify_case(0, 1024, 8)
+    K, V = build_cache(orc, case, 1024, 8)
+    got = orc.verify(case["Q"], K, V, 1024, splits=splits)
+    want = orc.attention_f64(case["Q"], 1024, K, V, 1032)
+    assert rel_err(got, want) < 2e-3
+
+
+def test_verify_window_and_gate(orc, synth):
+    case = synth.verify_case(5, 700, 5)
+    K, V = build_cache(orc, case, 700, 5)
+    gate = synth.Stream(9).normal_f16((5, 32))
+    got = orc.verify(case["Q"], K, V, 700, window=256, gate=gate, splits=4)
+    want = orc.attention_f64(case["Q"], 700, K, V, 705, window=256)
+    sig = 1.0 / (1.0 + np.exp(-gate.astype(np.float64)))
+    assert rel_err(got, want * sig[..., None]) < 2e-3
+
+
+def test_verify_split_invariance(orc, synth):
+    case = synth.verify_case(1, 3000, 16)
+    K, V = build_cache(orc, case, 3000, 16)
+    a = orc.verify(case["Q"], K, V, 3000, splits=1)
+    b = orc.verify(case["Q"], K, V, 3000, splits=37)
+    assert rel_err(b, a) < 1e-3
+
+
+@pytest.mark.parametrize("context,window", [(0, 0), (96, 0), (160, 100)])
+def test_prefill_exact_and_i8_match_fp64(orc, synth, context, window):
+    t = 200
+    case = synth.prefill_case(3, context + t)
+    K, V, Q = case["K"], case["V"], case["Q"][context:]
+    V8, vs = orc.quantize_v8(V, context + t)
+    want = orc.attention_f64(Q, context, K, V, context + t, window=window)
+    ex = orc.prefill_exact(Q, context, K, V, window=window)
+    # fp16 probabilities carry a 2^-11 relative rounding each: a few 1e-3 of the output RMS against fp64.
+    assert rel_err(ex, want) < 4e-3
+    # The int8 arithmetic is checked against fp64 attention over the dequantised int8 V: what remains is
+    # the u8 rounding of the probabilities (per row and 64-key tile), up to ~8% of the output RMS at
+    # worst and far less on average. The 2e-2 bar applies between implementations of the same arithmetic.
+    i8 = orc.prefill_i8pv(Q, context, K, V8, vs, window=window)
+    n = context + t
+    v_dq = (V8[:n].astype(np.float32) * np.repeat(vs, 64, axis=0)[:n, :, None]).astype(np.float16)
+    want_dq = orc.attention_f64(Q, context, K, v_dq, n, window=window)
+    rms = float(np.sqrt(np.mean(want_dq.astype(np.float64) ** 2)))
+    assert rel_err(i8, want_dq) < 0.15
+    assert float(np.mean(np.abs(i8 - want_dq))) / rms < 5e-3
+
+
+def test_prefill_row_sampling(orc, synth):
+    case = synth.prefill_case(4, 300)
+    full = orc.prefill_exact(case["Q"], 0, case["K"], case["V"])
+    some = orc.prefill_exact(case["Q"], 0, case["K"], case["V"], row_step=7)
+    assert np.array_equal(full[::7], some[::7])
+    assert not some[1].any()
