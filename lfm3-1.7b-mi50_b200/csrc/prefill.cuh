@@ -1,5 +1,19 @@
-// Prefill attention (MODE_F16, head_dim 64) and the u8 quantiser of softmax rows it shares with the
-// lfm3a_quantize_p_u8 test hook.
+// Prefill attention on the 5th-generation tensor cores (MODE_F16, head_dim 64, 4 query heads per kv head),
+// and the u8 quantiser of softmax rows it shares with the lfm3a_quantize_p_u8 test hook.
+//
+// One CTA = 32 query tokens x one kv head = 128 query rows (row r = 4 t + j: token t0 + t, query head
+// 4 h + j; prefill_attn.hip:3-5), against 64-key tiles aligned to 64 (the int8 V block). Warps:
+//   0-3  softmax, thread = row: TMEM -> registers (tcgen05.ld), mask, lazy running max (rescale only when
+//        a tile beats it by 2^8, prefill_attn.hip:33,278-304), p = 2^(s - m); exact: P fp16 -> smem;
+//        int8: P' = p x v_scale quantised to u8 per row and tile (prefill_attn.hip:305-331) -> smem, and
+//        acc += scale x (int32 PV) in registers one tile later;
+//   4    producer: bulk copies of the K and V (or int8 V) sections of the tile's two 32-token pages;
+//   5    MMA issuer (one thread): S = Q K^T (kind::f16, M128 N64, 4 k-steps) into TMEM, then the previous
+//        tile's PV: exact O += P V (kind::f16, O stays in TMEM), int8 Dpv = P8 V8 (kind::i8, s32 in TMEM).
+// QK of tile j is issued before PV of tile j - 1, so the softmax of j - 1 overlaps the QK of j.
+// TMEM columns: S[2] at 0 and 64; O (exact) at 128, or Dpv[2] (int8) at 128 and 192.
+// Every operand sits in shared memory as 8-row x 16-byte core tiles (no swizzle, K-major); the page
+// sections are already in that order, so a page moves with plain bulk copies.
 #pragma once
 #include "common.cuh"
 #include "kv.cuh"
@@ -40,8 +54,426 @@ __global__ __launch_bounds__(128) void quantize_p_rows_kernel(const float* p, in
   for (int i = 0; i < 16; ++i) reinterpret_cast<uint32_t*>(q + (int64_t)r * 64)[i] = w[i];
 }
 
-inline int launch_prefill(const KvGeom&, const __half*, int, int, int, int, bool, __half*, cudaStream_t) {
-  return LFM3A_ENOTSUP;
+struct PrefillArgs {
+  KvGeom g;
+  const __half* q;   // [T][QH][64]
+  __half* out;       // [T][QH][64]
+  int T, q_heads, context, window, qtiles;
+  float qk_scale;    // (1 / sqrt(64)) * log2(e)
+};
+
+constexpr int kPfThreads = 192;
+constexpr int kPfStages = 3;
+constexpr int kPfQBytes = 16384;   // 128 rows x 64 dims fp16
+
+template <bool I8>
+struct PfLayout {
+  static constexpr int kStage = I8 ? 12288 : 16384;   // K (2 pages) | V (2 pages) or int8 V (2 pages)
+  static constexpr int kPBuf = I8 ? 8192 : 16384;     // 128 rows x 64 keys, u8 or fp16
+  static constexpr int kOffStage = kPfQBytes;
+  static constexpr int kOffP = kOffStage + kPfStages * kStage;
+  static constexpr int kOffBar = kOffP + 2 * kPBuf;
+  static constexpr int kBars = 2 * kPfStages + 4 * 2 + 2;
+  static constexpr int kOffTmemSlot = kOffBar + kBars * 8;
+  static constexpr int kBytes = kOffTmemSlot + 16;
+  // Request enough shared memory that two CTAs share an SM and a third cannot (TMEM holds 2 x 256 columns).
+  static constexpr int kRequest = kBytes > 80 * 1024 ? kBytes : 80 * 1024;
+};
+
+template <bool I8>
+__global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
+  using L = PfLayout<I8>;
+  constexpr int NS = kPfStages;
+  constexpr uint32_t kTmemCols = 256;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ int s_abort;
+  uint8_t* sQ = smem;
+  uint8_t* sStage = smem + L::kOffStage;
+  uint8_t* sP = smem + L::kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + NS;
+  uint64_t* s_full = bars + 2 * NS;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* q_ready = pv_done + 2;
+  uint64_t* drain = q_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffTmemSlot);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = a.qtiles - 1 - blockIdx.x;   // the longest rows first
+  const int h = blockIdx.y;
+  const int t0 = qt * 32, ntok = min(32, a.T - t0);
+  const int qfirst = a.context + t0, qlast = qfirst + ntok - 1, kend = qlast + 1;
+  const int kbegin = a.window > 0 ? max(0, qfirst - a.window + 1) : 0;
+  const int kt_begin = kbegin / kQuantBlock * kQuantBlock;
+  const int ntiles = (kend - kt_begin + kQuantBlock - 1) / kQuantBlock;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 4);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&pv_done[b], 1);
+    }
+    mbar_init(q_ready, 4);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    // ================================================================ softmax warps, thread = query row
+    const int r = threadIdx.x, t = r >> 2, j = r & 3;
+    const bool row_ok = t < ntok;
+    const int qpos = qfirst + t;
+    const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
+    // Q row -> core tiles: row r, dims 8c .. 8c + 7 at ((r / 8) * 8 + c) * 128 + (r % 8) * 16.
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(a.q + grow * 64);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    float acc[I8 ? 64 : 1];
+    float sc_prev = 0.f;
+    if (I8) {
+#pragma unroll
+      for (int d = 0; d < (I8 ? 64 : 1); ++d) acc[d] = 0.f;
+    }
+    // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
+    bool ok = true;
+    for (int jt = 0; jt < ntiles && ok; ++jt) {
+      const int b = jt & 1, k0 = kt_begin + jt * kQuantBlock;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(jt >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[64];
+      {
+        uint32_t rr[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld16(lane_base + b * 64 + c * 16, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[e]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
+
+      const bool interior = ntok == 32 && k0 + kQuantBlock - 1 <= qfirst && (a.window == 0 || k0 > qlast - a.window);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 64; ++k) {
+        float v = x[k] * a.qk_scale;
+        if (!interior) {
+          const int kpos = k0 + k;
+          const bool valid = row_ok && kpos <= qpos && kpos >= kbegin && (a.window == 0 || kpos > qpos - a.window);
+          v = valid ? v : -INFINITY;
+        }
+        x[k] = v;
+        mx = fmaxf(mx, v);
+      }
+      const bool grow_max = mx > m_run + kLazy;
+      if (!I8) {
+        // O lives in TMEM: rescaling it needs the previous PV finished; rare after the first tiles.
+        if (__any_sync(0xffffffffu, grow_max)) {
+          const float corr = grow_max ? fast_exp2(m_run - mx) : 1.f;
+          if (grow_max) m_run = mx;
+          l_run *= corr;
+          if (jt >= 1) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
+              raise_error(kErrWaitMma);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t rr[16];
+              tmem_ld16(lane_base + 128 + c * 16, rr);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+              tmem_st16(lane_base + 128 + c * 16, rr);
+            }
+            tmem_wait_st();
+          }
+        }
+      } else if (grow_max) {
+        const float corr = fast_exp2(m_run - mx);
+        m_run = mx;
+        l_run *= corr;
+        sc_prev *= corr;   // the previous tile's PV is folded in later, already at the new max
+#pragma unroll
+        for (int d = 0; d < 64; ++d) acc[d] *= corr;
+      }
+#pragma unroll
+      for (int k = 0; k < 64; ++k) {
+        const float p = x[k] == -INFINITY ? 0.f : fast_exp2(x[k] - m_run);
+        x[k] = p;
+        l_run += p;
+      }
+      uint8_t* pb = sP + b * L::kPBuf;
+      if (!I8) {
+        // P[b] was last read by PV(jt - 2).
+        if (jt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
+          raise_error(kErrWaitMma);
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 v;
+          v.x = pack_half2(x[8 * c], x[8 * c + 1]);
+          v.y = pack_half2(x[8 * c + 2], x[8 * c + 3]);
+          v.z = pack_half2(x[8 * c + 4], x[8 * c + 5]);
+          v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
+          *reinterpret_cast<uint4*>(pb + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+        }
+      } else {
+        // P' = p x v_scale of the tile's 64-token block (kept in the block's first page).
+        const char* sec = a.g.pool + phys_block(a.g, k0 / kBlockTokens) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+        const float vs = *reinterpret_cast<const float*>(sec + F16Section<64>::kOffScale);
+#pragma unroll
+        for (int k = 0; k < 64; ++k) x[k] = __fmul_rn(x[k], vs);
+        uint32_t q8[16];
+        const float sc = quantize_p_row<64>(x, q8);
+        // P8[b] was last read by PV(jt - 2), whose completion the previous epilogue waited for.
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(pb + ((r >> 3) * 4 + c) * 128 + (r & 7) * 16) =
+              make_uint4(q8[4 * c], q8[4 * c + 1], q8[4 * c + 2], q8[4 * c + 3]);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[b]);
+        // Epilogue of the previous tile: acc += scale x (int32 sum of u8 P x int8 V).
+        if (jt >= 1) {
+          const int bp = (jt - 1) & 1;
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[bp], (uint32_t)((jt - 1) >> 1) & 1u))) {
+            raise_error(kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t rr[16];
+            tmem_ld16(lane_base + 128 + bp * 64 + c * 16, rr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[c * 16 + e] = fmaf((float)(int32_t)rr[e], sc_prev, acc[c * 16 + e]);
+          }
+          tc_fence_before();
+        }
+        sc_prev = sc;
+        continue;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    if (!ok) {
+      atomicExch(&s_abort, 1);
+    } else {
+      const int last = ntiles - 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[last & 1], (uint32_t)(last >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        atomicExch(&s_abort, 1);
+      } else {
+        tc_fence_after();
+        float o[64];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rr[16];
+          tmem_ld16(lane_base + 128 + (I8 ? (last & 1) * 64 : 0) + c * 16, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (I8) o[c * 16 + e] = fmaf((float)(int32_t)rr[e], sc_prev, acc[I8 ? c * 16 + e : 0]);
+            else o[c * 16 + e] = __uint_as_float(rr[e]);
+          }
+        }
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4 v;
+            v.x = pack_half2(o[8 * c] * inv, o[8 * c + 1] * inv);
+            v.y = pack_half2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+            v.z = pack_half2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+            v.w = pack_half2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+            dst[c] = v;
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ================================================================ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int jt = 0; jt < ntiles; ++jt) {
+        const int st = jt % NS;
+        if (jt >= NS && !mbar_wait(&empty[st], (uint32_t)((jt / NS) - 1) & 1u)) {
+          raise_error(kErrWaitEmpty);
+          atomicExch(&s_abort, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        const int k0 = kt_begin + jt * kQuantBlock;
+        const int lp0 = k0 / kBlockTokens;
+        // A second page wholly past the keys may have no table entry: copy the first page again (masked).
+        const int lp1 = (lp0 + 1) * kBlockTokens < kend ? lp0 + 1 : lp0;
+        const char* s0 = a.g.pool + phys_block(a.g, lp0) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+        const char* s1 = a.g.pool + phys_block(a.g, lp1) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+        uint8_t* dst = sStage + st * L::kStage;
+        mbar_arrive_expect_tx(&full[st], L::kStage);
+        bulk_g2s(dst, s0, 4096, &full[st]);
+        bulk_g2s(dst + 4096, s1, 4096, &full[st]);
+        if (!I8) {
+          bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV, 4096, &full[st]);
+          bulk_g2s(dst + 12288, s1 + F16Section<64>::kOffV, 4096, &full[st]);
+        } else {
+          bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV8, 2048, &full[st]);
+          bulk_g2s(dst + 10240, s1 + F16Section<64>::kOffV8, 2048, &full[st]);
+        }
+        issued = jt + 1;
+      }
+      // On an abort, wait (bounded) for the copies still landing in shared memory.
+      if (*reinterpret_cast<volatile int*>(&s_abort)) {
+        for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
+      }
+    }
+  } else {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_ready, 0);
+      if (!ok) raise_error(kErrWaitOther);
+      const uint32_t q_addr = smem_u32(sQ);
+      for (int jt = 0; jt <= ntiles && ok; ++jt) {
+        if (jt < ntiles) {
+          const int st = jt % NS, b = jt & 1;
+          if (!mbar_wait(&full[st], (uint32_t)(jt / NS) & 1u) ||
+              (jt >= 2 && !mbar_wait(&s_free[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
+            raise_error(kErrWaitFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sStage + st * L::kStage);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f16_ss(tmem + b * 64, umma_desc(q_addr + ks * 256, 128, 1024), umma_desc(k_addr + ks * 256, 128, 1024),
+                        kIdescF16M128N64, ks > 0 ? 1u : 0u);
+          umma_commit(&s_full[b]);
+        }
+        if (jt >= 1) {
+          const int jp = jt - 1, bp = jp & 1, stp = jp % NS;
+          if (!mbar_wait(&p_full[bp], (uint32_t)(jp >> 1) & 1u)) {
+            raise_error(kErrWaitOther);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t p_addr = smem_u32(sP + bp * L::kPBuf);
+          const uint32_t v_addr = smem_u32(sStage + stp * L::kStage + 8192);
+          if (!I8) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma_f16_ss(tmem + 128, umma_desc(p_addr + ks * 256, 128, 1024),
+                          umma_desc(v_addr + (ks >> 1) * 4096 + (ks & 1) * 256, 128, 512), kIdescF16M128N64,
+                          (jp > 0 || ks > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+              umma_i8_ss(tmem + 128 + bp * 64, umma_desc(p_addr + ks * 256, 128, 512),
+                         umma_desc(v_addr + ks * 2048, 128, 256), kIdescI8M128N64, ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stp]);
+          umma_commit(&pv_done[bp]);
+        }
+      }
+      // Leave no tensor-core work in flight behind an abort.
+      umma_commit(drain);
+      mbar_wait(drain, 0);
+      if (!ok) atomicExch(&s_abort, 1);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st) {
+  static bool done[2][64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LFM3A_ECUDA;
+  const dim3 grid(a.qtiles, a.g.kv_heads);
+  if (i8) {
+    if (!done[1][dev]) {
+      if (cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PfLayout<true>::kRequest) != cudaSuccess)
+        return LFM3A_ECUDA;
+      done[1][dev] = true;
+    }
+    prefill_kernel<true><<<grid, kPfThreads, PfLayout<true>::kRequest, st>>>(a);
+  } else {
+    if (!done[0][dev]) {
+      if (cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PfLayout<false>::kRequest) != cudaSuccess)
+        return LFM3A_ECUDA;
+      done[0][dev] = true;
+    }
+    prefill_kernel<false><<<grid, kPfThreads, PfLayout<false>::kRequest, st>>>(a);
+  }
+  return cudaGetLastError() == cudaSuccess ? LFM3A_OK : LFM3A_ELAUNCH;
+}
+
+inline int launch_prefill(const KvGeom& g, const __half* q, int tokens, int q_heads, int context, int window, bool exact,
+                          __half* out, cudaStream_t st) {
+  PrefillArgs a;
+  a.g = g;
+  a.q = q;
+  a.out = out;
+  a.T = tokens;
+  a.q_heads = q_heads;
+  a.context = context;
+  a.window = window;
+  a.qtiles = (tokens + 31) / 32;
+  a.qk_scale = 0.125f * kLog2e;
+  return launch_prefill_kernel(a, !exact, st);
 }
 
 }  // namespace lfm3a

@@ -314,16 +314,36 @@ __global__ __launch_bounds__(128) void combine_kernel(const float* part, int row
   for (int s = lane; s < splits; s += 32) M = fmaxf(M, base[(int64_t)s * split_stride + D]);
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float L = 0.f, acc[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  for (int s = 0; s < splits; ++s) {
+  // Sum of the splits' l weighted by 2^(m_s - M): lanes take splits, then a warp sum.
+  float L = 0.f;
+  for (int s = lane; s < splits; s += 32) {
     const float* p = base + (int64_t)s * split_stride;
     const float ms = p[D];
-    const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
-    L += f * p[D + 1];
+    L += ms == -INFINITY ? 0.f : exp2f(ms - M) * p[D + 1];
+  }
 #pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] += f * p[lane * E + e];
+  for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  // acc: every lane its E dims over all splits, 8 splits' loads in flight at a time.
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  for (int s0 = 0; s0 < splits; s0 += 8) {
+    float f[8], v[8][E];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int s = s0 + u;
+      const float* p = base + (int64_t)min(s, splits - 1) * split_stride;
+      const float ms = p[D];
+      f[u] = (s < splits && ms != -INFINITY) ? ms : -INFINITY;
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[u][e] = p[lane * E + e];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float w = f[u] == -INFINITY ? 0.f : exp2f(f[u] - M);
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = fmaf(w, v[u][e], acc[e]);
+    }
   }
   if (out16) {
     const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row);

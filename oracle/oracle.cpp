@@ -341,8 +341,7 @@ void orc_attention_f64(const uint16_t* q, int nq, int qpos0, int q_heads, int kv
 namespace {
 
 // One query row of the prefill kernels: CTA of 32 query tokens (t0 = t & ~31), 64-key tiles from the
-// CTA's first key rounded down to 64, lazy running max with the first tile of the CTA setting it
-// (prefill_attn.hip:212-332,373-486).
+// CTA's first key rounded down to 64 (prefill_attn.hip:212-332,373-486; prefill_attn_exact.hip:173-344).
 template <bool I8>
 void prefill_row(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int D, const uint16_t* K,
                  const uint16_t* V, const int8_t* V8, const float* vscale, int window, int t, int qh, float* o) {
@@ -354,7 +353,10 @@ void prefill_row(const uint16_t* q, int T, int context, int q_heads, int kv_head
   const float qk_scale = (1.f / sqrtf((float)D)) * LOG2E;
   float qf[128];
   for (int d = 0; d < D; ++d) qf[d] = orc_f16_to_f32(q[((size_t)t * q_heads + qh) * D + d]);
-  float m = 0.f, l = 0.f, acc[128] = {0};
+  // int8 kernel: running max starts at 0 and moves on the CTA's first tile or when a tile beats it by 2^8
+  // (prefill_attn.hip:278-304); exact kernel: running max from -inf, moved by every larger tile max
+  // (prefill_attn_exact.hip:300-306).
+  float m = I8 ? 0.f : -INFINITY, l = 0.f, acc[128] = {0};
   bool first = true;
   for (int k0 = kt_begin; k0 < kend; k0 += QB, first = false) {
     float s[QB];
@@ -373,8 +375,9 @@ void prefill_row(const uint16_t* q, int T, int context, int q_heads, int kv_head
       s[kk] = dot * qk_scale;
       tm = fmaxf(tm, s[kk]);
     }
-    if (tm > -INFINITY && (first || tm > m + LAZY)) {
-      const float corr = exp2f(m - tm);
+    const bool move = I8 ? tm > -INFINITY && (first || tm > m + LAZY) : tm > m;
+    if (move) {
+      const float corr = m == -INFINITY ? 0.f : exp2f(m - tm);
       m = tm;
       l *= corr;
       for (int d = 0; d < D; ++d) acc[d] *= corr;

@@ -1,11 +1,17 @@
 """DSpark verify attention on the GPU against the oracle (same arithmetic) and exact fp64 attention.
-Tolerance: max |gpu - reference| <= 2e-3 x RMS(reference) (fp16 probabilities, fp32 accumulation)."""
+
+Tolerance: max(|gpu - fp64| - ulp16(fp64) / 2) <= 2e-3 x RMS(fp64). The output is fp16, and its own
+rounding (half an fp16 ulp, up to ~2e-3 of the RMS for short contexts) is exempt; the arithmetic before it
+(fp16 probabilities, fp32 accumulation) must stay within 2e-3. Both the kernel and the oracle round each
+probability to fp16 against a running maximum, and those maxima differ with the split/page order, so gpu vs
+oracle carries two independent fp16 roundings: that comparison uses 4e-3."""
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-3
+TOL_PAIR = 4e-3
 
 
 def dev(a, cuda):
@@ -15,8 +21,11 @@ def dev(a, cuda):
 
 
 def rel_err(got, want):
-    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
-    return float(np.max(np.abs(got.astype(np.float64) - want))) / rms
+    """Max error relative to the RMS of want, beyond half an fp16 ulp of want (the output rounding)."""
+    want = want.astype(np.float64)
+    rms = float(np.sqrt(np.mean(want ** 2)))
+    half_ulp = 0.5 * np.abs(np.spacing(want.astype(np.float16))).astype(np.float64)
+    return float(np.max(np.clip(np.abs(got.astype(np.float64) - want) - half_ulp, 0.0, None))) / rms
 
 
 def setup(la, orc, synth, cuda, seed, ctx_len, m, window=0, theta=1e6):
@@ -37,7 +46,7 @@ def test_verify_c1(la, orc, synth, cuda, splits):
     out = cache.verify(dev(case["Q"], cuda), 1024, splits=splits)
     la.sync()
     got = out.float().cpu().numpy()
-    assert rel_err(got, orc.verify(case["Q"], K, V, 1024, splits=max(splits, 1))) < TOL
+    assert rel_err(got, orc.verify(case["Q"], K, V, 1024, splits=max(splits, 1))) < TOL_PAIR
     assert rel_err(got, orc.attention_f64(case["Q"], 1024, K, V, 1032)) < TOL
 
 
