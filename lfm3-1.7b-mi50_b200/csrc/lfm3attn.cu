@@ -56,6 +56,8 @@ int ensure_smem(K kernel, int bytes, bool* done_per_device) {
   if (dev < 0 || dev >= 64) return fail(LFM3A_EINVAL, "device index out of range");
   if (!done_per_device[dev]) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    // All of the unified L1 / shared storage as shared memory, so two blocks share an SM.
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     done_per_device[dev] = true;
   }
@@ -100,10 +102,10 @@ int launch_v8(const lfm3a_kv_view* kv, int qb0, int qb1, int len, cudaStream_t s
 
 int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count) {
   const int start = window > 0 ? std::max(0, ctx_len - window + 1) : 0;
-  const int p_total = (ctx_len + m - 1) / kBlockTokens - start / kBlockTokens + 1;
-  // Two resident blocks per SM, at least two pages per split.
+  const int t_total = (ctx_len + m - 1) / kQuantBlock - start / kQuantBlock + 1;
+  // Two resident blocks per SM, at least two 64-key tiles per split.
   int splits = (2 * sm_count + kv_heads - 1) / kv_heads;
-  splits = std::min(splits, std::max(1, p_total / 2));
+  splits = std::min(splits, std::max(1, t_total / 2));
   return std::max(1, splits);
 }
 
@@ -139,13 +141,14 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   a.q_heads = q_heads;
   a.ctx_len = ctx_len;
   a.window = window;
-  a.start = std::max(kv_begin, window > 0 ? std::max(0, ctx_len - window + 1) : 0);
+  a.kv_begin = kv_begin;
   a.kv_end = kv_end;
-  // A shard wholly below the window start still runs its last page, with every key masked.
-  a.p_begin = std::min(a.start, kv_end - 1) / kBlockTokens;
-  a.p_total = (kv_end - 1) / kBlockTokens - a.p_begin + 1;
-  if (splits <= 0) splits = verify_splits_for(L.kv_heads, a.p_total * kBlockTokens, 1, 0, current_sm_count());
-  a.splits = std::min(splits, a.p_total);
+  a.start = std::max(kv_begin, window > 0 ? std::max(0, ctx_len - window + 1) : 0);
+  // 64-key tiles over [start, kv_end); a shard wholly below the window start runs its last tile, all masked.
+  a.t_begin = std::min(a.start, kv_end - 1) / kQuantBlock;
+  a.t_total = (kv_end - 1) / kQuantBlock - a.t_begin + 1;
+  if (splits <= 0) splits = verify_splits_for(L.kv_heads, a.t_total * kQuantBlock, 1, 0, current_sm_count());
+  a.splits = std::min(splits, a.t_total);
   a.qk_scale = 0.125f * kLog2e;
   const int rows = m * q_heads;
   // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
@@ -159,26 +162,12 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   } else {
     a.part = nullptr;
   }
-  const bool direct = a.splits == 1 && out16;
-  if (!direct) a.out = nullptr;
+  if (!(a.splits == 1 && out16)) a.out = nullptr;
   const dim3 grid(a.splits, L.kv_heads);
-  const int smem = kVerifyStages * kVerifyStageBytes + 2 * kVerifyStages * 8;
-  const int wpg = (m + 7) / 8;
-  static bool done[4][64];
-  switch (wpg) {
-#define LFM3A_VERIFY_CASE(W)                                               \
-  case W:                                                                  \
-    rc = ensure_smem(verify_kernel<W>, smem, done[W - 1]);                 \
-    if (rc != LFM3A_OK) return rc;                                         \
-    verify_kernel<W><<<grid, (2 * W + 1) * 32, smem, st>>>(a);             \
-    break;
-    LFM3A_VERIFY_CASE(1)
-    LFM3A_VERIFY_CASE(2)
-    LFM3A_VERIFY_CASE(3)
-    LFM3A_VERIFY_CASE(4)
-#undef LFM3A_VERIFY_CASE
-    default: return fail(LFM3A_EINVAL, "m out of range");
-  }
+  static bool done[64];
+  rc = ensure_smem(verify_kernel, kVfSmem, done);
+  if (rc != LFM3A_OK) return rc;
+  verify_kernel<<<grid, kVfThreads, kVfSmem, st>>>(a);
   rc = check_launch("verify_kernel");
   if (rc != LFM3A_OK || a.splits == 1) return rc;
   return launch_combine(a.part, rows, a.splits, 64, kVerifyPart, (int64_t)a.splits * kVerifyPart,

@@ -444,7 +444,8 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
   if (i8) {
     if (!done[1][dev]) {
       if (cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               PfLayout<true>::kRequest) != cudaSuccess)
+                               PfLayout<true>::kRequest) != cudaSuccess ||
+          cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return LFM3A_ECUDA;
       done[1][dev] = true;
     }
@@ -452,7 +453,8 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
   } else {
     if (!done[0][dev]) {
       if (cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               PfLayout<false>::kRequest) != cudaSuccess)
+                               PfLayout<false>::kRequest) != cudaSuccess ||
+          cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return LFM3A_ECUDA;
       done[0][dev] = true;
     }

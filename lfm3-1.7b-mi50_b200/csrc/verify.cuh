@@ -1,15 +1,18 @@
-// DSpark verify attention on the B200 page layout (MODE_F16, head_dim 64, 4 query heads per kv head).
+// DSpark verify attention on the B200 page layout (MODE_F16, head_dim 64, 4 query heads per kv head),
+// on the 5th-generation tensor cores.
 //
-// Grid (splits, kv heads). A block reads each K/V page of its split once, for every verified token:
-// query rows r = 4 t + j (token t, query head 4 h + j), 64 rows for 16 tokens. One producer warp moves
-// whole pages (K and V sections, 8 KiB contiguous) into an 8-stage shared-memory ring with bulk copies;
-// two groups of WPG consumer warps take alternate pages, each warp holding 32 rows: QK^T and PV run on
-// the tensor cores (m16n8k16, fp32 accumulation), the online softmax stays in registers with warp
-// shuffles and a lazy running max (rescale only when a page beats it by 2^8). The two groups merge
-// their (acc, max, sum) in shared memory; a block writes the fp16 output directly (one split) or its
-// log-sum-exp partial for lfm3a_combine.
-// Reference: dspark.hip:1809-2121 (attention_v3: one K/V pass for all tokens, page partition,
-// split 0 on the fresh keys), :975-979 (attn_start), :2134-2185 (combine_phase).
+// Grid (splits, kv heads). A block reads each K/V page of its split once for every verified token: the
+// query rows r = 4 t + j (token t, query head 4 h + j; up to 32 tokens = 128 rows) form the M = 128 operand
+// of one tcgen05 MMA per 16 dims, rows past 4 m are padding. The keys stream in 64-key tiles (two 32-token
+// pages) through a bulk-copy ring:
+//   warps 0-3  softmax, thread = query row (warps past the last real row idle): S from TMEM, masks, lazy
+//              running max (rescale only when a tile beats it by 2^8; O is rescaled in TMEM), p = 2^(s - m),
+//              P fp16 -> shared memory; finally O / l (or the unnormalised partial) out;
+//   warp 4     producer: bulk copies of the K and V sections of the tile's two pages;
+//   warp 5     MMA issuer (one thread): S = Q K^T (kind::f16, M128 N64) into TMEM, then O += P V of the
+//              previous tile (O stays in TMEM across the whole split).
+// The arithmetic is that of dspark.hip:1809-2121 (attention_v3): one K/V pass for all tokens, page partition
+// into splits, fp16 P, fp32 accumulation, (acc, max, sum) partials merged by the combine (:2134-2185).
 #pragma once
 #include "common.cuh"
 #include "kv.cuh"
@@ -20,16 +23,24 @@ struct VerifyArgs {
   KvGeom g;
   const __half* q;      // [m][QH][64]
   const __half* gate;   // [m][QH] or null
-  __half* out;          // [m][QH][64]
+  __half* out;          // [m][QH][64]: one split with fp16 output, else null
   float* part;          // [m * QH][splits][66]
-  int m, q_heads, ctx_len, window, start, p_begin, p_total, splits;
-  int kv_end;           // keys present end here (ctx_len + m unless the cache holds a shard)
+  int m, q_heads, ctx_len, window, start, splits;
+  int kv_begin, kv_end; // the keys this cache holds: [kv_begin, kv_end)
+  int t_begin, t_total; // 64-key tiles of the whole range
   float qk_scale;       // (1 / sqrt(64)) * log2(e)
 };
 
-constexpr int kVerifyStages = 8;
-constexpr int kVerifyStageBytes = 8192;   // one page: K (4 KiB) then V (4 KiB)
 constexpr int kVerifyPart = 66;           // acc[64], max, sum
+constexpr int kVfThreads = 192;
+constexpr int kVfStages = 3;
+constexpr int kVfStage = 16384;           // K (2 pages) | V (2 pages)
+constexpr int kVfOffStage = 16384;        // after Q
+constexpr int kVfOffP = kVfOffStage + kVfStages * kVfStage;
+constexpr int kVfOffBar = kVfOffP + 2 * 16384;
+constexpr int kVfBars = 2 * kVfStages + 4 * 2 + 2;
+constexpr int kVfOffTmemSlot = kVfOffBar + kVfBars * 8;
+constexpr int kVfSmem = kVfOffTmemSlot + 16;
 
 __device__ __forceinline__ float sigmoid_gate(const __half* gate, int row) {
   if (!gate) return 1.f;
@@ -37,265 +48,292 @@ __device__ __forceinline__ float sigmoid_gate(const __half* gate, int row) {
   return 1.f / (1.f + exp2f(-g * kLog2e));
 }
 
-template <int WPG>
-__global__ __launch_bounds__((2 * WPG + 1) * 32) void verify_kernel(VerifyArgs a) {
-  constexpr int D = 64, NS = kVerifyStages, SB = kVerifyStageBytes;
-  constexpr int NCW = 2 * WPG;   // consumer warps
+__global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
+  constexpr int NS = kVfStages;
+  constexpr uint32_t kTmemCols = 256;   // S[2] at 0 and 64, O at 128
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB);
-  uint64_t* empty = full + NS;
   __shared__ int s_abort;
+  uint8_t* sQ = smem;
+  uint8_t* sStage = smem + kVfOffStage;
+  uint8_t* sP = smem + kVfOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kVfOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + NS;
+  uint64_t* s_full = bars + 2 * NS;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* q_ready = pv_done + 2;
+  uint64_t* drain = q_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kVfOffTmemSlot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y;
-  const int g0 = a.p_begin + (int)((int64_t)a.p_total * split / a.splits);
-  const int g1 = a.p_begin + (int)((int64_t)a.p_total * (split + 1) / a.splits);
-  const int npages = g1 - g0;
+  const int tile0 = a.t_begin + (int)((int64_t)a.t_total * split / a.splits);
+  const int ntiles = a.t_begin + (int)((int64_t)a.t_total * (split + 1) / a.splits) - tile0;
+  const int nsw = (4 * a.m + 31) / 32;   // softmax warps holding real rows
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], WPG);
+      mbar_init(&empty[s], 1);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], nsw);
+      mbar_init(&p_full[b], nsw);
+      mbar_init(&pv_done[b], 1);
+    }
+    mbar_init(q_ready, nsw);
+    mbar_init(drain, 1);
     fence_barrier_init();
   }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  if (warp == NCW) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      for (int i = 0; i < npages; ++i) {
-        const int st = i % NS;
-        const uint32_t ph = (uint32_t)(i / NS) & 1u;
-        if (i >= NS && !mbar_wait(&empty[st], ph ^ 1u)) {
-          raise_error(kErrWaitEmpty);
-          atomicExch(&s_abort, 1);
-          break;
-        }
-        const char* sec = a.g.pool + phys_block(a.g, g0 + i) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
-        mbar_arrive_expect_tx(&full[st], SB);
-        bulk_g2s(smem + st * SB, sec, SB, &full[st]);
+  if (warp < nsw) {
+    // ================================================================ softmax warps, thread = query row
+    const int r = threadIdx.x, t = r >> 2, j = r & 3;
+    const bool row_ok = t < a.m;
+    const int qpos = a.ctx_len + t;
+    const int row = t * a.q_heads + 4 * h + j;   // output / partial row (valid when row_ok)
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)(row_ok ? row : 0) * 64);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
     }
-  } else {
-    // ---------------------------------------------------------------- consumers
-    const int group = warp / WPG, wg = warp % WPG;
-    const int gr = lane >> 2, gc = lane & 3;
-    // Query fragments (A operand, row-major 16 x 16 per k-step) of rows 32 wg + 16 i + {gr, gr + 8}.
-    uint32_t qa[2][4][4];
-    int row_tok[2][2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const int r = 32 * wg + 16 * i + gr + 8 * hr;
-        row_tok[i][hr] = r >> 2;
-      }
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int hr = e & 1, dhi = e >> 1;
-          const int r = 32 * wg + 16 * i + gr + 8 * hr, t = r >> 2, qh = h * 4 + (r & 3);
-          const int dim = 16 * ks + 8 * dhi + 2 * gc;
-          qa[i][ks][e] = t < a.m ? *reinterpret_cast<const uint32_t*>(a.q + ((int64_t)t * a.q_heads + qh) * D + dim) : 0u;
-        }
-
-    float o[2][8][4];
-    float m_run[2][2], l_run[2][2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        m_run[i][hr] = -INFINITY;
-        l_run[i][hr] = 0.f;
-      }
-#pragma unroll
-      for (int dt = 0; dt < 8; ++dt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[i][dt][e] = 0.f;
-    }
-
-    const int kv_end = a.kv_end;
-    for (int i = group; i < npages; i += 2) {
-      const int st = i % NS;
-      const uint32_t ph = (uint32_t)(i / NS) & 1u;
-      if (*reinterpret_cast<volatile int*>(&s_abort)) break;
-      if (!mbar_wait(&full[st], ph)) {
-        raise_error(kErrWaitFull);
-        atomicExch(&s_abort, 1);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    const int qlast = a.ctx_len + a.m - 1;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
+    for (int jt = 0; jt < ntiles && ok; ++jt) {
+      const int b = jt & 1, k0 = (tile0 + jt) * kQuantBlock;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(jt >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        ok = false;
         break;
       }
-      const uint32_t kbase = smem_u32(smem + st * SB), vbase = kbase + 4096;
-      const int page = g0 + i, kp0 = page * kBlockTokens;
-
-      // S = Q K^T for 32 keys: s[i][nt] holds rows (gr, gr + 8) x keys nt*8 + 2 gc + {0, 1}.
-      float s[2][4][4];
+      tc_fence_after();
+      float x[64];
+      {
+        uint32_t rr[16];
 #pragma unroll
-      for (int ii = 0; ii < 2; ++ii)
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld16(lane_base + b * 64 + c * 16, rr);
+          tmem_wait_ld();
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) s[ii][nt][e] = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(kbase + nt * 1024 + q2 * 512 + lane * 16, b0, b1, b2, b3);
-#pragma unroll
-          for (int ii = 0; ii < 2; ++ii) {
-            mma_16816(s[ii][nt], qa[ii][2 * q2], b0, b1);
-            mma_16816(s[ii][nt], qa[ii][2 * q2 + 1], b2, b3);
-          }
-        }
-
-      // Masks: only pages that reach below start, into the window edge or onto the drafts.
-      const bool interior = kp0 >= a.start && kp0 + kBlockTokens <= min(a.ctx_len, kv_end) &&
-                            (a.window == 0 || kp0 > a.ctx_len + a.m - 1 - a.window);
-#pragma unroll
-      for (int ii = 0; ii < 2; ++ii)
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float x = s[ii][nt][e] * a.qk_scale;
-            if (!interior) {
-              const int kpos = kp0 + nt * 8 + 2 * gc + (e & 1);
-              const int qpos = a.ctx_len + row_tok[ii][e >> 1];
-              bool valid;
-              if (kpos < a.ctx_len) valid = kpos >= a.start && kpos < kv_end && (a.window == 0 || kpos > qpos - a.window);
-              else valid = kpos <= qpos && kpos < kv_end;
-              x = valid ? x : -INFINITY;
-            }
-            s[ii][nt][e] = x;
-          }
-
-      // Lazy running max per row, then p = 2^(s - m) packed as the fp16 A operand of PV.
-      uint32_t pa[2][2][4];
-#pragma unroll
-      for (int ii = 0; ii < 2; ++ii) {
-#pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          float mx = -INFINITY;
-#pragma unroll
-          for (int nt = 0; nt < 4; ++nt) mx = fmaxf(mx, fmaxf(s[ii][nt][2 * hr], s[ii][nt][2 * hr + 1]));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          if (mx > m_run[ii][hr] + kLazy) {
-            const float corr = fast_exp2(m_run[ii][hr] - mx);
-            m_run[ii][hr] = mx;
-            l_run[ii][hr] *= corr;
-#pragma unroll
-            for (int dt = 0; dt < 8; ++dt) {
-              o[ii][dt][2 * hr] *= corr;
-              o[ii][dt][2 * hr + 1] *= corr;
-            }
-          }
-          const float mr = m_run[ii][hr];
-#pragma unroll
-          for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const float x = s[ii][nt][2 * hr + c];
-              const float p = x == -INFINITY ? 0.f : fast_exp2(x - mr);
-              s[ii][nt][2 * hr + c] = p;
-              l_run[ii][hr] += p;
-            }
-        }
-#pragma unroll
-        for (int kp = 0; kp < 2; ++kp) {
-          pa[ii][kp][0] = pack_half2(s[ii][2 * kp][0], s[ii][2 * kp][1]);
-          pa[ii][kp][1] = pack_half2(s[ii][2 * kp][2], s[ii][2 * kp][3]);
-          pa[ii][kp][2] = pack_half2(s[ii][2 * kp + 1][0], s[ii][2 * kp + 1][1]);
-          pa[ii][kp][3] = pack_half2(s[ii][2 * kp + 1][2], s[ii][2 * kp + 1][3]);
+          for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[e]);
         }
       }
-
-      // O += P V: dims dt*8 .. +7, keys 16 kp .. +15.
-#pragma unroll
-      for (int dt = 0; dt < 8; ++dt) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(vbase + dt * 512 + lane * 16, b0, b1, b2, b3);
-#pragma unroll
-        for (int ii = 0; ii < 2; ++ii) {
-          mma_16816(o[ii][dt], pa[ii][0], b0, b1);
-          mma_16816(o[ii][dt], pa[ii][1], b2, b3);
-        }
-      }
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-    }
+      if (lane == 0) mbar_arrive(&s_free[b]);
 
-    // Row sums over the four lanes of a row.
+      const bool interior = k0 >= a.start && k0 + kQuantBlock <= min(a.ctx_len, a.kv_end) &&
+                            (a.window == 0 || k0 > qlast - a.window);
+      float mx = -INFINITY;
 #pragma unroll
-    for (int ii = 0; ii < 2; ++ii)
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        float l = l_run[ii][hr];
-        l += __shfl_xor_sync(0xffffffffu, l, 1);
-        l += __shfl_xor_sync(0xffffffffu, l, 2);
-        l_run[ii][hr] = l;
-      }
-
-    // Merge the two groups: group 1 hands its state to the same lane of group 0's twin warp.
-    named_bar_sync(1, NCW * 32);   // every page consumed: the stage memory is free
-    float* xfer = reinterpret_cast<float*>(smem) + (wg * 32 + lane) * 72;
-    if (group == 1) {
-#pragma unroll
-      for (int ii = 0; ii < 2; ++ii) {
-#pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          xfer[ii * 2 + hr] = m_run[ii][hr];
-          xfer[4 + ii * 2 + hr] = l_run[ii][hr];
+      for (int k = 0; k < 64; ++k) {
+        float v = x[k] * a.qk_scale;
+        if (!interior) {
+          const int kpos = k0 + k;
+          bool valid;
+          if (kpos < a.ctx_len) valid = kpos >= a.start && kpos < a.kv_end && (a.window == 0 || kpos > qpos - a.window);
+          else valid = kpos <= qpos && kpos < a.kv_end;
+          v = (valid && row_ok) ? v : -INFINITY;
         }
-#pragma unroll
-        for (int dt = 0; dt < 8; ++dt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) xfer[8 + ii * 32 + dt * 4 + e] = o[ii][dt][e];
+        x[k] = v;
+        mx = fmaxf(mx, v);
       }
+      const bool grow_max = mx > m_run + kLazy;
+      if (__any_sync(0xffffffffu, grow_max)) {
+        const float corr = grow_max ? fast_exp2(m_run - mx) : 1.f;
+        if (grow_max) m_run = mx;
+        l_run *= corr;
+        if (jt >= 1) {
+          // O holds PV up to the previous tile: wait for it, then rescale in TMEM.
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
+            raise_error(kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t rr[16];
+            tmem_ld16(lane_base + 128 + c * 16, rr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+            tmem_st16(lane_base + 128 + c * 16, rr);
+          }
+          tmem_wait_st();
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 64; ++k) {
+        const float p = x[k] == -INFINITY ? 0.f : fast_exp2(x[k] - m_run);
+        x[k] = p;
+        l_run += p;
+      }
+      // P[b] was last read by PV(jt - 2).
+      if (jt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        ok = false;
+        break;
+      }
+      uint8_t* pb = sP + b * 16384;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 v;
+        v.x = pack_half2(x[8 * c], x[8 * c + 1]);
+        v.y = pack_half2(x[8 * c + 2], x[8 * c + 3]);
+        v.z = pack_half2(x[8 * c + 4], x[8 * c + 5]);
+        v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
+        *reinterpret_cast<uint4*>(pb + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
     }
-    named_bar_sync(1, NCW * 32);
-    if (group == 0) {
-      const bool direct = a.out != nullptr;   // one split with fp16 output
+    if (!ok) {
+      atomicExch(&s_abort, 1);
+    } else {
+      const int last = ntiles - 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[last & 1], (uint32_t)(last >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        atomicExch(&s_abort, 1);
+      } else {
+        tc_fence_after();
+        float o[64];
 #pragma unroll
-      for (int ii = 0; ii < 2; ++ii)
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rr[16];
+          tmem_ld16(lane_base + 128 + c * 16, rr);
+          tmem_wait_ld();
 #pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          const float m0 = m_run[ii][hr], m1 = xfer[ii * 2 + hr];
-          const float M = fmaxf(m0, m1);
-          const float f0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - M);
-          const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - M);
-          const float L = f0 * l_run[ii][hr] + f1 * xfer[4 + ii * 2 + hr];
-          const int r = 32 * wg + 16 * ii + gr + 8 * hr, t = r >> 2;
-          if (t >= a.m) continue;
-          const int row = t * a.q_heads + h * 4 + (r & 3);
-          if (direct) {
-            const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(a.gate, row);
+          for (int e = 0; e < 16; ++e) o[c * 16 + e] = __uint_as_float(rr[e]);
+        }
+        if (row_ok) {
+          if (a.out) {
+            const float scale = (l_run > 0.f ? 1.f / l_run : 0.f) * sigmoid_gate(a.gate, row);
+            uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)row * 64);
 #pragma unroll
-            for (int dt = 0; dt < 8; ++dt) {
-              const float v0 = (f0 * o[ii][dt][2 * hr] + f1 * xfer[8 + ii * 32 + dt * 4 + 2 * hr]) * scale;
-              const float v1 = (f0 * o[ii][dt][2 * hr + 1] + f1 * xfer[8 + ii * 32 + dt * 4 + 2 * hr + 1]) * scale;
-              *reinterpret_cast<uint32_t*>(a.out + (int64_t)row * D + dt * 8 + 2 * gc) = pack_half2(v0, v1);
+            for (int c = 0; c < 8; ++c) {
+              uint4 v;
+              v.x = pack_half2(o[8 * c] * scale, o[8 * c + 1] * scale);
+              v.y = pack_half2(o[8 * c + 2] * scale, o[8 * c + 3] * scale);
+              v.z = pack_half2(o[8 * c + 4] * scale, o[8 * c + 5] * scale);
+              v.w = pack_half2(o[8 * c + 6] * scale, o[8 * c + 7] * scale);
+              dst[c] = v;
             }
           } else {
             float* dst = a.part + ((int64_t)row * a.splits + split) * kVerifyPart;
 #pragma unroll
-            for (int dt = 0; dt < 8; ++dt) {
-              const float v0 = f0 * o[ii][dt][2 * hr] + f1 * xfer[8 + ii * 32 + dt * 4 + 2 * hr];
-              const float v1 = f0 * o[ii][dt][2 * hr + 1] + f1 * xfer[8 + ii * 32 + dt * 4 + 2 * hr + 1];
-              *reinterpret_cast<float2*>(dst + dt * 8 + 2 * gc) = make_float2(v0, v1);
-            }
-            if (gc == 0) {
-              dst[D] = M;
-              dst[D + 1] = L;
-            }
+            for (int c = 0; c < 32; ++c) *reinterpret_cast<float2*>(dst + 2 * c) = make_float2(o[2 * c], o[2 * c + 1]);
+            *reinterpret_cast<float2*>(dst + 64) = make_float2(m_run, l_run);
           }
         }
+      }
     }
+  } else if (warp == 4) {
+    // ================================================================ producer
+    if (lane == 0) {
+      const int pv0 = a.kv_begin / kBlockTokens, pv1 = (a.kv_end - 1) / kBlockTokens;   // pages this cache holds
+      int issued = 0;
+      for (int jt = 0; jt < ntiles; ++jt) {
+        const int st = jt % NS;
+        if (jt >= NS && !mbar_wait(&empty[st], (uint32_t)((jt / NS) - 1) & 1u)) {
+          raise_error(kErrWaitEmpty);
+          atomicExch(&s_abort, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        const int lp = (tile0 + jt) * 2;
+        // A page outside the held range may have no table entry: copy a held page instead (its keys are masked).
+        const int lp0 = min(max(lp, pv0), pv1), lp1 = min(max(lp + 1, pv0), pv1);
+        const char* s0 = a.g.pool + phys_block(a.g, lp0) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+        const char* s1 = a.g.pool + phys_block(a.g, lp1) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+        uint8_t* dst = sStage + st * kVfStage;
+        mbar_arrive_expect_tx(&full[st], kVfStage);
+        bulk_g2s(dst, s0, 4096, &full[st]);
+        bulk_g2s(dst + 4096, s1, 4096, &full[st]);
+        bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV, 4096, &full[st]);
+        bulk_g2s(dst + 12288, s1 + F16Section<64>::kOffV, 4096, &full[st]);
+        issued = jt + 1;
+      }
+      if (*reinterpret_cast<volatile int*>(&s_abort)) {
+        for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
+      }
+    }
+  } else if (warp == 5) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_ready, 0);
+      if (!ok) raise_error(kErrWaitOther);
+      const uint32_t q_addr = smem_u32(sQ);
+      for (int jt = 0; jt <= ntiles && ok; ++jt) {
+        if (jt < ntiles) {
+          const int st = jt % NS, b = jt & 1;
+          if (!mbar_wait(&full[st], (uint32_t)(jt / NS) & 1u) ||
+              (jt >= 2 && !mbar_wait(&s_free[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
+            raise_error(kErrWaitFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sStage + st * kVfStage);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f16_ss(tmem + b * 64, umma_desc(q_addr + ks * 256, 128, 1024), umma_desc(k_addr + ks * 256, 128, 1024),
+                        kIdescF16M128N64, ks > 0 ? 1u : 0u);
+          umma_commit(&s_full[b]);
+        }
+        if (jt >= 1) {
+          const int jp = jt - 1, bp = jp & 1, stp = jp % NS;
+          if (!mbar_wait(&p_full[bp], (uint32_t)(jp >> 1) & 1u)) {
+            raise_error(kErrWaitOther);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t p_addr = smem_u32(sP + bp * 16384);
+          const uint32_t v_addr = smem_u32(sStage + stp * kVfStage + 8192);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f16_ss(tmem + 128, umma_desc(p_addr + ks * 256, 128, 1024),
+                        umma_desc(v_addr + (ks >> 1) * 4096 + (ks & 1) * 256, 128, 512), kIdescF16M128N64,
+                        (jp > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&empty[stp]);
+          umma_commit(&pv_done[bp]);
+        }
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0);
+      if (!ok) atomicExch(&s_abort, 1);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 

@@ -83,9 +83,9 @@ def test_split_choice(la):
     lay = la.layout(0, 8, 64)
     assert la.verify_splits(lay, 32768, 16, 0, 148) == 37
     assert la.verify_splits(lay, 131072, 16, 0, 148) == 37
-    assert la.verify_splits(lay, 100, 8, 0, 148) == 2
+    assert la.verify_splits(lay, 100, 8, 0, 148) == 1
     assert la.verify_splits(lay, 20, 8, 0, 148) == 1
-    assert la.verify_splits(lay, 1024, 8, 0, 148) == 16
+    assert la.verify_splits(lay, 1024, 8, 0, 148) == 8
     ws = la.lib().lfm3a_verify_workspace_bytes(16, 32, 64, 37)
     assert ws == 16 * 32 * 37 * 66 * 4
 
