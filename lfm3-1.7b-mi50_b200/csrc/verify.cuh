@@ -3,14 +3,16 @@
 //
 // Grid (splits, kv heads). A block reads each K/V page of its split once for every verified token: the
 // query rows r = 4 t + j (token t, query head 4 h + j; up to 32 tokens = 128 rows) form the M = 128 operand
-// of one tcgen05 MMA per 16 dims, rows past 4 m are padding. The keys stream in 64-key tiles (two 32-token
-// pages) through a bulk-copy ring:
-//   warps 0-3  softmax, thread = query row (warps past the last real row idle): S from TMEM, masks, lazy
-//              running max (rescale only when a tile beats it by 2^8; O is rescaled in TMEM), p = 2^(s - m),
-//              P fp16 -> shared memory; finally O / l (or the unnormalised partial) out;
-//   warp 4     producer: bulk copies of the K and V sections of the tile's two pages;
-//   warp 5     MMA issuer (one thread): S = Q K^T (kind::f16, M128 N64) into TMEM, then O += P V of the
-//              previous tile (O stays in TMEM across the whole split).
+// of one tcgen05 MMA per 16 dims. The 4m real rows are spread over the four TMEM lane quadrants (m rows
+// each, at lanes 32 q .. 32 q + m - 1) so that every SM sub-partition takes a share of the softmax. Keys
+// stream in 64-key tiles (two 32-token pages) through a bulk-copy ring:
+//   warps 0-7  softmax in two warpgroups, warpgroup g on keys 32 g .. 32 g + 31 of every tile, thread =
+//              query row: S from TMEM, masks, lazy running max per half (rescale only when a tile beats
+//              it by 2^8; O_g is rescaled in TMEM), p = 2^(s - m), P fp16 -> shared memory. At the end the
+//              two halves merge (log-sum-exp) and O / l, or the unnormalised partial, is written;
+//   warp 8     producer: bulk copies of the K and V sections of the tile's two pages;
+//   warp 9     MMA issuer (one thread): S = Q K^T (kind::f16, M128 N64) into TMEM, then O_g += P_g V_g of the
+//              previous tile for both halves (O_0, O_1 stay in TMEM across the whole split).
 // The arithmetic is that of dspark.hip:1809-2121 (attention_v3): one K/V pass for all tokens, page partition
 // into splits, fp16 P, fp32 accumulation, (acc, max, sum) partials merged by the combine (:2134-2185).
 #pragma once
@@ -32,12 +34,15 @@ struct VerifyArgs {
 };
 
 constexpr int kVerifyPart = 66;           // acc[64], max, sum
-constexpr int kVfThreads = 192;
+constexpr int kVfSoftmaxWarps = 8;
+constexpr int kVfThreads = (kVfSoftmaxWarps + 2) * 32;
 constexpr int kVfStages = 3;
 constexpr int kVfStage = 16384;           // K (2 pages) | V (2 pages)
+constexpr int kVfPHalf = 8192;            // 128 rows x 32 keys fp16
 constexpr int kVfOffStage = 16384;        // after Q
 constexpr int kVfOffP = kVfOffStage + kVfStages * kVfStage;
-constexpr int kVfOffBar = kVfOffP + 2 * 16384;
+constexpr int kVfOffML = kVfOffP + 4 * kVfPHalf;   // the second half's (max, sum) per row, for the merge
+constexpr int kVfOffBar = kVfOffML + 128 * 8;
 constexpr int kVfBars = 2 * kVfStages + 4 * 2 + 2;
 constexpr int kVfOffTmemSlot = kVfOffBar + kVfBars * 8;
 constexpr int kVfSmem = kVfOffTmemSlot + 16;
@@ -50,12 +55,13 @@ __device__ __forceinline__ float sigmoid_gate(const __half* gate, int row) {
 
 __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
   constexpr int NS = kVfStages;
-  constexpr uint32_t kTmemCols = 256;   // S[2] at 0 and 64, O at 128
+  constexpr uint32_t kTmemCols = 256;   // S[2] at 0 and 64, O_0 at 128, O_1 at 192
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_abort;
   uint8_t* sQ = smem;
   uint8_t* sStage = smem + kVfOffStage;
-  uint8_t* sP = smem + kVfOffP;
+  uint8_t* sP = smem + kVfOffP;          // [buffer b][half g] 8 KiB each
+  float2* sML = reinterpret_cast<float2*>(smem + kVfOffML);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kVfOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + NS;
@@ -71,7 +77,6 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
   const int split = blockIdx.x, h = blockIdx.y;
   const int tile0 = a.t_begin + (int)((int64_t)a.t_total * split / a.splits);
   const int ntiles = a.t_begin + (int)((int64_t)a.t_total * (split + 1) / a.splits) - tile0;
-  const int nsw = (4 * a.m + 31) / 32;   // softmax warps holding real rows
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -81,15 +86,15 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], nsw);
-      mbar_init(&p_full[b], nsw);
+      mbar_init(&s_free[b], kVfSoftmaxWarps);
+      mbar_init(&p_full[b], kVfSoftmaxWarps);
       mbar_init(&pv_done[b], 1);
     }
-    mbar_init(q_ready, nsw);
+    mbar_init(q_ready, 4);
     mbar_init(drain, 1);
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == kVfSoftmaxWarps + 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -98,42 +103,46 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < nsw) {
+  if (warp < kVfSoftmaxWarps) {
     // ================================================================ softmax warps, thread = query row
-    const int r = threadIdx.x, t = r >> 2, j = r & 3;
-    const bool row_ok = t < a.m;
+    const int half = warp >> 2, quad = warp & 3;
+    const int pos = 32 * quad + lane;                 // M row / TMEM lane
+    const int r = quad * a.m + lane;                  // query row held at this lane
+    const bool row_ok = lane < a.m;                   // m <= 32: quadrant q holds rows q m .. q m + m - 1
+    const int t = r >> 2, jh = r & 3;
     const int qpos = a.ctx_len + t;
-    const int row = t * a.q_heads + 4 * h + j;   // output / partial row (valid when row_ok)
-    {
+    const int row = t * a.q_heads + 4 * h + jh;       // output / partial row (valid when row_ok)
+    if (half == 0) {
       const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)(row_ok ? row : 0) * 64);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+        *reinterpret_cast<uint4*>(sQ + ((pos >> 3) * 8 + c) * 128 + (pos & 7) * 16) = v;
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
     }
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
+    const uint32_t o_col = 128 + 64 * half;
     const int qlast = a.ctx_len + a.m - 1;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
     for (int jt = 0; jt < ntiles && ok; ++jt) {
-      const int b = jt & 1, k0 = (tile0 + jt) * kQuantBlock;
+      const int b = jt & 1, k0 = (tile0 + jt) * kQuantBlock + 32 * half;
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(jt >> 1) & 1u))) {
         raise_error(kErrWaitMma);
         ok = false;
         break;
       }
       tc_fence_after();
-      float x[64];
+      float x[32];
       {
         uint32_t rr[16];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld16(lane_base + b * 64 + c * 16, rr);
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld16(lane_base + b * 64 + 32 * half + c * 16, rr);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[e]);
@@ -143,21 +152,27 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);
 
-      const bool interior = k0 >= a.start && k0 + kQuantBlock <= min(a.ctx_len, a.kv_end) &&
+      // Masks only on edge tiles; raw scores are masked to -inf before the (scaled) max.
+      const bool interior = k0 >= a.start && k0 + 32 <= min(a.ctx_len, a.kv_end) &&
                             (a.window == 0 || k0 > qlast - a.window);
-      float mx = -INFINITY;
+      if (!interior) {
 #pragma unroll
-      for (int k = 0; k < 64; ++k) {
-        float v = x[k] * a.qk_scale;
-        if (!interior) {
+        for (int k = 0; k < 32; ++k) {
           const int kpos = k0 + k;
           bool valid;
           if (kpos < a.ctx_len) valid = kpos >= a.start && kpos < a.kv_end && (a.window == 0 || kpos > qpos - a.window);
           else valid = kpos <= qpos && kpos < a.kv_end;
-          v = (valid && row_ok) ? v : -INFINITY;
+          x[k] = (valid && row_ok) ? x[k] : -INFINITY;
         }
-        x[k] = v;
-        mx = fmaxf(mx, v);
+      }
+      float mx;
+      {
+        float t4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) t4[u] = fmaxf(fmaxf(x[u], x[u + 4]), fmaxf(x[u + 8], x[u + 12]));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) t4[u] = fmaxf(t4[u], fmaxf(fmaxf(x[u + 16], x[u + 20]), fmaxf(x[u + 24], x[u + 28])));
+        mx = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3])) * a.qk_scale;
       }
       const bool grow_max = mx > m_run + kLazy;
       if (__any_sync(0xffffffffu, grow_max)) {
@@ -165,7 +180,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
         if (grow_max) m_run = mx;
         l_run *= corr;
         if (jt >= 1) {
-          // O holds PV up to the previous tile: wait for it, then rescale in TMEM.
+          // O_g holds PV up to the previous tile: wait for it, then rescale in TMEM.
           if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
             raise_error(kErrWaitMma);
             ok = false;
@@ -175,63 +190,74 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t rr[16];
-            tmem_ld16(lane_base + 128 + c * 16, rr);
+            tmem_ld16(lane_base + o_col + c * 16, rr);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
-            tmem_st16(lane_base + 128 + c * 16, rr);
+            tmem_st16(lane_base + o_col + c * 16, rr);
           }
           tmem_wait_st();
         }
       }
+      // p = 2^(s * scale - m): masked scores are -inf and give 0; a row without a valid key so far uses 0.
+      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < 64; ++k) {
-        const float p = x[k] == -INFINITY ? 0.f : fast_exp2(x[k] - m_run);
-        x[k] = p;
-        l_run += p;
+      for (int k = 0; k < 32; ++k) {
+        x[k] = fast_exp2(fmaf(x[k], a.qk_scale, neg_m));
+        ls[k & 3] += x[k];
       }
-      // P[b] was last read by PV(jt - 2).
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      // P_g[b] was last read by PV(jt - 2).
       if (jt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
         raise_error(kErrWaitMma);
         ok = false;
         break;
       }
-      uint8_t* pb = sP + b * 16384;
+      uint8_t* pb = sP + (2 * b + half) * kVfPHalf;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint4 v;
         v.x = pack_half2(x[8 * c], x[8 * c + 1]);
         v.y = pack_half2(x[8 * c + 2], x[8 * c + 3]);
         v.z = pack_half2(x[8 * c + 4], x[8 * c + 5]);
         v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
-        *reinterpret_cast<uint4*>(pb + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+        *reinterpret_cast<uint4*>(pb + ((pos >> 3) * 4 + c) * 128 + (pos & 7) * 16) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
     }
-    if (!ok) {
-      atomicExch(&s_abort, 1);
-    } else {
-      const int last = ntiles - 1;
+    if (!ok) atomicExch(&s_abort, 1);
+    // Merge the halves: the second warpgroup hands (max, sum) over; the first reads both O_g from TMEM.
+    if (half == 1) sML[pos] = make_float2(m_run, l_run);
+    named_bar_sync(1, kVfSoftmaxWarps * 32);
+    const int last = ntiles - 1;
+    if (half == 0 && !*reinterpret_cast<volatile int*>(&s_abort)) {
       if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[last & 1], (uint32_t)(last >> 1) & 1u))) {
         raise_error(kErrWaitMma);
         atomicExch(&s_abort, 1);
       } else {
         tc_fence_after();
+        const float2 mb = sML[pos];
+        const float M = fmaxf(m_run, mb.x);
+        const float f0 = m_run == -INFINITY ? 0.f : fast_exp2(m_run - M);
+        const float f1 = mb.x == -INFINITY ? 0.f : fast_exp2(mb.x - M);
+        const float L = f0 * l_run + f1 * mb.y;
         float o[64];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t rr[16];
-          tmem_ld16(lane_base + 128 + c * 16, rr);
+          uint32_t r0[16], r1[16];
+          tmem_ld16(lane_base + 128 + c * 16, r0);
+          tmem_ld16(lane_base + 192 + c * 16, r1);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[c * 16 + e] = __uint_as_float(rr[e]);
+          for (int e = 0; e < 16; ++e) o[c * 16 + e] = f0 * __uint_as_float(r0[e]) + f1 * __uint_as_float(r1[e]);
         }
         if (row_ok) {
           if (a.out) {
-            const float scale = (l_run > 0.f ? 1.f / l_run : 0.f) * sigmoid_gate(a.gate, row);
+            const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(a.gate, row);
             uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)row * 64);
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -246,12 +272,12 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
             float* dst = a.part + ((int64_t)row * a.splits + split) * kVerifyPart;
 #pragma unroll
             for (int c = 0; c < 32; ++c) *reinterpret_cast<float2*>(dst + 2 * c) = make_float2(o[2 * c], o[2 * c + 1]);
-            *reinterpret_cast<float2*>(dst + 64) = make_float2(m_run, l_run);
+            *reinterpret_cast<float2*>(dst + 64) = make_float2(M, L);
           }
         }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == kVfSoftmaxWarps) {
     // ================================================================ producer
     if (lane == 0) {
       const int pv0 = a.kv_begin / kBlockTokens, pv1 = (a.kv_end - 1) / kBlockTokens;   // pages this cache holds
@@ -281,7 +307,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
         for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
       }
     }
-  } else if (warp == 5) {
+  } else {
     // ================================================================ MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(q_ready, 0);
@@ -312,13 +338,16 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
             break;
           }
           tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP + bp * 16384);
           const uint32_t v_addr = smem_u32(sStage + stp * kVfStage + 8192);
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_f16_ss(tmem + 128, umma_desc(p_addr + ks * 256, 128, 1024),
-                        umma_desc(v_addr + (ks >> 1) * 4096 + (ks & 1) * 256, 128, 512), kIdescF16M128N64,
-                        (jp > 0 || ks > 0) ? 1u : 0u);
+          for (int g = 0; g < 2; ++g) {
+            const uint32_t p_addr = smem_u32(sP + (2 * bp + g) * kVfPHalf);
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+              umma_f16_ss(tmem + 128 + 64 * g, umma_desc(p_addr + ks * 256, 128, 512),
+                          umma_desc(v_addr + g * 4096 + ks * 256, 128, 512), kIdescF16M128N64,
+                          (jp > 0 || ks > 0) ? 1u : 0u);
+          }
           umma_commit(&empty[stp]);
           umma_commit(&pv_done[bp]);
         }
@@ -331,7 +360,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kVfSoftmaxWarps + 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
