@@ -80,6 +80,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Polling form for latency-critical waits of a lone issuing thread: test_wait never suspends, so the thread
+// sees the phase flip within a few cycles; still bounded by kWaitLimitNs.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_test_wait(a, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test_wait(a, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -94,6 +117,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
           smem_u32(dst_smem)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Bulk prefetch of global memory into L2 (16-byte aligned, size a multiple of 16); no completion tracking.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {

@@ -164,10 +164,16 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   }
   if (!(a.splits == 1 && out16)) a.out = nullptr;
   const dim3 grid(a.splits, L.kv_heads);
-  static bool done[64];
-  rc = ensure_smem(verify_kernel, kVfSmem, done);
-  if (rc != LFM3A_OK) return rc;
-  verify_kernel<<<grid, kVfThreads, kVfSmem, st>>>(a);
+  static bool done[2][64];
+  if (m <= 16) {
+    rc = ensure_smem(verify_kernel<true>, kVfSmem, done[1]);
+    if (rc != LFM3A_OK) return rc;
+    verify_kernel<true><<<grid, kVfThreads, kVfSmem, st>>>(a);
+  } else {
+    rc = ensure_smem(verify_kernel<false>, kVfSmem, done[0]);
+    if (rc != LFM3A_OK) return rc;
+    verify_kernel<false><<<grid, kVfThreads, kVfSmem, st>>>(a);
+  }
   rc = check_launch("verify_kernel");
   if (rc != LFM3A_OK || a.splits == 1) return rc;
   return launch_combine(a.part, rows, a.splits, 64, kVerifyPart, (int64_t)a.splits * kVerifyPart,

@@ -73,7 +73,7 @@ struct PfLayout {
   static constexpr int kOffStage = kPfQBytes;
   static constexpr int kOffP = kOffStage + kPfStages * kStage;
   static constexpr int kOffBar = kOffP + 2 * kPBuf;
-  static constexpr int kBars = 2 * kPfStages + 4 * 2 + 2;
+  static constexpr int kBars = 2 * kPfStages + 3 * 2 + 2;
   static constexpr int kOffTmemSlot = kOffBar + kBars * 8;
   static constexpr int kBytes = kOffTmemSlot + 16;
   // Request enough shared memory that two CTAs share an SM and a third cannot (TMEM holds 2 x 256 columns).
@@ -94,8 +94,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   uint64_t* full = bars;
   uint64_t* empty = bars + NS;
   uint64_t* s_full = bars + 2 * NS;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
+  uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* q_ready = pv_done + 2;
   uint64_t* drain = q_ready + 1;
@@ -118,7 +117,6 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 4);
       mbar_init(&p_full[b], 4);
       mbar_init(&pv_done[b], 1);
     }
@@ -182,10 +180,6 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
           for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[e]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[b]);
-
       const bool interior = ntok == 32 && k0 + kQuantBlock - 1 <= qfirst && (a.window == 0 || k0 > qlast - a.window);
       float mx = -INFINITY;
 #pragma unroll
@@ -241,12 +235,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
       }
       uint8_t* pb = sP + b * L::kPBuf;
       if (!I8) {
-        // P[b] was last read by PV(jt - 2).
-        if (jt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
-          raise_error(kErrWaitMma);
-          ok = false;
-          break;
-        }
+        // P[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint4 v;
@@ -264,7 +253,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         for (int k = 0; k < 64; ++k) x[k] = __fmul_rn(x[k], vs);
         uint32_t q8[16];
         const float sc = quantize_p_row<64>(x, q8);
-        // P8[b] was last read by PV(jt - 2), whose completion the previous epilogue waited for.
+        // P8[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           *reinterpret_cast<uint4*>(pb + ((r >> 3) * 4 + c) * 128 + (r & 7) * 16) =
@@ -338,16 +327,17 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
     }
   } else if (warp == 4) {
     // ================================================================ producer
-    if (lane == 0) {
+    // The whole warp runs the loop; lane 0 issues the copies.
+    {
       int issued = 0;
       for (int jt = 0; jt < ntiles; ++jt) {
         const int st = jt % NS;
-        if (jt >= NS && !mbar_wait(&empty[st], (uint32_t)((jt / NS) - 1) & 1u)) {
+        if (jt >= NS && !__all_sync(0xffffffffu, mbar_spin(&empty[st], (uint32_t)((jt / NS) - 1) & 1u))) {
           raise_error(kErrWaitEmpty);
           atomicExch(&s_abort, 1);
           break;
         }
-        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) break;
         const int k0 = kt_begin + jt * kQuantBlock;
         const int lp0 = k0 / kBlockTokens;
         // A second page wholly past the keys may have no table entry: copy the first page again (masked).
@@ -355,74 +345,94 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         const char* s0 = a.g.pool + phys_block(a.g, lp0) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
         const char* s1 = a.g.pool + phys_block(a.g, lp1) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
         uint8_t* dst = sStage + st * L::kStage;
-        mbar_arrive_expect_tx(&full[st], L::kStage);
-        bulk_g2s(dst, s0, 4096, &full[st]);
-        bulk_g2s(dst + 4096, s1, 4096, &full[st]);
-        if (!I8) {
-          bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV, 4096, &full[st]);
-          bulk_g2s(dst + 12288, s1 + F16Section<64>::kOffV, 4096, &full[st]);
-        } else {
-          bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV8, 2048, &full[st]);
-          bulk_g2s(dst + 10240, s1 + F16Section<64>::kOffV8, 2048, &full[st]);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[st], L::kStage);
+          bulk_g2s(dst, s0, 4096, &full[st]);
+          bulk_g2s(dst + 4096, s1, 4096, &full[st]);
+          if (!I8) {
+            bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV, 4096, &full[st]);
+            bulk_g2s(dst + 12288, s1 + F16Section<64>::kOffV, 4096, &full[st]);
+          } else {
+            bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV8, 2048, &full[st]);
+            bulk_g2s(dst + 10240, s1 + F16Section<64>::kOffV8, 2048, &full[st]);
+          }
         }
+        __syncwarp();
         issued = jt + 1;
       }
       // On an abort, wait (bounded) for the copies still landing in shared memory.
-      if (*reinterpret_cast<volatile int*>(&s_abort)) {
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
         for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
       }
     }
   } else {
     // ================================================================ MMA issuer
-    if (lane == 0) {
-      bool ok = mbar_wait(q_ready, 0);
+    // QK runs two tiles ahead of PV: after PV(j), S buffer j & 1 is free (the softmax read S(j) before it
+    // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores.
+    // The whole warp runs the loop (its values stay warp-uniform); lane 0 alone issues the tensor-core work.
+    {
+      bool ok = __all_sync(0xffffffffu, mbar_spin(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
-      const uint32_t q_addr = smem_u32(sQ);
-      for (int jt = 0; jt <= ntiles && ok; ++jt) {
-        if (jt < ntiles) {
-          const int st = jt % NS, b = jt & 1;
-          if (!mbar_wait(&full[st], (uint32_t)(jt / NS) & 1u) ||
-              (jt >= 2 && !mbar_wait(&s_free[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
-            raise_error(kErrWaitFull);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sStage + st * L::kStage);
+      const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
+      auto issue_qk = [&](int jt) -> bool {
+        const int st = jt % NS, b = jt & 1;
+        if (!__all_sync(0xffffffffu, mbar_spin(&full[st], (uint32_t)(jt / NS) & 1u))) return false;
+        tc_fence_after();
+        const uint64_t k_desc = umma_desc(smem_u32(sStage + st * L::kStage), 128, 1024);
+        if (lane == 0) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_f16_ss(tmem + b * 64, umma_desc(q_addr + ks * 256, 128, 1024), umma_desc(k_addr + ks * 256, 128, 1024),
-                        kIdescF16M128N64, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < 4; ++ks)   // +256 bytes per 16 dims: +16 in the descriptor's address field
+            umma_f16_ss(tmem + b * 64, q_desc + 16 * ks, k_desc + 16 * ks, kIdescF16M128N64, ks > 0 ? 1u : 0u);
           umma_commit(&s_full[b]);
         }
-        if (jt >= 1) {
-          const int jp = jt - 1, bp = jp & 1, stp = jp % NS;
-          if (!mbar_wait(&p_full[bp], (uint32_t)(jp >> 1) & 1u)) {
-            raise_error(kErrWaitOther);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP + bp * L::kPBuf);
-          const uint32_t v_addr = smem_u32(sStage + stp * L::kStage + 8192);
-          if (!I8) {
+        __syncwarp();
+        return true;
+      };
+      for (int jt = 0; jt < min(2, ntiles) && ok; ++jt) {
+        if (!issue_qk(jt)) {
+          raise_error(kErrWaitFull);
+          ok = false;
+        }
+      }
+      for (int jt = 0; jt < ntiles && ok; ++jt) {
+        const int bp = jt & 1, stp = jt % NS;
+        if (!__all_sync(0xffffffffu, mbar_spin(&p_full[bp], (uint32_t)(jt >> 1) & 1u))) {
+          raise_error(kErrWaitOther);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + bp * L::kPBuf);
+        const uint32_t v_addr = smem_u32(sStage + stp * L::kStage + 8192);
+        if (!I8) {
+          const uint64_t p_desc = umma_desc(p_addr, 128, 1024), v_desc = umma_desc(v_addr, 128, 512);
+          if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-              umma_f16_ss(tmem + 128, umma_desc(p_addr + ks * 256, 128, 1024),
-                          umma_desc(v_addr + (ks >> 1) * 4096 + (ks & 1) * 256, 128, 512), kIdescF16M128N64,
-                          (jp > 0 || ks > 0) ? 1u : 0u);
-          } else {
+              umma_f16_ss(tmem + 128, p_desc + 16 * ks, v_desc + 256 * (ks >> 1) + 16 * (ks & 1), kIdescF16M128N64,
+                          (jt > 0 || ks > 0) ? 1u : 0u);
+          }
+        } else {
+          const uint64_t p_desc = umma_desc(p_addr, 128, 512), v_desc = umma_desc(v_addr, 128, 256);
+          if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)
-              umma_i8_ss(tmem + 128 + bp * 64, umma_desc(p_addr + ks * 256, 128, 512),
-                         umma_desc(v_addr + ks * 2048, 128, 256), kIdescI8M128N64, ks > 0 ? 1u : 0u);
+              umma_i8_ss(tmem + 128 + bp * 64, p_desc + 16 * ks, v_desc + 128 * ks, kIdescI8M128N64, ks > 0 ? 1u : 0u);
           }
+        }
+        if (lane == 0) {
           umma_commit(&empty[stp]);
           umma_commit(&pv_done[bp]);
         }
+        __syncwarp();
+        if (jt + 2 < ntiles && !issue_qk(jt + 2)) {
+          raise_error(kErrWaitFull);
+          ok = false;
+        }
       }
       // Leave no tensor-core work in flight behind an abort.
-      umma_commit(drain);
+      if (lane == 0) umma_commit(drain);
+      __syncwarp();
       mbar_wait(drain, 0);
       if (!ok) atomicExch(&s_abort, 1);
     }

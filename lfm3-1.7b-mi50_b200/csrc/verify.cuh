@@ -43,7 +43,7 @@ constexpr int kVfOffStage = 16384;        // after Q
 constexpr int kVfOffP = kVfOffStage + kVfStages * kVfStage;
 constexpr int kVfOffML = kVfOffP + 4 * kVfPHalf;   // the second half's (max, sum) per row, for the merge
 constexpr int kVfOffBar = kVfOffML + 128 * 8;
-constexpr int kVfBars = 2 * kVfStages + 4 * 2 + 2;
+constexpr int kVfBars = 2 * kVfStages + 3 * 2 + 2;
 constexpr int kVfOffTmemSlot = kVfOffBar + kVfBars * 8;
 constexpr int kVfSmem = kVfOffTmemSlot + 16;
 
@@ -53,6 +53,11 @@ __device__ __forceinline__ float sigmoid_gate(const __half* gate, int row) {
   return 1.f / (1.f + exp2f(-g * kLog2e));
 }
 
+// DUP (m <= 16): quadrant q holds rows q m .. q m + m - 1 at lanes 0 .. m - 1 and the same rows again at lanes
+// 16 .. 16 + m - 1; the copies score the same keys, so lane 16 + i takes the upper 16 of its warpgroup's 32 keys
+// and lane i the lower 16, halving the exponentials per lane. Each lane keeps its own (max, sum, O row); the two
+// merge at the end. Without DUP (16 < m <= 32) lane = row over all 32 keys of the half.
+template <bool DUP>
 __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
   constexpr int NS = kVfStages;
   constexpr uint32_t kTmemCols = 256;   // S[2] at 0 and 64, O_0 at 128, O_1 at 192
@@ -66,8 +71,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
   uint64_t* full = bars;
   uint64_t* empty = bars + NS;
   uint64_t* s_full = bars + 2 * NS;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
+  uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* q_ready = pv_done + 2;
   uint64_t* drain = q_ready + 1;
@@ -86,7 +90,6 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], kVfSoftmaxWarps);
       mbar_init(&p_full[b], kVfSoftmaxWarps);
       mbar_init(&pv_done[b], 1);
     }
@@ -107,12 +110,16 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     // ================================================================ softmax warps, thread = query row
     const int half = warp >> 2, quad = warp & 3;
     const int pos = 32 * quad + lane;                 // M row / TMEM lane
-    const int r = quad * a.m + lane;                  // query row held at this lane
-    const bool row_ok = lane < a.m;                   // m <= 32: quadrant q holds rows q m .. q m + m - 1
+    const int sub = DUP ? lane >> 4 : 0;              // which 16 keys of the half (DUP)
+    const int li = DUP ? lane & 15 : lane;
+    const int r = quad * a.m + li;                    // query row held at this lane
+    const bool row_ok = li < a.m;                     // quadrant q holds rows q m .. q m + m - 1
+    constexpr int KL = DUP ? 16 : 32;                 // keys per lane per tile
     const int t = r >> 2, jh = r & 3;
     const int qpos = a.ctx_len + t;
     const int row = t * a.q_heads + 4 * h + jh;       // output / partial row (valid when row_ok)
     if (half == 0) {
+      // DUP: lane 16 + i stages the same query row as lane i.
       const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)(row_ok ? row : 0) * 64);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -123,6 +130,16 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
     }
+    if (DUP) {
+      // The other lane's 16 keys of each P row stay 0 for the whole split.
+#pragma unroll
+      for (int bb = 0; bb < 2; ++bb) {
+        uint8_t* pb = sP + (2 * bb + half) * kVfPHalf;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          *reinterpret_cast<uint4*>(pb + ((pos >> 3) * 4 + 2 * (1 - sub) + c) * 128 + (pos & 7) * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
     const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
     const uint32_t o_col = 128 + 64 * half;
     const int qlast = a.ctx_len + a.m - 1;
@@ -130,34 +147,36 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     bool ok = true;
     // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
     for (int jt = 0; jt < ntiles && ok; ++jt) {
-      const int b = jt & 1, k0 = (tile0 + jt) * kQuantBlock + 32 * half;
+      const int b = jt & 1, k0 = (tile0 + jt) * kQuantBlock + 32 * half + KL * sub;
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(jt >> 1) & 1u))) {
         raise_error(kErrWaitMma);
         ok = false;
         break;
       }
       tc_fence_after();
-      float x[32];
+      float x[KL];
       {
-        uint32_t rr[16];
+        uint32_t r0[16], r1[16];
+        tmem_ld16(lane_base + b * 64 + 32 * half, r0);
+        tmem_ld16(lane_base + b * 64 + 32 * half + 16, r1);
+        tmem_wait_ld();
+        if (DUP) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld16(lane_base + b * 64 + 32 * half + c * 16, rr);
-          tmem_wait_ld();
+          for (int e = 0; e < 16; ++e) x[e] = __uint_as_float(sub ? r1[e] : r0[e]);
+        } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[e]);
+          for (int e = 0; e < 16; ++e) {
+            x[e] = __uint_as_float(r0[e]);
+            x[(e + 16) % KL] = __uint_as_float(r1[e]);
+          }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[b]);
-
       // Masks only on edge tiles; raw scores are masked to -inf before the (scaled) max.
-      const bool interior = k0 >= a.start && k0 + 32 <= min(a.ctx_len, a.kv_end) &&
+      const bool interior = k0 >= a.start && k0 + KL <= min(a.ctx_len, a.kv_end) &&
                             (a.window == 0 || k0 > qlast - a.window);
       if (!interior) {
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
+        for (int k = 0; k < KL; ++k) {
           const int kpos = k0 + k;
           bool valid;
           if (kpos < a.ctx_len) valid = kpos >= a.start && kpos < a.kv_end && (a.window == 0 || kpos > qpos - a.window);
@@ -170,8 +189,10 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
         float t4[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) t4[u] = fmaxf(fmaxf(x[u], x[u + 4]), fmaxf(x[u + 8], x[u + 12]));
+        if (!DUP) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) t4[u] = fmaxf(t4[u], fmaxf(fmaxf(x[u + 16], x[u + 20]), fmaxf(x[u + 24], x[u + 28])));
+          for (int u = 0; u < 4; ++u) t4[u] = fmaxf(t4[u], fmaxf(fmaxf(x[(u + 16) % KL], x[(u + 20) % KL]), fmaxf(x[(u + 24) % KL], x[(u + 28) % KL])));
+        }
         mx = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3])) * a.qk_scale;
       }
       const bool grow_max = mx > m_run + kLazy;
@@ -203,26 +224,22 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
+      for (int k = 0; k < KL; ++k) {
         x[k] = fast_exp2(fmaf(x[k], a.qk_scale, neg_m));
         ls[k & 3] += x[k];
       }
       l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      // P_g[b] was last read by PV(jt - 2).
-      if (jt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
-        raise_error(kErrWaitMma);
-        ok = false;
-        break;
-      }
+      // P_g[b] was last read by PV(jt - 2), issued before QK(jt); the commit that signalled S(jt) covers every
+      // earlier tensor-core operation of the issuing thread, so that PV has finished.
       uint8_t* pb = sP + (2 * b + half) * kVfPHalf;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < KL / 8; ++c) {
         uint4 v;
         v.x = pack_half2(x[8 * c], x[8 * c + 1]);
         v.y = pack_half2(x[8 * c + 2], x[8 * c + 3]);
         v.z = pack_half2(x[8 * c + 4], x[8 * c + 5]);
         v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
-        *reinterpret_cast<uint4*>(pb + ((pos >> 3) * 4 + c) * 128 + (pos & 7) * 16) = v;
+        *reinterpret_cast<uint4*>(pb + ((pos >> 3) * 4 + (KL / 8) * sub + c) * 128 + (pos & 7) * 16) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -241,10 +258,10 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
       } else {
         tc_fence_after();
         const float2 mb = sML[pos];
-        const float M = fmaxf(m_run, mb.x);
+        float M = fmaxf(m_run, mb.x);
         const float f0 = m_run == -INFINITY ? 0.f : fast_exp2(m_run - M);
         const float f1 = mb.x == -INFINITY ? 0.f : fast_exp2(mb.x - M);
-        const float L = f0 * l_run + f1 * mb.y;
+        float L = f0 * l_run + f1 * mb.y;
         float o[64];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -255,7 +272,17 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) o[c * 16 + e] = f0 * __uint_as_float(r0[e]) + f1 * __uint_as_float(r1[e]);
         }
-        if (row_ok) {
+        if (DUP) {
+          // Lanes i and 16 + i hold the same row over different keys: merge them (lane i keeps the result).
+          const float Mo = __shfl_xor_sync(0xffffffffu, M, 16), Lo = __shfl_xor_sync(0xffffffffu, L, 16);
+          const float Mm = fmaxf(M, Mo);
+          const float fa = M == -INFINITY ? 0.f : fast_exp2(M - Mm), fb = Mo == -INFINITY ? 0.f : fast_exp2(Mo - Mm);
+#pragma unroll
+          for (int d = 0; d < 64; ++d) o[d] = fa * o[d] + fb * __shfl_xor_sync(0xffffffffu, o[d], 16);
+          M = Mm;
+          L = fa * L + fb * Lo;
+        }
+        if (row_ok && sub == 0) {
           if (a.out) {
             const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(a.gate, row);
             uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)row * 64);
@@ -279,80 +306,96 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     }
   } else if (warp == kVfSoftmaxWarps) {
     // ================================================================ producer
-    if (lane == 0) {
+    // The whole warp runs the loop; lane 0 issues the copies.
+    {
       const int pv0 = a.kv_begin / kBlockTokens, pv1 = (a.kv_end - 1) / kBlockTokens;   // pages this cache holds
       int issued = 0;
       for (int jt = 0; jt < ntiles; ++jt) {
         const int st = jt % NS;
-        if (jt >= NS && !mbar_wait(&empty[st], (uint32_t)((jt / NS) - 1) & 1u)) {
+        if (jt >= NS && !__all_sync(0xffffffffu, mbar_spin(&empty[st], (uint32_t)((jt / NS) - 1) & 1u))) {
           raise_error(kErrWaitEmpty);
           atomicExch(&s_abort, 1);
           break;
         }
-        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) break;
         const int lp = (tile0 + jt) * 2;
         // A page outside the held range may have no table entry: copy a held page instead (its keys are masked).
         const int lp0 = min(max(lp, pv0), pv1), lp1 = min(max(lp + 1, pv0), pv1);
         const char* s0 = a.g.pool + phys_block(a.g, lp0) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
         const char* s1 = a.g.pool + phys_block(a.g, lp1) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
         uint8_t* dst = sStage + st * kVfStage;
-        mbar_arrive_expect_tx(&full[st], kVfStage);
-        bulk_g2s(dst, s0, 4096, &full[st]);
-        bulk_g2s(dst + 4096, s1, 4096, &full[st]);
-        bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV, 4096, &full[st]);
-        bulk_g2s(dst + 12288, s1 + F16Section<64>::kOffV, 4096, &full[st]);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[st], kVfStage);
+          bulk_g2s(dst, s0, 4096, &full[st]);
+          bulk_g2s(dst + 4096, s1, 4096, &full[st]);
+          bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV, 4096, &full[st]);
+          bulk_g2s(dst + 12288, s1 + F16Section<64>::kOffV, 4096, &full[st]);
+        }
+        __syncwarp();
         issued = jt + 1;
       }
-      if (*reinterpret_cast<volatile int*>(&s_abort)) {
+      // On an abort, wait (bounded) for the copies still landing in shared memory.
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
         for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
       }
     }
   } else {
     // ================================================================ MMA issuer
-    if (lane == 0) {
-      bool ok = mbar_wait(q_ready, 0);
+    // QK runs two tiles ahead of PV: after PV(j), S buffer j & 1 is free (the softmax read S(j) before it
+    // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores.
+    // The whole warp runs the loop (its values stay warp-uniform); lane 0 alone issues the tensor-core work.
+    {
+      bool ok = __all_sync(0xffffffffu, mbar_spin(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
-      const uint32_t q_addr = smem_u32(sQ);
-      for (int jt = 0; jt <= ntiles && ok; ++jt) {
-        if (jt < ntiles) {
-          const int st = jt % NS, b = jt & 1;
-          if (!mbar_wait(&full[st], (uint32_t)(jt / NS) & 1u) ||
-              (jt >= 2 && !mbar_wait(&s_free[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
-            raise_error(kErrWaitFull);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sStage + st * kVfStage);
+      const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
+      auto issue_qk = [&](int jt) -> bool {
+        const int st = jt % NS, b = jt & 1;
+        if (!__all_sync(0xffffffffu, mbar_spin(&full[st], (uint32_t)(jt / NS) & 1u))) return false;
+        tc_fence_after();
+        const uint64_t k_desc = umma_desc(smem_u32(sStage + st * kVfStage), 128, 1024);
+        if (lane == 0) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_f16_ss(tmem + b * 64, umma_desc(q_addr + ks * 256, 128, 1024), umma_desc(k_addr + ks * 256, 128, 1024),
-                        kIdescF16M128N64, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < 4; ++ks)   // +256 bytes per 16 dims: +16 in the descriptor's address field
+            umma_f16_ss(tmem + b * 64, q_desc + 16 * ks, k_desc + 16 * ks, kIdescF16M128N64, ks > 0 ? 1u : 0u);
           umma_commit(&s_full[b]);
         }
-        if (jt >= 1) {
-          const int jp = jt - 1, bp = jp & 1, stp = jp % NS;
-          if (!mbar_wait(&p_full[bp], (uint32_t)(jp >> 1) & 1u)) {
-            raise_error(kErrWaitOther);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sStage + stp * kVfStage + 8192);
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            const uint32_t p_addr = smem_u32(sP + (2 * bp + g) * kVfPHalf);
-#pragma unroll
-            for (int ks = 0; ks < 2; ++ks)
-              umma_f16_ss(tmem + 128 + 64 * g, umma_desc(p_addr + ks * 256, 128, 512),
-                          umma_desc(v_addr + g * 4096 + ks * 256, 128, 512), kIdescF16M128N64,
-                          (jp > 0 || ks > 0) ? 1u : 0u);
-          }
-          umma_commit(&empty[stp]);
-          umma_commit(&pv_done[bp]);
+        __syncwarp();
+        return true;
+      };
+      for (int jt = 0; jt < min(2, ntiles) && ok; ++jt) {
+        if (!issue_qk(jt)) {
+          raise_error(kErrWaitFull);
+          ok = false;
         }
       }
-      umma_commit(drain);
+      for (int jt = 0; jt < ntiles && ok; ++jt) {
+        const int b = jt & 1, st = jt % NS;
+        if (!__all_sync(0xffffffffu, mbar_spin(&p_full[b], (uint32_t)(jt >> 1) & 1u))) {
+          raise_error(kErrWaitOther);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t v_desc = umma_desc(smem_u32(sStage + st * kVfStage + 8192), 128, 512);
+        const uint64_t p_desc = umma_desc(smem_u32(sP + 2 * b * kVfPHalf), 128, 512);
+        if (lane == 0) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g)
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)   // P half g at +8 KiB (+512), V page g at +4 KiB (+256)
+              umma_f16_ss(tmem + 128 + 64 * g, p_desc + 512 * g + 16 * ks, v_desc + 256 * g + 16 * ks, kIdescF16M128N64,
+                          (jt > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&empty[st]);
+          umma_commit(&pv_done[b]);
+        }
+        __syncwarp();
+        if (jt + 2 < ntiles && !issue_qk(jt + 2)) {
+          raise_error(kErrWaitFull);
+          ok = false;
+        }
+      }
+      if (lane == 0) umma_commit(drain);
+      __syncwarp();
       mbar_wait(drain, 0);
       if (!ok) atomicExch(&s_abort, 1);
     }
