@@ -102,7 +102,8 @@ int launch_v8(const lfm3a_kv_view* kv, int qb0, int qb1, int len, cudaStream_t s
 
 int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count) {
   const int start = window > 0 ? std::max(0, ctx_len - window + 1) : 0;
-  const int t_total = (ctx_len + m - 1) / kQuantBlock - start / kQuantBlock + 1;
+  const int tile_keys = m <= 16 ? 128 : 64;
+  const int t_total = (ctx_len + m - 1) / tile_keys - start / tile_keys + 1;
   // Two resident blocks per SM, at least two 64-key tiles per split.
   int splits = (2 * sm_count + kv_heads - 1) / kv_heads;
   splits = std::min(splits, std::max(1, t_total / 2));
@@ -111,11 +112,10 @@ int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count
 
 int launch_combine(const float* part, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
                    const __half* gate, __half* out16, float* out32, cudaStream_t st) {
-  const int blocks = (rows + 3) / 4;
   if (head_dim == 64)
-    combine_kernel<64><<<blocks, 128, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
+    combine_kernel<64><<<(rows + 3) / 4, 256, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
   else
-    combine_kernel<128><<<blocks, 128, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
+    combine_kernel<128><<<(rows + 1) / 2, 256, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
   return check_launch("combine_kernel");
 }
 
@@ -144,10 +144,12 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   a.kv_begin = kv_begin;
   a.kv_end = kv_end;
   a.start = std::max(kv_begin, window > 0 ? std::max(0, ctx_len - window + 1) : 0);
-  // 64-key tiles over [start, kv_end); a shard wholly below the window start runs its last tile, all masked.
-  a.t_begin = std::min(a.start, kv_end - 1) / kQuantBlock;
-  a.t_total = (kv_end - 1) / kQuantBlock - a.t_begin + 1;
-  if (splits <= 0) splits = verify_splits_for(L.kv_heads, a.t_total * kQuantBlock, 1, 0, current_sm_count());
+  // Key tiles over [start, kv_end): 128 keys for up to 16 tokens (M = 64 kernel), else 64; a shard wholly below
+  // the window start runs its last tile, all masked.
+  const int tile_keys = m <= 16 ? 128 : 64;
+  a.t_begin = std::min(a.start, kv_end - 1) / tile_keys;
+  a.t_total = (kv_end - 1) / tile_keys - a.t_begin + 1;
+  if (splits <= 0) splits = verify_splits_for(L.kv_heads, a.t_total * tile_keys, 1, 0, current_sm_count());
   a.splits = std::min(splits, a.t_total);
   a.qk_scale = 0.125f * kLog2e;
   const int rows = m * q_heads;
@@ -166,9 +168,9 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   const dim3 grid(a.splits, L.kv_heads);
   static bool done[2][64];
   if (m <= 16) {
-    rc = ensure_smem(verify_kernel<true>, kVfSmem, done[1]);
+    rc = ensure_smem(verify_m64_kernel, kV6Smem, done[1]);
     if (rc != LFM3A_OK) return rc;
-    verify_kernel<true><<<grid, kVfThreads, kVfSmem, st>>>(a);
+    verify_m64_kernel<<<grid, kVfThreads, kV6Smem, st>>>(a);
   } else {
     rc = ensure_smem(verify_kernel<false>, kVfSmem, done[0]);
     if (rc != LFM3A_OK) return rc;

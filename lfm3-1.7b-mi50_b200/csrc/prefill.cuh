@@ -332,7 +332,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
       int issued = 0;
       for (int jt = 0; jt < ntiles; ++jt) {
         const int st = jt % NS;
-        if (jt >= NS && !__all_sync(0xffffffffu, mbar_spin(&empty[st], (uint32_t)((jt / NS) - 1) & 1u))) {
+        if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&empty[st], (uint32_t)((jt / NS) - 1) & 1u))) {
           raise_error(kErrWaitEmpty);
           atomicExch(&s_abort, 1);
           break;
@@ -371,12 +371,12 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
     // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores.
     // The whole warp runs the loop (its values stay warp-uniform); lane 0 alone issues the tensor-core work.
     {
-      bool ok = __all_sync(0xffffffffu, mbar_spin(q_ready, 0));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
       const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
       auto issue_qk = [&](int jt) -> bool {
         const int st = jt % NS, b = jt & 1;
-        if (!__all_sync(0xffffffffu, mbar_spin(&full[st], (uint32_t)(jt / NS) & 1u))) return false;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (uint32_t)(jt / NS) & 1u))) return false;
         tc_fence_after();
         const uint64_t k_desc = umma_desc(smem_u32(sStage + st * L::kStage), 128, 1024);
         if (lane == 0) {
@@ -396,7 +396,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
       }
       for (int jt = 0; jt < ntiles && ok; ++jt) {
         const int bp = jt & 1, stp = jt % NS;
-        if (!__all_sync(0xffffffffu, mbar_spin(&p_full[bp], (uint32_t)(jt >> 1) & 1u))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_full[bp], (uint32_t)(jt >> 1) & 1u))) {
           raise_error(kErrWaitOther);
           ok = false;
           break;

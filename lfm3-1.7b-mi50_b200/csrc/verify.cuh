@@ -36,16 +36,18 @@ struct VerifyArgs {
 constexpr int kVerifyPart = 66;           // acc[64], max, sum
 constexpr int kVfSoftmaxWarps = 8;
 constexpr int kVfThreads = (kVfSoftmaxWarps + 2) * 32;
-constexpr int kVfStages = 3;
+constexpr int kVfStages = 4;
 constexpr int kVfStage = 16384;           // K (2 pages) | V (2 pages)
 constexpr int kVfPHalf = 8192;            // 128 rows x 32 keys fp16
 constexpr int kVfOffStage = 16384;        // after Q
 constexpr int kVfOffP = kVfOffStage + kVfStages * kVfStage;
-constexpr int kVfOffML = kVfOffP + 4 * kVfPHalf;   // the second half's (max, sum) per row, for the merge
-constexpr int kVfOffBar = kVfOffML + 128 * 8;
-constexpr int kVfBars = 2 * kVfStages + 3 * 2 + 2;
+constexpr int kVfOffBar = kVfOffP + 4 * kVfPHalf;
+constexpr int kVfBars = 2 * kVfStages + 4 * 2 + 2;   // full, empty, s_full[2], p_full[2][2], pv_done[2], q_ready, drain
 constexpr int kVfOffTmemSlot = kVfOffBar + kVfBars * 8;
+constexpr int kVfOffAbort = kVfOffTmemSlot + 4;
 constexpr int kVfSmem = kVfOffTmemSlot + 16;
+// The second warpgroup's (max, sum) per row, for the final merge, lives in the Q region: every QK has
+// finished by the time the last tile's softmax runs.
 
 __device__ __forceinline__ float sigmoid_gate(const __half* gate, int row) {
   if (!gate) return 1.f;
@@ -62,17 +64,17 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
   constexpr int NS = kVfStages;
   constexpr uint32_t kTmemCols = 256;   // S[2] at 0 and 64, O_0 at 128, O_1 at 192
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ int s_abort;
+  int& s_abort = *reinterpret_cast<int*>(smem + kVfOffAbort);
   uint8_t* sQ = smem;
   uint8_t* sStage = smem + kVfOffStage;
   uint8_t* sP = smem + kVfOffP;          // [buffer b][half g] 8 KiB each
-  float2* sML = reinterpret_cast<float2*>(smem + kVfOffML);
+  float2* sML = reinterpret_cast<float2*>(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kVfOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + NS;
   uint64_t* s_full = bars + 2 * NS;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
+  uint64_t* p_full = s_full + 2;         // [buffer b][half g]
+  uint64_t* pv_done = p_full + 4;
   uint64_t* q_ready = pv_done + 2;
   uint64_t* drain = q_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kVfOffTmemSlot);
@@ -90,7 +92,8 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], kVfSoftmaxWarps);
+      mbar_init(&p_full[2 * b], kVfSoftmaxWarps / 2);
+      mbar_init(&p_full[2 * b + 1], kVfSoftmaxWarps / 2);
       mbar_init(&pv_done[b], 1);
     }
     mbar_init(q_ready, 4);
@@ -244,7 +247,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(&p_full[2 * b + half]);
     }
     if (!ok) atomicExch(&s_abort, 1);
     // Merge the halves: the second warpgroup hands (max, sum) over; the first reads both O_g from TMEM.
@@ -312,7 +315,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
       int issued = 0;
       for (int jt = 0; jt < ntiles; ++jt) {
         const int st = jt % NS;
-        if (jt >= NS && !__all_sync(0xffffffffu, mbar_spin(&empty[st], (uint32_t)((jt / NS) - 1) & 1u))) {
+        if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&empty[st], (uint32_t)((jt / NS) - 1) & 1u))) {
           raise_error(kErrWaitEmpty);
           atomicExch(&s_abort, 1);
           break;
@@ -345,12 +348,12 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores.
     // The whole warp runs the loop (its values stay warp-uniform); lane 0 alone issues the tensor-core work.
     {
-      bool ok = __all_sync(0xffffffffu, mbar_spin(q_ready, 0));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
       const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
       auto issue_qk = [&](int jt) -> bool {
         const int st = jt % NS, b = jt & 1;
-        if (!__all_sync(0xffffffffu, mbar_spin(&full[st], (uint32_t)(jt / NS) & 1u))) return false;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (uint32_t)(jt / NS) & 1u))) return false;
         tc_fence_after();
         const uint64_t k_desc = umma_desc(smem_u32(sStage + st * kVfStage), 128, 1024);
         if (lane == 0) {
@@ -370,21 +373,27 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
       }
       for (int jt = 0; jt < ntiles && ok; ++jt) {
         const int b = jt & 1, st = jt % NS;
-        if (!__all_sync(0xffffffffu, mbar_spin(&p_full[b], (uint32_t)(jt >> 1) & 1u))) {
-          raise_error(kErrWaitOther);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const uint64_t v_desc = umma_desc(smem_u32(sStage + st * kVfStage + 8192), 128, 512);
         const uint64_t p_desc = umma_desc(smem_u32(sP + 2 * b * kVfPHalf), 128, 512);
-        if (lane == 0) {
+        // Each warpgroup's half of the keys goes to the tensor core as soon as that warpgroup hands its P over.
 #pragma unroll
-          for (int g = 0; g < 2; ++g)
+        for (int g = 0; g < 2; ++g) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&p_full[2 * b + g], (uint32_t)(jt >> 1) & 1u))) {
+            raise_error(kErrWaitOther);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)   // P half g at +8 KiB (+512), V page g at +4 KiB (+256)
               umma_f16_ss(tmem + 128 + 64 * g, p_desc + 512 * g + 16 * ks, v_desc + 256 * g + 16 * ks, kIdescF16M128N64,
                           (jt > 0 || ks > 0) ? 1u : 0u);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (lane == 0) {
           umma_commit(&empty[st]);
           umma_commit(&pv_done[b]);
         }
@@ -409,22 +418,404 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
   }
 }
 
-// Log-sum-exp merge of split partials, one warp per (token, query head) row. Partial s of row r starts
-// at part + r * row_stride + s * split_stride (floats). With out16 the result is the gate-scaled fp16
-// output; otherwise the merged partial (acc relative to the common max, max, sum) goes to out32[r][D + 2].
+// ---------------------------------------------------------------- up to 16 verified tokens: M = 64 MMAs
+// The 4m <= 64 real query rows are the M = 64 operand. An M = 64 accumulator occupies TMEM lanes
+// (r % 16) + 32 (r / 16) of its rows r; a second one at lane offset 16 fills the other lanes. Here the two
+// hold the same 64 rows against the two 64-key halves of a 128-key tile (h = 0: keys 0..63 at lane offset 0,
+// h = 1: keys 64..127 at offset 16), so every lane of the softmax warps scores a distinct (row, key range) and
+// no MMA row is padding. Warpgroup g takes keys 32 g .. 32 g + 31 of each half: per tile a lane handles 32
+// keys of one row. QK is two interleaved M64 N64 chains per tile; PV is four independent M64 N64 chains
+// (warpgroup g, half h) into O_g at lane offset 16 h, so the tensor pipe overlaps them.
+constexpr int kV6Stages = 2;               // per ring
+constexpr int kV6Ring = 16384;             // K (or V) of one 128-key tile: 4 pages
+constexpr int kV6OffStage = 8192;          // after Q: 64 rows x 64 dims fp16; then the K ring, then the V ring
+constexpr int kV6PBuf = 16384;             // [warpgroup g][half h] 64 rows x 32 keys fp16, 4 KiB each
+constexpr int kV6OffP = kV6OffStage + 2 * kV6Stages * kV6Ring;
+constexpr int kV6OffBar = kV6OffP + 2 * kV6PBuf;
+constexpr int kV6Bars = 4 * kV6Stages + 2 + 4 + 2 + 2;   // K/V full/empty, s_full[2], p_full[2][2], pv_done[2], q_ready, drain
+constexpr int kV6OffTmemSlot = kV6OffBar + kV6Bars * 8;
+constexpr int kV6OffAbort = kV6OffTmemSlot + 4;
+constexpr int kV6Smem = kV6OffTmemSlot + 16;
+constexpr uint32_t kIdescF16M64N64 = (1u << 4) | ((64u >> 3) << 17) | ((64u >> 4) << 24);
+
+__global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a) {
+  constexpr int NS = kV6Stages;   // per ring: K tiles and V tiles have separate rings
+  constexpr uint32_t kTmemCols = 256;   // S[2] at columns 0 and 64, O_0 at 128, O_1 at 192 (halves at lane +0 / +16)
+  extern __shared__ __align__(1024) uint8_t smem[];
+  int& s_abort = *reinterpret_cast<int*>(smem + kV6OffAbort);
+  uint8_t* sQ = smem;
+  uint8_t* sStage = smem + kV6OffStage;
+  uint8_t* sP = smem + kV6OffP;          // [buffer b][warpgroup g][half h]
+  float2* sML = reinterpret_cast<float2*>(smem);   // Q is dead once the last QK finished
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kV6OffBar);
+  uint64_t* k_full = bars;             // K ring: loaded / released once QK of the tile finished
+  uint64_t* k_empty = bars + NS;
+  uint64_t* v_full = bars + 2 * NS;    // V ring: loaded / released once PV of the tile finished
+  uint64_t* v_empty = bars + 3 * NS;
+  uint64_t* s_full = bars + 4 * NS;
+  uint64_t* p_full = s_full + 2;         // [buffer b][warpgroup g]
+  uint64_t* pv_done = p_full + 4;
+  uint64_t* q_ready = pv_done + 2;
+  uint64_t* drain = q_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kV6OffTmemSlot);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, h = blockIdx.y;
+  const int tile0 = a.t_begin + (int)((int64_t)a.t_total * split / a.splits);
+  const int ntiles = a.t_begin + (int)((int64_t)a.t_total * (split + 1) / a.splits) - tile0;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[2 * b], 4);
+      mbar_init(&p_full[2 * b + 1], 4);
+      mbar_init(&pv_done[b], 1);
+    }
+    mbar_init(q_ready, 4);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == kVfSoftmaxWarps + 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < kVfSoftmaxWarps) {
+    // ================================================================ softmax warps
+    const int g = warp >> 2, quad = warp & 3, hh = lane >> 4;
+    const int r = 16 * quad + (lane & 15);            // query row of this lane (both halves)
+    const bool row_ok = r < 4 * a.m;
+    const int t = r >> 2, jh = r & 3;
+    const int qpos = a.ctx_len + t;
+    const int row = t * a.q_heads + 4 * h + jh;       // output / partial row (valid when row_ok)
+    if (g == 0) {
+      if (hh == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)(row_ok ? row : 0) * 64);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
+    const uint32_t o_col = 128 + 64 * g;
+    const int qlast = a.ctx_len + a.m - 1;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
+    for (int jt = 0; jt < ntiles && ok; ++jt) {
+      const int b = jt & 1, k0 = (tile0 + jt) * 128 + 64 * hh + 32 * g;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(jt >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[32];
+      {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(lane_base + b * 64 + 32 * g, r0);
+        tmem_ld16(lane_base + b * 64 + 32 * g + 16, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          x[e] = __uint_as_float(r0[e]);
+          x[16 + e] = __uint_as_float(r1[e]);
+        }
+      }
+      const bool interior = k0 >= a.start && k0 + 32 <= min(a.ctx_len, a.kv_end) &&
+                            (a.window == 0 || k0 > qlast - a.window);
+      if (!interior) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int kpos = k0 + k;
+          bool valid;
+          if (kpos < a.ctx_len) valid = kpos >= a.start && kpos < a.kv_end && (a.window == 0 || kpos > qpos - a.window);
+          else valid = kpos <= qpos && kpos < a.kv_end;
+          x[k] = (valid && row_ok) ? x[k] : -INFINITY;
+        }
+      }
+      float mx;
+      {
+        float t4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          t4[u] = fmaxf(fmaxf(fmaxf(x[u], x[u + 4]), fmaxf(x[u + 8], x[u + 12])),
+                        fmaxf(fmaxf(x[u + 16], x[u + 20]), fmaxf(x[u + 24], x[u + 28])));
+        mx = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3])) * a.qk_scale;
+      }
+      const bool grow_max = mx > m_run + kLazy;
+      if (__any_sync(0xffffffffu, grow_max)) {
+        const float corr = grow_max ? fast_exp2(m_run - mx) : 1.f;
+        if (grow_max) m_run = mx;
+        l_run *= corr;
+        if (jt >= 1) {
+          // O_g holds PV up to the previous tile: wait for it, then rescale this lane's row in TMEM.
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
+            raise_error(kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t rr[16];
+            tmem_ld16(lane_base + o_col + c * 16, rr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+            tmem_st16(lane_base + o_col + c * 16, rr);
+          }
+          tmem_wait_st();
+        }
+      }
+      // p = 2^(s * scale - m): masked scores are -inf and give 0; a row without a valid key so far uses 0.
+      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        x[k] = fast_exp2(fmaf(x[k], a.qk_scale, neg_m));
+        ls[k & 3] += x[k];
+      }
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      // P_{g,h}[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
+      uint8_t* pb = sP + b * kV6PBuf + (2 * g + hh) * 4096;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 v;
+        v.x = pack_half2(x[8 * c], x[8 * c + 1]);
+        v.y = pack_half2(x[8 * c + 2], x[8 * c + 3]);
+        v.z = pack_half2(x[8 * c + 4], x[8 * c + 5]);
+        v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
+        *reinterpret_cast<uint4*>(pb + ((r >> 3) * 4 + c) * 128 + (r & 7) * 16) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[2 * b + g]);
+    }
+    if (!ok) atomicExch(&s_abort, 1);
+    // Merge: warpgroup 1 hands (max, sum) over per lane; warpgroup 0 reads both O_g from TMEM, then the two
+    // halves of a row (lanes i and 16 + i) merge through shuffles.
+    if (g == 1) sML[32 * quad + lane] = make_float2(m_run, l_run);
+    named_bar_sync(1, kVfSoftmaxWarps * 32);
+    const int last = ntiles - 1;
+    if (g == 0 && !*reinterpret_cast<volatile int*>(&s_abort)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[last & 1], (uint32_t)(last >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        atomicExch(&s_abort, 1);
+      } else {
+        tc_fence_after();
+        const float2 mb = sML[32 * quad + lane];
+        float M = fmaxf(m_run, mb.x);
+        const float f0 = m_run == -INFINITY ? 0.f : fast_exp2(m_run - M);
+        const float f1 = mb.x == -INFINITY ? 0.f : fast_exp2(mb.x - M);
+        float L = f0 * l_run + f1 * mb.y;
+        float o[64];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r0[16], r1[16];
+          tmem_ld16(lane_base + 128 + c * 16, r0);
+          tmem_ld16(lane_base + 192 + c * 16, r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[c * 16 + e] = f0 * __uint_as_float(r0[e]) + f1 * __uint_as_float(r1[e]);
+        }
+        {
+          const float Mo = __shfl_xor_sync(0xffffffffu, M, 16), Lo = __shfl_xor_sync(0xffffffffu, L, 16);
+          const float Mm = fmaxf(M, Mo);
+          const float fa = M == -INFINITY ? 0.f : fast_exp2(M - Mm), fb = Mo == -INFINITY ? 0.f : fast_exp2(Mo - Mm);
+#pragma unroll
+          for (int d = 0; d < 64; ++d) o[d] = fa * o[d] + fb * __shfl_xor_sync(0xffffffffu, o[d], 16);
+          M = Mm;
+          L = fa * L + fb * Lo;
+        }
+        if (row_ok && hh == 0) {
+          if (a.out) {
+            const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(a.gate, row);
+            uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)row * 64);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint4 v;
+              v.x = pack_half2(o[8 * c] * scale, o[8 * c + 1] * scale);
+              v.y = pack_half2(o[8 * c + 2] * scale, o[8 * c + 3] * scale);
+              v.z = pack_half2(o[8 * c + 4] * scale, o[8 * c + 5] * scale);
+              v.w = pack_half2(o[8 * c + 6] * scale, o[8 * c + 7] * scale);
+              dst[c] = v;
+            }
+          } else {
+            float* dst = a.part + ((int64_t)row * a.splits + split) * kVerifyPart;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) *reinterpret_cast<float2*>(dst + 2 * c) = make_float2(o[2 * c], o[2 * c + 1]);
+            *reinterpret_cast<float2*>(dst + 64) = make_float2(M, L);
+          }
+        }
+      }
+    }
+  } else if (warp == kVfSoftmaxWarps) {
+    // ================================================================ producer: K and V rings, 4 pages per tile
+    // Order K(0), K(1), then V(j), K(j + 2): V(j) waits for PV(j - 2) and K(j + 2) for QK(j), which finish
+    // at about the same time, and each load lands two tiles before its MMA wants it.
+    {
+      const int pv0 = a.kv_begin / kBlockTokens, pv1 = (a.kv_end - 1) / kBlockTokens;   // pages this cache holds
+      auto load = [&](int jt, bool is_v) -> bool {
+        const int st = jt % NS;
+        uint64_t* emp = is_v ? v_empty : k_empty;
+        uint64_t* ful = is_v ? v_full : k_full;
+        if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&emp[st], (uint32_t)((jt / NS) - 1) & 1u))) return false;
+        const int lp = (tile0 + jt) * 4;
+        uint8_t* dst = sStage + (is_v ? NS * kV6Ring : 0) + st * kV6Ring;
+        const char* src[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // A page outside the held range may have no table entry: copy a held page instead (its keys are masked).
+          const int pg = min(max(lp + e, pv0), pv1);
+          src[e] = a.g.pool + phys_block(a.g, pg) * a.g.block_bytes + (int64_t)h * a.g.head_bytes +
+                   (is_v ? F16Section<64>::kOffV : 0);
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&ful[st], kV6Ring);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) bulk_g2s(dst + 4096 * e, src[e], 4096, &ful[st]);
+        }
+        __syncwarp();
+        return true;
+      };
+      bool ok = true;
+      int k_issued = 0, v_issued = 0;
+      for (int jt = 0; jt < min(2, ntiles) && ok; ++jt) ok = load(jt, false), k_issued += ok;
+      for (int jt = 0; jt < ntiles && ok; ++jt) {
+        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) break;
+        ok = load(jt, true);
+        v_issued += ok;
+        if (ok && jt + 2 < ntiles) ok = load(jt + 2, false), k_issued += ok;
+      }
+      if (!ok) {
+        raise_error(kErrWaitEmpty);
+        atomicExch(&s_abort, 1);
+      }
+      // On an abort, wait (bounded) for the copies still landing in shared memory.
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
+        for (int jt = max(0, k_issued - NS); jt < k_issued; ++jt) mbar_wait(&k_full[jt % NS], (uint32_t)(jt / NS) & 1u);
+        for (int jt = max(0, v_issued - NS); jt < v_issued; ++jt) mbar_wait(&v_full[jt % NS], (uint32_t)(jt / NS) & 1u);
+      }
+    }
+  } else {
+    // ================================================================ MMA issuer (the whole warp loops, lane 0 issues)
+    {
+      bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
+      if (!ok) raise_error(kErrWaitOther);
+      const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
+      auto issue_qk = [&](int jt) -> bool {
+        const int st = jt % NS, b = jt & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (uint32_t)(jt / NS) & 1u))) return false;
+        tc_fence_after();
+        const uint64_t k_desc = umma_desc(smem_u32(sStage + st * kV6Ring), 128, 1024);
+        if (lane == 0) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh)   // keys 64 hh..: +8 KiB (+512); lanes +16 hh
+              umma_f16_ss(tmem + ((uint32_t)(16 * hh) << 16) + b * 64, q_desc + 16 * ks, k_desc + 512 * hh + 16 * ks,
+                          kIdescF16M64N64, ks > 0 ? 1u : 0u);
+          umma_commit(&s_full[b]);
+          umma_commit(&k_empty[st]);
+        }
+        __syncwarp();
+        return true;
+      };
+      for (int jt = 0; jt < min(2, ntiles) && ok; ++jt) {
+        if (!issue_qk(jt)) {
+          raise_error(kErrWaitFull);
+          ok = false;
+        }
+      }
+      for (int jt = 0; jt < ntiles && ok; ++jt) {
+        const int b = jt & 1, st = jt % NS;
+        const uint64_t v_desc = umma_desc(smem_u32(sStage + NS * kV6Ring + st * kV6Ring), 128, 512);
+        if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (uint32_t)(jt / NS) & 1u))) {
+          raise_error(kErrWaitFull);
+          ok = false;
+          break;
+        }
+        const uint64_t p_desc = umma_desc(smem_u32(sP + b * kV6PBuf), 128, 512);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&p_full[2 * b + g], (uint32_t)(jt >> 1) & 1u))) {
+            raise_error(kErrWaitOther);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh)   // P_{g,h} at +4 KiB (2g + h); V page 2h + g at +4 KiB each
+                umma_f16_ss(tmem + ((uint32_t)(16 * hh) << 16) + 128 + 64 * g, p_desc + 256 * (2 * g + hh) + 16 * ks,
+                            v_desc + 256 * (2 * hh + g) + 16 * ks, kIdescF16M64N64, (jt > 0 || ks > 0) ? 1u : 0u);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (lane == 0) {
+          umma_commit(&v_empty[st]);
+          umma_commit(&pv_done[b]);
+        }
+        __syncwarp();
+        if (jt + 2 < ntiles && !issue_qk(jt + 2)) {
+          raise_error(kErrWaitFull);
+          ok = false;
+        }
+      }
+      if (lane == 0) umma_commit(drain);
+      __syncwarp();
+      mbar_wait(drain, 0);
+      if (!ok) atomicExch(&s_abort, 1);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kVfSoftmaxWarps + 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Log-sum-exp merge of split partials. Thread = (row, dim): 256 / D rows per block. Partial s of row r starts
+// at part + r * row_stride + s * split_stride (floats). Each warp of a row reduces the splits' (max, sum) with
+// its lanes striding over the splits, then every thread sums 2^(m_s - M) acc_s[dim] with 16 splits' loads in
+// flight at a time. With out16 the result is the gate-scaled fp16 output; otherwise the merged partial (acc
+// relative to the common max, max, sum) goes to out32[r][D + 2].
 template <int D>
-__global__ __launch_bounds__(128) void combine_kernel(const float* part, int rows, int splits, int64_t split_stride,
+__global__ __launch_bounds__(256) void combine_kernel(const float* part, int rows, int splits, int64_t split_stride,
                                                       int64_t row_stride, const __half* gate, __half* out16,
                                                       float* out32) {
-  constexpr int P = D + 2, E = D / 32;
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  constexpr int RPB = 256 / D, CH = 16;
+  const int d = threadIdx.x % D, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * RPB + threadIdx.x / D;
+  if (row >= rows) return;   // D is a multiple of 32: whole warps leave together
   const float* base = part + (int64_t)row * row_stride;
   float M = -INFINITY;
   for (int s = lane; s < splits; s += 32) M = fmaxf(M, base[(int64_t)s * split_stride + D]);
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  // Sum of the splits' l weighted by 2^(m_s - M): lanes take splits, then a warp sum.
   float L = 0.f;
   for (int s = lane; s < splits; s += 32) {
     const float* p = base + (int64_t)s * split_stride;
@@ -433,37 +824,26 @@ __global__ __launch_bounds__(128) void combine_kernel(const float* part, int row
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  // acc: every lane its E dims over all splits, 8 splits' loads in flight at a time.
-  float acc[E];
+  float acc = 0.f;
+  for (int s0 = 0; s0 < splits; s0 += CH) {
+    float ms[CH], v[CH];
 #pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  for (int s0 = 0; s0 < splits; s0 += 8) {
-    float f[8], v[8][E];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < CH; ++u) {
       const int s = s0 + u;
       const float* p = base + (int64_t)min(s, splits - 1) * split_stride;
-      const float ms = p[D];
-      f[u] = (s < splits && ms != -INFINITY) ? ms : -INFINITY;
-#pragma unroll
-      for (int e = 0; e < E; ++e) v[u][e] = p[lane * E + e];
+      ms[u] = s < splits ? p[D] : -INFINITY;
+      v[u] = p[d];
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float w = f[u] == -INFINITY ? 0.f : exp2f(f[u] - M);
-#pragma unroll
-      for (int e = 0; e < E; ++e) acc[e] = fmaf(w, v[u][e], acc[e]);
-    }
+    for (int u = 0; u < CH; ++u) acc = fmaf(ms[u] == -INFINITY ? 0.f : exp2f(ms[u] - M), v[u], acc);
   }
   if (out16) {
     const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row);
-#pragma unroll
-    for (int e = 0; e < E; ++e) out16[(int64_t)row * D + lane * E + e] = __float2half_rn(acc[e] * scale);
+    out16[(int64_t)row * D + d] = __float2half_rn(acc * scale);
   } else {
-    float* dst = out32 + (int64_t)row * P;
-#pragma unroll
-    for (int e = 0; e < E; ++e) dst[lane * E + e] = acc[e];
-    if (lane == 0) {
+    float* dst = out32 + (int64_t)row * (D + 2);
+    dst[d] = acc;
+    if (d == 0) {
       dst[D] = M;
       dst[D + 1] = L;
     }

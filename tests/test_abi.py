@@ -67,7 +67,7 @@ def test_argument_checks_without_device(la):
     assert lib.lfm3a_verify_attention(ctypes.byref(bad_geom), 64, 16, 16, 100, 0, None, 64, None, 0, 1, None) == la.ENOTSUP
     assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 16, 100, 0, None, 64, None, 0, 1, None) == la.ENOTSUP
     assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 40, 32, 100, 0, None, 64, None, 0, 1, None) == la.EINVAL
-    assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 32, 100, 0, None, 64, None, 0, 4, None) == la.EINVAL
+    assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 32, 1000, 0, None, 64, None, 0, 4, None) == la.EINVAL
     assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 32, 1000, 0, None, 64, 64, 16, 4, None) == la.EWORKSPACE
     assert lib.lfm3a_verify_partial(ctypes.byref(good), 64, 16, 32, 500, 400, 1000, 0, 64, None, 0, 1, None) == la.EINVAL
     assert lib.lfm3a_combine(None, 4, 2, 64, 0, 0, None, 64, None) == la.EINVAL
@@ -85,7 +85,8 @@ def test_split_choice(la):
     assert la.verify_splits(lay, 131072, 16, 0, 148) == 37
     assert la.verify_splits(lay, 100, 8, 0, 148) == 1
     assert la.verify_splits(lay, 20, 8, 0, 148) == 1
-    assert la.verify_splits(lay, 1024, 8, 0, 148) == 8
+    assert la.verify_splits(lay, 1024, 8, 0, 148) == 4     # 128-key tiles for m <= 16
+    assert la.verify_splits(lay, 1024, 32, 0, 148) == 8    # 64-key tiles above
     ws = la.lib().lfm3a_verify_workspace_bytes(16, 32, 64, 37)
     assert ws == 16 * 32 * 37 * 66 * 4
 
