@@ -127,6 +127,25 @@ int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_
                            const void* gate, void* out, void* workspace, size_t workspace_bytes, int splits,
                            void* stream);
 
+/* Largest split-partial scratch lfm3a_verify_attention_static uses: a fixed device array of the library. */
+#define LFM3A_VERIFY_SCRATCH_BYTES (16u << 20)
+
+/* lfm3a_verify_attention without a workspace argument. It has no reference counterpart: the reference
+ * sizes its verify scratch with the engine's other buffers. It is for callers that cannot allocate device
+ * memory at the call site. One example is an engine that carves up all device memory once at start-up and
+ * has no allocator on the decode path, as the reference engine does with kfd.Alloc. Another is a binding
+ * whose language runtime has no handle on the CUDA allocator. This entry point allocates nothing: the split
+ * partials go to a file-scope device array of LFM3A_VERIFY_SCRATCH_BYTES, one per device.
+ * - The first call on each device, made with that device current, looks up the array's address. Make that
+ *   call before any stream capture.
+ * - A call whose partials (m * q_heads * splits * (head_dim + 2) floats) exceed the array fails with
+ *   LFM3A_EWORKSPACE before launching anything.
+ * - Every call on a device shares the one array, so calls that overlap on the GPU race; serialise them, for
+ *   example on one stream.
+ * Other arguments and results as lfm3a_verify_attention. */
+int lfm3a_verify_attention_static(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len,
+                                  int window, const void* gate, void* out, int splits, void* stream);
+
 /* The same pass over the keys a cache shard holds, for verify attention split across GPUs by sequence
  * blocks: the cache holds positions [kv_begin, kv_end) of the sequence (its block table is indexed by
  * global position); the queries sit at ctx_len + t as above, and the drafts count only where the shard

@@ -15,6 +15,11 @@
 
 using namespace lfm3a;
 
+// Split partials of lfm3a_verify_attention_static: one fixed array per device, loaded with the module, so that
+// entry point allocates nothing. 16 MiB holds m * q_heads * splits * 66 floats for, e.g., 16 tokens x 32 query
+// heads x 121 splits.
+static __device__ __align__(256) float g_verify_scratch[LFM3A_VERIFY_SCRATCH_BYTES / sizeof(float)];
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -347,6 +352,32 @@ int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_
   if (splits <= 0 && kv) splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count());
   return run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, static_cast<__half*>(out), nullptr,
                     workspace, workspace_bytes, splits, as_stream(stream));
+}
+
+// The first call on each device looks up that device's copy of g_verify_scratch (cudaGetSymbolAddress, with the
+// device current); later calls reuse the pointer. The scratch needs no clearing: splits never exceed the key tiles,
+// so every split block writes its whole (acc, max, sum) partial before the combine kernel reads it.
+int lfm3a_verify_attention_static(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len,
+                                  int window, const void* gate, void* out, int splits, void* stream) {
+  static void* scratch[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(LFM3A_EINVAL, "device index out of range");
+  if (!scratch[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_verify_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_verify_scratch)");
+    scratch[dev] = p;
+  }
+  if (splits <= 0 && kv) splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count());
+  const int rc = run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, static_cast<__half*>(out),
+                            nullptr, scratch[dev], LFM3A_VERIFY_SCRATCH_BYTES, splits, as_stream(stream));
+  if (rc == LFM3A_EWORKSPACE)
+    return fail(rc, "verify partials exceed the " + std::to_string(LFM3A_VERIFY_SCRATCH_BYTES >> 20) +
+                        " MiB static scratch (m * q_heads * splits * 66 floats); pass fewer splits or call "
+                        "lfm3a_verify_attention with a workspace");
+  return rc;
 }
 
 int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int kv_begin, int kv_end,

@@ -74,6 +74,7 @@ SIGNATURES = {
     "lfm3a_verify_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "lfm3a_verify_splits": (_I, [ctypes.POINTER(KvLayout), _I, _I, _I, _I]),
     "lfm3a_verify_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _P, _SZ, _I, _P]),
+    "lfm3a_verify_attention_static": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _I, _P]),
     "lfm3a_verify_partial": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_combine": (_I, [_P, _I, _I, _I, _I64, _I64, _P, _P, _P]),
     "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
