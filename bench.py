@@ -247,8 +247,8 @@ def run_ours(args):
     kernel_events = []
 
     def step(c, timing=None):
-        """One verify round of one layer (kernels: append, int8 V, verify, combine; rollback adds none
-        at a 64-aligned length)."""
+        """One verify round of one layer (kernels: append with the int8 V of its block, verify, combine;
+        rollback adds none at a 64-aligned length)."""
         if last:
             c.append(nk, nv, ctx_len, rope=rope)
         if timing is not None:
@@ -266,7 +266,7 @@ def run_ours(args):
         if last:
             c.truncate(ctx_len)
 
-    launches_per_step = (2 if last else 0) + 2 if world == 1 else (2 if last else 0) + (2 if splits > 1 else 1) + 1
+    launches_per_step = (1 if last else 0) + (2 if splits > 1 else 1) + (1 if world > 1 else 0)
 
     # Warm-up (eager), then capture the timed graph with per-step kernel events.
     for i in range(max(args.warmup, 3)):
@@ -368,7 +368,7 @@ def run_ours(args):
     if rank == 0:
         pk = peaks()
         achieved = bytes_rank / (kern_avg_ms * 1e-3) / 1e9
-        traffic = ncu_traffic("verify_kernel_c2.txt") if world == 1 else None
+        traffic = ncu_traffic("verify_m64_kernel_c2.txt") if world == 1 else None
         line = {
             "metric": METRIC,
             "value": round(bytes_step / (ms_step * 1e-3) / 1e9, 2),
@@ -395,7 +395,7 @@ def run_ours(args):
                 "graph": "each timed step replayed from one CUDA graph of K steps",
             },
             "roofline": {
-                "kernel": "verify_kernel" + (" (+ per-rank partial)" if world > 1 else " + combine_kernel"),
+                "kernel": "verify_m64_kernel" + (" (+ per-rank partial)" if world > 1 else " + combine_kernel"),
                 "bound": "hbm",
                 "achieved": round(achieved, 1),
                 "peak": pk["hbm_gbs"],

@@ -2,6 +2,7 @@
 // waits, bulk copies into shared memory, legacy warp MMA fragments and the tcgen05 (TMEM) wrappers.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace lfm3a {
@@ -124,6 +125,15 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// Programmatic dependent launch. Every kernel of the library is launched with programmatic stream
+// serialisation, so it may start while the previous kernel of its stream is still running:
+// pdl_wait() returns once that kernel has completed and its writes are visible (at once if there is
+// none), and every thread calls it before its first global access. pdl_trigger() lets the next kernel's
+// blocks launch early (they wait in their own pdl_wait()); the small kernels call it, the tcgen05 kernels
+// do not, so the next kernel launches as their blocks exit.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -219,6 +229,23 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Host side of the programmatic dependent launch (see pdl_wait): every library kernel goes through here.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // A failed launch is reported through cudaGetLastError by the caller's check.
+  (void)cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 }  // namespace lfm3a

@@ -89,29 +89,85 @@ __device__ __forceinline__ void norm_rope_pairs(const AppendArgs& a, const __hal
   }
 }
 
-// One warp per (token, kv head); 4 warps per block.
+// MODE_F16 append, one block of 256 threads per (64-token block, kv head) the new tokens touch. Each warp
+// takes new tokens in turn: k-norm + RoPE, fp16 K and V stores, and V kept in shared memory beside the
+// block's earlier tokens (read back from the pool). The block's int8 V and scale then come from shared
+// memory: absmax over the live tokens (those below pos0 + n), scale max(amax/127, 1e-6), rounding half away
+// from zero, zeros past the live tokens; a page past the sequence end is not touched.
 template <int D>
-__global__ __launch_bounds__(128) void kv_append_f16_kernel(AppendArgs a) {
+__global__ __launch_bounds__(256) void kv_append_f16_kernel(AppendArgs a) {
   using S = F16Section<D>;
   constexpr int J = D / 64, HALF = D / 2;
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (row >= a.n * a.g.kv_heads) return;
-  const int t = row / a.g.kv_heads, h = row % a.g.kv_heads, pos = a.pos0 + t;
-  const __half* ks = a.k + (int64_t)t * a.stride + h * D;
-  const __half* vs = a.v + (int64_t)t * a.stride + h * D;
-  float ra[J], rb[J];
-  norm_rope_pairs<D>(a, ks, pos, lane, ra, rb);
-  char* sec = a.g.pool + phys_block(a.g, pos / kBlockTokens) * a.g.block_bytes + h * a.g.head_bytes;
-  __half* K = reinterpret_cast<__half*>(sec);
-  __half* V = reinterpret_cast<__half*>(sec + S::kOffV);
-  const int s = pos % kBlockTokens;
+  __shared__ __half sv[kQuantBlock * D];   // [token of the block][dim]
+  __shared__ float red[8];
+  pdl_wait();
+  const int qb = a.pos0 / kQuantBlock + blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int t0 = qb * kQuantBlock, len = a.pos0 + a.n;
+  const int lo = max(a.pos0, t0), hi = min(len, t0 + kQuantBlock), live = hi - t0;
+  const int pages = (live + kBlockTokens - 1) / kBlockTokens;
+  char* sec[2];
 #pragma unroll
-  for (int j = 0; j < J; ++j) {
-    const int d0 = lane + 32 * j, d1 = d0 + HALF;
-    K[S::k_index(s, d0)] = __float2half_rn(ra[j]);
-    K[S::k_index(s, d1)] = __float2half_rn(rb[j]);
-    V[S::v_index(s, d0)] = vs[d0];
-    V[S::v_index(s, d1)] = vs[d1];
+  for (int p = 0; p < 2; ++p)
+    sec[p] = p < pages ? a.g.pool + phys_block(a.g, qb * 2 + p) * a.g.block_bytes + h * a.g.head_bytes : nullptr;
+  pdl_trigger();
+  for (int t = lo + warp; t < hi; t += 8) {
+    const int i = t - a.pos0, b = t - t0;
+    const __half* ks = a.k + (int64_t)i * a.stride + h * D;
+    const __half* vs = a.v + (int64_t)i * a.stride + h * D;
+    float ra[J], rb[J];
+    norm_rope_pairs<D>(a, ks, t, lane, ra, rb);
+    __half* K = reinterpret_cast<__half*>(sec[b / kBlockTokens]);
+    __half* V = reinterpret_cast<__half*>(sec[b / kBlockTokens] + S::kOffV);
+    const int s = b % kBlockTokens;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int d0 = lane + 32 * j, d1 = d0 + HALF;
+      const __half v0 = vs[d0], v1 = vs[d1];
+      K[S::k_index(s, d0)] = __float2half_rn(ra[j]);
+      K[S::k_index(s, d1)] = __float2half_rn(rb[j]);
+      V[S::v_index(s, d0)] = v0;
+      V[S::v_index(s, d1)] = v1;
+      sv[b * D + d0] = v0;
+      sv[b * D + d1] = v1;
+    }
+  }
+  // Earlier tokens of the block, read in the V tiles' memory order: tile i/64 = (d/8, s/8), element (d%8, s%8).
+  const int old = lo - t0;
+  for (int p = 0; p * kBlockTokens < old; ++p) {
+    const __half* V = reinterpret_cast<const __half*>(sec[p] + S::kOffV);
+    for (int i = tid; i < kBlockTokens * D; i += 256) {
+      const int tile = i >> 6, s = (tile & 3) * 8 + (i & 7), d = (tile >> 2) * 8 + ((i >> 3) & 7);
+      const int b = p * kBlockTokens + s;
+      if (b < old) sv[b * D + d] = V[i];
+    }
+  }
+  __syncthreads();
+  float amax = 0.f;
+  for (int i = tid; i < live * D; i += 256) amax = fmaxf(amax, fabsf(__half2float(sv[i])));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (lane == 0) red[warp] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
+  const float scale = fmaxf(__fdiv_rn(amax, 127.f), 1e-6f), inv = __fdiv_rn(1.f, scale);
+  for (int p = 0; p < pages; ++p) {
+    int8_t* V8 = reinterpret_cast<int8_t*>(sec[p] + S::kOffV8);
+    for (int i = tid; i < 32 * D; i += 256) {
+      // i walks the V8 tiles in memory order: tile i/128 = (d/8, s/16), element (d%8, s%16).
+      const int tile = i >> 7, e = i & 127;
+      const int d = (tile >> 1) * 8 + (e >> 4), b = p * kBlockTokens + (tile & 1) * 16 + (e & 15);
+      int8_t q = 0;
+      if (b < live) {
+        float x = __fmul_rn(__half2float(sv[b * D + d]), inv);
+        x = x >= 0.f ? __fadd_rn(x, 0.5f) : __fsub_rn(x, 0.5f);
+        q = (int8_t)truncf(fminf(fmaxf(x, -128.f), 127.f));
+      }
+      V8[i] = q;
+    }
+    if (tid == 0) *reinterpret_cast<float*>(sec[p] + S::kOffScale) = scale;
   }
 }
 
@@ -144,6 +200,8 @@ __device__ __forceinline__ float quantize_pair_warp(const float (&x0)[D / 64], c
 template <int D>
 __global__ __launch_bounds__(128) void kv_append_i8rec_kernel(AppendArgs a) {
   constexpr int J = D / 64, HALF = D / 2, REC = 2 * D + 8;
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= a.n * a.g.kv_heads) return;
   const int t = row / a.g.kv_heads, h = row % a.g.kv_heads, pos = a.pos0 + t;
@@ -178,6 +236,8 @@ template <int D>
 __global__ __launch_bounds__(256) void v8_quant_kernel(V8Args a) {
   using S = F16Section<D>;
   __shared__ float red[8];
+  pdl_wait();
+  pdl_trigger();
   const int qb = a.qb0 + blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int t0 = qb * kQuantBlock;
   if (t0 >= a.len) return;
@@ -225,6 +285,8 @@ __global__ __launch_bounds__(256) void v8_quant_kernel(V8Args a) {
 
 // The acceptance of a verify round (dspark.hip:2848-2895), one thread.
 __global__ void accept_kernel(const int32_t* best, const int32_t* tokens, int m, int32_t* state) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int acc = 0;
   for (int t = 0; t < m - 1; ++t) {

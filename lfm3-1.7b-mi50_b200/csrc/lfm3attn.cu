@@ -100,8 +100,8 @@ int launch_v8(const lfm3a_kv_view* kv, int qb0, int qb1, int len, cudaStream_t s
   a.qb0 = qb0;
   a.len = len;
   const dim3 grid(qb1 - qb0, kv->layout.kv_heads);
-  if (kv->layout.head_dim == 64) v8_quant_kernel<64><<<grid, 256, 0, st>>>(a);
-  else v8_quant_kernel<128><<<grid, 256, 0, st>>>(a);
+  if (kv->layout.head_dim == 64) launch_pdl(v8_quant_kernel<64>, grid, 256, 0, st, a);
+  else launch_pdl(v8_quant_kernel<128>, grid, 256, 0, st, a);
   return check_launch("v8_quant_kernel");
 }
 
@@ -118,9 +118,9 @@ int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count
 int launch_combine(const float* part, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
                    const __half* gate, __half* out16, float* out32, cudaStream_t st) {
   if (head_dim == 64)
-    combine_kernel<64><<<(rows + 3) / 4, 256, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
+    launch_pdl(combine_kernel<64>, (rows + 3) / 4, 256, 0, st, part, rows, splits, split_stride, row_stride, gate, out16, out32);
   else
-    combine_kernel<128><<<(rows + 1) / 2, 256, 0, st>>>(part, rows, splits, split_stride, row_stride, gate, out16, out32);
+    launch_pdl(combine_kernel<128>, (rows + 1) / 2, 256, 0, st, part, rows, splits, split_stride, row_stride, gate, out16, out32);
   return check_launch("combine_kernel");
 }
 
@@ -175,11 +175,11 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   if (m <= 16) {
     rc = ensure_smem(verify_m64_kernel, kV6Smem, done[1]);
     if (rc != LFM3A_OK) return rc;
-    verify_m64_kernel<<<grid, kVfThreads, kV6Smem, st>>>(a);
+    launch_pdl(verify_m64_kernel, grid, kVfThreads, kV6Smem, st, a);
   } else {
     rc = ensure_smem(verify_kernel<false>, kVfSmem, done[0]);
     if (rc != LFM3A_OK) return rc;
-    verify_kernel<false><<<grid, kVfThreads, kVfSmem, st>>>(a);
+    launch_pdl(verify_kernel<false>, grid, kVfThreads, kVfSmem, st, a);
   }
   rc = check_launch("verify_kernel");
   if (rc != LFM3A_OK || a.splits == 1) return rc;
@@ -299,15 +299,14 @@ int lfm3a_kv_append(const lfm3a_kv_view* kv, const void* k, const void* v, int64
   const cudaStream_t st = as_stream(stream);
   const int blocks = (n * H + 3) / 4;
   if (kv->layout.mode == LFM3A_MODE_F16) {
-    if (D == 64) kv_append_f16_kernel<64><<<blocks, 128, 0, st>>>(a);
-    else kv_append_f16_kernel<128><<<blocks, 128, 0, st>>>(a);
-    rc = check_launch("kv_append_f16_kernel");
-    if (rc != LFM3A_OK) return rc;
-    const int len = pos0 + n;
-    return launch_v8(kv, pos0 / kQuantBlock, (len - 1) / kQuantBlock + 1, len, st);
+    // One block per (64-token block, kv head) the new tokens touch; it also rewrites that block's int8 V.
+    const dim3 grid((pos0 + n - 1) / kQuantBlock - pos0 / kQuantBlock + 1, H);
+    if (D == 64) launch_pdl(kv_append_f16_kernel<64>, grid, 256, 0, st, a);
+    else launch_pdl(kv_append_f16_kernel<128>, grid, 256, 0, st, a);
+    return check_launch("kv_append_f16_kernel");
   }
-  if (D == 64) kv_append_i8rec_kernel<64><<<blocks, 128, 0, st>>>(a);
-  else kv_append_i8rec_kernel<128><<<blocks, 128, 0, st>>>(a);
+  if (D == 64) launch_pdl(kv_append_i8rec_kernel<64>, blocks, 128, 0, st, a);
+  else launch_pdl(kv_append_i8rec_kernel<128>, blocks, 128, 0, st, a);
   return check_launch("kv_append_i8rec_kernel");
 }
 
@@ -322,7 +321,7 @@ int lfm3a_kv_truncate(const lfm3a_kv_view* kv, int new_len, void* stream) {
 
 int lfm3a_accept(const int32_t* best, const int32_t* tokens, int m, int32_t* state, void* stream) {
   if (!best || !tokens || !state || m < 1) return fail(LFM3A_EINVAL, "bad accept arguments");
-  accept_kernel<<<1, 32, 0, as_stream(stream)>>>(best, tokens, m, state);
+  launch_pdl(accept_kernel, 1, 32, 0, as_stream(stream), best, tokens, m, state);
   return check_launch("accept_kernel");
 }
 
@@ -413,7 +412,7 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
 int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* stream) {
   if (!p || !q || !sc || rows < 0) return fail(LFM3A_EINVAL, "bad quantize_p arguments");
   if (rows == 0) return LFM3A_OK;
-  quantize_p_rows_kernel<<<(rows + 127) / 128, 128, 0, as_stream(stream)>>>(p, rows, q, sc);
+  launch_pdl(quantize_p_rows_kernel, (rows + 127) / 128, 128, 0, as_stream(stream), p, rows, q, sc);
   return check_launch("quantize_p_rows_kernel");
 }
 

@@ -43,6 +43,8 @@ __device__ __forceinline__ float quantize_p_row(const float (&p)[N], uint32_t (&
 }
 
 __global__ __launch_bounds__(128) void quantize_p_rows_kernel(const float* p, int rows, uint8_t* q, float* sc) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x * 128 + threadIdx.x;
   if (r >= rows) return;
   float v[64];
@@ -124,6 +126,10 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
     mbar_init(drain, 1);
     fence_barrier_init();
   }
+  // Launched as a programmatic dependent: nothing global is touched, and no TMEM is taken, before the
+  // previous kernel of the stream has completed (a waiting block holding TMEM could starve it). No early
+  // trigger: the next kernel's blocks launch as these exit (waiting blocks beside a running one slowed it).
+  pdl_wait();
   if (warp == 5) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -459,7 +465,7 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
         return LFM3A_ECUDA;
       done[1][dev] = true;
     }
-    prefill_kernel<true><<<grid, kPfThreads, PfLayout<true>::kRequest, st>>>(a);
+    launch_pdl(prefill_kernel<true>, grid, kPfThreads, PfLayout<true>::kRequest, st, a);
   } else {
     if (!done[0][dev]) {
       if (cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -468,7 +474,7 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
         return LFM3A_ECUDA;
       done[0][dev] = true;
     }
-    prefill_kernel<false><<<grid, kPfThreads, PfLayout<false>::kRequest, st>>>(a);
+    launch_pdl(prefill_kernel<false>, grid, kPfThreads, PfLayout<false>::kRequest, st, a);
   }
   return cudaGetLastError() == cudaSuccess ? LFM3A_OK : LFM3A_ELAUNCH;
 }

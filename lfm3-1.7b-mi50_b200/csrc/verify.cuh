@@ -100,6 +100,10 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
     mbar_init(drain, 1);
     fence_barrier_init();
   }
+  // Launched as a programmatic dependent: nothing global is touched, and no TMEM is taken, before the
+  // previous kernel of the stream has completed (a waiting block holding TMEM could starve it). No early
+  // trigger: the next kernel's blocks launch as these exit (waiting blocks beside a running one slowed it).
+  pdl_wait();
   if (warp == kVfSoftmaxWarps + 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -482,6 +486,10 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
     mbar_init(drain, 1);
     fence_barrier_init();
   }
+  // Launched as a programmatic dependent: nothing global is touched, and no TMEM is taken, before the
+  // previous kernel of the stream has completed (a waiting block holding TMEM could starve it). No early
+  // trigger: the next kernel's blocks launch as these exit (waiting blocks beside a running one slowed it).
+  pdl_wait();
   if (warp == kVfSoftmaxWarps + 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -808,6 +816,8 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
                                                       int64_t row_stride, const __half* gate, __half* out16,
                                                       float* out32) {
   constexpr int RPB = 256 / D, CH = 16;
+  pdl_wait();
+  pdl_trigger();
   const int d = threadIdx.x % D, lane = threadIdx.x & 31;
   const int row = blockIdx.x * RPB + threadIdx.x / D;
   if (row >= rows) return;   // D is a multiple of 32: whole warps leave together

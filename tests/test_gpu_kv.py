@@ -127,3 +127,34 @@ def test_accept_on_device(la, orc, cuda):
     la.sync()
     commit = orc.accept(best, toks)
     assert state.cpu().tolist() == [1024 + commit, commit - 1, 8, commit]
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_draft_rounds_append_rollback(la, orc, synth, cuda, d):
+    """DSpark rounds on one cache: 5 drafts appended at the length, 2 kept (rollback of 3), repeated across
+    64-token and page boundaries from an unaligned start; bytes and int8 V bit-exact after every round."""
+    s = synth.Stream(14 + d)
+    heads = 512 // d
+    n0, rounds, drafts, keep = 61, 12, 5, 2
+    total = n0 + rounds * keep + drafts
+    k = s.normal_f16((total, heads, d))
+    v = s.normal_f16((total, heads, d))
+    kd = s.normal_f16((rounds, drafts, heads, d))
+    vd = s.normal_f16((rounds, drafts, heads, d))
+    table_np = orc.rope_table(1e6, 1.0, d, total + 8)
+    rope = dev(table_np.view(np.float16), cuda)
+    cache = la.LayerCache(la.MODE_F16, heads, d, total + 32, device=cuda)
+    cache.append(dev(k[:n0], cuda), dev(v[:n0], cuda), 0, rope=rope)
+    K, V = orc.kv_append_f16(k[:n0], v[:n0], 0, rope=table_np)
+    length = n0
+    for r in range(rounds):
+        cache.append(dev(kd[r], cuda), dev(vd[r], cuda), length, rope=rope)
+        kn, vn = orc.kv_append_f16(kd[r], vd[r], length, rope=table_np)
+        K = np.concatenate([K[:length], kn])
+        V = np.concatenate([V[:length], vn])
+        la.sync()
+        check_f16_cache(cache.logical(length + drafts), K, V, length + drafts, orc)
+        length += keep
+        cache.truncate(length)
+        la.sync()
+        check_f16_cache(cache.logical(length), K, V, length, orc)
