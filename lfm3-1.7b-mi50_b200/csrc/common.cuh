@@ -214,6 +214,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// tmem_ld16 that the compiler keeps after the computation of dep (an unused operand): it bounds how far
+// later loads are hoisted, and with them the registers in flight.
+__device__ __forceinline__ void tmem_ld16_after(uint32_t taddr, uint32_t (&r)[16], uint32_t dep) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr), "r"(dep));
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -224,6 +233,39 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Ties registers written by tcgen05.ld to the preceding tcgen05.wait::ld: no use moves above it.
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
+// 64 consecutive columns of this warp's 32 lanes: four loads in flight, one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[4][16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) tmem_ld16(taddr + 16 * c, r[c]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int c = 0; c < 4; ++c) reg_fence16(r[c]);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
+
+// Maximum of 64 values: four interleaved chains of three-input maxima (8 steps each), four temporaries.
+__device__ __forceinline__ float max64(const float (&x)[64]) {
+  float m[4] = {x[0], x[1], x[2], x[3]};
+#pragma unroll
+  for (int k = 4; k < 60; k += 8)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = fmax3(m[i], x[k + i], x[k + 4 + i]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], x[60 + i]);
+  return fmaxf(fmax3(m[0], m[1], m[2]), m[3]);
+}
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

@@ -6,12 +6,12 @@
 //   0-3  softmax, thread = row: TMEM -> registers (tcgen05.ld), mask, lazy running max (rescale only when
 //        a tile beats it by 2^8, prefill_attn.hip:33,278-304), p = 2^(s - m); exact: P fp16 -> smem;
 //        int8: P' = p x v_scale quantised to u8 per row and tile (prefill_attn.hip:305-331) -> smem, and
-//        acc += scale x (int32 PV) in registers one tile later;
-//   4    producer: bulk copies of the K and V (or int8 V) sections of the tile's two 32-token pages;
-//   5    MMA issuer (one thread): S = Q K^T (kind::f16, M128 N64, 4 k-steps) into TMEM, then the previous
-//        tile's PV: exact O += P V (kind::f16, O stays in TMEM), int8 Dpv = P8 V8 (kind::i8, s32 in TMEM).
-// QK of tile j is issued before PV of tile j - 1, so the softmax of j - 1 overlaps the QK of j.
-// TMEM columns: S[2] at 0 and 64; O (exact) at 128, or Dpv[2] (int8) at 128 and 192.
+//        acc += scale x (int32 PV) in TMEM one tile later, before the next P is handed over;
+//   4    producer and MMA issuer in one loop (lane 0 issues): bulk copies of the K and V (or int8 V) sections
+//        of the tile's two 32-token pages into a 3-stage ring; S = Q K^T (kind::f16, M128 N64, 4 k-steps)
+//        into TMEM two tiles ahead; PV: exact O += P V (kind::f16, O stays in TMEM), int8 Dpv = P8 V8
+//        (kind::i8, s32 in TMEM). 160 threads leave the softmax rows 204 registers at two CTAs per SM.
+// TMEM columns: S[2] at 0 and 64; O (exact) at 128, or int8 Dpv (s32) at 128 and the fp32 accumulator at 192.
 // Every operand sits in shared memory as 8-row x 16-byte core tiles (no swizzle, K-major); the page
 // sections are already in that order, so a page moves with plain bulk copies.
 #pragma once
@@ -64,7 +64,7 @@ struct PrefillArgs {
   float qk_scale;    // (1 / sqrt(64)) * log2(e)
 };
 
-constexpr int kPfThreads = 192;
+constexpr int kPfThreads = 160;
 constexpr int kPfStages = 3;
 constexpr int kPfQBytes = 16384;   // 128 rows x 64 dims fp16
 
@@ -130,7 +130,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   // previous kernel of the stream has completed (a waiting block holding TMEM could starve it). No early
   // trigger: the next kernel's blocks launch as these exit (waiting blocks beside a running one slowed it).
   pdl_wait();
-  if (warp == 5) {
+  if (warp == 4) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -159,13 +159,9 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
     }
     const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
     float m_run = -INFINITY, l_run = 0.f;
-    float acc[I8 ? 64 : 1];
-    float sc_prev = 0.f;
-    if (I8) {
-#pragma unroll
-      for (int d = 0; d < (I8 ? 64 : 1); ++d) acc[d] = 0.f;
-    }
+    float sc_prev = 0.f;   // int8: the row's scale of the previous tile's int32 PV
     // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
+    constexpr float kLog2of255 = 7.99435343685886f;
     bool ok = true;
     for (int jt = 0; jt < ntiles && ok; ++jt) {
       const int b = jt & 1, k0 = kt_begin + jt * kQuantBlock;
@@ -175,30 +171,37 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         break;
       }
       tc_fence_after();
-      float x[64];
+      float x[64];   // raw scores q.k of this row and tile
       {
-        uint32_t rr[16];
+        uint32_t rr[4][16];
+        tmem_ld64(lane_base + b * 64, rr);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld16(lane_base + b * 64 + c * 16, rr);
-          tmem_wait_ld();
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[e]);
-        }
+          for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[c][e]);
       }
+      // The causal / window / sequence mask, only on tiles that straddle a boundary.
       const bool interior = ntok == 32 && k0 + kQuantBlock - 1 <= qfirst && (a.window == 0 || k0 > qlast - a.window);
-      float mx = -INFINITY;
+      if (!interior) {
+        // The row's keys form one interval [lo, hi] of tile offsets (causal end, window and CTA start).
+        const int lo = max(kbegin, a.window > 0 ? qpos - a.window + 1 : 0) - k0;
+        const int hi = row_ok ? qpos - k0 : -1;
 #pragma unroll
-      for (int k = 0; k < 64; ++k) {
-        float v = x[k] * a.qk_scale;
-        if (!interior) {
-          const int kpos = k0 + k;
-          const bool valid = row_ok && kpos <= qpos && kpos >= kbegin && (a.window == 0 || kpos > qpos - a.window);
-          v = valid ? v : -INFINITY;
+        for (int k = 0; k < 64; ++k) x[k] = (k >= lo && k <= hi) ? x[k] : -INFINITY;
+        if (I8) {
+          // The int8 pass below reads the scores again: it finds them masked (and keeps no predicates alive).
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(x[16 * c + e]);
+            tmem_st16(lane_base + b * 64 + 16 * c, w);
+          }
+          tmem_wait_st();
         }
-        x[k] = v;
-        mx = fmaxf(mx, v);
       }
+      // fl(x * scale) is monotone in x, so the scaled maximum is the maximum of the scaled scores.
+      const float mx = max64(x) * a.qk_scale;
       const bool grow_max = mx > m_run + kLazy;
       if (!I8) {
         // O lives in TMEM: rescaling it needs the previous PV finished; rare after the first tiles.
@@ -218,6 +221,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
               uint32_t rr[16];
               tmem_ld16(lane_base + 128 + c * 16, rr);
               tmem_wait_ld();
+              reg_fence16(rr);
 #pragma unroll
               for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
               tmem_st16(lane_base + 128 + c * 16, rr);
@@ -225,23 +229,17 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
             tmem_wait_st();
           }
         }
-      } else if (grow_max) {
-        const float corr = fast_exp2(m_run - mx);
-        m_run = mx;
-        l_run *= corr;
-        sc_prev *= corr;   // the previous tile's PV is folded in later, already at the new max
+        // p = 2^(x * scale - m) in one FFMA + EX2 (ex2 of -inf is 0 for masked keys); l in four partial sums.
+        const float neg = m_run == -INFINITY ? 0.f : -m_run;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int d = 0; d < 64; ++d) acc[d] *= corr;
-      }
-#pragma unroll
-      for (int k = 0; k < 64; ++k) {
-        const float p = x[k] == -INFINITY ? 0.f : fast_exp2(x[k] - m_run);
-        x[k] = p;
-        l_run += p;
-      }
-      uint8_t* pb = sP + b * L::kPBuf;
-      if (!I8) {
+        for (int k = 0; k < 64; ++k) {
+          x[k] = fast_exp2(fmaf(x[k], a.qk_scale, neg));
+          ls[k & 3] += x[k];
+        }
+        l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
         // P[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
+        uint8_t* pb = sP + b * L::kPBuf;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint4 v;
@@ -251,45 +249,101 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
           v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
           *reinterpret_cast<uint4*>(pb + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
         }
-      } else {
-        // P' = p x v_scale of the tile's 64-token block (kept in the block's first page).
-        const char* sec = a.g.pool + phys_block(a.g, k0 / kBlockTokens) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
-        const float vs = *reinterpret_cast<const float*>(sec + F16Section<64>::kOffScale);
-#pragma unroll
-        for (int k = 0; k < 64; ++k) x[k] = __fmul_rn(x[k], vs);
-        uint32_t q8[16];
-        const float sc = quantize_p_row<64>(x, q8);
-        // P8[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(pb + ((r >> 3) * 4 + c) * 128 + (r & 7) * 16) =
-              make_uint4(q8[4 * c], q8[4 * c + 1], q8[4 * c + 2], q8[4 * c + 3]);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[b]);
-        // Epilogue of the previous tile: acc += scale x (int32 sum of u8 P x int8 V).
-        if (jt >= 1) {
-          const int bp = (jt - 1) & 1;
-          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[bp], (uint32_t)((jt - 1) >> 1) & 1u))) {
-            raise_error(kErrWaitMma);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t rr[16];
-            tmem_ld16(lane_base + 128 + bp * 64 + c * 16, rr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) acc[c * 16 + e] = fmaf((float)(int32_t)rr[e], sc_prev, acc[c * 16 + e]);
-          }
-          tc_fence_before();
-        }
-        sc_prev = sc;
         continue;
       }
+      float corr = 1.f;   // applied to the accumulator and the previous tile's scale in the epilogue below
+      if (grow_max) {
+        corr = fast_exp2(m_run - mx);
+        m_run = mx;
+        l_run *= corr;
+      }
+      // u8 P of the tile: with p = 2^(x*scale - m) and pm its maximum, the reference's rne(p * vs * 255 /
+      // (pm * vs)) is rne(e), e = 2^(x*scale - mx + log2 255), the V scale cancelling. The row's scale of the
+      // tile's int32 PV is pm * vs / 255 with pm = 2^(mx - m), and sum(p) = pm / 255 * sum(e).
+      const char* sec = a.g.pool + phys_block(a.g, k0 / kBlockTokens) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+      const float vs = *reinterpret_cast<const float*>(sec + F16Section<64>::kOffScale);
+      const float off = mx == -INFINITY ? 0.f : kLog2of255 - mx;
+      float es[4] = {0.f, 0.f, 0.f, 0.f};
+      uint8_t* pb = sP + b * L::kPBuf;
+      // P8[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
+      // The accumulator holds 64 registers, so the scores are read from TMEM a second time, 16 at a time,
+      // and each 16-key core-tile row is stored as soon as it is packed.
+      uint32_t dep = __float_as_uint(off);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float xs[16];
+        {
+          uint32_t rr[16];
+          tmem_ld16_after(lane_base + b * 64 + 16 * c, rr, dep);
+          tmem_wait_ld();
+          reg_fence16(rr);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) xs[e] = __uint_as_float(rr[e]);
+        }
+        uint32_t q8[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint32_t u[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float e = fast_exp2(fmaf(xs[4 * w + i], a.qk_scale, off));
+            es[i] += e;
+            u[i] = __float_as_uint(__fadd_rn(e, 12582912.f));   // low byte = rne(e), e <= 255
+          }
+          q8[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
+        }
+        *reinterpret_cast<uint4*>(pb + ((r >> 3) * 4 + c) * 128 + (r & 7) * 16) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
+        dep = q8[3];
+      }
+      const float pm255 = mx == -INFINITY ? 0.f : fast_exp2(mx - m_run) * (1.f / 255.f);
+      l_run = fmaf(pm255, (es[0] + es[1]) + (es[2] + es[3]), l_run);
+      const float sc = pm255 * vs;
+      // Epilogue of the previous tile, before P(jt) is handed over (PV(jt) rewrites the s32 columns):
+      // acc = corr x (acc + sc_prev x Dpv(jt - 1)), acc in fp32 TMEM columns 192..255. |Dpv| <= 64 * 255 * 127
+      // < 2^22, so 0x4B400000 + Dpv is the float 1.5 * 2^23 + Dpv, and one FADD gives Dpv exactly.
+      if (jt >= 1) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
+          raise_error(kErrWaitMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float scp = sc_prev * corr;
+        uint32_t dep2 = __float_as_uint(scp);   // keeps each half's loads after the previous half's arithmetic
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t dv[2][16], av[2][16];
+          tmem_ld16_after(lane_base + 128 + 32 * half, dv[0], dep2);
+          tmem_ld16_after(lane_base + 128 + 32 * half + 16, dv[1], dep2);
+          if (jt >= 2) {
+            tmem_ld16_after(lane_base + 192 + 32 * half, av[0], dep2);
+            tmem_ld16_after(lane_base + 192 + 32 * half + 16, av[1], dep2);
+          }
+          tmem_wait_ld();
+          reg_fence16(dv[0]);
+          reg_fence16(dv[1]);
+          if (jt >= 2) {
+            reg_fence16(av[0]);
+            reg_fence16(av[1]);
+          }
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float prev = jt >= 2 ? __uint_as_float(av[c][e]) * corr : 0.f;
+              av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, scp, prev));
+            }
+          tmem_st16(lane_base + 192 + 32 * half, av[0]);
+          tmem_st16(lane_base + 192 + 32 * half + 16, av[1]);
+          dep2 = av[1][15];
+        }
+        tmem_wait_st();
+      }
+      sc_prev = sc;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -304,46 +358,49 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         atomicExch(&s_abort, 1);
       } else {
         tc_fence_after();
-        float o[64];
+        // 16 columns at a time: exact O, or int8 acc + sc x Dpv of the last tile.
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t rr[16];
-          tmem_ld16(lane_base + 128 + (I8 ? (last & 1) * 64 : 0) + c * 16, rr);
+          uint32_t rr[16], av[16];
+          tmem_ld16(lane_base + 128 + 16 * c, rr);
+          if (I8 && last >= 1) tmem_ld16(lane_base + 192 + 16 * c, av);
           tmem_wait_ld();
+          reg_fence16(rr);
+          if (I8 && last >= 1) reg_fence16(av);
+          float o[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            if (I8) o[c * 16 + e] = fmaf((float)(int32_t)rr[e], sc_prev, acc[I8 ? c * 16 + e : 0]);
-            else o[c * 16 + e] = __uint_as_float(rr[e]);
-          }
-        }
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+          for (int e = 0; e < 16; ++e)
+            o[e] = I8 ? fmaf(__uint_as_float(rr[e] + 0x4B400000u) - 12582912.f, sc_prev,
+                             last >= 1 ? __uint_as_float(av[e]) : 0.f)
+                      : __uint_as_float(rr[e]);
+          if (row_ok) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 v;
-            v.x = pack_half2(o[8 * c] * inv, o[8 * c + 1] * inv);
-            v.y = pack_half2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-            v.z = pack_half2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-            v.w = pack_half2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-            dst[c] = v;
+            for (int hh = 0; hh < 2; ++hh) {
+              uint4 v;
+              v.x = pack_half2(o[8 * hh] * inv, o[8 * hh + 1] * inv);
+              v.y = pack_half2(o[8 * hh + 2] * inv, o[8 * hh + 3] * inv);
+              v.z = pack_half2(o[8 * hh + 4] * inv, o[8 * hh + 5] * inv);
+              v.w = pack_half2(o[8 * hh + 6] * inv, o[8 * hh + 7] * inv);
+              dst[2 * c + hh] = v;
+            }
           }
         }
       }
     }
-  } else if (warp == 4) {
-    // ================================================================ producer
-    // The whole warp runs the loop; lane 0 issues the copies.
+  } else {
+    // ================================================================ producer + MMA issuer (warp 4)
+    // One warp runs both roles in one loop (its values stay warp-uniform); lane 0 alone issues the bulk
+    // copies and the tensor-core work. QK runs two tiles ahead of PV: after PV(j), S buffer j & 1 is free
+    // (the softmax read S(j) before it handed over P(j)), so QK(j + 2) goes out at once and the softmax
+    // never waits for scores. The copies of tile j + NS go out once PV(j), the last reader of its stage,
+    // has completed.
     {
+      bool ok = true;
       int issued = 0;
-      for (int jt = 0; jt < ntiles; ++jt) {
+      auto issue_load = [&](int jt) {
         const int st = jt % NS;
-        if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&empty[st], (uint32_t)((jt / NS) - 1) & 1u))) {
-          raise_error(kErrWaitEmpty);
-          atomicExch(&s_abort, 1);
-          break;
-        }
-        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) break;
         const int k0 = kt_begin + jt * kQuantBlock;
         const int lp0 = k0 / kBlockTokens;
         // A second page wholly past the keys may have no table entry: copy the first page again (masked).
@@ -365,19 +422,9 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         }
         __syncwarp();
         issued = jt + 1;
-      }
-      // On an abort, wait (bounded) for the copies still landing in shared memory.
-      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
-        for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
-      }
-    }
-  } else {
-    // ================================================================ MMA issuer
-    // QK runs two tiles ahead of PV: after PV(j), S buffer j & 1 is free (the softmax read S(j) before it
-    // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores.
-    // The whole warp runs the loop (its values stay warp-uniform); lane 0 alone issues the tensor-core work.
-    {
-      bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
+      };
+      for (int jt = 0; jt < min(NS, ntiles); ++jt) issue_load(jt);
+      ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
       const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
       auto issue_qk = [&](int jt) -> bool {
@@ -401,6 +448,10 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         }
       }
       for (int jt = 0; jt < ntiles && ok; ++jt) {
+        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
+          ok = false;
+          break;
+        }
         const int bp = jt & 1, stp = jt % NS;
         if (!__all_sync(0xffffffffu, mbar_wait(&p_full[bp], (uint32_t)(jt >> 1) & 1u))) {
           raise_error(kErrWaitOther);
@@ -423,7 +474,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
           if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)
-              umma_i8_ss(tmem + 128 + bp * 64, p_desc + 16 * ks, v_desc + 128 * ks, kIdescI8M128N64, ks > 0 ? 1u : 0u);
+              umma_i8_ss(tmem + 128, p_desc + 16 * ks, v_desc + 128 * ks, kIdescI8M128N64, ks > 0 ? 1u : 0u);
           }
         }
         if (lane == 0) {
@@ -434,19 +485,31 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         if (jt + 2 < ntiles && !issue_qk(jt + 2)) {
           raise_error(kErrWaitFull);
           ok = false;
+          break;
+        }
+        if (jt + NS < ntiles) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&empty[stp], (uint32_t)(jt / NS) & 1u))) {
+            raise_error(kErrWaitEmpty);
+            ok = false;
+            break;
+          }
+          issue_load(jt + NS);
         }
       }
-      // Leave no tensor-core work in flight behind an abort.
+      // Leave no tensor-core work in flight behind an abort, and wait (bounded) for copies still landing.
       if (lane == 0) umma_commit(drain);
       __syncwarp();
       mbar_wait(drain, 0);
-      if (!ok) atomicExch(&s_abort, 1);
+      if (!ok) {
+        atomicExch(&s_abort, 1);
+        for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 4) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
