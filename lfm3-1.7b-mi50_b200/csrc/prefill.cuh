@@ -7,10 +7,10 @@
 //        a tile beats it by 2^8, prefill_attn.hip:33,278-304), p = 2^(s - m); exact: P fp16 -> smem;
 //        int8: P' = p x v_scale quantised to u8 per row and tile (prefill_attn.hip:305-331) -> smem, and
 //        acc += scale x (int32 PV) in TMEM one tile later, before the next P is handed over;
-//   4    producer and MMA issuer in one loop (lane 0 issues): bulk copies of the K and V (or int8 V) sections
-//        of the tile's two 32-token pages into a 3-stage ring; S = Q K^T (kind::f16, M128 N64, 4 k-steps)
-//        into TMEM two tiles ahead; PV: exact O += P V (kind::f16, O stays in TMEM), int8 Dpv = P8 V8
-//        (kind::i8, s32 in TMEM). 160 threads leave the softmax rows 204 registers at two CTAs per SM.
+//   4    producer: bulk copies of the tile's two 32-token pages, K (8 KiB) and V (8 KiB, or int8 V 4 KiB) into
+//        two 4-stage rings; the K ring runs ahead (a K stage frees when its QK completes);
+//   5    MMA issuer (one thread): S = Q K^T (kind::f16, M128 N64, 4 k-steps) into TMEM two tiles ahead, then
+//        PV: exact O += P V (kind::f16, O stays in TMEM), int8 Dpv = P8 V8 (kind::i8, s32 in TMEM).
 // TMEM columns: S[2] at 0 and 64; O (exact) at 128, or int8 Dpv (s32) at 128 and the fp32 accumulator at 192.
 // Every operand sits in shared memory as 8-row x 16-byte core tiles (no swizzle, K-major); the page
 // sections are already in that order, so a page moves with plain bulk copies.
@@ -64,20 +64,23 @@ struct PrefillArgs {
   float qk_scale;    // (1 / sqrt(64)) * log2(e)
 };
 
-constexpr int kPfThreads = 160;
-constexpr int kPfStages = 3;
+constexpr int kPfThreads = 192;
+constexpr int kPfStages = 4;       // per ring (K and V)
 constexpr int kPfQBytes = 16384;   // 128 rows x 64 dims fp16
 
 template <bool I8>
 struct PfLayout {
-  static constexpr int kStage = I8 ? 12288 : 16384;   // K (2 pages) | V (2 pages) or int8 V (2 pages)
-  static constexpr int kPBuf = I8 ? 8192 : 16384;     // 128 rows x 64 keys, u8 or fp16
-  static constexpr int kOffStage = kPfQBytes;
-  static constexpr int kOffP = kOffStage + kPfStages * kStage;
+  static constexpr int kKStage = 8192;                 // K of 64 keys: two 32-token pages
+  static constexpr int kVStage = I8 ? 4096 : 8192;     // V (or int8 V) of the same keys
+  static constexpr int kPBuf = I8 ? 8192 : 16384;      // 128 rows x 64 keys, u8 or fp16
+  static constexpr int kOffK = kPfQBytes;
+  static constexpr int kOffV = kOffK + kPfStages * kKStage;
+  static constexpr int kOffP = kOffV + kPfStages * kVStage;
   static constexpr int kOffBar = kOffP + 2 * kPBuf;
-  static constexpr int kBars = 2 * kPfStages + 3 * 2 + 2;
+  static constexpr int kBars = 4 * kPfStages + 3 * 2 + 2;
   static constexpr int kOffTmemSlot = kOffBar + kBars * 8;
-  static constexpr int kBytes = kOffTmemSlot + 16;
+  static constexpr int kOffAbort = kOffTmemSlot + 8;   // in the dynamic region: static shared memory would
+  static constexpr int kBytes = kOffTmemSlot + 16;      // pad to the 1 KiB alignment and cost the second CTA
   // Request enough shared memory that two CTAs share an SM and a third cannot (TMEM holds 2 x 256 columns).
   static constexpr int kRequest = kBytes > 80 * 1024 ? kBytes : 80 * 1024;
 };
@@ -88,19 +91,22 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   constexpr int NS = kPfStages;
   constexpr uint32_t kTmemCols = 256;
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ int s_abort;
   uint8_t* sQ = smem;
-  uint8_t* sStage = smem + L::kOffStage;
+  uint8_t* sK = smem + L::kOffK;
+  uint8_t* sV = smem + L::kOffV;
   uint8_t* sP = smem + L::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + NS;
-  uint64_t* s_full = bars + 2 * NS;
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = bars + NS;
+  uint64_t* v_full = bars + 2 * NS;
+  uint64_t* v_empty = bars + 3 * NS;
+  uint64_t* s_full = bars + 4 * NS;
   uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* q_ready = pv_done + 2;
   uint64_t* drain = q_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffTmemSlot);
+  int& s_abort = *reinterpret_cast<int*>(smem + L::kOffAbort);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = a.qtiles - 1 - blockIdx.x;   // the longest rows first
@@ -114,8 +120,10 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
@@ -130,7 +138,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   // previous kernel of the stream has completed (a waiting block holding TMEM could starve it). No early
   // trigger: the next kernel's blocks launch as these exit (waiting blocks beside a running one slowed it).
   pdl_wait();
-  if (warp == 4) {
+  if (warp == 5) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -389,54 +397,85 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         }
       }
     }
-  } else {
-    // ================================================================ producer + MMA issuer (warp 4)
-    // One warp runs both roles in one loop (its values stay warp-uniform); lane 0 alone issues the bulk
-    // copies and the tensor-core work. QK runs two tiles ahead of PV: after PV(j), S buffer j & 1 is free
-    // (the softmax read S(j) before it handed over P(j)), so QK(j + 2) goes out at once and the softmax
-    // never waits for scores. The copies of tile j + NS go out once PV(j), the last reader of its stage,
-    // has completed.
+  } else if (warp == 4) {
+    // ================================================================ producer
+    // The K ring runs ahead of the V ring: K(0 .. NS-1), then V(j), K(j + NS). A K stage frees when its QK
+    // completes, a V stage when its PV completes. The whole warp runs the loop; lane 0 issues the copies.
     {
-      bool ok = true;
-      int issued = 0;
-      auto issue_load = [&](int jt) {
-        const int st = jt % NS;
-        const int k0 = kt_begin + jt * kQuantBlock;
-        const int lp0 = k0 / kBlockTokens;
+      int k_issued = 0, v_issued = 0;
+      auto pages = [&](int jt, const char*& s0, const char*& s1) {
+        const int lp0 = (kt_begin + jt * kQuantBlock) / kBlockTokens;
         // A second page wholly past the keys may have no table entry: copy the first page again (masked).
         const int lp1 = (lp0 + 1) * kBlockTokens < kend ? lp0 + 1 : lp0;
-        const char* s0 = a.g.pool + phys_block(a.g, lp0) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
-        const char* s1 = a.g.pool + phys_block(a.g, lp1) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
-        uint8_t* dst = sStage + st * L::kStage;
+        s0 = a.g.pool + phys_block(a.g, lp0) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+        s1 = a.g.pool + phys_block(a.g, lp1) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
+      };
+      auto load_k = [&](int jt) -> bool {
+        const int st = jt % NS;
+        if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&k_empty[st], (uint32_t)((jt / NS) - 1) & 1u))) return false;
+        const char *s0, *s1;
+        pages(jt, s0, s1);
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[st], L::kStage);
-          bulk_g2s(dst, s0, 4096, &full[st]);
-          bulk_g2s(dst + 4096, s1, 4096, &full[st]);
-          if (!I8) {
-            bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV, 4096, &full[st]);
-            bulk_g2s(dst + 12288, s1 + F16Section<64>::kOffV, 4096, &full[st]);
-          } else {
-            bulk_g2s(dst + 8192, s0 + F16Section<64>::kOffV8, 2048, &full[st]);
-            bulk_g2s(dst + 10240, s1 + F16Section<64>::kOffV8, 2048, &full[st]);
-          }
+          mbar_arrive_expect_tx(&k_full[st], L::kKStage);
+          bulk_g2s(sK + st * L::kKStage, s0, 4096, &k_full[st]);
+          bulk_g2s(sK + st * L::kKStage + 4096, s1, 4096, &k_full[st]);
         }
         __syncwarp();
-        issued = jt + 1;
+        k_issued = jt + 1;
+        return true;
       };
-      for (int jt = 0; jt < min(NS, ntiles); ++jt) issue_load(jt);
-      ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
+      auto load_v = [&](int jt) -> bool {
+        const int st = jt % NS;
+        if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&v_empty[st], (uint32_t)((jt / NS) - 1) & 1u))) return false;
+        const char *s0, *s1;
+        pages(jt, s0, s1);
+        constexpr int off = I8 ? F16Section<64>::kOffV8 : F16Section<64>::kOffV, half = L::kVStage / 2;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&v_full[st], L::kVStage);
+          bulk_g2s(sV + st * L::kVStage, s0 + off, half, &v_full[st]);
+          bulk_g2s(sV + st * L::kVStage + half, s1 + off, half, &v_full[st]);
+        }
+        __syncwarp();
+        v_issued = jt + 1;
+        return true;
+      };
+      bool ok = true;
+      for (int jt = 0; jt < min(NS, ntiles) && ok; ++jt) ok = load_k(jt);
+      for (int jt = 0; jt < ntiles && ok; ++jt) {
+        if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) break;
+        ok = load_v(jt);
+        if (ok && jt + NS < ntiles) ok = load_k(jt + NS);
+      }
+      if (!ok) {
+        raise_error(kErrWaitEmpty);
+        atomicExch(&s_abort, 1);
+      }
+      // On an abort, wait (bounded) for the copies still landing in shared memory.
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
+        for (int jt = max(0, k_issued - NS); jt < k_issued; ++jt) mbar_wait(&k_full[jt % NS], (uint32_t)(jt / NS) & 1u);
+        for (int jt = max(0, v_issued - NS); jt < v_issued; ++jt) mbar_wait(&v_full[jt % NS], (uint32_t)(jt / NS) & 1u);
+      }
+    }
+  } else {
+    // ================================================================ MMA issuer (warp 5)
+    // QK runs two tiles ahead of PV: after PV(j), S buffer j & 1 is free (the softmax read S(j) before it
+    // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores.
+    // The whole warp runs the loop (its values stay warp-uniform); lane 0 alone issues the tensor-core work.
+    {
+      bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
       const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
       auto issue_qk = [&](int jt) -> bool {
         const int st = jt % NS, b = jt & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (uint32_t)(jt / NS) & 1u))) return false;
+        if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (uint32_t)(jt / NS) & 1u))) return false;
         tc_fence_after();
-        const uint64_t k_desc = umma_desc(smem_u32(sStage + st * L::kStage), 128, 1024);
+        const uint64_t k_desc = umma_desc(smem_u32(sK + st * L::kKStage), 128, 1024);
         if (lane == 0) {
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)   // +256 bytes per 16 dims: +16 in the descriptor's address field
             umma_f16_ss(tmem + b * 64, q_desc + 16 * ks, k_desc + 16 * ks, kIdescF16M128N64, ks > 0 ? 1u : 0u);
           umma_commit(&s_full[b]);
+          umma_commit(&k_empty[st]);
         }
         __syncwarp();
         return true;
@@ -452,7 +491,12 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
           ok = false;
           break;
         }
-        const int bp = jt & 1, stp = jt % NS;
+        const int bp = jt & 1, st = jt % NS;
+        if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (uint32_t)(jt / NS) & 1u))) {
+          raise_error(kErrWaitFull);
+          ok = false;
+          break;
+        }
         if (!__all_sync(0xffffffffu, mbar_wait(&p_full[bp], (uint32_t)(jt >> 1) & 1u))) {
           raise_error(kErrWaitOther);
           ok = false;
@@ -460,7 +504,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         }
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sP + bp * L::kPBuf);
-        const uint32_t v_addr = smem_u32(sStage + stp * L::kStage + 8192);
+        const uint32_t v_addr = smem_u32(sV + st * L::kVStage);
         if (!I8) {
           const uint64_t p_desc = umma_desc(p_addr, 128, 1024), v_desc = umma_desc(v_addr, 128, 512);
           if (lane == 0) {
@@ -478,7 +522,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
           }
         }
         if (lane == 0) {
-          umma_commit(&empty[stp]);
+          umma_commit(&v_empty[st]);
           umma_commit(&pv_done[bp]);
         }
         __syncwarp();
@@ -487,29 +531,18 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
           ok = false;
           break;
         }
-        if (jt + NS < ntiles) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&empty[stp], (uint32_t)(jt / NS) & 1u))) {
-            raise_error(kErrWaitEmpty);
-            ok = false;
-            break;
-          }
-          issue_load(jt + NS);
-        }
       }
-      // Leave no tensor-core work in flight behind an abort, and wait (bounded) for copies still landing.
+      // Leave no tensor-core work in flight behind an abort.
       if (lane == 0) umma_commit(drain);
       __syncwarp();
       mbar_wait(drain, 0);
-      if (!ok) {
-        atomicExch(&s_abort, 1);
-        for (int jt = max(0, issued - NS); jt < issued; ++jt) mbar_wait(&full[jt % NS], (uint32_t)(jt / NS) & 1u);
-      }
+      if (!ok) atomicExch(&s_abort, 1);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 5) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
