@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--load-seconds", type=float, default=2.0, help="untimed replays while the clock sampler runs")
+    ap.add_argument("--shard", choices=["heads", "seq"], default="heads", help="multi-GPU plan (N > 1)")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 fields (N = 1)")
     return ap.parse_args()
 
 
@@ -58,8 +60,8 @@ def peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         p = json.loads(path.read_text())
-        return {"hbm_gbs": float(p["hbm_gbs"]), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p.get("bf16_tflops") or 1590.0), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
 def ncu_traffic(name: str):
@@ -181,6 +183,200 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ GPU arm
+class Rank:
+    """This process's share of the config-2 workload under the chosen plan (one process per GPU).
+
+    single  one GPU: 32768 cached tokens x 8 kv heads, the 16 drafts and all 32 query heads.
+    heads   the context grows with the world (32768 x N tokens, weak scaling); rank r holds kv heads
+            [8r/N, 8(r+1)/N) of all of it and their query heads, appends its heads' drafts, verifies them,
+            and the outputs are all-gathered (NCCL).
+    seq     the context grows the same way; rank r holds 32768 tokens of it (all heads), the last rank also
+            the drafts; the log-sum-exp partials are all-gathered (NCCL) and merged on every rank.
+    Both multi-GPU plans keep 32768 x 8 x 64 fp16 K and V per GPU, as on one GPU."""
+
+    def __init__(self, world: int, rank: int, plan: str):
+        from shard import head_range, query_head_range, seq_range
+
+        self.world, self.rank, self.plan = world, rank, plan
+        self.ctx_len = CTX * world
+        self.kvh, self.qh = KVH, QH
+        self.h0, self.h1, self.q0, self.q1 = 0, KVH, 0, QH
+        self.kv_begin, self.kv_end = 0, self.ctx_len + M
+        if plan == "heads":
+            self.h0, self.h1 = head_range(world, rank, KVH)
+            self.q0, self.q1 = query_head_range(world, rank, KVH, QH)
+            self.kvh, self.qh = self.h1 - self.h0, self.q1 - self.q0
+        elif plan == "seq":
+            self.kv_begin, self.kv_end = seq_range(world, rank, self.ctx_len, M)
+        self.drafts = plan != "seq" or rank == world - 1
+        self.cached = min(self.kv_end, self.ctx_len) - self.kv_begin   # context tokens this rank holds
+
+    def bytes_read(self) -> int:
+        """K/V bytes this rank's attention reads per step."""
+        return (self.kv_end - self.kv_begin) * self.kvh * D * 2 * 2
+
+
+def measure_c3(la, synth, dev, peak_gbs: float, steps: int = 60) -> dict:
+    """Config 3 on one GPU: verify rounds at 131072 cached tokens (seed 2), two rotating 256 MiB caches."""
+    import numpy as np
+    import torch
+
+    ctx = 131072
+    case = synth.verify_case(2, ctx, M)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    rope = t(la.rope_table(1e6, 1.0, D, ctx + M + 1).view(np.float16))
+    K0, V0 = t(case["K"]), t(case["V"])
+    caches = []
+    for _ in range(2):
+        c = la.LayerCache(la.MODE_F16, KVH, D, ctx + M + 64, device=dev)
+        c.append(K0, V0, 0)
+        caches.append(c)
+    del K0, V0
+    q, nk, nv = t(case["Q"]), t(case["newK"]), t(case["newV"])
+    out = torch.empty_like(q)
+    splits = la.verify_splits(caches[0].layout, ctx, M, 0)
+    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(M, QH, D, splits), dtype=torch.uint8, device=dev)
+
+    def step(c, ev=None):
+        c.append(nk, nv, ctx, rope=rope)
+        if ev:
+            ev[0].record()
+        c.verify(q, ctx, out=out, workspace=ws, splits=splits)
+        if ev:
+            ev[1].record()
+        c.truncate(ctx)
+
+    for i in range(4):
+        step(caches[i % 2])
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+           for _ in range(steps)]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(steps):
+            step(caches[i % 2], evs[i])
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    step_us = e0.elapsed_time(e1) * 1e3 / steps
+    att_us = statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e3
+    la.sync()
+    byts = kv_bytes(ctx + M)
+    del g
+    return {"workload": "config 3 on 1 GPU: verify round at 131072 cached tokens, 16 drafts (seed 2)",
+            "us_per_layer": round(step_us, 2), "verify_us": round(att_us, 2), "splits": splits,
+            "hbm_gbs": round(byts / (att_us * 1e-6) / 1e9, 1), "frac": round(byts / (att_us * 1e-6) / 1e9 / peak_gbs, 4),
+            "bytes": byts}
+
+
+def measure_c4(la, synth, dev, peaks_: dict, reps: int = 5) -> dict:
+    """Config 4: causal prefill attention of 32768 tokens (seed 3), int8-PV and exact fp16."""
+    import numpy as np
+    import torch
+
+    T = 32768
+    case = synth.prefill_case(3, T)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    cache = la.LayerCache(la.MODE_F16, KVH, D, T + 64, device=dev)
+    cache.append(t(case["K"]), t(case["V"]), 0)
+    q = t(case["Q"])
+    out = torch.empty_like(q)
+    flops = 2.0 * QH * D * T * (T + 1) / 2   # QK; PV has the same count
+    res = {"workload": "config 4: causal prefill attention, 32768 tokens, GQA 32/8, head_dim 64 (seed 3)",
+           "qk_flop": flops, "pv_ops": flops}
+    tf16 = peaks_.get("bf16_tflops")
+    for name, exact in (("int8_pv", False), ("exact", True)):
+        for _ in range(2):
+            cache.prefill(q, 0, exact=exact, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            cache.prefill(q, 0, exact=exact, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        entry = {"ms": round(ms, 3), "pv_tops": round(flops / (ms * 1e-3) / 1e12, 1)}
+        if tf16:
+            # roofline time: QK at the fp16 (bf16-measured) dense peak, PV at the int8 peak (twice the fp16 rate)
+            # or at the fp16 peak for the exact kernel
+            t_roof = flops / (tf16 * 1e12) + flops / ((2.0 if not exact else 1.0) * tf16 * 1e12)
+            entry["tensor_frac"] = round(t_roof / (ms * 1e-3), 4)
+        res[name] = entry
+    la.sync()
+    if tf16:
+        res["peak"] = f"{tf16} TFLOP/s dense fp16 (measured bf16), int8 at twice that (nominal ratio)"
+    return res
+
+
+def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, seed: int = 4) -> dict:
+    """Config 5, the KV lifecycle: per layer a causal prefill of ctx tokens (append with RoPE + int8-PV
+    attention), then `steps` DSpark rounds over all layers (append 16 drafts, verify 16, keep
+    n = min(16, X), X ~ geometric(0.3), roll back 16 - n). Inputs N(0,1) fp16 from torch's seeded generator
+    on the device (the splitmix64 stream is too slow on the host at this size)."""
+    import numpy as np
+    import torch
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    rnd = lambda *shape: torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).half()
+    rng = np.random.default_rng(seed)
+    keep = np.minimum(16, rng.geometric(0.3, size=steps))
+    cap = ctx + int(keep.sum()) + M + 64
+    rope = torch.from_numpy(la.rope_table(1e6, 1.0, D, cap + 1).view(np.float16)).to(dev)
+    caches = [la.LayerCache(la.MODE_F16, KVH, D, cap, device=dev) for _ in range(layers)]
+    q_pre = rnd(ctx, QH, D)
+    out_pre = torch.empty_like(q_pre)
+    torch.cuda.synchronize()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    k_in = [(rnd(ctx, KVH, D), rnd(ctx, KVH, D)) for _ in range(layers)]
+    torch.cuda.synchronize()
+    e0.record()
+    for c, (k, v) in zip(caches, k_in):
+        c.append(k, v, 0, rope=rope)
+        c.prefill(q_pre, 0, exact=False, out=out_pre)
+    e1.record()
+    torch.cuda.synchronize()
+    del k_in, q_pre, out_pre
+    drafts = rnd(steps, 2, M, KVH, D)
+    qs = rnd(steps, M, QH, D)
+    splits_ws = la.lib().lfm3a_verify_workspace_bytes(M, QH, D, 2 * 148)
+    ws = torch.empty(splits_ws, dtype=torch.uint8, device=dev)
+    out = torch.empty((M, QH, D), dtype=torch.float16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    g = torch.cuda.CUDAGraph()
+    length = ctx
+    with torch.cuda.graph(g, stream=stream):
+        for s in range(steps):
+            for c in caches:
+                c.append(drafts[s, 0], drafts[s, 1], length, rope=rope)
+                c.verify(qs[s], length, out=out, workspace=ws)
+                c.truncate(length + int(keep[s]))
+            length += int(keep[s])
+    torch.cuda.synchronize()
+    e1.record()
+    g.replay()
+    e2.record()
+    torch.cuda.synchronize()
+    la.sync()
+    prefill_ms = e0.elapsed_time(e1)
+    verify_ms = e1.elapsed_time(e2)
+    lengths = sorted({c.length for c in caches})
+    del g, caches
+    return {"workload": f"config 5: KV lifecycle, {layers} layers, {ctx}-token causal prefill (int8-PV), then "
+                        f"{steps} rounds of 16 drafts (keep min(16, Geom(0.3)))",
+            "data": "torch.randn N(0,1) fp16 on the device, seed 4; keep lengths from numpy default_rng(4)",
+            "total_ms": round(prefill_ms + verify_ms, 2), "prefill_ms": round(prefill_ms, 2),
+            "verify_ms": round(verify_ms, 2),
+            "us_per_layer_round": round(verify_ms * 1e3 / (steps * layers), 2),
+            "final_length": lengths[0] if len(lengths) == 1 else lengths, "expected_length": ctx + int(keep.sum())}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -203,70 +399,81 @@ def run_ours(args):
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         pg = dist
+    R = Rank(world, rank, args.shard if world > 1 else "single")
 
-    last = rank == world - 1
-    case = synth.verify_case(SEED + rank, CTX, M)   # this rank's shard of the context; drafts/Q on every rank
-    if world > 1:
-        # every rank uses the same drafts and queries (those of rank world - 1's stream), as one sequence would
-        ref_case = synth.verify_case(SEED + world - 1, CTX, M)
-        case["newK"], case["newV"], case["Q"] = ref_case["newK"], ref_case["newV"], ref_case["Q"]
-    kv_begin = rank * CTX
-    ctx_len = world * CTX              # global context length before the drafts
-    bytes_rank = kv_bytes(CTX + (M if last else 0))
-    bytes_step = kv_bytes(world * CTX + M)
+    # Inputs: on one GPU the config-2 stream (seed 1: K, V, new K, new V, Q); on N GPUs each rank draws its
+    # own K/V (seed 101 + rank) and every rank slices the same drafts and queries (seed 1).
+    if world == 1:
+        case = synth.verify_case(SEED, CTX, M)
+        Kc, Vc = case["K"], case["V"]
+    else:
+        case = synth.verify_case(SEED, 0, M)
+        st = synth.Stream(SEED + 100 + rank)
+        Kc = st.normal_f16((R.cached, R.kvh, D))
+        Vc = st.normal_f16((R.cached, R.kvh, D))
+    newK = np.ascontiguousarray(case["newK"][:, R.h0:R.h1])
+    newV = np.ascontiguousarray(case["newV"][:, R.h0:R.h1])
+    Qr = np.ascontiguousarray(case["Q"][:, R.q0:R.q1])
 
-    # Rotating layer caches: consecutive steps read different memory, more than the L2 in total.
-    n_layers = max(2, math.ceil(3 * L2_BYTES / kv_bytes(CTX)))
-    rope_np = la.rope_table(1e6, 1.0, D, ctx_len + M + 1)
+    n_layers = max(2, math.ceil(3 * L2_BYTES / (R.cached * R.kvh * D * 4)))
+    rope_np = la.rope_table(1e6, 1.0, D, R.ctx_len + M + 1)
     rope = torch.from_numpy(rope_np.view(np.float16)).to(dev)
 
     def t(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
-    K0, V0 = t(case["K"]), t(case["V"])
+    K0, V0 = t(Kc), t(Vc)
+    del Kc, Vc
     caches = []
+    cap = R.ctx_len + M + 64
     for _ in range(n_layers):
-        blocks_total = (ctx_len + M + 64) // 32 + 1
-        table = torch.zeros(blocks_total, dtype=torch.int32, device=dev)
-        first_blk = kv_begin // 32
-        local_blocks = (CTX + (M + 64 if last else 0)) // 32 + 1
-        table[first_blk:first_blk + local_blocks] = torch.arange(local_blocks, dtype=torch.int32, device=dev)
-        c = la.LayerCache(la.MODE_F16, KVH, D, ctx_len + M + 64, device=dev, block_table=table, pool_blocks=local_blocks)
-        c.append(K0, V0, kv_begin)
+        table = torch.zeros((cap + 31) // 32, dtype=torch.int32, device=dev)
+        lb0 = R.kv_begin // 32
+        local_blocks = (R.cached + (M + 64 if R.drafts else 0)) // 32 + 1
+        table[lb0:lb0 + local_blocks] = torch.arange(local_blocks, dtype=torch.int32, device=dev)
+        c = la.LayerCache(la.MODE_F16, R.kvh, D, cap, device=dev, block_table=table, pool_blocks=local_blocks)
+        c.append(K0, V0, R.kv_begin)
         caches.append(c)
     del K0, V0
-    q = t(case["Q"])
-    nk, nv = t(case["newK"]), t(case["newV"])
-    out = torch.empty_like(q)
-    splits = la.verify_splits(caches[0].layout, CTX, M, 0)
-    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(M, QH, D, splits), dtype=torch.uint8, device=dev)
+    q = t(Qr)
+    nk, nv = t(newK), t(newV)
+    out = torch.empty((M, QH, D), dtype=torch.float16, device=dev)
+    out_l = torch.empty_like(q)
+    splits = la.verify_splits(caches[0].layout, R.kv_end - R.kv_begin if R.plan == "seq" else R.ctx_len, M, 0)
+    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(M, R.qh, D, splits), dtype=torch.uint8, device=dev)
     part = torch.empty((M * QH, D + 2), dtype=torch.float32, device=dev)
     gathered = torch.empty((world, M * QH, D + 2), dtype=torch.float32, device=dev)
+    gathered_out = torch.empty((world, M, R.qh, D), dtype=torch.float16, device=dev)
     torch.cuda.synchronize()
 
-    kernel_events = []
-
-    def step(c, timing=None):
-        """One verify round of one layer (kernels: append with the int8 V of its block, verify, combine;
-        rollback adds none at a 64-aligned length)."""
-        if last:
-            c.append(nk, nv, ctx_len, rope=rope)
+    def attend(c, dq, timing=None):
         if timing is not None:
             timing[0].record()
-        if world == 1:
-            c.verify(q, ctx_len, out=out, workspace=ws, splits=splits)
+        if R.plan == "seq":
+            c.verify_partial(dq, R.kv_begin, R.kv_end, R.ctx_len, out=part, workspace=ws, splits=splits)
+        elif R.plan == "heads":
+            c.verify(dq, R.ctx_len, out=out_l, workspace=ws, splits=splits)
         else:
-            end = kv_begin + CTX + (M if last else 0)
-            c.verify_partial(q, kv_begin, end, ctx_len, out=part, workspace=ws, splits=splits)
+            c.verify(dq, R.ctx_len, out=out, workspace=ws, splits=splits)
         if timing is not None:
             timing[1].record()
-        if world > 1:
+        if R.plan == "seq":
             pg.all_gather_into_tensor(gathered, part)
-            la.combine(gathered, M * QH, world, D, split_stride=M * QH * (D + 2), row_stride=D + 2, out=out.view(M * QH, D))
-        if last:
-            c.truncate(ctx_len)
+            la.combine(gathered, M * QH, world, D, split_stride=M * QH * (D + 2), row_stride=D + 2,
+                       out=out.view(M * QH, D))
+        elif R.plan == "heads":
+            pg.all_gather_into_tensor(gathered_out, out_l)
 
-    launches_per_step = (1 if last else 0) + (2 if splits > 1 else 1) + (1 if world > 1 else 0)
+    def step(c, timing=None, dq=None, dk=None, dv=None):
+        """One verify round of one layer (kernels: append with the int8 V of its block, verify, combine;
+        rollback adds none at a 64-aligned length)."""
+        if R.drafts:
+            c.append(nk if dk is None else dk, nv if dv is None else dv, R.ctx_len, rope=rope)
+        attend(c, q if dq is None else dq, timing)
+        if R.drafts:
+            c.truncate(R.ctx_len)
+
+    launches_per_step = (1 if R.drafts else 0) + (2 if splits > 1 else 1) + (1 if R.plan == "seq" else 0)
 
     # Warm-up (eager), then capture the timed graph with per-step kernel events.
     for i in range(max(args.warmup, 3)):
@@ -315,10 +522,11 @@ def run_ours(args):
 
     # ---- e2e: the public API with host buffers, one step at a time, copies and the result read included
     e2e_steps = min(K, 200)
-    hq = torch.from_numpy(np.ascontiguousarray(case["Q"])).pin_memory()
-    hk = torch.from_numpy(np.ascontiguousarray(case["newK"])).pin_memory()
-    hv = torch.from_numpy(np.ascontiguousarray(case["newV"])).pin_memory()
-    hout = torch.empty(q.shape, dtype=torch.float16).pin_memory()
+    hq = torch.from_numpy(Qr).pin_memory()
+    hk = torch.from_numpy(newK).pin_memory()
+    hv = torch.from_numpy(newV).pin_memory()
+    res = gathered_out if R.plan == "heads" else out
+    hout = torch.empty(res.shape, dtype=torch.float16).pin_memory()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(nk), torch.empty_like(nv)
     if pg:
         pg.barrier()
@@ -328,22 +536,11 @@ def run_ours(args):
     s1 = torch.cuda.Event(enable_timing=True)
     s0.record()
     for i in range(e2e_steps):
-        c = caches[i % n_layers]
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        if last:
-            c.append(dk, dv, ctx_len, rope=rope)
-        if world == 1:
-            c.verify(dq, ctx_len, out=out, workspace=ws, splits=splits)
-        else:
-            end = kv_begin + CTX + (M if last else 0)
-            c.verify_partial(dq, kv_begin, end, ctx_len, out=part, workspace=ws, splits=splits)
-            pg.all_gather_into_tensor(gathered, part)
-            la.combine(gathered, M * QH, world, D, split_stride=M * QH * (D + 2), row_stride=D + 2, out=out.view(M * QH, D))
-        if last:
-            c.truncate(ctx_len)
-        hout.copy_(out, non_blocking=True)
+        step(caches[i % n_layers], None, dq, dk, dv)
+        hout.copy_(res, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     s1.record()
     torch.cuda.synchronize()
@@ -357,6 +554,7 @@ def run_ours(args):
         pg.all_reduce(stats, op=pg.ReduceOp.MAX)
     total_ms, kern_avg_ms, e2e_ms, e2e_wall_ms = stats.tolist()
     ms_step = total_ms / K
+    bytes_step = kv_bytes(R.ctx_len + M)   # all ranks together
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -364,11 +562,24 @@ def run_ours(args):
         cpu = {"value": round(kv_bytes(CTX + M) / sec / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"{calls} full verify rounds of one layer at config 2 (oracle, {threads} threads, "
                          f"{sec * 1e3:.1f} ms each)"}
+    del graph, load_graph
+
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        pk = peaks()
+        del caches
+        torch.cuda.empty_cache()
+        extras["c3"] = measure_c3(la, synth, dev, pk["hbm_gbs"])
+        torch.cuda.empty_cache()
+        extras["c4"] = measure_c4(la, synth, dev, pk)
+        torch.cuda.empty_cache()
+        extras["c5"] = measure_c5(la, dev)
 
     if rank == 0:
         pk = peaks()
-        achieved = bytes_rank / (kern_avg_ms * 1e-3) / 1e9
+        achieved = R.bytes_read() / (kern_avg_ms * 1e-3) / 1e9
         traffic = ncu_traffic("verify_m64_kernel_c2.txt") if world == 1 else None
+        plan_text = {"single": "single GPU", "heads": f"kv-head shard x{world}", "seq": f"sequence shard x{world}"}
         line = {
             "metric": METRIC,
             "value": round(bytes_step / (ms_step * 1e-3) / 1e9, 2),
@@ -382,20 +593,22 @@ def run_ours(args):
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "fp16 (fp32 accumulation)",
-            "data": "synthetic (splitmix64 + Box-Muller fp16, seed 1 + rank)",
+            "data": "synthetic (splitmix64 + Box-Muller fp16; seed 1, and seed 101 + rank for each rank's K/V)",
             "config": {
                 "workload": "config 2: verify round of one layer (append 16 drafts with RoPE, verify attention of 16 "
                             "tokens over 32768 cached + drafts, rollback), GQA 32/8, head_dim 64, fp16 KV"
-                            + (f"; sequence sharded over {world} GPUs, 32768 cached tokens each" if world > 1 else ""),
-                "context_tokens": ctx_len,
+                            + (f"; {plan_text[R.plan]}, 32768 x 8 x 64 K/V per GPU, context 32768 x {world}"
+                               if world > 1 else ""),
+                "context_tokens": R.ctx_len,
                 "drafts": M,
                 "splits_per_gpu": splits,
-                "l2": f"{n_layers} rotating layer caches of {kv_bytes(CTX) >> 20} MiB (> 126 MB L2), no flush",
-                "parallelism": f"sequence-shard x{world}" if world > 1 else "single GPU",
+                "l2": f"{n_layers} rotating layer caches of {R.cached * R.kvh * D * 4 >> 20} MiB (> 126 MB L2), "
+                      "no flush",
+                "parallelism": plan_text[R.plan],
                 "graph": "each timed step replayed from one CUDA graph of K steps",
             },
             "roofline": {
-                "kernel": "verify_m64_kernel" + (" (+ per-rank partial)" if world > 1 else " + combine_kernel"),
+                "kernel": "verify_m64_kernel + combine_kernel" + (" (per rank)" if world > 1 else ""),
                 "bound": "hbm",
                 "achieved": round(achieved, 1),
                 "peak": pk["hbm_gbs"],
@@ -403,7 +616,7 @@ def run_ours(args):
                 "frac": round(achieved / pk["hbm_gbs"], 4),
                 "peak_src": pk["src"],
                 "traffic": traffic,
-                "algorithmic_bytes_per_launch": bytes_rank,
+                "algorithmic_bytes_per_launch": R.bytes_read(),
                 "avg_launch_us": round(kern_avg_ms * 1e3, 3),
             },
             "cpu_baseline": cpu,
@@ -415,8 +628,8 @@ def run_ours(args):
             "gpu_launches": int(launches_per_step * K),
             "clocks": clocks,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
-    del graph, load_graph
     if pg:
         pg.barrier()
         pg.destroy_process_group()

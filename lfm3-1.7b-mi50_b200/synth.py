@@ -7,6 +7,8 @@ Arrays are drawn row-major from one stream in the order K, V, new K, new V, Q.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 _GAMMA = np.uint64(0x9E3779B97F4A7C15)
@@ -31,15 +33,18 @@ class Stream:
         self.seed = seed
         self.pos = 0   # splitmix64 outputs consumed
 
-    def normal(self, count: int, chunk: int = 1 << 24) -> np.ndarray:
+    def normal(self, count: int, chunk: int = 1 << 22) -> np.ndarray:
+        """count normal values (float64). Chunks are independent (the stream is indexed by position), so they
+        are drawn on all host threads; the values do not depend on the chunking."""
         if count % 2:
             raise ValueError("draw an even number of values")
         out = np.empty(count, dtype=np.float64)
-        done = 0
-        while done < count:
+        base = self.pos
+        self.pos += count
+
+        def fill(done: int) -> None:
             n = min(chunk, count - done)
-            raw = _splitmix(self.seed, self.pos, n)
-            self.pos += n
+            raw = _splitmix(self.seed, base + done, n)
             u = (raw >> np.uint64(11)).astype(np.float64) * (2.0 ** -53)
             u1 = np.maximum(u[0::2], 2.0 ** -53)
             u2 = u[1::2]
@@ -47,7 +52,16 @@ class Stream:
             ang = 2.0 * np.pi * u2
             out[done:done + n:2] = r * np.cos(ang)
             out[done + 1:done + n:2] = r * np.sin(ang)
-            done += n
+
+        starts = range(0, count, chunk)
+        if count > chunk:
+            from concurrent.futures import ThreadPoolExecutor
+
+            with ThreadPoolExecutor(max_workers=min(len(starts), os.cpu_count() or 1)) as pool:
+                list(pool.map(fill, starts))
+        else:
+            for done in starts:
+                fill(done)
         return out
 
     def normal_f16(self, shape) -> np.ndarray:

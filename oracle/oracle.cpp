@@ -235,6 +235,79 @@ void orc_quantize_p_u8(const float* p, int rows, int cols, uint8_t* q, float* sc
   }
 }
 
+}  // extern "C"
+
+namespace {
+
+// One verify row over the 32-key pages [g0, g1), restricted to the keys [klo, khi): exact running max with
+// rescale, p = 2^(s - m), l += p, acc += fp16(p) x V (dspark.hip:1914-2076). Leaves the unnormalised
+// (acc, m, l) of that key range.
+void verify_pages(const float* qf, int D, int kv_heads, int h, int qpos, int ctx_len, int start, int window,
+                  const uint16_t* K, const uint16_t* V, int g0, int g1, int klo, int khi, float qk_scale,
+                  float* acc, float& m_out, float& l_out) {
+  float m_run = -1e30f, l_run = 0.f;
+  for (int d = 0; d < D; ++d) acc[d] = 0.f;
+  for (int pg = g0; pg < g1; ++pg) {
+    float sc[BS];
+    float mx = -INFINITY;
+    for (int kk = 0; kk < BS; ++kk) {
+      const int kpos = pg * BS + kk;
+      bool valid;
+      if (kpos < ctx_len) valid = kpos >= start && (window == 0 || kpos > qpos - window);
+      else valid = kpos <= qpos;
+      valid = valid && kpos >= klo && kpos < khi;
+      if (!valid) {
+        sc[kk] = -INFINITY;
+        continue;
+      }
+      const uint16_t* kr = K + ((size_t)kpos * kv_heads + h) * D;
+      float dot = 0.f;
+#pragma omp simd reduction(+ : dot)
+      for (int d = 0; d < D; ++d) dot += qf[d] * orc_f16_to_f32(kr[d]);
+      sc[kk] = dot * qk_scale;
+      mx = fmaxf(mx, sc[kk]);
+    }
+    if (mx > m_run) {
+      const float corr = exp2f(m_run - mx);
+      m_run = mx;
+      l_run *= corr;
+      for (int d = 0; d < D; ++d) acc[d] *= corr;
+    }
+    for (int kk = 0; kk < BS; ++kk) {
+      if (sc[kk] == -INFINITY) continue;
+      const int kpos = pg * BS + kk;
+      const float p = exp2f(sc[kk] - m_run);
+      l_run += p;
+      const float p16 = r16(p);
+      const uint16_t* vr = V + ((size_t)kpos * kv_heads + h) * D;
+      for (int d = 0; d < D; ++d) acc[d] += p16 * orc_f16_to_f32(vr[d]);
+    }
+  }
+  m_out = m_run;
+  l_out = l_run;
+}
+
+// Log-sum-exp merge of S partials (dspark.hip:2134-2185): out = gate x sum f_s acc_s / sum f_s l_s,
+// f_s = 2^(m_s - max m), gate = sigmoid(gate logit) when given.
+void merge_row(const float* acc, const float* pm, const float* pl, int S, int D, const uint16_t* gate, int row,
+               float* out) {
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s) M = fmaxf(M, pm[s]);
+  float L = 0.f, o[128] = {0};
+  for (int s = 0; s < S; ++s) {
+    const float f = exp2f(pm[s] - M);
+    L += f * pl[s];
+    for (int d = 0; d < D; ++d) o[d] += f * acc[(size_t)s * D + d];
+  }
+  float g = 1.f;
+  if (gate) g = 1.f / (1.f + exp2f(-orc_f16_to_f32(gate[row]) * LOG2E));
+  for (int d = 0; d < D; ++d) out[d] = (L > 0.f ? o[d] / L : 0.f) * g;
+}
+
+}  // namespace
+
+extern "C" {
+
 void orc_verify(const uint16_t* q, int m, int q_heads, int kv_heads, int head_dim, const uint16_t* K,
                 const uint16_t* V, int ctx_len, int window, const uint16_t* gate, int splits, float* out) {
   const int D = head_dim, G = q_heads / kv_heads;
@@ -250,57 +323,46 @@ void orc_verify(const uint16_t* q, int m, int q_heads, int kv_heads, int head_di
     std::vector<float> pacc((size_t)S * D, 0.f), pm(S, -1e30f), pl(S, 0.f);
     for (int s = 0; s < S; ++s) {
       const int g0 = p_begin + (int)((int64_t)p_total * s / S), g1 = p_begin + (int)((int64_t)p_total * (s + 1) / S);
-      float m_run = -1e30f, l_run = 0.f, acc[128] = {0};
-      for (int pg = g0; pg < g1; ++pg) {
-        float sc[BS];
-        float mx = -INFINITY;
-        for (int kk = 0; kk < BS; ++kk) {
-          const int kpos = pg * BS + kk;
-          bool valid;
-          if (kpos < ctx_len) valid = kpos >= start && (window == 0 || kpos > qpos - window);
-          else valid = kpos <= qpos;
-          if (!valid) {
-            sc[kk] = -INFINITY;
-            continue;
-          }
-          const uint16_t* kr = K + ((size_t)kpos * kv_heads + h) * D;
-          float dot = 0.f;
-#pragma omp simd reduction(+ : dot)
-          for (int d = 0; d < D; ++d) dot += qf[d] * orc_f16_to_f32(kr[d]);
-          sc[kk] = dot * qk_scale;
-          mx = fmaxf(mx, sc[kk]);
-        }
-        if (mx > m_run) {
-          const float corr = exp2f(m_run - mx);
-          m_run = mx;
-          l_run *= corr;
-          for (int d = 0; d < D; ++d) acc[d] *= corr;
-        }
-        for (int kk = 0; kk < BS; ++kk) {
-          if (sc[kk] == -INFINITY) continue;
-          const int kpos = pg * BS + kk;
-          const float p = exp2f(sc[kk] - m_run);
-          l_run += p;
-          const float p16 = r16(p);
-          const uint16_t* vr = V + ((size_t)kpos * kv_heads + h) * D;
-          for (int d = 0; d < D; ++d) acc[d] += p16 * orc_f16_to_f32(vr[d]);
-        }
-      }
-      for (int d = 0; d < D; ++d) pacc[(size_t)s * D + d] = acc[d];
-      pm[s] = m_run;
-      pl[s] = l_run;
+      verify_pages(qf, D, kv_heads, h, qpos, ctx_len, start, window, K, V, g0, g1, 0, kv_end, qk_scale,
+                   &pacc[(size_t)s * D], pm[s], pl[s]);
     }
-    float M = -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, pm[s]);
-    float L = 0.f, o[128] = {0};
-    for (int s = 0; s < S; ++s) {
-      const float f = exp2f(pm[s] - M);
-      L += f * pl[s];
-      for (int d = 0; d < D; ++d) o[d] += f * pacc[(size_t)s * D + d];
+    merge_row(pacc.data(), pm.data(), pl.data(), S, D, gate, row, out + (size_t)row * D);
+  }
+}
+
+// The verify partial of one cache shard (keys [kv_begin, kv_end) of the sequence, K/V indexed by global
+// position): per row [acc[D] (unnormalised, at the shard's max), max, sum], as lfm3a_verify_partial leaves
+// it for the cross-GPU merge.
+void orc_verify_partial(const uint16_t* q, int m, int q_heads, int kv_heads, int head_dim, const uint16_t* K,
+                        const uint16_t* V, int kv_begin, int kv_end, int ctx_len, int window, float* part) {
+  const int D = head_dim, G = q_heads / kv_heads;
+  const int start = kv_start(ctx_len, window);
+  const float qk_scale = (1.f / sqrtf((float)D)) * LOG2E;
+  const int g0 = kv_begin / BS, g1 = (kv_end - 1) / BS + 1;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int row = 0; row < m * q_heads; ++row) {
+    const int t = row / q_heads, qh = row % q_heads, h = qh / G, qpos = ctx_len + t;
+    float qf[128];
+    for (int d = 0; d < D; ++d) qf[d] = orc_f16_to_f32(q[(size_t)row * D + d]);
+    float* pr = part + (size_t)row * (D + 2);
+    verify_pages(qf, D, kv_heads, h, qpos, ctx_len, start, window, K, V, g0, g1, kv_begin, kv_end, qk_scale, pr,
+                 pr[D], pr[D + 1]);
+  }
+}
+
+// Merge of S partials laid out [S][rows][D + 2] (acc, max, sum) into out [rows][D] (dspark.hip:2134-2185).
+void orc_combine(const float* parts, int rows, int splits, int head_dim, const uint16_t* gate, float* out) {
+  const int D = head_dim;
+#pragma omp parallel for schedule(static)
+  for (int row = 0; row < rows; ++row) {
+    std::vector<float> acc((size_t)splits * D), pm(splits), pl(splits);
+    for (int s = 0; s < splits; ++s) {
+      const float* pr = parts + ((size_t)s * rows + row) * (D + 2);
+      for (int d = 0; d < D; ++d) acc[(size_t)s * D + d] = pr[d];
+      pm[s] = pr[D];
+      pl[s] = pr[D + 1];
     }
-    float g = 1.f;
-    if (gate) g = 1.f / (1.f + exp2f(-orc_f16_to_f32(gate[row]) * LOG2E));
-    for (int d = 0; d < D; ++d) out[(size_t)row * D + d] = (L > 0.f ? o[d] / L : 0.f) * g;
+    merge_row(acc.data(), pm.data(), pl.data(), splits, D, gate, row, out + (size_t)row * D);
   }
 }
 

@@ -62,6 +62,17 @@ void orc_quantize_p_u8(const float* p, int rows, int cols, uint8_t* q, float* sc
 void orc_verify(const uint16_t* q, int m, int q_heads, int kv_heads, int head_dim, const uint16_t* K,
                 const uint16_t* V, int ctx_len, int window, const uint16_t* gate, int splits, float* out);
 
+/* The verify partial of one cache shard: keys [kv_begin, kv_end) of the sequence (K/V indexed by global
+ * position), the same masks as orc_verify, one pass over the shard's pages. part: [m * q_heads][head_dim + 2]
+ * = unnormalised acc at the shard's running max, the max (log2 units), the sum (the (acc, m, l) partial of
+ * dspark.hip:2100-2120, as lfm3a_verify_partial leaves it). */
+void orc_verify_partial(const uint16_t* q, int m, int q_heads, int kv_heads, int head_dim, const uint16_t* K,
+                        const uint16_t* V, int kv_begin, int kv_end, int ctx_len, int window, float* part);
+
+/* Log-sum-exp merge of splits partials laid out [splits][rows][head_dim + 2] into out [rows][head_dim] f32,
+ * with the optional sigmoid gate (dspark.hip:2134-2185). */
+void orc_combine(const float* parts, int rows, int splits, int head_dim, const uint16_t* gate, float* out);
+
 /* Exact fp64 attention for query tokens at positions qpos0 + t (t < nq) over keys [0, kv_len), causal,
  * optional sliding window; rows t = 0, row_step, 2*row_step, ... only. out [nq][q_heads][head_dim] f32
  * (rows not computed are left untouched). */

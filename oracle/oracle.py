@@ -28,6 +28,8 @@ _SIGS = {
     "orc_quantize_v8": (None, [_P, _I, _I, _I, _P, _P]),
     "orc_quantize_p_u8": (None, [_P, _I, _I, _P, _P]),
     "orc_verify": (None, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _P]),
+    "orc_verify_partial": (None, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _I, _I, _P]),
+    "orc_combine": (None, [_P, _I, _I, _I, _P, _P]),
     "orc_attention_f64": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
     "orc_prefill_i8pv": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
     "orc_prefill_exact": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _P]),
@@ -131,6 +133,28 @@ def verify(q, K, V, ctx_len: int, window: int = 0, gate=None, splits: int = 1) -
     gate, gp = _c(gate, np.float16)
     out = np.empty((m, qh, d), dtype=np.float32)
     lib().orc_verify(qp, m, qh, kvh, d, kp, vp, ctx_len, window, gp, splits, out.ctypes.data)
+    return out
+
+
+def verify_partial(q, K, V, kv_begin: int, kv_end: int, ctx_len: int, window: int = 0) -> np.ndarray:
+    """Partial [m * q_heads][d + 2] (acc, max, sum) of the keys [kv_begin, kv_end); K/V by global position."""
+    m, qh, d = q.shape
+    kvh = K.shape[1]
+    q, qp = _c(q, np.float16)
+    K, kp = _c(K, np.float16)
+    V, vp = _c(V, np.float16)
+    part = np.empty((m * qh, d + 2), dtype=np.float32)
+    lib().orc_verify_partial(qp, m, qh, kvh, d, kp, vp, kv_begin, kv_end, ctx_len, window, part.ctypes.data)
+    return part
+
+
+def combine(parts, head_dim: int, gate=None) -> np.ndarray:
+    """Merge of partials [splits][rows][head_dim + 2] into [rows][head_dim] f32."""
+    parts = np.ascontiguousarray(parts, dtype=np.float32)
+    splits, rows = parts.shape[0], parts.shape[1]
+    gate, gp = _c(gate, np.float16)
+    out = np.empty((rows, head_dim), dtype=np.float32)
+    lib().orc_combine(parts.ctypes.data, rows, splits, head_dim, gp, out.ctypes.data)
     return out
 
 
