@@ -807,46 +807,62 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
 }
 
 // Log-sum-exp merge of split partials. Thread = (row, dim): 256 / D rows per block. Partial s of row r starts
-// at part + r * row_stride + s * split_stride (floats). Each warp of a row reduces the splits' (max, sum) with
-// its lanes striding over the splits, then every thread sums 2^(m_s - M) acc_s[dim] with 16 splits' loads in
-// flight at a time. With out16 the result is the gate-scaled fp16 output; otherwise the merged partial (acc
-// relative to the common max, max, sum) goes to out32[r][D + 2].
+// at part + r * row_stride + s * split_stride (floats). Every load of the first 64 splits is issued up front, so
+// the merge costs one L2 round trip: each thread its dim of every split's acc, each lane the (max, sum) of
+// splits lane and lane + 32. The row max is a warp reduction; the weight 2^(m_s - M) of split s is computed
+// once, by the lane holding it, and broadcast with shuffles. Splits past 64 are merged 32 at a time. With
+// out16 the result is the gate-scaled fp16 output; otherwise the merged partial (acc relative to the common
+// max, max, sum) goes to out32[r][D + 2].
 template <int D>
 __global__ __launch_bounds__(256) void combine_kernel(const float* part, int rows, int splits, int64_t split_stride,
                                                       int64_t row_stride, const __half* gate, __half* out16,
                                                       float* out32) {
-  constexpr int RPB = 256 / D, CH = 16;
+  constexpr int RPB = 256 / D;
   pdl_wait();
   pdl_trigger();
   const int d = threadIdx.x % D, lane = threadIdx.x & 31;
   const int row = blockIdx.x * RPB + threadIdx.x / D;
   if (row >= rows) return;   // D is a multiple of 32: whole warps leave together
   const float* base = part + (int64_t)row * row_stride;
-  float M = -INFINITY;
-  for (int s = lane; s < splits; s += 32) M = fmaxf(M, base[(int64_t)s * split_stride + D]);
+  const int s_lo = min(splits, 64);
+  float ml0 = -INFINITY, ll0 = 0.f, ml1 = -INFINITY, ll1 = 0.f;
+  if (lane < s_lo) {
+    ml0 = base[(int64_t)lane * split_stride + D];
+    ll0 = base[(int64_t)lane * split_stride + D + 1];
+  }
+  if (lane + 32 < s_lo) {
+    ml1 = base[(int64_t)(lane + 32) * split_stride + D];
+    ll1 = base[(int64_t)(lane + 32) * split_stride + D + 1];
+  }
+  float v[64];
+#pragma unroll
+  for (int u = 0; u < 64; ++u) v[u] = u < s_lo ? base[(int64_t)u * split_stride + d] : 0.f;
+  float M = fmaxf(ml0, ml1);
+  for (int s = 64 + lane; s < splits; s += 32) M = fmaxf(M, base[(int64_t)s * split_stride + D]);
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float L = 0.f;
-  for (int s = lane; s < splits; s += 32) {
-    const float* p = base + (int64_t)s * split_stride;
-    const float ms = p[D];
-    L += ms == -INFINITY ? 0.f : exp2f(ms - M) * p[D + 1];
+  const float w0 = ml0 == -INFINITY ? 0.f : exp2f(ml0 - M), w1 = ml1 == -INFINITY ? 0.f : exp2f(ml1 - M);
+  float L = fmaf(w0, ll0, w1 * ll1);
+  float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+  for (int u = 0; u < 32; ++u) {
+    acc0 = fmaf(__shfl_sync(0xffffffffu, w0, u), v[u], acc0);
+    acc1 = fmaf(__shfl_sync(0xffffffffu, w1, u), v[32 + u], acc1);
+  }
+  float acc = acc0 + acc1;
+  for (int s0 = 64; s0 < splits; s0 += 32) {   // beyond 64 splits (many splits over few kv heads)
+    const int sl = s0 + lane;
+    float w = 0.f;
+    if (sl < splits) {
+      const float ms = base[(int64_t)sl * split_stride + D];
+      w = ms == -INFINITY ? 0.f : exp2f(ms - M);
+      L = fmaf(w, base[(int64_t)sl * split_stride + D + 1], L);
+    }
+    for (int u = 0; u < 32 && s0 + u < splits; ++u)
+      acc = fmaf(__shfl_sync(0xffffffffu, w, u), base[(int64_t)(s0 + u) * split_stride + d], acc);
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  float acc = 0.f;
-  for (int s0 = 0; s0 < splits; s0 += CH) {
-    float ms[CH], v[CH];
-#pragma unroll
-    for (int u = 0; u < CH; ++u) {
-      const int s = s0 + u;
-      const float* p = base + (int64_t)min(s, splits - 1) * split_stride;
-      ms[u] = s < splits ? p[D] : -INFINITY;
-      v[u] = p[d];
-    }
-#pragma unroll
-    for (int u = 0; u < CH; ++u) acc = fmaf(ms[u] == -INFINITY ? 0.f : exp2f(ms[u] - M), v[u], acc);
-  }
   if (out16) {
     const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row);
     out16[(int64_t)row * D + d] = __float2half_rn(acc * scale);
