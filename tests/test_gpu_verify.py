@@ -122,3 +122,35 @@ def test_verify_lifecycle_small(la, orc, synth, cuda):
     v8, sc = orc.quantize_v8(V, V.shape[0])
     assert np.array_equal(got["V8"], v8)
     assert np.array_equal(got["vscale"].view(np.uint32), sc.view(np.uint32))
+
+
+@pytest.mark.parametrize("ctx,splits", [(20000, 0), (1500, 13)])
+def test_verify_dirty_workspace_and_graph_replays(la, orc, synth, cuda, ctx, splits):
+    """Nothing in the workspace needs clearing: a workspace full of junk, consecutive calls on it, and replays of
+    a captured graph all give the exact-attention result, also with one split per tile (1500 tokens, 13 splits)."""
+    import torch
+
+    case, cache, K, V = setup(la, orc, synth, cuda, 90 + splits, ctx, 16)
+    want = orc.attention_f64(case["Q"], ctx, K, V, ctx + 16)
+    q = dev(case["Q"], cuda)
+    sp = splits or la.verify_splits(cache.layout, ctx, 16, 0)
+    ws = torch.full((la.lib().lfm3a_verify_workspace_bytes(16, 32, 64, sp),), 0xAB, dtype=torch.uint8, device=cuda)
+    outs = [torch.empty_like(q) for _ in range(2)]
+    for _ in range(3):
+        cache.verify(q, ctx, out=outs[0], workspace=ws, splits=sp)
+        la.sync()
+        assert rel_err(outs[0].float().cpu().numpy(), want) < TOL
+    stream = torch.cuda.Stream(device=cuda)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for o in outs:
+            cache.verify(q, ctx, out=o, workspace=ws, splits=sp)
+    for _ in range(3):
+        for o in outs:
+            o.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        la.sync()
+        for o in outs:
+            assert rel_err(o.float().cpu().numpy(), want) < TOL
+    del graph
