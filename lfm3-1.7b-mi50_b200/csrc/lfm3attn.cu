@@ -117,10 +117,14 @@ int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count
 
 int launch_combine(const float* part, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
                    const __half* gate, __half* out16, float* out32, cudaStream_t st) {
-  if (head_dim == 64)
-    launch_pdl(combine_kernel<64>, (rows + 3) / 4, 256, 0, st, part, rows, splits, split_stride, row_stride, gate, out16, out32);
-  else
-    launch_pdl(combine_kernel<128>, (rows + 1) / 2, 256, 0, st, part, rows, splits, split_stride, row_stride, gate, out16, out32);
+  // Up to 64 splits the lanes hold two (max, sum) pairs each; more splits (few kv heads) take the wide variant.
+  const bool narrow = splits <= 64;
+  auto go = [&](auto kernel, int rows_per_block) {
+    launch_pdl(kernel, (rows + rows_per_block - 1) / rows_per_block, 256, 0, st, part, rows, splits, split_stride,
+               row_stride, gate, out16, out32);
+  };
+  if (head_dim == 64) narrow ? go(combine_kernel<64, 2>, 4) : go(combine_kernel<64, 12>, 4);
+  else narrow ? go(combine_kernel<128, 2>, 2) : go(combine_kernel<128, 12>, 2);
   return check_launch("combine_kernel");
 }
 

@@ -807,13 +807,14 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
 }
 
 // Log-sum-exp merge of split partials. Thread = (row, dim): 256 / D rows per block. Partial s of row r starts
-// at part + r * row_stride + s * split_stride (floats). Every load of the first 64 splits is issued up front, so
-// the merge costs one L2 round trip: each thread its dim of every split's acc, each lane the (max, sum) of
-// splits lane and lane + 32. The row max is a warp reduction; the weight 2^(m_s - M) of split s is computed
-// once, by the lane holding it, and broadcast with shuffles. Splits past 64 are merged 32 at a time. With
-// out16 the result is the gate-scaled fp16 output; otherwise the merged partial (acc relative to the common
-// max, max, sum) goes to out32[r][D + 2].
-template <int D>
+// at part + r * row_stride + s * split_stride (floats). The loads are issued up front: each lane the (max, sum)
+// of splits lane, lane + 32, ... (up to 32 * KM splits in registers: KM = 2 up to 64 splits, 12 up to 384),
+// each thread its dim of the first 64 splits' acc, so the usual merge (up to 64 splits) costs one L2 round
+// trip and every further 64
+// splits one more. The row max is a warp reduction; the weight 2^(m_s - M) of split s is computed once, by the
+// lane holding it, and broadcast with shuffles. With out16 the result is the gate-scaled fp16 output;
+// otherwise the merged partial (acc relative to the common max, max, sum) goes to out32[r][D + 2].
+template <int D, int KM>
 __global__ __launch_bounds__(256) void combine_kernel(const float* part, int rows, int splits, int64_t split_stride,
                                                       int64_t row_stride, const __half* gate, __half* out16,
                                                       float* out32) {
@@ -824,33 +825,46 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
   const int row = blockIdx.x * RPB + threadIdx.x / D;
   if (row >= rows) return;   // D is a multiple of 32: whole warps leave together
   const float* base = part + (int64_t)row * row_stride;
-  const int s_lo = min(splits, 64);
-  float ml0 = -INFINITY, ll0 = 0.f, ml1 = -INFINITY, ll1 = 0.f;
-  if (lane < s_lo) {
-    ml0 = base[(int64_t)lane * split_stride + D];
-    ll0 = base[(int64_t)lane * split_stride + D + 1];
-  }
-  if (lane + 32 < s_lo) {
-    ml1 = base[(int64_t)(lane + 32) * split_stride + D];
-    ll1 = base[(int64_t)(lane + 32) * split_stride + D + 1];
+  float wk[KM], lk[KM];   // (max, then weight) and sum of split lane + 32 k
+#pragma unroll
+  for (int k = 0; k < KM; ++k) {
+    const int s = lane + 32 * k;
+    wk[k] = s < splits ? base[(int64_t)s * split_stride + D] : -INFINITY;
+    lk[k] = s < splits ? base[(int64_t)s * split_stride + D + 1] : 0.f;
   }
   float v[64];
 #pragma unroll
-  for (int u = 0; u < 64; ++u) v[u] = u < s_lo ? base[(int64_t)u * split_stride + d] : 0.f;
-  float M = fmaxf(ml0, ml1);
-  for (int s = 64 + lane; s < splits; s += 32) M = fmaxf(M, base[(int64_t)s * split_stride + D]);
+  for (int u = 0; u < 64; ++u) v[u] = u < splits ? base[(int64_t)u * split_stride + d] : 0.f;
+  float M = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < KM; ++k) M = fmaxf(M, wk[k]);
+  for (int s = 32 * KM + lane; s < splits; s += 32) M = fmaxf(M, base[(int64_t)s * split_stride + D]);
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  const float w0 = ml0 == -INFINITY ? 0.f : exp2f(ml0 - M), w1 = ml1 == -INFINITY ? 0.f : exp2f(ml1 - M);
-  float L = fmaf(w0, ll0, w1 * ll1);
-  float acc0 = 0.f, acc1 = 0.f;
+  float L = 0.f;
 #pragma unroll
-  for (int u = 0; u < 32; ++u) {
-    acc0 = fmaf(__shfl_sync(0xffffffffu, w0, u), v[u], acc0);
-    acc1 = fmaf(__shfl_sync(0xffffffffu, w1, u), v[32 + u], acc1);
+  for (int k = 0; k < KM; ++k) {
+    wk[k] = wk[k] == -INFINITY ? 0.f : exp2f(wk[k] - M);
+    L = fmaf(wk[k], lk[k], L);
   }
-  float acc = acc0 + acc1;
-  for (int s0 = 64; s0 < splits; s0 += 32) {   // beyond 64 splits (many splits over few kv heads)
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < (KM + 1) / 2; ++c) {   // 64 splits per chunk: weights in wk[2c] (splits 64c + u), wk[2c + 1]
+    if (64 * c >= splits) break;
+    if (c > 0) {
+#pragma unroll
+      for (int u = 0; u < 64; ++u)
+        v[u] = 64 * c + u < splits ? base[(int64_t)(64 * c + u) * split_stride + d] : 0.f;
+    }
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      a0 = fmaf(__shfl_sync(0xffffffffu, wk[2 * c], u), v[u], a0);
+      if (2 * c + 1 < KM) a1 = fmaf(__shfl_sync(0xffffffffu, wk[2 * c + 1], u), v[32 + u], a1);
+    }
+    acc += a0 + a1;
+  }
+  for (int s0 = 32 * KM; s0 < splits; s0 += 32) {   // past 32 * KM splits (not reached by verify)
     const int sl = s0 + lane;
     float w = 0.f;
     if (sl < splits) {
