@@ -494,10 +494,18 @@ def run_ours(args):
             step(caches[i % n_layers])
     torch.cuda.synchronize()
 
+    # Load phase for the clock sampler. The graphs hold NCCL collectives on N > 1, so every rank must replay
+    # them the same number of times: the count comes from the slowest rank's replay time, not from a clock.
+    t0 = time.perf_counter()
+    load_graph.replay()
+    torch.cuda.synchronize()
+    one = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(one, op=pg.ReduceOp.MAX)
+    n_load = max(1, int(args.load_seconds / max(float(one.item()), 1e-4)))
     sampler = ClockSampler(local)
     sampler.start()
-    t_end = time.time() + args.load_seconds
-    while time.time() < t_end:
+    for _ in range(n_load):
         load_graph.replay()
         torch.cuda.synchronize()
     graph.replay()   # one more warm replay of the timed graph itself
