@@ -64,20 +64,27 @@ struct PrefillArgs {
   float qk_scale;    // (1 / sqrt(64)) * log2(e)
 };
 
-constexpr int kPfThreads = 192;
 constexpr int kPfStages = 4;       // per ring (K and V)
 constexpr int kPfQBytes = 16384;   // 128 rows x 64 dims fp16
 
 template <bool I8>
 struct PfLayout {
+  // Warps 0-3 softmax; int8 also 4-7 epilogue; then the producer and the MMA issuer. (Two softmax
+  // warpgroups on the key halves of a tile made the exact kernel slower: it is bound by the exponentials'
+  // throughput, not by latency, and the extra warps only add per-tile overhead.)
+  static constexpr int kProducerWarp = I8 ? 8 : 4;
+  static constexpr int kMmaWarp = I8 ? 9 : 5;
+  static constexpr int kThreads = (kMmaWarp + 1) * 32;
   static constexpr int kKStage = 8192;                 // K of 64 keys: two 32-token pages
   static constexpr int kVStage = I8 ? 4096 : 8192;     // V (or int8 V) of the same keys
   static constexpr int kPBuf = I8 ? 8192 : 16384;      // 128 rows x 64 keys, u8 or fp16
   static constexpr int kOffK = kPfQBytes;
   static constexpr int kOffV = kOffK + kPfStages * kKStage;
   static constexpr int kOffP = kOffV + kPfStages * kVStage;
-  static constexpr int kOffBar = kOffP + 2 * kPBuf;
-  static constexpr int kBars = 4 * kPfStages + 3 * 2 + 2;
+  static constexpr int kOffSc = kOffP + 2 * kPBuf;     // int8: [2][128] (corr, scale) of a tile, softmax -> epilogue
+  static constexpr int kOffL = kOffSc + (I8 ? 2 * 128 * 8 : 0);   // int8: [128] row sums for the epilogue's output
+  static constexpr int kOffBar = kOffL + (I8 ? 128 * 4 : 0);
+  static constexpr int kBars = 4 * kPfStages + 2 + 4 + 2 + 2 + 2;
   static constexpr int kOffTmemSlot = kOffBar + kBars * 8;
   static constexpr int kOffAbort = kOffTmemSlot + 8;   // in the dynamic region: static shared memory would
   static constexpr int kBytes = kOffTmemSlot + 16;      // pad to the 1 KiB alignment and cost the second CTA
@@ -86,7 +93,7 @@ struct PfLayout {
 };
 
 template <bool I8>
-__global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
+__global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(PrefillArgs a) {
   using L = PfLayout<I8>;
   constexpr int NS = kPfStages;
   constexpr uint32_t kTmemCols = 256;
@@ -95,15 +102,18 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   uint8_t* sK = smem + L::kOffK;
   uint8_t* sV = smem + L::kOffV;
   uint8_t* sP = smem + L::kOffP;
+  float2* sSc = reinterpret_cast<float2*>(smem + L::kOffSc);
+  float* sL = reinterpret_cast<float*>(smem + L::kOffL);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* k_full = bars;
   uint64_t* k_empty = bars + NS;
   uint64_t* v_full = bars + 2 * NS;
   uint64_t* v_empty = bars + 3 * NS;
   uint64_t* s_full = bars + 4 * NS;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
-  uint64_t* q_ready = pv_done + 2;
+  uint64_t* p_full = s_full + 2;     // P(b) written: p_full[2 b] (the odd entries are spare)
+  uint64_t* pv_done = p_full + 4;
+  uint64_t* ep_free = pv_done + 2;   // int8: the epilogue of tile j read its s32 columns and sSc[j & 1]
+  uint64_t* q_ready = ep_free + 2;
   uint64_t* drain = q_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffTmemSlot);
   int& s_abort = *reinterpret_cast<int*>(smem + L::kOffAbort);
@@ -127,8 +137,10 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 4);
+      mbar_init(&p_full[2 * b], 4);
+      mbar_init(&p_full[2 * b + 1], 4);
       mbar_init(&pv_done[b], 1);
+      mbar_init(&ep_free[b], 4);
     }
     mbar_init(q_ready, 4);
     mbar_init(drain, 1);
@@ -138,7 +150,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   // previous kernel of the stream has completed (a waiting block holding TMEM could starve it). No early
   // trigger: the next kernel's blocks launch as these exit (waiting blocks beside a running one slowed it).
   pdl_wait();
-  if (warp == 5) {
+  if (warp == L::kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -147,8 +159,8 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {
-    // ================================================================ softmax warps, thread = query row
+  if (!I8 && warp < 4) {
+    // ================================================================ exact softmax, thread = query row
     const int r = threadIdx.x, t = r >> 2, j = r & 3;
     const bool row_ok = t < ntok;
     const int qpos = qfirst + t;
@@ -167,7 +179,138 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
     }
     const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
     float m_run = -INFINITY, l_run = 0.f;
-    float sc_prev = 0.f;   // int8: the row's scale of the previous tile's int32 PV
+    // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
+    bool ok = true;
+    for (int jt = 0; jt < ntiles && ok; ++jt) {
+      const int b = jt & 1, k0 = kt_begin + jt * kQuantBlock;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(jt >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[64];   // raw scores q.k of this row and tile
+      {
+        uint32_t rr[4][16];
+        tmem_ld64(lane_base + b * 64, rr);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[c * 16 + e] = __uint_as_float(rr[c][e]);
+      }
+      // The causal / window / sequence mask, only on tiles that straddle a boundary.
+      const bool interior = ntok == 32 && k0 + kQuantBlock - 1 <= qfirst && (a.window == 0 || k0 > qlast - a.window);
+      if (!interior) {
+        // The row's keys form one interval [lo, hi] of tile offsets (causal end, window and CTA start).
+        const int lo = max(kbegin, a.window > 0 ? qpos - a.window + 1 : 0) - k0;
+        const int hi = row_ok ? qpos - k0 : -1;
+#pragma unroll
+        for (int k = 0; k < 64; ++k) x[k] = (k >= lo && k <= hi) ? x[k] : -INFINITY;
+      }
+      // fl(x * scale) is monotone in x, so the scaled maximum is the maximum of the scaled scores.
+      const float mx = max64(x) * a.qk_scale;
+      const bool grow_max = mx > m_run + kLazy;
+      // O lives in TMEM: rescaling it needs the previous PV finished; rare after the first tiles.
+      if (__any_sync(0xffffffffu, grow_max)) {
+        const float corr = grow_max ? fast_exp2(m_run - mx) : 1.f;
+        if (grow_max) m_run = mx;
+        l_run *= corr;
+        if (jt >= 1) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
+            raise_error(kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t rr[16];
+            tmem_ld16(lane_base + 128 + c * 16, rr);
+            tmem_wait_ld();
+            reg_fence16(rr);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+            tmem_st16(lane_base + 128 + c * 16, rr);
+          }
+          tmem_wait_st();
+        }
+      }
+      // p = 2^(x * scale - m) in one FFMA + EX2 (ex2 of -inf is 0 for masked keys); l in four partial sums.
+      const float neg = m_run == -INFINITY ? 0.f : -m_run;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 64; ++k) {
+        x[k] = fast_exp2(fmaf(x[k], a.qk_scale, neg));
+        ls[k & 3] += x[k];
+      }
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      // P[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
+      uint8_t* pb = sP + b * L::kPBuf;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 v;
+        v.x = pack_half2(x[8 * c], x[8 * c + 1]);
+        v.y = pack_half2(x[8 * c + 2], x[8 * c + 3]);
+        v.z = pack_half2(x[8 * c + 4], x[8 * c + 5]);
+        v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
+        *reinterpret_cast<uint4*>(pb + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[2 * b]);
+    }
+    if (!ok) {
+      atomicExch(&s_abort, 1);
+    } else {
+      const int last = ntiles - 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[last & 1], (uint32_t)(last >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        atomicExch(&s_abort, 1);
+      } else {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {   // 16 columns of O at a time
+          uint32_t rr[16];
+          tmem_ld16(lane_base + 128 + 16 * c, rr);
+          tmem_wait_ld();
+          reg_fence16(rr);
+          if (row_ok) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint4 v;
+              v.x = pack_half2(__uint_as_float(rr[8 * hh]) * inv, __uint_as_float(rr[8 * hh + 1]) * inv);
+              v.y = pack_half2(__uint_as_float(rr[8 * hh + 2]) * inv, __uint_as_float(rr[8 * hh + 3]) * inv);
+              v.z = pack_half2(__uint_as_float(rr[8 * hh + 4]) * inv, __uint_as_float(rr[8 * hh + 5]) * inv);
+              v.w = pack_half2(__uint_as_float(rr[8 * hh + 6]) * inv, __uint_as_float(rr[8 * hh + 7]) * inv);
+              dst[2 * c + hh] = v;
+            }
+          }
+        }
+      }
+    }
+  } else if (I8 && warp < 4) {
+    // ================================================================ int8 softmax warps, thread = query row
+    const int r = threadIdx.x, t = r >> 2, j = r & 3;
+    const bool row_ok = t < ntok;
+    const int qpos = qfirst + t;
+    const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
+    // Q row -> core tiles: row r, dims 8c .. 8c + 7 at ((r / 8) * 8 + c) * 128 + (r % 8) * 16.
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(a.q + grow * 64);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
     // Every wait result is made warp-uniform: the tcgen05.ld/st that follow are warp-collective.
     constexpr float kLog2of255 = 7.99435343685886f;
     bool ok = true;
@@ -211,59 +354,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
       // fl(x * scale) is monotone in x, so the scaled maximum is the maximum of the scaled scores.
       const float mx = max64(x) * a.qk_scale;
       const bool grow_max = mx > m_run + kLazy;
-      if (!I8) {
-        // O lives in TMEM: rescaling it needs the previous PV finished; rare after the first tiles.
-        if (__any_sync(0xffffffffu, grow_max)) {
-          const float corr = grow_max ? fast_exp2(m_run - mx) : 1.f;
-          if (grow_max) m_run = mx;
-          l_run *= corr;
-          if (jt >= 1) {
-            if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
-              raise_error(kErrWaitMma);
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint32_t rr[16];
-              tmem_ld16(lane_base + 128 + c * 16, rr);
-              tmem_wait_ld();
-              reg_fence16(rr);
-#pragma unroll
-              for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
-              tmem_st16(lane_base + 128 + c * 16, rr);
-            }
-            tmem_wait_st();
-          }
-        }
-        // p = 2^(x * scale - m) in one FFMA + EX2 (ex2 of -inf is 0 for masked keys); l in four partial sums.
-        const float neg = m_run == -INFINITY ? 0.f : -m_run;
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 0; k < 64; ++k) {
-          x[k] = fast_exp2(fmaf(x[k], a.qk_scale, neg));
-          ls[k & 3] += x[k];
-        }
-        l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-        // P[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
-        uint8_t* pb = sP + b * L::kPBuf;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 v;
-          v.x = pack_half2(x[8 * c], x[8 * c + 1]);
-          v.y = pack_half2(x[8 * c + 2], x[8 * c + 3]);
-          v.z = pack_half2(x[8 * c + 4], x[8 * c + 5]);
-          v.w = pack_half2(x[8 * c + 6], x[8 * c + 7]);
-          *reinterpret_cast<uint4*>(pb + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[b]);
-        continue;
-      }
-      float corr = 1.f;   // applied to the accumulator and the previous tile's scale in the epilogue below
+      float corr = 1.f;   // the epilogue multiplies the accumulator by it before adding this tile
       if (grow_max) {
         corr = fast_exp2(m_run - mx);
         m_run = mx;
@@ -278,8 +369,8 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
       float es[4] = {0.f, 0.f, 0.f, 0.f};
       uint8_t* pb = sP + b * L::kPBuf;
       // P8[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
-      // The accumulator holds 64 registers, so the scores are read from TMEM a second time, 16 at a time,
-      // and each 16-key core-tile row is stored as soon as it is packed.
+      // The scores are read from TMEM a second time, 16 at a time, and each 16-key core-tile row is stored
+      // as soon as it is packed.
       uint32_t dep = __float_as_uint(off);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -309,95 +400,106 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
       }
       const float pm255 = mx == -INFINITY ? 0.f : fast_exp2(mx - m_run) * (1.f / 255.f);
       l_run = fmaf(pm255, (es[0] + es[1]) + (es[2] + es[3]), l_run);
-      const float sc = pm255 * vs;
-      // Epilogue of the previous tile, before P(jt) is handed over (PV(jt) rewrites the s32 columns):
-      // acc = corr x (acc + sc_prev x Dpv(jt - 1)), acc in fp32 TMEM columns 192..255. |Dpv| <= 64 * 255 * 127
-      // < 2^22, so 0x4B400000 + Dpv is the float 1.5 * 2^23 + Dpv, and one FADD gives Dpv exactly.
-      if (jt >= 1) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
-          raise_error(kErrWaitMma);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float scp = sc_prev * corr;
-        uint32_t dep2 = __float_as_uint(scp);   // keeps each half's loads after the previous half's arithmetic
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t dv[2][16], av[2][16];
-          tmem_ld16_after(lane_base + 128 + 32 * half, dv[0], dep2);
-          tmem_ld16_after(lane_base + 128 + 32 * half + 16, dv[1], dep2);
-          if (jt >= 2) {
-            tmem_ld16_after(lane_base + 192 + 32 * half, av[0], dep2);
-            tmem_ld16_after(lane_base + 192 + 32 * half + 16, av[1], dep2);
-          }
-          tmem_wait_ld();
-          reg_fence16(dv[0]);
-          reg_fence16(dv[1]);
-          if (jt >= 2) {
-            reg_fence16(av[0]);
-            reg_fence16(av[1]);
-          }
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float prev = jt >= 2 ? __uint_as_float(av[c][e]) * corr : 0.f;
-              av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, scp, prev));
-            }
-          tmem_st16(lane_base + 192 + 32 * half, av[0]);
-          tmem_st16(lane_base + 192 + 32 * half + 16, av[1]);
-          dep2 = av[1][15];
-        }
-        tmem_wait_st();
+      // (corr, scale) for the epilogue warpgroup; its slot was last read by the epilogue of tile jt - 2.
+      if (jt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&ep_free[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
+        raise_error(kErrWaitOther);
+        ok = false;
+        break;
       }
-      sc_prev = sc;
+      sSc[b * 128 + r] = make_float2(corr, pm255 * vs);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(&p_full[2 * b]);
     }
-    if (!ok) {
-      atomicExch(&s_abort, 1);
-    } else {
-      const int last = ntiles - 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[last & 1], (uint32_t)(last >> 1) & 1u))) {
+    if (!ok) atomicExch(&s_abort, 1);
+    // The epilogue warpgroup writes the output: hand it the row sums.
+    sL[r] = l_run;
+    named_bar_sync(2, 256);
+  } else if (I8 && warp < 8) {
+    // ================================================================ int8 epilogue warpgroup, thread = row
+    // Tile j: acc = corr_j x acc + scale_j x Dpv(j), acc in fp32 TMEM columns 192..255, Dpv the tile's int32
+    // PV at 128..191. |Dpv| <= 64 * 255 * 127 < 2^22, so 0x4B400000 + Dpv is the float 1.5 * 2^23 + Dpv and
+    // one FADD gives Dpv exactly (no conversion on the MUFU pipe). Then the s32 columns are free for PV(j + 1).
+    const int r = threadIdx.x - 128, t = r >> 2, j = r & 3;
+    const bool row_ok = t < ntok;
+    const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp - 4)) << 16);
+    bool ok = true;
+    for (int jt = 0; jt < ntiles && ok; ++jt) {
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
+        ok = false;
+        break;
+      }
+      const int b = jt & 1;
+      const uint32_t par = (uint32_t)(jt >> 1) & 1u;
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[b], par) && mbar_wait(&p_full[2 * b], par))) {
         raise_error(kErrWaitMma);
-        atomicExch(&s_abort, 1);
-      } else {
-        tc_fence_after();
-        // 16 columns at a time: exact O, or int8 acc + sc x Dpv of the last tile.
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float2 cs = sSc[b * 128 + r];
+      uint32_t dep = __float_as_uint(cs.y);   // keeps each half's loads after the previous half's arithmetic
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t rr[16], av[16];
-          tmem_ld16(lane_base + 128 + 16 * c, rr);
-          if (I8 && last >= 1) tmem_ld16(lane_base + 192 + 16 * c, av);
-          tmem_wait_ld();
-          reg_fence16(rr);
-          if (I8 && last >= 1) reg_fence16(av);
-          float o[16];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t dv[2][16], av[2][16];
+        tmem_ld16_after(lane_base + 128 + 32 * half, dv[0], dep);
+        tmem_ld16_after(lane_base + 128 + 32 * half + 16, dv[1], dep);
+        if (jt >= 1) {
+          tmem_ld16_after(lane_base + 192 + 32 * half, av[0], dep);
+          tmem_ld16_after(lane_base + 192 + 32 * half + 16, av[1], dep);
+        }
+        tmem_wait_ld();
+        reg_fence16(dv[0]);
+        reg_fence16(dv[1]);
+        if (jt >= 1) {
+          reg_fence16(av[0]);
+          reg_fence16(av[1]);
+        }
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            o[e] = I8 ? fmaf(__uint_as_float(rr[e] + 0x4B400000u) - 12582912.f, sc_prev,
-                             last >= 1 ? __uint_as_float(av[e]) : 0.f)
-                      : __uint_as_float(rr[e]);
-          if (row_ok) {
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              uint4 v;
-              v.x = pack_half2(o[8 * hh] * inv, o[8 * hh + 1] * inv);
-              v.y = pack_half2(o[8 * hh + 2] * inv, o[8 * hh + 3] * inv);
-              v.z = pack_half2(o[8 * hh + 4] * inv, o[8 * hh + 5] * inv);
-              v.w = pack_half2(o[8 * hh + 6] * inv, o[8 * hh + 7] * inv);
-              dst[2 * c + hh] = v;
-            }
+          for (int e = 0; e < 16; ++e) {
+            const float prev = jt >= 1 ? __uint_as_float(av[c][e]) * cs.x : 0.f;
+            av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, cs.y, prev));
+          }
+        tmem_st16(lane_base + 192 + 32 * half, av[0]);
+        tmem_st16(lane_base + 192 + 32 * half + 16, av[1]);
+        dep = av[1][15];
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ep_free[b]);
+    }
+    if (!ok) atomicExch(&s_abort, 1);
+    named_bar_sync(2, 256);
+    if (!*reinterpret_cast<volatile int*>(&s_abort)) {
+      tc_fence_after();
+      const float l = sL[r];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rr[16];
+        tmem_ld16(lane_base + 192 + 16 * c, rr);
+        tmem_wait_ld();
+        reg_fence16(rr);
+        if (row_ok) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint4 v;
+            v.x = pack_half2(__uint_as_float(rr[8 * hh]) * inv, __uint_as_float(rr[8 * hh + 1]) * inv);
+            v.y = pack_half2(__uint_as_float(rr[8 * hh + 2]) * inv, __uint_as_float(rr[8 * hh + 3]) * inv);
+            v.z = pack_half2(__uint_as_float(rr[8 * hh + 4]) * inv, __uint_as_float(rr[8 * hh + 5]) * inv);
+            v.w = pack_half2(__uint_as_float(rr[8 * hh + 6]) * inv, __uint_as_float(rr[8 * hh + 7]) * inv);
+            dst[2 * c + hh] = v;
           }
         }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == L::kProducerWarp) {
     // ================================================================ producer
     // The K ring runs ahead of the V ring: K(0 .. NS-1), then V(j), K(j + NS). A K stage frees when its QK
     // completes, a V stage when its PV completes. The whole warp runs the loop; lane 0 issues the copies.
@@ -456,10 +558,11 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
         for (int jt = max(0, v_issued - NS); jt < v_issued; ++jt) mbar_wait(&v_full[jt % NS], (uint32_t)(jt / NS) & 1u);
       }
     }
-  } else {
-    // ================================================================ MMA issuer (warp 5)
+  } else if (warp == L::kMmaWarp) {
+    // ================================================================ MMA issuer
     // QK runs two tiles ahead of PV: after PV(j), S buffer j & 1 is free (the softmax read S(j) before it
-    // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores.
+    // handed over P(j)), so QK(j + 2) goes out at once and the softmax never waits for scores. The int8
+    // PV(j) also waits for the epilogue of tile j - 1 to have read the s32 columns it overwrites.
     // The whole warp runs the loop (its values stay warp-uniform); lane 0 alone issues the tensor-core work.
     {
       bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
@@ -497,7 +600,13 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
           ok = false;
           break;
         }
-        if (!__all_sync(0xffffffffu, mbar_wait(&p_full[bp], (uint32_t)(jt >> 1) & 1u))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_full[2 * bp], (uint32_t)(jt >> 1) & 1u))) {
+          raise_error(kErrWaitOther);
+          ok = false;
+          break;
+        }
+        if (I8 && jt >= 1 &&
+            !__all_sync(0xffffffffu, mbar_wait(&ep_free[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
           raise_error(kErrWaitOther);
           ok = false;
           break;
@@ -542,7 +651,7 @@ __global__ __launch_bounds__(kPfThreads, 2) void prefill_kernel(PrefillArgs a) {
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == L::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -561,7 +670,7 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
         return LFM3A_ECUDA;
       done[1][dev] = true;
     }
-    launch_pdl(prefill_kernel<true>, grid, kPfThreads, PfLayout<true>::kRequest, st, a);
+    launch_pdl(prefill_kernel<true>, grid, PfLayout<true>::kThreads, PfLayout<true>::kRequest, st, a);
   } else {
     if (!done[0][dev]) {
       if (cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -570,7 +679,7 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
         return LFM3A_ECUDA;
       done[0][dev] = true;
     }
-    launch_pdl(prefill_kernel<false>, grid, kPfThreads, PfLayout<false>::kRequest, st, a);
+    launch_pdl(prefill_kernel<false>, grid, PfLayout<false>::kThreads, PfLayout<false>::kRequest, st, a);
   }
   return cudaGetLastError() == cudaSuccess ? LFM3A_OK : LFM3A_ELAUNCH;
 }
