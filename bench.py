@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--load-seconds", type=float, default=2.0, help="untimed replays while the clock sampler runs")
     ap.add_argument("--shard", choices=["heads", "seq"], default="heads", help="multi-GPU plan (N > 1)")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="nccl",
+                    help="heads plan: NCCL all-gather of the outputs, or the combine's scatter over NVLink peer "
+                         "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
+                         "synchronisation, which both pay)")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 fields (N = 1)")
     return ap.parse_args()
 
@@ -444,6 +448,14 @@ def run_ours(args):
     part = torch.empty((M * QH, D + 2), dtype=torch.float32, device=dev)
     gathered = torch.empty((world, M * QH, D + 2), dtype=torch.float32, device=dev)
     gathered_out = torch.empty((world, M, R.qh, D), dtype=torch.float16, device=dev)
+    gg = None
+    if R.plan == "heads" and args.exchange == "p2p":
+        def exchange(handle):
+            handles = [None] * world
+            pg.all_gather_object(handles, handle)
+            return handles
+
+        gg = la.GatherGroup(world, rank, M * R.qh, D, exchange=exchange)
     torch.cuda.synchronize()
 
     def attend(c, dq, timing=None):
@@ -451,6 +463,8 @@ def run_ours(args):
             timing[0].record()
         if R.plan == "seq":
             c.verify_partial(dq, R.kv_begin, R.kv_end, R.ctx_len, out=part, workspace=ws, splits=splits)
+        elif gg is not None:
+            gg.verify(c, dq, R.ctx_len, workspace=ws, splits=splits)
         elif R.plan == "heads":
             c.verify(dq, R.ctx_len, out=out_l, workspace=ws, splits=splits)
         else:
@@ -461,6 +475,8 @@ def run_ours(args):
             pg.all_gather_into_tensor(gathered, part)
             la.combine(gathered, M * QH, world, D, split_stride=M * QH * (D + 2), row_stride=D + 2,
                        out=out.view(M * QH, D))
+        elif gg is not None:
+            gg.wait(gathered_out)
         elif R.plan == "heads":
             pg.all_gather_into_tensor(gathered_out, out_l)
 
@@ -473,7 +489,7 @@ def run_ours(args):
         if R.drafts:
             c.truncate(R.ctx_len)
 
-    launches_per_step = (1 if R.drafts else 0) + (2 if splits > 1 else 1) + (1 if R.plan == "seq" else 0)
+    launches_per_step = (1 if R.drafts else 0) + (2 if splits > 1 else 1) + (1 if R.plan == "seq" or gg else 0)
 
     # Warm-up (eager), then capture the timed graph with per-step kernel events.
     for i in range(max(args.warmup, 3)):
@@ -587,7 +603,9 @@ def run_ours(args):
         pk = peaks()
         achieved = R.bytes_read() / (kern_avg_ms * 1e-3) / 1e9
         traffic = ncu_traffic("verify_m64_kernel_c2.txt") if world == 1 else None
-        plan_text = {"single": "single GPU", "heads": f"kv-head shard x{world}", "seq": f"sequence shard x{world}"}
+        plan_text = {"single": "single GPU",
+                     "heads": f"kv-head shard x{world}" + (", outputs over NVLink peer stores" if gg else ", NCCL all-gather"),
+                     "seq": f"sequence shard x{world}, NCCL all-gather of partials"}
         line = {
             "metric": METRIC,
             "value": round(bytes_step / (ms_step * 1e-3) / 1e9, 2),
@@ -640,6 +658,10 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if pg:
         pg.barrier()
+        if gg is not None:   # every rank unmaps its peers' regions before any region is freed
+            gg.unmap()
+            pg.barrier()
+            gg.free()
         pg.destroy_process_group()
     return 0
 

@@ -177,10 +177,44 @@ size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim);
 int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
                             int exact, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- multi-GPU exchange
+ * No reference counterpart: the reference engine runs one GPU. For kv-head sharding over the GPUs of one
+ * node (one process per GPU), each rank's verify output goes straight into every rank's gather region
+ * through NVLink peer stores from the combine kernel, and a flag per source rank says that its slice
+ * landed, in place of a separate all-gather.
+ *
+ * A gather region holds [2][world][rows][head_dim] fp16 (the gathered outputs of even and odd calls), then
+ * uint32 flags per (source rank, combine block) and a call counter. It must be its own allocation (so that
+ * other processes can map it) and start zeroed: lfm3a_gather_region_alloc gives one. head_dim 64, at most
+ * 1024 rows. */
+size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim);
+int lfm3a_gather_region_alloc(int world, int rows, int head_dim, void** region_out);
+int lfm3a_gather_region_free(void* region);
+
+/* CUDA IPC: a 64-byte handle of this process's region, and the mapping of another process's region from
+ * its handle (valid on the current device; peer access over NVLink). */
+int lfm3a_peer_export(void* region, void* handle_out);
+int lfm3a_peer_open(const void* handle, void** region_out);
+int lfm3a_peer_close(void* region);
+
+/* lfm3a_verify_attention of one rank of the kv-head plan (q_heads = this rank's query heads, rows =
+ * m * q_heads). peers[w]: rank w's region as mapped in this process (peers[rank] = this rank's own).
+ * The combine writes this rank's rows into slice `rank` of the call's half of every region, then raises
+ * this rank's flag in each; lfm3a_gather_wait on the same stream waits (bounded, 2 s, else the device error
+ * word) until every rank's slice of this call has landed in the own region, then copies the gathered
+ * [world][m][q_heads][head_dim] fp16 output to out (device, or NULL to leave it in the region at
+ * region + (n % 2) * world * rows * head_dim halves for call n). Every rank makes the same calls in the
+ * same order; needs splits > 1 (a combine); world <= 8. */
+int lfm3a_verify_attention_gather(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
+                                  const void* gate, void* const* peers, int world, int rank, void* workspace,
+                                  size_t workspace_bytes, int splits, void* stream);
+int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out, void* stream);
+
 /* ---------------------------------------------------------------- test hooks */
-/* The device u8 quantiser of softmax rows (kernels/prefill_attn.hip:305-331): for each row of 64 P'
- * values, q = rne_sat_u8(P' * (255 / max(rowmax, 1e-30))), sc = rowmax * (1/255). p: device f32
- * [rows][64]; q: device u8 [rows][64]; sc: device f32 [rows]. Same device function as the prefill kernel. */
+/* The u8 quantiser of softmax rows in the reference's operation order (kernels/prefill_attn.hip:305-331):
+ * for each row of 64 P' values, q = rne_sat_u8(P' * (255 / max(rowmax, 1e-30))), sc = rowmax * (1/255).
+ * p: device f32 [rows][64]; q: device u8 [rows][64]; sc: device f32 [rows]. The prefill kernel computes the
+ * same quantity from the exponent, rne(2^(s - max s + log2 255)), within the int8-PV tolerance. */
 int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* stream);
 
 #ifdef __cplusplus

@@ -22,6 +22,7 @@ enum DeviceError : int {
   kErrWaitEmpty = 2,   // the producer's wait for a free stage ran out
   kErrWaitMma = 3,     // a wait on a tensor-core commit ran out
   kErrWaitOther = 4,
+  kErrWaitPeer = 5,    // a wait for another GPU's flag ran out
 };
 
 // A bounded wait gives up after this long (ns of %globaltimer).

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <chrono>
 #include <string>
 #include <thread>
@@ -116,30 +117,39 @@ int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count
 }
 
 int launch_combine(const float* part, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
-                   const __half* gate, __half* out16, float* out32, cudaStream_t st) {
+                   const __half* gate, __half* out16, float* out32, cudaStream_t st, const GatherOut* gather = nullptr) {
   // Up to 64 splits the lanes hold two (max, sum) pairs each; more splits (few kv heads) take the wide variant.
   const bool narrow = splits <= 64;
-  auto go = [&](auto kernel, int rows_per_block) {
+  const GatherOut go = gather ? *gather : GatherOut{};
+  auto run = [&](auto kernel, int rows_per_block) {
     launch_pdl(kernel, (rows + rows_per_block - 1) / rows_per_block, 256, 0, st, part, rows, splits, split_stride,
-               row_stride, gate, out16, out32);
+               row_stride, gate, out16, out32, go);
   };
-  if (head_dim == 64) narrow ? go(combine_kernel<64, 2>, 4) : go(combine_kernel<64, 12>, 4);
-  else narrow ? go(combine_kernel<128, 2>, 2) : go(combine_kernel<128, 12>, 2);
+  if (gather) {   // the kv-head plan's scatter to the ranks' gather regions (head_dim 64 only)
+    narrow ? run(combine_kernel<64, 2, true>, 4) : run(combine_kernel<64, 12, true>, 4);
+  } else if (head_dim == 64) {
+    narrow ? run(combine_kernel<64, 2, false>, 4) : run(combine_kernel<64, 12, false>, 4);
+  } else {
+    narrow ? run(combine_kernel<128, 2, false>, 2) : run(combine_kernel<128, 12, false>, 2);
+  }
   return check_launch("combine_kernel");
 }
 
-// Shared body of lfm3a_verify_attention (out16 set) and lfm3a_verify_partial (out32 set).
+// Shared body of lfm3a_verify_attention (out16 set), lfm3a_verify_partial (out32 set) and
+// lfm3a_verify_attention_gather (gather set: the combine scatters the output to the ranks' regions).
 int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int kv_begin, int kv_end, int ctx_len,
                int window, const void* gate, __half* out16, float* out32, void* workspace, size_t workspace_bytes,
-               int splits, cudaStream_t st) {
+               int splits, cudaStream_t st, GatherOut* gather = nullptr) {
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
   const lfm3a_kv_layout& L = kv->layout;
   if (L.mode != LFM3A_MODE_F16 || L.head_dim != 64) return fail(LFM3A_ENOTSUP, "verify attention needs MODE_F16, head_dim 64");
   if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "verify attention needs 4 query heads per kv head");
-  if (!q || (!out16 && !out32) || m < 1 || m > 32 || ctx_len < 0 || window < 0) return fail(LFM3A_EINVAL, "bad verify arguments");
+  if (!q || (!out16 && !out32 && !gather) || m < 1 || m > 32 || ctx_len < 0 || window < 0)
+    return fail(LFM3A_EINVAL, "bad verify arguments");
   if (kv_begin < 0 || kv_end <= kv_begin || kv_end > ctx_len + m) return fail(LFM3A_EINVAL, "bad key range");
-  if (!aligned16(q) || !aligned16(out16 ? (const void*)out16 : (const void*)out32)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
+  if (!aligned16(q) || (!gather && !aligned16(out16 ? (const void*)out16 : (const void*)out32)))
+    return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
   if (window > 0 && window < m) return fail(LFM3A_EINVAL, "window shorter than the verified tokens");
   VerifyArgs a;
   a.g = geom_of(kv);
@@ -187,8 +197,12 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   }
   rc = check_launch("verify_kernel");
   if (rc != LFM3A_OK || a.splits == 1) return rc;
+  if (gather) {
+    if (a.splits == 1) return fail(LFM3A_ENOTSUP, "the gather needs several splits (a combine)");
+    gather->half_stride = (int64_t)gather->world * rows * 64;
+  }
   return launch_combine(a.part, rows, a.splits, 64, kVerifyPart, (int64_t)a.splits * kVerifyPart,
-                        static_cast<const __half*>(gate), out16, out32, st);
+                        static_cast<const __half*>(gate), out16, out32, st, gather);
 }
 
 }  // namespace
@@ -411,6 +425,77 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
   if (!aligned16(q) || !aligned16(out)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
   return launch_prefill(geom_of(kv), static_cast<const __half*>(q), tokens, q_heads, context, window, exact != 0,
                         static_cast<__half*>(out), as_stream(stream));
+}
+
+size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim) {
+  if (world < 1 || world > 8 || rows < 1 || head_dim < 1) return 0;
+  if ((rows + 3) / 4 > kGatherBlocks) return 0;
+  const size_t data = (size_t)2 * world * rows * head_dim * sizeof(__half);
+  return (data + ((size_t)world * kGatherBlocks + 1) * sizeof(unsigned) + 255) / 256 * 256;
+}
+
+int lfm3a_gather_region_alloc(int world, int rows, int head_dim, void** region_out) {
+  const size_t bytes = lfm3a_gather_region_bytes(world, rows, head_dim);
+  if (!bytes || !region_out) return fail(LFM3A_EINVAL, "bad gather region arguments");
+  // Its own allocation: CUDA IPC maps whole allocations.
+  cudaError_t e = cudaMalloc(region_out, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*region_out, 0, bytes);
+  return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, "gather region");
+}
+
+int lfm3a_gather_region_free(void* region) {
+  const cudaError_t e = cudaFree(region);
+  return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, "cudaFree");
+}
+
+int lfm3a_peer_export(void* region, void* handle_out) {
+  if (!region || !handle_out) return fail(LFM3A_EINVAL, "bad export arguments");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, region);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  memcpy(handle_out, &h, sizeof(h));
+  return LFM3A_OK;
+}
+
+int lfm3a_peer_open(const void* handle, void** region_out) {
+  if (!handle || !region_out) return fail(LFM3A_EINVAL, "bad open arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(region_out, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int lfm3a_peer_close(void* region) {
+  const cudaError_t e = cudaIpcCloseMemHandle(region);
+  return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int lfm3a_verify_attention_gather(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
+                                  const void* gate, void* const* peers, int world, int rank, void* workspace,
+                                  size_t workspace_bytes, int splits, void* stream) {
+  if (!peers || world < 1 || world > 8 || rank < 0 || rank >= world) return fail(LFM3A_EINVAL, "bad gather ranks");
+  GatherOut go;
+  go.world = world;
+  go.rank = rank;
+  for (int w = 0; w < world; ++w) {
+    if (!peers[w] || !aligned16(peers[w])) return fail(LFM3A_EINVAL, "gather regions must be 16-byte aligned");
+    go.peers[w] = static_cast<__half*>(peers[w]);
+  }
+  if (splits <= 0 && kv) splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count());
+  return run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, nullptr, nullptr, workspace,
+                    workspace_bytes, splits, as_stream(stream), &go);
+}
+
+int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out, void* stream) {
+  if (!region || world < 1 || world > 8 || rows < 1 || head_dim < 1 || (out && !aligned16(out)))
+    return fail(LFM3A_EINVAL, "bad gather wait arguments");
+  const int64_t half_stride = (int64_t)world * rows * head_dim;
+  const int blocks = (rows + 3) / 4;   // the combine's blocks (4 rows of 64 dims each)
+  if (head_dim != 64 || blocks > kGatherBlocks) return fail(LFM3A_ENOTSUP, "gather: head_dim 64, at most 1024 rows");
+  launch_pdl(gather_wait_kernel, 1, 1024, 0, as_stream(stream), static_cast<__half*>(region), world, half_stride, blocks,
+             static_cast<__half*>(out));
+  return check_launch("gather_wait_kernel");
 }
 
 int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* stream) {

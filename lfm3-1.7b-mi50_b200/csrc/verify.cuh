@@ -814,16 +814,31 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
 // splits one more. The row max is a warp reduction; the weight 2^(m_s - M) of split s is computed once, by the
 // lane holding it, and broadcast with shuffles. With out16 the result is the gate-scaled fp16 output;
 // otherwise the merged partial (acc relative to the common max, max, sum) goes to out32[r][D + 2].
-template <int D, int KM>
+// Where the kv-head plan's combine sends a rank's output: slice `rank` of the current call's half of every
+// rank's gather region (peers[w], mapped here), then a flag per (source rank, combine block) in each region.
+// The region is [2][world][rows][D] fp16, flags [world][kGatherBlocks] u32, then this rank's call counter.
+constexpr int kGatherBlocks = 256;   // combine blocks of one call at most: 1024 rows of 64 dims
+struct GatherOut {
+  __half* peers[8];
+  int world = 0, rank = 0;
+  int64_t half_stride = 0;   // halves in one call's half: world * rows * D
+};
+
+__device__ __forceinline__ unsigned* gather_flags(__half* region, int64_t half_stride) {
+  return reinterpret_cast<unsigned*>(region + 2 * half_stride);
+}
+
+template <int D, int KM, bool GATHER>
 __global__ __launch_bounds__(256) void combine_kernel(const float* part, int rows, int splits, int64_t split_stride,
                                                       int64_t row_stride, const __half* gate, __half* out16,
-                                                      float* out32) {
+                                                      float* out32, GatherOut go) {
   constexpr int RPB = 256 / D;
   pdl_wait();
   pdl_trigger();
   const int d = threadIdx.x % D, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * RPB + threadIdx.x / D;
-  if (row >= rows) return;   // D is a multiple of 32: whole warps leave together
+  const int row_raw = blockIdx.x * RPB + threadIdx.x / D;
+  const bool live = row_raw < rows;   // whole warps: D is a multiple of 32
+  const int row = live ? row_raw : rows - 1;
   const float* base = part + (int64_t)row * row_stride;
   float wk[KM], lk[KM];   // (max, then weight) and sum of split lane + 32 k
 #pragma unroll
@@ -877,6 +892,34 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  if (GATHER) {
+    // The block's rows (contiguous in every region) are staged in shared memory and sent to every rank's
+    // region as 16-byte peer stores; after a block barrier one thread fences at system scope and raises this
+    // block's flag in every region with release stores.
+    __shared__ __align__(16) __half s_out[256];
+    unsigned* my_flags = gather_flags(go.peers[go.rank], go.half_stride);
+    const unsigned calls = *reinterpret_cast<volatile unsigned*>(my_flags + go.world * kGatherBlocks);
+    s_out[threadIdx.x] = __float2half_rn(live ? acc * (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row) : 0.f);
+    __syncthreads();
+    const int r0 = blockIdx.x * RPB, nvec = min(RPB, rows - r0) * D / 8;
+    const int64_t off = (int64_t)(calls & 1u) * go.half_stride + ((int64_t)go.rank * rows + r0) * D;
+    for (int i = threadIdx.x; i < nvec * go.world; i += blockDim.x) {
+      const int w = i / nvec, c = i - w * nvec;
+      reinterpret_cast<uint4*>(go.peers[w] + off)[c] = reinterpret_cast<const uint4*>(s_out)[c];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+#pragma unroll 1
+      for (int w = 0; w < go.world; ++w)
+        asm volatile("st.release.sys.global.u32 [%0], %1;"
+                     ::"l"(gather_flags(go.peers[w], go.half_stride) + go.rank * kGatherBlocks + blockIdx.x),
+                     "r"(calls + 1)
+                     : "memory");
+    }
+    return;
+  }
+  if (!live) return;
   if (out16) {
     const float scale = (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row);
     out16[(int64_t)row * D + d] = __float2half_rn(acc * scale);
@@ -888,6 +931,56 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
       dst[D + 1] = L;
     }
   }
+}
+
+// One block: waits (bounded) until every (rank, combine block) flag of this rank's current call has been
+// raised in the own region (acquire loads at system scope), copies the call's [world][rows][D] half to out (if
+// given), and advances the call counter that the next combine reads.
+__global__ __launch_bounds__(1024) void gather_wait_kernel(__half* region, int world, int64_t half_stride, int blocks,
+                                                           __half* out) {
+  pdl_wait();
+  pdl_trigger();
+  unsigned* flags = gather_flags(region, half_stride);
+  unsigned* counter = flags + world * kGatherBlocks;
+  const unsigned target = *reinterpret_cast<volatile unsigned*>(counter) + 1u;
+  __shared__ int s_fail;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < world * blocks; i += blockDim.x) {
+    const unsigned* f = flags + (i / blocks) * kGatherBlocks + i % blocks;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if ((int)(v - target) >= 0) break;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        raise_error(kErrWaitPeer);
+        s_fail = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_fail && out) {   // eight 16-byte loads in flight per thread, then their stores
+    const uint4* src = reinterpret_cast<const uint4*>(region + (int64_t)((target - 1u) & 1u) * half_stride);
+    uint4* dst = reinterpret_cast<uint4*>(out);
+    const int64_t n = half_stride / 8;
+    for (int64_t i0 = threadIdx.x; i0 < n; i0 += 8 * (int64_t)blockDim.x) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t i = i0 + (int64_t)u * blockDim.x;
+        if (i < n) v[u] = src[i];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t i = i0 + (int64_t)u * blockDim.x;
+        if (i < n) dst[i] = v[u];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(counter) = target;   // even after a give-up: stay in step
 }
 
 }  // namespace lfm3a

@@ -80,6 +80,15 @@ SIGNATURES = {
     "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
     "lfm3a_prefill_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "lfm3a_quantize_p_u8": (_I, [_P, _I, _P, _P, _P]),
+    "lfm3a_gather_region_bytes": (_SZ, [_I, _I, _I]),
+    "lfm3a_gather_region_alloc": (_I, [_I, _I, _I, ctypes.POINTER(_P)]),
+    "lfm3a_gather_region_free": (_I, [_P]),
+    "lfm3a_peer_export": (_I, [_P, _P]),
+    "lfm3a_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "lfm3a_peer_close": (_I, [_P]),
+    "lfm3a_verify_attention_gather": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, ctypes.POINTER(_P), _I, _I,
+                                           _P, _SZ, _I, _P]),
+    "lfm3a_gather_wait": (_I, [_P, _I, _I, _I, _P, _P]),
 }
 
 _lib = None
@@ -338,3 +347,77 @@ class Geometry:
     @property
     def qk_scale(self) -> float:
         return 1.0 / math.sqrt(self.head_dim)
+
+
+class GatherGroup:
+    """This rank's gather region and every rank's region mapped here (the kv-head plan's exchange over
+    NVLink peer stores, in place of an all-gather; include/lfm3attn.h, multi-GPU exchange).
+
+    exchange(handle_bytes) -> list of every rank's handle bytes, in rank order (for example through
+    torch.distributed.all_gather_object). regions, when given, are existing regions used as the ranks' regions
+    directly (all in this process: the one-GPU tests emulate ranks that way)."""
+
+    def __init__(self, world: int, rank: int, rows: int, head_dim: int, exchange=None, regions=None):
+        self.world, self.rank, self.rows, self.head_dim = world, rank, rows, head_dim
+        self.opened = []
+        self.owned = None
+        if regions is not None:
+            self.region = regions[rank]
+            ptrs = list(regions)
+        else:
+            reg = _P()
+            _check(lib().lfm3a_gather_region_alloc(world, rows, head_dim, ctypes.byref(reg)))
+            self.region = self.owned = reg.value
+            handle = (ctypes.c_char * 64)()
+            _check(lib().lfm3a_peer_export(self.region, handle))
+            handles = exchange(bytes(handle))
+            ptrs = []
+            for w in range(world):
+                if w == rank:
+                    ptrs.append(self.region)
+                    continue
+                buf = ctypes.create_string_buffer(bytes(handles[w]), 64)
+                p = _P()
+                _check(lib().lfm3a_peer_open(buf, ctypes.byref(p)))
+                self.opened.append(p.value)
+                ptrs.append(p.value)
+        self.peers = (_P * world)(*ptrs)
+
+    @staticmethod
+    def alloc_region(world: int, rows: int, head_dim: int) -> int:
+        reg = _P()
+        _check(lib().lfm3a_gather_region_alloc(world, rows, head_dim, ctypes.byref(reg)))
+        return reg.value
+
+    def verify(self, cache: "LayerCache", q, ctx_len: int, window: int = 0, gate=None, workspace=None, splits: int = 0,
+               stream=None) -> None:
+        """This rank's verify attention, its output scattered to every rank's region (q: this rank's heads)."""
+        import torch
+
+        m, qh, d = q.shape
+        if splits <= 0:
+            splits = verify_splits(cache.layout, ctx_len, m, window)
+        if workspace is None:
+            workspace = torch.empty(lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8,
+                                    device=q.device)
+        ws_bytes = workspace.numel() * workspace.element_size()
+        _check(lib().lfm3a_verify_attention_gather(ctypes.byref(cache.view), _ptr(q), m, qh, ctx_len, window,
+                                                   _ptr(gate), self.peers, self.world, self.rank, _ptr(workspace),
+                                                   ws_bytes, splits, _stream(stream)))
+
+    def wait(self, out=None, stream=None) -> None:
+        """Waits for every rank's slice of the latest call; copies [world][rows][head_dim] fp16 to out."""
+        _check(lib().lfm3a_gather_wait(self.region, self.world, self.rows, self.head_dim, _ptr(out), _stream(stream)))
+
+    def unmap(self) -> None:
+        """Unmaps the other ranks' regions (after every rank's last call has finished)."""
+        for p in self.opened:
+            lib().lfm3a_peer_close(p)
+        self.opened = []
+
+    def free(self) -> None:
+        """Frees this rank's region: only once every other rank has unmapped it."""
+        if self.owned is not None:
+            lib().lfm3a_gather_region_free(self.owned)
+            self.owned = None
+

@@ -1,0 +1,59 @@
+"""The kv-head plan's exchange on one GPU: two ranks emulated in one process (their gather regions both local),
+each verifying its 4 kv heads and scattering its output into both regions. Per call the ranks' combines run
+before either waits (one stream), so no kernel waits on another that has not run. Three calls in a row
+alternate the regions' halves; every gathered output must match the oracle's verify of all 8 heads
+(4e-3 of the RMS beyond half an fp16 ulp)."""
+import numpy as np
+import pytest
+
+from shard import head_range, query_head_range
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, cuda):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def rel_err(got, want):
+    want = want.astype(np.float64)
+    rms = float(np.sqrt(np.mean(want ** 2)))
+    half_ulp = 0.5 * np.abs(np.spacing(want.astype(np.float16))).astype(np.float64)
+    return float(np.max(np.clip(np.abs(got.astype(np.float64) - want) - half_ulp, 0.0, None))) / rms
+
+
+def test_heads_gather_two_emulated_ranks(la, orc, synth, cuda):
+    import torch
+
+    ctx, m, world = 6000, 16, 2
+    c = synth.verify_case(61, ctx, m)
+    K = np.concatenate([c["K"], c["newK"]])
+    V = np.concatenate([c["V"], c["newV"]])
+    rows = m * 16
+    regions = [la.GatherGroup.alloc_region(world, rows, 64) for _ in range(world)]
+    try:
+        groups = [la.GatherGroup(world, r, rows, 64, regions=regions) for r in range(world)]
+        caches = []
+        for r in range(world):
+            h0, h1 = head_range(world, r, 8)
+            cache = la.LayerCache(la.MODE_F16, h1 - h0, 64, ctx + m + 64, device=cuda)
+            cache.append(dev(K[:, h0:h1], cuda), dev(V[:, h0:h1], cuda), 0)
+            caches.append(cache)
+        s = synth.Stream(62)
+        for call in range(3):
+            Q = c["Q"] if call == 0 else s.normal_f16((m, 32, 64))
+            for r in range(world):
+                q0, q1 = query_head_range(world, r, 8, 32)
+                groups[r].verify(caches[r], dev(Q[:, q0:q1], cuda), ctx)
+            want = orc.verify(Q, K, V, ctx)
+            for r in range(world):
+                out = torch.zeros((world, m, 16, 64), dtype=torch.float16, device=cuda)
+                groups[r].wait(out)
+                la.sync()
+                got = out.permute(1, 0, 2, 3).reshape(m, 32, 64).float().cpu().numpy()
+                assert rel_err(got, want) < 4e-3, (call, r)
+    finally:
+        for reg in regions:
+            la.lib().lfm3a_gather_region_free(reg)
