@@ -53,7 +53,28 @@ def parse():
                          "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
                          "synchronisation, which both pay)")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 fields (N = 1)")
+    ap.add_argument("--only", choices=["c3", "c4", "c5"],
+                    help="run only that configuration's measurement on one GPU and print its fields (for profiling)")
     return ap.parse_args()
+
+
+def run_only(args) -> int:
+    import torch
+
+    import lfm3attn as la
+    import synth
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    if args.only == "c3":
+        res = measure_c3(la, synth, dev, pk["hbm_gbs"])
+    elif args.only == "c4":
+        res = measure_c4(la, synth, dev, pk)
+    else:
+        res = measure_c5(la, dev)
+    print(json.dumps({args.only: res}), flush=True)
+    return 0
 
 
 def kv_bytes(tokens: int) -> int:
@@ -670,6 +691,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.only:
+        return run_only(args)
     return run_ours(args)
 
 
