@@ -440,6 +440,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       }
       tc_fence_after();
       const float2 cs = sSc[b * 128 + r];
+      const bool unit = __all_sync(0xffffffffu, cs.x == 1.f);
       uint32_t dep = __float_as_uint(cs.y);   // keeps each half's loads after the previous half's arithmetic
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -457,13 +458,23 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
           reg_fence16(av[0]);
           reg_fence16(av[1]);
         }
+        if (unit) {   // the running max did not move for any row of the warp (the usual case)
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float prev = jt >= 1 ? __uint_as_float(av[c][e]) * cs.x : 0.f;
-            av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, cs.y, prev));
-          }
+            for (int e = 0; e < 16; ++e) {
+              const float prev = jt >= 1 ? __uint_as_float(av[c][e]) : 0.f;
+              av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, cs.y, prev));
+            }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float prev = jt >= 1 ? __uint_as_float(av[c][e]) * cs.x : 0.f;
+              av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, cs.y, prev));
+            }
+        }
         tmem_st16(lane_base + 192 + 32 * half, av[0]);
         tmem_st16(lane_base + 192 + 32 * half + 16, av[1]);
         dep = av[1][15];
