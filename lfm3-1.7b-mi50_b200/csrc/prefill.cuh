@@ -158,6 +158,18 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (I8) {
+    // The int8 PV accumulates onto 0x4B400000 in its s32 columns (see the epilogue warpgroup).
+    if (warp >= 4 && warp < 8) {
+      const uint32_t lb = tmem + ((uint32_t)(32 * (warp - 4)) << 16);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_st16_fill(lb + 128 + 16 * c, 0x4B400000u);
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
 
   if (!I8 && warp < 4) {
     // ================================================================ exact softmax, thread = query row
@@ -236,14 +248,19 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
         }
       }
       // p = 2^(x * scale - m) in one FFMA + EX2 (ex2 of -inf is 0 for masked keys); l in four partial sums.
+      // Pairs of keys in packed fp32 (ls01 and ls23 sum keys 4i, 4i + 1 and 4i + 2, 4i + 3).
       const float neg = m_run == -INFINITY ? 0.f : -m_run;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      const float2 sc2 = make_float2(a.qk_scale, a.qk_scale), neg2 = make_float2(neg, neg);
+      float2 ls01 = make_float2(0.f, 0.f), ls23 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int k = 0; k < 64; ++k) {
-        x[k] = fast_exp2(fmaf(x[k], a.qk_scale, neg));
-        ls[k & 3] += x[k];
+      for (int k = 0; k < 64; k += 2) {
+        const float2 g = ffma2(make_float2(x[k], x[k + 1]), sc2, neg2);
+        x[k] = fast_exp2(g.x);
+        x[k + 1] = fast_exp2(g.y);
+        if (k & 2) ls23 = fadd2(ls23, make_float2(x[k], x[k + 1]));
+        else ls01 = fadd2(ls01, make_float2(x[k], x[k + 1]));
       }
-      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      l_run += (ls01.x + ls01.y) + (ls23.x + ls23.y);
       // P[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
       uint8_t* pb = sP + b * L::kPBuf;
 #pragma unroll
@@ -366,7 +383,9 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       const char* sec = a.g.pool + phys_block(a.g, k0 / kBlockTokens) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
       const float vs = *reinterpret_cast<const float*>(sec + F16Section<64>::kOffScale);
       const float off = mx == -INFINITY ? 0.f : kLog2of255 - mx;
-      float es[4] = {0.f, 0.f, 0.f, 0.f};
+      const float2 sc2 = make_float2(a.qk_scale, a.qk_scale), off2 = make_float2(off, off);
+      const float2 mag2 = make_float2(12582912.f, 12582912.f);
+      float2 es01 = make_float2(0.f, 0.f), es23 = make_float2(0.f, 0.f);   // keys 4i, 4i + 1 and 4i + 2, 4i + 3
       uint8_t* pb = sP + b * L::kPBuf;
       // P8[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
       // The scores are read from TMEM a second time, 16 at a time, and each 16-key core-tile row is stored
@@ -386,20 +405,21 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
         uint32_t q8[4];
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-          uint32_t u[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float e = fast_exp2(fmaf(xs[4 * w + i], a.qk_scale, off));
-            es[i] += e;
-            u[i] = __float_as_uint(__fadd_rn(e, 12582912.f));   // low byte = rne(e), e <= 255
-          }
-          q8[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
+          const float2 g01 = ffma2(make_float2(xs[4 * w], xs[4 * w + 1]), sc2, off2);
+          const float2 g23 = ffma2(make_float2(xs[4 * w + 2], xs[4 * w + 3]), sc2, off2);
+          const float2 e01 = make_float2(fast_exp2(g01.x), fast_exp2(g01.y));
+          const float2 e23 = make_float2(fast_exp2(g23.x), fast_exp2(g23.y));
+          es01 = fadd2(es01, e01);
+          es23 = fadd2(es23, e23);
+          const float2 u01 = fadd2(e01, mag2), u23 = fadd2(e23, mag2);   // low byte = rne(e), e <= 255
+          q8[w] = __byte_perm(__byte_perm(__float_as_uint(u01.x), __float_as_uint(u01.y), 0x0040),
+                              __byte_perm(__float_as_uint(u23.x), __float_as_uint(u23.y), 0x0040), 0x5410);
         }
         *reinterpret_cast<uint4*>(pb + ((r >> 3) * 4 + c) * 128 + (r & 7) * 16) = make_uint4(q8[0], q8[1], q8[2], q8[3]);
         dep = q8[3];
       }
       const float pm255 = mx == -INFINITY ? 0.f : fast_exp2(mx - m_run) * (1.f / 255.f);
-      l_run = fmaf(pm255, (es[0] + es[1]) + (es[2] + es[3]), l_run);
+      l_run = fmaf(pm255, (es01.x + es01.y) + (es23.x + es23.y), l_run);
       // (corr, scale) for the epilogue warpgroup; its slot was last read by the epilogue of tile jt - 2.
       if (jt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&ep_free[b], (uint32_t)((jt - 2) >> 1) & 1u))) {
         raise_error(kErrWaitOther);
@@ -419,8 +439,10 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
   } else if (I8 && warp < 8) {
     // ================================================================ int8 epilogue warpgroup, thread = row
     // Tile j: acc = corr_j x acc + scale_j x Dpv(j), acc in fp32 TMEM columns 192..255, Dpv the tile's int32
-    // PV at 128..191. |Dpv| <= 64 * 255 * 127 < 2^22, so 0x4B400000 + Dpv is the float 1.5 * 2^23 + Dpv and
-    // one FADD gives Dpv exactly (no conversion on the MUFU pipe). Then the s32 columns are free for PV(j + 1).
+    // PV at 128..191. Those s32 columns hold 0x4B400000 before every PV (set in the prologue, and here again
+    // after each read), and the MMA accumulates onto it: |Dpv| <= 64 * 255 * 127 < 2^22, so the column reads
+    // back as the float 1.5 * 2^23 + Dpv and one FADD gives Dpv exactly (no conversion on the MUFU pipe, no
+    // integer add). Then the s32 columns are free for PV(j + 1). Column pairs go through packed fp32.
     const int r = threadIdx.x - 128, t = r >> 2, j = r & 3;
     const bool row_ok = t < ntok;
     const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
@@ -441,43 +463,41 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       tc_fence_after();
       const float2 cs = sSc[b * 128 + r];
       const bool unit = __all_sync(0xffffffffu, cs.x == 1.f);
-      uint32_t dep = __float_as_uint(cs.y);   // keeps each half's loads after the previous half's arithmetic
+      uint32_t dep = __float_as_uint(cs.y);   // keeps each quarter's loads after the previous one's arithmetic
+      const float2 sc2 = make_float2(cs.y, cs.y), nmag2 = make_float2(-12582912.f, -12582912.f);
+      const float2 corr2 = make_float2(cs.x, cs.x);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t dv[2][16], av[2][16];
-        tmem_ld16_after(lane_base + 128 + 32 * half, dv[0], dep);
-        tmem_ld16_after(lane_base + 128 + 32 * half + 16, dv[1], dep);
-        if (jt >= 1) {
-          tmem_ld16_after(lane_base + 192 + 32 * half, av[0], dep);
-          tmem_ld16_after(lane_base + 192 + 32 * half + 16, av[1], dep);
-        }
+      for (int qc = 0; qc < 4; ++qc) {
+        uint32_t dv[16], av[16];
+        tmem_ld16_after(lane_base + 128 + 16 * qc, dv, dep);
+        if (jt >= 1) tmem_ld16_after(lane_base + 192 + 16 * qc, av, dep);
         tmem_wait_ld();
-        reg_fence16(dv[0]);
-        reg_fence16(dv[1]);
-        if (jt >= 1) {
-          reg_fence16(av[0]);
-          reg_fence16(av[1]);
-        }
+        reg_fence16(dv);
+        if (jt >= 1) reg_fence16(av);
+        tmem_st16_fill(lane_base + 128 + 16 * qc, 0x4B400000u);
         if (unit) {   // the running max did not move for any row of the warp (the usual case)
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float prev = jt >= 1 ? __uint_as_float(av[c][e]) : 0.f;
-              av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, cs.y, prev));
-            }
+          for (int e = 0; e < 16; e += 2) {
+            const float2 d = fadd2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nmag2);
+            const float2 prev = jt >= 1 ? make_float2(__uint_as_float(av[e]), __uint_as_float(av[e + 1]))
+                                        : make_float2(0.f, 0.f);
+            const float2 r2 = ffma2(d, sc2, prev);
+            av[e] = __float_as_uint(r2.x);
+            av[e + 1] = __float_as_uint(r2.y);
+          }
         } else {
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float prev = jt >= 1 ? __uint_as_float(av[c][e]) * cs.x : 0.f;
-              av[c][e] = __float_as_uint(fmaf(__uint_as_float(dv[c][e] + 0x4B400000u) - 12582912.f, cs.y, prev));
-            }
+          for (int e = 0; e < 16; e += 2) {
+            const float2 d = fadd2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nmag2);
+            const float2 prev = jt >= 1 ? fmul2(make_float2(__uint_as_float(av[e]), __uint_as_float(av[e + 1])), corr2)
+                                        : make_float2(0.f, 0.f);
+            const float2 r2 = ffma2(d, sc2, prev);
+            av[e] = __float_as_uint(r2.x);
+            av[e + 1] = __float_as_uint(r2.y);
+          }
         }
-        tmem_st16(lane_base + 192 + 32 * half, av[0]);
-        tmem_st16(lane_base + 192 + 32 * half + 16, av[1]);
-        dep = av[1][15];
+        tmem_st16(lane_base + 192 + 16 * qc, av);
+        dep = av[15];
       }
       tmem_wait_st();
       tc_fence_before();
@@ -638,7 +658,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
           if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)
-              umma_i8_ss(tmem + 128, p_desc + 16 * ks, v_desc + 128 * ks, kIdescI8M128N64, ks > 0 ? 1u : 0u);
+              umma_i8_ss(tmem + 128, p_desc + 16 * ks, v_desc + 128 * ks, kIdescI8M128N64, 1u);   // onto the bias
           }
         }
         if (lane == 0) {
