@@ -466,38 +466,54 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       uint32_t dep = __float_as_uint(cs.y);   // keeps each quarter's loads after the previous one's arithmetic
       const float2 sc2 = make_float2(cs.y, cs.y), nmag2 = make_float2(-12582912.f, -12582912.f);
       const float2 corr2 = make_float2(cs.x, cs.x);
+      if (jt == 0) {   // the first tile starts the accumulator
 #pragma unroll
-      for (int qc = 0; qc < 4; ++qc) {
-        uint32_t dv[16], av[16];
-        tmem_ld16_after(lane_base + 128 + 16 * qc, dv, dep);
-        if (jt >= 1) tmem_ld16_after(lane_base + 192 + 16 * qc, av, dep);
-        tmem_wait_ld();
-        reg_fence16(dv);
-        if (jt >= 1) reg_fence16(av);
-        tmem_st16_fill(lane_base + 128 + 16 * qc, 0x4B400000u);
-        if (unit) {   // the running max did not move for any row of the warp (the usual case)
+        for (int qc = 0; qc < 4; ++qc) {
+          uint32_t dv[16];
+          tmem_ld16_after(lane_base + 128 + 16 * qc, dv, dep);
+          tmem_wait_ld();
+          reg_fence16(dv);
+          tmem_st16_fill(lane_base + 128 + 16 * qc, 0x4B400000u);
 #pragma unroll
           for (int e = 0; e < 16; e += 2) {
-            const float2 d = fadd2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nmag2);
-            const float2 prev = jt >= 1 ? make_float2(__uint_as_float(av[e]), __uint_as_float(av[e + 1]))
-                                        : make_float2(0.f, 0.f);
-            const float2 r2 = ffma2(d, sc2, prev);
-            av[e] = __float_as_uint(r2.x);
-            av[e + 1] = __float_as_uint(r2.y);
+            const float2 r2 = fmul2(fadd2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nmag2), sc2);
+            dv[e] = __float_as_uint(r2.x);
+            dv[e + 1] = __float_as_uint(r2.y);
           }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const float2 d = fadd2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nmag2);
-            const float2 prev = jt >= 1 ? fmul2(make_float2(__uint_as_float(av[e]), __uint_as_float(av[e + 1])), corr2)
-                                        : make_float2(0.f, 0.f);
-            const float2 r2 = ffma2(d, sc2, prev);
-            av[e] = __float_as_uint(r2.x);
-            av[e + 1] = __float_as_uint(r2.y);
-          }
+          tmem_st16(lane_base + 192 + 16 * qc, dv);
+          dep = dv[15];
         }
-        tmem_st16(lane_base + 192 + 16 * qc, av);
-        dep = av[15];
+      } else {
+#pragma unroll
+        for (int qc = 0; qc < 4; ++qc) {
+          uint32_t dv[16], av[16];
+          tmem_ld16_after(lane_base + 128 + 16 * qc, dv, dep);
+          tmem_ld16_after(lane_base + 192 + 16 * qc, av, dep);
+          tmem_wait_ld();
+          reg_fence16(dv);
+          reg_fence16(av);
+          tmem_st16_fill(lane_base + 128 + 16 * qc, 0x4B400000u);
+          if (unit) {   // the running max did not move for any row of the warp (the usual case)
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float2 d = fadd2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nmag2);
+              const float2 r2 = ffma2(d, sc2, make_float2(__uint_as_float(av[e]), __uint_as_float(av[e + 1])));
+              av[e] = __float_as_uint(r2.x);
+              av[e + 1] = __float_as_uint(r2.y);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float2 d = fadd2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nmag2);
+              const float2 prev = fmul2(make_float2(__uint_as_float(av[e]), __uint_as_float(av[e + 1])), corr2);
+              const float2 r2 = ffma2(d, sc2, prev);
+              av[e] = __float_as_uint(r2.x);
+              av[e + 1] = __float_as_uint(r2.y);
+            }
+          }
+          tmem_st16(lane_base + 192 + 16 * qc, av);
+          dep = av[15];
+        }
       }
       tmem_wait_st();
       tc_fence_before();
