@@ -52,8 +52,8 @@ def parse():
                     help="heads plan: NCCL all-gather of the outputs, or the combine's scatter over NVLink peer "
                          "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
                          "synchronisation, which both pay)")
-    ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 fields (N = 1)")
-    ap.add_argument("--only", choices=["c3", "c4", "c5"],
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 and decode fields (N = 1)")
+    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode"],
                     help="run only that configuration's measurement on one GPU and print its fields (for profiling)")
     return ap.parse_args()
 
@@ -71,6 +71,8 @@ def run_only(args) -> int:
         res = measure_c3(la, synth, dev, pk["hbm_gbs"])
     elif args.only == "c4":
         res = measure_c4(la, synth, dev, pk)
+    elif args.only == "decode":
+        res = measure_decodes(la, synth, dev, pk["hbm_gbs"])
     else:
         res = measure_c5(la, dev)
     print(json.dumps({args.only: res}), flush=True)
@@ -327,6 +329,75 @@ def measure_c3(la, synth, dev, peak_gbs: float, steps: int = 60) -> dict:
             "bytes": byts,
             "note": "verify_us: events around each verify inside the round's graph (as the headline roofline); "
                     "back_to_back: a graph of consecutive verify calls timed whole"}
+
+
+def measure_decode(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_caches: int, steps: int = 60) -> dict:
+    """Decode attention (the scope table's first next row): one query token (m = 1) over ctx cached tokens, the
+    same verify call with M = 1: append the token's K/V with RoPE, attend, roll back. Rotating caches keep
+    the K/V reads above L2."""
+    import numpy as np
+    import torch
+
+    case = synth.verify_case(seed, ctx, 1)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    rope = t(la.rope_table(1e6, 1.0, D, ctx + 2).view(np.float16))
+    K0, V0 = t(case["K"]), t(case["V"])
+    caches = []
+    for _ in range(n_caches):
+        c = la.LayerCache(la.MODE_F16, KVH, D, ctx + 64, device=dev)
+        c.append(K0, V0, 0)
+        caches.append(c)
+    del K0, V0
+    q, nk, nv = t(case["Q"]), t(case["newK"]), t(case["newV"])
+    out = torch.empty_like(q)
+    splits = la.verify_splits(caches[0].layout, ctx, 1, 0)
+    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(1, QH, D, splits), dtype=torch.uint8, device=dev)
+
+    def step(c, ev=None):
+        c.append(nk, nv, ctx, rope=rope)
+        if ev:
+            ev[0].record()
+        c.verify(q, ctx, out=out, workspace=ws, splits=splits)
+        if ev:
+            ev[1].record()
+        c.truncate(ctx)
+
+    for i in range(2 * n_caches):
+        step(caches[i % n_caches])
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+           for _ in range(steps)]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(steps):
+            step(caches[i % n_caches], evs[i])
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    step_us = e0.elapsed_time(e1) * 1e3 / steps
+    att_us = statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e3
+    del g
+    b2b_us = back_to_back_us(torch, lambda i: caches[i % n_caches].verify(q, ctx, out=out, workspace=ws, splits=splits),
+                             60)
+    la.sync()
+    byts = kv_bytes(ctx + 1)
+    return {"workload": f"decode: one query token over {ctx} cached tokens (seed {seed}), GQA 32/8, head_dim 64",
+            "us_per_layer": round(step_us, 2), "attention_us": round(att_us, 2), "splits": splits,
+            "hbm_gbs": round(byts / (att_us * 1e-6) / 1e9, 1), "frac": round(byts / (att_us * 1e-6) / 1e9 / peak_gbs, 4),
+            "attention_us_back_to_back": round(b2b_us, 2),
+            "frac_back_to_back": round(byts / (b2b_us * 1e-6) / 1e9 / peak_gbs, 4), "bytes": byts,
+            "caches": n_caches}
+
+
+def measure_decodes(la, synth, dev, peak_gbs: float) -> dict:
+    """Decode (m = 1) at config 2's and config 3's context lengths and seeds."""
+    return {"32k": measure_decode(la, synth, dev, peak_gbs, CTX, SEED, 4),
+            "128k": measure_decode(la, synth, dev, peak_gbs, 131072, 2, 2)}
 
 
 def measure_c4(la, synth, dev, peaks_: dict, reps: int = 5) -> dict:
@@ -649,6 +720,8 @@ def run_ours(args):
         del caches
         torch.cuda.empty_cache()
         extras["c3"] = measure_c3(la, synth, dev, pk["hbm_gbs"])
+        torch.cuda.empty_cache()
+        extras["decode"] = measure_decodes(la, synth, dev, pk["hbm_gbs"])
         torch.cuda.empty_cache()
         extras["c4"] = measure_c4(la, synth, dev, pk)
         torch.cuda.empty_cache()

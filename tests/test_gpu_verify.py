@@ -154,3 +154,13 @@ def test_verify_dirty_workspace_and_graph_replays(la, orc, synth, cuda, ctx, spl
         for o in outs:
             assert rel_err(o.float().cpu().numpy(), want) < TOL
     del graph
+
+
+@pytest.mark.parametrize("ctx_len,seed", [(32768, 1), (131072, 2)])
+def test_decode_full_size(la, orc, synth, cuda, ctx_len, seed):
+    """Decode (m = 1, the scope table's first next row) at the benchmark's context lengths, against fp64."""
+    case, cache, K, V = setup(la, orc, synth, cuda, seed, ctx_len, 1)
+    out = cache.verify(dev(case["Q"], cuda), ctx_len)
+    la.sync()
+    got = out.float().cpu().numpy()
+    assert rel_err(got, orc.attention_f64(case["Q"], ctx_len, K, V, ctx_len + 1)) < TOL
