@@ -394,6 +394,37 @@ def measure_decode(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_cache
             "caches": n_caches}
 
 
+def measure_prefix(la, tokens: int = 131072, reps: int = 5) -> dict:
+    """The prefix cache (host code in the library): register a prompt's blocks, then reuse them from a new
+    sequence, for a 131072-token prompt (4096 blocks, every block chain-hashed each time)."""
+    import numpy as np
+
+    blocks = tokens // 32
+    prompt = np.random.default_rng(5).integers(0, 65536, size=tokens + 1).astype(np.int32)
+    reg_s, reuse_s = [], []
+    for _ in range(reps):
+        pc = la.PrefixCache(blocks + 8, 4 * blocks, 8)
+        s = pc.sequence("bench")
+        s.ensure(blocks - 1)
+        _, ep = pc.alloc_conv()
+        t0 = time.perf_counter()
+        s.register(prompt, tokens, ep)
+        reg_s.append(time.perf_counter() - t0)
+        s.release()
+        r = pc.sequence("bench")
+        t0 = time.perf_counter()
+        n, _ = r.reuse(prompt, window=256, align=2)
+        reuse_s.append(time.perf_counter() - t0)
+        assert n == tokens
+        r.close()
+        s.close()
+        pc.close()
+    reg, reuse = statistics.median(reg_s), statistics.median(reuse_s)
+    return {"workload": f"prefix cache: register then reuse a {tokens}-token prompt ({blocks} blocks), host",
+            "register_us": round(reg * 1e6, 1), "reuse_us": round(reuse * 1e6, 1),
+            "reuse_ns_per_block": round(reuse * 1e9 / blocks, 1), "cores": 1}
+
+
 def measure_decodes(la, synth, dev, peak_gbs: float) -> dict:
     """Decode (m = 1) at config 2's and config 3's context lengths and seeds."""
     return {"32k": measure_decode(la, synth, dev, peak_gbs, CTX, SEED, 4),
@@ -722,6 +753,7 @@ def run_ours(args):
         extras["c3"] = measure_c3(la, synth, dev, pk["hbm_gbs"])
         torch.cuda.empty_cache()
         extras["decode"] = measure_decodes(la, synth, dev, pk["hbm_gbs"])
+        extras["prefix"] = measure_prefix(la)
         torch.cuda.empty_cache()
         extras["c4"] = measure_c4(la, synth, dev, pk)
         torch.cuda.empty_cache()

@@ -32,7 +32,8 @@ enum {
   LFM3A_ECUDA = -4,       /* a CUDA runtime call failed; lfm3a_last_error() has the detail */
   LFM3A_ENOTSUP = -5,     /* geometry or cache mode this entry point does not implement */
   LFM3A_EWORKSPACE = -6,  /* the workspace is smaller than the *_workspace_bytes figure */
-  LFM3A_EDEVICE = -7      /* a kernel gave up a bounded wait and raised the device error word */
+  LFM3A_EDEVICE = -7,     /* a kernel gave up a bounded wait and raised the device error word */
+  LFM3A_ENOSPACE = -8     /* the prefix cache has no free or evictable full block (generate.go:286-287) */
 };
 
 /* Cache modes. */
@@ -209,6 +210,57 @@ int lfm3a_verify_attention_gather(const lfm3a_kv_view* kv, const void* q, int m,
                                   const void* gate, void* const* peers, int world, int rank, void* workspace,
                                   size_t workspace_bytes, int splits, void* stream);
 int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out, void* stream);
+
+/* ---------------------------------------------------------------- prefix cache (host only)
+ * The paged pool's block manager: internal/model/cache.go (prefixCache) and the per-sequence bookkeeping
+ * of internal/model/generate.go:222-385 (reuse, ensureBlock, registerAt, release). Host memory only; the
+ * returned physical block numbers go into the block table of each layer's lfm3a_kv_view, so sequences
+ * with a common prefix share pages. One thread at a time per cache (the reference serialises Generate,
+ * generate.go:63). */
+typedef struct lfm3a_pcache lfm3a_pcache;
+typedef struct lfm3a_pseq lfm3a_pseq;
+
+/* newPrefixCache (cache.go:39-46): full_blocks pool blocks, a ring of slide_blocks sliding-window blocks
+ * and conv_slots conv-state slots (slot 0 is the running state). */
+int lfm3a_pcache_create(int full_blocks, int slide_blocks, int conv_slots, lfm3a_pcache** out);
+void lfm3a_pcache_destroy(lfm3a_pcache* pc);
+/* reset (cache.go:127-136): forget every cached prefix; blocks live sequences reference stay theirs. */
+void lfm3a_pcache_reset(lfm3a_pcache* pc);
+int lfm3a_pcache_free_blocks(const lfm3a_pcache* pc);
+int lfm3a_pcache_cached_blocks(const lfm3a_pcache* pc);
+/* allocSlide / slideValid (cache.go:103-112) and allocConv / convValid / convSlotOf (cache.go:114-125). */
+int lfm3a_pcache_alloc_slide(lfm3a_pcache* pc, int64_t* epoch);
+int lfm3a_pcache_slide_valid(const lfm3a_pcache* pc, int64_t epoch);
+int lfm3a_pcache_alloc_conv(lfm3a_pcache* pc, int64_t* epoch);
+int lfm3a_pcache_conv_valid(const lfm3a_pcache* pc, int64_t epoch);
+int lfm3a_pcache_conv_slot(const lfm3a_pcache* pc, int64_t epoch);
+
+/* saltSeed (cache.go:138-143) and chainHash over one 32-token block (cache.go:145-154). */
+uint64_t lfm3a_prefix_salt(const char* salt);
+uint64_t lfm3a_prefix_chain(uint64_t prev, const int32_t* tokens32);
+
+/* A sequence whose chain starts at saltSeed(salt) (generate.go:77). */
+int lfm3a_pseq_create(lfm3a_pcache* pc, const char* salt, lfm3a_pseq** out);
+/* Releases the sequence's blocks (if lfm3a_pseq_release was not called) and frees it. */
+void lfm3a_pseq_destroy(lfm3a_pcache* pc, lfm3a_pseq* seq);
+/* reuse (generate.go:222-279): maps the longest usable cached prefix of prompt[n] into an empty sequence;
+ * *reused = tokens reused (a multiple of 32 * align, < n), *conv_slot = the checkpoint slot to restore
+ * (0: none). window: attention window of the sliding layers in tokens (engine.go:33 Window = 256).
+ * align: blocks reused come in multiples of it: 2 for MODE_F16 pools (the int8 V copy is quantised per
+ * 64-token block, two pages, which a shared prefix must hold whole), 1 for MODE_I8REC (as the reference). */
+int lfm3a_pseq_reuse(lfm3a_pcache* pc, lfm3a_pseq* seq, const int32_t* prompt, int n, int window, int align,
+                     int* reused, int32_t* conv_slot);
+/* ensureBlock (generate.go:281-295): physical blocks for logical blocks 0..logical; LFM3A_ENOSPACE when
+ * every full block is referenced. */
+int lfm3a_pseq_ensure(lfm3a_pcache* pc, lfm3a_pseq* seq, int logical);
+/* registerAt (generate.go:346-373): hands the complete blocks of tokens[0..upto) to the cache; the last of
+ * them owns conv checkpoint conv_epoch (-1: none). Blocks must have been ensured. */
+int lfm3a_pseq_register(lfm3a_pcache* pc, lfm3a_pseq* seq, const int32_t* tokens, int upto, int64_t conv_epoch);
+/* release (generate.go:376-385). */
+int lfm3a_pseq_release(lfm3a_pcache* pc, lfm3a_pseq* seq);
+/* The sequence's logical -> physical full blocks and sliding-ring blocks (either may be NULL); returns the
+ * number of blocks (copies at most cap of each). */
+int lfm3a_pseq_blocks(const lfm3a_pseq* seq, int32_t* full, int32_t* slide, int cap);
 
 /* ---------------------------------------------------------------- test hooks */
 /* The u8 quantiser of softmax rows in the reference's operation order (kernels/prefill_attn.hip:305-331):

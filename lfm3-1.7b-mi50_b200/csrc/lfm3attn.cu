@@ -11,6 +11,7 @@
 #include "../../include/lfm3attn.h"
 #include "common.cuh"
 #include "kv.cuh"
+#include "pcache.h"
 #include "prefill.cuh"
 #include "verify.cuh"
 
@@ -221,6 +222,7 @@ const char* lfm3a_strerror(int code) {
     case LFM3A_ENOTSUP: return "not supported";
     case LFM3A_EWORKSPACE: return "workspace too small";
     case LFM3A_EDEVICE: return "a kernel gave up a bounded wait";
+    case LFM3A_ENOSPACE: return "KV pool exhausted";
     default: return "unknown error";
   }
 }
@@ -503,6 +505,114 @@ int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* s
   if (rows == 0) return LFM3A_OK;
   launch_pdl(quantize_p_rows_kernel, (rows + 127) / 128, 128, 0, as_stream(stream), p, rows, q, sc);
   return check_launch("quantize_p_rows_kernel");
+}
+
+// ---------------------------------------------------------------- prefix cache (host only)
+struct lfm3a_pcache {
+  lfm3a::PrefixPool pool;
+  lfm3a_pcache(int f, int s, int c) : pool(f, s, c) {}
+};
+struct lfm3a_pseq {
+  lfm3a::PrefixSeq seq;
+};
+
+int lfm3a_pcache_create(int full_blocks, int slide_blocks, int conv_slots, lfm3a_pcache** out) {
+  if (!out || full_blocks < 0 || slide_blocks <= lfm3a::PrefixPool::kSlideReuseMargin || conv_slots < 2)
+    return fail(LFM3A_EINVAL, "prefix cache needs full_blocks >= 0, slide_blocks > 128, conv_slots >= 2");
+  try {
+    *out = new lfm3a_pcache(full_blocks, slide_blocks, conv_slots);
+  } catch (...) {
+    return fail(LFM3A_ENOSPACE, "host allocation failed");
+  }
+  return LFM3A_OK;
+}
+void lfm3a_pcache_destroy(lfm3a_pcache* pc) { delete pc; }
+void lfm3a_pcache_reset(lfm3a_pcache* pc) {
+  if (pc) pc->pool.reset();
+}
+int lfm3a_pcache_free_blocks(const lfm3a_pcache* pc) { return pc ? pc->pool.free_blocks() : LFM3A_EINVAL; }
+int lfm3a_pcache_cached_blocks(const lfm3a_pcache* pc) { return pc ? pc->pool.cached_entries() : LFM3A_EINVAL; }
+int lfm3a_pcache_alloc_slide(lfm3a_pcache* pc, int64_t* epoch) {
+  if (!pc || !epoch) return fail(LFM3A_EINVAL, "null argument");
+  return pc->pool.alloc_slide(epoch);
+}
+int lfm3a_pcache_slide_valid(const lfm3a_pcache* pc, int64_t epoch) { return pc && pc->pool.slide_valid(epoch); }
+int lfm3a_pcache_alloc_conv(lfm3a_pcache* pc, int64_t* epoch) {
+  if (!pc || !epoch) return fail(LFM3A_EINVAL, "null argument");
+  return pc->pool.alloc_conv(epoch);
+}
+int lfm3a_pcache_conv_valid(const lfm3a_pcache* pc, int64_t epoch) { return pc && pc->pool.conv_valid(epoch); }
+int lfm3a_pcache_conv_slot(const lfm3a_pcache* pc, int64_t epoch) {
+  if (!pc || epoch < 0) return fail(LFM3A_EINVAL, "bad epoch");
+  return pc->pool.conv_slot_of(epoch);
+}
+uint64_t lfm3a_prefix_salt(const char* salt) { return lfm3a::prefix_salt_seed(salt); }
+uint64_t lfm3a_prefix_chain(uint64_t prev, const int32_t* tokens32) {
+  return tokens32 ? lfm3a::prefix_chain_hash(prev, tokens32) : prev;
+}
+
+int lfm3a_pseq_create(lfm3a_pcache* pc, const char* salt, lfm3a_pseq** out) {
+  if (!pc || !out) return fail(LFM3A_EINVAL, "null argument");
+  try {
+    *out = new lfm3a_pseq;
+  } catch (...) {
+    return fail(LFM3A_ENOSPACE, "host allocation failed");
+  }
+  (*out)->seq.hash = lfm3a::prefix_salt_seed(salt);
+  return LFM3A_OK;
+}
+void lfm3a_pseq_destroy(lfm3a_pcache* pc, lfm3a_pseq* seq) {
+  if (!seq) return;
+  if (pc) lfm3a::prefix_release(pc->pool, seq->seq);
+  delete seq;
+}
+int lfm3a_pseq_reuse(lfm3a_pcache* pc, lfm3a_pseq* seq, const int32_t* prompt, int n, int window, int align,
+                     int* reused, int32_t* conv_slot) {
+  if (!pc || !seq || (!prompt && n > 0) || n < 0 || window < 0 || align < 1 || !reused || !conv_slot)
+    return fail(LFM3A_EINVAL, "bad reuse arguments");
+  if (!seq->seq.full.empty() || seq->seq.released) return fail(LFM3A_EINVAL, "reuse needs a fresh sequence");
+  try {
+    *reused = lfm3a::prefix_reuse(pc->pool, seq->seq, prompt, n, window, align, conv_slot);
+  } catch (...) {
+    return fail(LFM3A_ENOSPACE, "host allocation failed");
+  }
+  return LFM3A_OK;
+}
+int lfm3a_pseq_ensure(lfm3a_pcache* pc, lfm3a_pseq* seq, int logical) {
+  if (!pc || !seq || logical < 0 || seq->seq.released) return fail(LFM3A_EINVAL, "bad ensure arguments");
+  bool ok;
+  try {
+    ok = lfm3a::prefix_ensure(pc->pool, seq->seq, logical);
+  } catch (...) {
+    return fail(LFM3A_ENOSPACE, "host allocation failed");
+  }
+  if (!ok) return fail(LFM3A_ENOSPACE, "KV cache exhausted at block " + std::to_string(seq->seq.full.size()));
+  return LFM3A_OK;
+}
+int lfm3a_pseq_register(lfm3a_pcache* pc, lfm3a_pseq* seq, const int32_t* tokens, int upto, int64_t conv_epoch) {
+  if (!pc || !seq || !tokens || upto < 0 || seq->seq.released) return fail(LFM3A_EINVAL, "bad register arguments");
+  bool ok;
+  try {
+    ok = lfm3a::prefix_register(pc->pool, seq->seq, tokens, upto, conv_epoch);
+  } catch (...) {
+    return fail(LFM3A_ENOSPACE, "host allocation failed");
+  }
+  if (!ok) return fail(LFM3A_EINVAL, "register past the ensured blocks");
+  return LFM3A_OK;
+}
+int lfm3a_pseq_release(lfm3a_pcache* pc, lfm3a_pseq* seq) {
+  if (!pc || !seq) return fail(LFM3A_EINVAL, "null argument");
+  lfm3a::prefix_release(pc->pool, seq->seq);
+  return LFM3A_OK;
+}
+int lfm3a_pseq_blocks(const lfm3a_pseq* seq, int32_t* full, int32_t* slide, int cap) {
+  if (!seq || cap < 0) return fail(LFM3A_EINVAL, "bad blocks arguments");
+  const int n = (int)seq->seq.full.size();
+  for (int i = 0; i < n && i < cap; ++i) {
+    if (full) full[i] = seq->seq.full[i];
+    if (slide) slide[i] = seq->seq.slide[i];
+  }
+  return n;
 }
 
 }  // extern "C"

@@ -26,7 +26,7 @@ MODE_I8REC = 1
 BLOCK_TOKENS = 32
 QUANT_BLOCK = 64
 
-OK, EINVAL, ELAUNCH, ETIMEOUT, ECUDA, ENOTSUP, EWORKSPACE, EDEVICE = 0, -1, -2, -3, -4, -5, -6, -7
+OK, EINVAL, ELAUNCH, ETIMEOUT, ECUDA, ENOTSUP, EWORKSPACE, EDEVICE, ENOSPACE = 0, -1, -2, -3, -4, -5, -6, -7, -8
 
 
 class LFM3AError(RuntimeError):
@@ -89,6 +89,25 @@ SIGNATURES = {
     "lfm3a_verify_attention_gather": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, ctypes.POINTER(_P), _I, _I,
                                            _P, _SZ, _I, _P]),
     "lfm3a_gather_wait": (_I, [_P, _I, _I, _I, _P, _P]),
+    "lfm3a_pcache_create": (_I, [_I, _I, _I, ctypes.POINTER(_P)]),
+    "lfm3a_pcache_destroy": (None, [_P]),
+    "lfm3a_pcache_reset": (None, [_P]),
+    "lfm3a_pcache_free_blocks": (_I, [_P]),
+    "lfm3a_pcache_cached_blocks": (_I, [_P]),
+    "lfm3a_pcache_alloc_slide": (_I, [_P, ctypes.POINTER(_I64)]),
+    "lfm3a_pcache_slide_valid": (_I, [_P, _I64]),
+    "lfm3a_pcache_alloc_conv": (_I, [_P, ctypes.POINTER(_I64)]),
+    "lfm3a_pcache_conv_valid": (_I, [_P, _I64]),
+    "lfm3a_pcache_conv_slot": (_I, [_P, _I64]),
+    "lfm3a_prefix_salt": (ctypes.c_uint64, [ctypes.c_char_p]),
+    "lfm3a_prefix_chain": (ctypes.c_uint64, [ctypes.c_uint64, _P]),
+    "lfm3a_pseq_create": (_I, [_P, ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "lfm3a_pseq_destroy": (None, [_P, _P]),
+    "lfm3a_pseq_reuse": (_I, [_P, _P, _P, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_int32)]),
+    "lfm3a_pseq_ensure": (_I, [_P, _P, _I]),
+    "lfm3a_pseq_register": (_I, [_P, _P, _P, _I, _I64]),
+    "lfm3a_pseq_release": (_I, [_P, _P]),
+    "lfm3a_pseq_blocks": (_I, [_P, _P, _P, _I]),
 }
 
 _lib = None
@@ -153,15 +172,23 @@ class LayerCache:
     """One layer's paged pool and block table in device memory (engine.go:474-512, 682-685)."""
 
     def __init__(self, mode: int, kv_heads: int, head_dim: int, capacity_tokens: int, device="cuda",
-                 block_table=None, pool_blocks: int | None = None):
+                 block_table=None, pool_blocks: int | None = None, pool=None):
+        """pool: another LayerCache of the same layout whose pool this one shares (a sequence reusing
+        another's prefix blocks through its own block table, as the reference's sequences share one
+        per-layer pool, engine.go:474-512); else a new zeroed pool of pool_blocks blocks."""
         import torch
 
         self.layout = layout(mode, kv_heads, head_dim)
         self.mode, self.kv_heads, self.head_dim = mode, kv_heads, head_dim
         self.capacity = capacity_tokens
         logical = (capacity_tokens + BLOCK_TOKENS - 1) // BLOCK_TOKENS
-        self.pool_blocks = pool_blocks if pool_blocks is not None else logical
-        self.pool = torch.zeros(self.pool_blocks * self.layout.block_bytes, dtype=torch.uint8, device=device)
+        if pool is not None:
+            if pool.layout.block_bytes != self.layout.block_bytes or pool.mode != mode:
+                raise LFM3AError(EINVAL, "a shared pool needs the same layout")
+            self.pool_blocks, self.pool = pool.pool_blocks, pool.pool
+        else:
+            self.pool_blocks = pool_blocks if pool_blocks is not None else logical
+            self.pool = torch.zeros(self.pool_blocks * self.layout.block_bytes, dtype=torch.uint8, device=device)
         if block_table is None:
             block_table = torch.arange(logical, dtype=torch.int32, device=device)
         self.table = block_table
@@ -244,6 +271,121 @@ class LayerCache:
         pool = self.pool.cpu().numpy()
         table = self.table.cpu().numpy()
         return decode_pool(pool, table, self.layout, length)
+
+
+class PrefixCache:
+    """The paged pool's block manager (internal/model/cache.go prefixCache): host memory, in the library.
+    full_blocks physical blocks per layer pool, a ring of slide_blocks sliding-window blocks, conv_slots
+    conv-state slots (slot 0 running)."""
+
+    def __init__(self, full_blocks: int, slide_blocks: int, conv_slots: int):
+        h = _P()
+        _check(lib().lfm3a_pcache_create(full_blocks, slide_blocks, conv_slots, ctypes.byref(h)))
+        self.handle = h.value
+
+    def close(self) -> None:
+        if self.handle:
+            lib().lfm3a_pcache_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self) -> None:
+        lib().lfm3a_pcache_reset(self.handle)
+
+    @property
+    def free_blocks(self) -> int:
+        return lib().lfm3a_pcache_free_blocks(self.handle)
+
+    @property
+    def cached_blocks(self) -> int:
+        return lib().lfm3a_pcache_cached_blocks(self.handle)
+
+    def alloc_slide(self) -> tuple[int, int]:
+        ep = _I64()
+        slot = lib().lfm3a_pcache_alloc_slide(self.handle, ctypes.byref(ep))
+        return slot, ep.value
+
+    def slide_valid(self, epoch: int) -> bool:
+        return bool(lib().lfm3a_pcache_slide_valid(self.handle, epoch))
+
+    def alloc_conv(self) -> tuple[int, int]:
+        ep = _I64()
+        slot = lib().lfm3a_pcache_alloc_conv(self.handle, ctypes.byref(ep))
+        return slot, ep.value
+
+    def conv_valid(self, epoch: int) -> bool:
+        return bool(lib().lfm3a_pcache_conv_valid(self.handle, epoch))
+
+    def conv_slot(self, epoch: int) -> int:
+        rc = lib().lfm3a_pcache_conv_slot(self.handle, epoch)
+        if rc < 0:
+            _check(rc)
+        return rc
+
+    def sequence(self, salt: str = "") -> "PrefixSeq":
+        return PrefixSeq(self, salt)
+
+
+def prefix_salt(salt: str) -> int:
+    """saltSeed (cache.go:138-143)."""
+    return lib().lfm3a_prefix_salt(salt.encode())
+
+
+def prefix_chain(prev: int, tokens) -> int:
+    """chainHash (cache.go:145-154) of one 32-token block."""
+    t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+    if t.shape != (BLOCK_TOKENS,):
+        raise LFM3AError(EINVAL, "a block has 32 tokens")
+    return lib().lfm3a_prefix_chain(prev, t.ctypes.data)
+
+
+class PrefixSeq:
+    """One sequence's blocks (generate.go:50-61): reuse, ensure, register, release."""
+
+    def __init__(self, cache: PrefixCache, salt: str = ""):
+        h = _P()
+        _check(lib().lfm3a_pseq_create(cache.handle, salt.encode(), ctypes.byref(h)))
+        self.cache, self.handle = cache, h.value
+
+    def close(self) -> None:
+        if self.handle and self.cache.handle:
+            lib().lfm3a_pseq_destroy(self.cache.handle, self.handle)
+        self.handle = None
+
+    def reuse(self, prompt, window: int = 256, align: int = 1) -> tuple[int, int]:
+        """(tokens reused, conv slot to restore). align = 2 for MODE_F16 pools (whole 64-token int8 V blocks)."""
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32))
+        n, slot = ctypes.c_int(), ctypes.c_int32()
+        _check(lib().lfm3a_pseq_reuse(self.cache.handle, self.handle, p.ctypes.data, p.size, window, align,
+                                      ctypes.byref(n), ctypes.byref(slot)))
+        return n.value, slot.value
+
+    def ensure(self, logical: int) -> None:
+        _check(lib().lfm3a_pseq_ensure(self.cache.handle, self.handle, logical))
+
+    def register(self, tokens, upto: int, conv_epoch: int = -1) -> None:
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        if t.size < upto:
+            raise LFM3AError(EINVAL, "register needs upto tokens")
+        _check(lib().lfm3a_pseq_register(self.cache.handle, self.handle, t.ctypes.data, upto, conv_epoch))
+
+    def release(self) -> None:
+        _check(lib().lfm3a_pseq_release(self.cache.handle, self.handle))
+
+    def blocks(self) -> tuple[np.ndarray, np.ndarray]:
+        """(full, slide) logical -> physical block numbers."""
+        n = lib().lfm3a_pseq_blocks(self.handle, None, None, 0)
+        if n < 0:
+            _check(n)
+        full = np.zeros(n, dtype=np.int32)
+        slide = np.zeros(n, dtype=np.int32)
+        lib().lfm3a_pseq_blocks(self.handle, full.ctypes.data, slide.ctypes.data, n)
+        return full, slide
 
 
 def verify_splits(lay: KvLayout, ctx_len: int, m: int, window: int = 0, sm_count: int = 0) -> int:
