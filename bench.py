@@ -53,7 +53,7 @@ def parse():
                          "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
                          "synchronisation, which both pay)")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 and decode fields (N = 1)")
-    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode"],
+    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode", "chunks"],
                     help="run only that configuration's measurement on one GPU and print its fields (for profiling)")
     return ap.parse_args()
 
@@ -73,6 +73,8 @@ def run_only(args) -> int:
         res = measure_c4(la, synth, dev, pk)
     elif args.only == "decode":
         res = measure_decodes(la, synth, dev, pk["hbm_gbs"])
+    elif args.only == "chunks":
+        res = measure_prefill_chunks(la, dev)
     else:
         res = measure_c5(la, dev)
     print(json.dumps({args.only: res}), flush=True)
@@ -425,6 +427,41 @@ def measure_prefix(la, tokens: int = 131072, reps: int = 5) -> dict:
             "reuse_ns_per_block": round(reuse * 1e9 / blocks, 1), "cores": 1}
 
 
+def measure_prefill_chunks(la, dev, ctx: int = 131072, chunks=(64, 512), reps: int = 5) -> dict:
+    """Prefill of a short chunk over a long cached context (a conversation's next turn, a prompt's last
+    partial chunk): key splits (lfm3a_prefill_splits) against the unsplit launch (no workspace), both
+    variants. K/V/Q N(0,1) from torch's seeded generator on the device."""
+    import torch
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6)
+    rnd = lambda *shape: torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).half()
+    top = max(chunks)
+    cache = la.LayerCache(la.MODE_F16, KVH, D, ctx + top + 64, device=dev)
+    cache.append(rnd(ctx + top, KVH, D), rnd(ctx + top, KVH, D), 0)
+    none = torch.empty(0, dtype=torch.uint8, device=dev)
+    out = {}
+    for t in chunks:
+        q = rnd(t, QH, D)
+        o = torch.empty_like(q)
+        ws = torch.empty(max(1, la.lib().lfm3a_prefill_workspace_bytes(t, QH, D)), dtype=torch.uint8, device=dev)
+        row = {"splits": la.lib().lfm3a_prefill_splits(t, QH, ctx, 0, 0)}
+        for exact in (False, True):
+            for name, w in (("split", ws), ("unsplit", none)):
+                for _ in range(2):
+                    cache.prefill(q, ctx, exact=exact, out=o, workspace=w)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    cache.prefill(q, ctx, exact=exact, out=o, workspace=w)
+                e1.record()
+                torch.cuda.synchronize()
+                row[f"{'exact' if exact else 'int8'}_{name}_us"] = round(e0.elapsed_time(e1) * 1e3 / reps, 1)
+        out[f"{t}x{ctx}"] = row
+    la.sync()
+    return {"workload": f"prefill chunks of {', '.join(map(str, chunks))} tokens over {ctx} cached tokens", **out}
+
+
 def measure_decodes(la, synth, dev, peak_gbs: float) -> dict:
     """Decode (m = 1) at config 2's and config 3's context lengths and seeds."""
     return {"32k": measure_decode(la, synth, dev, peak_gbs, CTX, SEED, 4),
@@ -756,6 +793,8 @@ def run_ours(args):
         extras["prefix"] = measure_prefix(la)
         torch.cuda.empty_cache()
         extras["c4"] = measure_c4(la, synth, dev, pk)
+        torch.cuda.empty_cache()
+        extras["prefill_chunks"] = measure_prefill_chunks(la, dev)
         torch.cuda.empty_cache()
         extras["c5"] = measure_c5(la, dev)
 

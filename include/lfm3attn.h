@@ -166,7 +166,14 @@ int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int
                   const void* gate, void* out, void* stream);
 
 /* ---------------------------------------------------------------- prefill attention */
+/* Workspace that lets lfm3a_prefill_attention split a chunk's keys at any context (0 when a chunk of this
+ * many tokens already fills the GPU). */
 size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim);
+/* The number of key splits lfm3a_prefill_attention uses for a chunk (the counterpart of attnSplits,
+ * internal/model/prefill.go:37-46): 1 when the chunk's CTAs (one per 32 query tokens and kv head) fill
+ * one wave of two per SM; else enough splits for one wave, each with at least 8 key tiles of the shortest
+ * row band, at most 64. sm_count 0: the current device's. */
+int lfm3a_prefill_splits(int tokens, int q_heads, int context, int window, int sm_count);
 
 /* Causal (optionally sliding-window) prefill attention of tokens query tokens at positions
  * context .. context + tokens - 1 over the cache [0, context + tokens) (kernels/prefill_attn.hip:373-486
@@ -174,7 +181,10 @@ size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim);
  * internal/model/prefill.go:476-511). The chunk's K/V must already be appended.
  * exact = 0: u8 softmax probabilities per row and 64-key tile times the int8 V copy (tcgen05 kind::i8);
  * exact = 1: fp16 probabilities times fp16 V (tcgen05 kind::f16). q, out: device fp16
- * [tokens][q_heads][head_dim]. MODE_F16, head_dim 64, q_heads = 4 * kv_heads. */
+ * [tokens][q_heads][head_dim]. MODE_F16, head_dim 64, q_heads = 4 * kv_heads.
+ * With a 16-byte aligned workspace of lfm3a_prefill_workspace_bytes, a chunk short of one wave of CTAs is
+ * split along the keys (lfm3a_prefill_splits) and its partials merged (the combine of lfm3a_combine);
+ * without one it runs unsplit. */
 int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
                             int exact, void* out, void* workspace, size_t workspace_bytes, void* stream);
 

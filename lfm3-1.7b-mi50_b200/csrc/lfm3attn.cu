@@ -407,16 +407,19 @@ int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_he
 }
 
 size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim) {
-  (void)tokens;
-  (void)q_heads;
-  (void)head_dim;
-  return 0;
+  if (tokens <= 0 || q_heads < 4 || head_dim != 64) return 0;
+  // The most splits any context can get for this chunk (the long-context bound of prefill_splits_for).
+  const int splits = prefill_splits_for(tokens, q_heads / 4, 1 << 30, 0, current_sm_count());
+  return splits > 1 ? (size_t)tokens * q_heads * splits * kPfPart * sizeof(float) : 0;
+}
+
+int lfm3a_prefill_splits(int tokens, int q_heads, int context, int window, int sm_count) {
+  if (tokens < 0 || q_heads < 4 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill split arguments");
+  return prefill_splits_for(tokens, q_heads / 4, context, window, sm_count > 0 ? sm_count : current_sm_count());
 }
 
 int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
                             int exact, void* out, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
   const lfm3a_kv_layout& L = kv->layout;
@@ -425,8 +428,16 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
   if (!q || !out || tokens < 0 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill arguments");
   if (tokens == 0) return LFM3A_OK;
   if (!aligned16(q) || !aligned16(out)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
-  return launch_prefill(geom_of(kv), static_cast<const __half*>(q), tokens, q_heads, context, window, exact != 0,
-                        static_cast<__half*>(out), as_stream(stream));
+  // Key splits when the chunk alone leaves the GPU short of CTAs and the caller gave the workspace for them.
+  int splits = prefill_splits_for(tokens, L.kv_heads, context, window, current_sm_count());
+  const size_t need = (size_t)tokens * q_heads * splits * kPfPart * sizeof(float);
+  if (splits > 1 && (!workspace || !aligned16(workspace) || workspace_bytes < need)) splits = 1;
+  float* part = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  rc = launch_prefill(geom_of(kv), static_cast<const __half*>(q), tokens, q_heads, context, window, exact != 0,
+                      static_cast<__half*>(out), splits, part, as_stream(stream));
+  if (rc != LFM3A_OK || splits == 1) return rc;
+  return launch_combine(part, tokens * q_heads, splits, 64, kPfPart, (int64_t)splits * kPfPart, nullptr,
+                        static_cast<__half*>(out), nullptr, as_stream(stream));
 }
 
 size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim) {

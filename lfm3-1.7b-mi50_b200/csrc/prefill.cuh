@@ -15,6 +15,8 @@
 // Every operand sits in shared memory as 8-row x 16-byte core tiles (no swizzle, K-major); the page
 // sections are already in that order, so a page moves with plain bulk copies.
 #pragma once
+#include <algorithm>
+
 #include "common.cuh"
 #include "kv.cuh"
 
@@ -59,10 +61,12 @@ __global__ __launch_bounds__(128) void quantize_p_rows_kernel(const float* p, in
 struct PrefillArgs {
   KvGeom g;
   const __half* q;   // [T][QH][64]
-  __half* out;       // [T][QH][64]
-  int T, q_heads, context, window, qtiles;
+  __half* out;       // [T][QH][64] (splits == 1)
+  float* part;       // splits > 1: [T * QH][splits][66] partials (unnormalised acc, running max, sum)
+  int T, q_heads, context, window, qtiles, splits;
   float qk_scale;    // (1 / sqrt(64)) * log2(e)
 };
+constexpr int kPfPart = 66;
 
 constexpr int kPfStages = 4;       // per ring (K and V)
 constexpr int kPfQBytes = 16384;   // 128 rows x 64 dims fp16
@@ -82,8 +86,8 @@ struct PfLayout {
   static constexpr int kOffV = kOffK + kPfStages * kKStage;
   static constexpr int kOffP = kOffV + kPfStages * kVStage;
   static constexpr int kOffSc = kOffP + 2 * kPBuf;     // int8: [2][128] (corr, scale) of a tile, softmax -> epilogue
-  static constexpr int kOffL = kOffSc + (I8 ? 2 * 128 * 8 : 0);   // int8: [128] row sums for the epilogue's output
-  static constexpr int kOffBar = kOffL + (I8 ? 128 * 4 : 0);
+  static constexpr int kOffL = kOffSc + (I8 ? 2 * 128 * 8 : 0);   // int8: row sums and maxima for the epilogue
+  static constexpr int kOffBar = kOffL + (I8 ? 256 * 4 : 0);   // int8: [128] sums, [128] running maxima
   static constexpr int kBars = 4 * kPfStages + 2 + 4 + 2 + 2 + 2;
   static constexpr int kOffTmemSlot = kOffBar + kBars * 8;
   static constexpr int kOffAbort = kOffTmemSlot + 8;   // in the dynamic region: static shared memory would
@@ -124,8 +128,24 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
   const int t0 = qt * 32, ntok = min(32, a.T - t0);
   const int qfirst = a.context + t0, qlast = qfirst + ntok - 1, kend = qlast + 1;
   const int kbegin = a.window > 0 ? max(0, qfirst - a.window + 1) : 0;
-  const int kt_begin = kbegin / kQuantBlock * kQuantBlock;
-  const int ntiles = (kend - kt_begin + kQuantBlock - 1) / kQuantBlock;
+  // Split z of the key tiles (prefill_attn.hip:388-391): tiles [n z / splits, n (z + 1) / splits) of the
+  // CTA's n; each split keeps its own running max and, when split, leaves an unnormalised partial.
+  const int kt_base = kbegin / kQuantBlock * kQuantBlock;
+  const int all_tiles = (kend - kt_base + kQuantBlock - 1) / kQuantBlock;
+  const int tile_lo = (int)((int64_t)all_tiles * blockIdx.z / a.splits);
+  const int ntiles = (int)((int64_t)all_tiles * (blockIdx.z + 1) / a.splits) - tile_lo;
+  const int kt_begin = kt_base + tile_lo * kQuantBlock;
+  if (ntiles <= 0) {   // an empty split (more splits than this row band's tiles): weight zero in the merge
+    pdl_wait();
+    const int r = threadIdx.x, t = r >> 2;
+    if (r < 128 && t < ntok) {
+      float* prow = a.part + ((int64_t)(t0 + t) * a.q_heads + 4 * h + (r & 3)) * a.splits * kPfPart +
+                    (int64_t)blockIdx.z * kPfPart;
+      for (int d = 0; d < 64; d += 2) *reinterpret_cast<float2*>(prow + d) = make_float2(0.f, 0.f);
+      *reinterpret_cast<float2*>(prow + 64) = make_float2(-INFINITY, 0.f);
+    }
+    return;
+  }
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -286,10 +306,26 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
         atomicExch(&s_abort, 1);
       } else {
         tc_fence_after();
+        if (a.splits > 1) {   // this split's unnormalised O, running max and sum
+          float* prow = a.part + (grow * a.splits + blockIdx.z) * kPfPart;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t rr[16];
+            tmem_ld16(lane_base + 128 + 16 * c, rr);
+            tmem_wait_ld();
+            reg_fence16(rr);
+            if (row_ok) {
+#pragma unroll
+              for (int e = 0; e < 16; e += 2)
+                *reinterpret_cast<float2*>(prow + 16 * c + e) = make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+            }
+          }
+          if (row_ok) *reinterpret_cast<float2*>(prow + 64) = make_float2(m_run, l_run);
+        }
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {   // 16 columns of O at a time
+        for (int c = 0; c < 4 && a.splits == 1; ++c) {   // 16 columns of O at a time
           uint32_t rr[16];
           tmem_ld16(lane_base + 128 + 16 * c, rr);
           tmem_wait_ld();
@@ -433,8 +469,9 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       if (lane == 0) mbar_arrive(&p_full[2 * b]);
     }
     if (!ok) atomicExch(&s_abort, 1);
-    // The epilogue warpgroup writes the output: hand it the row sums.
+    // The epilogue warpgroup writes the output: hand it the row sums (and, for a partial, the running max).
     sL[r] = l_run;
+    sL[128 + r] = m_run;
     named_bar_sync(2, 256);
   } else if (I8 && warp < 8) {
     // ================================================================ int8 epilogue warpgroup, thread = row
@@ -525,10 +562,26 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     if (!*reinterpret_cast<volatile int*>(&s_abort)) {
       tc_fence_after();
       const float l = sL[r];
+      if (a.splits > 1) {   // this split's unnormalised accumulator, running max and sum
+        float* prow = a.part + (grow * a.splits + blockIdx.z) * kPfPart;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rr[16];
+          tmem_ld16(lane_base + 192 + 16 * c, rr);
+          tmem_wait_ld();
+          reg_fence16(rr);
+          if (row_ok) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2)
+              *reinterpret_cast<float2*>(prow + 16 * c + e) = make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+          }
+        }
+        if (row_ok) *reinterpret_cast<float2*>(prow + 64) = make_float2(sL[128 + r], l);
+      }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 4 && a.splits == 1; ++c) {
         uint32_t rr[16];
         tmem_ld16(lane_base + 192 + 16 * c, rr);
         tmem_wait_ld();
@@ -708,7 +761,7 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
   static bool done[2][64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LFM3A_ECUDA;
-  const dim3 grid(a.qtiles, a.g.kv_heads);
+  const dim3 grid(a.qtiles, a.g.kv_heads, a.splits);
   if (i8) {
     if (!done[1][dev]) {
       if (cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -731,17 +784,47 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
   return cudaGetLastError() == cudaSuccess ? LFM3A_OK : LFM3A_ELAUNCH;
 }
 
+// Key splits for a chunk that leaves the GPU short of one wave of CTAs (two per SM): a short chunk over a
+// long context (the reference's attnSplits, prefill.go:37-46). Each split keeps at least 8 tiles of the
+// shortest row band (the first 32 query tokens), at most 64 splits and at most four waves of CTAs (which
+// bounds the partials: workspace and combine traffic). Among those, the count with the least modelled
+// time: waves of CTAs x (tiles per split + 2 tiles of fixed cost per CTA), fewest splits on ties (a
+// chunk's row bands hold nearly equal tile counts when the context is long).
+inline int prefill_splits_for(int tokens, int kv_heads, int context, int window, int sm_count) {
+  const int blocks = (tokens + 31) / 32 * kv_heads;
+  const int target = 2 * sm_count;
+  if (tokens <= 0 || blocks >= target) return 1;
+  const int keys_min = window > 0 ? std::min(window + 31, context + std::min(tokens, 32))
+                                  : context + std::min(tokens, 32);
+  const int tiles_min = (keys_min + kQuantBlock - 1) / kQuantBlock;
+  const int most = std::max(1, std::min(std::min(64, tiles_min / 8), 4 * target / blocks));
+  int best = 1;
+  double best_cost = 0.0;
+  for (int s = 1; s <= most; ++s) {
+    const int waves = (blocks * s + target - 1) / target;
+    const double cost = waves * ((double)tiles_min / s + 2.0);
+    if (s == 1 || cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+// splits > 1: part receives [tokens * q_heads][splits][kPfPart] partials for the combine.
 inline int launch_prefill(const KvGeom& g, const __half* q, int tokens, int q_heads, int context, int window, bool exact,
-                          __half* out, cudaStream_t st) {
+                          __half* out, int splits, float* part, cudaStream_t st) {
   PrefillArgs a;
   a.g = g;
   a.q = q;
   a.out = out;
+  a.part = part;
   a.T = tokens;
   a.q_heads = q_heads;
   a.context = context;
   a.window = window;
   a.qtiles = (tokens + 31) / 32;
+  a.splits = splits;
   a.qk_scale = 0.125f * kLog2e;
   return launch_prefill_kernel(a, !exact, st);
 }

@@ -78,6 +78,7 @@ SIGNATURES = {
     "lfm3a_verify_partial": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_combine": (_I, [_P, _I, _I, _I, _I64, _I64, _P, _P, _P]),
     "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "lfm3a_prefill_splits": (_I, [_I, _I, _I, _I, _I]),
     "lfm3a_prefill_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "lfm3a_quantize_p_u8": (_I, [_P, _I, _P, _P, _P]),
     "lfm3a_gather_region_bytes": (_SZ, [_I, _I, _I]),

@@ -402,25 +402,30 @@ void orc_attention_f64(const uint16_t* q, int nq, int qpos0, int q_heads, int kv
 
 namespace {
 
-// One query row of the prefill kernels: CTA of 32 query tokens (t0 = t & ~31), 64-key tiles from the
-// CTA's first key rounded down to 64 (prefill_attn.hip:212-332,373-486; prefill_attn_exact.hip:173-344).
+// One query row of the prefill kernels over split z of S: CTA of 32 query tokens (t0 = t & ~31), 64-key
+// tiles from the CTA's first key rounded down to 64, split z taking tiles [n z / S, n (z + 1) / S) of the
+// CTA's n (prefill_attn.hip:212-332,373-486,388-391; prefill_attn_exact.hip:173-344). Leaves the
+// unnormalised accumulator acc[D], the running max *pm and the sum *pl.
 template <bool I8>
-void prefill_row(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int D, const uint16_t* K,
-                 const uint16_t* V, const int8_t* V8, const float* vscale, int window, int t, int qh, float* o) {
+void prefill_part(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int D, const uint16_t* K,
+                  const uint16_t* V, const int8_t* V8, const float* vscale, int window, int t, int qh, int z, int S,
+                  float* acc_out, float* pm, float* pl) {
   const int G = q_heads / kv_heads, h = qh / G;
   const int t0 = t & ~31, ntok = std::min(32, T - t0);
   const int qpos = context + t, qfirst = context + t0, kend = context + t0 + ntok;
   const int kbegin = window > 0 ? std::max(0, qfirst - window + 1) : 0;
-  const int kt_begin = kbegin / QB * QB;
+  const int kt_base = kbegin / QB * QB;
+  const int all_tiles = (kend - kt_base + QB - 1) / QB;
+  const int tile_lo = (int)((int64_t)all_tiles * z / S), tile_hi = (int)((int64_t)all_tiles * (z + 1) / S);
   const float qk_scale = (1.f / sqrtf((float)D)) * LOG2E;
   float qf[128];
   for (int d = 0; d < D; ++d) qf[d] = orc_f16_to_f32(q[((size_t)t * q_heads + qh) * D + d]);
-  // int8 kernel: running max starts at 0 and moves on the CTA's first tile or when a tile beats it by 2^8
-  // (prefill_attn.hip:278-304); exact kernel: running max from -inf, moved by every larger tile max
+  // int8 kernel: running max starts at 0 and moves on the split's first tile or when a tile beats it by
+  // 2^8 (prefill_attn.hip:278-304); exact kernel: running max from -inf, moved by every larger tile max
   // (prefill_attn_exact.hip:300-306).
   float m = I8 ? 0.f : -INFINITY, l = 0.f, acc[128] = {0};
   bool first = true;
-  for (int k0 = kt_begin; k0 < kend; k0 += QB, first = false) {
+  for (int k0 = kt_base + tile_lo * QB; k0 < kt_base + tile_hi * QB; k0 += QB, first = false) {
     float s[QB];
     float tm = -INFINITY;
     for (int kk = 0; kk < QB; ++kk) {
@@ -473,17 +478,36 @@ void prefill_row(const uint16_t* q, int T, int context, int q_heads, int kv_head
       }
     }
   }
-  for (int d = 0; d < D; ++d) o[d] = l > 0.f ? acc[d] / l : 0.f;
+  for (int d = 0; d < D; ++d) acc_out[d] = acc[d];
+  *pm = m;
+  *pl = l;
+}
+
+// One row over all S splits: unsplit, the normalised accumulator; split, the log-sum-exp merge of the
+// splits' partials (prefill_attn.hip:489-505, the verify merge above).
+template <bool I8>
+void prefill_row(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int D, const uint16_t* K,
+                 const uint16_t* V, const int8_t* V8, const float* vscale, int window, int t, int qh, int S, float* o) {
+  std::vector<float> acc((size_t)S * D), pm(S), pl(S);
+  for (int z = 0; z < S; ++z)
+    prefill_part<I8>(q, T, context, q_heads, kv_heads, D, K, V, V8, vscale, window, t, qh, z, S,
+                     acc.data() + (size_t)z * D, &pm[z], &pl[z]);
+  if (S == 1) {
+    for (int d = 0; d < D; ++d) o[d] = pl[0] > 0.f ? acc[d] / pl[0] : 0.f;
+  } else {
+    merge_row(acc.data(), pm.data(), pl.data(), S, D, nullptr, 0, o);
+  }
 }
 
 template <bool I8>
 void prefill_all(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int D, const uint16_t* K,
-                 const uint16_t* V, const int8_t* V8, const float* vscale, int window, int row_step, float* out) {
+                 const uint16_t* V, const int8_t* V8, const float* vscale, int window, int row_step, int S,
+                 float* out) {
   const int rows = (T + row_step - 1) / row_step;
 #pragma omp parallel for schedule(dynamic, 1)
   for (int ri = 0; ri < rows * q_heads; ++ri) {
     const int t = (ri / q_heads) * row_step, qh = ri % q_heads;
-    prefill_row<I8>(q, T, context, q_heads, kv_heads, D, K, V, V8, vscale, window, t, qh,
+    prefill_row<I8>(q, T, context, q_heads, kv_heads, D, K, V, V8, vscale, window, t, qh, S,
                     out + ((size_t)t * q_heads + qh) * D);
   }
 }
@@ -493,13 +517,16 @@ void prefill_all(const uint16_t* q, int T, int context, int q_heads, int kv_head
 extern "C" {
 
 void orc_prefill_i8pv(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
-                      const uint16_t* K, const int8_t* V8, const float* vscale, int window, int row_step, float* out) {
-  prefill_all<true>(q, T, context, q_heads, kv_heads, head_dim, K, nullptr, V8, vscale, window, row_step, out);
+                      const uint16_t* K, const int8_t* V8, const float* vscale, int window, int row_step, int splits,
+                      float* out) {
+  prefill_all<true>(q, T, context, q_heads, kv_heads, head_dim, K, nullptr, V8, vscale, window, row_step,
+                    std::max(1, splits), out);
 }
 
 void orc_prefill_exact(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
-                       const uint16_t* K, const uint16_t* V, int window, int row_step, float* out) {
-  prefill_all<false>(q, T, context, q_heads, kv_heads, head_dim, K, V, nullptr, nullptr, window, row_step, out);
+                       const uint16_t* K, const uint16_t* V, int window, int row_step, int splits, float* out) {
+  prefill_all<false>(q, T, context, q_heads, kv_heads, head_dim, K, V, nullptr, nullptr, window, row_step,
+                     std::max(1, splits), out);
 }
 
 int orc_accept(const int32_t* best, const int32_t* tokens, int m) {

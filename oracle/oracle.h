@@ -81,13 +81,17 @@ void orc_attention_f64(const uint16_t* q, int nq, int qpos0, int q_heads, int kv
 
 /* Prefill attention with u8 P and int8 V (prefill_attn.hip:212-367,373-486): 64-key tiles aligned to 64,
  * lazy running max (threshold 2^8), P' = p * vscale quantised per row and tile, PV in exact integers.
- * Query tokens t < T at positions context + t; keys [0, context + T). Rows t % row_step == 0 only. */
+ * Query tokens t < T at positions context + t; keys [0, context + T). Rows t % row_step == 0 only.
+ * splits > 1: each CTA's key tiles are split as prefill_attn.hip:388-391 (split z takes tiles
+ * [n z / splits, n (z + 1) / splits) of its n), each split with its own running max, and the partials are
+ * merged as prefill_attn.hip:489-505. */
 void orc_prefill_i8pv(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
-                      const uint16_t* K, const int8_t* V8, const float* vscale, int window, int row_step, float* out);
+                      const uint16_t* K, const int8_t* V8, const float* vscale, int window, int row_step, int splits,
+                      float* out);
 
 /* The same with fp16 P and fp16 V (prefill_attn_exact.hip:173-344 with fp16 V). */
 void orc_prefill_exact(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
-                       const uint16_t* K, const uint16_t* V, int window, int row_step, float* out);
+                       const uint16_t* K, const uint16_t* V, int window, int row_step, int splits, float* out);
 
 /* Acceptance of a verify round (dspark.hip:2848-2895): the longest prefix t with best[t] == tokens[t+1],
  * then commit = accepted + 1 positions. Returns commit. */

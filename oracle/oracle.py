@@ -31,8 +31,8 @@ _SIGS = {
     "orc_verify_partial": (None, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _I, _I, _P]),
     "orc_combine": (None, [_P, _I, _I, _I, _P, _P]),
     "orc_attention_f64": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
-    "orc_prefill_i8pv": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
-    "orc_prefill_exact": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _P]),
+    "orc_prefill_i8pv": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _I, _P]),
+    "orc_prefill_exact": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
     "orc_accept": (_I, [_P, _P, _I]),
     "orc_set_threads": (None, [_I]),
     "orc_get_threads": (_I, []),
@@ -169,7 +169,7 @@ def attention_f64(q, qpos0: int, K, V, kv_len: int, window: int = 0, row_step: i
     return out
 
 
-def prefill_i8pv(q, context: int, K, V8, vscale, window: int = 0, row_step: int = 1) -> np.ndarray:
+def prefill_i8pv(q, context: int, K, V8, vscale, window: int = 0, row_step: int = 1, splits: int = 1) -> np.ndarray:
     t, qh, d = q.shape
     kvh = K.shape[1]
     q, qp = _c(q, np.float16)
@@ -177,18 +177,18 @@ def prefill_i8pv(q, context: int, K, V8, vscale, window: int = 0, row_step: int 
     V8, v8p = _c(V8, np.int8)
     vscale, sp = _c(vscale, np.float32)
     out = np.zeros((t, qh, d), dtype=np.float32)
-    lib().orc_prefill_i8pv(qp, t, context, qh, kvh, d, kp, v8p, sp, window, row_step, out.ctypes.data)
+    lib().orc_prefill_i8pv(qp, t, context, qh, kvh, d, kp, v8p, sp, window, row_step, splits, out.ctypes.data)
     return out
 
 
-def prefill_exact(q, context: int, K, V, window: int = 0, row_step: int = 1) -> np.ndarray:
+def prefill_exact(q, context: int, K, V, window: int = 0, row_step: int = 1, splits: int = 1) -> np.ndarray:
     t, qh, d = q.shape
     kvh = K.shape[1]
     q, qp = _c(q, np.float16)
     K, kp = _c(K, np.float16)
     V, vp = _c(V, np.float16)
     out = np.zeros((t, qh, d), dtype=np.float32)
-    lib().orc_prefill_exact(qp, t, context, qh, kvh, d, kp, vp, window, row_step, out.ctypes.data)
+    lib().orc_prefill_exact(qp, t, context, qh, kvh, d, kp, vp, window, row_step, splits, out.ctypes.data)
     return out
 
 

@@ -100,3 +100,20 @@ def test_synth_generator_is_deterministic(synth):
     assert abs(z.mean()) < 0.01 and abs(z.std() - 1) < 0.01
     keep = synth.geometric_keep(4, 256)
     assert keep.min() >= 1 and keep.max() <= 16 and 2.5 < keep.mean() < 4.0
+
+
+def test_prefill_split_choice(la):
+    """Chunks that fill one wave of two CTAs per SM run unsplit; short chunks over long contexts split into
+    the count with the least modelled time (whole waves, 2 tiles of fixed cost per CTA), each split with at
+    least 8 key tiles of the shortest row band, at most 64 splits and four waves."""
+    sp = lambda t, ctx, w=0: la.lib().lfm3a_prefill_splits(t, 32, ctx, w, 148)
+    assert sp(32768, 0) == 1 and sp(1184, 100000) == 1
+    assert sp(32, 131072) == 37          # 8 CTAs x 37 = 296: one wave
+    assert sp(512, 131072) == 9          # 128 CTAs x 9 = 1152: four nearly full waves (cap: four waves)
+    assert sp(1024, 131072) == 1         # 256 CTAs: splitting gains nothing within four waves
+    assert sp(64, 20000) == 18           # 16 x 18 = 288
+    assert sp(200, 1000) == 2            # 17 tiles in the first band: at most 2 splits of >= 8
+    assert sp(32, 100) == 1              # too few tiles to split
+    assert sp(32, 10 ** 6, 300) == 1     # a 300-token window: bands of 6 tiles
+    assert sp(32, 10 ** 6, 4096) == 8    # 4127 keys: 65 tiles, at most 8 splits
+    assert la.lib().lfm3a_prefill_splits(-1, 32, 0, 0, 148) == la.EINVAL

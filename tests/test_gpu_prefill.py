@@ -86,3 +86,26 @@ def test_prefill_c4_sampled_rows(la, orc, synth, cuda):
     emu = orc.prefill_i8pv(case["Q"], 0, case["K"], v8, vs, row_step=257)
     assert rel_err(i8.float().cpu().numpy(), emu, rows) < TOL_I8
     assert torch.isfinite(ex).all() and torch.isfinite(i8).all()
+
+
+SPLIT_CASES = [(20000, 64, 0), (5000, 100, 2000), (3000, 32, 0), (1000, 200, 0)]
+
+
+@pytest.mark.parametrize("exact", [True, False])
+@pytest.mark.parametrize("context,T,window", SPLIT_CASES)
+def test_prefill_key_splits(la, orc, synth, cuda, context, T, window, exact):
+    """A short chunk over a long context is split along the keys (lfm3a_prefill_splits) and merged; checked
+    against the oracle with the same split and, for exact, against fp64 attention."""
+    splits = la.lib().lfm3a_prefill_splits(T, 32, context, window, 0)
+    assert splits > 1
+    case, cache, got = run(la, synth, cuda, 80 + T, context, T, window, exact)
+    n = context + T
+    q = case["Q"][context:]
+    if exact:
+        emu = orc.prefill_exact(q, context, case["K"], case["V"], window=window, splits=splits)
+        assert rel_err(got, emu) < TOL_EXACT
+        assert rel_err(got, orc.attention_f64(q, context, case["K"], case["V"], n, window=window)) < TOL_EXACT
+    else:
+        v8, vs = orc.quantize_v8(case["V"], n)
+        emu = orc.prefill_i8pv(q, context, case["K"], v8, vs, window=window, splits=splits)
+        assert rel_err(got, emu) < TOL_I8

@@ -71,3 +71,16 @@ def test_prefill_row_sampling(orc, synth):
     some = orc.prefill_exact(case["Q"], 0, case["K"], case["V"], row_step=7)
     assert np.array_equal(full[::7], some[::7])
     assert not some[1].any()
+
+
+def test_prefill_split_merge(orc, synth):
+    """The oracle's key-split prefill (per-split running maxima, log-sum-exp merge) against its unsplit pass
+    and exact fp64 attention."""
+    ctx, T = 3000, 40
+    case = synth.prefill_case(90, ctx + T)
+    q = case["Q"][ctx:]
+    want = orc.attention_f64(q, ctx, case["K"], case["V"], ctx + T).astype(np.float64)
+    rms = float(np.sqrt(np.mean(want ** 2)))
+    for splits in (1, 3, 6):
+        got = orc.prefill_exact(q, ctx, case["K"], case["V"], splits=splits)
+        assert float(np.max(np.abs(got - want))) / rms < 2e-3
