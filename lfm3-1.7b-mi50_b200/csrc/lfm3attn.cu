@@ -418,14 +418,19 @@ int lfm3a_prefill_splits(int tokens, int q_heads, int context, int window, int s
   return prefill_splits_for(tokens, q_heads / 4, context, window, sm_count > 0 ? sm_count : current_sm_count());
 }
 
-int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
-                            int exact, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_t q_stride, const void* q_norm,
+                                  const void* rope, const void* gate, int64_t gate_stride, int tokens, int q_heads,
+                                  int context, int window, int exact, void* out, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
   const lfm3a_kv_layout& L = kv->layout;
   if (L.mode != LFM3A_MODE_F16 || L.head_dim != 64) return fail(LFM3A_ENOTSUP, "prefill attention needs MODE_F16, head_dim 64");
   if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "prefill attention needs 4 query heads per kv head");
   if (!q || !out || tokens < 0 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill arguments");
+  if (q_stride < (int64_t)q_heads * 64 || q_stride % 8 != 0)
+    return fail(LFM3A_EINVAL, "q_stride must be a multiple of 8 and at least q_heads * head_dim");
+  if (gate && gate_stride < q_heads) return fail(LFM3A_EINVAL, "gate_stride must be at least q_heads");
   if (tokens == 0) return LFM3A_OK;
   if (!aligned16(q) || !aligned16(out)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
   // Key splits when the chunk alone leaves the GPU short of CTAs and the caller gave the workspace for them.
@@ -433,11 +438,24 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
   const size_t need = (size_t)tokens * q_heads * splits * kPfPart * sizeof(float);
   if (splits > 1 && (!workspace || !aligned16(workspace) || workspace_bytes < need)) splits = 1;
   float* part = splits > 1 ? static_cast<float*>(workspace) : nullptr;
-  rc = launch_prefill(geom_of(kv), static_cast<const __half*>(q), tokens, q_heads, context, window, exact != 0,
-                      static_cast<__half*>(out), splits, part, as_stream(stream));
+  const cudaStream_t st = as_stream(stream);
+  rc = launch_prefill(geom_of(kv), static_cast<const __half*>(q), q_stride, static_cast<const __half*>(q_norm),
+                      static_cast<const __half*>(rope), static_cast<const __half*>(gate), gate_stride, tokens, q_heads,
+                      context, window, exact != 0, static_cast<__half*>(out), splits, part, st);
   if (rc != LFM3A_OK || splits == 1) return rc;
-  return launch_combine(part, tokens * q_heads, splits, 64, kPfPart, (int64_t)splits * kPfPart, nullptr,
-                        static_cast<__half*>(out), nullptr, as_stream(stream));
+  rc = launch_combine(part, tokens * q_heads, splits, 64, kPfPart, (int64_t)splits * kPfPart, nullptr,
+                      static_cast<__half*>(out), nullptr, st);
+  if (rc != LFM3A_OK || !gate) return rc;
+  const int64_t groups = (int64_t)tokens * q_heads * 8;
+  launch_pdl(prefill_gate_kernel, (unsigned)((groups + 255) / 256), 256, 0, st, static_cast<__half*>(out),
+             static_cast<const __half*>(gate), gate_stride, tokens * q_heads, q_heads);
+  return check_launch("prefill_gate_kernel");
+}
+
+int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
+                            int exact, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  return lfm3a_prefill_attention_fused(kv, q, (int64_t)q_heads * 64, nullptr, nullptr, nullptr, 0, tokens, q_heads,
+                                       context, window, exact, out, workspace, workspace_bytes, stream);
 }
 
 size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim) {

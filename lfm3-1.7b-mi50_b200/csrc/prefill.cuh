@@ -60,13 +60,136 @@ __global__ __launch_bounds__(128) void quantize_p_rows_kernel(const float* p, in
 
 struct PrefillArgs {
   KvGeom g;
-  const __half* q;   // [T][QH][64]
-  __half* out;       // [T][QH][64] (splits == 1)
-  float* part;       // splits > 1: [T * QH][splits][66] partials (unnormalised acc, running max, sum)
+  const __half* q;        // row (t, qh) at q + t * q_stride + qh * 64
+  __half* out;            // [T][QH][64] (splits == 1)
+  float* part;            // splits > 1: [T * QH][splits][66] partials (unnormalised acc, running max, sum)
+  const __half* q_norm;   // fp16 [64] RMS weights of the fused q-norm, or null
+  const __half* rope;     // RoPE table rows [position][64] (cos | sin) of the fused Q rotation, or null
+  const __half* gate;     // output gate logits at gate + t * gate_stride + qh (splits == 1 only), or null
+  int64_t q_stride, gate_stride;
   int T, q_heads, context, window, qtiles, splits;
-  float qk_scale;    // (1 / sqrt(64)) * log2(e)
+  float qk_scale;         // (1 / sqrt(64)) * log2(e)
 };
 constexpr int kPfPart = 66;
+
+// Query row (tok, qh) into its core tiles: row r, dims 8c .. 8c + 7 at ((r / 8) * 8 + c) * 128 + (r % 8) * 16.
+// With q_norm or rope the row is first RMS-normalised (eps 1e-5) and rotated, each step rounded to fp16 as
+// q_norm_rope does (kernels/ops.hip:193-210); the sum of squares follows the reference's 64-lane reduction
+// as the K append does: pair terms (l, l + 32) summed in a 32-lane butterfly order. The row is streamed in
+// chunk pairs (dims 8c .. 8c + 7 and their rotation partners 8c + 32 ..), so it never sits whole in
+// registers.
+__device__ __forceinline__ void unpack8(uint4 v, float (&x)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_half2(w[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&x)[8]) {
+  return make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]), pack_half2(x[6], x[7]));
+}
+__device__ __forceinline__ float r16f(float x) { return __half2float(__float2half_rn(x)); }
+
+template <bool GLUE>
+__device__ __forceinline__ void load_q_row(const PrefillArgs& a, uint8_t* sQ, int r, bool row_ok, int tok, int qh) {
+  const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)tok * a.q_stride + (int64_t)qh * 64);
+  uint4* dst = reinterpret_cast<uint4*>(sQ + (r >> 3) * 8 * 128 + (r & 7) * 16);
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  if (!GLUE || (!a.q_norm && !a.rope)) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) dst[c * 8] = row_ok ? src[c] : zero;
+    return;
+  }
+  float inv = 1.f;
+  if (a.q_norm) {
+    float v[32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float lo[8], hi[8];
+      unpack8(row_ok ? src[c] : zero, lo);
+      unpack8(row_ok ? src[c + 4] : zero, hi);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[8 * c + i] = __fadd_rn(__fmul_rn(lo[i], lo[i]), __fmul_rn(hi[i], hi[i]));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+      for (int l = 0; l < o; ++l) v[l] = __fadd_rn(v[l], v[l + o]);
+    inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v[0], 64.f), 1e-5f)));
+  }
+  const uint4* w4 = reinterpret_cast<const uint4*>(a.q_norm);
+  const uint4* cs4 = a.rope ? reinterpret_cast<const uint4*>(a.rope + (int64_t)(a.context + tok) * 64) : nullptr;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float lo[8], hi[8];
+    unpack8(row_ok ? src[c] : zero, lo);
+    unpack8(row_ok ? src[c + 4] : zero, hi);
+    if (a.q_norm) {
+      float wl[8], wh[8];
+      unpack8(w4[c], wl);
+      unpack8(w4[c + 4], wh);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        lo[i] = r16f(__fmul_rn(__fmul_rn(lo[i], inv), wl[i]));
+        hi[i] = r16f(__fmul_rn(__fmul_rn(hi[i], inv), wh[i]));
+      }
+    }
+    if (cs4) {
+      float cv[8], sv[8];
+      unpack8(cs4[c], cv);
+      unpack8(cs4[c + 4], sv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float a1 = lo[i], b1 = hi[i];
+        lo[i] = r16f(__fsub_rn(__fmul_rn(a1, cv[i]), __fmul_rn(b1, sv[i])));
+        hi[i] = r16f(__fadd_rn(__fmul_rn(b1, cv[i]), __fmul_rn(a1, sv[i])));
+      }
+    }
+    dst[c * 8] = row_ok ? pack8(lo) : zero;
+    dst[(c + 4) * 8] = row_ok ? pack8(hi) : zero;
+  }
+}
+
+// The output gate of a row (kernels/ops.hip:254-264 gate_mul): fp16(sigmoid(logit)), 1 without a gate.
+__device__ __forceinline__ __half2 gate_half2(const PrefillArgs& a, int tok, int qh) {
+  if (!a.gate) return __float2half2_rn(1.f);
+  const float g = __half2float(a.gate[(int64_t)tok * a.gate_stride + qh]);
+  return __float2half2_rn(__fdiv_rn(1.f, __fadd_rn(1.f, expf(-g))));
+}
+
+// A row's eight output halves: fp16(acc * inv), then (with a gate) fp16(that * gate), as gate_mul rounds.
+__device__ __forceinline__ uint4 out_pack8(const uint32_t* rr, float inv, __half2 g2, bool gated) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(__uint_as_float(rr[2 * i]) * inv, __uint_as_float(rr[2 * i + 1]) * inv);
+    if (gated) h = __hmul2(h, g2);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// In-place output gate for split chunks (the combine leaves fp16(acc / l) in out): 8 halves per thread.
+__global__ __launch_bounds__(256) void prefill_gate_kernel(__half* out, const __half* gate, int64_t gate_stride,
+                                                           int rows, int q_heads) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // 8-half group
+  if (i >= (int64_t)rows * 8) return;
+  const int row = (int)(i >> 3), tok = row / q_heads, qh = row - tok * q_heads;
+  const float g = __half2float(gate[(int64_t)tok * gate_stride + qh]);
+  const __half2 g2 = __float2half2_rn(__fdiv_rn(1.f, __fadd_rn(1.f, expf(-g))));
+  uint4 v = reinterpret_cast<uint4*>(out)[i];
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    __half2 h = __hmul2(*reinterpret_cast<__half2*>(&w[k]), g2);
+    w[k] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  reinterpret_cast<uint4*>(out)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+}
 
 constexpr int kPfStages = 4;       // per ring (K and V)
 constexpr int kPfQBytes = 16384;   // 128 rows x 64 dims fp16
@@ -96,7 +219,11 @@ struct PfLayout {
   static constexpr int kRequest = kBytes > 80 * 1024 ? kBytes : 80 * 1024;
 };
 
-template <bool I8>
+// SPLIT: the launch splits the keys (a.splits > 1) and this CTA leaves a partial; the unsplit instantiation
+// carries none of that code, so the tile loops keep their register allocation.
+// GLUE: the launch fuses the q-norm / RoPE of the query rows or the output gate (lfm3a_prefill_attention_fused);
+// the plain instantiation reads Q as it is and stores the output ungated.
+template <bool I8, bool SPLIT, bool GLUE>
 __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(PrefillArgs a) {
   using L = PfLayout<I8>;
   constexpr int NS = kPfStages;
@@ -132,10 +259,11 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
   // CTA's n; each split keeps its own running max and, when split, leaves an unnormalised partial.
   const int kt_base = kbegin / kQuantBlock * kQuantBlock;
   const int all_tiles = (kend - kt_base + kQuantBlock - 1) / kQuantBlock;
-  const int tile_lo = (int)((int64_t)all_tiles * blockIdx.z / a.splits);
-  const int ntiles = (int)((int64_t)all_tiles * (blockIdx.z + 1) / a.splits) - tile_lo;
+  const int nsplit = SPLIT ? a.splits : 1;
+  const int tile_lo = SPLIT ? (int)((int64_t)all_tiles * blockIdx.z / nsplit) : 0;
+  const int ntiles = SPLIT ? (int)((int64_t)all_tiles * (blockIdx.z + 1) / nsplit) - tile_lo : all_tiles;
   const int kt_begin = kt_base + tile_lo * kQuantBlock;
-  if (ntiles <= 0) {   // an empty split (more splits than this row band's tiles): weight zero in the merge
+  if (SPLIT && ntiles <= 0) {   // an empty split (more splits than this row band's tiles): weight zero in the merge
     pdl_wait();
     const int r = threadIdx.x, t = r >> 2;
     if (r < 128 && t < ntok) {
@@ -197,14 +325,8 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     const bool row_ok = t < ntok;
     const int qpos = qfirst + t;
     const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
-    // Q row -> core tiles: row r, dims 8c .. 8c + 7 at ((r / 8) * 8 + c) * 128 + (r % 8) * 16.
     {
-      const uint4* src = reinterpret_cast<const uint4*>(a.q + grow * 64);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
-      }
+      load_q_row<GLUE>(a, sQ, r, row_ok, t0 + (row_ok ? t : 0), 4 * h + j);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -306,7 +428,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
         atomicExch(&s_abort, 1);
       } else {
         tc_fence_after();
-        if (a.splits > 1) {   // this split's unnormalised O, running max and sum
+        if (SPLIT) {   // this split's unnormalised O, running max and sum
           float* prow = a.part + (grow * a.splits + blockIdx.z) * kPfPart;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -324,22 +446,17 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
         }
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+        const bool gated = GLUE && a.gate != nullptr;
+        const __half2 g2 = GLUE ? gate_half2(a, t0 + (row_ok ? t : 0), 4 * h + j) : __float2half2_rn(1.f);
 #pragma unroll
-        for (int c = 0; c < 4 && a.splits == 1; ++c) {   // 16 columns of O at a time
+        for (int c = 0; c < 4 && !SPLIT; ++c) {   // 16 columns of O at a time
           uint32_t rr[16];
           tmem_ld16(lane_base + 128 + 16 * c, rr);
           tmem_wait_ld();
           reg_fence16(rr);
           if (row_ok) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              uint4 v;
-              v.x = pack_half2(__uint_as_float(rr[8 * hh]) * inv, __uint_as_float(rr[8 * hh + 1]) * inv);
-              v.y = pack_half2(__uint_as_float(rr[8 * hh + 2]) * inv, __uint_as_float(rr[8 * hh + 3]) * inv);
-              v.z = pack_half2(__uint_as_float(rr[8 * hh + 4]) * inv, __uint_as_float(rr[8 * hh + 5]) * inv);
-              v.w = pack_half2(__uint_as_float(rr[8 * hh + 6]) * inv, __uint_as_float(rr[8 * hh + 7]) * inv);
-              dst[2 * c + hh] = v;
-            }
+            dst[2 * c] = out_pack8(rr, inv, g2, gated);
+            dst[2 * c + 1] = out_pack8(rr + 8, inv, g2, gated);
           }
         }
       }
@@ -350,14 +467,8 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     const bool row_ok = t < ntok;
     const int qpos = qfirst + t;
     const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
-    // Q row -> core tiles: row r, dims 8c .. 8c + 7 at ((r / 8) * 8 + c) * 128 + (r % 8) * 16.
     {
-      const uint4* src = reinterpret_cast<const uint4*>(a.q + grow * 64);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
-      }
+      load_q_row<GLUE>(a, sQ, r, row_ok, t0 + (row_ok ? t : 0), 4 * h + j);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -562,7 +673,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     if (!*reinterpret_cast<volatile int*>(&s_abort)) {
       tc_fence_after();
       const float l = sL[r];
-      if (a.splits > 1) {   // this split's unnormalised accumulator, running max and sum
+      if (SPLIT) {   // this split's unnormalised accumulator, running max and sum
         float* prow = a.part + (grow * a.splits + blockIdx.z) * kPfPart;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -580,22 +691,17 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+      const bool gated = GLUE && a.gate != nullptr;
+      const __half2 g2 = GLUE ? gate_half2(a, t0 + (row_ok ? t : 0), 4 * h + j) : __float2half2_rn(1.f);
 #pragma unroll
-      for (int c = 0; c < 4 && a.splits == 1; ++c) {
+      for (int c = 0; c < 4 && !SPLIT; ++c) {
         uint32_t rr[16];
         tmem_ld16(lane_base + 192 + 16 * c, rr);
         tmem_wait_ld();
         reg_fence16(rr);
         if (row_ok) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint4 v;
-            v.x = pack_half2(__uint_as_float(rr[8 * hh]) * inv, __uint_as_float(rr[8 * hh + 1]) * inv);
-            v.y = pack_half2(__uint_as_float(rr[8 * hh + 2]) * inv, __uint_as_float(rr[8 * hh + 3]) * inv);
-            v.z = pack_half2(__uint_as_float(rr[8 * hh + 4]) * inv, __uint_as_float(rr[8 * hh + 5]) * inv);
-            v.w = pack_half2(__uint_as_float(rr[8 * hh + 6]) * inv, __uint_as_float(rr[8 * hh + 7]) * inv);
-            dst[2 * c + hh] = v;
-          }
+          dst[2 * c] = out_pack8(rr, inv, g2, gated);
+          dst[2 * c + 1] = out_pack8(rr + 8, inv, g2, gated);
         }
       }
     }
@@ -758,29 +864,36 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
 }
 
 inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st) {
-  static bool done[2][64];
+  static bool done[8][64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LFM3A_ECUDA;
   const dim3 grid(a.qtiles, a.g.kv_heads, a.splits);
+  const bool split = a.splits > 1, glue = a.q_norm || a.rope || a.gate;
+  auto run = [&](auto kernel, int request, int threads, int slot) -> bool {
+    if (!done[slot][dev]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, request) != cudaSuccess ||
+          cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+        return false;
+      done[slot][dev] = true;
+    }
+    launch_pdl(kernel, grid, threads, request, st, a);
+    return true;
+  };
+  using LI = PfLayout<true>;
+  using LE = PfLayout<false>;
+  bool ok;
   if (i8) {
-    if (!done[1][dev]) {
-      if (cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               PfLayout<true>::kRequest) != cudaSuccess ||
-          cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
-        return LFM3A_ECUDA;
-      done[1][dev] = true;
-    }
-    launch_pdl(prefill_kernel<true>, grid, PfLayout<true>::kThreads, PfLayout<true>::kRequest, st, a);
+    if (split) ok = glue ? run(prefill_kernel<true, true, true>, LI::kRequest, LI::kThreads, 7)
+                         : run(prefill_kernel<true, true, false>, LI::kRequest, LI::kThreads, 6);
+    else ok = glue ? run(prefill_kernel<true, false, true>, LI::kRequest, LI::kThreads, 5)
+                   : run(prefill_kernel<true, false, false>, LI::kRequest, LI::kThreads, 4);
   } else {
-    if (!done[0][dev]) {
-      if (cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               PfLayout<false>::kRequest) != cudaSuccess ||
-          cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
-        return LFM3A_ECUDA;
-      done[0][dev] = true;
-    }
-    launch_pdl(prefill_kernel<false>, grid, PfLayout<false>::kThreads, PfLayout<false>::kRequest, st, a);
+    if (split) ok = glue ? run(prefill_kernel<false, true, true>, LE::kRequest, LE::kThreads, 3)
+                         : run(prefill_kernel<false, true, false>, LE::kRequest, LE::kThreads, 2);
+    else ok = glue ? run(prefill_kernel<false, false, true>, LE::kRequest, LE::kThreads, 1)
+                   : run(prefill_kernel<false, false, false>, LE::kRequest, LE::kThreads, 0);
   }
+  if (!ok) return LFM3A_ECUDA;
   return cudaGetLastError() == cudaSuccess ? LFM3A_OK : LFM3A_ELAUNCH;
 }
 
@@ -811,12 +924,19 @@ inline int prefill_splits_for(int tokens, int kv_heads, int context, int window,
   return best;
 }
 
-// splits > 1: part receives [tokens * q_heads][splits][kPfPart] partials for the combine.
-inline int launch_prefill(const KvGeom& g, const __half* q, int tokens, int q_heads, int context, int window, bool exact,
-                          __half* out, int splits, float* part, cudaStream_t st) {
+// splits > 1: part receives [tokens * q_heads][splits][kPfPart] partials for the combine (and the gate,
+// if any, is left to prefill_gate_kernel after it).
+inline int launch_prefill(const KvGeom& g, const __half* q, int64_t q_stride, const __half* q_norm, const __half* rope,
+                          const __half* gate, int64_t gate_stride, int tokens, int q_heads, int context, int window,
+                          bool exact, __half* out, int splits, float* part, cudaStream_t st) {
   PrefillArgs a;
   a.g = g;
   a.q = q;
+  a.q_stride = q_stride;
+  a.q_norm = q_norm;
+  a.rope = rope;
+  a.gate = splits > 1 ? nullptr : gate;
+  a.gate_stride = gate_stride;
   a.out = out;
   a.part = part;
   a.T = tokens;

@@ -80,6 +80,8 @@ SIGNATURES = {
     "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
     "lfm3a_prefill_splits": (_I, [_I, _I, _I, _I, _I]),
     "lfm3a_prefill_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "lfm3a_prefill_attention_fused": (_I, [ctypes.POINTER(KvView), _P, _I64, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _P,
+                                           _P, _SZ, _P]),
     "lfm3a_quantize_p_u8": (_I, [_P, _I, _P, _P, _P]),
     "lfm3a_gather_region_bytes": (_SZ, [_I, _I, _I]),
     "lfm3a_gather_region_alloc": (_I, [_I, _I, _I, ctypes.POINTER(_P)]),
@@ -250,19 +252,28 @@ class LayerCache:
                                           _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
         return out
 
-    def prefill(self, q, context: int, window: int = 0, exact: bool = False, out=None, workspace=None, stream=None):
-        """Causal prefill attention of q ([T][q_heads][head_dim] fp16) at positions context.."""
+    def prefill(self, q, context: int, window: int = 0, exact: bool = False, out=None, workspace=None, stream=None,
+                q_norm=None, rope=None, gate=None, q_heads: int | None = None):
+        """Causal prefill attention of q at positions context... q: [T][q_heads][head_dim] fp16, or with
+        q_heads given any [T][>= q_heads * head_dim] row-strided view of raw projections. q_norm (fp16 [64]),
+        rope (a rope_table on the device) and gate (fp16 logits [T][>= q_heads], row-strided) fuse the
+        reference's q_norm_rope and gate_mul around the attention."""
         import torch
 
-        t, qh, d = q.shape
+        d = self.head_dim
+        t = q.shape[0]
+        qh = q.shape[1] if q_heads is None else q_heads
+        q_stride = q.stride(0)
         if out is None:
-            out = torch.empty_like(q)
+            out = torch.empty((t, qh, d), dtype=torch.float16, device=q.device)
         need = lib().lfm3a_prefill_workspace_bytes(t, qh, d)
         if workspace is None and need:
             workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
-        _check(lib().lfm3a_prefill_attention(ctypes.byref(self.view), _ptr(q), t, qh, context, window, int(exact),
-                                             _ptr(out), _ptr(workspace), ws_bytes, _stream(stream)))
+        gate_stride = gate.stride(0) if gate is not None else 0
+        _check(lib().lfm3a_prefill_attention_fused(ctypes.byref(self.view), _ptr(q), q_stride, _ptr(q_norm),
+                                                   _ptr(rope), _ptr(gate), gate_stride, t, qh, context, window,
+                                                   int(exact), _ptr(out), _ptr(workspace), ws_bytes, _stream(stream)))
         return out
 
     # -------------------------------------------------------------- host-side inspection

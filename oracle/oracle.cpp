@@ -529,6 +529,21 @@ void orc_prefill_exact(const uint16_t* q, int T, int context, int q_heads, int k
                      std::max(1, splits), out);
 }
 
+// q_norm_rope (ops.hip:202-210): per (token, head) RMS norm with qnorm (or none), RoPE at position
+// context + t (or none), each step rounded to fp16; the same steps as the K side (norm_rope_head).
+void orc_q_norm_rope(const uint16_t* q, int T, int q_heads, int head_dim, int64_t q_stride, const uint16_t* qnorm,
+                     const uint16_t* rope, int context, uint16_t* out) {
+  const int D = head_dim;
+#pragma omp parallel for
+  for (int r = 0; r < T * q_heads; ++r) {
+    const int t = r / q_heads, h = r % q_heads;
+    float x[256], o[256];
+    for (int d = 0; d < D; ++d) x[d] = orc_f16_to_f32(q[(size_t)t * q_stride + (size_t)h * D + d]);
+    norm_rope_head(x, D, rope ? rope + (size_t)(context + t) * D : nullptr, qnorm, o);
+    for (int d = 0; d < D; ++d) out[(size_t)r * D + d] = orc_f32_to_f16(o[d]);
+  }
+}
+
 int orc_accept(const int32_t* best, const int32_t* tokens, int m) {
   int acc = 0;
   for (int t = 0; t < m - 1; ++t) {

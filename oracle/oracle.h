@@ -93,6 +93,12 @@ void orc_prefill_i8pv(const uint16_t* q, int T, int context, int q_heads, int kv
 void orc_prefill_exact(const uint16_t* q, int T, int context, int q_heads, int kv_heads, int head_dim,
                        const uint16_t* K, const uint16_t* V, int window, int row_step, int splits, float* out);
 
+/* q_norm_rope (ops.hip:202-210): q rows at q + t * q_stride + h * head_dim, RMS-normalised with qnorm
+ * (NULL: none) and rotated at position context + t (NULL rope: none), each step rounded to fp16. out: fp16
+ * [T][q_heads][head_dim]. */
+void orc_q_norm_rope(const uint16_t* q, int T, int q_heads, int head_dim, int64_t q_stride, const uint16_t* qnorm,
+                     const uint16_t* rope, int context, uint16_t* out);
+
 /* Acceptance of a verify round (dspark.hip:2848-2895): the longest prefix t with best[t] == tokens[t+1],
  * then commit = accepted + 1 positions. Returns commit. */
 int orc_accept(const int32_t* best, const int32_t* tokens, int m);

@@ -33,6 +33,7 @@ _SIGS = {
     "orc_attention_f64": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
     "orc_prefill_i8pv": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _I, _P]),
     "orc_prefill_exact": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
+    "orc_q_norm_rope": (None, [_P, _I, _I, _I, ctypes.c_int64, _P, _P, _I, _P]),
     "orc_accept": (_I, [_P, _P, _I]),
     "orc_set_threads": (None, [_I]),
     "orc_get_threads": (_I, []),
@@ -190,6 +191,27 @@ def prefill_exact(q, context: int, K, V, window: int = 0, row_step: int = 1, spl
     out = np.zeros((t, qh, d), dtype=np.float32)
     lib().orc_prefill_exact(qp, t, context, qh, kvh, d, kp, vp, window, row_step, splits, out.ctypes.data)
     return out
+
+
+def q_norm_rope(q, q_heads: int, head_dim: int, context: int, qnorm=None, rope=None) -> np.ndarray:
+    """ops.hip:202-210. q: [T][>= q_heads * head_dim] fp16 rows; returns fp16 [T][q_heads][head_dim]."""
+    q = np.ascontiguousarray(np.asarray(q, dtype=np.float16).reshape(q.shape[0], -1))
+    t = q.shape[0]
+    out = np.empty((t, q_heads, head_dim), dtype=np.float16)
+    qn = None if qnorm is None else np.ascontiguousarray(np.asarray(qnorm).view(np.uint16))
+    rp = None if rope is None else np.ascontiguousarray(np.asarray(rope).view(np.uint16))
+    lib().orc_q_norm_rope(q.ctypes.data, t, q_heads, head_dim, q.shape[1], None if qn is None else qn.ctypes.data,
+                          None if rp is None else rp.ctypes.data, context, out.ctypes.data)
+    return out
+
+
+def gate_mul(att, gate) -> np.ndarray:
+    """ops.hip:254-264: the attention output rounded to fp16, times fp16(sigmoid(logit)) per (token, head),
+    rounded to fp16 again (the product of two fp16 values is exact in fp32, so one rounding). att: fp32 or
+    fp16 [T][QH][D]; gate: fp16 [T][>= QH]. sigmoid in fp32 with the host's expf."""
+    g = np.asarray(gate, dtype=np.float16)[:, :att.shape[1]].astype(np.float32)
+    s = (np.float32(1.0) / (np.float32(1.0) + np.exp(-g))).astype(np.float32).astype(np.float16)
+    return (np.asarray(att).astype(np.float16).astype(np.float32) * s.astype(np.float32)[..., None]).astype(np.float16)
 
 
 def accept(best, tokens) -> int:

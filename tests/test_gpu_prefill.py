@@ -109,3 +109,34 @@ def test_prefill_key_splits(la, orc, synth, cuda, context, T, window, exact):
         v8, vs = orc.quantize_v8(case["V"], n)
         emu = orc.prefill_i8pv(q, context, case["K"], v8, vs, window=window, splits=splits)
         assert rel_err(got, emu) < TOL_I8
+
+
+@pytest.mark.parametrize("exact", [True, False])
+@pytest.mark.parametrize("context,T", [(37, 100), (3000, 64)])
+def test_prefill_fused_glue(la, orc, synth, cuda, context, T, exact):
+    """lfm3a_prefill_attention_fused: raw row-strided query projections, normalised and rotated in the
+    kernel, give bit for bit the plain call on the oracle's q_norm_rope output; the fused output gate equals
+    gate_mul of that output, up to one fp16 ulp where the device's and the host's expf round the sigmoid
+    differently. (3000, 64) runs split along the keys, where the gate is applied after the combine."""
+    case = synth.prefill_case(90 + T, context + T)
+    cache = la.LayerCache(la.MODE_F16, 8, 64, context + T + 64, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    s = synth.Stream(95)
+    width = 32 * 64 + 3 * 64   # a projection row: the 32 query heads, then other columns
+    f = s.normal_f16((T, width))
+    qnorm = (1.0 + 0.25 * s.normal_f16((64,)).astype(np.float32)).astype(np.float16)
+    table = orc.rope_table(1e6, 1.0, 64, context + T + 1)
+    gate = s.normal_f16((T, 40))
+    fd, qn_d, rope_d = dev(f, cuda), dev(qnorm, cuda), dev(table.view(np.float16), cuda)
+    fused = cache.prefill(fd[:, :32 * 64], context, exact=exact, q_norm=qn_d, rope=rope_d, q_heads=32)
+    gated = cache.prefill(fd[:, :32 * 64], context, exact=exact, q_norm=qn_d, rope=rope_d, gate=dev(gate, cuda),
+                          q_heads=32)
+    q_ref = orc.q_norm_rope(f, 32, 64, context, qnorm=qnorm, rope=table)
+    plain = cache.prefill(dev(q_ref, cuda), context, exact=exact)
+    la.sync()
+    plain_np = plain.cpu().numpy()
+    assert np.array_equal(fused.cpu().numpy().view(np.uint16), plain_np.view(np.uint16))
+    want = orc.gate_mul(plain_np, gate)
+    got = gated.cpu().numpy()
+    ulps = np.abs(got.view(np.int16).astype(np.int32) - want.view(np.int16).astype(np.int32))
+    assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3
