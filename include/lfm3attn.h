@@ -165,6 +165,19 @@ int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_he
 int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
                   const void* gate, void* out, void* stream);
 
+/* ---------------------------------------------------------------- drafter ring attention
+ * The drafter's KV ring (kernels/dspark.hip:69-70,1070-1412 attention_pass<1, true>, called at :2527):
+ * the drafter keeps its context K/V in a ring of pages, logical block b in ring block b mod ring_blocks,
+ * and attends m draft queries over the ring's live context [ctx_lo, ctx_len) plus all m drafts' own keys,
+ * not causal among the drafts. Here the ring is an ordinary view whose block table wraps: lfm3a_ring_table
+ * fills table[b] = b mod ring_blocks (host memory; copy it to the device table), and lfm3a_kv_append /
+ * lfm3a_kv_truncate work on it unchanged (positions ctx_len .. for the drafts). The live context plus the
+ * drafts must fit in the ring: ctx_len + m - ctx_lo + 64 <= ring_blocks * 32 (whole int8 V blocks). */
+int lfm3a_ring_table(int ring_blocks, int logical_blocks, int32_t* table);
+/* out: fp16 [m][q_heads][head_dim]; workspace as lfm3a_verify_attention (lfm3a_verify_workspace_bytes). */
+int lfm3a_ring_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_lo, int ctx_len,
+                         void* out, void* workspace, size_t workspace_bytes, int splits, void* stream);
+
 /* ---------------------------------------------------------------- prefill attention */
 /* Workspace that lets lfm3a_prefill_attention split a chunk's keys at any context (0 when a chunk of this
  * many tokens already fills the GPU). */

@@ -140,7 +140,7 @@ int launch_combine(const float* part, int rows, int splits, int head_dim, int64_
 // lfm3a_verify_attention_gather (gather set: the combine scatters the output to the ranks' regions).
 int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int kv_begin, int kv_end, int ctx_len,
                int window, const void* gate, __half* out16, float* out32, void* workspace, size_t workspace_bytes,
-               int splits, cudaStream_t st, GatherOut* gather = nullptr) {
+               int splits, cudaStream_t st, GatherOut* gather = nullptr, bool causal = true) {
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
   const lfm3a_kv_layout& L = kv->layout;
@@ -172,6 +172,7 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   if (splits <= 0) splits = verify_splits_for(L.kv_heads, a.t_total * tile_keys, 1, 0, current_sm_count());
   a.splits = std::min(splits, a.t_total);
   a.qk_scale = 0.125f * kLog2e;
+  a.causal = causal ? 1 : 0;
   const int rows = m * q_heads;
   // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
   if (a.splits == 1 && out32) {
@@ -404,6 +405,20 @@ int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_he
                          void* stream) {
   return run_verify(kv, q, m, q_heads, kv_begin, kv_end, ctx_len, window, nullptr, nullptr, partial, workspace,
                     workspace_bytes, splits, as_stream(stream));
+}
+
+int lfm3a_ring_table(int ring_blocks, int logical_blocks, int32_t* table) {
+  if (ring_blocks < 2 || ring_blocks % 2 != 0 || logical_blocks < 0 || (!table && logical_blocks > 0))
+    return fail(LFM3A_EINVAL, "a ring needs an even number of blocks (whole 64-token int8 V blocks)");
+  for (int b = 0; b < logical_blocks; ++b) table[b] = b % ring_blocks;
+  return LFM3A_OK;
+}
+
+int lfm3a_ring_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_lo, int ctx_len,
+                         void* out, void* workspace, size_t workspace_bytes, int splits, void* stream) {
+  if (ctx_lo < 0 || ctx_lo > ctx_len) return fail(LFM3A_EINVAL, "ctx_lo must lie in [0, ctx_len]");
+  return run_verify(kv, q, m, q_heads, ctx_lo, ctx_len + m, ctx_len, 0, nullptr, static_cast<__half*>(out), nullptr,
+                    workspace, workspace_bytes, splits, as_stream(stream), nullptr, false);
 }
 
 size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim) {

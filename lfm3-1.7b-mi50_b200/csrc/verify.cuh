@@ -30,6 +30,7 @@ struct VerifyArgs {
   int m, q_heads, ctx_len, window, start, splits;
   int kv_begin, kv_end; // the keys this cache holds: [kv_begin, kv_end)
   int t_begin, t_total; // 64-key tiles of the whole range
+  int causal;           // 1: draft t sees drafts <= t (verify); 0: every draft (the drafter's ring attention)
   float qk_scale;       // (1 / sqrt(64)) * log2(e)
 };
 
@@ -187,7 +188,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
           const int kpos = k0 + k;
           bool valid;
           if (kpos < a.ctx_len) valid = kpos >= a.start && kpos < a.kv_end && (a.window == 0 || kpos > qpos - a.window);
-          else valid = kpos <= qpos && kpos < a.kv_end;
+          else valid = (kpos <= qpos || !a.causal) && kpos < a.kv_end;
           x[k] = (valid && row_ok) ? x[k] : -INFINITY;
         }
       }
@@ -554,7 +555,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
           const int kpos = k0 + k;
           bool valid;
           if (kpos < a.ctx_len) valid = kpos >= a.start && kpos < a.kv_end && (a.window == 0 || kpos > qpos - a.window);
-          else valid = kpos <= qpos && kpos < a.kv_end;
+          else valid = (kpos <= qpos || !a.causal) && kpos < a.kv_end;
           x[k] = (valid && row_ok) ? x[k] : -INFINITY;
         }
       }

@@ -77,6 +77,8 @@ SIGNATURES = {
     "lfm3a_verify_attention_static": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _I, _P]),
     "lfm3a_verify_partial": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_combine": (_I, [_P, _I, _I, _I, _I64, _I64, _P, _P, _P]),
+    "lfm3a_ring_table": (_I, [_I, _I, _P]),
+    "lfm3a_ring_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
     "lfm3a_prefill_splits": (_I, [_I, _I, _I, _I, _I]),
     "lfm3a_prefill_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
@@ -234,6 +236,25 @@ class LayerCache:
                                             _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
         return out
 
+    def ring_attention(self, q, ctx_lo: int, ctx_len: int, out=None, workspace=None, splits: int = 0, stream=None):
+        """The drafter's ring attention (dspark.hip:1070-1412 with RING): q ([m][q_heads][head_dim] fp16) over
+        the live context [ctx_lo, ctx_len) and all m drafts (not causal among them). The cache's block table
+        must wrap (ring_table)."""
+        import torch
+
+        m, qh, d = q.shape
+        if out is None:
+            out = torch.empty_like(q)
+        if splits <= 0:   # as verify over the live range
+            splits = verify_splits(self.layout, ctx_len - ctx_lo, m, 0)
+        if workspace is None and splits > 1:
+            need = lib().lfm3a_verify_workspace_bytes(m, qh, d, splits)
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib().lfm3a_ring_attention(ctypes.byref(self.view), _ptr(q), m, qh, ctx_lo, ctx_len, _ptr(out),
+                                          _ptr(workspace), ws_bytes, splits, _stream(stream)))
+        return out
+
     def verify_partial(self, q, kv_begin: int, kv_end: int, ctx_len: int, window: int = 0, out=None, workspace=None,
                        splits: int = 0, stream=None):
         """This cache shard's log-sum-exp partial [m * q_heads][head_dim + 2] over positions [kv_begin, kv_end)."""
@@ -341,6 +362,13 @@ class PrefixCache:
 
     def sequence(self, salt: str = "") -> "PrefixSeq":
         return PrefixSeq(self, salt)
+
+
+def ring_table(ring_blocks: int, logical_blocks: int) -> np.ndarray:
+    """Block table of a ring view: logical block b in ring block b mod ring_blocks (dspark.hip:69-70)."""
+    out = np.empty(logical_blocks, dtype=np.int32)
+    _check(lib().lfm3a_ring_table(ring_blocks, logical_blocks, out.ctypes.data))
+    return out
 
 
 def prefix_salt(salt: str) -> int:

@@ -117,3 +117,10 @@ def test_prefill_split_choice(la):
     assert sp(32, 10 ** 6, 300) == 1     # a 300-token window: bands of 6 tiles
     assert sp(32, 10 ** 6, 4096) == 8    # 4127 keys: 65 tiles, at most 8 splits
     assert la.lib().lfm3a_prefill_splits(-1, 32, 0, 0, 148) == la.EINVAL
+
+
+def test_ring_table(la):
+    t = la.ring_table(6, 20)
+    assert list(t) == [b % 6 for b in range(20)]
+    with pytest.raises(la.LFM3AError):
+        la.ring_table(5, 4)   # whole 64-token int8 V blocks: an even ring

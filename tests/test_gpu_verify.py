@@ -164,3 +164,33 @@ def test_decode_full_size(la, orc, synth, cuda, ctx_len, seed):
     la.sync()
     got = out.float().cpu().numpy()
     assert rel_err(got, orc.attention_f64(case["Q"], ctx_len, K, V, ctx_len + 1)) < TOL
+
+
+@pytest.mark.parametrize("m", [16, 24])
+def test_ring_attention(la, orc, synth, cuda, m):
+    """The drafter's KV ring (dspark.hip:1070-1412 with RING): 24 ring blocks (768 positions) take a
+    1500-token context appended in chunks through the wrapping table (older pages are overwritten), then m
+    drafts; the drafts attend the live 600 tokens [ctx_len - 600, ctx_len) and all m drafts, not causally.
+    Checked against exact fp64 attention over those keys."""
+    ring_blocks, ctx_len, live = 24, 1500, 600
+    table = la.ring_table(ring_blocks, (ctx_len + m + 31) // 32 + 1)
+    cache = la.LayerCache(la.MODE_F16, 8, 64, len(table) * 32, device=cuda, block_table=dev(table, cuda),
+                          pool_blocks=ring_blocks)
+    case = synth.verify_case(50 + m, ctx_len, m)
+    rope_np = orc.rope_table(1e6, 1.0, 64, ctx_len + m + 1)
+    rope = dev(rope_np.view(np.float16), cuda)
+    for p0 in range(0, ctx_len, 250):
+        cache.append(dev(case["K"][p0:p0 + 250], cuda), dev(case["V"][p0:p0 + 250], cuda), p0, rope=rope)
+    cache.append(dev(case["newK"], cuda), dev(case["newV"], cuda), ctx_len, rope=rope)
+    ctx_lo = ctx_len - live
+    out = cache.ring_attention(dev(case["Q"], cuda), ctx_lo, ctx_len)
+    la.sync()
+    K, V = orc.kv_append_f16(np.concatenate([case["K"], case["newK"]]), np.concatenate([case["V"], case["newV"]]), 0,
+                             rope=rope_np)
+    kh = np.repeat(K[ctx_lo:].astype(np.float64), 4, axis=1)   # query head 4 h + j reads kv head h
+    vh = np.repeat(V[ctx_lo:].astype(np.float64), 4, axis=1)
+    s = np.einsum("mhd,nhd->hmn", case["Q"].astype(np.float64), kh) / 8.0
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    want = np.einsum("hmn,nhd->mhd", p, vh)
+    assert rel_err(out.float().cpu().numpy(), want) < TOL
