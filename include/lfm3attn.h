@@ -92,7 +92,8 @@ int lfm3a_sync(void* stream, int timeout_ms);
  * k, v: device fp16, token t head h at k + t * token_stride + h * head_dim (token_stride 0 means
  * kv_heads * head_dim; the reference reads them out of the fused projection with f_stride).
  * rope: device fp16 table [positions][head_dim] (lfm3a_rope_table) applied to K at each position,
- * or NULL. k_norm: device fp16 RMS-norm weights [head_dim] applied to K first (eps 1e-5), or NULL.
+ * or NULL; it must hold rows up to pos0 + n - 1 (the table's length is not passed, as in the reference's
+ * KvArgs, so rows past it are read as they lie). k_norm: device fp16 RMS-norm weights [head_dim] applied to K first (eps 1e-5), or NULL.
  * MODE_F16 also re-quantises the int8 V of every 64-token block the append touches, over the
  * tokens below pos0 + n. The block-table entries of all positions written must be in place. */
 int lfm3a_kv_append(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride, int pos0, int n,
@@ -164,6 +165,16 @@ int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_he
  * logits or NULL. Merges the partials of one GPU's splits and the partials gathered from several GPUs. */
 int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
                   const void* gate, void* out, void* stream);
+
+/* One DSpark verify round's device work in one call: lfm3a_kv_append of the m drafts (k, v, token_stride,
+ * rope, k_norm as there) at positions ctx_len .. ctx_len + m - 1, then lfm3a_verify_attention of q over
+ * them (the reference's query_fresh then attention phases of one launch, kernels/dspark.hip:999-1061,
+ * 1488-2185). For m <= 16 the append runs inside the attention kernel, in the CTA of each kv head whose
+ * keys include the drafts (when the split leaves it every 64-token block they touch; else the append
+ * kernel runs first); the cache bytes and the output are the same as the two calls'. */
+int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride, const void* rope,
+                       const void* k_norm, const void* q, int m, int q_heads, int ctx_len, int window, const void* gate,
+                       void* out, void* workspace, size_t workspace_bytes, int splits, void* stream);
 
 /* ---------------------------------------------------------------- drafter ring attention
  * The drafter's KV ring (kernels/dspark.hip:69-70,1070-1412 attention_pass<1, true>, called at :2527):

@@ -89,19 +89,17 @@ __device__ __forceinline__ void norm_rope_pairs(const AppendArgs& a, const __hal
   }
 }
 
-// MODE_F16 append, one block of 256 threads per (64-token block, kv head) the new tokens touch. Each warp
-// takes new tokens in turn: k-norm + RoPE, fp16 K and V stores, and V kept in shared memory beside the
-// block's earlier tokens (read back from the pool). The block's int8 V and scale then come from shared
-// memory: absmax over the live tokens (those below pos0 + n), scale max(amax/127, 1e-6), rounding half away
-// from zero, zeros past the live tokens; a page past the sequence end is not touched.
-template <int D>
-__global__ __launch_bounds__(256) void kv_append_f16_kernel(AppendArgs a) {
+// MODE_F16 append of one (64-token block qb, kv head h) the new tokens touch, by 256 threads (tid 0..255)
+// that `sync` brings together. Each warp takes new tokens in turn: k-norm + RoPE, fp16 K and V stores, and V
+// kept in shared memory (sv: 64 x D halves, red: 8 floats) beside the block's earlier tokens (read back from
+// the pool). The block's int8 V and scale then come from shared memory: absmax over the live tokens (those
+// below pos0 + n), scale max(amax/127, 1e-6), rounding half away from zero, zeros past the live tokens; a
+// page past the sequence end is not touched.
+template <int D, typename Sync>
+__device__ __forceinline__ void append_quant_block(const AppendArgs& a, int qb, int h, int tid, __half* sv, float* red,
+                                                   Sync sync) {
   using S = F16Section<D>;
   constexpr int J = D / 64, HALF = D / 2;
-  __shared__ __half sv[kQuantBlock * D];   // [token of the block][dim]
-  __shared__ float red[8];
-  pdl_wait();
-  const int qb = a.pos0 / kQuantBlock + blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int t0 = qb * kQuantBlock, len = a.pos0 + a.n;
   const int lo = max(a.pos0, t0), hi = min(len, t0 + kQuantBlock), live = hi - t0;
@@ -110,7 +108,6 @@ __global__ __launch_bounds__(256) void kv_append_f16_kernel(AppendArgs a) {
 #pragma unroll
   for (int p = 0; p < 2; ++p)
     sec[p] = p < pages ? a.g.pool + phys_block(a.g, qb * 2 + p) * a.g.block_bytes + h * a.g.head_bytes : nullptr;
-  pdl_trigger();
   for (int t = lo + warp; t < hi; t += 8) {
     const int i = t - a.pos0, b = t - t0;
     const __half* ks = a.k + (int64_t)i * a.stride + h * D;
@@ -142,13 +139,13 @@ __global__ __launch_bounds__(256) void kv_append_f16_kernel(AppendArgs a) {
       if (b < old) sv[b * D + d] = V[i];
     }
   }
-  __syncthreads();
+  sync();
   float amax = 0.f;
   for (int i = tid; i < live * D; i += 256) amax = fmaxf(amax, fabsf(__half2float(sv[i])));
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if (lane == 0) red[warp] = amax;
-  __syncthreads();
+  sync();
   amax = red[0];
 #pragma unroll
   for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
@@ -169,6 +166,16 @@ __global__ __launch_bounds__(256) void kv_append_f16_kernel(AppendArgs a) {
     }
     if (tid == 0) *reinterpret_cast<float*>(sec[p] + S::kOffScale) = scale;
   }
+}
+
+// MODE_F16 append, one block of 256 threads per (64-token block, kv head) the new tokens touch.
+template <int D>
+__global__ __launch_bounds__(256) void kv_append_f16_kernel(AppendArgs a) {
+  __shared__ __half sv[kQuantBlock * D];   // [token of the block][dim]
+  __shared__ float red[8];
+  pdl_wait();
+  pdl_trigger();
+  append_quant_block<D>(a, a.pos0 / kQuantBlock + blockIdx.x, blockIdx.y, threadIdx.x, sv, red, [] { __syncthreads(); });
 }
 
 // The reference's int8 record append (kernels/ops.hip:213-251): per (token, kv head) scale

@@ -138,9 +138,14 @@ int launch_combine(const float* part, int rows, int splits, int head_dim, int64_
 
 // Shared body of lfm3a_verify_attention (out16 set), lfm3a_verify_partial (out32 set) and
 // lfm3a_verify_attention_gather (gather set: the combine scatters the output to the ranks' regions).
+int launch_append(const lfm3a_kv_view* kv, const AppendArgs& a, cudaStream_t st);
+
+// app: a verify round's drafts to append first (at ctx_len). Fused into verify_m64_kernel when its last split
+// holds every 64-token block they touch; else launched as the append kernel before the attention.
 int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int kv_begin, int kv_end, int ctx_len,
                int window, const void* gate, __half* out16, float* out32, void* workspace, size_t workspace_bytes,
-               int splits, cudaStream_t st, GatherOut* gather = nullptr, bool causal = true) {
+               int splits, cudaStream_t st, GatherOut* gather = nullptr, bool causal = true,
+               const AppendArgs* app = nullptr) {
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
   const lfm3a_kv_layout& L = kv->layout;
@@ -173,6 +178,25 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   a.splits = std::min(splits, a.t_total);
   a.qk_scale = 0.125f * kLog2e;
   a.causal = causal ? 1 : 0;
+  a.append = 0;
+  a.lighten = 0;
+  if (app) {
+    // The appending split gives up kAppendTiles tiles of attention (the append takes about that long) when
+    // it keeps at least two; it must hold every 64-token block the drafts touch.
+    constexpr int kAppendTiles = 2;
+    const int lighten = a.splits > 1 && a.t_total / a.splits >= kAppendTiles + 2 ? kAppendTiles : 0;
+    const int span = a.t_total + lighten;
+    const int last_tile0 = a.t_begin + std::min(a.t_total, (int)((int64_t)span * (a.splits - 1) / a.splits));
+    const bool fuse = m <= 16 && last_tile0 * tile_keys <= app->pos0 / kQuantBlock * kQuantBlock;
+    if (fuse) {
+      a.append = 1;
+      a.lighten = lighten;
+      a.app = *app;
+    } else {
+      rc = launch_append(kv, *app, st);
+      if (rc != LFM3A_OK) return rc;
+    }
+  }
   const int rows = m * q_heads;
   // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
   if (a.splits == 1 && out32) {
@@ -299,6 +323,27 @@ int lfm3a_sync(void* stream, int timeout_ms) {
   return LFM3A_OK;
 }
 
+}  // extern "C"
+
+namespace {
+int launch_append(const lfm3a_kv_view* kv, const AppendArgs& a, cudaStream_t st) {
+  const int D = kv->layout.head_dim, H = kv->layout.kv_heads;
+  if (kv->layout.mode == LFM3A_MODE_F16) {
+    // One block per (64-token block, kv head) the new tokens touch; it also rewrites that block's int8 V.
+    const dim3 grid((a.pos0 + a.n - 1) / kQuantBlock - a.pos0 / kQuantBlock + 1, H);
+    if (D == 64) launch_pdl(kv_append_f16_kernel<64>, grid, 256, 0, st, a);
+    else launch_pdl(kv_append_f16_kernel<128>, grid, 256, 0, st, a);
+    return check_launch("kv_append_f16_kernel");
+  }
+  const int blocks = (a.n * H + 3) / 4;
+  if (D == 64) launch_pdl(kv_append_i8rec_kernel<64>, blocks, 128, 0, st, a);
+  else launch_pdl(kv_append_i8rec_kernel<128>, blocks, 128, 0, st, a);
+  return check_launch("kv_append_i8rec_kernel");
+}
+}  // namespace
+
+extern "C" {
+
 int lfm3a_kv_append(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride, int pos0, int n,
                     const void* rope, const void* k_norm, void* stream) {
   int rc = check_view(kv);
@@ -317,18 +362,7 @@ int lfm3a_kv_append(const lfm3a_kv_view* kv, const void* k, const void* v, int64
   a.stride = token_stride;
   a.pos0 = pos0;
   a.n = n;
-  const cudaStream_t st = as_stream(stream);
-  const int blocks = (n * H + 3) / 4;
-  if (kv->layout.mode == LFM3A_MODE_F16) {
-    // One block per (64-token block, kv head) the new tokens touch; it also rewrites that block's int8 V.
-    const dim3 grid((pos0 + n - 1) / kQuantBlock - pos0 / kQuantBlock + 1, H);
-    if (D == 64) launch_pdl(kv_append_f16_kernel<64>, grid, 256, 0, st, a);
-    else launch_pdl(kv_append_f16_kernel<128>, grid, 256, 0, st, a);
-    return check_launch("kv_append_f16_kernel");
-  }
-  if (D == 64) launch_pdl(kv_append_i8rec_kernel<64>, blocks, 128, 0, st, a);
-  else launch_pdl(kv_append_i8rec_kernel<128>, blocks, 128, 0, st, a);
-  return check_launch("kv_append_i8rec_kernel");
+  return launch_append(kv, a, as_stream(stream));
 }
 
 int lfm3a_kv_truncate(const lfm3a_kv_view* kv, int new_len, void* stream) {
@@ -405,6 +439,28 @@ int lfm3a_verify_partial(const lfm3a_kv_view* kv, const void* q, int m, int q_he
                          void* stream) {
   return run_verify(kv, q, m, q_heads, kv_begin, kv_end, ctx_len, window, nullptr, nullptr, partial, workspace,
                     workspace_bytes, splits, as_stream(stream));
+}
+
+int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride, const void* rope,
+                       const void* k_norm, const void* q, int m, int q_heads, int ctx_len, int window, const void* gate,
+                       void* out, void* workspace, size_t workspace_bytes, int splits, void* stream) {
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  const int D = kv->layout.head_dim, H = kv->layout.kv_heads;
+  if (!k || !v || m < 1 || ctx_len < 0) return fail(LFM3A_EINVAL, "bad round arguments");
+  if (token_stride == 0) token_stride = (int64_t)H * D;
+  if (token_stride < (int64_t)H * D) return fail(LFM3A_EINVAL, "token_stride smaller than kv_heads * head_dim");
+  AppendArgs app;
+  app.g = geom_of(kv);
+  app.k = static_cast<const __half*>(k);
+  app.v = static_cast<const __half*>(v);
+  app.rope = static_cast<const __half*>(rope);
+  app.knorm = static_cast<const __half*>(k_norm);
+  app.stride = token_stride;
+  app.pos0 = ctx_len;
+  app.n = m;
+  return run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, static_cast<__half*>(out), nullptr,
+                    workspace, workspace_bytes, splits, as_stream(stream), nullptr, true, &app);
 }
 
 int lfm3a_ring_table(int ring_blocks, int logical_blocks, int32_t* table) {

@@ -32,6 +32,9 @@ struct VerifyArgs {
   int t_begin, t_total; // 64-key tiles of the whole range
   int causal;           // 1: draft t sees drafts <= t (verify); 0: every draft (the drafter's ring attention)
   float qk_scale;       // (1 / sqrt(64)) * log2(e)
+  int append;           // verify_m64_kernel: the last split of each kv head first appends app (the drafts)
+  int lighten;          // with append: tiles of attention the last split leaves to the others (its append costs them)
+  AppendArgs app;
 };
 
 constexpr int kVerifyPart = 66;           // acc[64], max, sum
@@ -437,7 +440,7 @@ constexpr int kV6OffStage = 8192;          // after Q: 64 rows x 64 dims fp16; t
 constexpr int kV6PBuf = 16384;             // [warpgroup g][half h] 64 rows x 32 keys fp16, 4 KiB each
 constexpr int kV6OffP = kV6OffStage + 2 * kV6Stages * kV6Ring;
 constexpr int kV6OffBar = kV6OffP + 2 * kV6PBuf;
-constexpr int kV6Bars = 4 * kV6Stages + 2 + 4 + 2 + 2;   // K/V full/empty, s_full[2], p_full[2][2], pv_done[2], q_ready, drain
+constexpr int kV6Bars = 4 * kV6Stages + 2 + 4 + 2 + 3;   // K/V full/empty, s_full[2], p_full[2][2], pv_done[2], q_ready, drain, app_done
 constexpr int kV6OffTmemSlot = kV6OffBar + kV6Bars * 8;
 constexpr int kV6OffAbort = kV6OffTmemSlot + 4;
 constexpr int kV6Smem = kV6OffTmemSlot + 16;
@@ -462,12 +465,19 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
   uint64_t* pv_done = p_full + 4;
   uint64_t* q_ready = pv_done + 2;
   uint64_t* drain = q_ready + 1;
+  uint64_t* app_done = drain + 1;        // the fused append's stores are out (softmax warps -> producer)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kV6OffTmemSlot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y;
-  const int tile0 = a.t_begin + (int)((int64_t)a.t_total * split / a.splits);
-  const int ntiles = a.t_begin + (int)((int64_t)a.t_total * (split + 1) / a.splits) - tile0;
+  // The fused append (a verify round's drafts at ctx_len): the last split of each kv head, which the host
+  // guarantees holds every 64-token block the drafts touch, writes them before loading those tiles.
+  const bool appender = a.append && split == a.splits - 1;
+  // Splits share t_total + lighten tiles evenly; the last (the appender, when lighten > 0) holds lighten
+  // tiles fewer.
+  const int span = a.t_total + a.lighten;
+  const int tile0 = a.t_begin + min(a.t_total, (int)((int64_t)span * split / a.splits));
+  const int ntiles = a.t_begin + min(a.t_total, (int)((int64_t)span * (split + 1) / a.splits)) - tile0;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -485,6 +495,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
     }
     mbar_init(q_ready, 4);
     mbar_init(drain, 1);
+    mbar_init(app_done, kVfSoftmaxWarps);
     fence_barrier_init();
   }
   // Launched as a programmatic dependent: nothing global is touched, and no TMEM is taken, before the
@@ -520,6 +531,22 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
+    }
+    if (appender) {
+      // The drafts' K (RoPE) and V into their pages, and the int8 V of every 64-token block they touch, by
+      // the 256 softmax threads while the first K tile loads; the P buffers are the scratch (P is first
+      // written after this). The stores are handed to the producer's bulk copies through app_done.
+      __half* sv = reinterpret_cast<__half*>(sP);
+      float* red = reinterpret_cast<float*>(sP + kQuantBlock * 64 * sizeof(__half));
+      auto sync = [] { named_bar_sync(2, kVfSoftmaxWarps * 32); };
+      const int qb0 = a.app.pos0 / kQuantBlock, qb1 = (a.app.pos0 + a.app.n - 1) / kQuantBlock;
+      for (int qb = qb0; qb <= qb1; ++qb) {
+        append_quant_block<64>(a.app, qb, h, threadIdx.x, sv, red, sync);
+        sync();   // sv and red are reused by the next block, then by P
+      }
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(app_done);
     }
     const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
     const uint32_t o_col = 128 + 64 * g;
@@ -682,11 +709,18 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
     // at about the same time, and each load lands two tiles before its MMA wants it.
     {
       const int pv0 = a.kv_begin / kBlockTokens, pv1 = (a.kv_end - 1) / kBlockTokens;   // pages this cache holds
+      bool appended = !appender;
       auto load = [&](int jt, bool is_v) -> bool {
         const int st = jt % NS;
         uint64_t* emp = is_v ? v_empty : k_empty;
         uint64_t* ful = is_v ? v_full : k_full;
         if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&emp[st], (uint32_t)((jt / NS) - 1) & 1u))) return false;
+        // A tile holding draft positions is copied only after the fused append has stored them.
+        if (!appended && (tile0 + jt + 1) * 128 > a.app.pos0) {
+          if (!__all_sync(0xffffffffu, mbar_wait(app_done, 0))) return false;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          appended = true;
+        }
         const int lp = (tile0 + jt) * 4;
         uint8_t* dst = sStage + (is_v ? NS * kV6Ring : 0) + st * kV6Ring;
         const char* src[4];

@@ -77,6 +77,8 @@ SIGNATURES = {
     "lfm3a_verify_attention_static": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _I, _P]),
     "lfm3a_verify_partial": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_combine": (_I, [_P, _I, _I, _I, _I64, _I64, _P, _P, _P]),
+    "lfm3a_verify_round": (_I, [ctypes.POINTER(KvView), _P, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _SZ, _I,
+                                _P]),
     "lfm3a_ring_table": (_I, [_I, _I, _P]),
     "lfm3a_ring_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
@@ -234,6 +236,29 @@ class LayerCache:
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
         _check(lib().lfm3a_verify_attention(ctypes.byref(self.view), _ptr(q), m, qh, ctx_len, window, _ptr(gate),
                                             _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
+        return out
+
+    def verify_round(self, k, v, q, ctx_len: int, rope=None, k_norm=None, window: int = 0, gate=None, out=None,
+                     workspace=None, splits: int = 0, stream=None):
+        """append(k, v, ctx_len, rope, k_norm) then verify(q, ctx_len, ...) in one library call (the append
+        fused into the attention kernel for up to 16 drafts)."""
+        import torch
+
+        m, qh, d = q.shape
+        if out is None:
+            out = torch.empty_like(q)
+        if ctx_len + m > self.capacity:
+            raise LFM3AError(EINVAL, "append past the cache capacity")
+        if splits <= 0:
+            splits = verify_splits(self.layout, ctx_len, m, window)
+        if workspace is None and splits > 1:
+            workspace = torch.empty(lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8,
+                                    device=q.device)
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib().lfm3a_verify_round(ctypes.byref(self.view), _ptr(k), _ptr(v), 0, _ptr(rope), _ptr(k_norm), _ptr(q),
+                                        m, qh, ctx_len, window, _ptr(gate), _ptr(out), _ptr(workspace), ws_bytes,
+                                        splits, _stream(stream)))
+        self.length = max(self.length, ctx_len + m)
         return out
 
     def ring_attention(self, q, ctx_lo: int, ctx_len: int, out=None, workspace=None, splits: int = 0, stream=None):

@@ -194,3 +194,45 @@ def test_ring_attention(la, orc, synth, cuda, m):
     p /= p.sum(-1, keepdims=True)
     want = np.einsum("hmn,nhd->mhd", p, vh)
     assert rel_err(out.float().cpu().numpy(), want) < TOL
+
+
+@pytest.mark.parametrize("ctx_len,m,splits", [(32768, 16, 0), (1000, 8, 0), (1020, 16, 0), (5, 16, 0),
+                                               (2000, 24, 0), (4000, 16, 31)])
+def test_verify_round_matches_two_calls(la, orc, synth, cuda, ctx_len, m, splits):
+    """lfm3a_verify_round (the drafts' append fused into the attention kernel for m <= 16; 1020 + 16 touches two
+    int8 V blocks; m = 24 and 31 splits of 4000 keys take the separate append) leaves the cache bytes of
+    lfm3a_kv_append + lfm3a_verify_attention bit for bit, over three rounds with rollbacks between. The output
+    matches within the two-rounding tolerance (the appending split holds fewer key tiles, so the splits round
+    their fp16 probabilities against different maxima) and exact fp64 attention within 2e-3."""
+    case = synth.verify_case(60 + m, ctx_len, m)
+    rope_np = la.rope_table(1e6, 1.0, 64, ctx_len + 4 * m + 1)   # rows for every round's drafts
+    rope = dev(rope_np.view(np.float16), cuda)
+    caches = []
+    for _ in range(2):
+        c = la.LayerCache(la.MODE_F16, 8, 64, ctx_len + 4 * m + 64, device=cuda)
+        c.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+        caches.append(c)
+    fused, plain = caches
+    s = synth.Stream(61)
+    length = ctx_len - 3 if ctx_len > 8 else ctx_len
+    fused.truncate(length)
+    plain.truncate(length)
+    for r in range(3):
+        nk, nv = dev(s.normal_f16((m, 8, 64)), cuda), dev(s.normal_f16((m, 8, 64)), cuda)
+        q = dev(s.normal_f16((m, 32, 64)), cuda)
+        a = fused.verify_round(nk, nv, q, length, rope=rope, splits=splits)
+        plain.append(nk, nv, length, rope=rope)
+        b = plain.verify(q, length, splits=splits)
+        la.sync()
+        ao = a.float().cpu().numpy()
+        assert rel_err(ao, b.float().cpu().numpy()) < TOL_PAIR
+        ga, gb = fused.logical(length + m), plain.logical(length + m)
+        for key in ("K", "V", "V8", "vscale", "page_scale"):
+            assert np.array_equal(ga[key], gb[key]), key
+        K = ga["K"][:length + m].view(np.float16)
+        V = ga["V"][:length + m].view(np.float16)
+        assert rel_err(ao, orc.attention_f64(q.cpu().numpy(), length, K, V, length + m)) < TOL
+        keep = (r * 5 + 3) % m + 1
+        length += keep
+        fused.truncate(length)
+        plain.truncate(length)
