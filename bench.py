@@ -322,11 +322,10 @@ def measure_c3(la, synth, dev, peak_gbs: float, steps: int = 60) -> dict:
     splits = la.verify_splits(caches[0].layout, ctx, M, 0)
     ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(M, QH, D, splits), dtype=torch.uint8, device=dev)
 
-    def step(c, ev=None):
-        c.append(nk, nv, ctx, rope=rope)
+    def step(c, ev=None):   # one round: the drafts' append fused into the attention call, then the rollback
         if ev:
             ev[0].record()
-        c.verify(q, ctx, out=out, workspace=ws, splits=splits)
+        c.verify_round(nk, nv, q, ctx, rope=rope, out=out, workspace=ws, splits=splits)
         if ev:
             ev[1].record()
         c.truncate(ctx)
@@ -344,8 +343,9 @@ def measure_c3(la, synth, dev, peak_gbs: float, steps: int = 60) -> dict:
             "verify_us_back_to_back": round(b2b_us, 2),
             "frac_back_to_back": round(byts / (b2b_us * 1e-6) / 1e9 / peak_gbs, 4),
             "bytes": byts,
-            "note": "verify_us: events around each verify inside the round's graph (as the headline roofline); "
-                    "back_to_back: a graph of consecutive verify calls timed whole"}
+            "note": "us_per_layer: a graph of rounds (the drafts' append fused into the attention call, rollback) "
+                    "timed whole; verify_us: events around each round's attention call in a second replay (as the "
+                    "headline roofline); back_to_back: a graph of consecutive verify calls timed whole"}
 
 
 def measure_decode(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_caches: int, steps: int = 60) -> dict:
@@ -370,11 +370,10 @@ def measure_decode(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_cache
     splits = la.verify_splits(caches[0].layout, ctx, 1, 0)
     ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(1, QH, D, splits), dtype=torch.uint8, device=dev)
 
-    def step(c, ev=None):
-        c.append(nk, nv, ctx, rope=rope)
+    def step(c, ev=None):   # one round: the drafts' append fused into the attention call, then the rollback
         if ev:
             ev[0].record()
-        c.verify(q, ctx, out=out, workspace=ws, splits=splits)
+        c.verify_round(nk, nv, q, ctx, rope=rope, out=out, workspace=ws, splits=splits)
         if ev:
             ev[1].record()
         c.truncate(ctx)
@@ -578,8 +577,7 @@ def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, se
     with torch.cuda.graph(g, stream=stream):
         for s in range(steps):
             for c in caches:
-                c.append(drafts[s, 0], drafts[s, 1], length, rope=rope)
-                c.verify(qs[s], length, out=out, workspace=ws)
+                c.verify_round(drafts[s, 0], drafts[s, 1], qs[s], length, rope=rope, out=out, workspace=ws)
                 c.truncate(length + int(keep[s]))
             length += int(keep[s])
     torch.cuda.synchronize()
