@@ -53,7 +53,7 @@ def parse():
                          "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
                          "synchronisation, which both pay)")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 and decode fields (N = 1)")
-    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode", "chunks"],
+    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode", "chunks", "gemm"],
                     help="run only that configuration's measurement on one GPU and print its fields (for profiling)")
     return ap.parse_args()
 
@@ -75,6 +75,8 @@ def run_only(args) -> int:
         res = measure_decodes(la, synth, dev, pk["hbm_gbs"])
     elif args.only == "chunks":
         res = measure_prefill_chunks(la, dev)
+    elif args.only == "gemm":
+        res = measure_gemm(la, dev, pk)
     else:
         res = measure_c5(la, dev)
     print(json.dumps({args.only: res}), flush=True)
@@ -537,6 +539,65 @@ def measure_c4(la, synth, dev, peaks_: dict, reps: int = 5) -> dict:
     return res
 
 
+# The prefill's W8A8 linear layers of one full-attention layer of LFM3-1.7B (H 2048, I 7680; mix 3088 outputs,
+# internal/model/prefill.go:100-110,420-450), at the reference's long-prompt chunk of 7680 tokens (prefill.go:24).
+GEMM_TOKENS = 7680
+GEMM_LAYERS = (("mix", 3088, 2048, False), ("out", 2048, 2048, False), ("w13", 15360, 2048, False),
+               ("w2", 2048, 7680, True))
+
+
+def measure_gemm(la, dev, peaks_: dict, reps: int = 10) -> dict:
+    """The hot-path table's fourth "next" row: per linear layer, the GEMM alone on quantised activations and the
+    whole linear call (quantiser + GEMM), CUDA events over reps back-to-back calls after two warm-up calls."""
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(5)
+    tf16 = peaks_.get("bf16_tflops")
+    res = {"workload": f"W8A8 group-128 linear layers of one attention layer, {GEMM_TOKENS}-token chunk "
+                       "(LFM3-1.7B shapes, random int8 weights)"}
+    total_ops, total_ms = 0.0, 0.0
+    for name, outputs, k, gated in GEMM_LAYERS:
+        x = (torch.randn((GEMM_TOKENS, 2 * k if gated else k), generator=g, device=dev) * 2).half()
+        w = torch.randint(-127, 128, (outputs, k), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+        ws = (torch.rand((outputs, k // 128), generator=g, device=dev) * 0.01 + 1e-3).half().float()
+        b = la.G128Operand.pack(w, ws)
+        del w
+        a = la.G128Operand.quantize(x, k, gated=gated)
+        out = torch.empty((GEMM_TOKENS, outputs), dtype=torch.float16, device=dev)
+        ws_buf = torch.empty(la.g128_workspace_bytes(GEMM_TOKENS, k), dtype=torch.uint8, device=dev)
+        ops = 2.0 * GEMM_TOKENS * outputs * k
+
+        def timed(fn):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / reps
+
+        ms_gemm = timed(lambda: la.g128_gemm(a, b, out=out))
+        ms_lin = timed(lambda: la.g128_linear(x, b, gated=gated, out=out, workspace=ws_buf))
+        entry = {"outputs": outputs, "k": k, "gated": gated, "gemm_us": round(ms_gemm * 1e3, 1),
+                 "gemm_tops": round(ops / (ms_gemm * 1e-3) / 1e12, 1), "linear_us": round(ms_lin * 1e3, 1)}
+        if tf16:
+            entry["int8_frac"] = round(ops / (ms_gemm * 1e-3) / (2.0 * tf16 * 1e12), 4)
+        res[name] = entry
+        total_ops += ops
+        total_ms += ms_lin
+        del x, a, b, out, ws_buf
+        torch.cuda.empty_cache()
+    la.sync()
+    res["layer_linear_us"] = round(total_ms * 1e3, 1)
+    res["layer_tops"] = round(total_ops / (total_ms * 1e-3) / 1e12, 1)
+    if tf16:
+        res["peak"] = f"int8 dense at twice the measured bf16 {tf16} TFLOP/s (nominal ratio)"
+    return res
+
+
 def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, seed: int = 4) -> dict:
     """Config 5, the KV lifecycle: per layer a causal prefill of ctx tokens (append with RoPE + int8-PV
     attention), then `steps` DSpark rounds over all layers (append 16 drafts, verify 16, keep
@@ -845,6 +906,8 @@ def run_ours(args):
         extras["c4"] = measure_c4(la, synth, dev, pk)
         torch.cuda.empty_cache()
         extras["prefill_chunks"] = measure_prefill_chunks(la, dev)
+        torch.cuda.empty_cache()
+        extras["gemm"] = measure_gemm(la, dev, pk)
         torch.cuda.empty_cache()
         extras["c5"] = measure_c5(la, dev)
 

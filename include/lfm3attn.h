@@ -308,6 +308,48 @@ int lfm3a_pseq_release(lfm3a_pcache* pc, lfm3a_pseq* seq);
  * number of blocks (copies at most cap of each). */
 int lfm3a_pseq_blocks(const lfm3a_pseq* seq, int32_t* full, int32_t* slide, int cap);
 
+/* ---------------------------------------------------------------- W8A8 linear layers of the prefill
+ * y = x W^T with int8 activations and int8 weights, one fp32 scale per 128 inputs on both sides
+ * (kernels/gemm.hip:1-8): y[m][n] = sum_g sa[g][m] * sb[g][n] * sum_{k in g} qa[m][k] * qb[n][k].
+ * Operands live in "g128 tiles": per (128-column group, 128-row tile) a 16 KiB block in tensor-core
+ * operand order, [k / 128][ceil(rows / 128)][16384] bytes; their scales are fp32
+ * [k / 128][ceil(rows / 128) * 128] (the reference's scale layout, internal/model/prefill.go:207-215),
+ * padding rows scale 1 and zero bytes. k must be a positive multiple of 128. */
+
+/* Bytes of an operand of rows x k in g128 tiles, and of its scales (prefill.go:81-84 g128Sizes). */
+int64_t lfm3a_g128_packed_bytes(int rows, int k);
+int64_t lfm3a_g128_scale_bytes(int rows, int k);
+
+/* Weights: row-major int8 w [rows][k] (row stride w_stride bytes, a multiple of 16) and fp32 group scales
+ * [rows][k / 128] (row stride s_stride floats) into g128 tiles. The layout step of buildPrefillWeights
+ * (prefill.go:141-215, fillPacked / fillScales); undoing the payload's +128 bias and fp16 scale interleave
+ * is the caller's. */
+int lfm3a_g128_pack(const int8_t* w, int64_t w_stride, const float* w_scales, int64_t s_stride, int rows, int k,
+                    void* packed, float* scales, void* stream);
+
+/* Activations: fp16 x [rows] rows of k (row stride x_stride elements, a multiple of 8) quantised per row and
+ * 128-column group into g128 tiles: scale = absmax / 127 (1 for a zero group), q = rint(clamp(v / scale,
+ * -127, 127)) (quantize_pack, kernels/gemm.hip:65-103). gated != 0: each row holds [gate (k) | up (k)]
+ * and v = silu(gate) * up (gemm.hip:73-77, the down projection's input). */
+int lfm3a_g128_quantize(const void* x, int64_t x_stride, int rows, int k, int gated, void* packed, float* scales,
+                        void* stream);
+
+/* The GEMM (kernels/gemm.hip:181-255): out[m][n] = fp16(acc + residual[m][n]) (residual optional, NULL
+ * for none) for m < rows, n < outputs, with acc accumulated group by group as
+ * acc = fma(float(int32 dot) * sb, sa, acc). a/sa: activations (rows x k), b/sb: weights (outputs x k), both
+ * in g128 tiles. Bit-identical to the reference arithmetic on the same int8 inputs. */
+int lfm3a_g128_gemm(const void* a, const float* sa, const void* b, const float* sb, int rows, int outputs, int k,
+                    const void* residual, int64_t residual_stride, void* out, int64_t out_stride, void* stream);
+
+/* Workspace of lfm3a_g128_linear: the packed activations and their scales. */
+int64_t lfm3a_g128_workspace_bytes(int rows, int k);
+
+/* One linear layer as the engine's g128 runs it (internal/model/prefill.go:357-382): quantise x (gated or
+ * not), then the GEMM against packed weights. */
+int lfm3a_g128_linear(const void* x, int64_t x_stride, int rows, int gated, const void* w, const float* w_scales,
+                      int outputs, int k, const void* residual, int64_t residual_stride, void* out,
+                      int64_t out_stride, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- test hooks */
 /* The u8 quantiser of softmax rows in the reference's operation order (kernels/prefill_attn.hip:305-331):
  * for each row of 64 P' values, q = rne_sat_u8(P' * (255 / max(rowmax, 1e-30))), sc = rowmax * (1/255).

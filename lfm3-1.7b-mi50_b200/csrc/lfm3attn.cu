@@ -10,6 +10,7 @@
 
 #include "../../include/lfm3attn.h"
 #include "common.cuh"
+#include "gemm.cuh"
 #include "kv.cuh"
 #include "pcache.h"
 #include "prefill.cuh"
@@ -605,6 +606,128 @@ int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* s
   if (rows == 0) return LFM3A_OK;
   launch_pdl(quantize_p_rows_kernel, (rows + 127) / 128, 128, 0, as_stream(stream), p, rows, q, sc);
   return check_launch("quantize_p_rows_kernel");
+}
+
+// ---------------------------------------------------------------- W8A8 linear layers
+namespace {
+
+int64_t g128_tiles(int rows) { return ((int64_t)rows + 127) / 128; }
+
+int check_g128_shape(int rows, int k) {
+  if (rows <= 0 || k <= 0 || k % kG128 != 0) return fail(LFM3A_EINVAL, "g128: rows must be positive, k a positive multiple of 128");
+  return LFM3A_OK;
+}
+
+int64_t align256(int64_t n) { return (n + 255) & ~int64_t(255); }
+
+}  // namespace
+
+int64_t lfm3a_g128_packed_bytes(int rows, int k) {
+  if (check_g128_shape(rows, k) != LFM3A_OK) return LFM3A_EINVAL;
+  return (int64_t)(k / kG128) * g128_tiles(rows) * kG128Block;
+}
+
+int64_t lfm3a_g128_scale_bytes(int rows, int k) {
+  if (check_g128_shape(rows, k) != LFM3A_OK) return LFM3A_EINVAL;
+  return (int64_t)(k / kG128) * g128_tiles(rows) * 128 * (int64_t)sizeof(float);
+}
+
+int lfm3a_g128_pack(const int8_t* w, int64_t w_stride, const float* w_scales, int64_t s_stride, int rows, int k,
+                    void* packed, float* scales, void* stream) {
+  int rc = check_g128_shape(rows, k);
+  if (rc != LFM3A_OK) return rc;
+  if (!w || !w_scales || !packed || !scales) return fail(LFM3A_EINVAL, "g128_pack: null pointer");
+  if (!aligned16(w) || !aligned16(packed) || (w_stride % 16) != 0 || w_stride < k || s_stride < k / kG128)
+    return fail(LFM3A_EINVAL, "g128_pack: w and packed must be 16-byte aligned, w_stride a multiple of 16 >= k");
+  const dim3 grid((unsigned)g128_tiles(rows), (unsigned)(k / kG128));
+  launch_pdl(g128_pack_kernel, grid, 128, 0, as_stream(stream), w, w_stride, w_scales, s_stride, rows, k,
+             static_cast<uint8_t*>(packed), scales);
+  return check_launch("g128_pack_kernel");
+}
+
+int lfm3a_g128_quantize(const void* x, int64_t x_stride, int rows, int k, int gated, void* packed, float* scales,
+                        void* stream) {
+  int rc = check_g128_shape(rows, k);
+  if (rc != LFM3A_OK) return rc;
+  if (!x || !packed || !scales) return fail(LFM3A_EINVAL, "g128_quantize: null pointer");
+  if (!aligned16(x) || !aligned16(packed) || (x_stride % 8) != 0 || x_stride < (gated ? 2LL * k : (int64_t)k))
+    return fail(LFM3A_EINVAL, "g128_quantize: x and packed must be 16-byte aligned, x_stride a multiple of 8 "
+                              "covering the row (2 k when gated)");
+  const dim3 grid((unsigned)g128_tiles(rows), (unsigned)(k / kG128));
+  const __half* xh = static_cast<const __half*>(x);
+  uint8_t* dst = static_cast<uint8_t*>(packed);
+  if (gated) launch_pdl(g128_quantize_kernel<true>, grid, 256, 0, as_stream(stream), xh, x_stride, dst, scales, rows, k);
+  else launch_pdl(g128_quantize_kernel<false>, grid, 256, 0, as_stream(stream), xh, x_stride, dst, scales, rows, k);
+  return check_launch("g128_quantize_kernel");
+}
+
+int lfm3a_g128_gemm(const void* a, const float* sa, const void* b, const float* sb, int rows, int outputs, int k,
+                    const void* residual, int64_t residual_stride, void* out, int64_t out_stride, void* stream) {
+  int rc = check_g128_shape(rows, k);
+  if (rc != LFM3A_OK) return rc;
+  if (outputs <= 0) return fail(LFM3A_EINVAL, "g128_gemm: outputs must be positive");
+  if (!a || !sa || !b || !sb || !out) return fail(LFM3A_EINVAL, "g128_gemm: null pointer");
+  if (!aligned16(a) || !aligned16(sa) || !aligned16(b) || !aligned16(sb) || !aligned16(out) ||
+      (residual && !aligned16(residual)))
+    return fail(LFM3A_EINVAL, "g128_gemm: every buffer must be 16-byte aligned");
+  if (out_stride < outputs || (residual && residual_stride < outputs))
+    return fail(LFM3A_EINVAL, "g128_gemm: row strides must cover the outputs");
+  static bool done[64];
+  static bool regs_ok[64];
+  rc = ensure_smem(g128_gemm_kernel, kGmRequest, done);
+  if (rc != LFM3A_OK) return rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(LFM3A_ECUDA, "cudaGetDevice");
+  if (!regs_ok[dev]) {
+    // The fold warps' setmaxnreg.inc waits until the block's launch registers cover both shares: refuse to
+    // launch a build whose register count would leave it waiting.
+    cudaFuncAttributes fa;
+    const cudaError_t e = cudaFuncGetAttributes(&fa, g128_gemm_kernel);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+    if (fa.numRegs * kGmThreads < 128 * kGmCtrlRegs + 256 * kGmFoldRegs)
+      return fail(LFM3A_ENOTSUP, "g128_gemm_kernel built with too few registers for its setmaxnreg split");
+    regs_ok[dev] = true;
+  }
+  G128Args g;
+  g.a = static_cast<const uint8_t*>(a);
+  g.sa = sa;
+  g.b = static_cast<const uint8_t*>(b);
+  g.sb = sb;
+  g.out = static_cast<__half*>(out);
+  g.residual = static_cast<const __half*>(residual);
+  g.out_stride = out_stride;
+  g.residual_stride = residual_stride;
+  g.rows = rows;
+  g.outputs = outputs;
+  g.groups = k / kG128;
+  g.m_tiles = (int)g128_tiles(rows);
+  g.n_blocks = (int)g128_tiles(outputs);
+  g.n_tiles = (g.n_blocks + 1) / 2;
+  const int total = g.m_tiles * g.n_tiles;
+  const int grid = std::min(total, current_sm_count());
+  launch_pdl(g128_gemm_kernel, grid, kGmThreads, kGmRequest, as_stream(stream), g);
+  return check_launch("g128_gemm_kernel");
+}
+
+int64_t lfm3a_g128_workspace_bytes(int rows, int k) {
+  if (check_g128_shape(rows, k) != LFM3A_OK) return LFM3A_EINVAL;
+  return align256(lfm3a_g128_packed_bytes(rows, k)) + align256(lfm3a_g128_scale_bytes(rows, k));
+}
+
+int lfm3a_g128_linear(const void* x, int64_t x_stride, int rows, int gated, const void* w, const float* w_scales,
+                      int outputs, int k, const void* residual, int64_t residual_stride, void* out,
+                      int64_t out_stride, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_g128_shape(rows, k);
+  if (rc != LFM3A_OK) return rc;
+  if (!workspace || !aligned16(workspace)) return fail(LFM3A_EINVAL, "g128_linear: workspace must be 16-byte aligned");
+  if ((int64_t)workspace_bytes < lfm3a_g128_workspace_bytes(rows, k))
+    return fail(LFM3A_EWORKSPACE, "g128_linear: workspace smaller than lfm3a_g128_workspace_bytes");
+  uint8_t* packed = static_cast<uint8_t*>(workspace);
+  float* scales = reinterpret_cast<float*>(packed + align256(lfm3a_g128_packed_bytes(rows, k)));
+  rc = lfm3a_g128_quantize(x, x_stride, rows, k, gated, packed, scales, stream);
+  if (rc != LFM3A_OK) return rc;
+  return lfm3a_g128_gemm(packed, scales, w, w_scales, rows, outputs, k, residual, residual_stride, out, out_stride,
+                         stream);
 }
 
 // ---------------------------------------------------------------- prefix cache (host only)

@@ -87,6 +87,13 @@ SIGNATURES = {
     "lfm3a_prefill_attention_fused": (_I, [ctypes.POINTER(KvView), _P, _I64, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _P,
                                            _P, _SZ, _P]),
     "lfm3a_quantize_p_u8": (_I, [_P, _I, _P, _P, _P]),
+    "lfm3a_g128_packed_bytes": (_I64, [_I, _I]),
+    "lfm3a_g128_scale_bytes": (_I64, [_I, _I]),
+    "lfm3a_g128_pack": (_I, [_P, _I64, _P, _I64, _I, _I, _P, _P, _P]),
+    "lfm3a_g128_quantize": (_I, [_P, _I64, _I, _I, _I, _P, _P, _P]),
+    "lfm3a_g128_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _I64, _P, _I64, _P]),
+    "lfm3a_g128_workspace_bytes": (_I64, [_I, _I]),
+    "lfm3a_g128_linear": (_I, [_P, _I64, _I, _I, _P, _P, _I, _I, _P, _I64, _P, _I64, _P, _SZ, _P]),
     "lfm3a_gather_region_bytes": (_SZ, [_I, _I, _I]),
     "lfm3a_gather_region_alloc": (_I, [_I, _I, _I, ctypes.POINTER(_P)]),
     "lfm3a_gather_region_free": (_I, [_P]),
@@ -485,6 +492,80 @@ def quantize_p_u8(p, stream=None):
     sc = torch.empty((rows,), dtype=torch.float32, device=p.device)
     _check(lib().lfm3a_quantize_p_u8(_ptr(p), rows, _ptr(q), _ptr(sc), _stream(stream)))
     return q, sc
+
+
+# ------------------------------------------------------------------ W8A8 linear layers (kernels/gemm.hip)
+class G128Operand:
+    """An int8 operand of rows x k in g128 tiles with its fp32 group scales, in device memory (torch-owned).
+    Weights come from `pack` (row-major int8 + per-row group scales, the layout step of buildPrefillWeights,
+    prefill.go:141-215); activations from `quantize` (quantize_pack, gemm.hip:65-103)."""
+
+    def __init__(self, rows: int, k: int, device="cuda"):
+        import torch
+
+        self.rows, self.k = rows, k
+        nbytes = lib().lfm3a_g128_packed_bytes(rows, k)
+        sbytes = lib().lfm3a_g128_scale_bytes(rows, k)
+        if nbytes < 0 or sbytes < 0:
+            _check(int(nbytes) if nbytes < 0 else int(sbytes))
+        self.data = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self.scales = torch.empty(sbytes // 4, dtype=torch.float32, device=device)
+
+    @classmethod
+    def pack(cls, w, w_scales, stream=None) -> "G128Operand":
+        """w: int8 [rows][k] (row stride a multiple of 16 bytes), w_scales: f32 [rows][k / 128], on the device."""
+        rows, k = w.shape
+        op = cls(rows, k, device=w.device)
+        _check(lib().lfm3a_g128_pack(_ptr(w), w.stride(0), _ptr(w_scales), w_scales.stride(0), rows, k, _ptr(op.data),
+                                     _ptr(op.scales), _stream(stream)))
+        return op
+
+    @classmethod
+    def quantize(cls, x, k: int, gated: bool = False, out: "G128Operand | None" = None, stream=None) -> "G128Operand":
+        """x: fp16 [rows][>= k] (>= 2k when gated: [gate | up]), row stride a multiple of 8 elements."""
+        rows = x.shape[0]
+        op = out if out is not None else cls(rows, k, device=x.device)
+        _check(lib().lfm3a_g128_quantize(_ptr(x), x.stride(0), rows, k, int(gated), _ptr(op.data), _ptr(op.scales),
+                                         _stream(stream)))
+        return op
+
+
+def g128_gemm(a: G128Operand, b: G128Operand, residual=None, out=None, stream=None):
+    """out[m][n] = fp16(sum_g sa sb int32-dot [+ residual]) for a (rows x k activations), b (outputs x k weights)."""
+    import torch
+
+    if a.k != b.k:
+        raise ValueError("operands differ in k")
+    if out is None:
+        out = torch.empty((a.rows, b.rows), dtype=torch.float16, device=a.data.device)
+    _check(lib().lfm3a_g128_gemm(_ptr(a.data), _ptr(a.scales), _ptr(b.data), _ptr(b.scales), a.rows, b.rows, a.k,
+                                 _ptr(residual), 0 if residual is None else residual.stride(0), _ptr(out),
+                                 out.stride(0), _stream(stream)))
+    return out
+
+
+def g128_workspace_bytes(rows: int, k: int) -> int:
+    n = lib().lfm3a_g128_workspace_bytes(rows, k)
+    if n < 0:
+        _check(int(n))
+    return int(n)
+
+
+def g128_linear(x, w: G128Operand, gated: bool = False, residual=None, out=None, workspace=None, stream=None):
+    """One linear layer as the engine's g128 runs it (prefill.go:357-382): quantise x, then the GEMM."""
+    import torch
+
+    rows = x.shape[0]
+    if out is None:
+        out = torch.empty((rows, w.rows), dtype=torch.float16, device=x.device)
+    need = g128_workspace_bytes(rows, w.k)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    _check(lib().lfm3a_g128_linear(_ptr(x), x.stride(0), rows, int(gated), _ptr(w.data), _ptr(w.scales), w.rows, w.k,
+                                   _ptr(residual), 0 if residual is None else residual.stride(0), _ptr(out),
+                                   out.stride(0), _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                   _stream(stream)))
+    return out
 
 
 # ------------------------------------------------------------------ page layout (host decoding)

@@ -553,4 +553,71 @@ int orc_accept(const int32_t* best, const int32_t* tokens, int m) {
   return acc + 1;
 }
 
+/* ---------------------------------------------------------------- W8A8 prefill GEMM (kernels/gemm.hip) */
+float orc_g128_exp(float x) {
+  if (!(x < 88.5f)) return x != x ? x : INFINITY;
+  if (x < -87.f) return 0.f;
+  const float n = rintf(x * 1.44269502f);
+  const float r = (x - n * 0.693145751953125f) - n * 1.42860677e-6f;
+  float p = 1.98412701e-4f;
+  p = 1.38888892e-3f + r * p;
+  p = 8.33333377e-3f + r * p;
+  p = 4.16666679e-2f + r * p;
+  p = 1.66666672e-1f + r * p;
+  p = 0.5f + r * p;
+  p = 1.f + r * p;
+  p = 1.f + r * p;
+  const int ni = (int)n, n1 = ni / 2, n2 = ni - n1;
+  uint32_t b1 = (uint32_t)(n1 + 127) << 23, b2 = (uint32_t)(n2 + 127) << 23;
+  float f1, f2;
+  memcpy(&f1, &b1, 4);
+  memcpy(&f2, &b2, 4);
+  return (p * f1) * f2;
+}
+
+void orc_g128_quantize(const uint16_t* x, int64_t x_stride, int rows, int k, int gated, int8_t* q, float* scales) {
+  const int groups = k / 128;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r) {
+    const uint16_t* row = x + (int64_t)r * x_stride;
+    for (int g = 0; g < groups; ++g) {
+      float v[128];
+      for (int i = 0; i < 128; ++i) {
+        v[i] = orc_f16_to_f32(row[g * 128 + i]);
+        if (gated) {
+          const float u = orc_f16_to_f32(row[k + g * 128 + i]);
+          v[i] = (v[i] / (1.f + orc_g128_exp(-v[i]))) * u;
+        }
+      }
+      float m = 0.f;
+      for (int i = 0; i < 128; ++i) m = fmaxf(m, fabsf(v[i]));
+      const float scale = m > 0.f ? m / 127.f : 1.f;
+      const float inv = 1.f / scale;
+      scales[(int64_t)r * groups + g] = scale;
+      for (int i = 0; i < 128; ++i)
+        q[(int64_t)r * k + g * 128 + i] = (int8_t)(int)rintf(fminf(fmaxf(v[i] * inv, -127.f), 127.f));
+    }
+  }
+}
+
+void orc_g128_gemm(const int8_t* qa, const float* sa, const int8_t* qb, const float* sb, int rows, int outputs, int k,
+                   const uint16_t* residual, int64_t residual_stride, uint16_t* out) {
+  const int groups = k / 128;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int m = 0; m < rows; ++m) {
+    const int8_t* a = qa + (int64_t)m * k;
+    for (int n = 0; n < outputs; ++n) {
+      const int8_t* b = qb + (int64_t)n * k;
+      float acc = 0.f;
+      for (int g = 0; g < groups; ++g) {
+        int32_t s = 0;
+        for (int i = 0; i < 128; ++i) s += (int32_t)a[g * 128 + i] * (int32_t)b[g * 128 + i];
+        acc = fmaf((float)s * sb[(int64_t)n * groups + g], sa[(int64_t)m * groups + g], acc);
+      }
+      if (residual) acc = acc + orc_f16_to_f32(residual[(int64_t)m * residual_stride + n]);
+      out[(int64_t)m * outputs + n] = orc_f32_to_f16(acc);
+    }
+  }
+}
+
 }  // extern "C"

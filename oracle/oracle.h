@@ -103,6 +103,25 @@ void orc_q_norm_rope(const uint16_t* q, int T, int q_heads, int head_dim, int64_
  * then commit = accepted + 1 positions. Returns commit. */
 int orc_accept(const int32_t* best, const int32_t* tokens, int m);
 
+/* e^x as the gated activation quantiser computes it: Cody-Waite reduction x = n ln2 + r (ln2 as a 15-bit
+ * head and a tail), the degree-7 Taylor polynomial of e^r, 2^n as two power-of-two factors; every step one
+ * IEEE-rounded operation. 0 below -87, +inf from 88.5. */
+float orc_g128_exp(float x);
+
+/* Activation quantiser of the W8A8 prefill GEMM (quantize_pack, kernels/gemm.hip:65-103): per row and
+ * 128-column group, scale = absmax / 127 (1 for an all-zero group), q = rint(clamp(v * (1 / scale), -127,
+ * 127)); gated: each row holds [gate (k) | up (k)] and v = silu(gate) * up = gate / (1 + e^-gate) * up
+ * (gemm.hip:73-77, with orc_g128_exp). x: fp16 rows at x + r * x_stride. q: row-major [rows][k] int8,
+ * scales: [rows][k / 128]. */
+void orc_g128_quantize(const uint16_t* x, int64_t x_stride, int rows, int k, int gated, int8_t* q, float* scales);
+
+/* The W8A8 GEMM (kernels/gemm.hip:181-255): acc = 0; for each 128-column group g in order,
+ * acc = fma(float(sum_k qa[m][k] qb[n][k]) * sb[n][g], sa[m][g], acc); out = fp16(acc [+ residual]).
+ * qa [rows][k], sa [rows][k / 128], qb [outputs][k], sb [outputs][k / 128], residual fp16 rows at
+ * residual + m * residual_stride (NULL: none), out fp16 [rows][outputs]. */
+void orc_g128_gemm(const int8_t* qa, const float* sa, const int8_t* qb, const float* sb, int rows, int outputs, int k,
+                   const uint16_t* residual, int64_t residual_stride, uint16_t* out);
+
 /* Threads the oracle may use (OpenMP). */
 void orc_set_threads(int n);
 int orc_get_threads(void);

@@ -35,6 +35,9 @@ _SIGS = {
     "orc_prefill_exact": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
     "orc_q_norm_rope": (None, [_P, _I, _I, _I, ctypes.c_int64, _P, _P, _I, _P]),
     "orc_accept": (_I, [_P, _P, _I]),
+    "orc_g128_exp": (ctypes.c_float, [ctypes.c_float]),
+    "orc_g128_quantize": (None, [_P, ctypes.c_int64, _I, _I, _I, _P, _P]),
+    "orc_g128_gemm": (None, [_P, _P, _P, _P, _I, _I, _I, _P, ctypes.c_int64, _P]),
     "orc_set_threads": (None, [_I]),
     "orc_get_threads": (_I, []),
 }
@@ -218,3 +221,58 @@ def accept(best, tokens) -> int:
     best, bp = _c(best, np.int32)
     tokens, tp = _c(tokens, np.int32)
     return lib().orc_accept(bp, tp, tokens.shape[0])
+
+
+# ------------------------------------------------------------------ W8A8 prefill GEMM (kernels/gemm.hip)
+def g128_exp(x: float) -> float:
+    return lib().orc_g128_exp(x)
+
+
+def g128_quantize(x, k: int, gated: bool = False):
+    """quantize_pack (gemm.hip:65-103). x: fp16 [rows][>= k] (>= 2k when gated). Returns q int8 [rows][k] and
+    scales f32 [rows][k / 128], both row-major."""
+    x = np.ascontiguousarray(np.asarray(x, dtype=np.float16))
+    rows = x.shape[0]
+    q = np.empty((rows, k), dtype=np.int8)
+    sc = np.empty((rows, k // 128), dtype=np.float32)
+    lib().orc_g128_quantize(x.ctypes.data, x.shape[1], rows, k, int(gated), q.ctypes.data, sc.ctypes.data)
+    return q, sc
+
+
+def g128_gemm(qa, sa, qb, sb, residual=None) -> np.ndarray:
+    """The W8A8 GEMM (gemm.hip:181-255) on row-major operands: qa [rows][k], sa [rows][k / 128], qb [outputs][k],
+    sb [outputs][k / 128]; returns fp16 [rows][outputs]."""
+    qa, ap = _c(qa, np.int8)
+    qb, bp = _c(qb, np.int8)
+    sa, sap = _c(sa, np.float32)
+    sb, sbp = _c(sb, np.float32)
+    rows, k = qa.shape
+    outputs = qb.shape[0]
+    res, rp = _c(residual, np.float16)
+    out = np.empty((rows, outputs), dtype=np.float16)
+    lib().orc_g128_gemm(ap, sap, bp, sbp, rows, outputs, k, rp, 0 if res is None else res.shape[1], out.ctypes.data)
+    return out
+
+
+def g128_pack(q, scales) -> tuple[np.ndarray, np.ndarray]:
+    """Row-major int8 [rows][k] and f32 [rows][k / 128] into g128 tiles ([k/128][tiles][16384] bytes; row r, column c
+    of a block at ((r/8)*8 + c/16)*128 + (r%8)*16 + c%16) and the scale layout [k/128][tiles * 128] (padding: 0, 1)."""
+    q = np.asarray(q, dtype=np.int8)
+    rows, k = q.shape
+    tiles, groups = (rows + 127) // 128, k // 128
+    qp = np.zeros((tiles * 128, k), dtype=np.int8)
+    qp[:rows] = q
+    # [tile][rg][r8][group][chunk][16] -> [group][tile][rg][chunk][r8][16]
+    blk = qp.reshape(tiles, 16, 8, groups, 8, 16).transpose(3, 0, 1, 4, 2, 5)
+    sp = np.ones((groups, tiles * 128), dtype=np.float32)
+    sp[:, :rows] = np.asarray(scales, dtype=np.float32).T
+    return np.ascontiguousarray(blk).reshape(-1).view(np.uint8), sp
+
+
+def g128_unpack(packed, scales, rows: int, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """Inverse of g128_pack: row-major int8 [rows][k] and f32 [rows][k / 128]."""
+    tiles, groups = (rows + 127) // 128, k // 128
+    blk = np.asarray(packed).view(np.int8).reshape(groups, tiles, 16, 8, 8, 16)
+    q = blk.transpose(1, 2, 4, 0, 3, 5).reshape(tiles * 128, k)[:rows]
+    sc = np.asarray(scales, dtype=np.float32).reshape(groups, tiles * 128)[:, :rows].T
+    return np.ascontiguousarray(q), np.ascontiguousarray(sc)

@@ -9,12 +9,15 @@ to a second, separately written restatement of the same source lines:
   int8 V blocks    the same quantiser per (kv head, 64-token block)
   u8 P             kernels/prefill_attn.hip:305-331 (IEEE division in place of v_rcp_f32)
   accept           kernels/dspark.hip:2851-2860
+  W8A8 GEMM        kernels/gemm.hip:65-103 (quantize_pack, plain and gated) and :181-255 (gemm), the fp32
+                   fma of every group emulated exactly with rationals
 Run: python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
 import math
 import pathlib
+from fractions import Fraction
 import sys
 
 import numpy as np
@@ -133,6 +136,72 @@ def accept(best, tokens):
     return acc + 1
 
 
+def g128_exp(x):
+    """e^x with the gated quantiser's steps (Cody-Waite, degree-7 Taylor), every step one float32 rounding."""
+    x = np.asarray(x, dtype=f32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        n = np.rint(x * f32(1.44269502))
+        r = (x - n * f32(0.693145751953125)) - n * f32(1.42860677e-6)
+        p = np.full_like(x, f32(1.98412701e-4))
+        for c in (1.38888892e-3, 8.33333377e-3, 4.16666679e-2, 1.66666672e-1, 0.5, 1.0, 1.0):
+            p = f32(c) + r * p
+        ni = np.clip(n, -126, 128).astype(np.int64)
+        n1 = np.trunc(ni / 2).astype(np.int64)
+        n2 = ni - n1
+        f1 = ((n1 + 127) << 23).astype(np.uint32).view(f32)
+        f2 = ((n2 + 127) << 23).astype(np.uint32).view(f32)
+        y = (p * f1) * f2
+    y = np.where(x < f32(-87.0), f32(0.0), y)
+    y = np.where(x >= f32(88.5), f32(np.inf), y)
+    return y.astype(f32)
+
+
+def g128_quantize(x, k, gated):
+    x = np.asarray(x, dtype=np.float16).astype(f32)
+    v = x[:, :k]
+    if gated:
+        v = (v / (f32(1.0) + g128_exp(-v))) * x[:, k:2 * k]
+    rows, groups = v.shape[0], k // 128
+    vg = v.reshape(rows, groups, 128)
+    m = np.abs(vg).max(axis=2)
+    scale = np.where(m > 0, m / f32(127.0), f32(1.0)).astype(f32)
+    inv = (f32(1.0) / scale).astype(f32)
+    q = np.rint(np.clip(vg * inv[:, :, None], f32(-127.0), f32(127.0))).astype(np.int8)
+    return q.reshape(rows, k), scale
+
+
+def round_f32(fr):
+    """Fraction -> the nearest float32, ties to even (normal range)."""
+    if fr == 0:
+        return f32(0.0)
+    sign, a = (-1 if fr < 0 else 1), abs(fr)
+    e = a.numerator.bit_length() - a.denominator.bit_length() - 24
+    while a / Fraction(2) ** e >= 2 ** 24:
+        e += 1
+    while a / Fraction(2) ** e < 2 ** 23:
+        e -= 1
+    q = round(a / Fraction(2) ** e)          # round() of a Fraction: half to even
+    return f32(sign * q * 2.0 ** e)
+
+
+def g128_gemm(qa, sa, qb, sb, residual):
+    rows, k = qa.shape
+    outputs, groups = qb.shape[0], k // 128
+    s = np.einsum("mgi,ngi->mng", qa.reshape(rows, groups, 128).astype(np.int64),
+                  qb.reshape(outputs, groups, 128).astype(np.int64))
+    out = np.empty((rows, outputs), dtype=np.float16)
+    for m in range(rows):
+        for n in range(outputs):
+            acc = f32(0.0)
+            for gi in range(groups):
+                t = f32(f32(s[m, n, gi]) * sb[n, gi])
+                acc = round_f32(Fraction(float(t)) * Fraction(float(sa[m, gi])) + Fraction(float(acc)))
+            if residual is not None:
+                acc = f32(acc + f32(residual[m, n]))
+            out[m, n] = np.float16(acc)
+    return out
+
+
 def main():
     g = {}
     # RoPE tables: the benchmark's (theta 1e6, all 32 pairs, D 64) and the reference model's two.
@@ -185,6 +254,31 @@ def main():
     toks = np.array([4, 5, 6, 7, 8, 9, 9, 9], dtype=np.int32)
     g["acc_best"], g["acc_tokens"] = best, toks
     g["acc_commit"] = np.array([accept(best, toks), accept(best[:1], toks[:1]), accept(best, np.array([4, 0, 0, 0, 0, 0, 0, 0]))])
+
+    # W8A8 GEMM: 40 activation rows (ragged against the 128-row tile) x 384 inputs (3 groups) against 72
+    # weight rows, with an all-zero group (scale 1), an exact .5 tie, and a residual; gated activations with
+    # gate values past both clamps of the exponential.
+    s = synth.Stream(104)
+    x = s.normal_f16((40, 384))
+    x[3, 128:256] = 0
+    x[5, :128] = np.float16(0.25)
+    x[5, 0] = np.float16(127.0 * 0.25 * 2 / 3)      # a value that lands near a .5 after scaling
+    wq = np.clip(np.rint(s.normal(72 * 384) * 40.0), -127, 127).astype(np.int8).reshape(72, 384)
+    ws = f16(np.abs(s.normal(72 * 3)) * 0.01 + 1e-3).astype(f32).reshape(72, 3)
+    resid = s.normal_f16((40, 72))
+    qa, sa = g128_quantize(x, 384, False)
+    g["g128_x"], g["g128_qa"], g["g128_sa"] = x, qa, sa
+    g["g128_wq"], g["g128_ws"], g["g128_resid"] = wq, ws, resid
+    g["g128_out"] = g128_gemm(qa, sa, wq, ws, None)
+    g["g128_out_resid"] = g128_gemm(qa, sa, wq, ws, resid)
+    xg = s.normal_f16((24, 512))
+    xg[0, :256] = np.float16(-100.0)
+    xg[1, :256] = np.float16(95.0)
+    xg[2, :256] = (np.arange(256) - 128).astype(np.float16)
+    g["g128_xg"] = xg
+    g["g128_qg"], g["g128_sg"] = g128_quantize(xg, 256, True)
+    ex = np.concatenate([np.linspace(-90, 90, 721, dtype=f32), f32([-87.0, -86.99, 88.49, 88.5, 0.0, -0.0])])
+    g["g128_exp_x"], g["g128_exp_y"] = ex, g128_exp(ex)
 
     np.savez_compressed(HERE / "golden.npz", **g)
     print("wrote", HERE / "golden.npz", sum(v.nbytes for v in g.values()), "bytes raw")

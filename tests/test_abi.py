@@ -124,3 +124,20 @@ def test_ring_table(la):
     assert list(t) == [b % 6 for b in range(20)]
     with pytest.raises(la.LFM3AError):
         la.ring_table(5, 4)   # whole 64-token int8 V blocks: an even ring
+
+
+def test_g128_sizes_and_checks(la):
+    lib = la.lib()
+    assert lib.lfm3a_g128_packed_bytes(300, 384) == 3 * 3 * 16384
+    assert lib.lfm3a_g128_scale_bytes(300, 384) == 3 * 384 * 4
+    assert lib.lfm3a_g128_workspace_bytes(300, 384) == 3 * 3 * 16384 + 3 * 384 * 4
+    assert lib.lfm3a_g128_packed_bytes(300, 100) == la.EINVAL
+    assert lib.lfm3a_g128_packed_bytes(0, 128) == la.EINVAL
+    # argument checks answer before anything reaches the device
+    assert lib.lfm3a_g128_gemm(None, None, None, None, 4, 4, 128, None, 0, None, 0, None) == la.EINVAL
+    assert lib.lfm3a_g128_gemm(None, None, None, None, 4, 4, 96, None, 0, None, 0, None) == la.EINVAL
+    assert lib.lfm3a_g128_quantize(None, 128, 4, 128, 0, None, None, None) == la.EINVAL
+    assert lib.lfm3a_g128_pack(None, 128, None, 1, 4, 128, None, None, None) == la.EINVAL
+    ws = ctypes.create_string_buffer(64)
+    addr = (ctypes.addressof(ws) + 15) & ~15
+    assert lib.lfm3a_g128_linear(None, 128, 4, 0, None, None, 4, 128, None, 0, None, 4, addr, 16, None) == la.EWORKSPACE

@@ -75,3 +75,48 @@ def test_accept(orc, g):
     assert orc.accept(best, toks) == want[0]
     assert orc.accept(best[:1], toks[:1]) == want[1]
     assert orc.accept(best, np.array([4, 0, 0, 0, 0, 0, 0, 0], dtype=np.int32)) == want[2]
+
+
+def test_g128_exp(orc, g):
+    got = np.array([orc.g128_exp(float(x)) for x in g["g128_exp_x"]], dtype=np.float32)
+    assert np.array_equal(got.view(np.uint32), g["g128_exp_y"].view(np.uint32))
+    # within 2 ulp of e^x over its finite range
+    x = g["g128_exp_x"].astype(np.float64)
+    live = (x >= -87) & (x < 88.5)
+    rel = np.abs(got[live] / np.exp(x[live]) - 1.0)
+    assert rel.max() < 2.5 * 2.0 ** -24
+
+
+def test_g128_quantize(orc, g):
+    q, sc = orc.g128_quantize(g["g128_x"], 384)
+    assert np.array_equal(q, g["g128_qa"])
+    assert np.array_equal(sc.view(np.uint32), g["g128_sa"].view(np.uint32))
+    assert sc[3, 1] == 1.0 and not q[3, 128:256].any()
+
+
+def test_g128_quantize_gated(orc, g):
+    q, sc = orc.g128_quantize(g["g128_xg"], 256, gated=True)
+    assert np.array_equal(q, g["g128_qg"])
+    assert np.array_equal(sc.view(np.uint32), g["g128_sg"].view(np.uint32))
+
+
+def test_g128_gemm(orc, g):
+    out = orc.g128_gemm(g["g128_qa"], g["g128_sa"], g["g128_wq"], g["g128_ws"])
+    assert np.array_equal(bits(out), bits(g["g128_out"]))
+    out = orc.g128_gemm(g["g128_qa"], g["g128_sa"], g["g128_wq"], g["g128_ws"], residual=g["g128_resid"])
+    assert np.array_equal(bits(out), bits(g["g128_out_resid"]))
+
+
+def test_g128_tiles_round_trip(orc):
+    rng = np.random.default_rng(5)
+    q = rng.integers(-127, 128, size=(300, 384)).astype(np.int8)
+    sc = rng.random((300, 3)).astype(np.float32)
+    packed, sp = orc.g128_pack(q, sc)
+    assert packed.size == 3 * 3 * 16384 and sp.shape == (3, 384)
+    assert np.all(sp[:, 300:] == 1.0)
+    q2, s2 = orc.g128_unpack(packed, sp, 300, 384)
+    assert np.array_equal(q2, q) and np.array_equal(s2, sc)
+    # row r, column c of group g, tile t sits at block (g, t), ((r/8)*8 + c/16)*128 + (r%8)*16 + c%16
+    blk = packed.view(np.int8).reshape(3, 3, 16384)
+    r, c = 133, 200
+    assert blk[c // 128, r // 128, ((r % 128) // 8 * 8 + (c % 128) // 16) * 128 + (r % 8) * 16 + c % 16] == q[r, c]
