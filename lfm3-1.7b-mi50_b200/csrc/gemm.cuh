@@ -151,18 +151,20 @@ __global__ __launch_bounds__(128) void g128_pack_kernel(const int8_t* __restrict
 // ---------------------------------------------------------------- GEMM
 // Persistent: each CTA walks output tiles of 128 rows x 256 columns (t = blockIdx.x, + gridDim.x, ...;
 // rows fastest, so the CTAs of one wave share weight tiles in L2). For every (tile, group) step:
-//   warp 8   producer: bulk copies of the A block (16 KiB) and the one or two B blocks (16 / 32 KiB) into
-//            a 4-stage ring, and of the step's scales (128 + 256 floats) into an 8-slot ring;
-//   warp 9   MMA issuer (one thread): Dacc(s32, TMEM) += A x B^T, kind::i8 s8 x s8, M128 N256, four K32
-//            steps, into one of two 256-column s32 buffers (steps alternate);
-//   warps 0-7 fold, thread = (row, 128-column half): acc = fma(float(s) * sb, sa, acc) for the row's 128
-//            columns in registers, then the buffer is handed back;
-//   warps 10-11 idle (they complete the control warpgroup, whose registers go to the fold warps:
-//            setmaxnreg 56 for warps 8-11, 216 for warps 0-7; 128 x 56 + 256 x 216 = 62464 of the
-//            384 x 168 the block is launched with, checked on the host before the first launch). The s32 columns hold 0x4B400000 before
-//            each MMA chain (set in the prologue and again after every read) and the MMA accumulates onto
-//            it: |s| <= 128 * 127 * 127 < 2^22, so a column reads back as the float 1.5 * 2^23 + s and one
-//            FADD gives float(s) exactly, with no integer conversion.
+//   warp 16    producer: bulk copies of the A block (16 KiB) and the one or two B blocks (16 / 32 KiB) into
+//              a 4-stage ring;
+//   warp 18    scale producer: the step's scales (128 + 256 floats) into an 8-slot ring;
+//   warp 17    MMA issuer (one thread): Dacc(s32, TMEM) += A x B^T, kind::i8 s8 x s8, M128 N256, four K32
+//              steps, into one of two 256-column s32 buffers (steps alternate);
+//   warps 0-15 fold, thread = (row, 64-column quarter): acc = fma(float(s) * sb, sa, acc) for the row's 64
+//              columns in registers, then the buffer is handed back. Four fold warps share each TMEM lane
+//              quadrant, so the latency of one warp's TMEM loads hides behind the other three's arithmetic;
+//   warp 19    idle: it completes the control warpgroup, whose registers go to the fold warps
+//              (setmaxnreg 32 for warps 16-19, 112 for warps 0-15; 128 x 32 + 512 x 112 = 61440, all of the
+//              640 x 96 the block is launched with, checked on the host before the first launch).
+// The s32 columns hold 0x4B400000 before each MMA chain (set in the prologue and again after every read) and
+// the MMA accumulates onto it: |s| <= 128 * 127 * 127 < 2^22, so a column reads back as the float
+// 1.5 * 2^23 + s and one FADD gives float(s) exactly, with no integer conversion.
 // Two s32 buffers let the MMAs of step i + 1 run while step i is folded, and across tile boundaries while
 // the fold warps store a finished tile (fp16, plus the optional residual, gemm.hip:232-254).
 constexpr int kGmStages = 4, kGmScSlots = 8;
@@ -175,9 +177,11 @@ constexpr int kGmOffTmemSlot = kGmOffBar + kGmBars * 8;
 constexpr int kGmOffAbort = kGmOffTmemSlot + 4;
 constexpr int kGmSmem = kGmOffAbort + 4;
 constexpr int kGmRequest = kGmSmem + 1024;                       // room to align the base to 1024
-constexpr int kGmThreads = 384;
-constexpr int kGmFoldRegs = 216, kGmCtrlRegs = 56;   // setmaxnreg shares (multiples of 8)
-constexpr int kGmProducerWarp = 8, kGmMmaWarp = 9;
+constexpr int kGmFoldWarps = 16;                                // four per TMEM lane quadrant
+constexpr int kGmFoldCols = 256 / (kGmFoldWarps / 4);           // columns of the tile a fold thread owns
+constexpr int kGmThreads = 32 * (kGmFoldWarps + 4);
+constexpr int kGmFoldRegs = 112, kGmCtrlRegs = 32;   // setmaxnreg shares (multiples of 8)
+constexpr int kGmProducerWarp = kGmFoldWarps, kGmMmaWarp = kGmFoldWarps + 1, kGmScaleWarp = kGmFoldWarps + 2;
 // kind::i8: s32 accumulator (bit 4), A and B signed (bits 7 and 10), N >> 3 at bit 17, M >> 4 at bit 24.
 constexpr uint32_t kIdescS8M128N256 = (2u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
 
@@ -219,11 +223,11 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
     }
     for (int s = 0; s < kGmScSlots; ++s) {
       mbar_init(&sc_full[s], 1);
-      mbar_init(&sc_empty[s], 8);
+      mbar_init(&sc_empty[s], kGmFoldWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&d_full[b], 1);
-      mbar_init(&d_free[b], 8);
+      mbar_init(&d_free[b], kGmFoldWarps);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -239,7 +243,7 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 8) {
+  if (warp < kGmFoldWarps) {
     // ================================================================ fold warps
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kGmFoldRegs) : "memory");
     const int h = warp >> 2, q = warp & 3, r = 32 * q + lane;
@@ -248,7 +252,7 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
 #pragma unroll
     for (int b = 0; b < 2; ++b)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) tmem_st16_fill(lane_base + 256 * b + 128 * h + 16 * c, 0x4B400000u);
+      for (int c = 0; c < kGmFoldCols / 8; ++c) tmem_st8_fill(lane_base + 256 * b + kGmFoldCols * h + 8 * c, 0x4B400000u);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -262,9 +266,9 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
     int it = 0;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       const int tm = t % a.m_tiles, tn = t / a.m_tiles;
-      float acc[128];
+      float acc[kGmFoldCols];
 #pragma unroll
-      for (int e = 0; e < 128; ++e) acc[e] = 0.f;
+      for (int e = 0; e < kGmFoldCols; ++e) acc[e] = 0.f;
       for (int g = 0; g < G; ++g, ++it) {
         if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
           ok = false;
@@ -281,22 +285,23 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
         const float* sc = sSc + slot * 384;
         const float sa = sc[r];
         const float2 sa2 = make_float2(sa, sa);
-        const float4* sb4 = reinterpret_cast<const float4*>(sc + 128 + 128 * h);
+        const float4* sb4 = reinterpret_cast<const float4*>(sc + 128 + kGmFoldCols * h);
         uint32_t dep = __float_as_uint(sa);
+        // Chunks of 8 columns: one TMEM load, its wait, the bias written back, two scale loads, the fold.
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t dv[16];
-          tmem_ld16_after(lane_base + 256 * b + 128 * h + 16 * c, dv, dep);
+        for (int c = 0; c < kGmFoldCols / 8; ++c) {
+          uint32_t dv[8];
+          tmem_ld8_after(lane_base + 256 * b + kGmFoldCols * h + 8 * c, dv, dep);
           tmem_wait_ld();
-          reg_fence16(dv);
-          tmem_st16_fill(lane_base + 256 * b + 128 * h + 16 * c, 0x4B400000u);
+          reg_fence8(dv);
+          tmem_st8_fill(lane_base + 256 * b + kGmFoldCols * h + 8 * c, 0x4B400000u);
 #pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            float4 s4;   // after this chunk's TMEM load: hoisted, the 32 scale loads of a step hold 128 registers
+          for (int e4 = 0; e4 < 2; ++e4) {
+            float4 s4;   // after this chunk's TMEM load: hoisted, a step's scale loads hold 64 registers
             asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
                          : "=f"(s4.x), "=f"(s4.y), "=f"(s4.z), "=f"(s4.w)
-                         : "r"(smem_u32(sb4 + 4 * c + e4)));
-            const int e = 16 * c + 4 * e4;
+                         : "r"(smem_u32(sb4 + 2 * c + e4)));
+            const int e = 8 * c + 4 * e4;
             const float2 d01 = fadd2(make_float2(__uint_as_float(dv[4 * e4]), __uint_as_float(dv[4 * e4 + 1])), nmag2);
             const float2 d23 =
                 fadd2(make_float2(__uint_as_float(dv[4 * e4 + 2]), __uint_as_float(dv[4 * e4 + 3])), nmag2);
@@ -309,7 +314,7 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
             acc[e + 2] = r23.x;
             acc[e + 3] = r23.y;
           }
-          dep = __float_as_uint(acc[16 * c + 15]);
+          dep = __float_as_uint(acc[8 * c + 7]);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -321,13 +326,13 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
       }
       if (!ok) break;
       // The finished tile: fp16(acc [+ residual]) as __floats2half2_rn rounds (gemm.hip:232-254).
-      const int m = tm * 128 + r, n0 = tn * 256 + 128 * h;
+      const int m = tm * 128 + r, n0 = tn * 256 + kGmFoldCols * h;
       if (m < a.rows && n0 < a.outputs) {
         __half* orow = a.out + (int64_t)m * a.out_stride + n0;
         const __half* rrow = a.residual ? a.residual + (int64_t)m * a.residual_stride + n0 : nullptr;
         const bool vec = ((reinterpret_cast<uintptr_t>(orow) | (rrow ? reinterpret_cast<uintptr_t>(rrow) : 0)) & 15u) == 0;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
+        for (int c = 0; c < kGmFoldCols / 8; ++c) {
           float y[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) y[i] = acc[8 * c + i];
@@ -365,9 +370,18 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kGmCtrlRegs) : "memory");
   }
-  if (warp == kGmProducerWarp) {
-    // ================================================================ producer
-    int it = 0, issued = 0, sc_issued = 0;
+  if (warp == kGmProducerWarp || warp == kGmScaleWarp) {
+    // ================================================================ producers
+    // Two independent streams: the operand blocks through the 4-stage ring (warp 16) and the scales through
+    // the 8-slot ring (warp 18). Only the fold reads the scales, so they run up to eight steps ahead of it,
+    // not behind the operand ring: tied to it, a scale copy was issued only once the MMAs of four steps back
+    // had completed, and its latency sat in the chain MMA(i) -> fold(i) -> MMA(i + 2) (0.72 us a step with
+    // no operand copies at all, against 0.36 us of MMAs).
+    const bool scales = warp == kGmScaleWarp;
+    const int ring = scales ? kGmScSlots : kGmStages;
+    uint64_t* ful = scales ? sc_full : full;
+    uint64_t* emp = scales ? sc_empty : empty;
+    int it = 0, issued = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       const int tm = t % a.m_tiles, tn = t / a.m_tiles;
@@ -377,45 +391,34 @@ __global__ __launch_bounds__(kGmThreads, 1) void g128_gemm_kernel(G128Args a) {
           ok = false;
           break;
         }
-        const int st = it % kGmStages, slot = it % kGmScSlots;
-        if (it >= kGmStages &&
-            !__all_sync(0xffffffffu, mbar_wait(&empty[st], (uint32_t)(it / kGmStages - 1) & 1u))) {
+        const int st = it % ring;
+        if (it >= ring && !__all_sync(0xffffffffu, mbar_wait(&emp[st], (uint32_t)(it / ring - 1) & 1u))) {
           raise_error(kErrWaitEmpty);
           ok = false;
           break;
         }
         if (lane == 0) {
-          uint8_t* dst = smem + st * kGmStage;
-          mbar_arrive_expect_tx(&full[st], (uint32_t)(kG128Block * (1 + nb)));
-          bulk_g2s(dst, a.a + ((int64_t)g * a.m_tiles + tm) * kG128Block, kG128Block, &full[st]);
-          bulk_g2s(dst + kG128Block, a.b + ((int64_t)g * a.n_blocks + 2 * tn) * kG128Block, kG128Block * nb,
-                   &full[st]);
+          if (scales) {
+            uint8_t* dst = smem + kGmOffSc + st * kGmScSlot;
+            mbar_arrive_expect_tx(&ful[st], (uint32_t)(512 * (1 + nb)));
+            bulk_g2s(dst, a.sa + (int64_t)g * a.m_tiles * 128 + tm * 128, 512, &ful[st]);
+            bulk_g2s(dst + 512, a.sb + (int64_t)g * a.n_blocks * 128 + tn * 256, 512 * nb, &ful[st]);
+          } else {
+            uint8_t* dst = smem + st * kGmStage;
+            mbar_arrive_expect_tx(&ful[st], (uint32_t)(kG128Block * (1 + nb)));
+            bulk_g2s(dst, a.a + ((int64_t)g * a.m_tiles + tm) * kG128Block, kG128Block, &ful[st]);
+            bulk_g2s(dst + kG128Block, a.b + ((int64_t)g * a.n_blocks + 2 * tn) * kG128Block, kG128Block * nb,
+                     &ful[st]);
+          }
         }
         __syncwarp();
         issued = it + 1;
-        if (it >= kGmScSlots &&
-            !__all_sync(0xffffffffu, mbar_wait(&sc_empty[slot], (uint32_t)(it / kGmScSlots - 1) & 1u))) {
-          raise_error(kErrWaitEmpty);
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
-          uint8_t* dst = smem + kGmOffSc + slot * kGmScSlot;
-          mbar_arrive_expect_tx(&sc_full[slot], (uint32_t)(512 * (1 + nb)));
-          bulk_g2s(dst, a.sa + (int64_t)g * a.m_tiles * 128 + tm * 128, 512, &sc_full[slot]);
-          bulk_g2s(dst + 512, a.sb + (int64_t)g * a.n_blocks * 128 + tn * 256, 512 * nb, &sc_full[slot]);
-        }
-        __syncwarp();
-        sc_issued = it + 1;
       }
     }
     if (!ok) atomicExch(&s_abort, 1);
     // Behind an abort, wait (bounded) for the copies still landing in shared memory.
     if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_abort) != 0)) {
-      for (int i = max(0, issued - kGmStages); i < issued; ++i)
-        mbar_wait(&full[i % kGmStages], (uint32_t)(i / kGmStages) & 1u);
-      for (int i = max(0, sc_issued - kGmScSlots); i < sc_issued; ++i)
-        mbar_wait(&sc_full[i % kGmScSlots], (uint32_t)(i / kGmScSlots) & 1u);
+      for (int i = max(0, issued - ring); i < issued; ++i) mbar_wait(&ful[i % ring], (uint32_t)(i / ring) & 1u);
     }
   } else if (warp == kGmMmaWarp) {
     // ================================================================ MMA issuer

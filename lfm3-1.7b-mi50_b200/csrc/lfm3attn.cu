@@ -684,7 +684,7 @@ int lfm3a_g128_gemm(const void* a, const float* sa, const void* b, const float* 
     cudaFuncAttributes fa;
     const cudaError_t e = cudaFuncGetAttributes(&fa, g128_gemm_kernel);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
-    if (fa.numRegs * kGmThreads < 128 * kGmCtrlRegs + 256 * kGmFoldRegs)
+    if (fa.numRegs * kGmThreads < 128 * kGmCtrlRegs + 32 * kGmFoldWarps * kGmFoldRegs)
       return fail(LFM3A_ENOTSUP, "g128_gemm_kernel built with too few registers for its setmaxnreg split");
     regs_ok[dev] = true;
   }
