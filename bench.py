@@ -53,7 +53,7 @@ def parse():
                          "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
                          "synchronisation, which both pay)")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 and decode fields (N = 1)")
-    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode", "chunks", "gemm"],
+    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode", "chunks", "gemm", "ref"],
                     help="run only that configuration's measurement on one GPU and print its fields (for profiling)")
     return ap.parse_args()
 
@@ -77,6 +77,8 @@ def run_only(args) -> int:
         res = measure_prefill_chunks(la, dev)
     elif args.only == "gemm":
         res = measure_gemm(la, dev, pk)
+    elif args.only == "ref":
+        res = measure_ref_geometries(la, synth, dev, pk["hbm_gbs"])
     else:
         res = measure_c5(la, dev)
     print(json.dumps({args.only: res}), flush=True)
@@ -394,6 +396,69 @@ def measure_decode(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_cache
             "attention_us_back_to_back": round(b2b_us, 2),
             "frac_back_to_back": round(byts / (b2b_us * 1e-6) / 1e9 / peak_gbs, 4), "bytes": byts,
             "caches": n_caches}
+
+
+# The reference's published verify timings on its MI50 (benchmarks/verify_attention.txt:11-14), M = 8 verified
+# tokens at its own geometry (16/4/128); its K/V are int8 records (264 B per token and head), these fp16.
+REF_MI50_VERIFY_US = {32768: 163.3, 131072: 557.3}
+
+
+def measure_ref_geometry(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_caches: int, m: int = 8,
+                         steps: int = 60) -> dict:
+    """Verify at the reference model's own geometry: 16 query heads, 4 kv heads, head_dim 128 (RoPE theta 1e6
+    over half the dims), m = 8 tokens over ctx cached tokens; rounds of append + attention + rollback, and the
+    attention back to back. The published MI50 figure for the same m and context is reported beside it."""
+    import numpy as np
+    import torch
+
+    qh, kvh, d = 16, 4, 128
+    case = synth.verify_case(seed, ctx, m, q_heads=qh, kv_heads=kvh, head_dim=d)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    rope = t(la.rope_table(1e6, 0.5, d, ctx + m + 1).view(np.float16))
+    K0, V0 = t(case["K"]), t(case["V"])
+    caches = []
+    for _ in range(n_caches):
+        c = la.LayerCache(la.MODE_F16, kvh, d, ctx + 64, device=dev)
+        c.append(K0, V0, 0)
+        caches.append(c)
+    del K0, V0
+    q, nk, nv = t(case["Q"]), t(case["newK"]), t(case["newV"])
+    out = torch.empty_like(q)
+    splits = la.verify_splits(caches[0].layout, ctx, m, 0)
+    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8, device=dev)
+
+    def step(c, ev=None):   # one round: append the drafts (its own kernel at head_dim 128), attend, roll back
+        if ev:
+            ev[0].record()
+        c.verify_round(nk, nv, q, ctx, rope=rope, out=out, workspace=ws, splits=splits)
+        if ev:
+            ev[1].record()
+        c.truncate(ctx)
+
+    for i in range(2 * n_caches):
+        step(caches[i % n_caches])
+    torch.cuda.synchronize()
+    step_us, att_us = graph_step_us(torch, dev, lambda i, ev=None: step(caches[i % n_caches], ev), steps)
+    b2b_us = back_to_back_us(torch, lambda i: caches[i % n_caches].verify(q, ctx, out=out, workspace=ws, splits=splits),
+                             60)
+    la.sync()
+    byts = (ctx + m) * kvh * d * 2 * 2
+    res = {"workload": f"verify at the reference geometry 16/4/128: {m} tokens over {ctx} cached tokens (seed {seed})",
+           "us_per_layer": round(step_us, 2), "attention_us_back_to_back": round(b2b_us, 2), "splits": splits,
+           "hbm_gbs_back_to_back": round(byts / (b2b_us * 1e-6) / 1e9, 1),
+           "frac_back_to_back": round(byts / (b2b_us * 1e-6) / 1e9 / peak_gbs, 4), "bytes": byts, "caches": n_caches}
+    if ctx in REF_MI50_VERIFY_US:
+        res["reference_mi50_us"] = REF_MI50_VERIFY_US[ctx]
+    return res
+
+
+def measure_ref_geometries(la, synth, dev, peak_gbs: float) -> dict:
+    import torch
+
+    res = {"32k": measure_ref_geometry(la, synth, dev, peak_gbs, 32768, 11, 4)}
+    torch.cuda.empty_cache()
+    res["128k"] = measure_ref_geometry(la, synth, dev, peak_gbs, 131072, 12, 2)
+    return res
 
 
 def measure_prefix(la, tokens: int = 131072, reps: int = 5) -> dict:
@@ -908,6 +973,8 @@ def run_ours(args):
         extras["prefill_chunks"] = measure_prefill_chunks(la, dev)
         torch.cuda.empty_cache()
         extras["gemm"] = measure_gemm(la, dev, pk)
+        torch.cuda.empty_cache()
+        extras["ref_geometry"] = measure_ref_geometries(la, synth, dev, pk["hbm_gbs"])
         torch.cuda.empty_cache()
         extras["c5"] = measure_c5(la, dev)
 

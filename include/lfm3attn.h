@@ -124,7 +124,9 @@ int lfm3a_verify_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int w
  * and the drafts ctx_len .. ctx_len + t. q: device fp16 [m][q_heads][head_dim]. gate: device fp16
  * [m][q_heads] logits (out *= sigmoid) or NULL. out: device fp16 [m][q_heads][head_dim].
  * workspace: lfm3a_verify_workspace_bytes bytes when splits > 1 (may be NULL for one split).
- * MODE_F16, head_dim 64, q_heads = 4 * kv_heads, 1 <= m <= 32. */
+ * MODE_F16, q_heads = 4 * kv_heads; head_dim 64 with 1 <= m <= 32, or head_dim 128 (the reference model's
+ * 16/4/128 geometry) with 1 <= m <= 16. The same holds for the other verify entry points below, except the
+ * gather exchange (head_dim 64). */
 int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
                            const void* gate, void* out, void* workspace, size_t workspace_bytes, int splits,
                            void* stream);

@@ -108,12 +108,12 @@ int launch_v8(const lfm3a_kv_view* kv, int qb0, int qb1, int len, cudaStream_t s
   return check_launch("v8_quant_kernel");
 }
 
-int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count) {
+int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count, int blocks_per_sm = 2) {
   const int start = window > 0 ? std::max(0, ctx_len - window + 1) : 0;
   const int tile_keys = m <= 16 ? 128 : 64;
   const int t_total = (ctx_len + m - 1) / tile_keys - start / tile_keys + 1;
-  // Two resident blocks per SM, at least two 64-key tiles per split.
-  int splits = (2 * sm_count + kv_heads - 1) / kv_heads;
+  // Two resident blocks per SM (one at head_dim 128), at least two tiles per split.
+  int splits = (blocks_per_sm * sm_count + kv_heads - 1) / kv_heads;
   splits = std::min(splits, std::max(1, t_total / 2));
   return std::max(1, splits);
 }
@@ -150,8 +150,11 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
   const lfm3a_kv_layout& L = kv->layout;
-  if (L.mode != LFM3A_MODE_F16 || L.head_dim != 64) return fail(LFM3A_ENOTSUP, "verify attention needs MODE_F16, head_dim 64");
+  if (L.mode != LFM3A_MODE_F16 || (L.head_dim != 64 && !(L.head_dim == 128 && m <= 16)))
+    return fail(LFM3A_ENOTSUP, "verify attention needs MODE_F16 and head_dim 64 (or 128 for up to 16 tokens)");
   if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "verify attention needs 4 query heads per kv head");
+  const int D = L.head_dim;
+  if (gather && D != 64) return fail(LFM3A_ENOTSUP, "the gather exchange needs head_dim 64");
   if (!q || (!out16 && !out32 && !gather) || m < 1 || m > 32 || ctx_len < 0 || window < 0)
     return fail(LFM3A_EINVAL, "bad verify arguments");
   if (kv_begin < 0 || kv_end <= kv_begin || kv_end > ctx_len + m) return fail(LFM3A_EINVAL, "bad key range");
@@ -175,9 +178,10 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   const int tile_keys = m <= 16 ? 128 : 64;
   a.t_begin = std::min(a.start, kv_end - 1) / tile_keys;
   a.t_total = (kv_end - 1) / tile_keys - a.t_begin + 1;
-  if (splits <= 0) splits = verify_splits_for(L.kv_heads, a.t_total * tile_keys, 1, 0, current_sm_count());
+  if (splits <= 0)
+    splits = verify_splits_for(L.kv_heads, a.t_total * tile_keys, 1, 0, current_sm_count(), D == 64 ? 2 : 1);
   a.splits = std::min(splits, a.t_total);
-  a.qk_scale = 0.125f * kLog2e;
+  a.qk_scale = (D == 64 ? 0.125f : 1.f / sqrtf(128.f)) * kLog2e;
   a.causal = causal ? 1 : 0;
   a.append = 0;
   a.lighten = 0;
@@ -188,7 +192,7 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
     const int lighten = a.splits > 1 && a.t_total / a.splits >= kAppendTiles + 2 ? kAppendTiles : 0;
     const int span = a.t_total + lighten;
     const int last_tile0 = a.t_begin + std::min(a.t_total, (int)((int64_t)span * (a.splits - 1) / a.splits));
-    const bool fuse = m <= 16 && last_tile0 * tile_keys <= app->pos0 / kQuantBlock * kQuantBlock;
+    const bool fuse = m <= 16 && D == 64 && last_tile0 * tile_keys <= app->pos0 / kQuantBlock * kQuantBlock;
     if (fuse) {
       a.append = 1;
       a.lighten = lighten;
@@ -204,7 +208,7 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
     a.part = out32;
   } else if (a.splits > 1) {
     if (!workspace || !aligned16(workspace)) return fail(LFM3A_EINVAL, "verify needs a 16-byte aligned workspace");
-    if (workspace_bytes < lfm3a_verify_workspace_bytes(m, q_heads, 64, a.splits))
+    if (workspace_bytes < lfm3a_verify_workspace_bytes(m, q_heads, D, a.splits))
       return fail(LFM3A_EWORKSPACE, "verify workspace too small");
     a.part = static_cast<float*>(workspace);
   } else {
@@ -212,11 +216,15 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   }
   if (!(a.splits == 1 && out16)) a.out = nullptr;
   const dim3 grid(a.splits, L.kv_heads);
-  static bool done[2][64];
-  if (m <= 16) {
-    rc = ensure_smem(verify_m64_kernel, kV6Smem, done[1]);
+  static bool done[3][64];
+  if (m <= 16 && D == 128) {
+    rc = ensure_smem(verify_m64_kernel<128>, V6Layout<128>::kSmem, done[2]);
     if (rc != LFM3A_OK) return rc;
-    launch_pdl(verify_m64_kernel, grid, kVfThreads, kV6Smem, st, a);
+    launch_pdl(verify_m64_kernel<128>, grid, kVfThreads, V6Layout<128>::kSmem, st, a);
+  } else if (m <= 16) {
+    rc = ensure_smem(verify_m64_kernel<64>, kV6Smem, done[1]);
+    if (rc != LFM3A_OK) return rc;
+    launch_pdl(verify_m64_kernel<64>, grid, kVfThreads, kV6Smem, st, a);
   } else {
     rc = ensure_smem(verify_kernel<false>, kVfSmem, done[0]);
     if (rc != LFM3A_OK) return rc;
@@ -228,7 +236,7 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
     if (a.splits == 1) return fail(LFM3A_ENOTSUP, "the gather needs several splits (a combine)");
     gather->half_stride = (int64_t)gather->world * rows * 64;
   }
-  return launch_combine(a.part, rows, a.splits, 64, kVerifyPart, (int64_t)a.splits * kVerifyPart,
+  return launch_combine(a.part, rows, a.splits, D, D + 2, (int64_t)a.splits * (D + 2),
                         static_cast<const __half*>(gate), out16, out32, st, gather);
 }
 
@@ -388,7 +396,8 @@ size_t lfm3a_verify_workspace_bytes(int m, int q_heads, int head_dim, int splits
 
 int lfm3a_verify_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int window, int sm_count) {
   if (!layout || ctx_len < 0 || m < 1) return fail(LFM3A_EINVAL, "bad verify split arguments");
-  return verify_splits_for(layout->kv_heads, ctx_len, m, window, sm_count > 0 ? sm_count : current_sm_count());
+  return verify_splits_for(layout->kv_heads, ctx_len, m, window, sm_count > 0 ? sm_count : current_sm_count(),
+                           layout->head_dim == 128 && m <= 16 ? 1 : 2);
 }
 
 int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
@@ -404,7 +413,9 @@ int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int
 int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
                            const void* gate, void* out, void* workspace, size_t workspace_bytes, int splits,
                            void* stream) {
-  if (splits <= 0 && kv) splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count());
+  if (splits <= 0 && kv)
+    splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count(),
+                               kv->layout.head_dim == 128 && m <= 16 ? 1 : 2);
   return run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, static_cast<__half*>(out), nullptr,
                     workspace, workspace_bytes, splits, as_stream(stream));
 }
@@ -425,7 +436,9 @@ int lfm3a_verify_attention_static(const lfm3a_kv_view* kv, const void* q, int m,
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_verify_scratch)");
     scratch[dev] = p;
   }
-  if (splits <= 0 && kv) splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count());
+  if (splits <= 0 && kv)
+    splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count(),
+                               kv->layout.head_dim == 128 && m <= 16 ? 1 : 2);
   const int rc = run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, static_cast<__half*>(out),
                             nullptr, scratch[dev], LFM3A_VERIFY_SCRATCH_BYTES, splits, as_stream(stream));
   if (rc == LFM3A_EWORKSPACE)
@@ -585,7 +598,9 @@ int lfm3a_verify_attention_gather(const lfm3a_kv_view* kv, const void* q, int m,
     if (!peers[w] || !aligned16(peers[w])) return fail(LFM3A_EINVAL, "gather regions must be 16-byte aligned");
     go.peers[w] = static_cast<__half*>(peers[w]);
   }
-  if (splits <= 0 && kv) splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count());
+  if (splits <= 0 && kv)
+    splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count(),
+                               kv->layout.head_dim == 128 && m <= 16 ? 1 : 2);
   return run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, nullptr, nullptr, workspace,
                     workspace_bytes, splits, as_stream(stream), &go);
 }

@@ -435,27 +435,41 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_kernel(VerifyArgs a) {
 // keys of one row. QK is two interleaved M64 N64 chains per tile; PV is four independent M64 N64 chains
 // (warpgroup g, half h) into O_g at lane offset 16 h, so the tensor pipe overlaps them.
 constexpr int kV6Stages = 2;               // per ring
-constexpr int kV6Ring = 16384;             // K (or V) of one 128-key tile: 4 pages
-constexpr int kV6OffStage = 8192;          // after Q: 64 rows x 64 dims fp16; then the K ring, then the V ring
-constexpr int kV6PBuf = 16384;             // [warpgroup g][half h] 64 rows x 32 keys fp16, 4 KiB each
-constexpr int kV6OffP = kV6OffStage + 2 * kV6Stages * kV6Ring;
-constexpr int kV6OffBar = kV6OffP + 2 * kV6PBuf;
 constexpr int kV6Bars = 4 * kV6Stages + 2 + 4 + 2 + 3;   // K/V full/empty, s_full[2], p_full[2][2], pv_done[2], q_ready, drain, app_done
-constexpr int kV6OffTmemSlot = kV6OffBar + kV6Bars * 8;
-constexpr int kV6OffAbort = kV6OffTmemSlot + 4;
-constexpr int kV6Smem = kV6OffTmemSlot + 16;
 constexpr uint32_t kIdescF16M64N64 = (1u << 4) | ((64u >> 3) << 17) | ((64u >> 4) << 24);
+// Shared-memory and TMEM layout per head_dim D (64: the benchmark geometry, two CTAs per SM; 128: the
+// reference model's, one CTA per SM).
+template <int D>
+struct V6Layout {
+  static constexpr int kRing = 256 * D;                  // K (or V) of one 128-key tile: 4 pages of 64 D bytes
+  static constexpr int kPage = 64 * D;                   // one page's K (or V) section
+  static constexpr int kOffStage = 128 * D;              // after Q: 64 rows x D dims fp16; then the K ring, the V ring
+  static constexpr int kPBuf = 16384;                    // [warpgroup g][half h] 64 rows x 32 keys fp16, 4 KiB each
+  static constexpr int kOffP = kOffStage + 2 * kV6Stages * kRing;
+  static constexpr int kOffBar = kOffP + 2 * kPBuf;
+  static constexpr int kOffTmemSlot = kOffBar + kV6Bars * 8;
+  static constexpr int kOffAbort = kOffTmemSlot + 4;
+  static constexpr int kSmem = kOffTmemSlot + 16;
+  static constexpr uint32_t kSbo = 16 * D;               // bytes between 8-row groups of Q and of a K page
+  static constexpr uint32_t kTmemCols = D == 64 ? 256 : 512;   // S[2] at 0 and 64, O_g at 128 + D g
+  static constexpr uint32_t kIdescPV = (1u << 4) | ((uint32_t)(D >> 3) << 17) | ((64u >> 4) << 24);   // M64 N=D
+  static constexpr int kPart = D + 2;                    // acc[D], max, sum
+  static constexpr int kBlocksPerSm = D == 64 ? 2 : 1;
+};
+constexpr int kV6Smem = V6Layout<64>::kSmem;
 
-__global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a) {
+template <int D>
+__global__ __launch_bounds__(kVfThreads, V6Layout<D>::kBlocksPerSm) void verify_m64_kernel(VerifyArgs a) {
+  using L6 = V6Layout<D>;
   constexpr int NS = kV6Stages;   // per ring: K tiles and V tiles have separate rings
-  constexpr uint32_t kTmemCols = 256;   // S[2] at columns 0 and 64, O_0 at 128, O_1 at 192 (halves at lane +0 / +16)
+  constexpr uint32_t kTmemCols = L6::kTmemCols;   // S[2] at columns 0 and 64, O_g at 128 + D g (halves at lane +0 / +16)
   extern __shared__ __align__(1024) uint8_t smem[];
-  int& s_abort = *reinterpret_cast<int*>(smem + kV6OffAbort);
+  int& s_abort = *reinterpret_cast<int*>(smem + L6::kOffAbort);
   uint8_t* sQ = smem;
-  uint8_t* sStage = smem + kV6OffStage;
-  uint8_t* sP = smem + kV6OffP;          // [buffer b][warpgroup g][half h]
+  uint8_t* sStage = smem + L6::kOffStage;
+  uint8_t* sP = smem + L6::kOffP;          // [buffer b][warpgroup g][half h]
   float2* sML = reinterpret_cast<float2*>(smem);   // Q is dead once the last QK finished
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kV6OffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L6::kOffBar);
   uint64_t* k_full = bars;             // K ring: loaded / released once QK of the tile finished
   uint64_t* k_empty = bars + NS;
   uint64_t* v_full = bars + 2 * NS;    // V ring: loaded / released once PV of the tile finished
@@ -466,7 +480,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
   uint64_t* q_ready = pv_done + 2;
   uint64_t* drain = q_ready + 1;
   uint64_t* app_done = drain + 1;        // the fused append's stores are out (softmax warps -> producer)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kV6OffTmemSlot);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L6::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y;
@@ -521,18 +535,18 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
     const int row = t * a.q_heads + 4 * h + jh;       // output / partial row (valid when row_ok)
     if (g == 0) {
       if (hh == 0) {
-        const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)(row_ok ? row : 0) * 64);
+        const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)(row_ok ? row : 0) * D);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < D / 8; ++c) {
           const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(sQ + ((r >> 3) * 8 + c) * 128 + (r & 7) * 16) = v;
+          *reinterpret_cast<uint4*>(sQ + ((r >> 3) * (D / 8) + c) * 128 + (r & 7) * 16) = v;
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
     }
-    if (appender) {
+    if constexpr (D == 64) if (appender) {
       // The drafts' K (RoPE) and V into their pages, and the int8 V of every 64-token block they touch, by
       // the 256 softmax threads while the first K tile loads; the P buffers are the scratch (P is first
       // written after this). The stores are handed to the producer's bulk copies through app_done.
@@ -549,7 +563,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
       if (lane == 0) mbar_arrive(app_done);
     }
     const uint32_t lane_base = tmem + ((uint32_t)(32 * quad) << 16);
-    const uint32_t o_col = 128 + 64 * g;
+    const uint32_t o_col = 128 + D * g;
     const int qlast = a.ctx_len + a.m - 1;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -609,7 +623,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
           }
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < D / 16; ++c) {
             uint32_t rr[16];
             tmem_ld16(lane_base + o_col + c * 16, rr);
             tmem_wait_ld();
@@ -630,7 +644,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
       }
       l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // P_{g,h}[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
-      uint8_t* pb = sP + b * kV6PBuf + (2 * g + hh) * 4096;
+      uint8_t* pb = sP + b * L6::kPBuf + (2 * g + hh) * 4096;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint4 v;
@@ -662,6 +676,7 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
         const float f0 = m_run == -INFINITY ? 0.f : fast_exp2(m_run - M);
         const float f1 = mb.x == -INFINITY ? 0.f : fast_exp2(mb.x - M);
         float L = f0 * l_run + f1 * mb.y;
+        if constexpr (D == 64) {
         float o[64];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -701,6 +716,48 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
             *reinterpret_cast<float2*>(dst + 64) = make_float2(M, L);
           }
         }
+        } else {
+          // The same merge streamed 16 dims at a time (a whole row of 128 in registers would spill): the two
+          // halves' (max, sum) first, then per chunk O_0 and O_1, the half merge, and the store.
+          const float Mo = __shfl_xor_sync(0xffffffffu, M, 16), Lo = __shfl_xor_sync(0xffffffffu, L, 16);
+          const float Mm = fmaxf(M, Mo);
+          const float fa = M == -INFINITY ? 0.f : fast_exp2(M - Mm), fb = Mo == -INFINITY ? 0.f : fast_exp2(Mo - Mm);
+          M = Mm;
+          L = fa * L + fb * Lo;
+          const float scale = a.out && row_ok ? (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(a.gate, row) : 1.f;
+          float* pdst = a.out ? nullptr : a.part + ((int64_t)row * a.splits + split) * L6::kPart;
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t r0[16], r1[16];
+            tmem_ld16(lane_base + 128 + c * 16, r0);
+            tmem_ld16(lane_base + 128 + D + c * 16, r1);
+            tmem_wait_ld();
+            float o[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = f0 * __uint_as_float(r0[e]) + f1 * __uint_as_float(r1[e]);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = fa * o[e] + fb * __shfl_xor_sync(0xffffffffu, o[e], 16);
+            if (row_ok && hh == 0) {
+              if (a.out) {
+                uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)row * D + 16 * c);
+#pragma unroll
+                for (int q8 = 0; q8 < 2; ++q8) {
+                  uint4 v;
+                  v.x = pack_half2(o[8 * q8] * scale, o[8 * q8 + 1] * scale);
+                  v.y = pack_half2(o[8 * q8 + 2] * scale, o[8 * q8 + 3] * scale);
+                  v.z = pack_half2(o[8 * q8 + 4] * scale, o[8 * q8 + 5] * scale);
+                  v.w = pack_half2(o[8 * q8 + 6] * scale, o[8 * q8 + 7] * scale);
+                  dst[q8] = v;
+                }
+              } else {
+#pragma unroll
+                for (int e = 0; e < 16; e += 2)
+                  *reinterpret_cast<float2*>(pdst + 16 * c + e) = make_float2(o[e], o[e + 1]);
+              }
+            }
+          }
+          if (row_ok && hh == 0 && !a.out) *reinterpret_cast<float2*>(pdst + D) = make_float2(M, L);
+        }
       }
     }
   } else if (warp == kVfSoftmaxWarps) {
@@ -722,19 +779,19 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
           appended = true;
         }
         const int lp = (tile0 + jt) * 4;
-        uint8_t* dst = sStage + (is_v ? NS * kV6Ring : 0) + st * kV6Ring;
+        uint8_t* dst = sStage + (is_v ? NS * L6::kRing : 0) + st * L6::kRing;
         const char* src[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           // A page outside the held range may have no table entry: copy a held page instead (its keys are masked).
           const int pg = min(max(lp + e, pv0), pv1);
           src[e] = a.g.pool + phys_block(a.g, pg) * a.g.block_bytes + (int64_t)h * a.g.head_bytes +
-                   (is_v ? F16Section<64>::kOffV : 0);
+                   (is_v ? F16Section<D>::kOffV : 0);
         }
         if (lane == 0) {
-          mbar_arrive_expect_tx(&ful[st], kV6Ring);
+          mbar_arrive_expect_tx(&ful[st], L6::kRing);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) bulk_g2s(dst + 4096 * e, src[e], 4096, &ful[st]);
+          for (int e = 0; e < 4; ++e) bulk_g2s(dst + L6::kPage * e, src[e], L6::kPage, &ful[st]);
         }
         __syncwarp();
         return true;
@@ -763,18 +820,19 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
     {
       bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
-      const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
+      const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, L6::kSbo);
       auto issue_qk = [&](int jt) -> bool {
         const int st = jt % NS, b = jt & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (uint32_t)(jt / NS) & 1u))) return false;
         tc_fence_after();
-        const uint64_t k_desc = umma_desc(smem_u32(sStage + st * kV6Ring), 128, 1024);
+        const uint64_t k_desc = umma_desc(smem_u32(sStage + st * L6::kRing), 128, L6::kSbo);
         if (lane == 0) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
+          for (int ks = 0; ks < D / 16; ++ks)
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh)   // keys 64 hh..: +8 KiB (+512); lanes +16 hh
-              umma_f16_ss(tmem + ((uint32_t)(16 * hh) << 16) + b * 64, q_desc + 16 * ks, k_desc + 512 * hh + 16 * ks,
+            for (int hh = 0; hh < 2; ++hh)   // keys 64 hh..: two pages on (+8 SBO); lanes +16 hh
+              umma_f16_ss(tmem + ((uint32_t)(16 * hh) << 16) + b * 64, q_desc + 16 * ks,
+                          k_desc + (8 * L6::kSbo >> 4) * hh + 16 * ks,
                           kIdescF16M64N64, ks > 0 ? 1u : 0u);
           umma_commit(&s_full[b]);
           umma_commit(&k_empty[st]);
@@ -790,13 +848,13 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
       }
       for (int jt = 0; jt < ntiles && ok; ++jt) {
         const int b = jt & 1, st = jt % NS;
-        const uint64_t v_desc = umma_desc(smem_u32(sStage + NS * kV6Ring + st * kV6Ring), 128, 512);
+        const uint64_t v_desc = umma_desc(smem_u32(sStage + NS * L6::kRing + st * L6::kRing), 128, 512);
         if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (uint32_t)(jt / NS) & 1u))) {
           raise_error(kErrWaitFull);
           ok = false;
           break;
         }
-        const uint64_t p_desc = umma_desc(smem_u32(sP + b * kV6PBuf), 128, 512);
+        const uint64_t p_desc = umma_desc(smem_u32(sP + b * L6::kPBuf), 128, 512);
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
           if (!__all_sync(0xffffffffu, mbar_wait(&p_full[2 * b + g], (uint32_t)(jt >> 1) & 1u))) {
@@ -809,9 +867,10 @@ __global__ __launch_bounds__(kVfThreads, 2) void verify_m64_kernel(VerifyArgs a)
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-              for (int hh = 0; hh < 2; ++hh)   // P_{g,h} at +4 KiB (2g + h); V page 2h + g at +4 KiB each
-                umma_f16_ss(tmem + ((uint32_t)(16 * hh) << 16) + 128 + 64 * g, p_desc + 256 * (2 * g + hh) + 16 * ks,
-                            v_desc + 256 * (2 * hh + g) + 16 * ks, kIdescF16M64N64, (jt > 0 || ks > 0) ? 1u : 0u);
+              for (int hh = 0; hh < 2; ++hh)   // P_{g,h} at +4 KiB (2g + h); V page 2h + g at +64 D bytes each
+                umma_f16_ss(tmem + ((uint32_t)(16 * hh) << 16) + 128 + D * g, p_desc + 256 * (2 * g + hh) + 16 * ks,
+                            v_desc + (L6::kPage >> 4) * (2 * hh + g) + 16 * ks, L6::kIdescPV,
+                            (jt > 0 || ks > 0) ? 1u : 0u);
           }
           __syncwarp();
         }

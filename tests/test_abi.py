@@ -64,7 +64,8 @@ def test_argument_checks_without_device(la):
     assert lib.lfm3a_kv_append(ctypes.byref(view), None, None, 0, 0, 1, None, None, None) == la.EINVAL
     good = la.KvView(64, 64, 10, la.layout(0, 8, 64))
     bad_geom = la.KvView(64, 64, 10, la.layout(0, 4, 128))
-    assert lib.lfm3a_verify_attention(ctypes.byref(bad_geom), 64, 16, 16, 100, 0, None, 64, None, 0, 1, None) == la.ENOTSUP
+    # head_dim 128 is served for up to 16 verified tokens (verify_m64_kernel<128>); more is refused on the host
+    assert lib.lfm3a_verify_attention(ctypes.byref(bad_geom), 64, 17, 16, 100, 0, None, 64, None, 0, 1, None) == la.ENOTSUP
     assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 16, 100, 0, None, 64, None, 0, 1, None) == la.ENOTSUP
     assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 40, 32, 100, 0, None, 64, None, 0, 1, None) == la.EINVAL
     assert lib.lfm3a_verify_attention(ctypes.byref(good), 64, 16, 32, 1000, 0, None, 64, None, 0, 4, None) == la.EINVAL

@@ -236,3 +236,98 @@ def test_verify_round_matches_two_calls(la, orc, synth, cuda, ctx_len, m, splits
         length += keep
         fused.truncate(length)
         plain.truncate(length)
+
+
+# ---------------------------------------------------------------- the reference model's geometry
+# LFM3-1.7B itself (internal/model/engine.go:22-40): 16 query heads, 4 kv heads, head_dim 128, RoPE theta 1e6 over
+# half the dimensions (factor 0.5, engine.go:333-338). verify_m64_kernel<128> serves up to 16 tokens (the
+# reference verifies at most 9: an anchor and 8 drafts, dspark.hip:65).
+def setup_ref(la, orc, synth, cuda, seed, ctx_len, m):
+    case = synth.verify_case(seed, ctx_len, m, q_heads=16, kv_heads=4, head_dim=128)
+    cache = la.LayerCache(la.MODE_F16, 4, 128, ctx_len + m + 64, device=cuda)
+    rope_np = la.rope_table(1e6, 0.5, 128, ctx_len + m + 1)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    cache.append(dev(case["newK"], cuda), dev(case["newV"], cuda), ctx_len, rope=dev(rope_np.view(np.float16), cuda))
+    k_new, v_new = orc.kv_append_f16(case["newK"], case["newV"], ctx_len, rope=rope_np.view(np.float16))
+    K = np.concatenate([case["K"], k_new])
+    V = np.concatenate([case["V"], v_new])
+    return case, cache, K, V
+
+
+@pytest.mark.parametrize("ctx_len,m,splits", [(2000, 1, 0), (2000, 9, 0), (2000, 16, 0), (2000, 9, 1), (33, 9, 0),
+                                              (0, 16, 0), (32768, 9, 0)])
+def test_verify_head_dim_128(la, orc, synth, cuda, ctx_len, m, splits):
+    case, cache, K, V = setup_ref(la, orc, synth, cuda, 60 + m + ctx_len % 97, ctx_len, m)
+    out = cache.verify(dev(case["Q"], cuda), ctx_len, splits=splits)
+    la.sync()
+    got = out.float().cpu().numpy()
+    assert rel_err(got, orc.attention_f64(case["Q"], ctx_len, K, V, ctx_len + m)) < TOL
+    assert rel_err(got, orc.verify(case["Q"], K, V, ctx_len, splits=max(splits, 1))) < TOL_PAIR
+
+
+def test_verify_head_dim_128_window_gate(la, orc, synth, cuda):
+    """A sliding-window layer (window 256, engine.go:36) with the output gate."""
+    case, cache, K, V = setup_ref(la, orc, synth, cuda, 70, 5000, 9)
+    gate = synth.Stream(71).normal_f16((9, 16))
+    out = cache.verify(dev(case["Q"], cuda), 5000, window=256, gate=dev(gate, cuda))
+    la.sync()
+    want = orc.attention_f64(case["Q"], 5000, K, V, 5009, window=256)
+    sig = 1.0 / (1.0 + np.exp(-gate.astype(np.float64)))
+    assert rel_err(out.float().cpu().numpy(), want * sig[..., None]) < TOL
+
+
+def test_verify_head_dim_128_partials(la, orc, synth, cuda):
+    """Two sequence shards' (acc, max, sum) partials at head_dim 128, merged by the combine."""
+    import torch
+
+    ctx, m = 6000, 9
+    case, cache, K, V = setup_ref(la, orc, synth, cuda, 72, ctx, m)
+    q = dev(case["Q"], cuda)
+    cut = 3072
+    parts = [cache.verify_partial(q, 0, cut, ctx), cache.verify_partial(q, cut, ctx + m, ctx)]
+    la.sync()
+    for part, (b, e) in zip(parts, [(0, cut), (cut, ctx + m)]):
+        got = part.cpu().numpy()
+        want = orc.verify_partial(case["Q"], K, V, b, e, ctx)
+        g = got[:, :128] / got[:, 129:130]
+        w = want[:, :128] / want[:, 129:130]
+        assert float(np.max(np.abs(g - w))) / float(np.sqrt(np.mean(w.astype(np.float64) ** 2))) < TOL_PAIR
+    rows = m * 16
+    out = la.combine(torch.stack(parts), rows, 2, 128, split_stride=rows * 130, row_stride=130)
+    la.sync()
+    want = orc.attention_f64(case["Q"], ctx, K, V, ctx + m)
+    assert rel_err(out.float().cpu().numpy().reshape(want.shape), want) < TOL
+
+
+def test_verify_head_dim_128_rejects_more_than_16_tokens(la, synth, cuda):
+    case = synth.verify_case(73, 100, 17, q_heads=16, kv_heads=4, head_dim=128)
+    cache = la.LayerCache(la.MODE_F16, 4, 128, 256, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    with pytest.raises(la.LFM3AError) as e:
+        cache.verify(dev(case["Q"], cuda), 100)
+    assert e.value.code == la.ENOTSUP
+
+
+def test_verify_round_head_dim_128(la, orc, synth, cuda):
+    """A verify round at the reference geometry: the drafts' append (its own kernel at head_dim 128), the attention
+    and the rollback; the cache bytes after the round are the oracle's, bit for bit."""
+    ctx, m = 3000, 8
+    case = synth.verify_case(74, ctx, m, q_heads=16, kv_heads=4, head_dim=128)
+    cache = la.LayerCache(la.MODE_F16, 4, 128, ctx + 128, device=cuda)
+    rope_np = la.rope_table(1e6, 0.5, 128, ctx + m + 1)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    out = cache.verify_round(dev(case["newK"], cuda), dev(case["newV"], cuda), dev(case["Q"], cuda), ctx,
+                             rope=dev(rope_np.view(np.float16), cuda))
+    la.sync()
+    k_new, v_new = orc.kv_append_f16(case["newK"], case["newV"], ctx, rope=rope_np.view(np.float16))
+    K = np.concatenate([case["K"], k_new])
+    V = np.concatenate([case["V"], v_new])
+    assert rel_err(out.float().cpu().numpy(), orc.attention_f64(case["Q"], ctx, K, V, ctx + m)) < TOL
+    logical = cache.logical(ctx + m)
+    assert np.array_equal(logical["K"].view(np.uint16), K.view(np.uint16))
+    assert np.array_equal(logical["V"].view(np.uint16), V.view(np.uint16))
+    cache.truncate(ctx + 3)
+    la.sync()
+    v8, sc = orc.quantize_v8(V[:ctx + 3], ctx + 3)
+    logical = cache.logical(ctx + 3)
+    assert np.array_equal(logical["V8"], v8) and np.array_equal(logical["vscale"], sc)
