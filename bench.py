@@ -452,12 +452,59 @@ def measure_ref_geometry(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n
     return res
 
 
+# The reference's published prefill attention launches on its MI50 (benchmarks/prefill_attention.txt:12,19), ms.
+REF_MI50_PREFILL_MS = {(2048, 0): {"exact": 1.43, "int8_pv": 0.72}, (7680, 115200): {"exact": 573.34, "int8_pv": 278.94}}
+
+
+def measure_ref_prefill(la, dev, tokens: int, context: int, reps: int = 3) -> dict:
+    """Prefill attention at the reference geometry (16/4/128): one launch of `tokens` query tokens over
+    `context` cached tokens plus themselves, both variants; K/V/Q N(0,1) fp16 drawn on the device."""
+    import torch
+
+    qh, kvh, d = 16, 4, 128
+    n = context + tokens
+    g = torch.Generator(device=dev).manual_seed(13)
+    cache = la.LayerCache(la.MODE_F16, kvh, d, n + 64, device=dev)
+    step = 16384
+    for p0 in range(0, n, step):
+        c = min(step, n - p0)
+        cache.append(torch.randn((c, kvh, d), generator=g, device=dev).half(),
+                     torch.randn((c, kvh, d), generator=g, device=dev).half(), p0)
+    q = torch.randn((tokens, qh, d), generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    qk = 2.0 * qh * d * (tokens * context + tokens * (tokens + 1) / 2)
+    res = {"workload": f"prefill attention at the reference geometry 16/4/128: {tokens} tokens over {context} cached",
+           "qk_flop": qk}
+    for name, exact in (("int8_pv", False), ("exact", True)):
+        cache.prefill(q, context, exact=exact, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            cache.prefill(q, context, exact=exact, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"ms": round(ms, 3), "tflops_qk_plus_pv": round(2 * qk / (ms * 1e-3) / 1e12, 1)}
+        ref = REF_MI50_PREFILL_MS.get((tokens, context))
+        if ref:
+            res[name]["reference_mi50_ms"] = ref[name]
+    la.sync()
+    del cache
+    return res
+
+
 def measure_ref_geometries(la, synth, dev, peak_gbs: float) -> dict:
     import torch
 
     res = {"32k": measure_ref_geometry(la, synth, dev, peak_gbs, 32768, 11, 4)}
     torch.cuda.empty_cache()
     res["128k"] = measure_ref_geometry(la, synth, dev, peak_gbs, 131072, 12, 2)
+    torch.cuda.empty_cache()
+    res["prefill_2048"] = measure_ref_prefill(la, dev, 2048, 0)
+    torch.cuda.empty_cache()
+    res["prefill_7680_at_115200"] = measure_ref_prefill(la, dev, 7680, 115200)
+    torch.cuda.empty_cache()
     return res
 
 

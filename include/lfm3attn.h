@@ -198,7 +198,8 @@ size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim);
 /* The number of key splits lfm3a_prefill_attention uses for a chunk (the counterpart of attnSplits,
  * internal/model/prefill.go:37-46): 1 when the chunk's CTAs (one per 32 query tokens and kv head) fill
  * one wave of two per SM; else enough splits for one wave, each with at least 8 key tiles of the shortest
- * row band, at most 64. sm_count 0: the current device's. */
+ * row band, at most 64. sm_count 0: the current device's. At head_dim 128 the kernels run one CTA per SM:
+ * their split count is this function's with half the SM count. */
 int lfm3a_prefill_splits(int tokens, int q_heads, int context, int window, int sm_count);
 
 /* Causal (optionally sliding-window) prefill attention of tokens query tokens at positions
@@ -207,7 +208,8 @@ int lfm3a_prefill_splits(int tokens, int q_heads, int context, int window, int s
  * internal/model/prefill.go:476-511). The chunk's K/V must already be appended.
  * exact = 0: u8 softmax probabilities per row and 64-key tile times the int8 V copy (tcgen05 kind::i8);
  * exact = 1: fp16 probabilities times fp16 V (tcgen05 kind::f16). q, out: device fp16
- * [tokens][q_heads][head_dim]. MODE_F16, head_dim 64, q_heads = 4 * kv_heads.
+ * [tokens][q_heads][head_dim]. MODE_F16, head_dim 64 or 128 (the reference model's 16/4/128 geometry),
+ * q_heads = 4 * kv_heads.
  * With a 16-byte aligned workspace of lfm3a_prefill_workspace_bytes, a chunk short of one wave of CTAs is
  * split along the keys (lfm3a_prefill_splits) and its partials merged (the combine of lfm3a_combine);
  * without one it runs unsplit. */
@@ -220,7 +222,9 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
  * (q_stride in halves, a multiple of 8). q_norm: fp16 [64] RMS weights (eps 1e-5) or NULL; rope: a table
  * of lfm3a_rope_table, row context + t, or NULL; the row is normalised, then rotated, each step rounded to
  * fp16 as q_norm_rope does. gate: fp16 logits at gate + t * gate_stride + qh, or NULL: the output row is
- * fp16(fp16(attention) * fp16(sigmoid(logit))), as gate_mul rounds. out stays [tokens][q_heads][64]. */
+ * fp16(fp16(attention) * fp16(sigmoid(logit))), as gate_mul rounds. out stays [tokens][q_heads][64].
+ * The fused glue is head_dim 64 only (LFM3A_ENOTSUP at 128); with all three NULL any q_stride works at either
+ * head_dim. */
 int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_t q_stride, const void* q_norm,
                                   const void* rope, const void* gate, int64_t gate_stride, int tokens, int q_heads,
                                   int context, int window, int exact, void* out, void* workspace,

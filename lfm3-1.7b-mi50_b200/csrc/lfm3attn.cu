@@ -492,10 +492,10 @@ int lfm3a_ring_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_he
 }
 
 size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim) {
-  if (tokens <= 0 || q_heads < 4 || head_dim != 64) return 0;
+  if (tokens <= 0 || q_heads < 4 || (head_dim != 64 && head_dim != 128)) return 0;
   // The most splits any context can get for this chunk (the long-context bound of prefill_splits_for).
-  const int splits = prefill_splits_for(tokens, q_heads / 4, 1 << 30, 0, current_sm_count());
-  return splits > 1 ? (size_t)tokens * q_heads * splits * kPfPart * sizeof(float) : 0;
+  const int splits = prefill_splits_for(tokens, q_heads / 4, 1 << 30, 0, current_sm_count(), head_dim == 64 ? 2 : 1);
+  return splits > 1 ? (size_t)tokens * q_heads * splits * (head_dim + 2) * sizeof(float) : 0;
 }
 
 int lfm3a_prefill_splits(int tokens, int q_heads, int context, int window, int sm_count) {
@@ -510,25 +510,29 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
   const lfm3a_kv_layout& L = kv->layout;
-  if (L.mode != LFM3A_MODE_F16 || L.head_dim != 64) return fail(LFM3A_ENOTSUP, "prefill attention needs MODE_F16, head_dim 64");
+  const int D = L.head_dim;
+  if (L.mode != LFM3A_MODE_F16 || (D != 64 && D != 128))
+    return fail(LFM3A_ENOTSUP, "prefill attention needs MODE_F16, head_dim 64 or 128");
+  if (D == 128 && (q_norm || rope || gate))
+    return fail(LFM3A_ENOTSUP, "the fused q-norm / RoPE / gate needs head_dim 64");
   if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "prefill attention needs 4 query heads per kv head");
   if (!q || !out || tokens < 0 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill arguments");
-  if (q_stride < (int64_t)q_heads * 64 || q_stride % 8 != 0)
+  if (q_stride < (int64_t)q_heads * D || q_stride % 8 != 0)
     return fail(LFM3A_EINVAL, "q_stride must be a multiple of 8 and at least q_heads * head_dim");
   if (gate && gate_stride < q_heads) return fail(LFM3A_EINVAL, "gate_stride must be at least q_heads");
   if (tokens == 0) return LFM3A_OK;
   if (!aligned16(q) || !aligned16(out)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
   // Key splits when the chunk alone leaves the GPU short of CTAs and the caller gave the workspace for them.
-  int splits = prefill_splits_for(tokens, L.kv_heads, context, window, current_sm_count());
-  const size_t need = (size_t)tokens * q_heads * splits * kPfPart * sizeof(float);
+  int splits = prefill_splits_for(tokens, L.kv_heads, context, window, current_sm_count(), D == 64 ? 2 : 1);
+  const size_t need = (size_t)tokens * q_heads * splits * (D + 2) * sizeof(float);
   if (splits > 1 && (!workspace || !aligned16(workspace) || workspace_bytes < need)) splits = 1;
   float* part = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   const cudaStream_t st = as_stream(stream);
   rc = launch_prefill(geom_of(kv), static_cast<const __half*>(q), q_stride, static_cast<const __half*>(q_norm),
                       static_cast<const __half*>(rope), static_cast<const __half*>(gate), gate_stride, tokens, q_heads,
-                      context, window, exact != 0, static_cast<__half*>(out), splits, part, st);
+                      context, window, exact != 0, static_cast<__half*>(out), splits, part, st, D);
   if (rc != LFM3A_OK || splits == 1) return rc;
-  rc = launch_combine(part, tokens * q_heads, splits, 64, kPfPart, (int64_t)splits * kPfPart, nullptr,
+  rc = launch_combine(part, tokens * q_heads, splits, D, D + 2, (int64_t)splits * (D + 2), nullptr,
                       static_cast<__half*>(out), nullptr, st);
   if (rc != LFM3A_OK || !gate) return rc;
   const int64_t groups = (int64_t)tokens * q_heads * 8;
@@ -539,7 +543,8 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
 
 int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, int q_heads, int context, int window,
                             int exact, void* out, void* workspace, size_t workspace_bytes, void* stream) {
-  return lfm3a_prefill_attention_fused(kv, q, (int64_t)q_heads * 64, nullptr, nullptr, nullptr, 0, tokens, q_heads,
+  const int64_t d = kv && kv->layout.head_dim == 128 ? 128 : 64;
+  return lfm3a_prefill_attention_fused(kv, q, (int64_t)q_heads * d, nullptr, nullptr, nullptr, 0, tokens, q_heads,
                                        context, window, exact, out, workspace, workspace_bytes, stream);
 }
 

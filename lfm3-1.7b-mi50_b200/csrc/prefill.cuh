@@ -11,7 +11,9 @@
 //        two 4-stage rings; the K ring runs ahead (a K stage frees when its QK completes);
 //   5    MMA issuer (one thread): S = Q K^T (kind::f16, M128 N64, 4 k-steps) into TMEM two tiles ahead, then
 //        PV: exact O += P V (kind::f16, O stays in TMEM), int8 Dpv = P8 V8 (kind::i8, s32 in TMEM).
-// TMEM columns: S[2] at 0 and 64; O (exact) at 128, or int8 Dpv (s32) at 128 and the fp32 accumulator at 192.
+// TMEM columns: S[2] at 0 and 64; O (exact) at 128, or int8 Dpv (s32) at 128 and the fp32 accumulator at 128 + D.
+// Head_dim D is 64 (the benchmark geometry, two CTAs per SM) or 128 (the reference model's, one CTA per SM; the
+// fused q-norm / RoPE / gate glue is head_dim 64 only).
 // Every operand sits in shared memory as 8-row x 16-byte core tiles (no swizzle, K-major); the page
 // sections are already in that order, so a page moves with plain bulk copies.
 #pragma once
@@ -92,16 +94,17 @@ __device__ __forceinline__ uint4 pack8(const float (&x)[8]) {
 }
 __device__ __forceinline__ float r16f(float x) { return __half2float(__float2half_rn(x)); }
 
-template <bool GLUE>
+template <int D, bool GLUE>
 __device__ __forceinline__ void load_q_row(const PrefillArgs& a, uint8_t* sQ, int r, bool row_ok, int tok, int qh) {
-  const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)tok * a.q_stride + (int64_t)qh * 64);
-  uint4* dst = reinterpret_cast<uint4*>(sQ + (r >> 3) * 8 * 128 + (r & 7) * 16);
+  const uint4* src = reinterpret_cast<const uint4*>(a.q + (int64_t)tok * a.q_stride + (int64_t)qh * D);
+  uint4* dst = reinterpret_cast<uint4*>(sQ + (r >> 3) * (D / 8) * 128 + (r & 7) * 16);
   const uint4 zero = make_uint4(0, 0, 0, 0);
   if (!GLUE || (!a.q_norm && !a.rope)) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) dst[c * 8] = row_ok ? src[c] : zero;
+    for (int c = 0; c < D / 8; ++c) dst[c * 8] = row_ok ? src[c] : zero;
     return;
   }
+  static_assert(!GLUE || D == 64, "the fused q-norm / RoPE serves head_dim 64");
   float inv = 1.f;
   if (a.q_norm) {
     float v[32];
@@ -194,7 +197,7 @@ __global__ __launch_bounds__(256) void prefill_gate_kernel(__half* out, const __
 constexpr int kPfStages = 4;       // per ring (K and V)
 constexpr int kPfQBytes = 16384;   // 128 rows x 64 dims fp16
 
-template <bool I8>
+template <int D, bool I8>
 struct PfLayout {
   // Warps 0-3 softmax; int8 also 4-7 epilogue; then the producer and the MMA issuer. (Two softmax
   // warpgroups on the key halves of a tile made the exact kernel slower: it is bound by the exponentials'
@@ -202,10 +205,12 @@ struct PfLayout {
   static constexpr int kProducerWarp = I8 ? 8 : 4;
   static constexpr int kMmaWarp = I8 ? 9 : 5;
   static constexpr int kThreads = (kMmaWarp + 1) * 32;
-  static constexpr int kKStage = 8192;                 // K of 64 keys: two 32-token pages
-  static constexpr int kVStage = I8 ? 4096 : 8192;     // V (or int8 V) of the same keys
+  static constexpr int kQBytes = 256 * D;              // 128 rows x D dims fp16
+  static constexpr int kPage = 64 * D;                 // one page's K (or fp16 V) section: 32 keys x D
+  static constexpr int kKStage = 2 * kPage;            // K of 64 keys: two 32-token pages
+  static constexpr int kVStage = I8 ? kPage : 2 * kPage;   // V (or int8 V) of the same keys
   static constexpr int kPBuf = I8 ? 8192 : 16384;      // 128 rows x 64 keys, u8 or fp16
-  static constexpr int kOffK = kPfQBytes;
+  static constexpr int kOffK = kQBytes;
   static constexpr int kOffV = kOffK + kPfStages * kKStage;
   static constexpr int kOffP = kOffV + kPfStages * kVStage;
   static constexpr int kOffSc = kOffP + 2 * kPBuf;     // int8: [2][128] (corr, scale) of a tile, softmax -> epilogue
@@ -215,19 +220,29 @@ struct PfLayout {
   static constexpr int kOffTmemSlot = kOffBar + kBars * 8;
   static constexpr int kOffAbort = kOffTmemSlot + 8;   // in the dynamic region: static shared memory would
   static constexpr int kBytes = kOffTmemSlot + 16;      // pad to the 1 KiB alignment and cost the second CTA
-  // Request enough shared memory that two CTAs share an SM and a third cannot (TMEM holds 2 x 256 columns).
-  static constexpr int kRequest = kBytes > 80 * 1024 ? kBytes : 80 * 1024;
+  // Head_dim 64: enough shared memory that two CTAs share an SM and a third cannot (TMEM holds 2 x 256 columns).
+  // Head_dim 128: one CTA per SM (its shared memory alone rules out a second).
+  static constexpr int kRequest = D == 64 ? (kBytes > 80 * 1024 ? kBytes : 80 * 1024) : kBytes;
+  static constexpr int kBlocksPerSm = D == 64 ? 2 : 1;
+  // TMEM: S[2] at 0 and 64; exact O at 128; int8 Dpv (s32) at 128 and the fp32 accumulator at 128 + D.
+  static constexpr uint32_t kTmemCols = (I8 && D == 128) ? 512 : 256;
+  static constexpr int kAcc = 128 + D;                 // int8: first fp32 accumulator column
+  static constexpr int kPart = D + 2;                  // split partial: acc[D], max, sum
+  static constexpr uint32_t kSbo = 16 * D;             // bytes between 8-row groups of Q and of a K page
+  static constexpr uint32_t kIdescPV = I8 ? ((2u << 4) | (1u << 10) | ((uint32_t)(D >> 3) << 17) | ((128u >> 4) << 24))
+                                          : ((1u << 4) | ((uint32_t)(D >> 3) << 17) | ((128u >> 4) << 24));
 };
+
 
 // SPLIT: the launch splits the keys (a.splits > 1) and this CTA leaves a partial; the unsplit instantiation
 // carries none of that code, so the tile loops keep their register allocation.
 // GLUE: the launch fuses the q-norm / RoPE of the query rows or the output gate (lfm3a_prefill_attention_fused);
 // the plain instantiation reads Q as it is and stores the output ungated.
-template <bool I8, bool SPLIT, bool GLUE>
-__global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(PrefillArgs a) {
-  using L = PfLayout<I8>;
+template <int D, bool I8, bool SPLIT, bool GLUE>
+__global__ __launch_bounds__(PfLayout<D, I8>::kThreads, PfLayout<D, I8>::kBlocksPerSm) void prefill_kernel(PrefillArgs a) {
+  using L = PfLayout<D, I8>;
   constexpr int NS = kPfStages;
-  constexpr uint32_t kTmemCols = 256;
+  constexpr uint32_t kTmemCols = L::kTmemCols;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* sQ = smem;
   uint8_t* sK = smem + L::kOffK;
@@ -267,10 +282,10 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     pdl_wait();
     const int r = threadIdx.x, t = r >> 2;
     if (r < 128 && t < ntok) {
-      float* prow = a.part + ((int64_t)(t0 + t) * a.q_heads + 4 * h + (r & 3)) * a.splits * kPfPart +
-                    (int64_t)blockIdx.z * kPfPart;
-      for (int d = 0; d < 64; d += 2) *reinterpret_cast<float2*>(prow + d) = make_float2(0.f, 0.f);
-      *reinterpret_cast<float2*>(prow + 64) = make_float2(-INFINITY, 0.f);
+      float* prow = a.part + ((int64_t)(t0 + t) * a.q_heads + 4 * h + (r & 3)) * a.splits * L::kPart +
+                    (int64_t)blockIdx.z * L::kPart;
+      for (int d = 0; d < D; d += 2) *reinterpret_cast<float2*>(prow + d) = make_float2(0.f, 0.f);
+      *reinterpret_cast<float2*>(prow + D) = make_float2(-INFINITY, 0.f);
     }
     return;
   }
@@ -311,7 +326,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     if (warp >= 4 && warp < 8) {
       const uint32_t lb = tmem + ((uint32_t)(32 * (warp - 4)) << 16);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_st16_fill(lb + 128 + 16 * c, 0x4B400000u);
+      for (int c = 0; c < D / 16; ++c) tmem_st16_fill(lb + 128 + 16 * c, 0x4B400000u);
       tmem_wait_st();
     }
     tc_fence_before();
@@ -326,7 +341,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     const int qpos = qfirst + t;
     const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
     {
-      load_q_row<GLUE>(a, sQ, r, row_ok, t0 + (row_ok ? t : 0), 4 * h + j);
+      load_q_row<D, GLUE>(a, sQ, r, row_ok, t0 + (row_ok ? t : 0), 4 * h + j);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -377,7 +392,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
           }
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < D / 16; ++c) {
             uint32_t rr[16];
             tmem_ld16(lane_base + 128 + c * 16, rr);
             tmem_wait_ld();
@@ -429,9 +444,9 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       } else {
         tc_fence_after();
         if (SPLIT) {   // this split's unnormalised O, running max and sum
-          float* prow = a.part + (grow * a.splits + blockIdx.z) * kPfPart;
+          float* prow = a.part + (grow * a.splits + blockIdx.z) * L::kPart;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < D / 16; ++c) {
             uint32_t rr[16];
             tmem_ld16(lane_base + 128 + 16 * c, rr);
             tmem_wait_ld();
@@ -442,14 +457,14 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
                 *reinterpret_cast<float2*>(prow + 16 * c + e) = make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
             }
           }
-          if (row_ok) *reinterpret_cast<float2*>(prow + 64) = make_float2(m_run, l_run);
+          if (row_ok) *reinterpret_cast<float2*>(prow + D) = make_float2(m_run, l_run);
         }
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+        uint4* dst = reinterpret_cast<uint4*>(a.out + grow * D);
         const bool gated = GLUE && a.gate != nullptr;
         const __half2 g2 = GLUE ? gate_half2(a, t0 + (row_ok ? t : 0), 4 * h + j) : __float2half2_rn(1.f);
 #pragma unroll
-        for (int c = 0; c < 4 && !SPLIT; ++c) {   // 16 columns of O at a time
+        for (int c = 0; c < D / 16 && !SPLIT; ++c) {   // 16 columns of O at a time
           uint32_t rr[16];
           tmem_ld16(lane_base + 128 + 16 * c, rr);
           tmem_wait_ld();
@@ -468,7 +483,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     const int qpos = qfirst + t;
     const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
     {
-      load_q_row<GLUE>(a, sQ, r, row_ok, t0 + (row_ok ? t : 0), 4 * h + j);
+      load_q_row<D, GLUE>(a, sQ, r, row_ok, t0 + (row_ok ? t : 0), 4 * h + j);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -528,7 +543,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       // (pm * vs)) is rne(e), e = 2^(x*scale - mx + log2 255), the V scale cancelling. The row's scale of the
       // tile's int32 PV is pm * vs / 255 with pm = 2^(mx - m), and sum(p) = pm / 255 * sum(e).
       const char* sec = a.g.pool + phys_block(a.g, k0 / kBlockTokens) * a.g.block_bytes + (int64_t)h * a.g.head_bytes;
-      const float vs = *reinterpret_cast<const float*>(sec + F16Section<64>::kOffScale);
+      const float vs = *reinterpret_cast<const float*>(sec + F16Section<D>::kOffScale);
       const float off = mx == -INFINITY ? 0.f : kLog2of255 - mx;
       const float2 sc2 = make_float2(a.qk_scale, a.qk_scale), off2 = make_float2(off, off);
       const float2 mag2 = make_float2(12582912.f, 12582912.f);
@@ -586,8 +601,8 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     named_bar_sync(2, 256);
   } else if (I8 && warp < 8) {
     // ================================================================ int8 epilogue warpgroup, thread = row
-    // Tile j: acc = corr_j x acc + scale_j x Dpv(j), acc in fp32 TMEM columns 192..255, Dpv the tile's int32
-    // PV at 128..191. Those s32 columns hold 0x4B400000 before every PV (set in the prologue, and here again
+    // Tile j: acc = corr_j x acc + scale_j x Dpv(j), acc in fp32 TMEM columns 128 + D .., Dpv the tile's int32
+    // PV at 128 .. 127 + D. Those s32 columns hold 0x4B400000 before every PV (set in the prologue, and here again
     // after each read), and the MMA accumulates onto it: |Dpv| <= 64 * 255 * 127 < 2^22, so the column reads
     // back as the float 1.5 * 2^23 + Dpv and one FADD gives Dpv exactly (no conversion on the MUFU pipe, no
     // integer add). Then the s32 columns are free for PV(j + 1). Column pairs go through packed fp32.
@@ -616,7 +631,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       const float2 corr2 = make_float2(cs.x, cs.x);
       if (jt == 0) {   // the first tile starts the accumulator
 #pragma unroll
-        for (int qc = 0; qc < 4; ++qc) {
+        for (int qc = 0; qc < D / 16; ++qc) {
           uint32_t dv[16];
           tmem_ld16_after(lane_base + 128 + 16 * qc, dv, dep);
           tmem_wait_ld();
@@ -628,15 +643,15 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
             dv[e] = __float_as_uint(r2.x);
             dv[e + 1] = __float_as_uint(r2.y);
           }
-          tmem_st16(lane_base + 192 + 16 * qc, dv);
+          tmem_st16(lane_base + L::kAcc + 16 * qc, dv);
           dep = dv[15];
         }
       } else {
 #pragma unroll
-        for (int qc = 0; qc < 4; ++qc) {
+        for (int qc = 0; qc < D / 16; ++qc) {
           uint32_t dv[16], av[16];
           tmem_ld16_after(lane_base + 128 + 16 * qc, dv, dep);
-          tmem_ld16_after(lane_base + 192 + 16 * qc, av, dep);
+          tmem_ld16_after(lane_base + L::kAcc + 16 * qc, av, dep);
           tmem_wait_ld();
           reg_fence16(dv);
           reg_fence16(av);
@@ -659,7 +674,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
               av[e + 1] = __float_as_uint(r2.y);
             }
           }
-          tmem_st16(lane_base + 192 + 16 * qc, av);
+          tmem_st16(lane_base + L::kAcc + 16 * qc, av);
           dep = av[15];
         }
       }
@@ -674,11 +689,11 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
       tc_fence_after();
       const float l = sL[r];
       if (SPLIT) {   // this split's unnormalised accumulator, running max and sum
-        float* prow = a.part + (grow * a.splits + blockIdx.z) * kPfPart;
+        float* prow = a.part + (grow * a.splits + blockIdx.z) * L::kPart;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < D / 16; ++c) {
           uint32_t rr[16];
-          tmem_ld16(lane_base + 192 + 16 * c, rr);
+          tmem_ld16(lane_base + L::kAcc + 16 * c, rr);
           tmem_wait_ld();
           reg_fence16(rr);
           if (row_ok) {
@@ -687,16 +702,16 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
               *reinterpret_cast<float2*>(prow + 16 * c + e) = make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
           }
         }
-        if (row_ok) *reinterpret_cast<float2*>(prow + 64) = make_float2(sL[128 + r], l);
+        if (row_ok) *reinterpret_cast<float2*>(prow + D) = make_float2(sL[128 + r], l);
       }
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(a.out + grow * 64);
+      uint4* dst = reinterpret_cast<uint4*>(a.out + grow * D);
       const bool gated = GLUE && a.gate != nullptr;
       const __half2 g2 = GLUE ? gate_half2(a, t0 + (row_ok ? t : 0), 4 * h + j) : __float2half2_rn(1.f);
 #pragma unroll
-      for (int c = 0; c < 4 && !SPLIT; ++c) {
+      for (int c = 0; c < D / 16 && !SPLIT; ++c) {
         uint32_t rr[16];
-        tmem_ld16(lane_base + 192 + 16 * c, rr);
+        tmem_ld16(lane_base + L::kAcc + 16 * c, rr);
         tmem_wait_ld();
         reg_fence16(rr);
         if (row_ok) {
@@ -725,8 +740,8 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
         pages(jt, s0, s1);
         if (lane == 0) {
           mbar_arrive_expect_tx(&k_full[st], L::kKStage);
-          bulk_g2s(sK + st * L::kKStage, s0, 4096, &k_full[st]);
-          bulk_g2s(sK + st * L::kKStage + 4096, s1, 4096, &k_full[st]);
+          bulk_g2s(sK + st * L::kKStage, s0, L::kPage, &k_full[st]);
+          bulk_g2s(sK + st * L::kKStage + L::kPage, s1, L::kPage, &k_full[st]);
         }
         __syncwarp();
         k_issued = jt + 1;
@@ -737,7 +752,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
         if (jt >= NS && !__all_sync(0xffffffffu, mbar_wait(&v_empty[st], (uint32_t)((jt / NS) - 1) & 1u))) return false;
         const char *s0, *s1;
         pages(jt, s0, s1);
-        constexpr int off = I8 ? F16Section<64>::kOffV8 : F16Section<64>::kOffV, half = L::kVStage / 2;
+        constexpr int off = I8 ? F16Section<D>::kOffV8 : F16Section<D>::kOffV, half = L::kVStage / 2;
         if (lane == 0) {
           mbar_arrive_expect_tx(&v_full[st], L::kVStage);
           bulk_g2s(sV + st * L::kVStage, s0 + off, half, &v_full[st]);
@@ -773,15 +788,15 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
     {
       bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0));
       if (!ok) raise_error(kErrWaitOther);
-      const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, 1024);
+      const uint64_t q_desc = umma_desc(smem_u32(sQ), 128, L::kSbo);
       auto issue_qk = [&](int jt) -> bool {
         const int st = jt % NS, b = jt & 1;
         if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (uint32_t)(jt / NS) & 1u))) return false;
         tc_fence_after();
-        const uint64_t k_desc = umma_desc(smem_u32(sK + st * L::kKStage), 128, 1024);
+        const uint64_t k_desc = umma_desc(smem_u32(sK + st * L::kKStage), 128, L::kSbo);
         if (lane == 0) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)   // +256 bytes per 16 dims: +16 in the descriptor's address field
+          for (int ks = 0; ks < D / 16; ++ks)   // +256 bytes per 16 dims: +16 in the descriptor's address field
             umma_f16_ss(tmem + b * 64, q_desc + 16 * ks, k_desc + 16 * ks, kIdescF16M128N64, ks > 0 ? 1u : 0u);
           umma_commit(&s_full[b]);
           umma_commit(&k_empty[st]);
@@ -825,7 +840,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
           if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-              umma_f16_ss(tmem + 128, p_desc + 16 * ks, v_desc + 256 * (ks >> 1) + 16 * (ks & 1), kIdescF16M128N64,
+              umma_f16_ss(tmem + 128, p_desc + 16 * ks, v_desc + (L::kPage >> 4) * (ks >> 1) + 16 * (ks & 1), L::kIdescPV,
                           (jt > 0 || ks > 0) ? 1u : 0u);
           }
         } else {
@@ -833,7 +848,7 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
           if (lane == 0) {
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)
-              umma_i8_ss(tmem + 128, p_desc + 16 * ks, v_desc + 128 * ks, kIdescI8M128N64, 1u);   // onto the bias
+              umma_i8_ss(tmem + 128, p_desc + 16 * ks, v_desc + (L::kPage >> 5) * ks, L::kIdescPV, 1u);   // onto the bias
           }
         }
         if (lane == 0) {
@@ -863,8 +878,8 @@ __global__ __launch_bounds__(PfLayout<I8>::kThreads, 2) void prefill_kernel(Pref
   }
 }
 
-inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st) {
-  static bool done[8][64];
+inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, int head_dim, cudaStream_t st) {
+  static bool done[12][64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LFM3A_ECUDA;
   const dim3 grid(a.qtiles, a.g.kv_heads, a.splits);
@@ -879,19 +894,29 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
     launch_pdl(kernel, grid, threads, request, st, a);
     return true;
   };
-  using LI = PfLayout<true>;
-  using LE = PfLayout<false>;
   bool ok;
-  if (i8) {
-    if (split) ok = glue ? run(prefill_kernel<true, true, true>, LI::kRequest, LI::kThreads, 7)
-                         : run(prefill_kernel<true, true, false>, LI::kRequest, LI::kThreads, 6);
-    else ok = glue ? run(prefill_kernel<true, false, true>, LI::kRequest, LI::kThreads, 5)
-                   : run(prefill_kernel<true, false, false>, LI::kRequest, LI::kThreads, 4);
+  if (head_dim == 128) {   // the reference model's geometry: no fused glue
+    if (glue) return LFM3A_ENOTSUP;
+    using LI = PfLayout<128, true>;
+    using LE = PfLayout<128, false>;
+    if (i8) ok = split ? run(prefill_kernel<128, true, true, false>, LI::kRequest, LI::kThreads, 11)
+                       : run(prefill_kernel<128, true, false, false>, LI::kRequest, LI::kThreads, 10);
+    else ok = split ? run(prefill_kernel<128, false, true, false>, LE::kRequest, LE::kThreads, 9)
+                    : run(prefill_kernel<128, false, false, false>, LE::kRequest, LE::kThreads, 8);
   } else {
-    if (split) ok = glue ? run(prefill_kernel<false, true, true>, LE::kRequest, LE::kThreads, 3)
-                         : run(prefill_kernel<false, true, false>, LE::kRequest, LE::kThreads, 2);
-    else ok = glue ? run(prefill_kernel<false, false, true>, LE::kRequest, LE::kThreads, 1)
-                   : run(prefill_kernel<false, false, false>, LE::kRequest, LE::kThreads, 0);
+    using LI = PfLayout<64, true>;
+    using LE = PfLayout<64, false>;
+    if (i8) {
+      if (split) ok = glue ? run(prefill_kernel<64, true, true, true>, LI::kRequest, LI::kThreads, 7)
+                           : run(prefill_kernel<64, true, true, false>, LI::kRequest, LI::kThreads, 6);
+      else ok = glue ? run(prefill_kernel<64, true, false, true>, LI::kRequest, LI::kThreads, 5)
+                     : run(prefill_kernel<64, true, false, false>, LI::kRequest, LI::kThreads, 4);
+    } else {
+      if (split) ok = glue ? run(prefill_kernel<64, false, true, true>, LE::kRequest, LE::kThreads, 3)
+                           : run(prefill_kernel<64, false, true, false>, LE::kRequest, LE::kThreads, 2);
+      else ok = glue ? run(prefill_kernel<64, false, false, true>, LE::kRequest, LE::kThreads, 1)
+                     : run(prefill_kernel<64, false, false, false>, LE::kRequest, LE::kThreads, 0);
+    }
   }
   if (!ok) return LFM3A_ECUDA;
   return cudaGetLastError() == cudaSuccess ? LFM3A_OK : LFM3A_ELAUNCH;
@@ -903,9 +928,9 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, cudaStream_t st)
 // bounds the partials: workspace and combine traffic). Among those, the count with the least modelled
 // time: waves of CTAs x (tiles per split + 2 tiles of fixed cost per CTA), fewest splits on ties (a
 // chunk's row bands hold nearly equal tile counts when the context is long).
-inline int prefill_splits_for(int tokens, int kv_heads, int context, int window, int sm_count) {
+inline int prefill_splits_for(int tokens, int kv_heads, int context, int window, int sm_count, int blocks_per_sm = 2) {
   const int blocks = (tokens + 31) / 32 * kv_heads;
-  const int target = 2 * sm_count;
+  const int target = blocks_per_sm * sm_count;
   if (tokens <= 0 || blocks >= target) return 1;
   const int keys_min = window > 0 ? std::min(window + 31, context + std::min(tokens, 32))
                                   : context + std::min(tokens, 32);
@@ -928,7 +953,7 @@ inline int prefill_splits_for(int tokens, int kv_heads, int context, int window,
 // if any, is left to prefill_gate_kernel after it).
 inline int launch_prefill(const KvGeom& g, const __half* q, int64_t q_stride, const __half* q_norm, const __half* rope,
                           const __half* gate, int64_t gate_stride, int tokens, int q_heads, int context, int window,
-                          bool exact, __half* out, int splits, float* part, cudaStream_t st) {
+                          bool exact, __half* out, int splits, float* part, cudaStream_t st, int head_dim = 64) {
   PrefillArgs a;
   a.g = g;
   a.q = q;
@@ -945,8 +970,8 @@ inline int launch_prefill(const KvGeom& g, const __half* q, int64_t q_stride, co
   a.window = window;
   a.qtiles = (tokens + 31) / 32;
   a.splits = splits;
-  a.qk_scale = 0.125f * kLog2e;
-  return launch_prefill_kernel(a, !exact, st);
+  a.qk_scale = (head_dim == 64 ? 0.125f : 1.f / sqrtf(128.f)) * kLog2e;
+  return launch_prefill_kernel(a, !exact, head_dim, st);
 }
 
 }  // namespace lfm3a

@@ -140,3 +140,80 @@ def test_prefill_fused_glue(la, orc, synth, cuda, context, T, exact):
     got = gated.cpu().numpy()
     ulps = np.abs(got.view(np.int16).astype(np.int32) - want.view(np.int16).astype(np.int32))
     assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3
+
+
+# ---------------------------------------------------------------- the reference model's geometry
+# 16 query heads, 4 kv heads, head_dim 128 (internal/model/engine.go:22-40). Both variants run one CTA per SM
+# there, so a chunk's key splits follow lfm3a_prefill_splits with half the SM count.
+def run_ref(la, synth, cuda, seed, context, T, window, exact):
+    case = synth.prefill_case(seed, context + T, q_heads=16, kv_heads=4, head_dim=128)
+    cache = la.LayerCache(la.MODE_F16, 4, 128, context + T + 64, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    out = cache.prefill(dev(case["Q"][context:], cuda), context, window=window, exact=exact)
+    la.sync()
+    return case, cache, out.float().cpu().numpy()
+
+
+REF_CASES = [(0, 32, 0), (0, 100, 0), (37, 100, 0), (160, 300, 100), (1000, 96, 256)]
+
+
+@pytest.mark.parametrize("exact", [True, False])
+@pytest.mark.parametrize("context,T,window", REF_CASES)
+def test_prefill_head_dim_128(la, orc, synth, cuda, context, T, window, exact):
+    case, cache, got = run_ref(la, synth, cuda, 100 + T + context, context, T, window, exact)
+    n = context + T
+    q = case["Q"][context:]
+    if exact:
+        assert rel_err(got, orc.attention_f64(q, context, case["K"], case["V"], n, window=window)) < TOL_EXACT
+        assert rel_err(got, orc.prefill_exact(q, context, case["K"], case["V"], window=window)) < TOL_EXACT
+    else:
+        logical = cache.logical(n)
+        v8, vs = orc.quantize_v8(case["V"], n)
+        assert np.array_equal(logical["V8"], v8)
+        assert rel_err(got, orc.prefill_i8pv(q, context, case["K"], v8, vs, window=window)) < TOL_I8
+
+
+@pytest.mark.parametrize("exact", [True, False])
+@pytest.mark.parametrize("context,T", [(20000, 64), (3000, 32)])
+def test_prefill_head_dim_128_key_splits(la, orc, synth, cuda, context, T, exact):
+    import torch
+
+    half_sms = torch.cuda.get_device_properties(cuda).multi_processor_count // 2
+    splits = la.lib().lfm3a_prefill_splits(T, 16, context, 0, half_sms)
+    assert splits > 1
+    case, _, got = run_ref(la, synth, cuda, 110 + T, context, T, 0, exact)
+    q = case["Q"][context:]
+    if exact:
+        assert rel_err(got, orc.prefill_exact(q, context, case["K"], case["V"], splits=splits)) < TOL_EXACT
+        assert rel_err(got, orc.attention_f64(q, context, case["K"], case["V"], context + T)) < TOL_EXACT
+    else:
+        v8, vs = orc.quantize_v8(case["V"], context + T)
+        assert rel_err(got, orc.prefill_i8pv(q, context, case["K"], v8, vs, splits=splits)) < TOL_I8
+
+
+def test_prefill_head_dim_128_sampled_rows(la, orc, synth, cuda):
+    """A 2048-token causal prompt at head_dim 128, both variants, on every 37th query row."""
+    T = 2048
+    case = synth.prefill_case(120, T, q_heads=16, kv_heads=4, head_dim=128)
+    cache = la.LayerCache(la.MODE_F16, 4, 128, T + 64, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    q = dev(case["Q"], cuda)
+    ex = cache.prefill(q, 0, exact=True)
+    i8 = cache.prefill(q, 0, exact=False)
+    la.sync()
+    rows = np.arange(0, T, 37)
+    want = orc.attention_f64(case["Q"], 0, case["K"], case["V"], T, row_step=37)
+    assert rel_err(ex.float().cpu().numpy(), want, rows) < TOL_EXACT
+    v8, vs = orc.quantize_v8(case["V"], T)
+    emu = orc.prefill_i8pv(case["Q"], 0, case["K"], v8, vs, row_step=37)
+    assert rel_err(i8.float().cpu().numpy(), emu, rows) < TOL_I8
+
+
+def test_prefill_head_dim_128_refuses_glue(la, synth, cuda):
+    case = synth.prefill_case(121, 64, q_heads=16, kv_heads=4, head_dim=128)
+    cache = la.LayerCache(la.MODE_F16, 4, 128, 128, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    gate = dev(synth.Stream(122).normal_f16((64, 16)), cuda)
+    with pytest.raises(la.LFM3AError) as e:
+        cache.prefill(dev(case["Q"], cuda), 0, exact=True, gate=gate)
+    assert e.value.code == la.ENOTSUP
