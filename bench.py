@@ -16,6 +16,7 @@ threads; the reference's own Go/HIP code cannot run here), same config and metri
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -961,14 +962,30 @@ def run_ours(args):
         b2b_us = back_to_back_us(torch, lambda i: attend(caches[i % n_layers], q), 3 * n_layers)
         la.sync()
 
-    # ---- e2e: the public API with host buffers, one step at a time, copies and the result read included
+    # ---- e2e: the public API with host buffers, one step at a time, copies and the result read included.
+    # The step's inputs (the drafts' queries, keys and values) travel from one pinned host buffer in one copy.
     e2e_steps = min(K, 200)
-    hq = torch.from_numpy(Qr).pin_memory()
-    hk = torch.from_numpy(newK).pin_memory()
-    hv = torch.from_numpy(newV).pin_memory()
+    nq_, nk_ = q.numel(), nk.numel()
+    hin = torch.empty(nq_ + 2 * nk_, dtype=torch.float16).pin_memory()
+    hin[:nq_].copy_(torch.from_numpy(np.ascontiguousarray(Qr)).reshape(-1))
+    hin[nq_:nq_ + nk_].copy_(torch.from_numpy(np.ascontiguousarray(newK)).reshape(-1))
+    hin[nq_ + nk_:].copy_(torch.from_numpy(np.ascontiguousarray(newV)).reshape(-1))
+    din = torch.empty(hin.shape, dtype=torch.float16, device=dev)
+    dq = din[:nq_].view(q.shape)
+    dk = din[nq_:nq_ + nk_].view(nk.shape)
+    dv = din[nq_ + nk_:].view(nv.shape)
     res = gathered_out if R.plan == "heads" else out
     hout = torch.empty(res.shape, dtype=torch.float16).pin_memory()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(nk), torch.empty_like(nv)
+    direct = world == 1 and fused_round
+    if direct:
+        # One GPU: the round is the two C-ABI calls the engine makes (lfm3a_verify_round, lfm3a_kv_truncate), with
+        # their arguments prepared once, as a caller that keeps its layer views does.
+        lib = la.lib()
+        views = [ctypes.byref(c.view) for c in caches]
+        st_ptr = torch.cuda.current_stream().cuda_stream
+        ws_bytes = ws.numel()
+        call_args = (dk.data_ptr(), dv.data_ptr(), 0, rope.data_ptr(), None, dq.data_ptr(), M, QH, R.ctx_len, 0, None,
+                     out.data_ptr(), ws.data_ptr(), ws_bytes, splits, st_ptr)
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
@@ -976,15 +993,20 @@ def run_ours(args):
     s0 = torch.cuda.Event(enable_timing=True)
     s1 = torch.cuda.Event(enable_timing=True)
     s0.record()
+    rc_e2e = 0
     for i in range(e2e_steps):
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        step(caches[i % n_layers], None, dq, dk, dv)
+        din.copy_(hin, non_blocking=True)
+        if direct:
+            rc_e2e |= lib.lfm3a_verify_round(views[i % n_layers], *call_args)
+            rc_e2e |= lib.lfm3a_kv_truncate(views[i % n_layers], R.ctx_len, st_ptr)
+        else:
+            step(caches[i % n_layers], None, dq, dk, dv)
         hout.copy_(res, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     s1.record()
     torch.cuda.synchronize()
+    if rc_e2e:
+        raise la.LFM3AError(rc_e2e, "e2e round")
     e2e_wall = (time.perf_counter() - w0) / e2e_steps
     e2e_ms = s0.elapsed_time(s1) / e2e_steps
     la.sync()
@@ -1080,9 +1102,12 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": round(bytes_step / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                     "us_per_layer": round(e2e_ms * 1e3, 2), "wall_us_per_layer": round(e2e_wall_ms * 1e3, 2),
-                    "h2d_bytes_per_step": int(hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2),
+                    "h2d_bytes_per_step": int(hin.numel() * 2),
                     "d2h_bytes_per_step": int(hout.numel() * 2),
-                    "how": "LayerCache.append/verify/truncate via ctypes, pinned-host copies, stream sync per step"},
+                    "how": ("one pinned-host copy of the drafts' q, k, v, lfm3a_verify_round + lfm3a_kv_truncate "
+                            "through ctypes, the output read back, a stream sync per step" if direct else
+                            "one pinned-host copy of the drafts' q, k, v, the plan's step (LayerCache calls and "
+                            "the exchange), the output read back, a stream sync per step")},
             "gpu_launches": int(launches_per_step * K),
             "clocks": clocks,
         }
