@@ -142,3 +142,20 @@ def test_g128_sizes_and_checks(la):
     ws = ctypes.create_string_buffer(64)
     addr = (ctypes.addressof(ws) + 15) & ~15
     assert lib.lfm3a_g128_linear(None, 128, 4, 0, None, None, 4, 128, None, 0, None, 4, addr, 16, None) == la.EWORKSPACE
+
+
+def test_head_dim_128_host_logic(la):
+    """The reference geometry (16/4/128) runs one CTA per SM: half the verify splits of head_dim 64 at the same
+    kv-head count, and prefill workspaces sized with head_dim + 2 floats per partial row."""
+    lib = la.lib()
+    l64, l128 = la.layout(0, 4, 64), la.layout(0, 4, 128)
+    s64 = lib.lfm3a_verify_splits(ctypes.byref(l64), 131072, 8, 0, 148)
+    s128 = lib.lfm3a_verify_splits(ctypes.byref(l128), 131072, 8, 0, 148)
+    assert (s64, s128) == (74, 37)
+    # past 16 tokens head_dim 128 is refused, so the split count follows the two-per-SM rule
+    assert lib.lfm3a_verify_splits(ctypes.byref(l128), 131072, 17, 0, 148) == 74
+    assert lib.lfm3a_verify_workspace_bytes(8, 16, 128, 37) == 8 * 16 * 37 * 130 * 4
+    # a 64-token chunk of 16 query heads never fills a wave: the workspace covers its long-context splits
+    assert lib.lfm3a_prefill_workspace_bytes(64, 16, 128) > 0
+    assert lib.lfm3a_prefill_workspace_bytes(64, 16, 96) == 0
+    assert lib.lfm3a_prefill_workspace_bytes(64, 16, 128) % (64 * 16 * 130 * 4) == 0
