@@ -72,7 +72,6 @@ struct PrefillArgs {
   int T, q_heads, context, window, qtiles, splits;
   float qk_scale;         // (1 / sqrt(64)) * log2(e)
 };
-constexpr int kPfPart = 66;
 
 // Query row (tok, qh) into its core tiles: row r, dims 8c .. 8c + 7 at ((r / 8) * 8 + c) * 128 + (r % 8) * 16.
 // With q_norm or rope the row is first RMS-normalised (eps 1e-5) and rotated, each step rounded to fp16 as
@@ -949,7 +948,7 @@ inline int prefill_splits_for(int tokens, int kv_heads, int context, int window,
   return best;
 }
 
-// splits > 1: part receives [tokens * q_heads][splits][kPfPart] partials for the combine (and the gate,
+// splits > 1: part receives [tokens * q_heads][splits][head_dim + 2] partials for the combine (and the gate,
 // if any, is left to prefill_gate_kernel after it).
 inline int launch_prefill(const KvGeom& g, const __half* q, int64_t q_stride, const __half* q_norm, const __half* rope,
                           const __half* gate, int64_t gate_stride, int tokens, int q_heads, int context, int window,
