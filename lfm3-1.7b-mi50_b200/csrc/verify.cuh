@@ -1,5 +1,6 @@
-// DSpark verify attention on the B200 page layout (MODE_F16, head_dim 64, 4 query heads per kv head),
-// on the 5th-generation tensor cores.
+// DSpark verify attention on the B200 page layout (MODE_F16, 4 query heads per kv head), on the
+// 5th-generation tensor cores. verify_kernel (17-32 tokens) is head_dim 64; verify_m64_kernel<D> (up to 16
+// tokens, below) serves head_dim 64 and the reference model's 128.
 //
 // Grid (splits, kv heads). A block reads each K/V page of its split once for every verified token: the
 // query rows r = 4 t + j (token t, query head 4 h + j; up to 32 tokens = 128 rows) form the M = 128 operand
