@@ -29,25 +29,26 @@ __host__ __device__ __forceinline__ int g128_offset(int r, int c) {
 }
 
 // ---------------------------------------------------------------- e^x for the SiLU gate
-// e^x by Cody-Waite reduction, x = n ln2 + r with ln2 split into a 15-bit head (n * head is exact for
-// |n| <= 256) and a tail, and the degree-7 Taylor polynomial of e^r for |r| <= ln2 / 2 (truncation
-// error below 2^-27 relative), then 2^n applied as two exact power-of-two factors. Every step is a
-// separately rounded IEEE operation (no fused multiply-add), so a CPU restatement of the same steps gives
-// the same bits. Inputs below -87 return 0 (1 + e^x is then 1 in fp32 anyway), inputs at or above 88.5
-// return +inf. The reference's gated quantiser uses __expf (gemm.hip:76); this one is reproducible.
+// e^x by Cody-Waite reduction, x = n ln2 + r with ln2 split into a 15-bit head and a tail, and the degree-7
+// Taylor polynomial of e^r for |r| <= ln2 / 2 (truncation error below 2^-27 relative) in Horner form, then 2^n
+// applied as two exact power-of-two factors. The reduction and the Horner steps are fused multiply-adds, each
+// rounded once as IEEE fma; the rest are single IEEE operations. A CPU restatement with fmaf (correctly
+// rounded there too) gives the same bits. Inputs below -87 return 0 (1 + e^x is then 1 in fp32 anyway),
+// inputs at or above 88.5 return +inf. The reference's gated quantiser uses __expf (gemm.hip:76); this one is
+// reproducible.
 __device__ __forceinline__ float g128_exp(float x) {
   if (!(x < 88.5f)) return x != x ? x : INFINITY;
   if (x < -87.f) return 0.f;
   const float n = rintf(__fmul_rn(x, 1.44269502f));
-  const float r = __fsub_rn(__fsub_rn(x, __fmul_rn(n, 0.693145751953125f)), __fmul_rn(n, 1.42860677e-6f));
+  const float r = __fmaf_rn(-n, 1.42860677e-6f, __fmaf_rn(-n, 0.693145751953125f, x));
   float p = 1.98412701e-4f;                                   // 1/7!
-  p = __fadd_rn(1.38888892e-3f, __fmul_rn(r, p));            // 1/6!
-  p = __fadd_rn(8.33333377e-3f, __fmul_rn(r, p));            // 1/5!
-  p = __fadd_rn(4.16666679e-2f, __fmul_rn(r, p));            // 1/4!
-  p = __fadd_rn(1.66666672e-1f, __fmul_rn(r, p));            // 1/3!
-  p = __fadd_rn(0.5f, __fmul_rn(r, p));
-  p = __fadd_rn(1.f, __fmul_rn(r, p));
-  p = __fadd_rn(1.f, __fmul_rn(r, p));
+  p = __fmaf_rn(r, p, 1.38888892e-3f);                        // 1/6!
+  p = __fmaf_rn(r, p, 8.33333377e-3f);                        // 1/5!
+  p = __fmaf_rn(r, p, 4.16666679e-2f);                        // 1/4!
+  p = __fmaf_rn(r, p, 1.66666672e-1f);                        // 1/3!
+  p = __fmaf_rn(r, p, 0.5f);
+  p = __fmaf_rn(r, p, 1.f);
+  p = __fmaf_rn(r, p, 1.f);
   const int ni = (int)n, n1 = ni / 2, n2 = ni - n1;           // -126 <= ni <= 128: both factors normal
   return __fmul_rn(__fmul_rn(p, __int_as_float((n1 + 127) << 23)), __int_as_float((n2 + 127) << 23));
 }

@@ -558,15 +558,15 @@ float orc_g128_exp(float x) {
   if (!(x < 88.5f)) return x != x ? x : INFINITY;
   if (x < -87.f) return 0.f;
   const float n = rintf(x * 1.44269502f);
-  const float r = (x - n * 0.693145751953125f) - n * 1.42860677e-6f;
+  const float r = fmaf(-n, 1.42860677e-6f, fmaf(-n, 0.693145751953125f, x));
   float p = 1.98412701e-4f;
-  p = 1.38888892e-3f + r * p;
-  p = 8.33333377e-3f + r * p;
-  p = 4.16666679e-2f + r * p;
-  p = 1.66666672e-1f + r * p;
-  p = 0.5f + r * p;
-  p = 1.f + r * p;
-  p = 1.f + r * p;
+  p = fmaf(r, p, 1.38888892e-3f);
+  p = fmaf(r, p, 8.33333377e-3f);
+  p = fmaf(r, p, 4.16666679e-2f);
+  p = fmaf(r, p, 1.66666672e-1f);
+  p = fmaf(r, p, 0.5f);
+  p = fmaf(r, p, 1.f);
+  p = fmaf(r, p, 1.f);
   const int ni = (int)n, n1 = ni / 2, n2 = ni - n1;
   uint32_t b1 = (uint32_t)(n1 + 127) << 23, b2 = (uint32_t)(n2 + 127) << 23;
   float f1, f2;

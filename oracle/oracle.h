@@ -104,8 +104,8 @@ void orc_q_norm_rope(const uint16_t* q, int T, int q_heads, int head_dim, int64_
 int orc_accept(const int32_t* best, const int32_t* tokens, int m);
 
 /* e^x as the gated activation quantiser computes it: Cody-Waite reduction x = n ln2 + r (ln2 as a 15-bit
- * head and a tail), the degree-7 Taylor polynomial of e^r, 2^n as two power-of-two factors; every step one
- * IEEE-rounded operation. 0 below -87, +inf from 88.5. */
+ * head and a tail) and the degree-7 Taylor polynomial of e^r in Horner form, both as fused multiply-adds
+ * (fmaf, one rounding each), 2^n as two power-of-two factors. 0 below -87, +inf from 88.5. */
 float orc_g128_exp(float x);
 
 /* Activation quantiser of the W8A8 prefill GEMM (quantize_pack, kernels/gemm.hip:65-103): per row and

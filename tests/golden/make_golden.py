@@ -9,8 +9,8 @@ to a second, separately written restatement of the same source lines:
   int8 V blocks    the same quantiser per (kv head, 64-token block)
   u8 P             kernels/prefill_attn.hip:305-331 (IEEE division in place of v_rcp_f32)
   accept           kernels/dspark.hip:2851-2860
-  W8A8 GEMM        kernels/gemm.hip:65-103 (quantize_pack, plain and gated) and :181-255 (gemm), the fp32
-                   fma of every group emulated exactly with rationals
+  W8A8 GEMM        kernels/gemm.hip:65-103 (quantize_pack, plain and gated) and :181-255 (gemm); every fp32
+                   fma (the GEMM's group fold, the gate's exponential) emulated exactly with rationals
 Run: python tests/golden/make_golden.py
 """
 from __future__ import annotations
@@ -136,24 +136,37 @@ def accept(best, tokens):
     return acc + 1
 
 
+def fma32(a, b, c):
+    """fmaf on float32 values: the exact a * b + c rounded once to float32 (ties to even)."""
+    return round_f32(Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c)))
+
+
+def g128_exp_one(x):
+    """e^x with the gated quantiser's steps: Cody-Waite reduction and degree-7 Taylor Horner, as fused
+    multiply-adds (fma32), 2^n as two power-of-two factors."""
+    x = f32(x)
+    if np.isnan(x):
+        return x
+    if not x < f32(88.5):
+        return f32(np.inf)
+    if x < f32(-87.0):
+        return f32(0.0)
+    n = f32(np.rint(f32(x * f32(1.44269502))))
+    r = fma32(-n, f32(1.42860677e-6), fma32(-n, f32(0.693145751953125), x))
+    p = f32(1.98412701e-4)
+    for c in (1.38888892e-3, 8.33333377e-3, 4.16666679e-2, 1.66666672e-1, 0.5, 1.0, 1.0):
+        p = fma32(r, p, f32(c))
+    ni = int(n)
+    n1 = int(ni / 2)
+    n2 = ni - n1
+    f1 = np.array([(n1 + 127) << 23], dtype=np.uint32).view(f32)[0]
+    f2 = np.array([(n2 + 127) << 23], dtype=np.uint32).view(f32)[0]
+    return f32(f32(p * f1) * f2)
+
+
 def g128_exp(x):
-    """e^x with the gated quantiser's steps (Cody-Waite, degree-7 Taylor), every step one float32 rounding."""
     x = np.asarray(x, dtype=f32)
-    with np.errstate(over="ignore", invalid="ignore"):
-        n = np.rint(x * f32(1.44269502))
-        r = (x - n * f32(0.693145751953125)) - n * f32(1.42860677e-6)
-        p = np.full_like(x, f32(1.98412701e-4))
-        for c in (1.38888892e-3, 8.33333377e-3, 4.16666679e-2, 1.66666672e-1, 0.5, 1.0, 1.0):
-            p = f32(c) + r * p
-        ni = np.clip(n, -126, 128).astype(np.int64)
-        n1 = np.trunc(ni / 2).astype(np.int64)
-        n2 = ni - n1
-        f1 = ((n1 + 127) << 23).astype(np.uint32).view(f32)
-        f2 = ((n2 + 127) << 23).astype(np.uint32).view(f32)
-        y = (p * f1) * f2
-    y = np.where(x < f32(-87.0), f32(0.0), y)
-    y = np.where(x >= f32(88.5), f32(np.inf), y)
-    return y.astype(f32)
+    return np.array([g128_exp_one(v) for v in x.reshape(-1)], dtype=f32).reshape(x.shape)
 
 
 def g128_quantize(x, k, gated):
