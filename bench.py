@@ -1,17 +1,19 @@
-"""Benchmark of the B200 verify-attention path (benchmark config 2 per GPU).
+"""Benchmark of the B200 verify-attention path: benchmark config 3, strong scaling over the GPUs.
 
-One step = one DSpark verify round of one layer: append 16 draft K/V (RoPE theta 1e6), verify attention
-of the 16 drafts over 32768 cached tokens + drafts (split-KV + log-sum-exp combine), rollback to the
-context length. value = K/V bytes the attention reads per step, all ranks, / the max-over-ranks step
-time (GB/s); us_per_layer is the same time per step.
+One step = one DSpark verify round of one layer: append the 16 drafts' K/V (RoPE theta 1e6), verify
+attention of the 16 drafts over 131072 cached tokens + drafts (split-KV + log-sum-exp merge), roll back to
+the context length. value = the K/V bytes the round reads (131088 x 8 kv heads x 64 x 2 x 2, whatever the
+number of GPUs) / the max-over-ranks step time (GB/s); us_per_layer is the same time per step.
 
-N > 1 (torchrun, one rank per GPU, NCCL): the sequence is sharded by blocks, 32768 cached tokens per
-rank (weak scaling: the context is 32768 x N); the last rank also holds the drafts. Each rank computes its
-shard's log-sum-exp partial, the partials are all-gathered over NVLink (NCCL) and merged by the combine
-kernel on every rank.
+N > 1 (torchrun, one rank per GPU, NCCL): the same 131072-token layer is sharded (strong scaling). Heads plan
+(default): rank r holds kv heads [8r/N, 8(r+1)/N) of the whole sequence, runs its round on them, and the
+outputs are exchanged (NCCL all-gather, or the combine's NVLink peer stores). Seq plan: rank r holds a run of
+64-token blocks of all heads, the last rank also the drafts; the log-sum-exp partials are all-gathered and
+merged. After the timed region rank 0 checks the exchanged output against a one-GPU round of all 8 heads.
 
 --impl reference: the reference arithmetic restated on the host cores (the C++ oracle, OpenMP over all
-threads; the reference's own Go/HIP code cannot run here), same config and metric, rank 0 only.
+threads; the reference's own Go/HIP code cannot run here), same config and metric, rank 0 only; each step is
+a bounded sample of the round (one kv head's share, the heads in turn).
 """
 from __future__ import annotations
 
@@ -33,10 +35,12 @@ for _p in (str(ROOT), str(PKG)):
         sys.path.insert(0, _p)
 
 METRIC = "verify-attn µs/layer & HBM GB/s at 32k/128k ctx; prefill-attn int8 TOPS"
-CTX = 32768
+CTX3, SEED3 = 131072, 2   # config 3: the headline, on 1 GPU and sharded over N
+CTX, SEED = 32768, 1      # config 2: an extra field on one GPU
 M = 16
 QH, KVH, D = 32, 8, 64
-SEED = 1
+WORKLOAD = ("config 3: verify round of one layer (append 16 drafts with RoPE, verify attention of 16 tokens over "
+            "131072 cached + drafts, rollback), GQA 32/8, head_dim 64, fp16 KV")
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -53,8 +57,8 @@ def parse():
                     help="heads plan: NCCL all-gather of the outputs, or the combine's scatter over NVLink peer "
                          "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
                          "synchronisation, which both pay)")
-    ap.add_argument("--no-extras", action="store_true", help="skip the config 3/4/5 and decode fields (N = 1)")
-    ap.add_argument("--only", choices=["c3", "c4", "c5", "decode", "chunks", "gemm", "ref"],
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 2/4/5 and decode fields (N = 1)")
+    ap.add_argument("--only", choices=["c2", "c4", "c5", "decode", "chunks", "gemm", "ref"],
                     help="run only that configuration's measurement on one GPU and print its fields (for profiling)")
     return ap.parse_args()
 
@@ -68,8 +72,8 @@ def run_only(args) -> int:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     pk = peaks()
-    if args.only == "c3":
-        res = measure_c3(la, synth, dev, pk["hbm_gbs"])
+    if args.only == "c2":
+        res = measure_verify_cfg(la, synth, dev, pk["hbm_gbs"], CTX, SEED, "config 2")
     elif args.only == "c4":
         res = measure_c4(la, synth, dev, pk)
     elif args.only == "decode":
@@ -156,60 +160,93 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU arm
-def cpu_verify_sample(case, budget_s: float = 8.0, max_calls: int = 20):
-    """The oracle (reference arithmetic restated on the host cores) on the config-2 inputs: full verify
-    rounds of one layer, repeated until budget_s passes. Returns (seconds per layer, calls, threads)."""
-    import numpy as np
+class CpuRound:
+    """The oracle (the reference arithmetic restated on the host cores, OpenMP over all threads) on config 3's
+    inputs, one kv head's share of the round per step, the heads in turn: the drafts' append (RoPE) and the
+    split-KV verify of its 4 query heads over 131072 cached tokens + drafts, with the combine. A step is a
+    bounded sample (1/8) of the GPU arm's round."""
 
-    from oracle import oracle as orc
+    def __init__(self):
+        import numpy as np
 
-    threads = os.cpu_count() or 1
-    orc.set_threads(threads)
-    table = orc.rope_table(1e6, 1.0, D, CTX + M)
-    k_new, v_new = orc.kv_append_f16(case["newK"], case["newV"], CTX, rope=table)
-    K = np.concatenate([case["K"], k_new])
-    V = np.concatenate([case["V"], v_new])
-    splits = 37
-    orc.verify(case["Q"], K, V, CTX, splits=splits)   # warm-up
+        import synth
+        from oracle import oracle as orc
+
+        self.orc = orc
+        self.threads = os.cpu_count() or 1
+        orc.set_threads(self.threads)
+        self.rope = orc.rope_table(1e6, 1.0, D, CTX3 + M)
+        self.heads = []
+        for h in range(KVH):
+            c = synth.verify_case_heads(SEED3, CTX3, M, h, h + 1)
+            k_new, v_new = orc.kv_append_f16(c["newK"], c["newV"], CTX3, rope=self.rope)
+            K = np.ascontiguousarray(np.concatenate([c["K"], k_new]))
+            V = np.ascontiguousarray(np.concatenate([c["V"], v_new]))
+            self.heads.append((c, K, V))
+        self.calls = 0
+
+    def step(self):
+        c, K, V = self.heads[self.calls % KVH]
+        self.orc.kv_append_f16(c["newK"], c["newV"], CTX3, rope=self.rope)
+        self.orc.verify(c["Q"], K, V, CTX3, splits=37)
+        self.calls += 1
+
+    @staticmethod
+    def bytes_per_step() -> int:
+        return (CTX3 + M) * D * 2 * 2   # one kv head's K and V
+
+
+def cpu_baseline_sample(budget_s: float = 10.0, max_calls: int = 64) -> dict:
+    """cpu_baseline of the GPU arm's line: CpuRound steps until budget_s passes."""
+    r = CpuRound()
+    r.step()   # warm-up
     calls, t0 = 0, time.perf_counter()
     while calls < max_calls:
-        orc.kv_append_f16(case["newK"], case["newV"], CTX, rope=table)
-        orc.verify(case["Q"], K, V, CTX, splits=splits)
+        r.step()
         calls += 1
         if time.perf_counter() - t0 > budget_s:
             break
-    return (time.perf_counter() - t0) / calls, calls, threads
+    sec = (time.perf_counter() - t0) / calls
+    return {"value": round(r.bytes_per_step() / sec / 1e9, 3), "unit": "GB/s", "cores": r.threads, "kind": "port",
+            "sample": f"{calls} steps of one kv head's share of the config-3 round (append + split-KV verify + "
+                      f"combine of 4 query heads over 131088 keys; oracle, {r.threads} threads, "
+                      f"{sec * 1e3:.1f} ms each)"}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import synth
-
-    case = synth.verify_case(SEED, CTX, M)
-    sec, calls, threads = cpu_verify_sample(case)
-    bytes_step = kv_bytes(CTX + M)
-    gbs = bytes_step / sec / 1e9
+    r = CpuRound()
+    for _ in range(args.warmup):
+        r.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r.step()
+    sec = (time.perf_counter() - t0) / max(args.steps, 1)
+    gbs = r.bytes_per_step() / sec / 1e9
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": round(gbs, 3),
         "unit": "GB/s",
         "n_gpus": args.gpus,
-        "steps": calls,
-        "warmup": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3),
-        "us_per_layer": round(sec * 1e6, 1),
+        "us_per_layer": round(sec * KVH * 1e6, 1),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32 softmax / fp16 P (host port)",
-        "data": "synthetic (splitmix64 + Box-Muller, seed 1)",
-        "config": {"workload": "config 2: verify attention, 32768 cached tokens, 16 drafts, GQA 32/8, head_dim 64",
-                   "parallelism": "host threads"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{calls} full verify rounds of one layer (append + attention + combine)"},
+        "data": "synthetic (splitmix64 + Box-Muller fp16, seed 2)",
+        "config": {"workload": WORKLOAD, "context_tokens": CTX3, "drafts": M,
+                   "parallelism": f"host threads ({r.threads})",
+                   "sample": "each step one kv head's share of the round (1/8 of its bytes), the heads in turn; "
+                             "us_per_layer = 8 steps"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": r.threads, "kind": "port",
+                         "sample": f"{args.steps} steps of one kv head's share of the config-3 round (append + "
+                                   "split-KV verify + combine over 131088 keys)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -218,21 +255,20 @@ def run_reference(args):
 
 # ------------------------------------------------------------------ GPU arm
 class Rank:
-    """This process's share of the config-2 workload under the chosen plan (one process per GPU).
+    """This process's share of the config-3 layer under the chosen plan (one process per GPU; strong scaling:
+    the layer is the same 131072 tokens x 8 kv heads for every N).
 
-    single  one GPU: 32768 cached tokens x 8 kv heads, the 16 drafts and all 32 query heads.
-    heads   the context grows with the world (32768 x N tokens, weak scaling); rank r holds kv heads
-            [8r/N, 8(r+1)/N) of all of it and their query heads, appends its heads' drafts, verifies them,
-            and the outputs are all-gathered (NCCL).
-    seq     the context grows the same way; rank r holds 32768 tokens of it (all heads), the last rank also
-            the drafts; the log-sum-exp partials are all-gathered (NCCL) and merged on every rank.
-    Both multi-GPU plans keep 32768 x 8 x 64 fp16 K and V per GPU, as on one GPU."""
+    single  one GPU: all 8 kv heads, the 16 drafts and all 32 query heads.
+    heads   rank r holds kv heads [8r/N, 8(r+1)/N) of the whole sequence and their query heads, appends its
+            heads' drafts, verifies them, and the outputs are exchanged.
+    seq     rank r holds a run of 64-token blocks of all heads, the last rank also the drafts; the log-sum-exp
+            partials are all-gathered and merged on every rank."""
 
     def __init__(self, world: int, rank: int, plan: str):
         from shard import head_range, query_head_range, seq_range
 
         self.world, self.rank, self.plan = world, rank, plan
-        self.ctx_len = CTX * world
+        self.ctx_len = CTX3
         self.kvh, self.qh = KVH, QH
         self.h0, self.h1, self.q0, self.q1 = 0, KVH, 0, QH
         self.kv_begin, self.kv_end = 0, self.ctx_len + M
@@ -306,18 +342,19 @@ def graph_step_us(torch, dev, step, steps: int) -> tuple[float, float]:
     return step_us, att_us
 
 
-def measure_c3(la, synth, dev, peak_gbs: float, steps: int = 60) -> dict:
-    """Config 3 on one GPU: verify rounds at 131072 cached tokens (seed 2), two rotating 256 MiB caches."""
+def measure_verify_cfg(la, synth, dev, peak_gbs: float, ctx: int, seed: int, label: str, steps: int = 60) -> dict:
+    """A verify configuration on one GPU (config 2 as an extra field): rounds at ctx cached tokens, rotating
+    layer caches that together exceed L2."""
     import numpy as np
     import torch
 
-    ctx = 131072
-    case = synth.verify_case(2, ctx, M)
+    case = synth.verify_case_heads(seed, ctx, M, 0, KVH)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     rope = t(la.rope_table(1e6, 1.0, D, ctx + M + 1).view(np.float16))
     K0, V0 = t(case["K"]), t(case["V"])
+    n_caches = max(2, math.ceil(3 * L2_BYTES / kv_bytes(ctx)))
     caches = []
-    for _ in range(2):
+    for _ in range(n_caches):
         c = la.LayerCache(la.MODE_F16, KVH, D, ctx + M + 64, device=dev)
         c.append(K0, V0, 0)
         caches.append(c)
@@ -325,7 +362,7 @@ def measure_c3(la, synth, dev, peak_gbs: float, steps: int = 60) -> dict:
     q, nk, nv = t(case["Q"]), t(case["newK"]), t(case["newV"])
     out = torch.empty_like(q)
     splits = la.verify_splits(caches[0].layout, ctx, M, 0)
-    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(M, QH, D, splits), dtype=torch.uint8, device=dev)
+    ws = la.verify_workspace(M, QH, D, splits, dev)
 
     def step(c, ev=None):   # one round: the drafts' append fused into the attention call, then the rollback
         if ev:
@@ -335,22 +372,25 @@ def measure_c3(la, synth, dev, peak_gbs: float, steps: int = 60) -> dict:
             ev[1].record()
         c.truncate(ctx)
 
-    for i in range(4):
-        step(caches[i % 2])
+    for i in range(2 * n_caches):
+        step(caches[i % n_caches])
     torch.cuda.synchronize()
-    step_us, att_us = graph_step_us(torch, dev, lambda i, ev=None: step(caches[i % 2], ev), steps)
-    b2b_us = back_to_back_us(torch, lambda i: caches[i % 2].verify(q, ctx, out=out, workspace=ws, splits=splits), 60)
+    step_us, att_us = graph_step_us(torch, dev, lambda i, ev=None: step(caches[i % n_caches], ev), steps)
+    b2b_us = back_to_back_us(torch, lambda i: caches[i % n_caches].verify(q, ctx, out=out, workspace=ws, splits=splits),
+                             60)
     la.sync()
     byts = kv_bytes(ctx + M)
-    return {"workload": "config 3 on 1 GPU: verify round at 131072 cached tokens, 16 drafts (seed 2)",
+    return {"workload": f"{label} on 1 GPU: verify round at {ctx} cached tokens, 16 drafts (seed {seed})",
             "us_per_layer": round(step_us, 2), "verify_us": round(att_us, 2), "splits": splits,
-            "hbm_gbs": round(byts / (att_us * 1e-6) / 1e9, 1), "frac": round(byts / (att_us * 1e-6) / 1e9 / peak_gbs, 4),
+            "hbm_gbs": round(byts / (step_us * 1e-6) / 1e9, 1),
+            "frac": round(byts / (step_us * 1e-6) / 1e9 / peak_gbs, 4),
             "verify_us_back_to_back": round(b2b_us, 2),
             "frac_back_to_back": round(byts / (b2b_us * 1e-6) / 1e9 / peak_gbs, 4),
-            "bytes": byts,
-            "note": "us_per_layer: a graph of rounds (the drafts' append fused into the attention call, rollback) "
-                    "timed whole; verify_us: events around each round's attention call in a second replay (as the "
-                    "headline roofline); back_to_back: a graph of consecutive verify calls timed whole"}
+            "bytes": byts, "caches": n_caches,
+            "note": "us_per_layer / hbm_gbs / frac: a graph of rounds (the drafts' append fused into the attention "
+                    "call, rollback) timed whole; verify_us: events around each round's attention call in a "
+                    "second replay (event nodes cut the launch overlap); back_to_back: a graph of consecutive "
+                    "verify calls timed whole"}
 
 
 def measure_decode(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_caches: int, steps: int = 60) -> dict:
@@ -797,19 +837,12 @@ def run_ours(args):
         pg = dist
     R = Rank(world, rank, args.shard if world > 1 else "single")
 
-    # Inputs: on one GPU the config-2 stream (seed 1: K, V, new K, new V, Q); on N GPUs each rank draws its
-    # own K/V (seed 101 + rank) and every rank slices the same drafts and queries (seed 1).
-    if world == 1:
-        case = synth.verify_case(SEED, CTX, M)
-        Kc, Vc = case["K"], case["V"]
-    else:
-        case = synth.verify_case(SEED, 0, M)
-        st = synth.Stream(SEED + 100 + rank)
-        Kc = st.normal_f16((R.cached, R.kvh, D))
-        Vc = st.normal_f16((R.cached, R.kvh, D))
-    newK = np.ascontiguousarray(case["newK"][:, R.h0:R.h1])
-    newV = np.ascontiguousarray(case["newV"][:, R.h0:R.h1])
-    Qr = np.ascontiguousarray(case["Q"][:, R.q0:R.q1])
+    # Inputs: config 3's stream (seed 2: K, V, new K, new V, Q); each rank draws only its kv heads (heads plan)
+    # or slices its token run (seq plan), bit-identical to slicing the whole draw.
+    case = synth.verify_case_heads(SEED3, CTX3, M, R.h0, R.h1)
+    Kc = case["K"][R.kv_begin:R.kv_begin + R.cached]
+    Vc = case["V"][R.kv_begin:R.kv_begin + R.cached]
+    newK, newV, Qr = case["newK"], case["newV"], case["Q"]
 
     n_layers = max(2, math.ceil(3 * L2_BYTES / (R.cached * R.kvh * D * 4)))
     rope_np = la.rope_table(1e6, 1.0, D, R.ctx_len + M + 1)
@@ -836,7 +869,7 @@ def run_ours(args):
     out = torch.empty((M, QH, D), dtype=torch.float16, device=dev)
     out_l = torch.empty_like(q)
     splits = la.verify_splits(caches[0].layout, R.kv_end - R.kv_begin if R.plan == "seq" else R.ctx_len, M, 0)
-    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(M, R.qh, D, splits), dtype=torch.uint8, device=dev)
+    ws = la.verify_workspace(M, R.qh, D, splits, dev)
     part = torch.empty((M * QH, D + 2), dtype=torch.float32, device=dev)
     gathered = torch.empty((world, M * QH, D + 2), dtype=torch.float32, device=dev)
     gathered_out = torch.empty((world, M, R.qh, D), dtype=torch.float16, device=dev)
@@ -881,7 +914,7 @@ def run_ours(args):
 
     def step(c, timing=None, dq=None, dk=None, dv=None):
         """One verify round of one layer: the drafts' append with the int8 V of their blocks (inside the attention
-        kernel on the fused plans), verify, combine; rollback adds no kernel at a 64-aligned length."""
+        kernel on the fused plans), verify, exchange; rollback adds no kernel at a 64-aligned length."""
         dk = nk if dk is None else dk
         dv = nv if dv is None else dv
         if R.drafts and not fused_round:
@@ -962,6 +995,28 @@ def run_ours(args):
         b2b_us = back_to_back_us(torch, lambda i: attend(caches[i % n_layers], q), 3 * n_layers)
         la.sync()
 
+    # ---- check: on N > 1 the exchanged output of one more eager step against a one-GPU round of all 8 heads
+    # (rank 0's GPU); on one GPU the round's output is what the test suite checks against the oracle.
+    check = None
+    step(caches[0])
+    torch.cuda.synchronize()
+    la.sync()
+    if world > 1 and rank == 0:
+        import shard
+
+        got = out if R.plan == "seq" else shard.assemble_heads(gathered_out)
+        full = synth.verify_case_heads(SEED3, CTX3, M, 0, KVH)
+        ref_cache = la.LayerCache(la.MODE_F16, KVH, D, CTX3 + M + 64, device=dev)
+        ref_cache.append(t(full["K"]), t(full["V"]), 0)
+        want = ref_cache.verify_round(t(full["newK"]), t(full["newV"]), t(full["Q"]), CTX3, rope=rope)
+        la.sync()
+        g64, w64 = got.double().cpu(), want.double().cpu()
+        rms = float(w64.pow(2).mean().sqrt())
+        check = {"against": "one-GPU lfm3a_verify_round of all 8 kv heads on rank 0's GPU",
+                 "max_abs_err_rel_rms": float((g64 - w64).abs().max()) / rms,
+                 "bit_identical": bool(torch.equal(got.cpu(), want.cpu()))}
+        del ref_cache, want, full
+
     # ---- e2e: the public API with host buffers, one step at a time, copies and the result read included.
     # The step's inputs (the drafts' queries, keys and values) travel from one pinned host buffer in one copy.
     e2e_steps = min(K, 200)
@@ -1021,10 +1076,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, calls, threads = cpu_verify_sample(case)
-        cpu = {"value": round(kv_bytes(CTX + M) / sec / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{calls} full verify rounds of one layer at config 2 (oracle, {threads} threads, "
-                         f"{sec * 1e3:.1f} ms each)"}
+        cpu = cpu_baseline_sample()
     del graph, kgraph, load_graph
 
     extras = {}
@@ -1032,7 +1084,7 @@ def run_ours(args):
         pk = peaks()
         del caches
         torch.cuda.empty_cache()
-        extras["c3"] = measure_c3(la, synth, dev, pk["hbm_gbs"])
+        extras["c2"] = measure_verify_cfg(la, synth, dev, pk["hbm_gbs"], CTX, SEED, "config 2")
         torch.cuda.empty_cache()
         extras["decode"] = measure_decodes(la, synth, dev, pk["hbm_gbs"])
         extras["prefix"] = measure_prefix(la)
@@ -1050,7 +1102,7 @@ def run_ours(args):
     if rank == 0:
         pk = peaks()
         achieved = R.bytes_read() / (kern_avg_ms * 1e-3) / 1e9
-        traffic = ncu_traffic("verify_m64_kernel_c2.txt") if world == 1 else None
+        traffic = ncu_traffic("verify_m64_kernel_c3.txt") if world == 1 else None
         plan_text = {"single": "single GPU",
                      "heads": f"kv-head shard x{world}" + (", outputs over NVLink peer stores" if gg else ", NCCL all-gather"),
                      "seq": f"sequence shard x{world}, NCCL all-gather of partials"}
@@ -1064,20 +1116,19 @@ def run_ours(args):
             "ms_per_step": round(ms_step, 5),
             "us_per_layer": round(ms_step * 1e3, 2),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "fp16 (fp32 accumulation)",
-            "data": "synthetic (splitmix64 + Box-Muller fp16; seed 1, and seed 101 + rank for each rank's K/V)",
+            "data": "synthetic (splitmix64 + Box-Muller fp16, seed 2)",
             "config": {
-                "workload": "config 2: verify round of one layer (append 16 drafts with RoPE, verify attention of 16 "
-                            "tokens over 32768 cached + drafts, rollback), GQA 32/8, head_dim 64, fp16 KV"
-                            + (f"; {plan_text[R.plan]}, 32768 x 8 x 64 K/V per GPU, context 32768 x {world}"
-                               if world > 1 else ""),
+                "workload": WORKLOAD + (f"; {plan_text[R.plan]}" if world > 1 else ""),
                 "context_tokens": R.ctx_len,
                 "drafts": M,
+                "kv_heads_per_gpu": R.kvh,
+                "tokens_per_gpu": R.kv_end - R.kv_begin,
                 "splits_per_gpu": splits,
-                "l2": f"{n_layers} rotating layer caches of {R.cached * R.kvh * D * 4 >> 20} MiB (> 126 MB L2), "
-                      "no flush",
+                "l2": f"{n_layers} rotating layer caches of {R.cached * R.kvh * D * 4 >> 20} MiB of K/V per GPU "
+                      "(> 126 MB L2 together), no flush",
                 "parallelism": plan_text[R.plan],
                 "graph": "each timed step replayed from one CUDA graph of K steps",
             },
@@ -1106,11 +1157,13 @@ def run_ours(args):
                     "d2h_bytes_per_step": int(hout.numel() * 2),
                     "how": ("one pinned-host copy of the drafts' q, k, v, lfm3a_verify_round + lfm3a_kv_truncate "
                             "through ctypes, the output read back, a stream sync per step" if direct else
-                            "one pinned-host copy of the drafts' q, k, v, the plan's step (LayerCache calls and "
-                            "the exchange), the output read back, a stream sync per step")},
+                            "one pinned-host copy of this rank's drafts' q, k, v, the plan's step (LayerCache calls "
+                            "and the exchange), the exchanged output read back, a stream sync per step")},
             "gpu_launches": int(launches_per_step * K),
             "clocks": clocks,
         }
+        if check is not None:
+            line["check"] = check
         line.update(extras)
         print(json.dumps(line), flush=True)
     if pg:

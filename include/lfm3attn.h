@@ -86,6 +86,12 @@ int lfm3a_rope_table(double theta, double factor, int head_dim, int positions, u
  * LFM3A_EDEVICE (clearing the word) when a kernel gave up a bounded wait since the last call. */
 int lfm3a_sync(void* stream, int timeout_ms);
 
+/* How long a kernel's bounded wait (a pipeline stage, a tensor-core commit, another GPU's flag) spins before it
+ * gives up and raises the device error word that lfm3a_sync reports as LFM3A_EDEVICE; 0 restores the default
+ * of 2 s. The device-side counterpart of the timeout that internal/kfd/queue.go:292-310 Wait takes. Applies to
+ * the current device, to kernels launched after the call returns (it is a synchronous copy). */
+int lfm3a_set_wait_limit(uint64_t limit_ns);
+
 /* ---------------------------------------------------------------- KV cache */
 /* Append n tokens at positions pos0 .. pos0 + n - 1 of one layer (kernels/ops.hip:236-251 kv_write,
  * Go call internal/model/prefill.go:469-475; the verify-side append dspark.hip:1050-1060).
@@ -141,7 +147,8 @@ int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_
  * whose language runtime has no handle on the CUDA allocator. This entry point allocates nothing: the split
  * partials go to a file-scope device array of LFM3A_VERIFY_SCRATCH_BYTES, one per device.
  * - The first call on each device, made with that device current, looks up the array's address. Make that
- *   call before any stream capture.
+ *   call before any stream capture. The address is kept for the life of the process: after a
+ *   cudaDeviceReset of that device it is stale, so do not call this entry point on a device after resetting it.
  * - A call whose partials (m * q_heads * splits * (head_dim + 2) floats) exceed the array fails with
  *   LFM3A_EWORKSPACE before launching anything.
  * - Every call on a device shares the one array, so calls that overlap on the GPU race; serialise them, for
@@ -253,11 +260,12 @@ int lfm3a_peer_close(void* region);
 /* lfm3a_verify_attention of one rank of the kv-head plan (q_heads = this rank's query heads, rows =
  * m * q_heads). peers[w]: rank w's region as mapped in this process (peers[rank] = this rank's own).
  * The combine writes this rank's rows into slice `rank` of the call's half of every region, then raises
- * this rank's flag in each; lfm3a_gather_wait on the same stream waits (bounded, 2 s, else the device error
- * word) until every rank's slice of this call has landed in the own region, then copies the gathered
- * [world][m][q_heads][head_dim] fp16 output to out (device, or NULL to leave it in the region at
+ * this rank's flag in each; lfm3a_gather_wait on the same stream waits (bounded by lfm3a_set_wait_limit, else
+ * the device error word) until every rank's slice of this call has landed in the own region, then copies the
+ * gathered [world][m][q_heads][head_dim] fp16 output to out (device, or NULL to leave it in the region at
  * region + (n % 2) * world * rows * head_dim halves for call n). Every rank makes the same calls in the
- * same order; needs splits > 1 (a combine); world <= 8. */
+ * same order; world <= 8. The scatter runs in the combine, so the call uses at least two splits; a context
+ * of a single key tile is refused with LFM3A_ENOTSUP before anything is launched. */
 int lfm3a_verify_attention_gather(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
                                   const void* gate, void* const* peers, int world, int rank, void* workspace,
                                   size_t workspace_bytes, int splits, void* stream);

@@ -1,5 +1,5 @@
 // Shared device helpers for the sm_100a KV-cache attention kernels: fp16 packing, bounded mbarrier
-// waits, bulk copies into shared memory, legacy warp MMA fragments and the tcgen05 (TMEM) wrappers.
+// waits, bulk copies into shared memory and the tcgen05 (TMEM) wrappers.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -25,8 +25,12 @@ enum DeviceError : int {
   kErrWaitPeer = 5,    // a wait for another GPU's flag ran out
 };
 
-// A bounded wait gives up after this long (ns of %globaltimer).
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// A bounded wait gives up after this long (ns of %globaltimer). A module-scope variable, 2 s unless the host
+// sets another limit (lfm3a_set_wait_limit); read only once a wait has already missed its first test.
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
+__device__ uint64_t g_wait_limit_ns = kDefaultWaitLimitNs;
+
+__device__ __forceinline__ uint64_t wait_limit_ns() { return *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns); }
 
 __device__ __forceinline__ void raise_error(int code) { atomicCAS(&g_device_error, 0, code); }
 
@@ -71,37 +75,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete; false when kWaitLimitNs passed first.
+// Waits for the phase with the given parity to complete; false when the wait limit passed first.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer();
+  const uint64_t limit = wait_limit_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((i & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
-  }
-}
-
-// Polling form for latency-critical waits of a lone issuing thread: test_wait never suspends, so the thread
-// sees the phase flip within a few cycles; still bounded by kWaitLimitNs.
-__device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_test_wait(a, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test_wait(a, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
+    if ((i & 63u) == 0 && globaltimer() - t0 > limit) return false;
   }
 }
 
@@ -121,11 +103,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
       : "memory");
 }
 
-// Bulk prefetch of global memory into L2 (16-byte aligned, size a multiple of 16); no completion tracking.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // Programmatic dependent launch. Every kernel of the library is launched with programmatic stream
 // serialisation, so it may start while the previous kernel of its stream is still running:
 // pdl_wait() returns once that kernel has completed and its writes are visible (at once if there is
@@ -138,21 +115,6 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
-
-// ---------------------------------------------------------------- warp MMA (m16n8k16, fp16 -> fp32)
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 
 // ---------------------------------------------------------------- tcgen05 (5th-generation tensor cores, TMEM)
 // Shared-memory matrix descriptor, no swizzle, K-major: 8-row x 16-byte core tiles of 128 contiguous bytes;

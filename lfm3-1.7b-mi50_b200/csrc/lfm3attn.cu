@@ -3,8 +3,10 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <chrono>
+#include <mutex>
 #include <string>
 #include <thread>
 
@@ -55,19 +57,21 @@ int current_sm_count() {
   return n;
 }
 
-// Sets a kernel's dynamic shared-memory limit once per device.
+// Sets a kernel's dynamic shared-memory limit once per device. The per-device flags are atomics: host threads
+// that drive different devices (or race on the first call of one) may call in concurrently; setting the
+// attributes twice is harmless, and a flag is raised only after they are set.
 template <typename K>
-int ensure_smem(K kernel, int bytes, bool* done_per_device) {
+int ensure_smem(K kernel, int bytes, std::atomic<bool>* done_per_device) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(LFM3A_EINVAL, "device index out of range");
-  if (!done_per_device[dev]) {
+  if (!done_per_device[dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     // All of the unified L1 / shared storage as shared memory, so two blocks share an SM.
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    done_per_device[dev] = true;
+    done_per_device[dev].store(true, std::memory_order_release);
   }
   return LFM3A_OK;
 }
@@ -185,6 +189,31 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   a.causal = causal ? 1 : 0;
   a.append = 0;
   a.lighten = 0;
+  const int rows = m * q_heads;
+  // Every check comes before the first launch, so a refused call leaves the cache and the outputs untouched.
+  if (gather) {
+    // The exchange runs in the combine: one split would leave no combine to scatter the rows.
+    if (a.splits < 2 && a.t_total >= 2) a.splits = 2;
+    if (a.splits < 2) return fail(LFM3A_ENOTSUP, "the gather needs several splits (a combine): context too short");
+    gather->half_stride = (int64_t)gather->world * rows * 64;
+  }
+  // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
+  if (a.splits == 1 && out32) {
+    a.part = out32;
+  } else if (a.splits > 1) {
+    if (!workspace || !aligned16(workspace)) return fail(LFM3A_EINVAL, "verify needs a 16-byte aligned workspace");
+    if (workspace_bytes < lfm3a_verify_workspace_bytes(m, q_heads, D, a.splits))
+      return fail(LFM3A_EWORKSPACE, "verify workspace too small");
+    a.part = static_cast<float*>(workspace);
+  } else {
+    a.part = nullptr;
+  }
+  if (!(a.splits == 1 && out16)) a.out = nullptr;
+  static std::atomic<bool> done[3][64];
+  if (m <= 16 && D == 128) rc = ensure_smem(verify_m64_kernel<128>, V6Layout<128>::kSmem, done[2]);
+  else if (m <= 16) rc = ensure_smem(verify_m64_kernel<64>, kV6Smem, done[1]);
+  else rc = ensure_smem(verify_kernel<false>, kVfSmem, done[0]);
+  if (rc != LFM3A_OK) return rc;
   if (app) {
     // The appending split gives up kAppendTiles tiles of attention (the append takes about that long) when
     // it keeps at least two; it must hold every 64-token block the drafts touch.
@@ -202,40 +231,12 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
       if (rc != LFM3A_OK) return rc;
     }
   }
-  const int rows = m * q_heads;
-  // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
-  if (a.splits == 1 && out32) {
-    a.part = out32;
-  } else if (a.splits > 1) {
-    if (!workspace || !aligned16(workspace)) return fail(LFM3A_EINVAL, "verify needs a 16-byte aligned workspace");
-    if (workspace_bytes < lfm3a_verify_workspace_bytes(m, q_heads, D, a.splits))
-      return fail(LFM3A_EWORKSPACE, "verify workspace too small");
-    a.part = static_cast<float*>(workspace);
-  } else {
-    a.part = nullptr;
-  }
-  if (!(a.splits == 1 && out16)) a.out = nullptr;
   const dim3 grid(a.splits, L.kv_heads);
-  static bool done[3][64];
-  if (m <= 16 && D == 128) {
-    rc = ensure_smem(verify_m64_kernel<128>, V6Layout<128>::kSmem, done[2]);
-    if (rc != LFM3A_OK) return rc;
-    launch_pdl(verify_m64_kernel<128>, grid, kVfThreads, V6Layout<128>::kSmem, st, a);
-  } else if (m <= 16) {
-    rc = ensure_smem(verify_m64_kernel<64>, kV6Smem, done[1]);
-    if (rc != LFM3A_OK) return rc;
-    launch_pdl(verify_m64_kernel<64>, grid, kVfThreads, kV6Smem, st, a);
-  } else {
-    rc = ensure_smem(verify_kernel<false>, kVfSmem, done[0]);
-    if (rc != LFM3A_OK) return rc;
-    launch_pdl(verify_kernel<false>, grid, kVfThreads, kVfSmem, st, a);
-  }
+  if (m <= 16 && D == 128) launch_pdl(verify_m64_kernel<128>, grid, kVfThreads, V6Layout<128>::kSmem, st, a);
+  else if (m <= 16) launch_pdl(verify_m64_kernel<64>, grid, kVfThreads, kV6Smem, st, a);
+  else launch_pdl(verify_kernel<false>, grid, kVfThreads, kVfSmem, st, a);
   rc = check_launch("verify_kernel");
   if (rc != LFM3A_OK || a.splits == 1) return rc;
-  if (gather) {
-    if (a.splits == 1) return fail(LFM3A_ENOTSUP, "the gather needs several splits (a combine)");
-    gather->half_stride = (int64_t)gather->world * rows * 64;
-  }
   return launch_combine(a.part, rows, a.splits, D, D + 2, (int64_t)a.splits * (D + 2),
                         static_cast<const __half*>(gate), out16, out32, st, gather);
 }
@@ -332,6 +333,12 @@ int lfm3a_sync(void* stream, int timeout_ms) {
   return LFM3A_OK;
 }
 
+int lfm3a_set_wait_limit(uint64_t limit_ns) {
+  const uint64_t v = limit_ns ? limit_ns : kDefaultWaitLimitNs;
+  const cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v));
+  return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, "setting the wait limit");
+}
+
 }  // extern "C"
 
 namespace {
@@ -421,21 +428,21 @@ int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_
 }
 
 // The first call on each device looks up that device's copy of g_verify_scratch (cudaGetSymbolAddress, with the
-// device current); later calls reuse the pointer. The scratch needs no clearing: splits never exceed the key tiles,
-// so every split block writes its whole (acc, max, sum) partial before the combine kernel reads it.
+// device current) under a per-device std::call_once, so host threads that make their first calls together
+// agree on one address; later calls reuse it (a cudaDeviceReset of that device makes it stale). The scratch
+// needs no clearing: splits never exceed the key tiles, so every split block writes its whole (acc, max, sum)
+// partial before the combine kernel reads it.
 int lfm3a_verify_attention_static(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len,
                                   int window, const void* gate, void* out, int splits, void* stream) {
+  static std::once_flag once[64];
   static void* scratch[64];
+  static cudaError_t lookup[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(LFM3A_EINVAL, "device index out of range");
-  if (!scratch[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_verify_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_verify_scratch)");
-    scratch[dev] = p;
-  }
+  std::call_once(once[dev], [dev] { lookup[dev] = cudaGetSymbolAddress(&scratch[dev], g_verify_scratch); });
+  if (lookup[dev] != cudaSuccess) return cuda_fail(lookup[dev], "cudaGetSymbolAddress(g_verify_scratch)");
   if (splits <= 0 && kv)
     splits = verify_splits_for(kv->layout.kv_heads, ctx_len, m, window, current_sm_count(),
                                kv->layout.head_dim == 128 && m <= 16 ? 1 : 2);
@@ -692,13 +699,13 @@ int lfm3a_g128_gemm(const void* a, const float* sa, const void* b, const float* 
     return fail(LFM3A_EINVAL, "g128_gemm: every buffer must be 16-byte aligned");
   if (out_stride < outputs || (residual && residual_stride < outputs))
     return fail(LFM3A_EINVAL, "g128_gemm: row strides must cover the outputs");
-  static bool done[64];
-  static bool regs_ok[64];
+  static std::atomic<bool> done[64];
+  static std::atomic<bool> regs_ok[64];
   rc = ensure_smem(g128_gemm_kernel, kGmRequest, done);
   if (rc != LFM3A_OK) return rc;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(LFM3A_ECUDA, "cudaGetDevice");
-  if (!regs_ok[dev]) {
+  if (!regs_ok[dev].load(std::memory_order_acquire)) {
     // The fold warps' setmaxnreg.inc waits until the block's launch registers cover both shares: refuse to
     // launch a build whose register count would leave it waiting.
     cudaFuncAttributes fa;
@@ -706,7 +713,7 @@ int lfm3a_g128_gemm(const void* a, const float* sa, const void* b, const float* 
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
     if (fa.numRegs * kGmThreads < 128 * kGmCtrlRegs + 32 * kGmFoldWarps * kGmFoldRegs)
       return fail(LFM3A_ENOTSUP, "g128_gemm_kernel built with too few registers for its setmaxnreg split");
-    regs_ok[dev] = true;
+    regs_ok[dev].store(true, std::memory_order_release);
   }
   G128Args g;
   g.a = static_cast<const uint8_t*>(a);

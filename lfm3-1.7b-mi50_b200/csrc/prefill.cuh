@@ -19,6 +19,8 @@
 #pragma once
 #include <algorithm>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "kv.cuh"
 
@@ -878,17 +880,17 @@ __global__ __launch_bounds__(PfLayout<D, I8>::kThreads, PfLayout<D, I8>::kBlocks
 }
 
 inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, int head_dim, cudaStream_t st) {
-  static bool done[12][64];
+  static std::atomic<bool> done[12][64];   // per device: set once the attributes are (see ensure_smem)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LFM3A_ECUDA;
   const dim3 grid(a.qtiles, a.g.kv_heads, a.splits);
   const bool split = a.splits > 1, glue = a.q_norm || a.rope || a.gate;
   auto run = [&](auto kernel, int request, int threads, int slot) -> bool {
-    if (!done[slot][dev]) {
+    if (!done[slot][dev].load(std::memory_order_acquire)) {
       if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, request) != cudaSuccess ||
           cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return false;
-      done[slot][dev] = true;
+      done[slot][dev].store(true, std::memory_order_release);
     }
     launch_pdl(kernel, grid, threads, request, st, a);
     return true;

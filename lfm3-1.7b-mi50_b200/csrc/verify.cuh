@@ -1048,7 +1048,7 @@ __global__ __launch_bounds__(1024) void gather_wait_kernel(__half* region, int w
       unsigned v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
       if ((int)(v - target) >= 0) break;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > wait_limit_ns()) {
         raise_error(kErrWaitPeer);
         s_fail = 1;
         break;

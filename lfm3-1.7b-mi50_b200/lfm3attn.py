@@ -68,6 +68,7 @@ SIGNATURES = {
     "lfm3a_kv_layout_init": (_I, [_I, _I, _I, _I, ctypes.POINTER(KvLayout)]),
     "lfm3a_rope_table": (_I, [ctypes.c_double, ctypes.c_double, _I, _I, _P]),
     "lfm3a_sync": (_I, [_P, _I]),
+    "lfm3a_set_wait_limit": (_I, [ctypes.c_uint64]),
     "lfm3a_kv_append": (_I, [ctypes.POINTER(KvView), _P, _P, _I64, _I, _I, _P, _P, _P]),
     "lfm3a_kv_truncate": (_I, [ctypes.POINTER(KvView), _I, _P]),
     "lfm3a_accept": (_I, [_P, _P, _I, _P, _P]),
@@ -180,6 +181,12 @@ def rope_table(theta: float, factor: float, head_dim: int, positions: int) -> np
 def sync(stream=None, timeout_ms: int = 120000) -> None:
     """Bounded wait for the stream plus the device error word (queue.go:292-310 Wait)."""
     _check(lib().lfm3a_sync(_stream(stream), timeout_ms))
+
+
+def set_wait_limit(limit_ns: int = 0) -> None:
+    """How long the current device's kernels spin in a bounded wait before raising the device error word
+    (0: the default 2 s)."""
+    _check(lib().lfm3a_set_wait_limit(limit_ns))
 
 
 class LayerCache:
@@ -465,6 +472,16 @@ def verify_splits(lay: KvLayout, ctx_len: int, m: int, window: int = 0, sm_count
     if rc < 0:
         _check(rc)
     return rc
+
+
+def verify_workspace(m: int, q_heads: int, head_dim: int, splits: int, device="cuda"):
+    """A zeroed device workspace of lfm3a_verify_workspace_bytes for a verify call (None for one split)."""
+    import torch
+
+    if splits <= 1:
+        return None
+    return torch.zeros(lib().lfm3a_verify_workspace_bytes(m, q_heads, head_dim, splits), dtype=torch.uint8,
+                       device=device)
 
 
 def combine(partials, rows: int, splits: int, head_dim: int, split_stride: int = 0, row_stride: int = 0, gate=None,

@@ -70,6 +70,62 @@ class Stream:
         return self.normal(n).astype(np.float32).astype(np.float16).reshape(shape)
 
 
+def _normal_rows(seed: int, first: int, rows: int, row_stride: int, offset: int, width: int,
+                 chunk_rows: int = 8192) -> np.ndarray:
+    """Values first + r * row_stride + offset + [0, width) of a stream, r < rows, as float16 [rows][width]:
+    the same numbers normal_f16 draws at those positions (offset, width and row_stride even), without the
+    positions between them."""
+    out = np.empty((rows, width), dtype=np.float16)
+
+    def fill(r0: int) -> None:
+        r1 = min(rows, r0 + chunk_rows)
+        pos = (first + offset + np.arange(r0, r1, dtype=np.int64)[:, None] * row_stride +
+               np.arange(0, width, 2, dtype=np.int64)[None, :]).reshape(-1)
+        i = pos.astype(np.uint64) + np.uint64(1)   # output pos of the stream is mix(seed + (pos + 1) gamma)
+        with np.errstate(over="ignore"):
+            z = []
+            for j in (i, i + np.uint64(1)):
+                v = np.uint64(seed) + j * _GAMMA
+                v = (v ^ (v >> np.uint64(30))) * _M1
+                v = (v ^ (v >> np.uint64(27))) * _M2
+                z.append(v ^ (v >> np.uint64(31)))
+        u1 = np.maximum((z[0] >> np.uint64(11)).astype(np.float64) * (2.0 ** -53), 2.0 ** -53)
+        u2 = (z[1] >> np.uint64(11)).astype(np.float64) * (2.0 ** -53)
+        r = np.sqrt(-2.0 * np.log(u1))
+        ang = 2.0 * np.pi * u2
+        vals = np.empty((pos.size, 2), dtype=np.float64)
+        vals[:, 0] = r * np.cos(ang)
+        vals[:, 1] = r * np.sin(ang)
+        out[r0:r1] = vals.reshape(r1 - r0, width).astype(np.float32).astype(np.float16)
+
+    starts = range(0, rows, chunk_rows)
+    if len(starts) > 1:
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(max_workers=min(len(starts), os.cpu_count() or 1)) as pool:
+            list(pool.map(fill, starts))
+    else:
+        for r0 in starts:
+            fill(r0)
+    return out
+
+
+def verify_case_heads(seed: int, ctx_len: int, m: int, h0: int, h1: int, q_heads: int = 32, kv_heads: int = 8,
+                      head_dim: int = 64) -> dict:
+    """kv heads [h0, h1) of verify_case(seed, ctx_len, m) (and their query heads), drawn without the others:
+    a rank of the kv-head plan generates only its share. Bit-identical to slicing verify_case."""
+    g = q_heads // kv_heads
+    row = kv_heads * head_dim
+    off, width = h0 * head_dim, (h1 - h0) * head_dim
+    base = 0
+    out = {}
+    for name, rows in (("K", ctx_len), ("V", ctx_len), ("newK", m), ("newV", m)):
+        out[name] = _normal_rows(seed, base, rows, row, off, width).reshape(rows, h1 - h0, head_dim)
+        base += rows * row
+    out["Q"] = _normal_rows(seed, base, m, q_heads * head_dim, g * off, g * width).reshape(m, g * (h1 - h0), head_dim)
+    return out
+
+
 def verify_case(seed: int, ctx_len: int, m: int, q_heads: int = 32, kv_heads: int = 8, head_dim: int = 64) -> dict:
     """Cache K, V [ctx_len][kv_heads][head_dim], drafts new K, new V [m][kv_heads][head_dim], Q [m][q_heads][head_dim]."""
     s = Stream(seed)

@@ -159,3 +159,34 @@ def test_head_dim_128_host_logic(la):
     assert lib.lfm3a_prefill_workspace_bytes(64, 16, 128) > 0
     assert lib.lfm3a_prefill_workspace_bytes(64, 16, 96) == 0
     assert lib.lfm3a_prefill_workspace_bytes(64, 16, 128) % (64 * 16 * 130 * 4) == 0
+
+
+def test_refusals_come_before_any_launch(la):
+    """Argument faults that only show once the split count is known are refused before the first launch: a
+    gather over a context of one key tile (no combine to scatter from), and a verify round whose workspace is
+    too small (the drafts would otherwise already be appended). On this CPU-only host a launch would fail
+    with LFM3A_ECUDA, so the codes below also show that nothing was launched."""
+    lib = la.lib()
+    good = la.KvView(64, 64, 10, la.layout(0, 8, 64))
+    half = la.KvView(64, 64, 10, la.layout(0, 4, 64))   # one rank of two under the kv-head plan
+    peers = (ctypes.c_void_p * 2)(64, 128)
+    # 40 cached tokens + 8 drafts: one 128-key tile.
+    rc = lib.lfm3a_verify_attention_gather(ctypes.byref(half), 64, 8, 16, 40, 0, None, peers, 2, 0, 64, 1 << 20, 1,
+                                           None)
+    assert rc == la.ENOTSUP
+    assert b"gather" in lib.lfm3a_last_error()
+    # 1000 cached tokens, 16 drafts, 4 splits: the partials need 16 * 32 * 4 * 66 * 4 bytes.
+    rc = lib.lfm3a_verify_round(ctypes.byref(good), 64, 64, 0, None, None, 64, 16, 32, 1000, 0, None, 64, 64, 16, 4,
+                                None)
+    assert rc == la.EWORKSPACE
+    assert lib.lfm3a_set_wait_limit  # exported; setting it needs a device
+
+
+def test_synth_head_slices_match_full_draw(synth):
+    """A rank of the kv-head plan draws only its heads (verify_case_heads); the values are the full draw's."""
+    full = synth.verify_case(9, 700, 16)
+    for h0, h1 in [(0, 8), (0, 1), (3, 5), (7, 8)]:
+        part = synth.verify_case_heads(9, 700, 16, h0, h1)
+        for k in ("K", "V", "newK", "newV"):
+            assert np.array_equal(part[k].view(np.uint16), full[k][:, h0:h1].view(np.uint16)), k
+        assert np.array_equal(part["Q"].view(np.uint16), full["Q"][:, 4 * h0:4 * h1].view(np.uint16))

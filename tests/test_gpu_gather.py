@@ -57,3 +57,52 @@ def test_heads_gather_two_emulated_ranks(la, orc, synth, cuda):
     finally:
         for reg in regions:
             la.lib().lfm3a_gather_region_free(reg)
+
+
+def test_gather_wait_runs_out_and_recovers(la, orc, synth, cuda):
+    """Failure detection without a GPU fault (the bounded Wait of internal/kfd/queue.go:292-310): of two emulated
+    ranks only rank 0 verifies in one call, so rank 1's slice never lands. Each region's wait, with the limit set
+    to 20 ms, gives up, raises the device error word and returns; lfm3a_sync reports LFM3A_EDEVICE. With the
+    default limit restored the ranks stay in step: the next call, made by both, gathers the right output."""
+    import torch
+
+    ctx, m, world = 3000, 8, 2
+    c = synth.verify_case(63, ctx, m)
+    K = np.concatenate([c["K"], c["newK"]])
+    V = np.concatenate([c["V"], c["newV"]])
+    rows = m * 16
+    regions = [la.GatherGroup.alloc_region(world, rows, 64) for _ in range(world)]
+    try:
+        groups = [la.GatherGroup(world, r, rows, 64, regions=regions) for r in range(world)]
+        caches, qs = [], []
+        for r in range(world):
+            h0, h1 = head_range(world, r, 8)
+            q0, q1 = query_head_range(world, r, 8, 32)
+            cache = la.LayerCache(la.MODE_F16, h1 - h0, 64, ctx + m + 64, device=cuda)
+            cache.append(dev(K[:, h0:h1], cuda), dev(V[:, h0:h1], cuda), 0)
+            caches.append(cache)
+            qs.append(dev(c["Q"][:, q0:q1], cuda))
+        la.sync()
+        la.set_wait_limit(20_000_000)
+        try:
+            groups[0].verify(caches[0], qs[0], ctx)      # rank 1 never verifies in this call
+            for r in range(world):
+                groups[r].wait(None)
+            with pytest.raises(la.LFM3AError) as err:
+                la.sync(timeout_ms=10000)
+            assert err.value.code == la.EDEVICE
+        finally:
+            la.set_wait_limit(0)
+        la.sync()                                        # the error word was cleared
+        for r in range(world):
+            groups[r].verify(caches[r], qs[r], ctx)
+        want = orc.verify(c["Q"], K, V, ctx)
+        for r in range(world):
+            out = torch.zeros((world, m, 16, 64), dtype=torch.float16, device=cuda)
+            groups[r].wait(out)
+            la.sync()
+            got = out.permute(1, 0, 2, 3).reshape(m, 32, 64).float().cpu().numpy()
+            assert rel_err(got, want) < 4e-3, r
+    finally:
+        for reg in regions:
+            la.lib().lfm3a_gather_region_free(reg)

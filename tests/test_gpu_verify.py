@@ -331,3 +331,58 @@ def test_verify_round_head_dim_128(la, orc, synth, cuda):
     v8, sc = orc.quantize_v8(V[:ctx + 3], ctx + 3)
     logical = cache.logical(ctx + 3)
     assert np.array_equal(logical["V8"], v8) and np.array_equal(logical["vscale"], sc)
+
+
+def test_verify_round_c3_full_size(la, orc, synth, cuda):
+    """Benchmark config 3 at full size through the round entry point: 131072 cached tokens (seed 2), 16 drafts
+    appended with RoPE inside the attention kernel, verified causally. The output against exact fp64 and against
+    the oracle's split-KV verify; the drafts' cache bytes (K, V, the int8 V of their block) bit-exact."""
+    ctx, m = 131072, 16
+    case = synth.verify_case(2, ctx, m)
+    rope_np = la.rope_table(1e6, 1.0, 64, ctx + m + 1)
+    cache = la.LayerCache(la.MODE_F16, 8, 64, ctx + m + 64, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    out = cache.verify_round(dev(case["newK"], cuda), dev(case["newV"], cuda), dev(case["Q"], cuda), ctx,
+                             rope=dev(rope_np.view(np.float16), cuda))
+    la.sync()
+    got = out.float().cpu().numpy()
+    k_new, v_new = orc.kv_append_f16(case["newK"], case["newV"], ctx, rope=rope_np.view(np.float16))
+    K = np.concatenate([case["K"], k_new])
+    V = np.concatenate([case["V"], v_new])
+    assert rel_err(got, orc.attention_f64(case["Q"], ctx, K, V, ctx + m)) < TOL
+    assert rel_err(got, orc.verify(case["Q"], K, V, ctx, splits=37)) < TOL_PAIR
+    pool = cache.pool.cpu().numpy()
+    table = cache.table.cpu().numpy()
+    tail = la.decode_pool(pool, table, cache.layout, ctx + m)
+    assert np.array_equal(tail["K"][ctx:], k_new.view(np.uint16))
+    assert np.array_equal(tail["V"][ctx:], v_new.view(np.uint16))
+    v8, sc = orc.quantize_v8(V, ctx + m)
+    assert np.array_equal(tail["V8"][ctx:ctx + m], v8[ctx:ctx + m])
+    assert np.array_equal(tail["vscale"][-1], sc[-1])
+
+
+def test_refused_round_leaves_cache_unchanged(la, synth, cuda):
+    """A verify round whose workspace is too small is refused (LFM3A_EWORKSPACE) before the drafts' append is
+    launched: the cache bytes stay as they were."""
+    import ctypes
+
+    import torch
+
+    ctx, m = 4000, 16
+    case = synth.verify_case(71, ctx, m)
+    cache = la.LayerCache(la.MODE_F16, 8, 64, ctx + m + 64, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    la.sync()
+    before = cache.pool.clone()
+    splits = la.verify_splits(cache.layout, ctx, m)
+    assert splits > 1
+    small = torch.empty(256, dtype=torch.uint8, device=cuda)
+    out = torch.zeros((m, 32, 64), dtype=torch.float16, device=cuda)
+    nk, nv, q = dev(case["newK"], cuda), dev(case["newV"], cuda), dev(case["Q"], cuda)
+    rc = la.lib().lfm3a_verify_round(ctypes.byref(cache.view), nk.data_ptr(), nv.data_ptr(), 0, None, None,
+                                     q.data_ptr(), m, 32, ctx, 0, None, out.data_ptr(), small.data_ptr(), 256, splits,
+                                     torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == la.EWORKSPACE
+    la.sync()
+    assert torch.equal(cache.pool, before)
+    assert not out.any()
