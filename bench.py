@@ -413,7 +413,7 @@ def measure_decode(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_cache
     q, nk, nv = t(case["Q"]), t(case["newK"]), t(case["newV"])
     out = torch.empty_like(q)
     splits = la.verify_splits(caches[0].layout, ctx, 1, 0)
-    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(1, QH, D, splits), dtype=torch.uint8, device=dev)
+    ws = la.verify_workspace(1, QH, D, splits, dev)
 
     def step(c, ev=None):   # one round: the drafts' append fused into the attention call, then the rollback
         if ev:
@@ -466,7 +466,7 @@ def measure_ref_geometry(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n
     q, nk, nv = t(case["Q"]), t(case["newK"]), t(case["newV"])
     out = torch.empty_like(q)
     splits = la.verify_splits(caches[0].layout, ctx, m, 0)
-    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8, device=dev)
+    ws = la.verify_workspace(m, qh, d, splits, dev)
 
     def step(c, ev=None):   # one round: append the drafts (its own kernel at head_dim 128), attend, roll back
         if ev:
@@ -635,7 +635,7 @@ def measure_ring(la, dev, live: int = 4096, m: int = M, ctx_len: int = 20000) ->
     cache.append(rnd(m, KVH, D), rnd(m, KVH, D), ctx_len)
     q, out = rnd(m, QH, D), torch.empty((m, QH, D), dtype=torch.float16, device=dev)
     splits = la.verify_splits(cache.layout, live, m, 0)
-    ws = torch.empty(max(1, la.lib().lfm3a_verify_workspace_bytes(m, QH, D, splits)), dtype=torch.uint8, device=dev)
+    ws = la.verify_workspace(m, QH, D, splits, dev)
     us = back_to_back_us(torch, lambda i: cache.ring_attention(q, ctx_len - live, ctx_len, out=out, workspace=ws,
                                                                splits=splits), 60)
     la.sync()
@@ -782,8 +782,7 @@ def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, se
     del k_in, q_pre, out_pre
     drafts = rnd(steps, 2, M, KVH, D)
     qs = rnd(steps, M, QH, D)
-    splits_ws = la.lib().lfm3a_verify_workspace_bytes(M, QH, D, 2 * 148)
-    ws = torch.empty(splits_ws, dtype=torch.uint8, device=dev)
+    ws = la.verify_workspace(M, QH, D, 2 * 148, dev)
     out = torch.empty((M, QH, D), dtype=torch.float16, device=dev)
     stream = torch.cuda.Stream(device=dev)
     g = torch.cuda.CUDAGraph()

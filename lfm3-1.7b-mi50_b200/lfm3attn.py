@@ -246,7 +246,7 @@ class LayerCache:
             splits = verify_splits(self.layout, ctx_len, m, window)
         need = lib().lfm3a_verify_workspace_bytes(m, qh, d, splits)
         if workspace is None and splits > 1:
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
         _check(lib().lfm3a_verify_attention(ctypes.byref(self.view), _ptr(q), m, qh, ctx_len, window, _ptr(gate),
                                             _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
@@ -266,7 +266,7 @@ class LayerCache:
         if splits <= 0:
             splits = verify_splits(self.layout, ctx_len, m, window)
         if workspace is None and splits > 1:
-            workspace = torch.empty(lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8,
+            workspace = torch.zeros(lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8,
                                     device=q.device)
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
         _check(lib().lfm3a_verify_round(ctypes.byref(self.view), _ptr(k), _ptr(v), 0, _ptr(rope), _ptr(k_norm), _ptr(q),
@@ -288,7 +288,7 @@ class LayerCache:
             splits = verify_splits(self.layout, ctx_len - ctx_lo, m, 0)
         if workspace is None and splits > 1:
             need = lib().lfm3a_verify_workspace_bytes(m, qh, d, splits)
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
         _check(lib().lfm3a_ring_attention(ctypes.byref(self.view), _ptr(q), m, qh, ctx_lo, ctx_len, _ptr(out),
                                           _ptr(workspace), ws_bytes, splits, _stream(stream)))
@@ -306,7 +306,7 @@ class LayerCache:
             splits = verify_splits(self.layout, kv_end - kv_begin, 1, 0)
         need = lib().lfm3a_verify_workspace_bytes(m, qh, d, splits)
         if workspace is None and splits > 1:
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
         _check(lib().lfm3a_verify_partial(ctypes.byref(self.view), _ptr(q), m, qh, kv_begin, kv_end, ctx_len, window,
                                           _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
@@ -328,7 +328,7 @@ class LayerCache:
             out = torch.empty((t, qh, d), dtype=torch.float16, device=q.device)
         need = lib().lfm3a_prefill_workspace_bytes(t, qh, d)
         if workspace is None and need:
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
         gate_stride = gate.stride(0) if gate is not None else 0
         _check(lib().lfm3a_prefill_attention_fused(ctypes.byref(self.view), _ptr(q), q_stride, _ptr(q_norm),
@@ -703,7 +703,7 @@ class GatherGroup:
         if splits <= 0:
             splits = verify_splits(cache.layout, ctx_len, m, window)
         if workspace is None:
-            workspace = torch.empty(lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8,
+            workspace = torch.zeros(lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8,
                                     device=q.device)
         ws_bytes = workspace.numel() * workspace.element_size()
         _check(lib().lfm3a_verify_attention_gather(ctypes.byref(cache.view), _ptr(q), m, qh, ctx_len, window,

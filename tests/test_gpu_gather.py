@@ -24,7 +24,10 @@ def rel_err(got, want):
     return float(np.max(np.clip(np.abs(got.astype(np.float64) - want) - half_ulp, 0.0, None))) / rms
 
 
-def test_heads_gather_two_emulated_ranks(la, orc, synth, cuda):
+@pytest.mark.parametrize("splits", [0, 7, 200])
+def test_heads_gather_two_emulated_ranks(la, orc, synth, cuda, splits):
+    """splits 0: the library's count; 7; 200: more splits than the narrow combine holds (the row-per-block
+    combine scatters)."""
     import torch
 
     ctx, m, world = 6000, 16, 2
@@ -46,7 +49,7 @@ def test_heads_gather_two_emulated_ranks(la, orc, synth, cuda):
             Q = c["Q"] if call == 0 else s.normal_f16((m, 32, 64))
             for r in range(world):
                 q0, q1 = query_head_range(world, r, 8, 32)
-                groups[r].verify(caches[r], dev(Q[:, q0:q1], cuda), ctx)
+                groups[r].verify(caches[r], dev(Q[:, q0:q1], cuda), ctx, splits=splits)
             want = orc.verify(Q, K, V, ctx)
             for r in range(world):
                 out = torch.zeros((world, m, 16, 64), dtype=torch.float16, device=cuda)

@@ -1,11 +1,12 @@
 """lfm3a_verify_attention_static (split partials in the library's fixed device scratch) against
-lfm3a_verify_attention (caller's workspace), both called through the C ABI.
+lfm3a_verify_attention (caller's workspace), both called through the C ABI, and against exact fp64 attention.
 
 Two static calls in a row on one stream share the one scratch array: a 16-token verify over 32768 cached
 tokens (M = 64 kernel, 37 splits) and then a 24-token verify over 5000 with a window (M = 128 kernel). Each
-output must match the workspace entry point within the verify tolerance between implementations (4e-3 of
-the output RMS beyond half an fp16 ulp). A call whose partials exceed the scratch must fail with
-LFM3A_EWORKSPACE before launching anything. The file sorts last so that it also runs after every other test.
+output must match the workspace entry point within the verify tolerance between implementations (4e-3 of the
+output RMS beyond half an fp16 ulp) and exact fp64 attention within the verify tolerance (2e-3). A call whose partials exceed the scratch
+must fail with LFM3A_EWORKSPACE before launching anything. The file sorts last so that it also runs after every
+other test.
 """
 import ctypes
 
@@ -15,6 +16,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 TOL_PAIR = 4e-3
+TOL_F64 = 2e-3
 
 
 def dev(a, cuda):
@@ -44,7 +46,7 @@ def call_static(la, cache, q, ctx_len, window, out, splits, stream):
                                                   None, out.data_ptr(), splits, stream)
 
 
-def test_static_scratch_matches_workspace_entry(la, synth, cuda):
+def test_static_scratch_matches_workspace_entry(la, orc, synth, cuda):
     import torch
 
     stream = torch.cuda.current_stream(cuda).cuda_stream
@@ -59,7 +61,11 @@ def test_static_scratch_matches_workspace_entry(la, synth, cuda):
     for (seed, ctx, m, window), (case, cache), q, out in zip(runs, cases, qs, outs):
         want = cache.verify(q, ctx, window=window)
         la.sync()
-        assert rel_err(out.float().cpu().numpy(), want.float().cpu().numpy()) < TOL_PAIR
+        got = out.float().cpu().numpy()
+        assert rel_err(got, want.float().cpu().numpy()) < TOL_PAIR
+        K = np.concatenate([case["K"], case["newK"]])
+        V = np.concatenate([case["V"], case["newV"]])
+        assert rel_err(got, orc.attention_f64(case["Q"], ctx, K, V, ctx + m, window=window)) < TOL_F64
 
 
 def test_static_scratch_rejects_oversize(la, synth, cuda):
