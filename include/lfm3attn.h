@@ -244,7 +244,7 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
  * landed, in place of a separate all-gather.
  *
  * A gather region holds [2][world][rows][head_dim] fp16 (the gathered outputs of even and odd calls), then
- * uint32 flags per (source rank, combine block) and a call counter. It must be its own allocation (so that
+ * uint32 flags per (source rank, row) and a call counter. It must be its own allocation (so that
  * other processes can map it) and start zeroed: lfm3a_gather_region_alloc gives one. head_dim 64, at most
  * 1024 rows. */
 size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim);

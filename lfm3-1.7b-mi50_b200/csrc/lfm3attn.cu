@@ -124,19 +124,24 @@ int verify_splits_for(int kv_heads, int ctx_len, int m, int window, int sm_count
 
 int launch_combine(const float* part, int rows, int splits, int head_dim, int64_t split_stride, int64_t row_stride,
                    const __half* gate, __half* out16, float* out32, cudaStream_t st, const GatherOut* gather = nullptr) {
-  // Up to 64 splits the lanes hold two (max, sum) pairs each; more splits (few kv heads) take the wide variant.
-  const bool narrow = splits <= 64;
   const GatherOut go = gather ? *gather : GatherOut{};
-  auto run = [&](auto kernel, int rows_per_block) {
-    launch_pdl(kernel, (rows + rows_per_block - 1) / rows_per_block, 256, 0, st, part, rows, splits, split_stride,
-               row_stride, gate, out16, out32, go);
-  };
-  if (gather) {   // the kv-head plan's scatter to the ranks' gather regions (head_dim 64 only)
-    narrow ? run(combine_kernel<64, 2, true>, 4) : run(combine_kernel<64, 12, true>, 4);
-  } else if (head_dim == 64) {
-    narrow ? run(combine_kernel<64, 2, false>, 4) : run(combine_kernel<64, 12, false>, 4);
-  } else {
-    narrow ? run(combine_kernel<128, 2, false>, 2) : run(combine_kernel<128, 12, false>, 2);
+  if (splits <= 64) {   // thread = (row, dim), every load up front
+    auto run = [&](auto kernel, int rows_per_block) {
+      launch_pdl(kernel, (rows + rows_per_block - 1) / rows_per_block, 256, 0, st, part, rows, splits, split_stride,
+                 row_stride, gate, out16, out32, go);
+    };
+    if (gather) run(combine_kernel<64, true>, 4);   // the kv-head plan's scatter to the ranks' regions (head_dim 64)
+    else if (head_dim == 64) run(combine_kernel<64, false>, 4);
+    else run(combine_kernel<128, false>, 2);
+  } else {              // a block per row, the splits spread over its threads
+    auto run = [&](auto kernel) {
+      launch_pdl(kernel, rows, kCombineRowThreads, (size_t)splits * sizeof(float), st, part, rows, splits,
+                 split_stride, row_stride, gate, out16, out32, go);
+    };
+    if (splits > 12288) return fail(LFM3A_EINVAL, "combine: at most 12288 splits");
+    if (gather) run(combine_row_kernel<64, true>);
+    else if (head_dim == 64) run(combine_row_kernel<64, false>);
+    else run(combine_row_kernel<128, false>);
   }
   return check_launch("combine_kernel");
 }
@@ -557,9 +562,9 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
 
 size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim) {
   if (world < 1 || world > 8 || rows < 1 || head_dim < 1) return 0;
-  if ((rows + 3) / 4 > kGatherBlocks) return 0;
+  if (rows > kGatherRows) return 0;
   const size_t data = (size_t)2 * world * rows * head_dim * sizeof(__half);
-  return (data + ((size_t)world * kGatherBlocks + 1) * sizeof(unsigned) + 255) / 256 * 256;
+  return (data + ((size_t)world * kGatherRows + 1) * sizeof(unsigned) + 255) / 256 * 256;
 }
 
 int lfm3a_gather_region_alloc(int world, int rows, int head_dim, void** region_out) {
@@ -621,9 +626,8 @@ int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out
   if (!region || world < 1 || world > 8 || rows < 1 || head_dim < 1 || (out && !aligned16(out)))
     return fail(LFM3A_EINVAL, "bad gather wait arguments");
   const int64_t half_stride = (int64_t)world * rows * head_dim;
-  const int blocks = (rows + 3) / 4;   // the combine's blocks (4 rows of 64 dims each)
-  if (head_dim != 64 || blocks > kGatherBlocks) return fail(LFM3A_ENOTSUP, "gather: head_dim 64, at most 1024 rows");
-  launch_pdl(gather_wait_kernel, 1, 1024, 0, as_stream(stream), static_cast<__half*>(region), world, half_stride, blocks,
+  if (head_dim != 64 || rows > kGatherRows) return fail(LFM3A_ENOTSUP, "gather: head_dim 64, at most 1024 rows");
+  launch_pdl(gather_wait_kernel, 1, 1024, 0, as_stream(stream), static_cast<__half*>(region), world, half_stride, rows,
              static_cast<__half*>(out));
   return check_launch("gather_wait_kernel");
 }

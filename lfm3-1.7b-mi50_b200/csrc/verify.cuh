@@ -901,18 +901,17 @@ __global__ __launch_bounds__(kVfThreads, V6Layout<D>::kBlocksPerSm) void verify_
   }
 }
 
-// Log-sum-exp merge of split partials. Thread = (row, dim): 256 / D rows per block. Partial s of row r starts
-// at part + r * row_stride + s * split_stride (floats). The loads are issued up front: each lane the (max, sum)
-// of splits lane, lane + 32, ... (up to 32 * KM splits in registers: KM = 2 up to 64 splits, 12 up to 384),
-// each thread its dim of the first 64 splits' acc, so the usual merge (up to 64 splits) costs one L2 round
-// trip and every further 64
-// splits one more. The row max is a warp reduction; the weight 2^(m_s - M) of split s is computed once, by the
-// lane holding it, and broadcast with shuffles. With out16 the result is the gate-scaled fp16 output;
-// otherwise the merged partial (acc relative to the common max, max, sum) goes to out32[r][D + 2].
+// Log-sum-exp merge of split partials (dspark.hip:2134-2185 combine_phase). Partial s of row r starts at
+// part + r * row_stride + s * split_stride (floats): acc[D] relative to its max, max (log2 units), sum. With out16
+// the result is the gate-scaled fp16 output; otherwise the merged partial (acc relative to the common max, max,
+// sum) goes to out32[r][D + 2]. Two kernels by the shape: up to 64 splits, combine_kernel (thread = (row, dim),
+// 256 / D rows per block, every load issued up front: one L2 round trip); beyond, combine_row_kernel (a block per
+// row, the splits spread over its threads), for the few rows and many splits of a kv-head shard.
+//
 // Where the kv-head plan's combine sends a rank's output: slice `rank` of the current call's half of every
-// rank's gather region (peers[w], mapped here), then a flag per (source rank, combine block) in each region.
-// The region is [2][world][rows][D] fp16, flags [world][kGatherBlocks] u32, then this rank's call counter.
-constexpr int kGatherBlocks = 256;   // combine blocks of one call at most: 1024 rows of 64 dims
+// rank's gather region (peers[w], mapped here), then a flag per (source rank, row) in each region.
+// The region is [2][world][rows][D] fp16, flags [world][kGatherRows] u32, then this rank's call counter.
+constexpr int kGatherRows = 1024;   // rows of one call at most
 struct GatherOut {
   __half* peers[8];
   int world = 0, rank = 0;
@@ -923,7 +922,27 @@ __device__ __forceinline__ unsigned* gather_flags(__half* region, int64_t half_s
   return reinterpret_cast<unsigned*>(region + 2 * half_stride);
 }
 
-template <int D, int KM, bool GATHER>
+// The gather exchange's call counter of this rank (advanced by gather_wait_kernel after each call).
+__device__ __forceinline__ unsigned gather_calls(const GatherOut& go) {
+  return *reinterpret_cast<volatile unsigned*>(gather_flags(go.peers[go.rank], go.half_stride) +
+                                               go.world * kGatherRows);
+}
+
+// After the block's peer stores of rows [r0, r1): one thread fences at system scope and raises those rows' flags in
+// every region with release stores (callers put a block barrier before it).
+__device__ __forceinline__ void gather_raise(const GatherOut& go, int r0, int r1, unsigned calls) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+#pragma unroll 1
+  for (int w = 0; w < go.world; ++w)
+    for (int r = r0; r < r1; ++r)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(gather_flags(go.peers[w], go.half_stride) +
+                                                                 go.rank * kGatherRows + r),
+                   "r"(calls + 1)
+                   : "memory");
+}
+
+template <int D, bool GATHER>
 __global__ __launch_bounds__(256) void combine_kernel(const float* part, int rows, int splits, int64_t split_stride,
                                                       int64_t row_stride, const __half* gate, __half* out16,
                                                       float* out32, GatherOut go) {
@@ -935,9 +954,9 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
   const bool live = row_raw < rows;   // whole warps: D is a multiple of 32
   const int row = live ? row_raw : rows - 1;
   const float* base = part + (int64_t)row * row_stride;
-  float wk[KM], lk[KM];   // (max, then weight) and sum of split lane + 32 k
+  float wk[2], lk[2];   // (max, then weight) and sum of splits lane, lane + 32
 #pragma unroll
-  for (int k = 0; k < KM; ++k) {
+  for (int k = 0; k < 2; ++k) {
     const int s = lane + 32 * k;
     wk[k] = s < splits ? base[(int64_t)s * split_stride + D] : -INFINITY;
     lk[k] = s < splits ? base[(int64_t)s * split_stride + D + 1] : 0.f;
@@ -945,73 +964,39 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
   float v[64];
 #pragma unroll
   for (int u = 0; u < 64; ++u) v[u] = u < splits ? base[(int64_t)u * split_stride + d] : 0.f;
-  float M = -INFINITY;
-#pragma unroll
-  for (int k = 0; k < KM; ++k) M = fmaxf(M, wk[k]);
-  for (int s = 32 * KM + lane; s < splits; s += 32) M = fmaxf(M, base[(int64_t)s * split_stride + D]);
+  float M = fmaxf(wk[0], wk[1]);
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   float L = 0.f;
 #pragma unroll
-  for (int k = 0; k < KM; ++k) {
+  for (int k = 0; k < 2; ++k) {
     wk[k] = wk[k] == -INFINITY ? 0.f : exp2f(wk[k] - M);
     L = fmaf(wk[k], lk[k], L);
   }
-  float acc = 0.f;
+  float a0 = 0.f, a1 = 0.f;   // the weight of split s is broadcast from the lane holding it
 #pragma unroll
-  for (int c = 0; c < (KM + 1) / 2; ++c) {   // 64 splits per chunk: weights in wk[2c] (splits 64c + u), wk[2c + 1]
-    if (64 * c >= splits) break;
-    if (c > 0) {
-#pragma unroll
-      for (int u = 0; u < 64; ++u)
-        v[u] = 64 * c + u < splits ? base[(int64_t)(64 * c + u) * split_stride + d] : 0.f;
-    }
-    float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      a0 = fmaf(__shfl_sync(0xffffffffu, wk[2 * c], u), v[u], a0);
-      if (2 * c + 1 < KM) a1 = fmaf(__shfl_sync(0xffffffffu, wk[2 * c + 1], u), v[32 + u], a1);
-    }
-    acc += a0 + a1;
+  for (int u = 0; u < 32; ++u) {
+    a0 = fmaf(__shfl_sync(0xffffffffu, wk[0], u), v[u], a0);
+    a1 = fmaf(__shfl_sync(0xffffffffu, wk[1], u), v[32 + u], a1);
   }
-  for (int s0 = 32 * KM; s0 < splits; s0 += 32) {   // past 32 * KM splits (not reached by verify)
-    const int sl = s0 + lane;
-    float w = 0.f;
-    if (sl < splits) {
-      const float ms = base[(int64_t)sl * split_stride + D];
-      w = ms == -INFINITY ? 0.f : exp2f(ms - M);
-      L = fmaf(w, base[(int64_t)sl * split_stride + D + 1], L);
-    }
-    for (int u = 0; u < 32 && s0 + u < splits; ++u)
-      acc = fmaf(__shfl_sync(0xffffffffu, w, u), base[(int64_t)(s0 + u) * split_stride + d], acc);
-  }
+  const float acc = a0 + a1;
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
   if (GATHER) {
     // The block's rows (contiguous in every region) are staged in shared memory and sent to every rank's
-    // region as 16-byte peer stores; after a block barrier one thread fences at system scope and raises this
-    // block's flag in every region with release stores.
+    // region as 16-byte peer stores; after a block barrier their flags go up.
     __shared__ __align__(16) __half s_out[256];
-    unsigned* my_flags = gather_flags(go.peers[go.rank], go.half_stride);
-    const unsigned calls = *reinterpret_cast<volatile unsigned*>(my_flags + go.world * kGatherBlocks);
+    const unsigned calls = gather_calls(go);
     s_out[threadIdx.x] = __float2half_rn(live ? acc * (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row) : 0.f);
     __syncthreads();
-    const int r0 = blockIdx.x * RPB, nvec = min(RPB, rows - r0) * D / 8;
+    const int r0 = blockIdx.x * RPB, r1 = min(r0 + RPB, rows), nvec = (r1 - r0) * D / 8;
     const int64_t off = (int64_t)(calls & 1u) * go.half_stride + ((int64_t)go.rank * rows + r0) * D;
     for (int i = threadIdx.x; i < nvec * go.world; i += blockDim.x) {
       const int w = i / nvec, c = i - w * nvec;
       reinterpret_cast<uint4*>(go.peers[w] + off)[c] = reinterpret_cast<const uint4*>(s_out)[c];
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-#pragma unroll 1
-      for (int w = 0; w < go.world; ++w)
-        asm volatile("st.release.sys.global.u32 [%0], %1;"
-                     ::"l"(gather_flags(go.peers[w], go.half_stride) + go.rank * kGatherBlocks + blockIdx.x),
-                     "r"(calls + 1)
-                     : "memory");
-    }
+    gather_raise(go, r0, r1, calls);
     return;
   }
   if (!live) return;
@@ -1028,21 +1013,119 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
   }
 }
 
-// One block: waits (bounded) until every (rank, combine block) flag of this rank's current call has been
+// One block of 512 threads per row. (1) The splits' maxima into shared memory and the row max; (2) each split's
+// weight 2^(m_s - M), the weighted sum of the sums; (3) thread (column pair c, split group g) adds up the weighted
+// acc of splits g, g + G, ... (G = 512 / (D / 2) groups, each thread's loads issued eight at a time); (4) the
+// groups meet in shared memory. Dynamic shared memory: splits floats.
+constexpr int kCombineRowThreads = 512;
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();   // red is free (its previous use has been read)
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : (is_max ? -INFINITY : 0.f);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  return v;
+}
+
+template <int D, bool GATHER>
+__global__ __launch_bounds__(kCombineRowThreads) void combine_row_kernel(const float* part, int rows, int splits,
+                                                                         int64_t split_stride, int64_t row_stride,
+                                                                         const __half* gate, __half* out16,
+                                                                         float* out32, GatherOut go) {
+  constexpr int C2 = D / 2, G = kCombineRowThreads / C2;
+  extern __shared__ float s_w[];                  // per split: its max, then its weight
+  __shared__ float red[32];
+  __shared__ float2 s_acc[G][C2];
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const float* base = part + (int64_t)row * row_stride;
+  float mx = -INFINITY;
+  for (int s = tid; s < splits; s += kCombineRowThreads) {
+    const float m = base[(int64_t)s * split_stride + D];
+    s_w[s] = m;
+    mx = fmaxf(mx, m);
+  }
+  mx = block_reduce(mx, true, red);
+  float l = 0.f;
+  for (int s = tid; s < splits; s += kCombineRowThreads) {
+    const float m = s_w[s];
+    const float w = m == -INFINITY ? 0.f : exp2f(m - mx);
+    s_w[s] = w;
+    l = fmaf(w, base[(int64_t)s * split_stride + D + 1], l);
+  }
+  l = block_reduce(l, false, red);   // its barriers also publish s_w
+  const int c = tid % C2, g = tid / C2;
+  float2 acc = make_float2(0.f, 0.f);
+  const float* col = base + 2 * c;
+#pragma unroll 8
+  for (int s = g; s < splits; s += G) {
+    const float w = s_w[s];
+    const float2 v = *reinterpret_cast<const float2*>(col + (int64_t)s * split_stride);
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+  }
+  s_acc[g][c] = acc;
+  __syncthreads();
+  if (tid < C2) {
+    float2 sum = s_acc[0][tid];
+#pragma unroll
+    for (int k = 1; k < G; ++k) {
+      sum.x += s_acc[k][tid].x;
+      sum.y += s_acc[k][tid].y;
+    }
+    if (GATHER || out16) {
+      const float scale = (l > 0.f ? 1.f / l : 0.f) * sigmoid_gate(gate, row);
+      const uint32_t hv = pack_half2(sum.x * scale, sum.y * scale);
+      if (GATHER) {
+        const unsigned calls = gather_calls(go);
+        const int64_t off = (int64_t)(calls & 1u) * go.half_stride + ((int64_t)go.rank * rows + row) * D + 2 * tid;
+        for (int w = 0; w < go.world; ++w) *reinterpret_cast<uint32_t*>(go.peers[w] + off) = hv;
+      } else {
+        *reinterpret_cast<uint32_t*>(out16 + (int64_t)row * D + 2 * tid) = hv;
+      }
+    } else {
+      float* dst = out32 + (int64_t)row * (D + 2);
+      dst[2 * tid] = sum.x;
+      dst[2 * tid + 1] = sum.y;
+      if (tid == 0) {
+        dst[D] = mx;
+        dst[D + 1] = l;
+      }
+    }
+  }
+  if (GATHER) {
+    __syncthreads();
+    gather_raise(go, row, row + 1, gather_calls(go));
+  }
+}
+
+// One block: waits (bounded) until every (rank, row) flag of this rank's current call has been
 // raised in the own region (acquire loads at system scope), copies the call's [world][rows][D] half to out (if
 // given), and advances the call counter that the next combine reads.
-__global__ __launch_bounds__(1024) void gather_wait_kernel(__half* region, int world, int64_t half_stride, int blocks,
+__global__ __launch_bounds__(1024) void gather_wait_kernel(__half* region, int world, int64_t half_stride, int rows,
                                                            __half* out) {
   pdl_wait();
   pdl_trigger();
   unsigned* flags = gather_flags(region, half_stride);
-  unsigned* counter = flags + world * kGatherBlocks;
+  unsigned* counter = flags + world * kGatherRows;
   const unsigned target = *reinterpret_cast<volatile unsigned*>(counter) + 1u;
   __shared__ int s_fail;
   if (threadIdx.x == 0) s_fail = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < world * blocks; i += blockDim.x) {
-    const unsigned* f = flags + (i / blocks) * kGatherBlocks + i % blocks;
+  for (int i = threadIdx.x; i < world * rows; i += blockDim.x) {
+    const unsigned* f = flags + (i / rows) * kGatherRows + i % rows;
     const uint64_t t0 = globaltimer();
     for (;;) {
       unsigned v;
