@@ -185,6 +185,36 @@ int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, in
                        const void* k_norm, const void* q, int m, int q_heads, int ctx_len, int window, const void* gate,
                        void* out, void* workspace, size_t workspace_bytes, int splits, void* stream);
 
+/* ---------------------------------------------------------------- the reference's arithmetic (MODE_I8REC)
+ * Attention over the reference's own cache bytes with its own arithmetic: int8 queries per 32-dim group against
+ * the int8 K of the 264-byte records, fp16 probabilities carrying the V scale times 4096 against the int8 V. */
+
+/* The query quantiser (kernels/prefill_attn.hip:120-135 quantize_q; the query part of kernels/dspark.hip:1042-1049
+ * query_fresh): per (token, head) row of q (token t at q + t * q_stride halves, head h at + h * head_dim;
+ * q_stride 0 means q_heads * head_dim) and 32-dim group, scale = max(amax / 127, 1e-20) and
+ * q = rint(x * (1 / scale)), ties to even. qbuf: device [tokens * q_heads][head_dim / 4 + head_dim / 32]
+ * dwords, the int8 dims packed four to a dword (dims 4i..4i+3 in dword i, byte order), then the group scales
+ * as f32 (the reference's QROW layout, prefill_attn.hip:32). head_dim 64 or 128. */
+int lfm3a_quantize_q(const void* q, int64_t q_stride, int tokens, int q_heads, int head_dim, uint32_t* qbuf,
+                     void* stream);
+
+/* The split count lfm3a_verify_attention_i8 uses when called with splits <= 0: one CTA per SM, at most one
+ * 32-token page each. */
+int lfm3a_verify_i8_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int window, int sm_count);
+
+/* DSpark verify attention over MODE_I8REC records (kernels/dspark.hip:1824-2121 attention_v3 and the combine,
+ * :2134-2185): per key s = (sum over 32-dim groups of the exact int32 dot times the query's group scale) times
+ * the key's scale and (1/sqrt(head_dim)) log2(e); exact running max per 32-key page; p = 2^(s - max); the
+ * probability P = fp16(p * v_scale * 4096) times the record's int8 V in fp32; partials / 4096, log-sum-exp
+ * merge, optional sigmoid gate. qbuf: the m tokens' rows of lfm3a_quantize_q; the drafts' records already
+ * appended at ctx_len .. ctx_len + m - 1 (lfm3a_kv_append on the MODE_I8REC view); masks as
+ * lfm3a_verify_attention. out: device fp16 [m][q_heads][head_dim]. workspace: lfm3a_verify_workspace_bytes(m,
+ * q_heads, head_dim, splits) bytes (needed for every split count). q_heads = 4 * kv_heads, head_dim 64 or 128,
+ * kv_heads * ceil(m / 4) <= 16 (the reference's 4 kv heads: up to 16 tokens; it verifies at most 9). */
+int lfm3a_verify_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int m, int q_heads, int ctx_len,
+                              int window, const void* gate, void* out, void* workspace, size_t workspace_bytes,
+                              int splits, void* stream);
+
 /* ---------------------------------------------------------------- drafter ring attention
  * The drafter's KV ring (kernels/dspark.hip:69-70,1070-1412 attention_pass<1, true>, called at :2527):
  * the drafter keeps its context K/V in a ring of pages, logical block b in ring block b mod ring_blocks,

@@ -1,0 +1,320 @@
+// The reference's own attention arithmetic over its own cache bytes (MODE_I8REC: 264-byte int8 records per token
+// and kv head at head_dim 128): the query quantiser of kernels/prefill_attn.hip:120-135 and the DSpark verify
+// attention of kernels/dspark.hip:1824-2121 (attention_v3), whose partials the combine kernel merges
+// (dspark.hip:2134-2185).
+//
+// verify_i8rec_kernel: grid = key splits (32-token pages in contiguous runs), one CTA per SM. A CTA streams its
+// pages whole (all kv heads of a page are one contiguous block of kv_heads x 32 records) through a ring of
+// shared-memory stages filled by 1-D bulk copies; thread 0 refills a stage once every warp has released it.
+// Warp (kv head h, m-tile mt) owns the 16 query rows r = 16 mt .. 16 mt + 15 (r = 4 t + j: token t, query head
+// 4 h + j) and runs the reference's arithmetic on the legacy warp-level tensor-core instructions:
+//   QK  per 32-dim group one mma.m16n8k32 s8 x s8 -> s32 (the group's exact int32 dot, as the reference's
+//       v_dot4 chain), then s = (fma(d1, qs1, d0 qs0) + fma(d3, qs3, d2 qs2)) x ks (:1914-1961 reduction order);
+//   softmax: exact running max per 32-key page (:2023-2040), p = 2^(s - m), l += p, P = fp16(p (vs 4096));
+//   PV  mma.m16n8k16 fp16 x fp16 -> fp32 with V's int8 made fp16 exactly in registers (the fp16 bits 0x64NN with
+//       NN = v + 128 are 1152 + v; one subtraction);
+//   partial acc / 4096, max, sum per (row, split) (:2100-2120).
+// Within a 32-dim group the order of the dims is free (the dot is exact), so each thread reads 8 contiguous dims
+// of a key; the output dims are permuted the same way for V (thread column c of n-tile j holds dim (D / 8) c + j)
+// and put back in order when the partial is written.
+#pragma once
+#include "common.cuh"
+#include "kv.cuh"
+
+namespace lfm3a {
+
+// ---------------------------------------------------------------- query quantiser
+// One warp per (token, head) row; lane l holds dims [l D / 32, (l + 1) D / 32). Group of 32 dims: 8 lanes at
+// head_dim 128, 16 at 64. qbuf row: D / 4 dwords of int8 (dims 4i..4i+3 in dword i) then D / 32 f32 scales.
+template <int D>
+__global__ __launch_bounds__(128) void quantize_q_kernel(const __half* q, int64_t q_stride, int tokens, int q_heads,
+                                                         uint32_t* qbuf) {
+  constexpr int E = D / 32, LG = 32 / E, QROW = D / 4 + D / 32;   // dims per lane, lanes per group
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= tokens * q_heads) return;
+  const int t = row / q_heads, h = row % q_heads;
+  const __half* src = q + (int64_t)t * q_stride + (int64_t)h * D + lane * E;
+  float x[E];
+  float amax = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    x[e] = __half2float(src[e]);
+    amax = fmaxf(amax, fabsf(x[e]));
+  }
+#pragma unroll
+  for (int o = 1; o < LG; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = fmaxf(__fdiv_rn(amax, 127.f), 1e-20f), inv = __fdiv_rn(1.f, scale);
+  uint32_t w = 0;
+#pragma unroll
+  for (int e = 0; e < E; ++e) w |= (uint32_t)(__float2int_rn(__fmul_rn(x[e], inv)) & 0xff) << (8 * e);
+  uint32_t* dst = qbuf + (int64_t)row * QROW;
+  if (E == 4) {
+    dst[lane] = w;
+  } else {   // two dims per lane: neighbouring lanes make a dword
+    const uint32_t other = __shfl_xor_sync(0xffffffffu, w, 1);
+    if ((lane & 1) == 0) dst[lane >> 1] = w | (other << 16);
+  }
+  if (lane % LG == 0) reinterpret_cast<float*>(dst)[D / 4 + lane / LG] = scale;
+}
+
+// ---------------------------------------------------------------- verify attention over int8 records
+struct VerifyI8Args {
+  KvGeom g;
+  const uint32_t* qbuf;   // [m * q_heads][D / 4 + D / 32] (quantize_q rows)
+  float* part;            // [m * q_heads][splits][D + 2]
+  int m, q_heads, ctx_len, window, start, splits;
+  int p_begin, p_total;   // 32-key pages of [start, ctx_len + m)
+  int mtiles;             // m-tiles of 16 rows per kv head: ceil(4 m / 16)
+  int stages;             // ring stages (each one block of the pool: kv_heads x 32 records)
+  float qk_scale;         // (1 / sqrt(D)) log2(e)
+};
+
+constexpr int kI8MaxWarps = 16;   // kv heads x m-tiles per CTA (512 threads)
+constexpr float kPScale = 4096.f;   // dspark.hip PSCALE: P carries the V scale times 4096
+
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Bytes `sel` of two words of int8 V (keys k and k + 1 at one dim) as an exact fp16 pair: 0x64NN is 1024 + NN,
+// NN = v + 128 = v ^ 0x80 as a byte, so the pair minus 1152 is (v_k, v_k+1).
+__device__ __forceinline__ uint32_t s8pair_to_f16x2(uint32_t wk, uint32_t wk1, int byte) {
+  const uint32_t x = __byte_perm(wk, wk1, (uint32_t)byte | ((uint32_t)(byte + 4) << 16));
+  const uint32_t y = (x & 0x00ff00ffu) ^ 0x64806480u;
+  __half2 h = *reinterpret_cast<const __half2*>(&y);
+  h = __hsub2(h, __floats2half2_rn(1152.f, 1152.f));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D>
+__global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
+  constexpr int REC = 2 * D + 8, NG = D / 32, NJ = D / 8;   // record bytes, 32-dim groups, output n-tiles
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int H = a.g.kv_heads, NS = a.stages;
+  const int page_bytes = H * kBlockTokens * REC;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * page_bytes);
+  uint64_t* empty = full + NS;
+  int* s_abort = reinterpret_cast<int*>(empty + NS);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int nwarps = H * a.mtiles;
+  const int h = warp / a.mtiles, mt = warp % a.mtiles;
+  const int split = blockIdx.x;
+  const int pg0 = a.p_begin + (int)((int64_t)a.p_total * split / a.splits);
+  const int npg = a.p_begin + (int)((int64_t)a.p_total * (split + 1) / a.splits) - pg0;
+
+  if (threadIdx.x == 0) {
+    *s_abort = 0;
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], nwarps);
+    }
+    fence_barrier_init();
+  }
+  pdl_wait();
+  __syncthreads();
+  auto issue = [&](int j) {   // page j of this split into stage j % NS
+    const int st = j % NS;
+    const char* src = a.g.pool + phys_block(a.g, pg0 + j) * a.g.block_bytes;
+    mbar_arrive_expect_tx(&full[st], (uint32_t)page_bytes);
+    bulk_g2s(smem + (size_t)st * page_bytes, src, (uint32_t)page_bytes, &full[st]);
+  };
+  int issued = 0;   // pages whose copies thread 0 has started
+  if (threadIdx.x == 0)
+    for (; issued < min(NS, npg); ++issued) issue(issued);
+
+  // The query rows of this warp: r0 = 16 mt + gid and r0 + 8; A fragments per group (dims 8 tig .. 8 tig + 7).
+  const int rA = 16 * mt + gid, rB = rA + 8;
+  const bool okA = rA < 4 * a.m, okB = rB < 4 * a.m;
+  const int rowA = (rA >> 2) * a.q_heads + 4 * h + (rA & 3), rowB = (rB >> 2) * a.q_heads + 4 * h + (rB & 3);
+  constexpr int QROW = D / 4 + D / 32;
+  uint32_t qa[NG][4];
+  float qsA[NG], qsB[NG];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const uint32_t* pa = a.qbuf + (int64_t)(okA ? rowA : 0) * QROW;
+    const uint32_t* pb = a.qbuf + (int64_t)(okB ? rowB : 0) * QROW;
+    qa[g][0] = okA ? pa[8 * g + 2 * tig] : 0u;
+    qa[g][1] = okB ? pb[8 * g + 2 * tig] : 0u;
+    qa[g][2] = okA ? pa[8 * g + 2 * tig + 1] : 0u;
+    qa[g][3] = okB ? pb[8 * g + 2 * tig + 1] : 0u;
+    qsA[g] = okA ? __uint_as_float(pa[D / 4 + g]) * a.qk_scale : 0.f;
+    qsB[g] = okB ? __uint_as_float(pb[D / 4 + g]) * a.qk_scale : 0.f;
+  }
+  const int tA = rA >> 2, tB = rB >> 2;
+  const int qposA = a.ctx_len + tA, qposB = a.ctx_len + tB;
+  const int qlast = a.ctx_len + a.m - 1, kv_end = a.ctx_len + a.m;
+
+  float acc[NJ][4];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  float mA = -1e30f, mB = -1e30f, lA = 0.f, lB = 0.f;
+  bool ok = true;
+
+  for (int j = 0; j < npg && ok; ++j) {
+    const int st = j % NS;
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (uint32_t)(j / NS) & 1u))) {
+      raise_error(kErrWaitFull);
+      ok = false;
+      break;
+    }
+    const uint8_t* page = smem + (size_t)st * page_bytes;
+    const int pg = pg0 + j, k0 = pg * kBlockTokens;
+    // ---- QK: 4 n-tiles of 8 keys; per group one s8 MMA
+    float s[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const uint8_t* krec = page + ((8 * n + gid) * H + h) * REC;   // key 8 n + gid of this kv head
+      int dg[NG][4];
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const uint2 kb = *reinterpret_cast<const uint2*>(krec + 32 * g + 8 * tig);
+        dg[g][0] = dg[g][1] = dg[g][2] = dg[g][3] = 0;
+        mma_s8_16832(dg[g], qa[g], kb.x, kb.y);
+      }
+      // the C fragment: (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1) of the n-tile
+      const float ksc0 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig) * H + h) * REC + D);
+      const float ksc1 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig + 1) * H + h) * REC + D);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float* qs = e < 2 ? qsA : qsB;
+        float v = fmaf((float)dg[1][e], qs[1], (float)dg[0][e] * qs[0]);
+        if (NG == 4) v = v + fmaf((float)dg[3][e], qs[3], (float)dg[2][e] * qs[2]);
+        s[n][e] = v * ((e & 1) ? ksc1 : ksc0);
+      }
+    }
+    // ---- masks (edge pages only) and the page maximum of each row
+    const bool interior = k0 >= a.start && k0 + kBlockTokens <= a.ctx_len && (a.window == 0 || k0 > qlast - a.window);
+    if (!interior || !okB) {
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kpos = k0 + 8 * n + 2 * tig + (e & 1);
+          const int qpos = e < 2 ? qposA : qposB;
+          const bool rok = e < 2 ? okA : okB;
+          bool valid;
+          if (kpos < a.ctx_len) valid = kpos >= a.start && (a.window == 0 || kpos > qpos - a.window);
+          else valid = kpos <= qpos && kpos < kv_end;
+          s[n][e] = valid && rok ? s[n][e] : -INFINITY;
+        }
+    }
+    float pmA = -INFINITY, pmB = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      pmA = fmaxf(pmA, fmaxf(s[n][0], s[n][1]));
+      pmB = fmaxf(pmB, fmaxf(s[n][2], s[n][3]));
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      pmA = fmaxf(pmA, __shfl_xor_sync(0xffffffffu, pmA, o));
+      pmB = fmaxf(pmB, __shfl_xor_sync(0xffffffffu, pmB, o));
+    }
+    if (pmA > mA || pmB > mB) {   // exact running max: rescale what came before
+      const float nA = fmaxf(mA, pmA), nB = fmaxf(mB, pmB);
+      const float cA = fast_exp2(mA - nA), cB = fast_exp2(mB - nB);
+      mA = nA;
+      mB = nB;
+      lA *= cA;
+      lB *= cB;
+#pragma unroll
+      for (int jn = 0; jn < NJ; ++jn) {
+        acc[jn][0] *= cA;
+        acc[jn][1] *= cA;
+        acc[jn][2] *= cB;
+        acc[jn][3] *= cB;
+      }
+    }
+    // ---- P = fp16(p (vs 4096)) as the A fragments of two 16-key k-steps
+    uint32_t pf[2][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const float vs0 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig) * H + h) * REC + 2 * D + 4) * kPScale;
+      const float vs1 =
+          *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig + 1) * H + h) * REC + 2 * D + 4) * kPScale;
+      const float p0 = fast_exp2(s[n][0] - mA), p1 = fast_exp2(s[n][1] - mA);
+      const float p2 = fast_exp2(s[n][2] - mB), p3 = fast_exp2(s[n][3] - mB);
+      lA += p0 + p1;
+      lB += p2 + p3;
+      // n-tiles 2 kk and 2 kk + 1 are k-step kk: a0/a1 from the first, a2/a3 from the second
+      pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(p0 * vs0, p1 * vs1);
+      pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(p2 * vs0, p3 * vs1);
+    }
+    // ---- PV: per k-step, the V bytes of keys 16 kk + 2 tig (+1, +8, +9) at dims [NJ gid, NJ gid + NJ)
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const int kb = 16 * kk + 2 * tig;
+      const uint8_t* v0 = page + ((kb + 0) * H + h) * REC + D + 4 + NJ * gid;
+      const uint8_t* v1 = page + ((kb + 1) * H + h) * REC + D + 4 + NJ * gid;
+      const uint8_t* v8 = page + ((kb + 8) * H + h) * REC + D + 4 + NJ * gid;
+      const uint8_t* v9 = page + ((kb + 9) * H + h) * REC + D + 4 + NJ * gid;
+#pragma unroll
+      for (int w = 0; w < NJ / 4; ++w) {
+        const uint32_t w0 = reinterpret_cast<const uint32_t*>(v0)[w], w1 = reinterpret_cast<const uint32_t*>(v1)[w];
+        const uint32_t w8 = reinterpret_cast<const uint32_t*>(v8)[w], w9 = reinterpret_cast<const uint32_t*>(v9)[w];
+#pragma unroll
+        for (int by = 0; by < 4; ++by) {
+          const int jn = 4 * w + by;   // n-tile: its column gid holds dim NJ gid + jn
+          mma_f16_16816(acc[jn], pf[kk], s8pair_to_f16x2(w0, w1, by), s8pair_to_f16x2(w8, w9, by));
+        }
+      }
+    }
+    // ---- release the stage; thread 0 refills it once every warp has
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (threadIdx.x == 0 && j + NS < npg) {
+      if (!mbar_wait(&empty[st], (uint32_t)(j / NS) & 1u)) {
+        raise_error(kErrWaitEmpty);
+        atomicExch(s_abort, 1);
+      } else {
+        issue(j + NS);
+        ++issued;
+      }
+    }
+    if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(s_abort) != 0)) ok = false;
+  }
+  if (!ok) atomicExch(s_abort, 1);
+
+  // ---- partial rows: acc / 4096 with the dims put back in order, the row max and the quad's summed l
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    lA += __shfl_xor_sync(0xffffffffu, lA, o);
+    lB += __shfl_xor_sync(0xffffffffu, lB, o);
+  }
+  const bool aborted = *reinterpret_cast<volatile int*>(s_abort) != 0;
+  if (!aborted && warp < nwarps) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const bool rok = half ? okB : okA;
+      if (!rok) continue;
+      float* dst = a.part + ((int64_t)(half ? rowB : rowA) * a.splits + split) * (D + 2);
+#pragma unroll
+      for (int jn = 0; jn < NJ; ++jn) {
+        // C fragment columns 2 tig, 2 tig + 1 of n-tile jn: dims NJ (2 tig) + jn and NJ (2 tig + 1) + jn
+        dst[NJ * (2 * tig) + jn] = acc[jn][2 * half] * (1.f / kPScale);
+        dst[NJ * (2 * tig + 1) + jn] = acc[jn][2 * half + 1] * (1.f / kPScale);
+      }
+      if (tig == 0) {
+        dst[D] = half ? mB : mA;
+        dst[D + 1] = half ? lB : lA;
+      }
+    }
+  }
+  // On an abort, wait (bounded) for the copies that may still be landing (the last NS started) before the
+  // shared memory goes away; every earlier one was consumed.
+  __syncthreads();
+  if (threadIdx.x == 0 && aborted)
+    for (int j = max(0, issued - NS); j < issued; ++j) mbar_wait(&full[j % NS], (uint32_t)(j / NS) & 1u);
+}
+
+}  // namespace lfm3a

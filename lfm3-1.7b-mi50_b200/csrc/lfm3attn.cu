@@ -13,6 +13,7 @@
 #include "../../include/lfm3attn.h"
 #include "common.cuh"
 #include "gemm.cuh"
+#include "i8rec.cuh"
 #include "kv.cuh"
 #include "pcache.h"
 #include "prefill.cuh"
@@ -630,6 +631,88 @@ int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out
   launch_pdl(gather_wait_kernel, 1, 1024, 0, as_stream(stream), static_cast<__half*>(region), world, half_stride, rows,
              static_cast<__half*>(out));
   return check_launch("gather_wait_kernel");
+}
+
+int lfm3a_quantize_q(const void* q, int64_t q_stride, int tokens, int q_heads, int head_dim, uint32_t* qbuf,
+                     void* stream) {
+  if (!q || !qbuf || tokens < 0 || q_heads < 1) return fail(LFM3A_EINVAL, "bad quantize_q arguments");
+  if (head_dim != 64 && head_dim != 128) return fail(LFM3A_ENOTSUP, "quantize_q: head_dim 64 or 128");
+  if (q_stride == 0) q_stride = (int64_t)q_heads * head_dim;
+  if (q_stride < (int64_t)q_heads * head_dim || (q_stride & 1) || (reinterpret_cast<uintptr_t>(q) & 3))
+    return fail(LFM3A_EINVAL, "quantize_q: q 4-byte aligned, q_stride even and at least q_heads * head_dim");
+  if (tokens == 0) return LFM3A_OK;
+  const int rows = tokens * q_heads;
+  if (head_dim == 128)
+    launch_pdl(quantize_q_kernel<128>, (rows + 3) / 4, 128, 0, as_stream(stream), static_cast<const __half*>(q),
+               q_stride, tokens, q_heads, qbuf);
+  else
+    launch_pdl(quantize_q_kernel<64>, (rows + 3) / 4, 128, 0, as_stream(stream), static_cast<const __half*>(q),
+               q_stride, tokens, q_heads, qbuf);
+  return check_launch("quantize_q_kernel");
+}
+
+int lfm3a_verify_i8_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int window, int sm_count) {
+  if (!layout || ctx_len < 0 || m < 1) return fail(LFM3A_EINVAL, "bad verify split arguments");
+  const int start = window > 0 ? std::max(0, ctx_len - window + 1) : 0;
+  const int pages = (ctx_len + m - 1) / kBlockTokens - start / kBlockTokens + 1;
+  return std::max(1, std::min(sm_count > 0 ? sm_count : current_sm_count(), pages));
+}
+
+int lfm3a_verify_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int m, int q_heads, int ctx_len,
+                              int window, const void* gate, void* out, void* workspace, size_t workspace_bytes,
+                              int splits, void* stream) {
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  const lfm3a_kv_layout& L = kv->layout;
+  const int D = L.head_dim, H = L.kv_heads;
+  if (L.mode != LFM3A_MODE_I8REC) return fail(LFM3A_ENOTSUP, "verify_attention_i8 reads MODE_I8REC records");
+  if (q_heads != 4 * H) return fail(LFM3A_ENOTSUP, "verify attention needs 4 query heads per kv head");
+  if (!qbuf || !out || m < 1 || ctx_len < 0 || window < 0) return fail(LFM3A_EINVAL, "bad verify arguments");
+  if (window > 0 && window < m) return fail(LFM3A_EINVAL, "window shorter than the verified tokens");
+  const int mtiles = (4 * m + 15) / 16;
+  if (H * mtiles > kI8MaxWarps)
+    return fail(LFM3A_ENOTSUP, "verify_attention_i8: kv_heads * ceil(m / 4) must be at most 16");
+  const int page_bytes = (int)L.block_bytes;
+  const int stages = std::min(4, (int)((220 * 1024) / page_bytes));
+  if (stages < 2) return fail(LFM3A_ENOTSUP, "verify_attention_i8: a block of records too large for the ring");
+  if (!aligned16(out) || (reinterpret_cast<uintptr_t>(qbuf) & 7)) return fail(LFM3A_EINVAL, "misaligned out or qbuf");
+  VerifyI8Args a;
+  a.g = geom_of(kv);
+  a.qbuf = qbuf;
+  a.m = m;
+  a.q_heads = q_heads;
+  a.ctx_len = ctx_len;
+  a.window = window;
+  a.start = window > 0 ? std::max(0, ctx_len - window + 1) : 0;
+  a.p_begin = a.start / kBlockTokens;
+  a.p_total = (ctx_len + m - 1) / kBlockTokens - a.p_begin + 1;
+  if (splits <= 0) splits = lfm3a_verify_i8_splits(&L, ctx_len, m, window, 0);
+  a.splits = std::max(1, std::min(splits, a.p_total));
+  a.mtiles = mtiles;
+  a.stages = stages;
+  a.qk_scale = (1.f / sqrtf((float)D)) * kLog2e;
+  if (!workspace || !aligned16(workspace)) return fail(LFM3A_EINVAL, "verify_attention_i8 needs a workspace");
+  if (workspace_bytes < lfm3a_verify_workspace_bytes(m, q_heads, D, a.splits))
+    return fail(LFM3A_EWORKSPACE, "verify workspace too small");
+  a.part = static_cast<float*>(workspace);
+  const size_t smem = (size_t)stages * page_bytes + 256;
+  static std::atomic<bool> done[2][64];
+  const cudaStream_t st = as_stream(stream);
+  // The limit is set once, to the most any geometry's ring asks for (220 KiB and the barriers).
+  constexpr int kRingLimit = 220 * 1024 + 256;
+  if (D == 128) {
+    rc = ensure_smem(verify_i8rec_kernel<128>, kRingLimit, done[1]);
+    if (rc != LFM3A_OK) return rc;
+    launch_pdl(verify_i8rec_kernel<128>, a.splits, 32 * H * mtiles, smem, st, a);
+  } else {
+    rc = ensure_smem(verify_i8rec_kernel<64>, kRingLimit, done[0]);
+    if (rc != LFM3A_OK) return rc;
+    launch_pdl(verify_i8rec_kernel<64>, a.splits, 32 * H * mtiles, smem, st, a);
+  }
+  rc = check_launch("verify_i8rec_kernel");
+  if (rc != LFM3A_OK) return rc;
+  return launch_combine(a.part, m * q_heads, a.splits, D, D + 2, (int64_t)a.splits * (D + 2),
+                        static_cast<const __half*>(gate), static_cast<__half*>(out), nullptr, st);
 }
 
 int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* stream) {

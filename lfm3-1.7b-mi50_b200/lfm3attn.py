@@ -88,6 +88,9 @@ SIGNATURES = {
     "lfm3a_prefill_attention_fused": (_I, [ctypes.POINTER(KvView), _P, _I64, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _P,
                                            _P, _SZ, _P]),
     "lfm3a_quantize_p_u8": (_I, [_P, _I, _P, _P, _P]),
+    "lfm3a_quantize_q": (_I, [_P, _I64, _I, _I, _I, _P, _P]),
+    "lfm3a_verify_i8_splits": (_I, [ctypes.POINTER(KvLayout), _I, _I, _I, _I]),
+    "lfm3a_verify_attention_i8": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _P, _SZ, _I, _P]),
     "lfm3a_g128_packed_bytes": (_I64, [_I, _I]),
     "lfm3a_g128_scale_bytes": (_I64, [_I, _I]),
     "lfm3a_g128_pack": (_I, [_P, _I64, _P, _I64, _I, _I, _P, _P, _P]),
@@ -273,6 +276,28 @@ class LayerCache:
                                         m, qh, ctx_len, window, _ptr(gate), _ptr(out), _ptr(workspace), ws_bytes,
                                         splits, _stream(stream)))
         self.length = max(self.length, ctx_len + m)
+        return out
+
+    def verify_i8(self, qbuf, m: int, q_heads: int, ctx_len: int, window: int = 0, gate=None, out=None,
+                  workspace=None, splits: int = 0, stream=None):
+        """Verify attention over this MODE_I8REC cache with the reference's arithmetic (dspark.hip:1824-2185):
+        qbuf = quantize_q(q) of the m tokens; returns fp16 [m][q_heads][head_dim]."""
+        import torch
+
+        d = self.head_dim
+        if out is None:
+            out = torch.empty((m, q_heads, d), dtype=torch.float16, device=qbuf.device)
+        if splits <= 0:
+            splits = lib().lfm3a_verify_i8_splits(ctypes.byref(self.layout), ctx_len, m, window, 0)
+            if splits < 0:
+                _check(splits)
+        if workspace is None:
+            workspace = torch.empty(lib().lfm3a_verify_workspace_bytes(m, q_heads, d, splits), dtype=torch.uint8,
+                                    device=qbuf.device)
+        ws_bytes = workspace.numel() * workspace.element_size()
+        _check(lib().lfm3a_verify_attention_i8(ctypes.byref(self.view), _ptr(qbuf), m, q_heads, ctx_len, window,
+                                               _ptr(gate), _ptr(out), _ptr(workspace), ws_bytes, splits,
+                                               _stream(stream)))
         return out
 
     def ring_attention(self, q, ctx_lo: int, ctx_len: int, out=None, workspace=None, splits: int = 0, stream=None):
@@ -499,6 +524,19 @@ def combine(partials, rows: int, splits: int, head_dim: int, split_stride: int =
 def accept(best, tokens, state, stream=None) -> None:
     m = tokens.numel()
     _check(lib().lfm3a_accept(_ptr(best), _ptr(tokens), m, _ptr(state), _stream(stream)))
+
+
+def quantize_q(q, q_heads: int | None = None, head_dim: int | None = None, stream=None):
+    """The reference's query quantiser (prefill_attn.hip:120-135): q fp16 [T][q_heads][head_dim] (or row-strided
+    [T][>= q_heads * head_dim] with q_heads, head_dim given) -> qbuf int32 [T * q_heads][head_dim/4 + head_dim/32]."""
+    import torch
+
+    t = q.shape[0]
+    if q_heads is None:
+        q_heads, head_dim = q.shape[1], q.shape[2]
+    qbuf = torch.empty((t * q_heads, head_dim // 4 + head_dim // 32), dtype=torch.int32, device=q.device)
+    _check(lib().lfm3a_quantize_q(_ptr(q), q.stride(0), t, q_heads, head_dim, _ptr(qbuf), _stream(stream)))
+    return qbuf
 
 
 def quantize_p_u8(p, stream=None):

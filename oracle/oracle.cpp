@@ -330,6 +330,113 @@ void orc_verify(const uint16_t* q, int m, int q_heads, int kv_heads, int head_di
   }
 }
 
+// The reference's query quantiser (kernels/prefill_attn.hip:120-135 quantize_q): per row and 32-dim group,
+// scale = max(amax / 127, 1e-20) and q = rint(x * (1 / scale)) (ties to even), packed four dims to a dword
+// (dims 4i..4i+3 in dword i, byte order), then the D / 32 scales as f32: QROW = D / 4 + D / 32 dwords.
+void orc_quantize_q(const uint16_t* q, int64_t q_stride, int tokens, int q_heads, int head_dim, uint32_t* qbuf) {
+  const int D = head_dim, qrow = D / 4 + D / 32;
+#pragma omp parallel for schedule(static)
+  for (int row = 0; row < tokens * q_heads; ++row) {
+    const int t = row / q_heads, h = row % q_heads;
+    const uint16_t* src = q + (int64_t)t * q_stride + (int64_t)h * D;
+    uint32_t* dst = qbuf + (size_t)row * qrow;
+    for (int g = 0; g < D / 32; ++g) {
+      float amax = 0.f;
+      for (int d = 32 * g; d < 32 * g + 32; ++d) amax = fmaxf(amax, fabsf(orc_f16_to_f32(src[d])));
+      const float scale = fmaxf(amax / 127.f, 1e-20f), inv = 1.f / scale;
+      for (int d = 32 * g; d < 32 * g + 32; d += 4) {
+        uint32_t w = 0;
+        for (int e = 0; e < 4; ++e) {
+          const int qi = (int)rintf(orc_f16_to_f32(src[d + e]) * inv);
+          w |= (uint32_t)(qi & 0xff) << (8 * e);
+        }
+        dst[d / 4] = w;
+      }
+      memcpy(dst + D / 4 + g, &scale, 4);
+    }
+  }
+}
+
+// Verify attention over the reference's int8 records (kernels/dspark.hip:1824-2121 attention_v3 with the
+// page partition, combined by :2134-2185): per key s = (fma(dot_1, qs_1, dot_0 qs_0) + fma(dot_3, qs_3,
+// dot_2 qs_2)) * ks with the int32 dot of each 32-dim group, qs the query's group scale times (1 / sqrt(D))
+// log2(e) (:1914-1945, the DPP reduction order of :1960-1961); exact running max per 32-key page (:2023-2040);
+// p = 2^(s - m), l += p, P = fp16(p * (vs * 4096)), acc += P * V8 in fp32, partial acc / 4096 (:2067-2116).
+void orc_verify_i8rec(const uint32_t* qbuf, int m, int q_heads, int kv_heads, int head_dim, const uint8_t* rec,
+                      int ctx_len, int window, const uint16_t* gate, int splits, float* out) {
+  const int D = head_dim, G = q_heads / kv_heads, R = 2 * D + 8, NG = D / 32, qrow = D / 4 + D / 32;
+  const int start = kv_start(ctx_len, window), kv_end = ctx_len + m;
+  const int p_begin = start / BS, p_total = (kv_end - 1) / BS - p_begin + 1;
+  const int S = std::max(1, std::min(splits, p_total));
+  const float qk_scale = (1.f / sqrtf((float)D)) * LOG2E;
+  constexpr float kPScale = 4096.f;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int row = 0; row < m * q_heads; ++row) {
+    const int t = row / q_heads, qh = row % q_heads, h = qh / G, qpos = ctx_len + t;
+    const int8_t* q8 = reinterpret_cast<const int8_t*>(qbuf + (size_t)row * qrow);
+    float qs[4];
+    for (int g = 0; g < NG; ++g) {
+      float sc;
+      memcpy(&sc, qbuf + (size_t)row * qrow + D / 4 + g, 4);
+      qs[g] = sc * qk_scale;
+    }
+    std::vector<float> pacc((size_t)S * D, 0.f), pm(S, -1e30f), pl(S, 0.f);
+    for (int s = 0; s < S; ++s) {
+      const int g0 = p_begin + (int)((int64_t)p_total * s / S), g1 = p_begin + (int)((int64_t)p_total * (s + 1) / S);
+      float* acc = &pacc[(size_t)s * D];
+      float m_run = -1e30f, l_run = 0.f;
+      for (int pg = g0; pg < g1; ++pg) {
+        float sc[BS];
+        float mx = -INFINITY;
+        for (int kk = 0; kk < BS; ++kk) {
+          const int kpos = pg * BS + kk;
+          bool valid;
+          if (kpos < ctx_len) valid = kpos >= start && (window == 0 || kpos > qpos - window);
+          else valid = kpos <= qpos;
+          valid = valid && kpos < kv_end;
+          if (!valid) {
+            sc[kk] = -INFINITY;
+            continue;
+          }
+          const uint8_t* r = rec + ((size_t)kpos * kv_heads + h) * R;
+          const int8_t* k8 = reinterpret_cast<const int8_t*>(r);
+          float ks;
+          memcpy(&ks, r + D, 4);
+          int dot[4] = {0, 0, 0, 0};
+          for (int g = 0; g < NG; ++g)
+            for (int d = 32 * g; d < 32 * g + 32; ++d) dot[g] += (int)q8[d] * (int)k8[d];
+          float v = fmaf((float)dot[1], qs[1], (float)dot[0] * qs[0]);
+          if (NG == 4) v = v + fmaf((float)dot[3], qs[3], (float)dot[2] * qs[2]);
+          sc[kk] = v * ks;
+          mx = fmaxf(mx, sc[kk]);
+        }
+        if (mx > m_run) {
+          const float corr = exp2f(m_run - mx);
+          m_run = mx;
+          l_run *= corr;
+          for (int d = 0; d < D; ++d) acc[d] *= corr;
+        }
+        for (int kk = 0; kk < BS; ++kk) {
+          if (sc[kk] == -INFINITY) continue;
+          const int kpos = pg * BS + kk;
+          const uint8_t* r = rec + ((size_t)kpos * kv_heads + h) * R;
+          const int8_t* v8 = reinterpret_cast<const int8_t*>(r + D + 4);
+          float vs;
+          memcpy(&vs, r + 2 * D + 4, 4);
+          const float p = exp2f(sc[kk] - m_run);
+          l_run += p;
+          const float p16 = r16(p * (vs * kPScale));
+          for (int d = 0; d < D; ++d) acc[d] += p16 * (float)v8[d];
+        }
+      }
+      for (int d = 0; d < D; ++d) acc[d] *= 1.f / kPScale;
+      pm[s] = m_run;
+      pl[s] = l_run;
+    }
+    merge_row(pacc.data(), pm.data(), pl.data(), S, D, gate, row, out + (size_t)row * D);
+  }
+}
+
 // The verify partial of one cache shard (keys [kv_begin, kv_end) of the sequence, K/V indexed by global
 // position): per row [acc[D] (unnormalised, at the shard's max), max, sum], as lfm3a_verify_partial leaves
 // it for the cross-GPU merge.

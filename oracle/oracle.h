@@ -55,6 +55,20 @@ void orc_quantize_v8(const uint16_t* v, int len, int kv_heads, int head_dim, int
  * q = rne_sat_u8(p * (255 / max(pm, 1e-30))), sc = pm * (1/255). p: [rows][cols]. */
 void orc_quantize_p_u8(const float* p, int rows, int cols, uint8_t* q, float* sc);
 
+/* The reference's query quantiser (kernels/prefill_attn.hip:120-135): per (token, head) row of q (token t at
+ * q + t * q_stride, head h at + h * head_dim) and 32-dim group, scale = max(amax/127, 1e-20), q = rint(x / scale)
+ * (as x * (1/scale), ties to even). qbuf: [tokens * q_heads][head_dim/4 + head_dim/32] dwords, int8 dims packed
+ * four to a dword, then the group scales as f32. */
+void orc_quantize_q(const uint16_t* q, int64_t q_stride, int tokens, int q_heads, int head_dim, uint32_t* qbuf);
+
+/* Verify attention over the reference's int8 records, the reference's own arithmetic (kernels/dspark.hip:
+ * 1824-2121, 2134-2185): int8 Q (orc_quantize_q rows of the m tokens) x int8 K per 32-dim group, exact int32,
+ * scaled per group and by the key scale; exact running max per 32-key page; P = fp16(p * vs * 4096) times the
+ * int8 V in fp32, partials / 4096, log-sum-exp merge with the optional gate. rec: [ctx_len + m][kv_heads]
+ * records of 2*head_dim+8 bytes (the drafts appended). out: [m][q_heads][head_dim] f32. */
+void orc_verify_i8rec(const uint32_t* qbuf, int m, int q_heads, int kv_heads, int head_dim, const uint8_t* rec,
+                      int ctx_len, int window, const uint16_t* gate, int splits, float* out);
+
 /* Verify attention over the cache (drafts already appended at ctx_len..ctx_len+m-1), restating the
  * split-KV page partition, exact running max, fp16 P and the log-sum-exp combine with the optional
  * sigmoid gate (dspark.hip:975-979,1809-2121,2134-2185). q: [m][q_heads][head_dim] fp16, gate: [m][q_heads]

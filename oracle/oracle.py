@@ -28,6 +28,8 @@ _SIGS = {
     "orc_quantize_v8": (None, [_P, _I, _I, _I, _P, _P]),
     "orc_quantize_p_u8": (None, [_P, _I, _I, _P, _P]),
     "orc_verify": (None, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _P]),
+    "orc_quantize_q": (None, [_P, ctypes.c_int64, _I, _I, _I, _P]),
+    "orc_verify_i8rec": (None, [_P, _I, _I, _I, _I, _P, _I, _I, _P, _I, _P]),
     "orc_verify_partial": (None, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _I, _I, _P]),
     "orc_combine": (None, [_P, _I, _I, _I, _P, _P]),
     "orc_attention_f64": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
@@ -138,6 +140,54 @@ def verify(q, K, V, ctx_len: int, window: int = 0, gate=None, splits: int = 1) -
     out = np.empty((m, qh, d), dtype=np.float32)
     lib().orc_verify(qp, m, qh, kvh, d, kp, vp, ctx_len, window, gp, splits, out.ctypes.data)
     return out
+
+
+def quantize_q(q, q_heads: int | None = None, head_dim: int | None = None) -> np.ndarray:
+    """prefill_attn.hip:120-135: q fp16 [T][q_heads][head_dim] (or [T][>= q_heads * head_dim] rows with
+    q_heads, head_dim given) -> qbuf uint32 [T * q_heads][head_dim / 4 + head_dim / 32]."""
+    q = np.ascontiguousarray(q, dtype=np.float16)
+    t = q.shape[0]
+    if q_heads is None:
+        q_heads, head_dim = q.shape[1], q.shape[2]
+    stride = int(np.prod(q.shape[1:]))
+    out = np.empty((t * q_heads, head_dim // 4 + head_dim // 32), dtype=np.uint32)
+    lib().orc_quantize_q(q.ctypes.data, stride, t, q_heads, head_dim, out.ctypes.data)
+    return out
+
+
+def dequantize_q(qbuf, head_dim: int) -> np.ndarray:
+    """The float values a qbuf row stands for: int8 dims times their group scale, [rows][head_dim] float64."""
+    qbuf = np.ascontiguousarray(qbuf, dtype=np.uint32)
+    q8 = qbuf[:, :head_dim // 4].view(np.int8).reshape(qbuf.shape[0], head_dim).astype(np.float64)
+    sc = qbuf[:, head_dim // 4:].view(np.float32).astype(np.float64)
+    return q8 * np.repeat(sc, 32, axis=1)
+
+
+def verify_i8rec(qbuf, m: int, q_heads: int, rec, ctx_len: int, window: int = 0, gate=None,
+                 splits: int = 1) -> np.ndarray:
+    """dspark.hip:1824-2185 over int8 records rec [ctx_len + m][kv_heads][2 * head_dim + 8] uint8 with the query
+    rows qbuf (quantize_q of the m tokens) -> out [m][q_heads][head_dim] float32."""
+    rec = np.ascontiguousarray(rec, dtype=np.uint8)
+    kvh, rb = rec.shape[1], rec.shape[2]
+    d = (rb - 8) // 2
+    qbuf = np.ascontiguousarray(qbuf, dtype=np.uint32)
+    gate, gp = _c(gate, np.float16)
+    out = np.empty((m, q_heads, d), dtype=np.float32)
+    lib().orc_verify_i8rec(qbuf.ctypes.data, m, q_heads, kvh, d, rec.ctypes.data, ctx_len, window, gp, splits,
+                           out.ctypes.data)
+    return out
+
+
+def dequantize_rec(rec) -> tuple[np.ndarray, np.ndarray]:
+    """K and V float64 [tokens][kv_heads][head_dim] that int8 records stand for (int8 times its scale)."""
+    rec = np.ascontiguousarray(rec, dtype=np.uint8)
+    t, h, rb = rec.shape
+    d = (rb - 8) // 2
+    k8 = rec[..., :d].view(np.int8).astype(np.float64)
+    ks = rec[..., d:d + 4].copy().view(np.float32).astype(np.float64)
+    v8 = rec[..., d + 4:2 * d + 4].view(np.int8).astype(np.float64)
+    vs = rec[..., 2 * d + 4:].copy().view(np.float32).astype(np.float64)
+    return k8 * ks, v8 * vs
 
 
 def verify_partial(q, K, V, kv_begin: int, kv_end: int, ctx_len: int, window: int = 0) -> np.ndarray:

@@ -8,6 +8,7 @@ to a second, separately written restatement of the same source lines:
   int8 records     kernels/ops.hip:213-251 (quantize_pair, kv_write), 264-byte records at head_dim 128
   int8 V blocks    the same quantiser per (kv head, 64-token block)
   u8 P             kernels/prefill_attn.hip:305-331 (IEEE division in place of v_rcp_f32)
+  int8 Q           kernels/prefill_attn.hip:120-135 (quantize_q: per 32-dim group, rint to nearest even)
   accept           kernels/dspark.hip:2851-2860
   W8A8 GEMM        kernels/gemm.hip:65-103 (quantize_pack, plain and gated) and :181-255 (gemm); every fp32
                    fma (the GEMM's group fold, the gate's exponential) emulated exactly with rationals
@@ -125,6 +126,21 @@ def p_u8(p):
     x = (p * inv[:, None]).astype(f32)
     q = np.clip(np.rint(x), 0, 255).astype(np.uint8)
     return q, (pm * f32(1.0 / 255.0)).astype(f32)
+
+
+def quantize_q(q):
+    """q: [rows][d] float16 -> dwords [rows][d/4 + d/32]: the int8 dims packed in byte order, then the scales."""
+    rows, d = q.shape
+    x = q.astype(f32).reshape(rows, d // 32, 32)
+    amax = np.abs(x).max(axis=2)
+    scale = np.maximum(amax / f32(127.0), f32(1e-20)).astype(f32)
+    inv = (f32(1.0) / scale).astype(f32)
+    qi = np.rint((x * inv[:, :, None]).astype(f32)).astype(np.int64).reshape(rows, d)
+    by = (qi & 0xFF).astype(np.uint8)
+    out = np.zeros((rows, d // 4 + d // 32), dtype=np.uint32)
+    out[:, :d // 4] = by.view(np.uint32).reshape(rows, d // 4)
+    out[:, d // 4:] = scale.view(np.uint32)
+    return out
 
 
 def accept(best, tokens):
@@ -261,6 +277,19 @@ def main():
     p[6] = f32(2.0) ** -40 * (np.arange(64, dtype=f32) + 1)
     g["p_in"] = p
     g["p_q"], g["p_sc"] = p_u8(p)
+
+    # int8 Q rows (reference geometry, head_dim 128): random, an all-zero row, tiny values, a large value,
+    # and values that land on .5 after scaling (ties to even).
+    s = synth.Stream(105)
+    q8 = s.normal_f16((12, 128))
+    q8[1] = 0
+    q8[2] = (q8[2].astype(f32) * f32(3e-5)).astype(np.float16)
+    q8[3, 5] = np.float16(60000.0)
+    q8[4, :32] = np.float16(0.5)
+    q8[4, 0] = np.float16(127.0)
+    q8[4, 1] = np.float16(2.5)
+    g["q8_in"] = q8
+    g["q8_out"] = quantize_q(q8)
 
     # accept
     best = np.array([5, 6, 7, 9, 1, 2, 3, 4], dtype=np.int32)

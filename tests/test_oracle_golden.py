@@ -120,3 +120,11 @@ def test_g128_tiles_round_trip(orc):
     blk = packed.view(np.int8).reshape(3, 3, 16384)
     r, c = 133, 200
     assert blk[c // 128, r // 128, ((r % 128) // 8 * 8 + (c % 128) // 16) * 128 + (r % 8) * 16 + c % 16] == q[r, c]
+
+
+def test_quantize_q(orc, g):
+    """The oracle's query quantiser (prefill_attn.hip:120-135) against the golden rows: zero, tiny, large and tie
+    values included."""
+    q = g["q8_in"]
+    got = orc.quantize_q(q.reshape(q.shape[0], 1, 128))
+    assert np.array_equal(got, g["q8_out"])
