@@ -535,10 +535,56 @@ def measure_ref_prefill(la, dev, tokens: int, context: int, reps: int = 3) -> di
     return res
 
 
+def measure_ref_i8(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_caches: int, m: int = 8) -> dict:
+    """The reference's own arithmetic over its own cache bytes at its geometry (16/4/128, int8 264-byte records):
+    the m tokens' query quantiser and the int8-QK verify attention with its combine (lfm3a_quantize_q,
+    lfm3a_verify_attention_i8), back to back over rotating caches. Beside it the reference's published MI50
+    time for the same m and context, which runs this arithmetic on these bytes."""
+    import numpy as np
+    import torch
+
+    qh, kvh, d = 16, 4, 128
+    case = synth.verify_case(seed, ctx, m, q_heads=qh, kv_heads=kvh, head_dim=d)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    K0 = t(np.concatenate([case["K"], case["newK"]]))
+    V0 = t(np.concatenate([case["V"], case["newV"]]))
+    rope = t(la.rope_table(1e6, 0.5, d, ctx + m + 1).view(np.float16))
+    caches = []
+    for _ in range(n_caches):
+        c = la.LayerCache(la.MODE_I8REC, kvh, d, ctx + m + 64, device=dev)
+        c.append(K0, V0, 0, rope=rope)
+        caches.append(c)
+    del K0, V0
+    q = t(case["Q"])
+    qbuf = la.quantize_q(q)
+    out = torch.empty_like(q)
+    splits = la.lib().lfm3a_verify_i8_splits(ctypes.byref(caches[0].layout), ctx, m, 0, 0)
+    ws = torch.empty(la.lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8, device=dev)
+
+    def call(i):   # the round's two calls: quantise the m tokens' queries, attend
+        la.quantize_q(q, out=qbuf)
+        caches[i % n_caches].verify_i8(qbuf, m, qh, ctx, out=out, workspace=ws, splits=splits)
+
+    us = back_to_back_us(torch, call, 30)
+    la.sync()
+    byts = (ctx + m) * kvh * (2 * d + 8)
+    res = {"workload": f"the reference's arithmetic on its int8 records, 16/4/128: {m} tokens over {ctx} cached "
+                       f"(seed {seed})", "us_per_layer": round(us, 2), "splits": splits,
+           "hbm_gbs": round(byts / (us * 1e-6) / 1e9, 1), "frac": round(byts / (us * 1e-6) / 1e9 / peak_gbs, 4),
+           "bytes": byts, "caches": n_caches}
+    if ctx in REF_MI50_VERIFY_US:
+        res["reference_mi50_us"] = REF_MI50_VERIFY_US[ctx]
+    return res
+
+
 def measure_ref_geometries(la, synth, dev, peak_gbs: float) -> dict:
     import torch
 
     res = {"32k": measure_ref_geometry(la, synth, dev, peak_gbs, 32768, 11, 4)}
+    torch.cuda.empty_cache()
+    res["i8rec_32k"] = measure_ref_i8(la, synth, dev, peak_gbs, 32768, 11, 4)
+    torch.cuda.empty_cache()
+    res["i8rec_128k"] = measure_ref_i8(la, synth, dev, peak_gbs, 131072, 12, 2)
     torch.cuda.empty_cache()
     res["128k"] = measure_ref_geometry(la, synth, dev, peak_gbs, 131072, 12, 2)
     torch.cuda.empty_cache()

@@ -92,6 +92,21 @@ int lfm3a_sync(void* stream, int timeout_ms);
  * the current device, to kernels launched after the call returns (it is a synchronous copy). */
 int lfm3a_set_wait_limit(uint64_t limit_ns);
 
+/* Runs the library's kernels from a cubin loaded through the CUDA driver API (cuModuleLoadData into the current
+ * device's primary context), in place of the copies linked into the library: the counterpart of the reference's
+ * code objects embedded in the binary (kernels/embed.go:7-10) and loaded by its driver (internal/kfd/kernel.go:58
+ * LoadCodeObject). image: the committed lfm3-1.7b-mi50_b200/cubin/lfm3attn_sm100a.cubin built from the same
+ * sources (the cgo shim embeds it). Every later launch on that device resolves its kernel in the module by name
+ * and goes through cuLaunchKernelEx; lfm3a_sync and lfm3a_set_wait_limit reach the module's error word and wait
+ * limit. The driver keeps no reference to the image after the call. One module per device: LFM3A_EINVAL if one is
+ * loaded; LFM3A_ENOTSUP if the image lacks this library's device globals. */
+int lfm3a_load_cubin(const void* image, size_t bytes);
+/* Unloads the current device's module (no launch of it may be in flight): launches go back to the library's own
+ * copies. */
+int lfm3a_unload_cubin(void);
+/* Launches made through the current device's module since it was loaded, or -1 when none is loaded. */
+long long lfm3a_cubin_launches(void);
+
 /* ---------------------------------------------------------------- KV cache */
 /* Append n tokens at positions pos0 .. pos0 + n - 1 of one layer (kernels/ops.hip:236-251 kv_write,
  * Go call internal/model/prefill.go:469-475; the verify-side append dspark.hip:1050-1060).

@@ -5,6 +5,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <tuple>
+#include <utility>
+
 namespace lfm3a {
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -286,9 +289,23 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
   return d;
 }
 
-// Host side of the programmatic dependent launch (see pdl_wait): every library kernel goes through here.
+// Launches through a cubin loaded with the CUDA driver API (module.cuh): true when the current device has one and
+// the launch was made there (its result is kept for check_launch), false to launch from the library's own image.
+bool module_launch(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** params);
+
+template <typename Tuple, size_t... I>
+inline void tuple_addresses(Tuple& t, void** out, std::index_sequence<I...>) {
+  ((out[I] = static_cast<void*>(&std::get<I>(t))), ...);
+}
+
+// Host side of the programmatic dependent launch (see pdl_wait): every library kernel goes through here, from the
+// library's own fatbin or, once lfm3a_load_cubin has loaded one for the device, from the committed cubin.
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  std::tuple<KArgs...> vals(static_cast<KArgs>(args)...);
+  void* params[sizeof...(KArgs) > 0 ? sizeof...(KArgs) : 1];
+  tuple_addresses(vals, params, std::index_sequence_for<KArgs...>{});
+  if (module_launch(reinterpret_cast<const void*>(kernel), grid, block, smem, st, params)) return;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -300,7 +317,7 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // A failed launch is reported through cudaGetLastError by the caller's check.
-  (void)cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  (void)cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kernel), params);
 }
 
 }  // namespace lfm3a

@@ -90,7 +90,7 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
 // Bytes `sel` of two words of int8 V (keys k and k + 1 at one dim) as an exact fp16 pair: 0x64NN is 1024 + NN,
 // NN = v + 128 = v ^ 0x80 as a byte, so the pair minus 1152 is (v_k, v_k+1).
 __device__ __forceinline__ uint32_t s8pair_to_f16x2(uint32_t wk, uint32_t wk1, int byte) {
-  const uint32_t x = __byte_perm(wk, wk1, (uint32_t)byte | ((uint32_t)(byte + 4) << 16));
+  const uint32_t x = __byte_perm(wk, wk1, (uint32_t)byte | ((uint32_t)(byte + 4) << 8));   // selector nibble n at bits 4n
   const uint32_t y = (x & 0x00ff00ffu) ^ 0x64806480u;
   __half2 h = *reinterpret_cast<const __half2*>(&y);
   h = __hsub2(h, __floats2half2_rn(1152.f, 1152.f));

@@ -15,6 +15,7 @@
 #include "gemm.cuh"
 #include "i8rec.cuh"
 #include "kv.cuh"
+#include "module.cuh"
 #include "pcache.h"
 #include "prefill.cuh"
 #include "verify.cuh"
@@ -43,6 +44,13 @@ int cuda_fail(cudaError_t e, const char* where) {
 }
 
 int check_launch(const char* what) {
+  if (g_module_result != CUDA_SUCCESS || !g_module_what.empty()) {   // a launch through the loaded cubin failed
+    const std::string detail = std::string(what) + ": " + g_module_what + " failed (CUresult " +
+                               std::to_string((int)g_module_result) + ")";
+    g_module_result = CUDA_SUCCESS;
+    g_module_what.clear();
+    return fail(LFM3A_ELAUNCH, detail);
+  }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, what);
 }
@@ -326,23 +334,88 @@ int lfm3a_sync(void* stream, int timeout_ms) {
     if (std::chrono::steady_clock::now() > deadline) return fail(LFM3A_ETIMEOUT, "stream still busy at the deadline");
     std::this_thread::yield();
   }
-  int word = 0;
+  // The error word of the library's own image and, with a cubin loaded, the module's.
+  int word = 0, mword = 0;
+  ModuleSlot* mod = current_module();
   cudaError_t e = cudaMemcpyFromSymbolAsync(&word, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess && mod && mod->error_word)
+    e = cudaMemcpyAsync(&mword, reinterpret_cast<void*>(mod->error_word), sizeof(int), cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
-  if (word != 0) {
+  if (word != 0 || mword != 0) {
     const int zero = 0;
     e = cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && mod && mod->error_word)
+      e = cudaMemcpyAsync(reinterpret_cast<void*>(mod->error_word), &zero, sizeof(int), cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    return fail(LFM3A_EDEVICE, "device error word " + std::to_string(word));
+    return fail(LFM3A_EDEVICE, "device error word " + std::to_string(word ? word : mword));
   }
   return LFM3A_OK;
 }
 
 int lfm3a_set_wait_limit(uint64_t limit_ns) {
   const uint64_t v = limit_ns ? limit_ns : kDefaultWaitLimitNs;
-  const cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v));
+  cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v));
+  ModuleSlot* mod = current_module();
+  if (e == cudaSuccess && mod && mod->wait_limit)
+    e = cudaMemcpy(reinterpret_cast<void*>(mod->wait_limit), &v, sizeof(v), cudaMemcpyHostToDevice);
   return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, "setting the wait limit");
+}
+
+int lfm3a_load_cubin(const void* image, size_t bytes) {
+  if (!image || bytes < 16) return fail(LFM3A_EINVAL, "no cubin image");
+  const DriverApi& api = driver_api();
+  if (!api.ok) return fail(LFM3A_ECUDA, "the CUDA driver entry points are not available");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaFree(nullptr);   // the runtime's primary context is current from here
+  if (e != cudaSuccess) return cuda_fail(e, "initialising the device");
+  if (dev < 0 || dev >= kMaxDevices) return fail(LFM3A_EINVAL, "device index out of range");
+  ModuleSlot& m = g_modules[dev];
+  std::lock_guard<std::mutex> lock(m.mu);
+  if (m.mod) return fail(LFM3A_EINVAL, "a cubin is already loaded on this device (lfm3a_unload_cubin first)");
+  CUmodule mod = nullptr;
+  CUresult r = api.module_load_data(&mod, image);
+  if (r != CUDA_SUCCESS) return fail(LFM3A_ECUDA, "cuModuleLoadData failed (CUresult " + std::to_string((int)r) + ")");
+  size_t sz = 0;
+  CUdeviceptr err = 0, lim = 0;
+  if (api.module_get_global(&err, &sz, mod, "_ZN5lfm3a14g_device_errorE") != CUDA_SUCCESS ||
+      api.module_get_global(&lim, &sz, mod, "_ZN5lfm3a15g_wait_limit_nsE") != CUDA_SUCCESS) {
+    api.module_unload(mod);
+    return fail(LFM3A_ENOTSUP, "the cubin lacks this library's device globals (built from other sources?)");
+  }
+  m.mod = mod;
+  m.error_word = err;
+  m.wait_limit = lim;
+  m.fns.clear();
+  m.launches.store(0);
+  g_modules_loaded.fetch_add(1, std::memory_order_release);
+  return LFM3A_OK;
+}
+
+int lfm3a_unload_cubin(void) {
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(LFM3A_EINVAL, "device index out of range");
+  ModuleSlot& m = g_modules[dev];
+  std::lock_guard<std::mutex> lock(m.mu);
+  if (!m.mod) return LFM3A_OK;
+  const CUresult r = driver_api().module_unload(m.mod);
+  m.mod = nullptr;
+  m.fns.clear();
+  m.error_word = m.wait_limit = 0;
+  g_modules_loaded.fetch_sub(1, std::memory_order_release);
+  return r == CUDA_SUCCESS ? LFM3A_OK : fail(LFM3A_ECUDA, "cuModuleUnload failed");
+}
+
+long long lfm3a_cubin_launches(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return -1;
+  }
+  return g_modules[dev].mod ? g_modules[dev].launches.load() : -1;
 }
 
 }  // extern "C"

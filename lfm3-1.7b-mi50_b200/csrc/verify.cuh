@@ -928,18 +928,16 @@ __device__ __forceinline__ unsigned gather_calls(const GatherOut& go) {
                                                go.world * kGatherRows);
 }
 
-// After the block's peer stores of rows [r0, r1): one thread fences at system scope and raises those rows' flags in
-// every region with release stores (callers put a block barrier before it).
+// After the block's peer stores of rows [r0, r1) and a block barrier (the caller's): thread w < world raises those
+// rows' flags in region w with release stores at system scope. The barrier orders the block's data stores before
+// each release, so a reader that acquires a flag sees the rows (no full system fence: that one cost several
+// microseconds per block).
 __device__ __forceinline__ void gather_raise(const GatherOut& go, int r0, int r1, unsigned calls) {
-  if (threadIdx.x != 0) return;
-  __threadfence_system();
-#pragma unroll 1
-  for (int w = 0; w < go.world; ++w)
-    for (int r = r0; r < r1; ++r)
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(gather_flags(go.peers[w], go.half_stride) +
-                                                                 go.rank * kGatherRows + r),
-                   "r"(calls + 1)
-                   : "memory");
+  const int w = threadIdx.x;
+  if (w >= go.world) return;
+  unsigned* f = gather_flags(go.peers[w], go.half_stride) + go.rank * kGatherRows;
+  for (int r = r0; r < r1; ++r)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f + r), "r"(calls + 1) : "memory");
 }
 
 template <int D, bool GATHER>

@@ -20,6 +20,7 @@ import numpy as np
 
 _HERE = pathlib.Path(__file__).resolve().parent
 LIB_PATH = _HERE / "liblfm3attn.so"
+CUBIN_PATH = _HERE / "cubin" / "lfm3attn_sm100a.cubin"
 
 MODE_F16 = 0
 MODE_I8REC = 1
@@ -69,6 +70,9 @@ SIGNATURES = {
     "lfm3a_rope_table": (_I, [ctypes.c_double, ctypes.c_double, _I, _I, _P]),
     "lfm3a_sync": (_I, [_P, _I]),
     "lfm3a_set_wait_limit": (_I, [ctypes.c_uint64]),
+    "lfm3a_load_cubin": (_I, [_P, _SZ]),
+    "lfm3a_unload_cubin": (_I, []),
+    "lfm3a_cubin_launches": (ctypes.c_longlong, []),
     "lfm3a_kv_append": (_I, [ctypes.POINTER(KvView), _P, _P, _I64, _I, _I, _P, _P, _P]),
     "lfm3a_kv_truncate": (_I, [ctypes.POINTER(KvView), _I, _P]),
     "lfm3a_accept": (_I, [_P, _P, _I, _P, _P]),
@@ -184,6 +188,27 @@ def rope_table(theta: float, factor: float, head_dim: int, positions: int) -> np
 def sync(stream=None, timeout_ms: int = 120000) -> None:
     """Bounded wait for the stream plus the device error word (queue.go:292-310 Wait)."""
     _check(lib().lfm3a_sync(_stream(stream), timeout_ms))
+
+
+_cubin_images = []   # images handed to the driver stay alive while loaded
+
+
+def load_cubin(path=None) -> None:
+    """Loads the committed sm_100a cubin (or `path`) through the CUDA driver API on the current device: from then
+    on the library's launches on that device run its kernels (the engine's embedded code objects, kernels/embed.go)."""
+    data = pathlib.Path(path or CUBIN_PATH).read_bytes()
+    buf = ctypes.create_string_buffer(data, len(data))
+    _check(lib().lfm3a_load_cubin(buf, len(data)))
+    _cubin_images.append(buf)
+
+
+def unload_cubin() -> None:
+    _check(lib().lfm3a_unload_cubin())
+
+
+def cubin_launches() -> int:
+    """Launches made through the loaded cubin on the current device (-1: none loaded)."""
+    return int(lib().lfm3a_cubin_launches())
 
 
 def set_wait_limit(limit_ns: int = 0) -> None:
@@ -526,7 +551,7 @@ def accept(best, tokens, state, stream=None) -> None:
     _check(lib().lfm3a_accept(_ptr(best), _ptr(tokens), m, _ptr(state), _stream(stream)))
 
 
-def quantize_q(q, q_heads: int | None = None, head_dim: int | None = None, stream=None):
+def quantize_q(q, q_heads: int | None = None, head_dim: int | None = None, out=None, stream=None):
     """The reference's query quantiser (prefill_attn.hip:120-135): q fp16 [T][q_heads][head_dim] (or row-strided
     [T][>= q_heads * head_dim] with q_heads, head_dim given) -> qbuf int32 [T * q_heads][head_dim/4 + head_dim/32]."""
     import torch
@@ -534,7 +559,8 @@ def quantize_q(q, q_heads: int | None = None, head_dim: int | None = None, strea
     t = q.shape[0]
     if q_heads is None:
         q_heads, head_dim = q.shape[1], q.shape[2]
-    qbuf = torch.empty((t * q_heads, head_dim // 4 + head_dim // 32), dtype=torch.int32, device=q.device)
+    qbuf = out if out is not None else torch.empty((t * q_heads, head_dim // 4 + head_dim // 32), dtype=torch.int32,
+                                                   device=q.device)
     _check(lib().lfm3a_quantize_q(_ptr(q), q.stride(0), t, q_heads, head_dim, _ptr(qbuf), _stream(stream)))
     return qbuf
 
@@ -651,22 +677,15 @@ def decode_pool(pool: np.ndarray, table: np.ndarray, lay: KvLayout, length: int)
             out[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS] = raw
         return {"rec": out[:length]}
     k_idx, v_idx, v8_idx = _f16_section_index(d)
-    K = np.zeros((pages * BLOCK_TOKENS, h, d), dtype=np.uint16)
-    V = np.zeros_like(K)
-    V8 = np.zeros((pages * BLOCK_TOKENS, h, d), dtype=np.int8)
-    page_scale = np.zeros((pages, h), dtype=np.float32)
-    for p in range(pages):
-        blk = int(table[p])
-        for hh in range(h):
-            base = blk * lay.block_bytes + hh * lay.head_bytes
-            sec = pool[base:base + lay.head_bytes]
-            kk = sec[:64 * d].view(np.uint16)
-            vv = sec[64 * d:128 * d].view(np.uint16)
-            v8 = sec[128 * d:160 * d].view(np.int8)
-            K[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS, hh] = kk[k_idx]
-            V[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS, hh] = vv[v_idx]
-            V8[p * BLOCK_TOKENS:(p + 1) * BLOCK_TOKENS, hh] = v8[v8_idx]
-            page_scale[p, hh] = sec[160 * d:160 * d + 4].view(np.float32)[0]
+    blocks = np.asarray(table[:pages], dtype=np.int64)
+    sec = pool[:pool.size // lay.block_bytes * lay.block_bytes].reshape(-1, h, lay.head_bytes)[blocks]   # [pages][h][bytes]
+    kk = np.ascontiguousarray(sec[:, :, :64 * d]).view(np.uint16)          # [pages][h][32 d]
+    vv = np.ascontiguousarray(sec[:, :, 64 * d:128 * d]).view(np.uint16)
+    v8 = np.ascontiguousarray(sec[:, :, 128 * d:160 * d]).view(np.int8)
+    K = kk[:, :, k_idx].transpose(0, 2, 1, 3).reshape(pages * BLOCK_TOKENS, h, d)
+    V = vv[:, :, v_idx].transpose(0, 2, 1, 3).reshape(pages * BLOCK_TOKENS, h, d)
+    V8 = v8[:, :, v8_idx].transpose(0, 2, 1, 3).reshape(pages * BLOCK_TOKENS, h, d)
+    page_scale = np.ascontiguousarray(sec[:, :, 160 * d:160 * d + 4]).view(np.float32).reshape(pages, h)
     qblocks = (length + QUANT_BLOCK - 1) // QUANT_BLOCK
     vscale = page_scale[0::2][:qblocks]
     v8_len = min(V8.shape[0], qblocks * QUANT_BLOCK)

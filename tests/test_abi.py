@@ -190,3 +190,11 @@ def test_synth_head_slices_match_full_draw(synth):
         for k in ("K", "V", "newK", "newV"):
             assert np.array_equal(part[k].view(np.uint16), full[k][:, h0:h1].view(np.uint16)), k
         assert np.array_equal(part["Q"].view(np.uint16), full["Q"][:, 4 * h0:4 * h1].view(np.uint16))
+
+
+def test_committed_cubin_is_an_sm100a_image(la):
+    """The committed kernel image that lfm3a_load_cubin takes: an ELF object for CUDA (e_machine 190)."""
+    data = la.CUBIN_PATH.read_bytes()
+    assert data[:4] == b"\x7fELF" and len(data) > 100000
+    assert int.from_bytes(data[18:20], "little") == 190
+    assert la.lib().lfm3a_load_cubin(None, 0) == la.EINVAL

@@ -10,10 +10,11 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("splits", [1, 37, 64, 65, 100, 130, 296, 400])
 @pytest.mark.parametrize("gated", [False, True])
-def test_combine_split_counts(la, orc, synth, cuda, splits, gated):
+@pytest.mark.parametrize("d", [64, 128])
+def test_combine_split_counts(la, orc, synth, cuda, splits, gated, d):
     import torch
 
-    rows, d = 64, 64
+    rows = 64
     rng = np.random.default_rng(splits)
     parts = np.empty((splits, rows, d + 2), dtype=np.float32)
     parts[:, :, :d] = rng.normal(size=(splits, rows, d)).astype(np.float32) * 5.0

@@ -73,3 +73,70 @@ def test_lifecycle_two_layers(la, orc, synth, cuda):
         v8, vs = orc.quantize_v8(V[:length], length)
         assert np.array_equal(logical["V8"], v8)
         assert np.array_equal(logical["vscale"].view(np.uint32), vs.view(np.uint32))
+
+
+def test_lifecycle_config5_full_size(la, orc, cuda):
+    """Config 5 at full size: 4 layers, a 131072-token causal prefill (append with RoPE, int8-PV attention), then 256
+    DSpark rounds per layer through the round entry point (16 drafts appended inside the attention kernel, verified,
+    n = min(16, X) kept with X geometric, P(stop) = 0.3, the rest rolled back). Inputs N(0,1) fp16 from torch's
+    seeded generator (seed 4); keep lengths from numpy's default_rng(4), as the benchmark's c5 field.
+    Checked against the oracle: sampled prefill rows (int8-PV, 2e-2), the verify outputs of rounds 0, 127 and 255 of
+    layer 0 (4e-3), and at the end every layer's K and V fp16 bytes, int8 V blocks, scales and length bit-exact."""
+    import torch
+
+    layers, T, rounds, M = 4, 131072, 256, 16
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(4)
+    rnd = lambda *shape: torch.randn(*shape, generator=gen, device=cuda, dtype=torch.float32).half()
+    keep = np.minimum(16, np.random.default_rng(4).geometric(0.3, size=rounds))
+    cap = T + int(keep.sum()) + M + 64
+    table = orc.rope_table(1e6, 1.0, 64, cap + 1)
+    rope = dev(table.view(np.float16), cuda)
+    caches, expect = [], []
+    prows = np.arange(0, T, 16411)
+    for layer in range(layers):
+        k, v, q = rnd(T, 8, 64), rnd(T, 8, 64), rnd(T, 32, 64)
+        cache = la.LayerCache(la.MODE_F16, 8, 64, cap, device=cuda)
+        cache.append(k, v, 0, rope=rope)
+        out = cache.prefill(q, 0, exact=False)
+        la.sync()
+        K, V = orc.kv_append_f16(k.cpu().numpy(), v.cpu().numpy(), 0, rope=table)
+        v8, vs = orc.quantize_v8(V, T)
+        emu = orc.prefill_i8pv(q.cpu().numpy(), 0, K, v8, vs, row_step=16411)
+        assert rel_err(out.float().cpu().numpy()[prows], emu[prows]) < 2e-2, layer
+        caches.append(cache)
+        Ke = np.zeros((cap, 8, 64), dtype=np.float16)   # the cache the oracle expects, written in place
+        Ve = np.zeros((cap, 8, 64), dtype=np.float16)
+        Ke[:T], Ve[:T] = K, V
+        expect.append((Ke, Ve))
+        del k, v, q, out, K, V
+    drafts = rnd(rounds, 2, M, 8, 64)
+    qs = rnd(rounds, M, 32, 64)
+    ws = la.verify_workspace(M, 32, 64, 2 * 148, cuda)
+    out = torch.empty((M, 32, 64), dtype=torch.float16, device=cuda)
+    length = T
+    checked = {0, 127, 255}
+    for r in range(rounds):
+        dk_h, dv_h = drafts[r, 0].cpu().numpy(), drafts[r, 1].cpu().numpy()
+        kn, vn = orc.kv_append_f16(dk_h, dv_h, length, rope=table)
+        for Ke, Ve in expect:   # every draft is appended; the next round overwrites the rejected ones
+            Ke[length:length + M], Ve[length:length + M] = kn, vn
+        for layer, cache in enumerate(caches):
+            cache.verify_round(drafts[r, 0], drafts[r, 1], qs[r], length, rope=rope, out=out, workspace=ws)
+            if layer == 0 and r in checked:
+                la.sync()
+                Ke, Ve = expect[0]
+                want = orc.verify(qs[r].cpu().numpy(), Ke[:length + M], Ve[:length + M], length, splits=37)
+                assert rel_err(out.float().cpu().numpy(), want) < 4e-3, r
+            cache.truncate(length + int(keep[r]))
+        length += int(keep[r])
+    la.sync()
+    assert length == T + int(keep.sum())
+    for cache, (Ke, Ve) in zip(caches, expect):
+        assert cache.length == length
+        logical = cache.logical(length)
+        assert np.array_equal(logical["K"], Ke[:length].view(np.uint16))
+        assert np.array_equal(logical["V"], Ve[:length].view(np.uint16))
+        v8, vs = orc.quantize_v8(Ve[:length], length)
+        assert np.array_equal(logical["V8"], v8)
+        assert np.array_equal(logical["vscale"].view(np.uint32), vs.view(np.uint32))
