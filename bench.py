@@ -7,7 +7,8 @@ number of GPUs) / the max-over-ranks step time (GB/s); us_per_layer is the same 
 
 N > 1 (torchrun, one rank per GPU, NCCL): the same 131072-token layer is sharded (strong scaling). Heads plan
 (default): rank r holds kv heads [8r/N, 8(r+1)/N) of the whole sequence, runs its round on them, and the
-outputs are exchanged (NCCL all-gather, or the combine's NVLink peer stores). Seq plan: rank r holds a run of
+outputs are exchanged (the combine's NVLink peer stores with a flag in every word, or --exchange nccl: an NCCL
+all-gather). Seq plan: rank r holds a run of
 64-token blocks of all heads, the last rank also the drafts; the log-sum-exp partials are all-gathered and
 merged. After the timed region rank 0 checks the exchanged output against a one-GPU round of all 8 heads.
 
@@ -53,10 +54,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--load-seconds", type=float, default=2.0, help="untimed replays while the clock sampler runs")
     ap.add_argument("--shard", choices=["heads", "seq"], default="heads", help="multi-GPU plan (N > 1)")
-    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="nccl",
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="heads plan: NCCL all-gather of the outputs, or the combine's scatter over NVLink peer "
-                         "stores (measured about 3 us per round slower at 2 GPUs: the cost is the ranks' per-round "
-                         "synchronisation, which both pay)")
+                         "stores with the call's flag in every word and the bounded wait kernel")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 2/4/5 and decode fields (N = 1)")
     ap.add_argument("--only", choices=["c2", "c4", "c5", "decode", "chunks", "gemm", "ref"],
                     help="run only that configuration's measurement on one GPU and print its fields (for profiling)")
@@ -797,14 +797,23 @@ def measure_gemm(la, dev, peaks_: dict, reps: int = 10) -> dict:
     return res
 
 
-def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, seed: int = 4) -> dict:
+def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, seed: int = 4, R=None, pg=None,
+               gg=None) -> dict:
     """Config 5, the KV lifecycle: per layer a causal prefill of ctx tokens (append with RoPE + int8-PV
     attention), then `steps` DSpark rounds over all layers (append 16 drafts, verify 16, keep
     n = min(16, X), X ~ geometric(0.3), roll back 16 - n). Inputs N(0,1) fp16 from torch's seeded generator
-    on the device (the splitmix64 stream is too slow on the host at this size)."""
+    on the device (the splitmix64 stream is too slow on the host at this size).
+
+    On N GPUs (R: the rank's kv-head plan) every rank draws the same inputs and keeps its kv heads: its prefill
+    stays local (its heads' outputs feed a row-parallel output projection), and each round's verify output is
+    exchanged (gg: the peer-store exchange, else the NCCL all-gather). Times are the max over ranks."""
     import numpy as np
     import torch
 
+    world = R.world if R is not None else 1
+    h0, h1 = (R.h0, R.h1) if R is not None else (0, KVH)
+    q0, q1 = (R.q0, R.q1) if R is not None else (0, QH)
+    kvh, qh = h1 - h0, q1 - q0
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed)
     rnd = lambda *shape: torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).half()
@@ -812,13 +821,15 @@ def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, se
     keep = np.minimum(16, rng.geometric(0.3, size=steps))
     cap = ctx + int(keep.sum()) + M + 64
     rope = torch.from_numpy(la.rope_table(1e6, 1.0, D, cap + 1).view(np.float16)).to(dev)
-    caches = [la.LayerCache(la.MODE_F16, KVH, D, cap, device=dev) for _ in range(layers)]
-    q_pre = rnd(ctx, QH, D)
+    caches = [la.LayerCache(la.MODE_F16, kvh, D, cap, device=dev) for _ in range(layers)]
+    q_pre = rnd(ctx, QH, D)[:, q0:q1].contiguous()
     out_pre = torch.empty_like(q_pre)
     torch.cuda.synchronize()
     e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
-    k_in = [(rnd(ctx, KVH, D), rnd(ctx, KVH, D)) for _ in range(layers)]
+    k_in = [(rnd(ctx, KVH, D)[:, h0:h1].contiguous(), rnd(ctx, KVH, D)[:, h0:h1].contiguous()) for _ in range(layers)]
     torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
     e0.record()
     for c, (k, v) in zip(caches, k_in):
         c.append(k, v, 0, rope=rope)
@@ -826,20 +837,29 @@ def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, se
     e1.record()
     torch.cuda.synchronize()
     del k_in, q_pre, out_pre
-    drafts = rnd(steps, 2, M, KVH, D)
-    qs = rnd(steps, M, QH, D)
-    ws = la.verify_workspace(M, QH, D, 2 * 148, dev)
-    out = torch.empty((M, QH, D), dtype=torch.float16, device=dev)
+    drafts = rnd(steps, 2, M, KVH, D)[:, :, :, h0:h1].contiguous()
+    qs = rnd(steps, M, QH, D)[:, :, q0:q1].contiguous()
+    ws = la.verify_workspace(M, qh, D, 2 * 148, dev)
+    out = torch.empty((M, qh, D), dtype=torch.float16, device=dev)
+    gathered = torch.empty((world, M, qh, D), dtype=torch.float16, device=dev)
     stream = torch.cuda.Stream(device=dev)
     g = torch.cuda.CUDAGraph()
     length = ctx
     with torch.cuda.graph(g, stream=stream):
         for s in range(steps):
             for c in caches:
-                c.verify_round(drafts[s, 0], drafts[s, 1], qs[s], length, rope=rope, out=out, workspace=ws)
+                if gg is not None:
+                    gg.verify_round(c, drafts[s, 0], drafts[s, 1], qs[s], length, rope=rope, workspace=ws)
+                    gg.wait(gathered)
+                else:
+                    c.verify_round(drafts[s, 0], drafts[s, 1], qs[s], length, rope=rope, out=out, workspace=ws)
+                    if pg:
+                        pg.all_gather_into_tensor(gathered, out)
                 c.truncate(length + int(keep[s]))
             length += int(keep[s])
     torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
     e2.record()
     g.replay()
     e3.record()
@@ -847,15 +867,24 @@ def measure_c5(la, dev, layers: int = 4, ctx: int = 131072, steps: int = 256, se
     la.sync()
     prefill_ms = e0.elapsed_time(e1)   # the prefill alone: the graph capture between e1 and e2 is host work
     verify_ms = e2.elapsed_time(e3)
+    t = torch.tensor([prefill_ms, verify_ms], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    prefill_ms, verify_ms = t.tolist()
     lengths = sorted({c.length for c in caches})
     del g, caches
-    return {"workload": f"config 5: KV lifecycle, {layers} layers, {ctx}-token causal prefill (int8-PV), then "
-                        f"{steps} rounds of 16 drafts (keep min(16, Geom(0.3)))",
-            "data": "torch.randn N(0,1) fp16 on the device, seed 4; keep lengths from numpy default_rng(4)",
-            "total_ms": round(prefill_ms + verify_ms, 2), "prefill_ms": round(prefill_ms, 2),
-            "verify_ms": round(verify_ms, 2),
-            "us_per_layer_round": round(verify_ms * 1e3 / (steps * layers), 2),
-            "final_length": lengths[0] if len(lengths) == 1 else lengths, "expected_length": ctx + int(keep.sum())}
+    res = {"workload": f"config 5: KV lifecycle, {layers} layers, {ctx}-token causal prefill (int8-PV), then "
+                       f"{steps} rounds of 16 drafts (keep min(16, Geom(0.3)))",
+           "data": "torch.randn N(0,1) fp16 on the device, seed 4; keep lengths from numpy default_rng(4)",
+           "total_ms": round(prefill_ms + verify_ms, 2), "prefill_ms": round(prefill_ms, 2),
+           "verify_ms": round(verify_ms, 2),
+           "us_per_layer_round": round(verify_ms * 1e3 / (steps * layers), 2),
+           "final_length": lengths[0] if len(lengths) == 1 else lengths, "expected_length": ctx + int(keep.sum())}
+    if world > 1:
+        res["parallelism"] = (f"kv-head shard x{world}: prefill local, each round's output exchanged "
+                              + ("over NVLink peer stores" if gg is not None else "by NCCL all-gather") +
+                              "; max over ranks")
+    return res
 
 
 def run_ours(args):
@@ -930,13 +959,15 @@ def run_ours(args):
 
     # The single-GPU and kv-head plans run each round's append and attention as one call (lfm3a_verify_round:
     # the drafts' append fused into the attention kernel); the others append first.
-    fused_round = R.drafts and R.plan in ("single", "heads") and gg is None
+    fused_round = R.drafts and R.plan in ("single", "heads")
 
     def attend(c, dq, timing=None, dk=None, dv=None):
         if timing is not None:
             timing[0].record()
         if R.plan == "seq":
             c.verify_partial(dq, R.kv_begin, R.kv_end, R.ctx_len, out=part, workspace=ws, splits=splits)
+        elif gg is not None and fused_round and dk is not None:
+            gg.verify_round(c, dk, dv, dq, R.ctx_len, rope=rope, workspace=ws, splits=splits)
         elif gg is not None:
             gg.verify(c, dq, R.ctx_len, workspace=ws, splits=splits)
         elif fused_round and dk is not None:
@@ -1125,6 +1156,10 @@ def run_ours(args):
     del graph, kgraph, load_graph
 
     extras = {}
+    if world > 1 and not args.no_extras and R.plan == "heads":   # config 5 on the same plan, every rank
+        del caches
+        torch.cuda.empty_cache()
+        extras["c5"] = measure_c5(la, dev, R=R, pg=pg, gg=gg)
     if rank == 0 and world == 1 and not args.no_extras:
         pk = peaks()
         del caches

@@ -285,13 +285,13 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
 /* ---------------------------------------------------------------- multi-GPU exchange
  * No reference counterpart: the reference engine runs one GPU. For kv-head sharding over the GPUs of one
  * node (one process per GPU), each rank's verify output goes straight into every rank's gather region
- * through NVLink peer stores from the combine kernel, and a flag per source rank says that its slice
- * landed, in place of a separate all-gather.
+ * through NVLink peer stores from the combine kernel, in place of a separate all-gather. Every 8-byte word
+ * carries two fp16 outputs and the call's flag, written with one 64-bit store, so a reader that sees the flag
+ * sees the data: no fence and no separate flag.
  *
- * A gather region holds [2][world][rows][head_dim] fp16 (the gathered outputs of even and odd calls), then
- * uint32 flags per (source rank, row) and a call counter. It must be its own allocation (so that
- * other processes can map it) and start zeroed: lfm3a_gather_region_alloc gives one. head_dim 64, at most
- * 1024 rows. */
+ * A gather region holds [2][world][rows][head_dim / 2] such words (the exchanges of even and odd calls), then a
+ * call counter. It must be its own allocation (so that other processes can map it) and start zeroed:
+ * lfm3a_gather_region_alloc gives one. head_dim 64, at most 1024 rows. */
 size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim);
 int lfm3a_gather_region_alloc(int world, int rows, int head_dim, void** region_out);
 int lfm3a_gather_region_free(void* region);
@@ -304,16 +304,21 @@ int lfm3a_peer_close(void* region);
 
 /* lfm3a_verify_attention of one rank of the kv-head plan (q_heads = this rank's query heads, rows =
  * m * q_heads). peers[w]: rank w's region as mapped in this process (peers[rank] = this rank's own).
- * The combine writes this rank's rows into slice `rank` of the call's half of every region, then raises
- * this rank's flag in each; lfm3a_gather_wait on the same stream waits (bounded by lfm3a_set_wait_limit, else
- * the device error word) until every rank's slice of this call has landed in the own region, then copies the
- * gathered [world][m][q_heads][head_dim] fp16 output to out (device, or NULL to leave it in the region at
- * region + (n % 2) * world * rows * head_dim halves for call n). Every rank makes the same calls in the
- * same order; world <= 8. The scatter runs in the combine, so the call uses at least two splits; a context
+ * The combine writes this rank's rows, with the call's flag in every word, into slice `rank` of the call's
+ * half of every region; lfm3a_gather_wait on the same stream waits (bounded by lfm3a_set_wait_limit, else the
+ * device error word) until every word of every rank's slice of this call carries the flag, writing the
+ * gathered [world][m][q_heads][head_dim] fp16 output to out (device; NULL only waits). Every rank makes the same
+ * calls in the same order; world <= 8. The scatter runs in the combine, so the call uses at least two splits; a context
  * of a single key tile is refused with LFM3A_ENOTSUP before anything is launched. */
 int lfm3a_verify_attention_gather(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
                                   const void* gate, void* const* peers, int world, int rank, void* workspace,
                                   size_t workspace_bytes, int splits, void* stream);
+/* lfm3a_verify_round (the drafts' append fused into the attention) of one rank of the kv-head plan, its output
+ * exchanged as lfm3a_verify_attention_gather's. */
+int lfm3a_verify_round_gather(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride,
+                              const void* rope, const void* k_norm, const void* q, int m, int q_heads, int ctx_len,
+                              int window, const void* gate, void* const* peers, int world, int rank, void* workspace,
+                              size_t workspace_bytes, int splits, void* stream);
 int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out, void* stream);
 
 /* ---------------------------------------------------------------- prefix cache (host only)

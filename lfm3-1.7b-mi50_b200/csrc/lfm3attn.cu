@@ -209,7 +209,7 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
     // The exchange runs in the combine: one split would leave no combine to scatter the rows.
     if (a.splits < 2 && a.t_total >= 2) a.splits = 2;
     if (a.splits < 2) return fail(LFM3A_ENOTSUP, "the gather needs several splits (a combine): context too short");
-    gather->half_stride = (int64_t)gather->world * rows * 64;
+    gather->half_stride = (int64_t)gather->world * rows * 32;   // 8-byte words: two of the 64 dims each
   }
   // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
   if (a.splits == 1 && out32) {
@@ -635,10 +635,9 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
 }
 
 size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim) {
-  if (world < 1 || world > 8 || rows < 1 || head_dim < 1) return 0;
-  if (rows > kGatherRows) return 0;
-  const size_t data = (size_t)2 * world * rows * head_dim * sizeof(__half);
-  return (data + ((size_t)world * kGatherRows + 1) * sizeof(unsigned) + 255) / 256 * 256;
+  if (world < 1 || world > 8 || rows < 1 || rows > kGatherMaxRows || head_dim < 2 || (head_dim & 1)) return 0;
+  const size_t words = (size_t)2 * world * rows * (head_dim / 2);   // two halves of [world][rows][head_dim / 2]
+  return (words * 8 + sizeof(unsigned) + 255) / 256 * 256;
 }
 
 int lfm3a_gather_region_alloc(int world, int rows, int head_dim, void** region_out) {
@@ -696,11 +695,43 @@ int lfm3a_verify_attention_gather(const lfm3a_kv_view* kv, const void* q, int m,
                     workspace_bytes, splits, as_stream(stream), &go);
 }
 
+int lfm3a_verify_round_gather(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride,
+                              const void* rope, const void* k_norm, const void* q, int m, int q_heads, int ctx_len,
+                              int window, const void* gate, void* const* peers, int world, int rank, void* workspace,
+                              size_t workspace_bytes, int splits, void* stream) {
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  if (!peers || world < 1 || world > 8 || rank < 0 || rank >= world) return fail(LFM3A_EINVAL, "bad gather ranks");
+  const int D = kv->layout.head_dim, H = kv->layout.kv_heads;
+  if (!k || !v || m < 1 || ctx_len < 0) return fail(LFM3A_EINVAL, "bad round arguments");
+  if (token_stride == 0) token_stride = (int64_t)H * D;
+  if (token_stride < (int64_t)H * D) return fail(LFM3A_EINVAL, "token_stride smaller than kv_heads * head_dim");
+  GatherOut go;
+  go.world = world;
+  go.rank = rank;
+  for (int w = 0; w < world; ++w) {
+    if (!peers[w] || !aligned16(peers[w])) return fail(LFM3A_EINVAL, "gather regions must be 16-byte aligned");
+    go.peers[w] = static_cast<__half*>(peers[w]);
+  }
+  AppendArgs app;
+  app.g = geom_of(kv);
+  app.k = static_cast<const __half*>(k);
+  app.v = static_cast<const __half*>(v);
+  app.rope = static_cast<const __half*>(rope);
+  app.knorm = static_cast<const __half*>(k_norm);
+  app.stride = token_stride;
+  app.pos0 = ctx_len;
+  app.n = m;
+  if (splits <= 0) splits = verify_splits_for(H, ctx_len, m, window, current_sm_count(), D == 128 && m <= 16 ? 1 : 2);
+  return run_verify(kv, q, m, q_heads, 0, ctx_len + m, ctx_len, window, gate, nullptr, nullptr, workspace,
+                    workspace_bytes, splits, as_stream(stream), &go, true, &app);
+}
+
 int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out, void* stream) {
   if (!region || world < 1 || world > 8 || rows < 1 || head_dim < 1 || (out && !aligned16(out)))
     return fail(LFM3A_EINVAL, "bad gather wait arguments");
-  const int64_t half_stride = (int64_t)world * rows * head_dim;
-  if (head_dim != 64 || rows > kGatherRows) return fail(LFM3A_ENOTSUP, "gather: head_dim 64, at most 1024 rows");
+  const int64_t half_stride = (int64_t)world * rows * (head_dim / 2);
+  if (head_dim != 64 || rows > kGatherMaxRows) return fail(LFM3A_ENOTSUP, "gather: head_dim 64, at most 1024 rows");
   launch_pdl(gather_wait_kernel, 1, 1024, 0, as_stream(stream), static_cast<__half*>(region), world, half_stride, rows,
              static_cast<__half*>(out));
   return check_launch("gather_wait_kernel");

@@ -908,36 +908,37 @@ __global__ __launch_bounds__(kVfThreads, V6Layout<D>::kBlocksPerSm) void verify_
 // 256 / D rows per block, every load issued up front: one L2 round trip); beyond, combine_row_kernel (a block per
 // row, the splits spread over its threads), for the few rows and many splits of a kv-head shard.
 //
-// Where the kv-head plan's combine sends a rank's output: slice `rank` of the current call's half of every
-// rank's gather region (peers[w], mapped here), then a flag per (source rank, row) in each region.
-// The region is [2][world][rows][D] fp16, flags [world][kGatherRows] u32, then this rank's call counter.
-constexpr int kGatherRows = 1024;   // rows of one call at most
+// Where the kv-head plan's combine sends a rank's output: slice `rank` of the current call's half of every rank's
+// gather region (peers[w], mapped here). Every 8-byte word of a slice carries two fp16 outputs and the call's flag
+// (the call counter + 1), written with one 64-bit store: a reader that sees the flag in a word sees its data, so
+// nothing is fenced (the flag-per-word form of a low-latency exchange). The region is [2][world][rows][D / 2] such
+// words (the halves of even and odd calls), then this rank's call counter, which gather_wait_kernel advances.
+constexpr int kGatherMaxRows = 1024;   // rows of one call at most
 struct GatherOut {
   __half* peers[8];
   int world = 0, rank = 0;
-  int64_t half_stride = 0;   // halves in one call's half: world * rows * D
+  int64_t half_stride = 0;   // words in one call's half: world * rows * D / 2
 };
 
-__device__ __forceinline__ unsigned* gather_flags(__half* region, int64_t half_stride) {
-  return reinterpret_cast<unsigned*>(region + 2 * half_stride);
+__device__ __forceinline__ unsigned long long* gather_words(__half* region) {
+  return reinterpret_cast<unsigned long long*>(region);
+}
+__device__ __forceinline__ unsigned* gather_counter(__half* region, int64_t half_stride) {
+  return reinterpret_cast<unsigned*>(gather_words(region) + 2 * half_stride);
 }
 
 // The gather exchange's call counter of this rank (advanced by gather_wait_kernel after each call).
 __device__ __forceinline__ unsigned gather_calls(const GatherOut& go) {
-  return *reinterpret_cast<volatile unsigned*>(gather_flags(go.peers[go.rank], go.half_stride) +
-                                               go.world * kGatherRows);
+  return *reinterpret_cast<volatile unsigned*>(gather_counter(go.peers[go.rank], go.half_stride));
 }
 
-// After the block's peer stores of rows [r0, r1) and a block barrier (the caller's): thread w < world raises those
-// rows' flags in region w with release stores at system scope. The barrier orders the block's data stores before
-// each release, so a reader that acquires a flag sees the rows (no full system fence: that one cost several
-// microseconds per block).
-__device__ __forceinline__ void gather_raise(const GatherOut& go, int r0, int r1, unsigned calls) {
-  const int w = threadIdx.x;
-  if (w >= go.world) return;
-  unsigned* f = gather_flags(go.peers[w], go.half_stride) + go.rank * kGatherRows;
-  for (int r = r0; r < r1; ++r)
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f + r), "r"(calls + 1) : "memory");
+// Row `row`, dims d0, d0 + 1 of this rank's output into every region: one 64-bit relaxed store per region.
+__device__ __forceinline__ void gather_put(const GatherOut& go, int rows, int row, int d0, int D, uint32_t pair,
+                                           unsigned calls) {
+  const int64_t at = (int64_t)(calls & 1u) * go.half_stride + ((int64_t)go.rank * rows + row) * (D / 2) + d0 / 2;
+  const unsigned long long word = (unsigned long long)pair | ((unsigned long long)(calls + 1u) << 32);
+  for (int w = 0; w < go.world; ++w)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(gather_words(go.peers[w]) + at), "l"(word) : "memory");
 }
 
 template <int D, bool GATHER>
@@ -980,21 +981,10 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* part, int row
   const float acc = a0 + a1;
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  if (GATHER) {
-    // The block's rows (contiguous in every region) are staged in shared memory and sent to every rank's
-    // region as 16-byte peer stores; after a block barrier their flags go up.
-    __shared__ __align__(16) __half s_out[256];
-    const unsigned calls = gather_calls(go);
-    s_out[threadIdx.x] = __float2half_rn(live ? acc * (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row) : 0.f);
-    __syncthreads();
-    const int r0 = blockIdx.x * RPB, r1 = min(r0 + RPB, rows), nvec = (r1 - r0) * D / 8;
-    const int64_t off = (int64_t)(calls & 1u) * go.half_stride + ((int64_t)go.rank * rows + r0) * D;
-    for (int i = threadIdx.x; i < nvec * go.world; i += blockDim.x) {
-      const int w = i / nvec, c = i - w * nvec;
-      reinterpret_cast<uint4*>(go.peers[w] + off)[c] = reinterpret_cast<const uint4*>(s_out)[c];
-    }
-    __syncthreads();
-    gather_raise(go, r0, r1, calls);
+  if (GATHER) {   // even dims send the pair (d, d + 1) with the call's flag to every rank's region
+    const float v = live ? acc * (L > 0.f ? 1.f / L : 0.f) * sigmoid_gate(gate, row) : 0.f;
+    const float vn = __shfl_down_sync(0xffffffffu, v, 1);
+    if (live && (d & 1) == 0) gather_put(go, rows, row, d, D, pack_half2(v, vn), gather_calls(go));
     return;
   }
   if (!live) return;
@@ -1087,9 +1077,7 @@ __global__ __launch_bounds__(kCombineRowThreads) void combine_row_kernel(const f
       const float scale = (l > 0.f ? 1.f / l : 0.f) * sigmoid_gate(gate, row);
       const uint32_t hv = pack_half2(sum.x * scale, sum.y * scale);
       if (GATHER) {
-        const unsigned calls = gather_calls(go);
-        const int64_t off = (int64_t)(calls & 1u) * go.half_stride + ((int64_t)go.rank * rows + row) * D + 2 * tid;
-        for (int w = 0; w < go.world; ++w) *reinterpret_cast<uint32_t*>(go.peers[w] + off) = hv;
+        gather_put(go, rows, row, 2 * tid, D, hv, gather_calls(go));
       } else {
         *reinterpret_cast<uint32_t*>(out16 + (int64_t)row * D + 2 * tid) = hv;
       }
@@ -1103,60 +1091,39 @@ __global__ __launch_bounds__(kCombineRowThreads) void combine_row_kernel(const f
       }
     }
   }
-  if (GATHER) {
-    __syncthreads();
-    gather_raise(go, row, row + 1, gather_calls(go));
-  }
 }
 
-// One block: waits (bounded) until every (rank, row) flag of this rank's current call has been
-// raised in the own region (acquire loads at system scope), copies the call's [world][rows][D] half to out (if
-// given), and advances the call counter that the next combine reads.
+// One block: every word of this rank's region for the current call (all ranks' rows) is polled until it carries the
+// call's flag (bounded; a word that never does raises the device error word), and its two fp16 outputs go to out
+// ([world][rows][D], when given). Then the call counter advances, even after a give-up, so the ranks stay in step.
 __global__ __launch_bounds__(1024) void gather_wait_kernel(__half* region, int world, int64_t half_stride, int rows,
                                                            __half* out) {
   pdl_wait();
   pdl_trigger();
-  unsigned* flags = gather_flags(region, half_stride);
-  unsigned* counter = flags + world * kGatherRows;
+  unsigned* counter = gather_counter(region, half_stride);
   const unsigned target = *reinterpret_cast<volatile unsigned*>(counter) + 1u;
-  __shared__ int s_fail;
-  if (threadIdx.x == 0) s_fail = 0;
-  __syncthreads();
-  for (int i = threadIdx.x; i < world * rows; i += blockDim.x) {
-    const unsigned* f = flags + (i / rows) * kGatherRows + i % rows;
-    const uint64_t t0 = globaltimer();
-    for (;;) {
-      unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if ((int)(v - target) >= 0) break;
-      if (globaltimer() - t0 > wait_limit_ns()) {
-        raise_error(kErrWaitPeer);
-        s_fail = 1;
-        break;
+  const unsigned long long* words = gather_words(region) + (int64_t)((target - 1u) & 1u) * half_stride;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(out);
+  bool gave_up = false;
+  for (int64_t i = threadIdx.x; i < half_stride && !gave_up; i += blockDim.x) {
+    unsigned long long wv;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(wv) : "l"(words + i) : "memory");
+    if ((unsigned)(wv >> 32) != target) {
+      const uint64_t t0 = globaltimer();
+      for (;;) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(wv) : "l"(words + i) : "memory");
+        if ((unsigned)(wv >> 32) == target) break;
+        if (globaltimer() - t0 > wait_limit_ns()) {
+          raise_error(kErrWaitPeer);
+          gave_up = true;
+          break;
+        }
       }
     }
+    if (dst && !gave_up) dst[i] = (uint32_t)wv;
   }
   __syncthreads();
-  if (!s_fail && out) {   // eight 16-byte loads in flight per thread, then their stores
-    const uint4* src = reinterpret_cast<const uint4*>(region + (int64_t)((target - 1u) & 1u) * half_stride);
-    uint4* dst = reinterpret_cast<uint4*>(out);
-    const int64_t n = half_stride / 8;
-    for (int64_t i0 = threadIdx.x; i0 < n; i0 += 8 * (int64_t)blockDim.x) {
-      uint4 v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int64_t i = i0 + (int64_t)u * blockDim.x;
-        if (i < n) v[u] = src[i];
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int64_t i = i0 + (int64_t)u * blockDim.x;
-        if (i < n) dst[i] = v[u];
-      }
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(counter) = target;   // even after a give-up: stay in step
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(counter) = target;
 }
 
 }  // namespace lfm3a

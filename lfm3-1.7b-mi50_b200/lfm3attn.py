@@ -111,6 +111,8 @@ SIGNATURES = {
     "lfm3a_verify_attention_gather": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, ctypes.POINTER(_P), _I, _I,
                                            _P, _SZ, _I, _P]),
     "lfm3a_gather_wait": (_I, [_P, _I, _I, _I, _P, _P]),
+    "lfm3a_verify_round_gather": (_I, [ctypes.POINTER(KvView), _P, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _P,
+                                       ctypes.POINTER(_P), _I, _I, _P, _SZ, _I, _P]),
     "lfm3a_pcache_create": (_I, [_I, _I, _I, ctypes.POINTER(_P)]),
     "lfm3a_pcache_destroy": (None, [_P]),
     "lfm3a_pcache_reset": (None, [_P]),
@@ -767,8 +769,26 @@ class GatherGroup:
                                                    _ptr(gate), self.peers, self.world, self.rank, _ptr(workspace),
                                                    ws_bytes, splits, _stream(stream)))
 
+    def verify_round(self, cache: "LayerCache", k, v, q, ctx_len: int, rope=None, k_norm=None, window: int = 0,
+                     gate=None, workspace=None, splits: int = 0, stream=None) -> None:
+        """This rank's verify round (the drafts' append fused into the attention), its output exchanged."""
+        import torch
+
+        m, qh, d = q.shape
+        if splits <= 0:
+            splits = verify_splits(cache.layout, ctx_len, m, window)
+        if workspace is None:
+            workspace = torch.zeros(lib().lfm3a_verify_workspace_bytes(m, qh, d, splits), dtype=torch.uint8,
+                                    device=q.device)
+        ws_bytes = workspace.numel() * workspace.element_size()
+        _check(lib().lfm3a_verify_round_gather(ctypes.byref(cache.view), _ptr(k), _ptr(v), 0, _ptr(rope), _ptr(k_norm),
+                                               _ptr(q), m, qh, ctx_len, window, _ptr(gate), self.peers, self.world,
+                                               self.rank, _ptr(workspace), ws_bytes, splits, _stream(stream)))
+        cache.length = max(cache.length, ctx_len + m)
+
     def wait(self, out=None, stream=None) -> None:
-        """Waits for every rank's slice of the latest call; copies [world][rows][head_dim] fp16 to out."""
+        """Waits for every rank's slice of the latest call; writes [world][rows][head_dim] fp16 to out (None: only
+        waits)."""
         _check(lib().lfm3a_gather_wait(self.region, self.world, self.rows, self.head_dim, _ptr(out), _stream(stream)))
 
     def unmap(self) -> None:

@@ -109,3 +109,55 @@ def test_gather_wait_runs_out_and_recovers(la, orc, synth, cuda):
     finally:
         for reg in regions:
             la.lib().lfm3a_gather_region_free(reg)
+
+
+def test_round_gather_two_emulated_ranks(la, orc, synth, cuda):
+    """lfm3a_verify_round_gather: each emulated rank appends its heads' drafts inside the attention kernel and
+    scatters its output; two rounds in a row (the second over the first's kept drafts); the gathered output against
+    the oracle's verify of all 8 heads, and the drafts' cache bytes bit-exact."""
+    import torch
+
+    ctx, m, world = 5000, 16, 2
+    c = synth.verify_case(64, ctx, m)
+    rope_np = la.rope_table(1e6, 1.0, 64, ctx + 2 * m + 1)
+    rope = dev(rope_np.view(np.float16), cuda)
+    rows = m * 16
+    regions = [la.GatherGroup.alloc_region(world, rows, 64) for _ in range(world)]
+    try:
+        groups = [la.GatherGroup(world, r, rows, 64, regions=regions) for r in range(world)]
+        caches = []
+        for r in range(world):
+            h0, h1 = head_range(world, r, 8)
+            cache = la.LayerCache(la.MODE_F16, h1 - h0, 64, ctx + 2 * m + 64, device=cuda)
+            cache.append(dev(c["K"][:, h0:h1], cuda), dev(c["V"][:, h0:h1], cuda), 0)
+            caches.append(cache)
+        K, V = c["K"], c["V"]
+        s = synth.Stream(65)
+        length = ctx
+        for rnd in range(2):
+            nk, nv = (c["newK"], c["newV"]) if rnd == 0 else (s.normal_f16((m, 8, 64)), s.normal_f16((m, 8, 64)))
+            Q = c["Q"] if rnd == 0 else s.normal_f16((m, 32, 64))
+            for r in range(world):
+                h0, h1 = head_range(world, r, 8)
+                q0, q1 = query_head_range(world, r, 8, 32)
+                groups[r].verify_round(caches[r], dev(nk[:, h0:h1], cuda), dev(nv[:, h0:h1], cuda),
+                                       dev(Q[:, q0:q1], cuda), length, rope=rope)
+            kn, vn = orc.kv_append_f16(nk, nv, length, rope=rope_np.view(np.float16))
+            K = np.concatenate([K[:length], kn])
+            V = np.concatenate([V[:length], vn])
+            want = orc.verify(Q, K, V, length)
+            for r in range(world):
+                out = torch.zeros((world, m, 16, 64), dtype=torch.float16, device=cuda)
+                groups[r].wait(out)
+                la.sync()
+                got = out.permute(1, 0, 2, 3).reshape(m, 32, 64).float().cpu().numpy()
+                assert rel_err(got, want) < 4e-3, (rnd, r)
+            for r in range(world):
+                h0, h1 = head_range(world, r, 8)
+                caches[r].truncate(length + 5)
+                logical = caches[r].logical(length + 5)
+                assert np.array_equal(logical["K"][length:], K[length:length + 5, h0:h1].view(np.uint16))
+            length += 5
+    finally:
+        for reg in regions:
+            la.lib().lfm3a_gather_region_free(reg)
