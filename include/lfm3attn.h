@@ -146,8 +146,7 @@ int lfm3a_verify_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int w
  * [m][q_heads] logits (out *= sigmoid) or NULL. out: device fp16 [m][q_heads][head_dim].
  * workspace: lfm3a_verify_workspace_bytes bytes when splits > 1 (may be NULL for one split).
  * MODE_F16, q_heads = 4 * kv_heads; head_dim 64 with 1 <= m <= 32, or head_dim 128 (the reference model's
- * 16/4/128 geometry) with 1 <= m <= 16. The same holds for the other verify entry points below, except the
- * gather exchange (head_dim 64). */
+ * 16/4/128 geometry) with 1 <= m <= 16. The same holds for the other verify entry points below. */
 int lfm3a_verify_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int ctx_len, int window,
                            const void* gate, void* out, void* workspace, size_t workspace_bytes, int splits,
                            void* stream);
@@ -193,8 +192,8 @@ int lfm3a_combine(const float* partials, int rows, int splits, int head_dim, int
 /* One DSpark verify round's device work in one call: lfm3a_kv_append of the m drafts (k, v, token_stride,
  * rope, k_norm as there) at positions ctx_len .. ctx_len + m - 1, then lfm3a_verify_attention of q over
  * them (the reference's query_fresh then attention phases of one launch, kernels/dspark.hip:999-1061,
- * 1488-2185). For m <= 16 the append runs inside the attention kernel, in the CTA of each kv head whose
- * keys include the drafts (when the split leaves it every 64-token block they touch; else the append
+ * 1488-2185). For m <= 16 (head_dim 64 or 128) the append runs inside the attention kernel, in the CTA of each
+ * kv head whose keys include the drafts (when the split leaves it every 64-token block they touch; else the append
  * kernel runs first); the cache bytes and the output are the same as the two calls'. */
 int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, int64_t token_stride, const void* rope,
                        const void* k_norm, const void* q, int m, int q_heads, int ctx_len, int window, const void* gate,
@@ -291,7 +290,7 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
  *
  * A gather region holds [2][world][rows][head_dim / 2] such words (the exchanges of even and odd calls), then a
  * call counter. It must be its own allocation (so that other processes can map it) and start zeroed:
- * lfm3a_gather_region_alloc gives one. head_dim 64, at most 1024 rows. */
+ * lfm3a_gather_region_alloc gives one. head_dim 64 or 128, at most 1024 rows. */
 size_t lfm3a_gather_region_bytes(int world, int rows, int head_dim);
 int lfm3a_gather_region_alloc(int world, int rows, int head_dim, void** region_out);
 int lfm3a_gather_region_free(void* region);

@@ -139,7 +139,8 @@ int launch_combine(const float* part, int rows, int splits, int head_dim, int64_
       launch_pdl(kernel, (rows + rows_per_block - 1) / rows_per_block, 256, 0, st, part, rows, splits, split_stride,
                  row_stride, gate, out16, out32, go);
     };
-    if (gather) run(combine_kernel<64, true>, 4);   // the kv-head plan's scatter to the ranks' regions (head_dim 64)
+    if (gather && head_dim == 64) run(combine_kernel<64, true>, 4);   // the kv-head plan's scatter to the regions
+    else if (gather) run(combine_kernel<128, true>, 2);
     else if (head_dim == 64) run(combine_kernel<64, false>, 4);
     else run(combine_kernel<128, false>, 2);
   } else {              // a block per row, the splits spread over its threads
@@ -148,7 +149,8 @@ int launch_combine(const float* part, int rows, int splits, int head_dim, int64_
                  split_stride, row_stride, gate, out16, out32, go);
     };
     if (splits > 12288) return fail(LFM3A_EINVAL, "combine: at most 12288 splits");
-    if (gather) run(combine_row_kernel<64, true>);
+    if (gather && head_dim == 64) run(combine_row_kernel<64, true>);
+    else if (gather) run(combine_row_kernel<128, true>);
     else if (head_dim == 64) run(combine_row_kernel<64, false>);
     else run(combine_row_kernel<128, false>);
   }
@@ -172,7 +174,6 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
     return fail(LFM3A_ENOTSUP, "verify attention needs MODE_F16 and head_dim 64 (or 128 for up to 16 tokens)");
   if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "verify attention needs 4 query heads per kv head");
   const int D = L.head_dim;
-  if (gather && D != 64) return fail(LFM3A_ENOTSUP, "the gather exchange needs head_dim 64");
   if (!q || (!out16 && !out32 && !gather) || m < 1 || m > 32 || ctx_len < 0 || window < 0)
     return fail(LFM3A_EINVAL, "bad verify arguments");
   if (kv_begin < 0 || kv_end <= kv_begin || kv_end > ctx_len + m) return fail(LFM3A_EINVAL, "bad key range");
@@ -209,7 +210,7 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
     // The exchange runs in the combine: one split would leave no combine to scatter the rows.
     if (a.splits < 2 && a.t_total >= 2) a.splits = 2;
     if (a.splits < 2) return fail(LFM3A_ENOTSUP, "the gather needs several splits (a combine): context too short");
-    gather->half_stride = (int64_t)gather->world * rows * 32;   // 8-byte words: two of the 64 dims each
+    gather->half_stride = (int64_t)gather->world * rows * (D / 2);   // 8-byte words: two dims each
   }
   // One split with fp16 output writes straight to out; otherwise the splits go to the workspace.
   if (a.splits == 1 && out32) {
@@ -235,7 +236,7 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
     const int lighten = a.splits > 1 && a.t_total / a.splits >= kAppendTiles + 2 ? kAppendTiles : 0;
     const int span = a.t_total + lighten;
     const int last_tile0 = a.t_begin + std::min(a.t_total, (int)((int64_t)span * (a.splits - 1) / a.splits));
-    const bool fuse = m <= 16 && D == 64 && last_tile0 * tile_keys <= app->pos0 / kQuantBlock * kQuantBlock;
+    const bool fuse = m <= 16 && last_tile0 * tile_keys <= app->pos0 / kQuantBlock * kQuantBlock;
     if (fuse) {
       a.append = 1;
       a.lighten = lighten;
@@ -731,7 +732,8 @@ int lfm3a_gather_wait(void* region, int world, int rows, int head_dim, void* out
   if (!region || world < 1 || world > 8 || rows < 1 || head_dim < 1 || (out && !aligned16(out)))
     return fail(LFM3A_EINVAL, "bad gather wait arguments");
   const int64_t half_stride = (int64_t)world * rows * (head_dim / 2);
-  if (head_dim != 64 || rows > kGatherMaxRows) return fail(LFM3A_ENOTSUP, "gather: head_dim 64, at most 1024 rows");
+  if ((head_dim != 64 && head_dim != 128) || rows > kGatherMaxRows)
+    return fail(LFM3A_ENOTSUP, "gather: head_dim 64 or 128, at most 1024 rows");
   launch_pdl(gather_wait_kernel, 1, 1024, 0, as_stream(stream), static_cast<__half*>(region), world, half_stride, rows,
              static_cast<__half*>(out));
   return check_launch("gather_wait_kernel");

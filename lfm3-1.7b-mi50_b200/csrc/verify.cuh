@@ -547,16 +547,18 @@ __global__ __launch_bounds__(kVfThreads, V6Layout<D>::kBlocksPerSm) void verify_
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
     }
-    if constexpr (D == 64) if (appender) {
+    if (appender) {
       // The drafts' K (RoPE) and V into their pages, and the int8 V of every 64-token block they touch, by
       // the 256 softmax threads while the first K tile loads; the P buffers are the scratch (P is first
-      // written after this). The stores are handed to the producer's bulk copies through app_done.
+      // written after this: 64 tokens x D halves, then the reduction slots). The stores are handed to the
+      // producer's bulk copies through app_done.
+      static_assert(kQuantBlock * D * sizeof(__half) + 64 <= 2 * L6::kPBuf, "append scratch in the P buffers");
       __half* sv = reinterpret_cast<__half*>(sP);
-      float* red = reinterpret_cast<float*>(sP + kQuantBlock * 64 * sizeof(__half));
+      float* red = reinterpret_cast<float*>(sP + kQuantBlock * D * sizeof(__half));
       auto sync = [] { named_bar_sync(2, kVfSoftmaxWarps * 32); };
       const int qb0 = a.app.pos0 / kQuantBlock, qb1 = (a.app.pos0 + a.app.n - 1) / kQuantBlock;
       for (int qb = qb0; qb <= qb1; ++qb) {
-        append_quant_block<64>(a.app, qb, h, threadIdx.x, sv, red, sync);
+        append_quant_block<D>(a.app, qb, h, threadIdx.x, sv, red, sync);
         sync();   // sv and red are reused by the next block, then by P
       }
       asm volatile("fence.proxy.async.global;" ::: "memory");

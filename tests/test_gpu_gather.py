@@ -161,3 +161,35 @@ def test_round_gather_two_emulated_ranks(la, orc, synth, cuda):
     finally:
         for reg in regions:
             la.lib().lfm3a_gather_region_free(reg)
+
+
+def test_gather_head_dim_128(la, orc, synth, cuda):
+    """The exchange at the reference model's 16/4/128 geometry: two emulated ranks of two kv heads each, rounds with
+    the drafts' append fused into the attention kernel, the gathered output against the oracle's verify."""
+    import torch
+
+    ctx, m, world, d = 7000, 9, 2, 128
+    c = synth.verify_case(66, ctx, m, q_heads=16, kv_heads=4, head_dim=d)
+    rope_np = la.rope_table(1e6, 0.5, d, ctx + m + 1)
+    rows = m * 8
+    regions = [la.GatherGroup.alloc_region(world, rows, d) for _ in range(world)]
+    try:
+        groups = [la.GatherGroup(world, r, rows, d, regions=regions) for r in range(world)]
+        for r in range(world):
+            h0, h1 = head_range(world, r, 4)
+            q0, q1 = query_head_range(world, r, 4, 16)
+            cache = la.LayerCache(la.MODE_F16, h1 - h0, d, ctx + m + 64, device=cuda)
+            cache.append(dev(c["K"][:, h0:h1], cuda), dev(c["V"][:, h0:h1], cuda), 0)
+            groups[r].verify_round(cache, dev(c["newK"][:, h0:h1], cuda), dev(c["newV"][:, h0:h1], cuda),
+                                   dev(c["Q"][:, q0:q1], cuda), ctx, rope=dev(rope_np.view(np.float16), cuda))
+        kn, vn = orc.kv_append_f16(c["newK"], c["newV"], ctx, rope=rope_np.view(np.float16))
+        want = orc.verify(c["Q"], np.concatenate([c["K"], kn]), np.concatenate([c["V"], vn]), ctx)
+        for r in range(world):
+            out = torch.zeros((world, m, 8, d), dtype=torch.float16, device=cuda)
+            groups[r].wait(out)
+            la.sync()
+            got = out.permute(1, 0, 2, 3).reshape(m, 16, d).float().cpu().numpy()
+            assert rel_err(got, want) < 4e-3, r
+    finally:
+        for reg in regions:
+            la.lib().lfm3a_gather_region_free(reg)

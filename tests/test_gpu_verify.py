@@ -308,11 +308,13 @@ def test_verify_head_dim_128_rejects_more_than_16_tokens(la, synth, cuda):
     assert e.value.code == la.ENOTSUP
 
 
-def test_verify_round_head_dim_128(la, orc, synth, cuda):
-    """A verify round at the reference geometry: the drafts' append (its own kernel at head_dim 128), the attention
+@pytest.mark.parametrize("ctx", [3000, 40000])
+def test_verify_round_head_dim_128(la, orc, synth, cuda, ctx):
+    """A verify round at the reference geometry: the drafts' append (inside the attention kernel, in the last split
+    of each kv head; at 40000 tokens that split also gives two tiles of attention to the others), the attention
     and the rollback; the cache bytes after the round are the oracle's, bit for bit."""
-    ctx, m = 3000, 8
-    case = synth.verify_case(74, ctx, m, q_heads=16, kv_heads=4, head_dim=128)
+    m = 8
+    case = synth.verify_case(74 + ctx % 7, ctx, m, q_heads=16, kv_heads=4, head_dim=128)
     cache = la.LayerCache(la.MODE_F16, 4, 128, ctx + 128, device=cuda)
     rope_np = la.rope_table(1e6, 0.5, 128, ctx + m + 1)
     cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
