@@ -1109,14 +1109,15 @@ def run_ours(args):
     hout = torch.empty(res.shape, dtype=torch.float16).pin_memory()
     direct = world == 1 and fused_round
     if direct:
-        # One GPU: the round is the two C-ABI calls the engine makes (lfm3a_verify_round, lfm3a_kv_truncate), with
-        # their arguments prepared once, as a caller that keeps its layer views does.
+        # One GPU: the round with host buffers is one C-ABI call (lfm3a_verify_round_host: the drafts' copy in, the
+        # round, the output's copy out, the stream wait), then the rollback (lfm3a_kv_truncate), with the arguments
+        # prepared once, as a caller that keeps its layer views does.
         lib = la.lib()
         views = [ctypes.byref(c.view) for c in caches]
         st_ptr = torch.cuda.current_stream().cuda_stream
         ws_bytes = ws.numel()
-        call_args = (dk.data_ptr(), dv.data_ptr(), 0, rope.data_ptr(), None, dq.data_ptr(), M, QH, R.ctx_len, 0, None,
-                     out.data_ptr(), ws.data_ptr(), ws_bytes, splits, st_ptr)
+        call_args = (hin.data_ptr(), din.data_ptr(), rope.data_ptr(), None, M, QH, R.ctx_len, 0, None, out.data_ptr(),
+                     hout.data_ptr(), ws.data_ptr(), ws_bytes, splits, st_ptr, 10000)
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
@@ -1126,14 +1127,14 @@ def run_ours(args):
     s0.record()
     rc_e2e = 0
     for i in range(e2e_steps):
-        din.copy_(hin, non_blocking=True)
         if direct:
-            rc_e2e |= lib.lfm3a_verify_round(views[i % n_layers], *call_args)
+            rc_e2e |= lib.lfm3a_verify_round_host(views[i % n_layers], *call_args)
             rc_e2e |= lib.lfm3a_kv_truncate(views[i % n_layers], R.ctx_len, st_ptr)
         else:
+            din.copy_(hin, non_blocking=True)
             step(caches[i % n_layers], None, dq, dk, dv)
-        hout.copy_(res, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+            hout.copy_(res, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
     s1.record()
     torch.cuda.synchronize()
     if rc_e2e:
@@ -1235,8 +1236,9 @@ def run_ours(args):
                     "us_per_layer": round(e2e_ms * 1e3, 2), "wall_us_per_layer": round(e2e_wall_ms * 1e3, 2),
                     "h2d_bytes_per_step": int(hin.numel() * 2),
                     "d2h_bytes_per_step": int(hout.numel() * 2),
-                    "how": ("one pinned-host copy of the drafts' q, k, v, lfm3a_verify_round + lfm3a_kv_truncate "
-                            "through ctypes, the output read back, a stream sync per step" if direct else
+                    "how": ("per step lfm3a_verify_round_host (one copy of the drafts' q, k, v from pinned host "
+                            "memory, the round, the output copied back to pinned host memory, the stream waited "
+                            "for) + lfm3a_kv_truncate, through ctypes" if direct else
                             "one pinned-host copy of this rank's drafts' q, k, v, the plan's step (LayerCache calls "
                             "and the exchange), the exchanged output read back, a stream sync per step")},
             "gpu_launches": int(launches_per_step * K),

@@ -199,6 +199,18 @@ int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, in
                        const void* k_norm, const void* q, int m, int q_heads, int ctx_len, int window, const void* gate,
                        void* out, void* workspace, size_t workspace_bytes, int splits, void* stream);
 
+/* lfm3a_verify_round with host buffers, in one call, for a caller whose drafts come from the host (and for the
+ * end-to-end leg of the benchmark): copies host_in, the drafts' q then k then v (fp16 [m][q_heads][head_dim],
+ * [m][kv_heads][head_dim], [m][kv_heads][head_dim], contiguous), into dev_in (device, 16-byte aligned, as many
+ * bytes), runs lfm3a_verify_round on them (out: device fp16 [m][q_heads][head_dim]), then copies out into
+ * host_out, all on stream. host_in and host_out should be pinned. timeout_ms >= 0: returns once the stream is
+ * done (LFM3A_ETIMEOUT after timeout_ms); < 0: returns at once. A kernel that gave up a bounded wait is reported
+ * by the next lfm3a_sync. No reference counterpart: the reference's drafts are produced on the GPU. */
+int lfm3a_verify_round_host(const lfm3a_kv_view* kv, const void* host_in, void* dev_in, const void* rope,
+                            const void* k_norm, int m, int q_heads, int ctx_len, int window, const void* gate,
+                            void* out, void* host_out, void* workspace, size_t workspace_bytes, int splits,
+                            void* stream, int timeout_ms);
+
 /* ---------------------------------------------------------------- the reference's arithmetic (MODE_I8REC)
  * Attention over the reference's own cache bytes with its own arithmetic: int8 queries per 32-dim group against
  * the int8 K of the 264-byte records, fp16 probabilities carrying the V scale times 4096 against the int8 V. */
@@ -249,8 +261,8 @@ size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim);
 /* The number of key splits lfm3a_prefill_attention uses for a chunk (the counterpart of attnSplits,
  * internal/model/prefill.go:37-46): 1 when the chunk's CTAs (one per 32 query tokens and kv head) fill
  * one wave of two per SM; else enough splits for one wave, each with at least 8 key tiles of the shortest
- * row band, at most 64. sm_count 0: the current device's. At head_dim 128 the kernels run one CTA per SM:
- * their split count is this function's with half the SM count. */
+ * row band, at most 64. sm_count 0: the current device's. At head_dim 128 the exact kernel also runs two CTAs
+ * per SM (this count); the int8-PV kernel runs one: its count is this function's with half the SM count. */
 int lfm3a_prefill_splits(int tokens, int q_heads, int context, int window, int sm_count);
 
 /* Causal (optionally sliding-window) prefill attention of tokens query tokens at positions

@@ -179,7 +179,9 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
         const uint2 kb = *reinterpret_cast<const uint2*>(krec + 32 * g + 8 * tig);
-        dg[g][0] = dg[g][1] = dg[g][2] = dg[g][3] = 0;
+        // The dot accumulates onto the bits of 1.5 * 2^23 (|dot| <= 32 * 127 * 128 < 2^22): read as fp32 that is
+        // 1.5 * 2^23 + dot exactly, so one FADD converts it (no I2F on the XU pipe).
+        dg[g][0] = dg[g][1] = dg[g][2] = dg[g][3] = 0x4B400000;
         mma_s8_16832(dg[g], qa[g], kb.x, kb.y);
       }
       // the C fragment: (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1) of the n-tile
@@ -188,8 +190,11 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float* qs = e < 2 ? qsA : qsB;
-        float v = fmaf((float)dg[1][e], qs[1], (float)dg[0][e] * qs[0]);
-        if (NG == 4) v = v + fmaf((float)dg[3][e], qs[3], (float)dg[2][e] * qs[2]);
+        float d[NG];
+#pragma unroll
+        for (int g = 0; g < NG; ++g) d[g] = __int_as_float(dg[g][e]) - 12582912.f;
+        float v = fmaf(d[1], qs[1], d[0] * qs[0]);
+        if (NG == 4) v = v + fmaf(d[3], qs[3], d[2] * qs[2]);
         s[n][e] = v * ((e & 1) ? ksc1 : ksc0);
       }
     }

@@ -564,6 +564,36 @@ int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, in
                     workspace, workspace_bytes, splits, as_stream(stream), nullptr, true, &app);
 }
 
+int lfm3a_verify_round_host(const lfm3a_kv_view* kv, const void* host_in, void* dev_in, const void* rope,
+                            const void* k_norm, int m, int q_heads, int ctx_len, int window, const void* gate,
+                            void* out, void* host_out, void* workspace, size_t workspace_bytes, int splits,
+                            void* stream, int timeout_ms) {
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  if (!host_in || !dev_in || !out || !host_out || m < 1 || q_heads < 1)
+    return fail(LFM3A_EINVAL, "bad host round arguments");
+  if (!aligned16(dev_in)) return fail(LFM3A_EINVAL, "dev_in must be 16-byte aligned");
+  const int D = kv->layout.head_dim, H = kv->layout.kv_heads;
+  const size_t qb = (size_t)m * q_heads * D * sizeof(__half), kb = (size_t)m * H * D * sizeof(__half);
+  const cudaStream_t st = as_stream(stream);
+  cudaError_t e = cudaMemcpyAsync(dev_in, host_in, qb + 2 * kb, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (drafts to the device)");
+  const char* d = static_cast<const char*>(dev_in);
+  rc = lfm3a_verify_round(kv, d + qb, d + qb + kb, 0, rope, k_norm, d, m, q_heads, ctx_len, window, gate, out,
+                          workspace, workspace_bytes, splits, stream);
+  if (rc != LFM3A_OK) return rc;
+  e = cudaMemcpyAsync(host_out, out, qb, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (output to the host)");
+  if (timeout_ms < 0) return LFM3A_OK;
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+  for (;;) {
+    e = cudaStreamQuery(st);
+    if (e == cudaSuccess) return LFM3A_OK;
+    if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
+    if (std::chrono::steady_clock::now() > deadline) return fail(LFM3A_ETIMEOUT, "stream still busy at the deadline");
+  }
+}
+
 int lfm3a_ring_table(int ring_blocks, int logical_blocks, int32_t* table) {
   if (ring_blocks < 2 || ring_blocks % 2 != 0 || logical_blocks < 0 || (!table && logical_blocks > 0))
     return fail(LFM3A_EINVAL, "a ring needs an even number of blocks (whole 64-token int8 V blocks)");
@@ -581,7 +611,10 @@ int lfm3a_ring_attention(const lfm3a_kv_view* kv, const void* q, int m, int q_he
 size_t lfm3a_prefill_workspace_bytes(int tokens, int q_heads, int head_dim) {
   if (tokens <= 0 || q_heads < 4 || (head_dim != 64 && head_dim != 128)) return 0;
   // The most splits any context can get for this chunk (the long-context bound of prefill_splits_for).
-  const int splits = prefill_splits_for(tokens, q_heads / 4, 1 << 30, 0, current_sm_count(), head_dim == 64 ? 2 : 1);
+  // Head_dim 128 runs two CTAs per SM (exact) or one (int8-PV): the larger of the two counts.
+  const int sms = current_sm_count();
+  const int splits = std::max(prefill_splits_for(tokens, q_heads / 4, 1 << 30, 0, sms, 2),
+                              head_dim == 64 ? 1 : prefill_splits_for(tokens, q_heads / 4, 1 << 30, 0, sms, 1));
   return splits > 1 ? (size_t)tokens * q_heads * splits * (head_dim + 2) * sizeof(float) : 0;
 }
 
@@ -610,7 +643,7 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
   if (tokens == 0) return LFM3A_OK;
   if (!aligned16(q) || !aligned16(out)) return fail(LFM3A_EINVAL, "q and out must be 16-byte aligned");
   // Key splits when the chunk alone leaves the GPU short of CTAs and the caller gave the workspace for them.
-  int splits = prefill_splits_for(tokens, L.kv_heads, context, window, current_sm_count(), D == 64 ? 2 : 1);
+  int splits = prefill_splits_for(tokens, L.kv_heads, context, window, current_sm_count(), (D == 64 || exact) ? 2 : 1);
   const size_t need = (size_t)tokens * q_heads * splits * (D + 2) * sizeof(float);
   if (splits > 1 && (!workspace || !aligned16(workspace) || workspace_bytes < need)) splits = 1;
   float* part = splits > 1 ? static_cast<float*>(workspace) : nullptr;

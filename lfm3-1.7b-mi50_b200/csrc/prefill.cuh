@@ -206,25 +206,34 @@ struct PfLayout {
   static constexpr int kProducerWarp = I8 ? 8 : 4;
   static constexpr int kMmaWarp = I8 ? 9 : 5;
   static constexpr int kThreads = (kMmaWarp + 1) * 32;
+  // Head_dim-128 exact: two-stage rings and one P buffer, so that two CTAs share an SM (112.2 KiB each;
+  // with four stages and two P buffers it took 192 KiB and ran alone). The softmax then waits for the previous
+  // PV to have read P before it writes the next.
+  static constexpr bool kCompact = D == 128 && !I8;
+  static constexpr int kStages = kCompact ? 2 : kPfStages;
+  static constexpr int kPBufs = kCompact ? 1 : 2;
   static constexpr int kQBytes = 256 * D;              // 128 rows x D dims fp16
   static constexpr int kPage = 64 * D;                 // one page's K (or fp16 V) section: 32 keys x D
   static constexpr int kKStage = 2 * kPage;            // K of 64 keys: two 32-token pages
   static constexpr int kVStage = I8 ? kPage : 2 * kPage;   // V (or int8 V) of the same keys
   static constexpr int kPBuf = I8 ? 8192 : 16384;      // 128 rows x 64 keys, u8 or fp16
   static constexpr int kOffK = kQBytes;
-  static constexpr int kOffV = kOffK + kPfStages * kKStage;
-  static constexpr int kOffP = kOffV + kPfStages * kVStage;
-  static constexpr int kOffSc = kOffP + 2 * kPBuf;     // int8: [2][128] (corr, scale) of a tile, softmax -> epilogue
+  static constexpr int kOffV = kOffK + kStages * kKStage;
+  static constexpr int kOffP = kOffV + kStages * kVStage;
+  static constexpr int kOffSc = kOffP + kPBufs * kPBuf;   // int8: [2][128] (corr, scale) of a tile, softmax -> epilogue
   static constexpr int kOffL = kOffSc + (I8 ? 2 * 128 * 8 : 0);   // int8: row sums and maxima for the epilogue
   static constexpr int kOffBar = kOffL + (I8 ? 256 * 4 : 0);   // int8: [128] sums, [128] running maxima
-  static constexpr int kBars = 4 * kPfStages + 2 + 4 + 2 + 2 + 2;
+  static constexpr int kBars = 4 * kStages + 2 + 4 + 2 + 2 + 2;
   static constexpr int kOffTmemSlot = kOffBar + kBars * 8;
   static constexpr int kOffAbort = kOffTmemSlot + 8;   // in the dynamic region: static shared memory would
   static constexpr int kBytes = kOffTmemSlot + 16;      // pad to the 1 KiB alignment and cost the second CTA
   // Head_dim 64: enough shared memory that two CTAs share an SM and a third cannot (TMEM holds 2 x 256 columns).
-  // Head_dim 128: one CTA per SM (its shared memory alone rules out a second).
+  // Head_dim 128 exact: two CTAs (the compact rings, 256 TMEM columns each). Head_dim-128 int8: one CTA per SM
+  // (its 512 TMEM columns and shared memory rule out a second).
   static constexpr int kRequest = D == 64 ? (kBytes > 80 * 1024 ? kBytes : 80 * 1024) : kBytes;
-  static constexpr int kBlocksPerSm = D == 64 ? 2 : 1;
+  static constexpr int kBlocksPerSm = (D == 64 || kCompact) ? 2 : 1;
+  // An SM has 228 KiB of shared memory, 1 KiB of it reserved per resident CTA.
+  static_assert(!kCompact || 2 * (kBytes + 1024) <= 228 * 1024, "two head_dim-128 CTAs must share an SM");
   // TMEM: S[2] at 0 and 64; exact O at 128; int8 Dpv (s32) at 128 and the fp32 accumulator at 128 + D.
   static constexpr uint32_t kTmemCols = (I8 && D == 128) ? 512 : 256;
   static constexpr int kAcc = 128 + D;                 // int8: first fp32 accumulator column
@@ -242,7 +251,7 @@ struct PfLayout {
 template <int D, bool I8, bool SPLIT, bool GLUE>
 __global__ __launch_bounds__(PfLayout<D, I8>::kThreads, PfLayout<D, I8>::kBlocksPerSm) void prefill_kernel(PrefillArgs a) {
   using L = PfLayout<D, I8>;
-  constexpr int NS = kPfStages;
+  constexpr int NS = L::kStages;
   constexpr uint32_t kTmemCols = L::kTmemCols;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* sQ = smem;
@@ -420,7 +429,14 @@ __global__ __launch_bounds__(PfLayout<D, I8>::kThreads, PfLayout<D, I8>::kBlocks
       }
       l_run += (ls01.x + ls01.y) + (ls23.x + ls23.y);
       // P[b] was last read by PV(jt - 2), issued before QK(jt): the commit that signalled S(jt) covers it.
-      uint8_t* pb = sP + b * L::kPBuf;
+      // With one P buffer, PV(jt - 1) must have read it: wait for its commit (already done when O was rescaled).
+      if (L::kPBufs == 1 && jt >= 1 &&
+          !__all_sync(0xffffffffu, mbar_wait(&pv_done[(jt - 1) & 1], (uint32_t)((jt - 1) >> 1) & 1u))) {
+        raise_error(kErrWaitMma);
+        ok = false;
+        break;
+      }
+      uint8_t* pb = sP + (L::kPBufs == 2 ? b : 0) * L::kPBuf;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint4 v;
@@ -834,7 +850,7 @@ __global__ __launch_bounds__(PfLayout<D, I8>::kThreads, PfLayout<D, I8>::kBlocks
           break;
         }
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + bp * L::kPBuf);
+        const uint32_t p_addr = smem_u32(sP + (L::kPBufs == 2 ? bp : 0) * L::kPBuf);
         const uint32_t v_addr = smem_u32(sV + st * L::kVStage);
         if (!I8) {
           const uint64_t p_desc = umma_desc(p_addr, 128, 1024), v_desc = umma_desc(v_addr, 128, 512);

@@ -84,6 +84,8 @@ SIGNATURES = {
     "lfm3a_combine": (_I, [_P, _I, _I, _I, _I64, _I64, _P, _P, _P]),
     "lfm3a_verify_round": (_I, [ctypes.POINTER(KvView), _P, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _SZ, _I,
                                 _P]),
+    "lfm3a_verify_round_host": (_I, [ctypes.POINTER(KvView), _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _SZ,
+                                     _I, _P, _I]),
     "lfm3a_ring_table": (_I, [_I, _I, _P]),
     "lfm3a_ring_attention": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_prefill_workspace_bytes": (_SZ, [_I, _I, _I]),
@@ -302,6 +304,32 @@ class LayerCache:
         _check(lib().lfm3a_verify_round(ctypes.byref(self.view), _ptr(k), _ptr(v), 0, _ptr(rope), _ptr(k_norm), _ptr(q),
                                         m, qh, ctx_len, window, _ptr(gate), _ptr(out), _ptr(workspace), ws_bytes,
                                         splits, _stream(stream)))
+        self.length = max(self.length, ctx_len + m)
+        return out
+
+    def verify_round_host(self, host_in, dev_in, host_out, m: int, q_heads: int, ctx_len: int, rope=None,
+                          k_norm=None, window: int = 0, gate=None, out=None, workspace=None, splits: int = 0,
+                          stream=None, timeout_ms: int = 10000):
+        """verify_round with host buffers in one library call: host_in (pinned fp16: the drafts' q, then k, then v,
+        contiguous) is copied into dev_in, the round runs, its output is copied into host_out (pinned fp16
+        [m][q_heads][head_dim]), and the call waits for the stream (timeout_ms >= 0)."""
+        import torch
+
+        d = self.head_dim
+        if out is None:
+            out = torch.empty((m, q_heads, d), dtype=torch.float16, device=dev_in.device)
+        if ctx_len + m > self.capacity:
+            raise LFM3AError(EINVAL, "append past the cache capacity")
+        if splits <= 0:
+            splits = verify_splits(self.layout, ctx_len, m, window)
+        if workspace is None and splits > 1:
+            workspace = torch.zeros(lib().lfm3a_verify_workspace_bytes(m, q_heads, d, splits), dtype=torch.uint8,
+                                    device=dev_in.device)
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib().lfm3a_verify_round_host(ctypes.byref(self.view), _ptr(host_in), _ptr(dev_in), _ptr(rope),
+                                             _ptr(k_norm), m, q_heads, ctx_len, window, _ptr(gate), _ptr(out),
+                                             _ptr(host_out), _ptr(workspace), ws_bytes, splits, _stream(stream),
+                                             timeout_ms))
         self.length = max(self.length, ctx_len + m)
         return out
 

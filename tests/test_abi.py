@@ -74,6 +74,12 @@ def test_argument_checks_without_device(la):
     assert lib.lfm3a_combine(None, 4, 2, 64, 0, 0, None, 64, None) == la.EINVAL
     assert lib.lfm3a_kv_truncate(ctypes.byref(good), -1, None) == la.EINVAL
     assert b"negative" in lib.lfm3a_last_error()
+    # the host-buffer round checks its buffers before any copy: no host input, a misaligned device staging buffer
+    assert lib.lfm3a_verify_round_host(ctypes.byref(good), None, 64, None, None, 16, 32, 100, 0, None, 64, 64, None,
+                                       0, 1, None, 0) == la.EINVAL
+    assert lib.lfm3a_verify_round_host(ctypes.byref(good), 64, 72, None, None, 16, 32, 100, 0, None, 64, 64, None,
+                                       0, 1, None, 0) == la.EINVAL
+    assert b"aligned" in lib.lfm3a_last_error()
     lay = la.layout(0, 8, 64)
     view_bad_stride = la.KvView(64, 64, 10, la.KvLayout(0, 8, 64, 32, 10000, 80000))
     assert lib.lfm3a_kv_truncate(ctypes.byref(view_bad_stride), 5, None) == la.EINVAL

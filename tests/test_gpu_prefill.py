@@ -143,8 +143,9 @@ def test_prefill_fused_glue(la, orc, synth, cuda, context, T, exact):
 
 
 # ---------------------------------------------------------------- the reference model's geometry
-# 16 query heads, 4 kv heads, head_dim 128 (internal/model/engine.go:22-40). Both variants run one CTA per SM
-# there, so a chunk's key splits follow lfm3a_prefill_splits with half the SM count.
+# 16 query heads, 4 kv heads, head_dim 128 (internal/model/engine.go:22-40). The exact kernel runs two CTAs per
+# SM there, as at head_dim 64; the int8-PV kernel one, so its key splits follow lfm3a_prefill_splits with half the
+# SM count.
 def run_ref(la, synth, cuda, seed, context, T, window, exact):
     case = synth.prefill_case(seed, context + T, q_heads=16, kv_heads=4, head_dim=128)
     cache = la.LayerCache(la.MODE_F16, 4, 128, context + T + 64, device=cuda)
@@ -178,8 +179,8 @@ def test_prefill_head_dim_128(la, orc, synth, cuda, context, T, window, exact):
 def test_prefill_head_dim_128_key_splits(la, orc, synth, cuda, context, T, exact):
     import torch
 
-    half_sms = torch.cuda.get_device_properties(cuda).multi_processor_count // 2
-    splits = la.lib().lfm3a_prefill_splits(T, 16, context, 0, half_sms)
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    splits = la.lib().lfm3a_prefill_splits(T, 16, context, 0, sms if exact else sms // 2)
     assert splits > 1
     case, _, got = run_ref(la, synth, cuda, 110 + T, context, T, 0, exact)
     q = case["Q"][context:]

@@ -238,6 +238,42 @@ def test_verify_round_matches_two_calls(la, orc, synth, cuda, ctx_len, m, splits
         plain.truncate(length)
 
 
+@pytest.mark.parametrize("d,ctx_len", [(64, 3000), (128, 2000)])
+def test_verify_round_host(la, orc, synth, cuda, d, ctx_len):
+    """lfm3a_verify_round_host (the drafts copied in from pinned host memory, the round, the output copied back,
+    the stream waited for) gives the bytes of lfm3a_verify_round on the same drafts, in the host buffer on return,
+    and the same cache; the output within 2e-3 of exact fp64 attention. Both geometries."""
+    import torch
+
+    qh, kvh = (32, 8) if d == 64 else (16, 4)
+    m = 16 if d == 64 else 9
+    case = synth.verify_case(70 + d, ctx_len, m, q_heads=qh, kv_heads=kvh, head_dim=d)
+    rope_np = la.rope_table(1e6, 1.0 if d == 64 else 0.5, d, ctx_len + m + 1)
+    rope = dev(rope_np.view(np.float16), cuda)
+    caches = []
+    for _ in range(2):
+        c = la.LayerCache(la.MODE_F16, kvh, d, ctx_len + m + 64, device=cuda)
+        c.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+        caches.append(c)
+    host, plain = caches
+    packed = np.concatenate([case["Q"].reshape(-1), case["newK"].reshape(-1), case["newV"].reshape(-1)])
+    hin = torch.from_numpy(packed).pin_memory()
+    din = torch.empty(hin.shape, dtype=torch.float16, device=cuda)
+    hout = torch.zeros((m, qh, d), dtype=torch.float16).pin_memory()
+    host.verify_round_host(hin, din, hout, m, qh, ctx_len, rope=rope)
+    got = hout.numpy().copy()   # the call returned after the stream finished: the host buffer holds the output
+    want = plain.verify_round(dev(case["newK"], cuda), dev(case["newV"], cuda), dev(case["Q"], cuda), ctx_len,
+                              rope=rope)
+    la.sync()
+    assert np.array_equal(got.view(np.uint16), want.cpu().numpy().view(np.uint16))
+    ga, gb = host.logical(ctx_len + m), plain.logical(ctx_len + m)
+    for key in ("K", "V", "V8", "vscale"):
+        assert np.array_equal(ga[key], gb[key]), key
+    K = ga["K"][:ctx_len + m].view(np.float16)
+    V = ga["V"][:ctx_len + m].view(np.float16)
+    assert rel_err(got, orc.attention_f64(case["Q"], ctx_len, K, V, ctx_len + m)) < TOL
+
+
 # ---------------------------------------------------------------- the reference model's geometry
 # LFM3-1.7B itself (internal/model/engine.go:22-40): 16 query heads, 4 kv heads, head_dim 128, RoPE theta 1e6 over
 # half the dimensions (factor 0.5, engine.go:333-338). verify_m64_kernel<128> serves up to 16 tokens (the
