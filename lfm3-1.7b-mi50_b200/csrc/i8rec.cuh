@@ -5,7 +5,8 @@
 //
 // verify_i8rec_kernel: grid = key splits (32-token pages in contiguous runs), one CTA per SM. A CTA streams its
 // pages whole (all kv heads of a page are one contiguous block of kv_heads x 32 records) through a ring of
-// shared-memory stages filled by 1-D bulk copies; thread 0 refills a stage once every warp has released it.
+// shared-memory stages filled by 1-D bulk copies; the last warp to release a stage refills it (no warp waits for
+// the slowest one).
 // Warp (kv head h, m-tile mt) owns the 16 query rows r = 16 mt .. 16 mt + 15 (r = 4 t + j: token t, query head
 // 4 h + j) and runs the reference's arithmetic on the legacy warp-level tensor-core instructions:
 //   QK  per 32-dim group one mma.m16n8k32 s8 x s8 -> s32 (the group's exact int32 dot, as the reference's
@@ -97,8 +98,11 @@ __device__ __forceinline__ uint32_t s8pair_to_f16x2(uint32_t wk, uint32_t wk1, i
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int D>
-__global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
+// MAXW: the most warps the instantiation launches with, which sets the register cap (65536 / (32 MAXW)). At head_dim
+// 128 a thread holds 64 accumulators; the 12-warp instance (up to 12 tokens at 4 kv heads: the reference verifies
+// at most 9) gets 170 registers and does not spill, the 16-warp one serves 13-16 tokens at 128.
+template <int D, int MAXW>
+__global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args a) {
   constexpr int REC = 2 * D + 8, NG = D / 32, NJ = D / 8;   // record bytes, 32-dim groups, output n-tiles
   extern __shared__ __align__(1024) uint8_t smem[];
   const int H = a.g.kv_heads, NS = a.stages;
@@ -106,6 +110,8 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * page_bytes);
   uint64_t* empty = full + NS;
   int* s_abort = reinterpret_cast<int*>(empty + NS);
+  int* s_issued = s_abort + 1;   // pages whose copies have been started
+  int* s_released = s_abort + 2;   // [NS] warps' releases of each stage so far (monotone)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const int nwarps = H * a.mtiles;
   const int h = warp / a.mtiles, mt = warp % a.mtiles;
@@ -115,9 +121,11 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
+    *s_issued = 0;
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], nwarps);
+      s_released[s] = 0;
     }
     fence_barrier_init();
   }
@@ -129,9 +137,10 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
     mbar_arrive_expect_tx(&full[st], (uint32_t)page_bytes);
     bulk_g2s(smem + (size_t)st * page_bytes, src, (uint32_t)page_bytes, &full[st]);
   };
-  int issued = 0;   // pages whose copies thread 0 has started
-  if (threadIdx.x == 0)
-    for (; issued < min(NS, npg); ++issued) issue(issued);
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < min(NS, npg); ++j) issue(j);
+    atomicMax(s_issued, min(NS, npg));
+  }
 
   // The query rows of this warp: r0 = 16 mt + gid and r0 + 8; A fragments per group (dims 8 tig .. 8 tig + 7).
   const int rA = 16 * mt + gid, rB = rA + 8;
@@ -175,26 +184,31 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
       const uint8_t* krec = page + ((8 * n + gid) * H + h) * REC;   // key 8 n + gid of this kv head
-      int dg[NG][4];
+      // Groups in pairs, each pair folded as soon as its two dots are out (fewer registers live): the C
+      // fragment is (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1) of the n-tile. Each dot
+      // accumulates onto the bits of 1.5 * 2^23 (|dot| <= 32 * 127 * 128 < 2^22): read as fp32 that is
+      // 1.5 * 2^23 + dot exactly, so one FADD converts it (no I2F on the XU pipe).
+      float pair[NG / 2][4];
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const uint2 kb = *reinterpret_cast<const uint2*>(krec + 32 * g + 8 * tig);
-        // The dot accumulates onto the bits of 1.5 * 2^23 (|dot| <= 32 * 127 * 128 < 2^22): read as fp32 that is
-        // 1.5 * 2^23 + dot exactly, so one FADD converts it (no I2F on the XU pipe).
-        dg[g][0] = dg[g][1] = dg[g][2] = dg[g][3] = 0x4B400000;
-        mma_s8_16832(dg[g], qa[g], kb.x, kb.y);
+      for (int g2 = 0; g2 < NG / 2; ++g2) {
+        int d0[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
+        int d1[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
+        const uint2 k0 = *reinterpret_cast<const uint2*>(krec + 64 * g2 + 8 * tig);
+        const uint2 k1 = *reinterpret_cast<const uint2*>(krec + 64 * g2 + 32 + 8 * tig);
+        mma_s8_16832(d0, qa[2 * g2], k0.x, k0.y);
+        mma_s8_16832(d1, qa[2 * g2 + 1], k1.x, k1.y);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float* qs = e < 2 ? qsA : qsB;
+          const float f0 = __int_as_float(d0[e]) - 12582912.f, f1 = __int_as_float(d1[e]) - 12582912.f;
+          pair[g2][e] = fmaf(f1, qs[2 * g2 + 1], f0 * qs[2 * g2]);
+        }
       }
-      // the C fragment: (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1) of the n-tile
       const float ksc0 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig) * H + h) * REC + D);
       const float ksc1 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig + 1) * H + h) * REC + D);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float* qs = e < 2 ? qsA : qsB;
-        float d[NG];
-#pragma unroll
-        for (int g = 0; g < NG; ++g) d[g] = __int_as_float(dg[g][e]) - 12582912.f;
-        float v = fmaf(d[1], qs[1], d[0] * qs[0]);
-        if (NG == 4) v = v + fmaf(d[3], qs[3], d[2] * qs[2]);
+        const float v = NG == 4 ? pair[0][e] + pair[NG / 2 - 1][e] : pair[0][e];
         s[n][e] = v * ((e & 1) ? ksc1 : ksc0);
       }
     }
@@ -274,18 +288,23 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
         }
       }
     }
-    // ---- release the stage; thread 0 refills it once every warp has
+    // ---- release the stage; the last warp to release it (the release count of this use of the stage reaches
+    // nwarps) refills it: its wait on the empty barrier completes at once, and no warp waits for the slowest.
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (threadIdx.x == 0 && j + NS < npg) {
-      if (!mbar_wait(&empty[st], (uint32_t)(j / NS) & 1u)) {
-        raise_error(kErrWaitEmpty);
-        atomicExch(s_abort, 1);
-      } else {
-        issue(j + NS);
-        ++issued;
+    if (lane == 0) {
+      mbar_arrive(&empty[st]);
+      const int before = atomicAdd(&s_released[st], 1);
+      if (before == (j / NS + 1) * nwarps - 1 && j + NS < npg) {
+        if (!mbar_wait(&empty[st], (uint32_t)(j / NS) & 1u)) {
+          raise_error(kErrWaitEmpty);
+          atomicExch(s_abort, 1);
+        } else {
+          issue(j + NS);
+          atomicMax(s_issued, j + NS + 1);
+        }
       }
     }
+    __syncwarp();
     if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(s_abort) != 0)) ok = false;
   }
   if (!ok) atomicExch(s_abort, 1);
@@ -303,11 +322,14 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
       const bool rok = half ? okB : okA;
       if (!rok) continue;
       float* dst = a.part + ((int64_t)(half ? rowB : rowA) * a.splits + split) * (D + 2);
+      // C fragment columns 2 tig, 2 tig + 1 of n-tile jn hold dims NJ (2 tig) + jn and NJ (2 tig + 1) + jn: the
+      // thread's 2 NJ dims of the row are contiguous, stored in 8-byte pairs (a row starts 8-byte aligned).
 #pragma unroll
-      for (int jn = 0; jn < NJ; ++jn) {
-        // C fragment columns 2 tig, 2 tig + 1 of n-tile jn: dims NJ (2 tig) + jn and NJ (2 tig + 1) + jn
-        dst[NJ * (2 * tig) + jn] = acc[jn][2 * half] * (1.f / kPScale);
-        dst[NJ * (2 * tig + 1) + jn] = acc[jn][2 * half + 1] * (1.f / kPScale);
+      for (int jn = 0; jn < NJ; jn += 2) {
+        *reinterpret_cast<float2*>(dst + NJ * (2 * tig) + jn) =
+            make_float2(acc[jn][2 * half] * (1.f / kPScale), acc[jn + 1][2 * half] * (1.f / kPScale));
+        *reinterpret_cast<float2*>(dst + NJ * (2 * tig + 1) + jn) =
+            make_float2(acc[jn][2 * half + 1] * (1.f / kPScale), acc[jn + 1][2 * half + 1] * (1.f / kPScale));
       }
       if (tig == 0) {
         dst[D] = half ? mB : mA;
@@ -318,8 +340,10 @@ __global__ __launch_bounds__(512, 1) void verify_i8rec_kernel(VerifyI8Args a) {
   // On an abort, wait (bounded) for the copies that may still be landing (the last NS started) before the
   // shared memory goes away; every earlier one was consumed.
   __syncthreads();
-  if (threadIdx.x == 0 && aborted)
+  if (threadIdx.x == 0 && aborted) {
+    const int issued = *reinterpret_cast<volatile int*>(s_issued);
     for (int j = max(0, issued - NS); j < issued; ++j) mbar_wait(&full[j % NS], (uint32_t)(j / NS) & 1u);
+  }
 }
 
 }  // namespace lfm3a

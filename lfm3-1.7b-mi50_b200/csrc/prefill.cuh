@@ -498,7 +498,6 @@ __global__ __launch_bounds__(PfLayout<D, I8>::kThreads, PfLayout<D, I8>::kBlocks
     const int r = threadIdx.x, t = r >> 2, j = r & 3;
     const bool row_ok = t < ntok;
     const int qpos = qfirst + t;
-    const int64_t grow = (int64_t)(t0 + (row_ok ? t : 0)) * a.q_heads + 4 * h + j;
     {
       load_q_row<D, GLUE>(a, sQ, r, row_ok, t0 + (row_ok ? t : 0), 4 * h + j);
       fence_proxy_async_smem();
