@@ -1110,14 +1110,14 @@ def run_ours(args):
     direct = world == 1 and fused_round
     if direct:
         # One GPU: the round with host buffers is one C-ABI call (lfm3a_verify_round_host: the drafts' copy in, the
-        # round, the output's copy out, the stream wait), then the rollback (lfm3a_kv_truncate), with the arguments
-        # prepared once, as a caller that keeps its layer views does.
+        # round, the output's copy out, queued without waiting), then the rollback (lfm3a_kv_truncate), then one
+        # stream synchronize, with the arguments prepared once, as a caller that keeps its layer views does.
         lib = la.lib()
         views = [ctypes.byref(c.view) for c in caches]
         st_ptr = torch.cuda.current_stream().cuda_stream
         ws_bytes = ws.numel()
         call_args = (hin.data_ptr(), din.data_ptr(), rope.data_ptr(), None, M, QH, R.ctx_len, 0, None, out.data_ptr(),
-                     hout.data_ptr(), ws.data_ptr(), ws_bytes, splits, st_ptr, 10000)
+                     hout.data_ptr(), ws.data_ptr(), ws_bytes, splits, st_ptr, -1)
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
@@ -1130,6 +1130,7 @@ def run_ours(args):
         if direct:
             rc_e2e |= lib.lfm3a_verify_round_host(views[i % n_layers], *call_args)
             rc_e2e |= lib.lfm3a_kv_truncate(views[i % n_layers], R.ctx_len, st_ptr)
+            torch.cuda.current_stream().synchronize()
         else:
             din.copy_(hin, non_blocking=True)
             step(caches[i % n_layers], None, dq, dk, dv)
@@ -1237,8 +1238,8 @@ def run_ours(args):
                     "h2d_bytes_per_step": int(hin.numel() * 2),
                     "d2h_bytes_per_step": int(hout.numel() * 2),
                     "how": ("per step lfm3a_verify_round_host (one copy of the drafts' q, k, v from pinned host "
-                            "memory, the round, the output copied back to pinned host memory, the stream waited "
-                            "for) + lfm3a_kv_truncate, through ctypes" if direct else
+                            "memory, the round, the output copied back to pinned host memory) + lfm3a_kv_truncate "
+                            "through ctypes, then a stream synchronize" if direct else
                             "one pinned-host copy of this rank's drafts' q, k, v, the plan's step (LayerCache calls "
                             "and the exchange), the exchanged output read back, a stream sync per step")},
             "gpu_launches": int(launches_per_step * K),

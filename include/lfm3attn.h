@@ -203,9 +203,10 @@ int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, in
  * end-to-end leg of the benchmark): copies host_in, the drafts' q then k then v (fp16 [m][q_heads][head_dim],
  * [m][kv_heads][head_dim], [m][kv_heads][head_dim], contiguous), into dev_in (device, 16-byte aligned, as many
  * bytes), runs lfm3a_verify_round on them (out: device fp16 [m][q_heads][head_dim]), then copies out into
- * host_out, all on stream. host_in and host_out should be pinned. timeout_ms >= 0: returns once the stream is
- * done (LFM3A_ETIMEOUT after timeout_ms); < 0: returns at once. A kernel that gave up a bounded wait is reported
- * by the next lfm3a_sync. No reference counterpart: the reference's drafts are produced on the GPU. */
+ * host_out, all on stream. host_in and host_out should be pinned. timeout_ms > 0: returns once the stream is
+ * done, LFM3A_ETIMEOUT after timeout_ms; 0: waits for the stream without a limit (cudaStreamSynchronize); < 0:
+ * returns at once (the caller waits, e.g. after queueing the rollback). A kernel that gave up a bounded wait is
+ * reported by the next lfm3a_sync. No reference counterpart: the reference's drafts are produced on the GPU. */
 int lfm3a_verify_round_host(const lfm3a_kv_view* kv, const void* host_in, void* dev_in, const void* rope,
                             const void* k_norm, int m, int q_heads, int ctx_len, int window, const void* gate,
                             void* out, void* host_out, void* workspace, size_t workspace_bytes, int splits,

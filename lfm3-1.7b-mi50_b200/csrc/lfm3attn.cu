@@ -585,6 +585,10 @@ int lfm3a_verify_round_host(const lfm3a_kv_view* kv, const void* host_in, void* 
   e = cudaMemcpyAsync(host_out, out, qb, cudaMemcpyDeviceToHost, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (output to the host)");
   if (timeout_ms < 0) return LFM3A_OK;
+  if (timeout_ms == 0) {
+    e = cudaStreamSynchronize(st);
+    return e == cudaSuccess ? LFM3A_OK : cuda_fail(e, "cudaStreamSynchronize");
+  }
   const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
   for (;;) {
     e = cudaStreamQuery(st);

@@ -312,7 +312,8 @@ class LayerCache:
                           stream=None, timeout_ms: int = 10000):
         """verify_round with host buffers in one library call: host_in (pinned fp16: the drafts' q, then k, then v,
         contiguous) is copied into dev_in, the round runs, its output is copied into host_out (pinned fp16
-        [m][q_heads][head_dim]), and the call waits for the stream (timeout_ms >= 0)."""
+        [m][q_heads][head_dim]); the call then waits for the stream up to timeout_ms (> 0), without a limit (0), or
+        not at all (< 0)."""
         import torch
 
         d = self.head_dim

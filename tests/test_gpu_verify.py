@@ -238,11 +238,12 @@ def test_verify_round_matches_two_calls(la, orc, synth, cuda, ctx_len, m, splits
         plain.truncate(length)
 
 
-@pytest.mark.parametrize("d,ctx_len", [(64, 3000), (128, 2000)])
-def test_verify_round_host(la, orc, synth, cuda, d, ctx_len):
+@pytest.mark.parametrize("d,ctx_len,timeout_ms", [(64, 3000, 10000), (128, 2000, 10000), (64, 3000, 0), (64, 3000, -1)])
+def test_verify_round_host(la, orc, synth, cuda, d, ctx_len, timeout_ms):
     """lfm3a_verify_round_host (the drafts copied in from pinned host memory, the round, the output copied back,
-    the stream waited for) gives the bytes of lfm3a_verify_round on the same drafts, in the host buffer on return,
-    and the same cache; the output within 2e-3 of exact fp64 attention. Both geometries."""
+    the stream waited for: bounded, unbounded, or by the caller) gives the bytes of lfm3a_verify_round on the same
+    drafts in the host buffer, and the same cache; the output within 2e-3 of exact fp64 attention. Both
+    geometries."""
     import torch
 
     qh, kvh = (32, 8) if d == 64 else (16, 4)
@@ -260,8 +261,10 @@ def test_verify_round_host(la, orc, synth, cuda, d, ctx_len):
     hin = torch.from_numpy(packed).pin_memory()
     din = torch.empty(hin.shape, dtype=torch.float16, device=cuda)
     hout = torch.zeros((m, qh, d), dtype=torch.float16).pin_memory()
-    host.verify_round_host(hin, din, hout, m, qh, ctx_len, rope=rope)
-    got = hout.numpy().copy()   # the call returned after the stream finished: the host buffer holds the output
+    host.verify_round_host(hin, din, hout, m, qh, ctx_len, rope=rope, timeout_ms=timeout_ms)
+    if timeout_ms < 0:
+        torch.cuda.current_stream().synchronize()
+    got = hout.numpy().copy()   # the stream has finished: the host buffer holds the output
     want = plain.verify_round(dev(case["newK"], cuda), dev(case["newV"], cuda), dev(case["Q"], cuda), ctx_len,
                               rope=rope)
     la.sync()
