@@ -577,6 +577,54 @@ def measure_ref_i8(la, synth, dev, peak_gbs: float, ctx: int, seed: int, n_cache
     return res
 
 
+def measure_ref_i8_prefill(la, dev, tokens: int, context: int, reps: int = 3) -> dict:
+    """The reference's own prefill arithmetic over its own cache bytes at its geometry (16/4/128, int8 264-byte
+    records): the tokens' query quantiser and the int8 prefill attention with its key splits and combine
+    (lfm3a_quantize_q, lfm3a_prefill_attention_i8), K/V/Q N(0,1) fp16 drawn on the device; beside it the
+    reference's published MI50 time for the same launch (its int8 kernel on these bytes)."""
+    import numpy as np
+    import torch
+
+    qh, kvh, d = 16, 4, 128
+    n = context + tokens
+    g = torch.Generator(device=dev).manual_seed(14)
+    rope = torch.from_numpy(la.rope_table(1e6, 0.5, d, n + 1).view(np.float16)).to(dev)
+    cache = la.LayerCache(la.MODE_I8REC, kvh, d, n + 64, device=dev)
+    for p0 in range(0, n, 16384):
+        c = min(16384, n - p0)
+        cache.append(torch.randn((c, kvh, d), generator=g, device=dev).half(),
+                     torch.randn((c, kvh, d), generator=g, device=dev).half(), p0, rope=rope)
+    q = torch.randn((tokens, qh, d), generator=g, device=dev).half()
+    qbuf = la.quantize_q(q)
+    out = torch.empty_like(q)
+    splits = la.lib().lfm3a_prefill_i8_splits(tokens, qh, context, 0, 0)
+    ws = torch.empty(tokens * qh * splits * (d + 2) * 4, dtype=torch.uint8, device=dev)
+
+    def call():
+        la.quantize_q(q, out=qbuf)
+        cache.prefill_i8(qbuf, tokens, qh, context, out=out, workspace=ws, splits=splits)
+
+    call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    la.sync()
+    ms = e0.elapsed_time(e1) / reps
+    qk = 2.0 * qh * d * (tokens * context + tokens * (tokens + 1) / 2)
+    res = {"workload": f"the reference's prefill arithmetic on its int8 records, 16/4/128: {tokens} tokens over "
+                       f"{context} cached", "ms": round(ms, 3), "splits": splits,
+           "tops_qk_plus_pv": round(2 * qk / (ms * 1e-3) / 1e12, 1)}
+    ref = REF_MI50_PREFILL_MS.get((tokens, context))
+    if ref:
+        res["reference_mi50_ms"] = ref["int8_pv"]
+    del cache
+    return res
+
+
 def measure_ref_geometries(la, synth, dev, peak_gbs: float) -> dict:
     import torch
 
@@ -591,6 +639,10 @@ def measure_ref_geometries(la, synth, dev, peak_gbs: float) -> dict:
     res["prefill_2048"] = measure_ref_prefill(la, dev, 2048, 0)
     torch.cuda.empty_cache()
     res["prefill_7680_at_115200"] = measure_ref_prefill(la, dev, 7680, 115200)
+    torch.cuda.empty_cache()
+    res["i8rec_prefill_2048"] = measure_ref_i8_prefill(la, dev, 2048, 0)
+    torch.cuda.empty_cache()
+    res["i8rec_prefill_7680_at_115200"] = measure_ref_i8_prefill(la, dev, 7680, 115200)
     torch.cuda.empty_cache()
     return res
 

@@ -242,6 +242,22 @@ int lfm3a_verify_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int
                               int window, const void* gate, void* out, void* workspace, size_t workspace_bytes,
                               int splits, void* stream);
 
+/* The key split count lfm3a_prefill_attention_i8 uses when called with splits <= 0 (lfm3a_prefill_splits for one
+ * CTA per SM). */
+int lfm3a_prefill_i8_splits(int tokens, int q_heads, int context, int window, int sm_count);
+
+/* Causal (optionally sliding-window) prefill attention over MODE_I8REC records with the reference's own arithmetic
+ * (kernels/prefill_attn.hip:212-505, the engine's default prefill attention): the tokens' queries quantised by
+ * lfm3a_quantize_q (qbuf), int8 Q x int8 K per 32-dim group, the lazy running max (2^8), P' = p * v_scale as u8
+ * per row and 64-key tile against the tile's largest P', u8 x (int8 V + 128) with the bias taken back, blocks of
+ * 32 query tokens and the reference's key splits, merged by the combine. The tokens' records must already be
+ * appended at context .. context + tokens - 1 (lfm3a_kv_append on the MODE_I8REC view). out: device fp16
+ * [tokens][q_heads][head_dim]. workspace: tokens * q_heads * splits * (head_dim + 2) * 4 bytes (needed for every
+ * split count; splits <= 0: lfm3a_prefill_i8_splits, at most 64). q_heads = 4 * kv_heads, head_dim 64 or 128. */
+int lfm3a_prefill_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int tokens, int q_heads, int context,
+                               int window, void* out, void* workspace, size_t workspace_bytes, int splits,
+                               void* stream);
+
 /* ---------------------------------------------------------------- drafter ring attention
  * The drafter's KV ring (kernels/dspark.hip:69-70,1070-1412 attention_pass<1, true>, called at :2527):
  * the drafter keeps its context K/V in a ring of pages, logical block b in ring block b mod ring_blocks,

@@ -346,4 +346,290 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
   }
 }
 
+// ---------------------------------------------------------------- prefill attention over int8 records
+// prefill_i8rec_kernel: the reference's prefill arithmetic over its own cache bytes (kernels/prefill_attn.hip:212-486),
+// with its blocking: grid = (32-token query blocks, longest rows first; kv heads; key splits, tiles
+// [n z / splits, n (z + 1) / splits) of the block's n 64-key tiles from kbegin / 64 * 64). Eight warps, warp w
+// owning rows 16 w .. 16 w + 15 of the block's 128 (row 4 t + j: token t, query head 4 h + j). The head's 64
+// records of a tile are copied into shared memory with 8-byte cp.async (a record is 8-byte aligned, not 16),
+// double-buffered. Per tile, as the reference:
+//   QK  per 32-dim group one mma.m16n8k32 s8 x s8 onto the bits of 1.5 * 2^23, read as a float and folded in
+//       order: s = fma(1.5 * 2^23 + dot_g, qs_g, s) from s = -1.5 * 2^23 (qs0 + qs1 + qs2 + qs3) (:217-254);
+//       u = fma(s, k_scale (1 / sqrt(D)) log2 e, -m), masked keys -inf;
+//   the lazy running max (m from 0; on the split's first tile, or when a row's u passes 8) (:274-297);
+//   e = 2^u, P' = e v_scale, l += e, P' to u8 against the row's largest P' of the tile (round to nearest
+//       even, saturated), bias += sum(q) 128 sc with sc = max P' / 255 (:298-317);
+//   PV  the exact sum_k q_k v_k from mma.m16n8k16 on fp16 (u8 and int8 are exact there, the fp32 sums of
+//       products stay below 2^24), plus 128 sum(q): the reference's u8 x (v + 128) dot, then
+//       acc = fma(that, sc, acc) (:320-350);
+//   the split's partial: acc - bias, m (-inf without tiles), l, merged by the combine kernel (:489-505).
+struct PrefillI8Args {
+  KvGeom g;
+  const uint32_t* qbuf;   // [tokens * q_heads][D / 4 + D / 32] (quantize_q rows)
+  float* part;            // [tokens * q_heads][splits][D + 2]
+  int T, q_heads, context, window, splits, qtiles;
+  float kscale;           // (1 / sqrt(D)) log2(e)
+};
+
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int D>
+__global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) {
+  constexpr int REC = 2 * D + 8, NG = D / 32, NJ = D / 8, KT = 64, QT = 32, CH = REC / 8;
+  constexpr float LAZY = 8.f, MAGIC_F = 12582912.f;
+  constexpr int MAGIC_I = 0x4B400000;
+  __shared__ __align__(16) uint8_t tiles[2][KT * REC];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int h = blockIdx.y, z = blockIdx.z, nz = a.splits, H = a.g.kv_heads;
+  const int t0 = (a.qtiles - 1 - blockIdx.x) * QT, ntok = min(QT, a.T - t0);
+  const int qfirst = a.context + t0, qlast = qfirst + ntok - 1, kend = qlast + 1;
+  const int kbegin = a.window > 0 ? max(0, qfirst - a.window + 1) : 0;
+  const int kt_begin = kbegin / KT * KT;
+  const int all_tiles = (kend - kt_begin + KT - 1) / KT;
+  const int tile_lo = (int)((int64_t)all_tiles * z / nz);
+  const int ntiles = (int)((int64_t)all_tiles * (z + 1) / nz) - tile_lo;
+  const int kt_first = kt_begin + tile_lo * KT;
+  pdl_wait();
+
+  auto load = [&](int s) {   // tile s of the split into buffer s & 1; keys past the end read the last key's record
+    const int k0 = kt_first + s * KT;
+    uint8_t* dst = tiles[s & 1];
+    for (int c = threadIdx.x; c < KT * CH; c += blockDim.x) {
+      const int kk = c / CH, off = (c - kk * CH) * 8;
+      const int key = min(k0 + kk, kend - 1);
+      const char* src = a.g.pool + phys_block(a.g, key / kBlockTokens) * a.g.block_bytes +
+                        ((int64_t)(key % kBlockTokens) * H + h) * REC + off;
+      cp_async8(dst + kk * REC + off, src);
+    }
+    cp_async_commit();
+  };
+
+  // This warp's rows: rA = 16 warp + gid and rB = rA + 8; the A fragments per group as the verify kernel's.
+  const int rA = 16 * warp + gid, rB = rA + 8, tA = rA >> 2, tB = rB >> 2;
+  const bool okA = tA < ntok, okB = tB < ntok;
+  const int qposA = qfirst + tA, qposB = qfirst + tB;
+  const int64_t rowA = (int64_t)(t0 + min(tA, ntok - 1)) * a.q_heads + 4 * h + (rA & 3);
+  const int64_t rowB = (int64_t)(t0 + min(tB, ntok - 1)) * a.q_heads + 4 * h + (rB & 3);
+  constexpr int QROW = D / 4 + D / 32;
+  uint32_t qa[NG][4];
+  float qsA[NG], qsB[NG];
+  {
+    const uint32_t* pa = a.qbuf + rowA * QROW;
+    const uint32_t* pb = a.qbuf + rowB * QROW;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      qa[g][0] = pa[8 * g + 2 * tig];
+      qa[g][1] = pb[8 * g + 2 * tig];
+      qa[g][2] = pa[8 * g + 2 * tig + 1];
+      qa[g][3] = pb[8 * g + 2 * tig + 1];
+      qsA[g] = __uint_as_float(pa[D / 4 + g]);
+      qsB[g] = __uint_as_float(pb[D / 4 + g]);
+    }
+  }
+  float qcA = qsA[0] + qsA[1], qcB = qsB[0] + qsB[1];
+  if (NG == 4) {
+    qcA = (qcA + qsA[NG - 2]) + qsA[NG - 1];
+    qcB = (qcB + qsB[NG - 2]) + qsB[NG - 1];
+  }
+  qcA *= -MAGIC_F;
+  qcB *= -MAGIC_F;
+
+  float acc[NJ][4];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  float mA = 0.f, mB = 0.f, lA = 0.f, lB = 0.f, bA = 0.f, bB = 0.f;   // l and the bias: this thread's keys
+
+  if (ntiles > 0) load(0);
+  for (int s = 0; s < ntiles; ++s) {
+    if (s + 1 < ntiles) {
+      load(s + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint8_t* tl = tiles[s & 1];
+    const int k0 = kt_first + s * KT;
+    // ---- QK: 8 n-tiles of 8 keys; C fragment (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1)
+    float u[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const uint8_t* krec = tl + (8 * n + gid) * REC;
+      float sv[4] = {qcA, qcA, qcB, qcB};
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        int d4[4] = {MAGIC_I, MAGIC_I, MAGIC_I, MAGIC_I};
+        const uint2 kb = *reinterpret_cast<const uint2*>(krec + 32 * g + 8 * tig);
+        mma_s8_16832(d4, qa[g], kb.x, kb.y);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sv[e] = fmaf(__int_as_float(d4[e]), e < 2 ? qsA[g] : qsB[g], sv[e]);
+      }
+      const float ks0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + D) * a.kscale;
+      const float ks1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + D) * a.kscale;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) u[n][e] = fmaf(sv[e], (e & 1) ? ks1 : ks0, -(e < 2 ? mA : mB));
+    }
+    const bool interior = k0 + KT - 1 <= qfirst && k0 >= kbegin && (a.window == 0 || k0 > qlast - a.window);
+    if (!interior || !okB) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kpos = k0 + 8 * n + 2 * tig + (e & 1);
+          const int qpos = e < 2 ? qposA : qposB;
+          const bool valid = kpos <= qpos && kpos >= kbegin && (a.window == 0 || kpos > qpos - a.window) &&
+                             (e < 2 ? okA : okB);
+          u[n][e] = valid ? u[n][e] : -INFINITY;
+        }
+    }
+    // ---- the lazy running max (the rows' tile maxima over the quad)
+    float tA_ = -INFINITY, tB_ = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      tA_ = fmaxf(tA_, fmaxf(u[n][0], u[n][1]));
+      tB_ = fmaxf(tB_, fmaxf(u[n][2], u[n][3]));
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      tA_ = fmaxf(tA_, __shfl_xor_sync(0xffffffffu, tA_, o));
+      tB_ = fmaxf(tB_, __shfl_xor_sync(0xffffffffu, tB_, o));
+    }
+    if (__any_sync(0xffffffffu, tA_ > LAZY || tB_ > LAZY) || s == 0) {
+      const float tmA = tA_ + mA, tmB = tB_ + mB;
+      const bool upA = tmA > -INFINITY && (s == 0 || tmA > mA + LAZY);
+      const bool upB = tmB > -INFINITY && (s == 0 || tmB > mB + LAZY);
+      const float dA = upA ? mA - tmA : 0.f, dB = upB ? mB - tmB : 0.f;
+      const float cA = fast_exp2(dA), cB = fast_exp2(dB);
+      mA = upA ? tmA : mA;
+      mB = upB ? tmB : mB;
+      lA *= cA;
+      lB *= cB;
+      bA *= cA;
+      bB *= cB;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        acc[j][0] *= cA;
+        acc[j][1] *= cA;
+        acc[j][2] *= cB;
+        acc[j][3] *= cB;
+      }
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        u[n][0] += dA;
+        u[n][1] += dA;
+        u[n][2] += dB;
+        u[n][3] += dB;
+      }
+    }
+    // ---- P' = 2^u v_scale, l += 2^u; u8 against the row's largest P' of the tile
+    float pmA = 0.f, pmB = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + 2 * D + 4);
+      const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + 2 * D + 4);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float ex = fast_exp2(u[n][e]);
+        if (e < 2) lA += ex;
+        else lB += ex;
+        u[n][e] = ex * ((e & 1) ? vs1 : vs0);   // u now holds P'
+      }
+      pmA = fmaxf(pmA, fmaxf(u[n][0], u[n][1]));
+      pmB = fmaxf(pmB, fmaxf(u[n][2], u[n][3]));
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      pmA = fmaxf(pmA, __shfl_xor_sync(0xffffffffu, pmA, o));
+      pmB = fmaxf(pmB, __shfl_xor_sync(0xffffffffu, pmB, o));
+    }
+    const float invA = 255.f * __frcp_rn(fmaxf(pmA, 1e-30f)), invB = 255.f * __frcp_rn(fmaxf(pmB, 1e-30f));
+    const float scA = pmA * (1.f / 255.f), scB = pmB * (1.f / 255.f);
+    int qsumA = 0, qsumB = 0;
+    uint32_t pf[4][4];   // the u8 probabilities as fp16 A fragments of the four 16-key k-steps
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      float qv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float x = fminf(u[n][e] * (e < 2 ? invA : invB), 255.f);
+        const int q = (int)(__float_as_uint(x + 12582912.f) & 0xffu);   // nearest even, in [0, 255]
+        qv[e] = (float)q;
+        if (e < 2) qsumA += q;
+        else qsumB += q;
+      }
+      pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(qv[0], qv[1]);
+      pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(qv[2], qv[3]);
+    }
+    bA = fmaf((float)qsumA, 128.f * scA, bA);
+    bB = fmaf((float)qsumB, 128.f * scB, bB);
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      qsumA += __shfl_xor_sync(0xffffffffu, qsumA, o);
+      qsumB += __shfl_xor_sync(0xffffffffu, qsumB, o);
+    }
+    const float biasA = 128.f * (float)qsumA, biasB = 128.f * (float)qsumB;   // the + 128 of every V byte
+    // ---- PV in passes of 32 dims: dot = sum_k q_k v_k exactly, then acc = fma(dot + 128 sum q, sc, acc)
+    constexpr int NP = NJ / 4;   // passes; a pass covers 4 n-tiles (one V word per key)
+#pragma unroll
+    for (int half = 0; half < NP; ++half) {
+      float dot[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dot[j][0] = dot[j][1] = dot[j][2] = dot[j][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int kb = 16 * kk + 2 * tig;
+        const uint32_t* v0 = reinterpret_cast<const uint32_t*>(tl + (kb + 0) * REC + D + 4 + NJ * gid);
+        const uint32_t* v1 = reinterpret_cast<const uint32_t*>(tl + (kb + 1) * REC + D + 4 + NJ * gid);
+        const uint32_t* v8 = reinterpret_cast<const uint32_t*>(tl + (kb + 8) * REC + D + 4 + NJ * gid);
+        const uint32_t* v9 = reinterpret_cast<const uint32_t*>(tl + (kb + 9) * REC + D + 4 + NJ * gid);
+        const uint32_t w0 = v0[half], w1 = v1[half], w8 = v8[half], w9 = v9[half];
+#pragma unroll
+        for (int by = 0; by < 4; ++by)
+          mma_f16_16816(dot[by], pf[kk], s8pair_to_f16x2(w0, w1, by), s8pair_to_f16x2(w8, w9, by));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int jn = 4 * half + j;
+        acc[jn][0] = fmaf(dot[j][0] + biasA, scA, acc[jn][0]);
+        acc[jn][1] = fmaf(dot[j][1] + biasA, scA, acc[jn][1]);
+        acc[jn][2] = fmaf(dot[j][2] + biasB, scB, acc[jn][2]);
+        acc[jn][3] = fmaf(dot[j][3] + biasB, scB, acc[jn][3]);
+      }
+    }
+    __syncthreads();   // every warp is done with this buffer before the copy of tile s + 2 lands in it
+  }
+  // ---- partials: acc - bias (dims put back in order), m (-inf without tiles), l
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    lA += __shfl_xor_sync(0xffffffffu, lA, o);
+    lB += __shfl_xor_sync(0xffffffffu, lB, o);
+    bA += __shfl_xor_sync(0xffffffffu, bA, o);
+    bB += __shfl_xor_sync(0xffffffffu, bB, o);
+  }
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    if (!(half ? okB : okA)) continue;
+    const float bias = half ? bB : bA;
+    float* dst = a.part + ((half ? rowB : rowA) * nz + z) * (D + 2);
+#pragma unroll
+    for (int jn = 0; jn < NJ; jn += 2) {
+      *reinterpret_cast<float2*>(dst + NJ * (2 * tig) + jn) =
+          make_float2(acc[jn][2 * half] - bias, acc[jn + 1][2 * half] - bias);
+      *reinterpret_cast<float2*>(dst + NJ * (2 * tig + 1) + jn) =
+          make_float2(acc[jn][2 * half + 1] - bias, acc[jn + 1][2 * half + 1] - bias);
+    }
+    if (tig == 0) {
+      dst[D] = ntiles > 0 ? (half ? mB : mA) : -INFINITY;
+      dst[D + 1] = half ? lB : lA;
+    }
+  }
+}
+
 }  // namespace lfm3a

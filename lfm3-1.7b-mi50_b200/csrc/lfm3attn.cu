@@ -863,6 +863,50 @@ int lfm3a_verify_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int
                         static_cast<const __half*>(gate), static_cast<__half*>(out), nullptr, st);
 }
 
+int lfm3a_prefill_i8_splits(int tokens, int q_heads, int context, int window, int sm_count) {
+  if (tokens < 0 || q_heads < 4 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill split arguments");
+  // One CTA per SM (its registers rule out a second).
+  return prefill_splits_for(tokens, q_heads / 4, context, window, sm_count > 0 ? sm_count : current_sm_count(), 1);
+}
+
+int lfm3a_prefill_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int tokens, int q_heads, int context,
+                               int window, void* out, void* workspace, size_t workspace_bytes, int splits,
+                               void* stream) {
+  int rc = check_view(kv);
+  if (rc != LFM3A_OK) return rc;
+  const lfm3a_kv_layout& L = kv->layout;
+  const int D = L.head_dim, H = L.kv_heads;
+  if (L.mode != LFM3A_MODE_I8REC) return fail(LFM3A_ENOTSUP, "prefill_attention_i8 reads MODE_I8REC records");
+  if (q_heads != 4 * H) return fail(LFM3A_ENOTSUP, "prefill attention needs 4 query heads per kv head");
+  if (!qbuf || !out || tokens < 0 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill arguments");
+  if (tokens == 0) return LFM3A_OK;
+  if (!aligned16(out) || (reinterpret_cast<uintptr_t>(qbuf) & 7)) return fail(LFM3A_EINVAL, "misaligned out or qbuf");
+  if (splits <= 0) splits = lfm3a_prefill_i8_splits(tokens, q_heads, context, window, 0);
+  if (splits > 64) return fail(LFM3A_EINVAL, "prefill_attention_i8: at most 64 key splits");
+  const size_t need = (size_t)tokens * q_heads * splits * (D + 2) * sizeof(float);
+  if (!workspace || !aligned16(workspace)) return fail(LFM3A_EINVAL, "prefill_attention_i8 needs a workspace");
+  if (workspace_bytes < need) return fail(LFM3A_EWORKSPACE, "prefill workspace too small");
+  PrefillI8Args a;
+  a.g = geom_of(kv);
+  a.qbuf = qbuf;
+  a.part = static_cast<float*>(workspace);
+  a.T = tokens;
+  a.q_heads = q_heads;
+  a.context = context;
+  a.window = window;
+  a.splits = splits;
+  a.qtiles = (tokens + 31) / 32;
+  a.kscale = (1.f / sqrtf((float)D)) * kLog2e;
+  const cudaStream_t st = as_stream(stream);
+  const dim3 grid(a.qtiles, H, splits);
+  if (D == 128) launch_pdl(prefill_i8rec_kernel<128>, grid, 256, 0, st, a);
+  else launch_pdl(prefill_i8rec_kernel<64>, grid, 256, 0, st, a);
+  rc = check_launch("prefill_i8rec_kernel");
+  if (rc != LFM3A_OK) return rc;
+  return launch_combine(a.part, tokens * q_heads, splits, D, D + 2, (int64_t)splits * (D + 2), nullptr,
+                        static_cast<__half*>(out), nullptr, st);
+}
+
 int lfm3a_quantize_p_u8(const float* p, int rows, uint8_t* q, float* sc, void* stream) {
   if (!p || !q || !sc || rows < 0) return fail(LFM3A_EINVAL, "bad quantize_p arguments");
   if (rows == 0) return LFM3A_OK;

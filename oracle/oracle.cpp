@@ -437,6 +437,132 @@ void orc_verify_i8rec(const uint32_t* qbuf, int m, int q_heads, int kv_heads, in
   }
 }
 
+// Prefill attention over the int8 records with the reference's own arithmetic (kernels/prefill_attn.hip:1-17,
+// 212-336 qk_softmax / pv_tile, 373-486 prefill_attention, 489-505 combine), per (token, head) row:
+//   blocks of 32 query tokens (t0 = t / 32 * 32), key tiles of 64 from kt_begin = kbegin / 64 * 64 with
+//   kbegin = max(0, context + t0 - window + 1) (0 without a window), split z taking tiles
+//   [n z / splits, n (z + 1) / splits) of the block's n = ceil((context + t0 + ntok - kt_begin) / 64);
+//   s = -1.5 * 2^23 (qs0 + qs1 + qs2 + qs3), then per group s = fma(float(1.5 * 2^23 + dot_g), qs_g, s) (:217-254);
+//   u = fma(s, k_scale * (1 / sqrt(D)) log2 e, -m), masked keys -inf (:259-273);
+//   m starts at 0; on the split's first tile, or when a tile's u beats LAZY = 8, the row's tile maximum tm (u + m)
+//   becomes m if it is finite (and on later tiles only if tm > m + LAZY): corr = 2^(m - tm) scales l, the bias
+//   and acc, and u moves by m - tm (:274-297);
+//   e = 2^u, P' = e * v_scale, l += e; pm = the row's largest P' in the tile, inv = 255 / max(pm, 1e-30),
+//   sc = pm / 255, q = P' * inv rounded to nearest even and saturated to u8; bias = fma(sum q, 128 sc, bias)
+//   (:298-317);
+//   acc_d = fma(float(sum_k q_k (v_kd + 128)), sc, acc_d) (:320-350);
+//   the split's partial: acc - bias, m (-inf for a split without tiles), l; the merge of the splits
+//   out = sum_z 2^(m_z - M) (acc_z - bias_z) / sum_z 2^(m_z - M) l_z (:489-505), as fp32.
+// qbuf rows come from orc_quantize_q; rec is [positions][kv_heads][2 D + 8] with positions up to
+// context + tokens. head_dim 64 or 128.
+void orc_prefill_i8rec(const uint32_t* qbuf, int tokens, int q_heads, int kv_heads, int head_dim, const uint8_t* rec,
+                       int context, int window, int splits, float* out) {
+  const int D = head_dim, G = q_heads / kv_heads, R = 2 * D + 8, NG = D / 32, qrow = D / 4 + D / 32;
+  constexpr int KT = 64, QT = 32;
+  constexpr float LAZY = 8.f, MAGIC_F = 12582912.f;
+  const float kscale = (1.f / sqrtf((float)D)) * LOG2E;
+  const int nz = std::max(1, splits);
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int row = 0; row < tokens * q_heads; ++row) {
+    const int t = row / q_heads, qh = row % q_heads, h = qh / G;
+    const int t0 = t / QT * QT, ntok = std::min(QT, tokens - t0);
+    const int qpos = context + t, qfirst = context + t0, qlast = context + t0 + ntok - 1, kend = qlast + 1;
+    const int kbegin = window > 0 ? std::max(0, qfirst - window + 1) : 0;
+    const int kt_begin = kbegin / KT * KT, all_tiles = (kend - kt_begin + KT - 1) / KT;
+    const int8_t* q8 = reinterpret_cast<const int8_t*>(qbuf + (size_t)row * qrow);
+    float qs[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int g = 0; g < NG; ++g) memcpy(&qs[g], qbuf + (size_t)row * qrow + D / 4 + g, 4);
+    const float qc = -MAGIC_F * (((qs[0] + qs[1]) + qs[2]) + qs[3]);
+    std::vector<float> pacc((size_t)nz * D), pm(nz), pl(nz), ones(nz, 0.f);
+    for (int z = 0; z < nz; ++z) {
+      const int tile_lo = all_tiles * z / nz, ntiles = all_tiles * (z + 1) / nz - tile_lo;
+      float m = 0.f, l = 0.f, bias = 0.f;
+      std::vector<float> acc(D, 0.f);
+      for (int s = 0; s < ntiles; ++s) {
+        const int k0 = kt_begin + (tile_lo + s) * KT;
+        float u[KT], pr[KT];
+        float tm = -INFINITY;
+        bool grow = false;
+        for (int kk = 0; kk < KT; ++kk) {
+          const int kpos = k0 + kk;
+          const bool valid = kpos <= qpos && kpos >= kbegin && (window == 0 || kpos > qpos - window);
+          if (!valid) {
+            u[kk] = -INFINITY;
+            continue;
+          }
+          const uint8_t* r = rec + ((size_t)kpos * kv_heads + h) * R;
+          const int8_t* k8 = reinterpret_cast<const int8_t*>(r);
+          float ks;
+          memcpy(&ks, r + D, 4);
+          float sc = qc;
+          for (int g = 0; g < NG; ++g) {
+            int dot = 0;
+            for (int d = 32 * g; d < 32 * g + 32; ++d) dot += (int)q8[d] * (int)k8[d];
+            sc = fmaf(MAGIC_F + (float)dot, qs[g], sc);
+          }
+          u[kk] = fmaf(sc, ks * kscale, -m);
+          grow = grow || u[kk] > LAZY;
+          tm = fmaxf(tm, u[kk]);
+        }
+        if (grow || s == 0) {
+          const float tmm = tm + m;
+          const bool up = tmm > -INFINITY && (s == 0 || tmm > m + LAZY);
+          const float d = up ? m - tmm : 0.f;
+          const float corr = exp2f(d);
+          m = up ? tmm : m;
+          l *= corr;
+          bias *= corr;
+          for (int e = 0; e < D; ++e) acc[e] *= corr;
+          for (int kk = 0; kk < KT; ++kk) u[kk] += d;
+        }
+        float pmax = -INFINITY;
+        for (int kk = 0; kk < KT; ++kk) {
+          const float e = exp2f(u[kk]);
+          float vs = 0.f;
+          if (u[kk] != -INFINITY) memcpy(&vs, rec + ((size_t)(k0 + kk) * kv_heads + h) * R + 2 * D + 4, 4);
+          pr[kk] = e * vs;
+          l += e;
+          pmax = fmaxf(pmax, pr[kk]);
+        }
+        const float inv = 255.f * (1.f / fmaxf(pmax, 1e-30f));
+        const float scl = pmax * (1.f / 255.f);
+        int qsum = 0;
+        uint8_t q[KT];
+        for (int kk = 0; kk < KT; ++kk) {
+          const float x = std::min(255.f, std::max(0.f, nearbyintf(pr[kk] * inv)));
+          q[kk] = (uint8_t)x;
+          qsum += q[kk];
+        }
+        bias = fmaf((float)qsum, 128.f * scl, bias);
+        for (int e = 0; e < D; ++e) {
+          uint32_t au = 0;
+          for (int kk = 0; kk < KT; ++kk) {
+            if (!q[kk]) continue;
+            const int8_t v = reinterpret_cast<const int8_t*>(rec + ((size_t)(k0 + kk) * kv_heads + h) * R + D + 4)[e];
+            au += (uint32_t)q[kk] * (uint32_t)(v + 128);
+          }
+          acc[e] = fmaf((float)au, scl, acc[e]);
+        }
+      }
+      for (int e = 0; e < D; ++e) pacc[(size_t)z * D + e] = acc[e] - bias;
+      pm[z] = ntiles > 0 ? m : -INFINITY;
+      pl[z] = l;
+    }
+    float mx = -INFINITY;
+    for (int z = 0; z < nz; ++z) mx = fmaxf(mx, pm[z]);
+    float lt = 0.f;
+    std::vector<float> a(D, 0.f);
+    for (int z = 0; z < nz; ++z) {
+      if (pm[z] == -INFINITY) continue;
+      const float w = exp2f(pm[z] - mx);
+      lt = fmaf(w, pl[z], lt);
+      for (int e = 0; e < D; ++e) a[e] = fmaf(w, pacc[(size_t)z * D + e], a[e]);
+    }
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    for (int e = 0; e < D; ++e) out[(size_t)row * D + e] = a[e] * inv;
+  }
+}
+
 // The verify partial of one cache shard (keys [kv_begin, kv_end) of the sequence, K/V indexed by global
 // position): per row [acc[D] (unnormalised, at the shard's max), max, sum], as lfm3a_verify_partial leaves
 // it for the cross-GPU merge.

@@ -68,6 +68,11 @@ void orc_quantize_q(const uint16_t* q, int64_t q_stride, int tokens, int q_heads
  * records of 2*head_dim+8 bytes (the drafts appended). out: [m][q_heads][head_dim] f32. */
 void orc_verify_i8rec(const uint32_t* qbuf, int m, int q_heads, int kv_heads, int head_dim, const uint8_t* rec,
                       int ctx_len, int window, const uint16_t* gate, int splits, float* out);
+/* Prefill attention over the int8 records with the reference's own arithmetic (kernels/prefill_attn.hip:212-505:
+ * int8 Q x int8 K per 32-dim group, lazy running max, P' = p * v_scale as u8 per row and 64-key tile, u8 x (V + 128)
+ * with the bias taken back, the split merge): out fp32 [tokens * q_heads][head_dim]. */
+void orc_prefill_i8rec(const uint32_t* qbuf, int tokens, int q_heads, int kv_heads, int head_dim, const uint8_t* rec,
+                       int context, int window, int splits, float* out);
 
 /* Verify attention over the cache (drafts already appended at ctx_len..ctx_len+m-1), restating the
  * split-KV page partition, exact running max, fp16 P and the log-sum-exp combine with the optional

@@ -122,3 +122,47 @@ def test_verify_i8_published_case(la, orc, synth, cuda):
     print(f"mode A verify, 8 tokens over 32768: max error vs fp64 {exact:.2e} of the RMS (beyond half an fp16 ulp); "
           f"vs the oracle {pair:.2e}")
     assert pair < TOL_PAIR and exact < TOL
+
+
+# ---------------------------------------------------------------- prefill over the records
+TOL_PREFILL = 2e-2   # against the oracle's restatement: u8 roundings that flip with the exponentials' last bits
+
+
+def run_prefill_i8(la, orc, synth, cuda, seed, context, tokens, q_heads, kv_heads, d, window=0, splits=1):
+    n = context + tokens
+    case = synth.prefill_case(seed, n, q_heads=q_heads, kv_heads=kv_heads, head_dim=d)
+    rope_np = la.rope_table(1e6, 0.5 if d == 128 else 1.0, d, n + 1)
+    cache = la.LayerCache(la.MODE_I8REC, kv_heads, d, n + 64, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0, rope=dev(rope_np.view(np.float16), cuda))
+    qbuf = la.quantize_q(dev(case["Q"][context:], cuda))
+    out = cache.prefill_i8(qbuf, tokens, q_heads, context, window=window, splits=splits)
+    la.sync()
+    rec = cache.logical(n)["rec"]
+    assert np.array_equal(rec, orc.kv_append_i8rec(case["K"], case["V"], 0, rope=rope_np.view(np.float16)))
+    qb = qbuf.cpu().numpy().view(np.uint32)
+    got = out.float().cpu().numpy()
+    if splits <= 0:
+        splits = la.lib().lfm3a_prefill_i8_splits(tokens, q_heads, context, window, 0)
+    want = orc.prefill_i8rec(qb, tokens, q_heads, rec, context, window=window, splits=splits)
+    return got, want, splits
+
+
+@pytest.mark.parametrize("context,tokens,window,splits", [(0, 70, 0, 1), (200, 40, 0, 1), (300, 33, 100, 1),
+                                                          (3000, 96, 0, 3), (5000, 64, 0, 0), (1000, 32, 256, 1),
+                                                          (129, 1, 0, 1)])
+def test_prefill_i8_reference_geometry(la, orc, synth, cuda, context, tokens, window, splits):
+    """lfm3a_prefill_attention_i8 (prefill_attn.hip:212-505 over the records) against the oracle's restatement with
+    the same 32-token blocks and key splits: within 2e-2 of the RMS beyond half an fp16 ulp, and within 1e-3 on
+    average. The default split count of a short chunk over a long context is above 1."""
+    got, want, used = run_prefill_i8(la, orc, synth, cuda, 1000 + tokens + context, context, tokens, 16, 4, 128,
+                                     window, splits)
+    if splits == 0:
+        assert used > 1
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    assert rel_err(got, want) < TOL_PREFILL
+    assert float(np.mean(np.abs(got - want))) / rms < 1e-3
+
+
+def test_prefill_i8_benchmark_geometry(la, orc, synth, cuda):
+    got, want, _ = run_prefill_i8(la, orc, synth, cuda, 1100, 150, 40, 32, 8, 64)
+    assert rel_err(got, want) < TOL_PREFILL
