@@ -135,7 +135,9 @@ int lfm3a_accept(const int32_t* best, const int32_t* tokens, int m, int32_t* sta
 /* Workspace for the split-KV partials of a verify call: m * q_heads * splits * (head_dim + 2) floats. */
 size_t lfm3a_verify_workspace_bytes(int m, int q_heads, int head_dim, int splits);
 
-/* The split count verify attention uses when called with splits <= 0. */
+/* The split count verify attention uses when called with splits <= 0: two CTAs per SM over the kv heads (one
+ * at head_dim 128 for up to 16 tokens), at least two key tiles each; one CTA per SM instead when two would leave
+ * a split fewer than 768 keys and one does not (a long context over few kv heads). */
 int lfm3a_verify_splits(const lfm3a_kv_layout* layout, int ctx_len, int m, int window, int sm_count);
 
 /* DSpark verify attention of m tokens (dspark.hip:1809-2131 attention_v3 / verify_attention_paged and

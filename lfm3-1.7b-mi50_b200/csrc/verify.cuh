@@ -1107,22 +1107,35 @@ __global__ __launch_bounds__(1024) void gather_wait_kernel(__half* region, int w
   const unsigned long long* words = gather_words(region) + (int64_t)((target - 1u) & 1u) * half_stride;
   uint32_t* dst = reinterpret_cast<uint32_t*>(out);
   bool gave_up = false;
-  for (int64_t i = threadIdx.x; i < half_stride && !gave_up; i += blockDim.x) {
-    unsigned long long wv;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(wv) : "l"(words + i) : "memory");
-    if ((unsigned)(wv >> 32) != target) {
-      const uint64_t t0 = globaltimer();
-      for (;;) {
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(wv) : "l"(words + i) : "memory");
-        if ((unsigned)(wv >> 32) == target) break;
-        if (globaltimer() - t0 > wait_limit_ns()) {
-          raise_error(kErrWaitPeer);
-          gave_up = true;
-          break;
+  // A thread's words in batches of kBatch loads issued back to back, then checked: one round trip to L2 per batch
+  // instead of one per word; a word whose flag is not there yet is polled alone (bounded).
+  constexpr int kBatch = 8;
+  for (int64_t base = threadIdx.x; base < half_stride && !gave_up; base += (int64_t)blockDim.x * kBatch) {
+    unsigned long long wv[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int64_t i = base + (int64_t)k * blockDim.x;
+      wv[k] = 0;
+      if (i < half_stride) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(wv[k]) : "l"(words + i) : "memory");
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int64_t i = base + (int64_t)k * blockDim.x;
+      if (i >= half_stride || gave_up) break;
+      if ((unsigned)(wv[k] >> 32) != target) {
+        const uint64_t t0 = globaltimer();
+        for (;;) {
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(wv[k]) : "l"(words + i) : "memory");
+          if ((unsigned)(wv[k] >> 32) == target) break;
+          if (globaltimer() - t0 > wait_limit_ns()) {
+            raise_error(kErrWaitPeer);
+            gave_up = true;
+            break;
+          }
         }
       }
+      if (dst && !gave_up) dst[i] = (uint32_t)wv[k];
     }
-    if (dst && !gave_up) dst[i] = (uint32_t)wv;
   }
   __syncthreads();
   if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(counter) = target;

@@ -90,6 +90,12 @@ def test_split_choice(la):
     lay = la.layout(0, 8, 64)
     assert la.verify_splits(lay, 32768, 16, 0, 148) == 37
     assert la.verify_splits(lay, 131072, 16, 0, 148) == 37
+    # one kv head (a GPU's share on eight): 296 splits would stream 443 keys each, 148 stream 886
+    one = la.layout(0, 1, 64)
+    assert la.verify_splits(one, 131072, 16, 0, 148) == 148
+    assert la.verify_splits(la.layout(0, 2, 64), 131072, 16, 0, 148) == 148
+    assert la.verify_splits(la.layout(0, 4, 64), 131072, 16, 0, 148) == 74
+    assert la.verify_splits(lay, 8192, 16, 0, 148) == 32   # mid contexts keep two per SM
     assert la.verify_splits(lay, 100, 8, 0, 148) == 1
     assert la.verify_splits(lay, 20, 8, 0, 148) == 1
     assert la.verify_splits(lay, 1024, 8, 0, 148) == 4     # 128-key tiles for m <= 16
