@@ -238,10 +238,12 @@ int run_verify(const lfm3a_kv_view* kv, const void* q, int m, int q_heads, int k
   else rc = ensure_smem(verify_kernel<false>, kVfSmem, done[0]);
   if (rc != LFM3A_OK) return rc;
   if (app) {
-    // The appending split gives up kAppendTiles tiles of attention (the append takes about that long) when
-    // it keeps at least two; it must hold every 64-token block the drafts touch.
-    constexpr int kAppendTiles = 2;
-    const int lighten = a.splits > 1 && a.t_total / a.splits >= kAppendTiles + 2 ? kAppendTiles : 0;
+    // The appending split gives up tiles of attention for the append: a per-CTA timeline at configs 2 and 3
+    // put the append at 5.4-7.2 us (its global round trips wait behind the whole GPU's K/V stream) against
+    // 1.35 us a tile, so up to kAppendTiles, keeping at least two; it must hold every 64-token block the
+    // drafts touch.
+    constexpr int kAppendTiles = 5;
+    const int lighten = a.splits > 1 ? std::max(0, std::min(kAppendTiles, a.t_total / a.splits - 2)) : 0;
     const int span = a.t_total + lighten;
     const int last_tile0 = a.t_begin + std::min(a.t_total, (int)((int64_t)span * (a.splits - 1) / a.splits));
     const bool fuse = m <= 16 && last_tile0 * tile_keys <= app->pos0 / kQuantBlock * kQuantBlock;
