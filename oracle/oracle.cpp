@@ -18,7 +18,7 @@ namespace {
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LAZY = 8.f;   // prefill_attn.hip:33: rescale only when a tile beats the max by 2^8
 constexpr int BS = 32;        // KV block tokens (engine.go:31)
-constexpr int QB = 64;        // prefill key tile and int8 V block (prefill_attn.hip:29)
+constexpr int QB = 64;        // prefill key tile and int8 V block (prefill_attn.hip:29; the benchmark's config 4)
 
 inline float r16(float x) { return orc_f16_to_f32(orc_f32_to_f16(x)); }
 
