@@ -600,27 +600,28 @@ def measure_ref_i8_prefill(la, dev, tokens: int, context: int, reps: int = 3) ->
     splits = la.lib().lfm3a_prefill_i8_splits(tokens, qh, context, 0, 0)
     ws = torch.empty(tokens * qh * splits * (d + 2) * 4, dtype=torch.uint8, device=dev)
 
-    def call():
-        la.quantize_q(q, out=qbuf)
-        cache.prefill_i8(qbuf, tokens, qh, context, out=out, workspace=ws, splits=splits)
-
-    call()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        call()
-    e1.record()
-    torch.cuda.synchronize()
-    la.sync()
-    ms = e0.elapsed_time(e1) / reps
     qk = 2.0 * qh * d * (tokens * context + tokens * (tokens + 1) / 2)
     res = {"workload": f"the reference's prefill arithmetic on its int8 records, 16/4/128: {tokens} tokens over "
-                       f"{context} cached", "ms": round(ms, 3), "splits": splits,
-           "tops_qk_plus_pv": round(2 * qk / (ms * 1e-3) / 1e12, 1)}
+                       f"{context} cached", "splits": splits}
     ref = REF_MI50_PREFILL_MS.get((tokens, context))
-    if ref:
-        res["reference_mi50_ms"] = ref["int8_pv"]
+    for name, exact in (("int8_pv", False), ("exact", True)):
+        def call():
+            la.quantize_q(q, out=qbuf)
+            cache.prefill_i8(qbuf, tokens, qh, context, out=out, workspace=ws, splits=splits, exact=exact)
+
+        call()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            call()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"ms": round(ms, 3), "tops_qk_plus_pv": round(2 * qk / (ms * 1e-3) / 1e12, 1)}
+        if ref:
+            res[name]["reference_mi50_ms"] = ref[name]
+    la.sync()
     del cache
     return res
 

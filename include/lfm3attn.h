@@ -248,16 +248,19 @@ int lfm3a_verify_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int
  * CTA per SM). */
 int lfm3a_prefill_i8_splits(int tokens, int q_heads, int context, int window, int sm_count);
 
-/* Causal (optionally sliding-window) prefill attention over MODE_I8REC records with the reference's own arithmetic
- * (kernels/prefill_attn.hip:212-505, the engine's default prefill attention): the tokens' queries quantised by
- * lfm3a_quantize_q (qbuf), int8 Q x int8 K per 32-dim group, the lazy running max (2^8), P' = p * v_scale as u8
- * per row and 64-key tile against the tile's largest P', u8 x (int8 V + 128) with the bias taken back, blocks of
- * 32 query tokens and the reference's key splits, merged by the combine. The tokens' records must already be
- * appended at context .. context + tokens - 1 (lfm3a_kv_append on the MODE_I8REC view). out: device fp16
- * [tokens][q_heads][head_dim]. workspace: tokens * q_heads * splits * (head_dim + 2) * 4 bytes (needed for every
- * split count; splits <= 0: lfm3a_prefill_i8_splits, at most 64). q_heads = 4 * kv_heads, head_dim 64 or 128. */
+/* Causal (optionally sliding-window) prefill attention over MODE_I8REC records with the reference's own arithmetic,
+ * the tokens' queries quantised by lfm3a_quantize_q (qbuf), int8 Q x int8 K per 32-dim group:
+ *   exact = 0 (kernels/prefill_attn.hip:212-505, the engine's default): the lazy running max (2^8), P' = p * v_scale
+ *     as u8 per row and 64-key tile against the tile's largest P', u8 x (int8 V + 128) with the bias taken back;
+ *   exact = 1 (kernels/prefill_attn_exact.hip:173-344, --exact-attention): an exact running max,
+ *     P' = fp16(p * v_scale * 4096) x V in fp32, out = acc / (l * 4096).
+ * Blocks of 32 query tokens and the reference's key splits (the exact kernel's splits are an extension), merged by
+ * the combine. The tokens' records must already be appended at context .. context + tokens - 1 (lfm3a_kv_append on
+ * the MODE_I8REC view). out: device fp16 [tokens][q_heads][head_dim]. workspace: tokens * q_heads * splits *
+ * (head_dim + 2) * 4 bytes (needed for every split count; splits <= 0: lfm3a_prefill_i8_splits, at most 64).
+ * q_heads = 4 * kv_heads, head_dim 64 or 128. */
 int lfm3a_prefill_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int tokens, int q_heads, int context,
-                               int window, void* out, void* workspace, size_t workspace_bytes, int splits,
+                               int window, int exact, void* out, void* workspace, size_t workspace_bytes, int splits,
                                void* stream);
 
 /* ---------------------------------------------------------------- drafter ring attention

@@ -363,6 +363,10 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
 //       products stay below 2^24), plus 128 sum(q): the reference's u8 x (v + 128) dot, then
 //       acc = fma(that, sc, acc) (:320-350);
 //   the split's partial: acc - bias, m (-inf without tiles), l, merged by the combine kernel (:489-505).
+// EXACT: the --exact-attention kernel over the same bytes (prefill_attn_exact.hip:173-344): s = sum_g float(dot_g) qs_g
+// from 0, times k_scale (1 / sqrt(D)) log2 e; an exact running max per tile (corr = 2^(m - mn), l = l corr + sum p);
+// P' = fp16(p v_scale 4096) times V's int8 made fp16, accumulated in fp32 by the MMAs across tiles (no per-tile fold);
+// the partial acc / 4096, m, l.
 struct PrefillI8Args {
   KvGeom g;
   const uint32_t* qbuf;   // [tokens * q_heads][D / 4 + D / 32] (quantize_q rows)
@@ -380,7 +384,7 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int D>
+template <int D, bool EXACT>
 __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) {
   constexpr int REC = 2 * D + 8, NG = D / 32, NJ = D / 8, KT = 64, QT = 32, CH = REC / 8;
   constexpr float LAZY = 8.f, MAGIC_F = 12582912.f;
@@ -444,7 +448,8 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
   float acc[NJ][4];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  float mA = 0.f, mB = 0.f, lA = 0.f, lB = 0.f, bA = 0.f, bB = 0.f;   // l and the bias: this thread's keys
+  // l and the bias: this thread's keys. The int8-PV max starts at 0 (the reference's), the exact one at -inf.
+  float mA = EXACT ? -INFINITY : 0.f, mB = EXACT ? -INFINITY : 0.f, lA = 0.f, lB = 0.f, bA = 0.f, bB = 0.f;
 
   if (ntiles > 0) load(0);
   for (int s = 0; s < ntiles; ++s) {
@@ -462,19 +467,25 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const uint8_t* krec = tl + (8 * n + gid) * REC;
-      float sv[4] = {qcA, qcA, qcB, qcB};
+      float sv[4] = {EXACT ? 0.f : qcA, EXACT ? 0.f : qcA, EXACT ? 0.f : qcB, EXACT ? 0.f : qcB};
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
         int d4[4] = {MAGIC_I, MAGIC_I, MAGIC_I, MAGIC_I};
         const uint2 kb = *reinterpret_cast<const uint2*>(krec + 32 * g + 8 * tig);
         mma_s8_16832(d4, qa[g], kb.x, kb.y);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sv[e] = fmaf(__int_as_float(d4[e]), e < 2 ? qsA[g] : qsB[g], sv[e]);
+        for (int e = 0; e < 4; ++e) {
+          const float d = EXACT ? __int_as_float(d4[e]) - MAGIC_F : __int_as_float(d4[e]);   // exact: float(dot)
+          sv[e] = fmaf(d, e < 2 ? qsA[g] : qsB[g], sv[e]);
+        }
       }
       const float ks0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + D) * a.kscale;
       const float ks1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + D) * a.kscale;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) u[n][e] = fmaf(sv[e], (e & 1) ? ks1 : ks0, -(e < 2 ? mA : mB));
+      for (int e = 0; e < 4; ++e) {
+        const float ks = (e & 1) ? ks1 : ks0;
+        u[n][e] = EXACT ? sv[e] * ks : fmaf(sv[e], ks, -(e < 2 ? mA : mB));
+      }
     }
     const bool interior = k0 + KT - 1 <= qfirst && k0 >= kbegin && (a.window == 0 || k0 > qlast - a.window);
     if (!interior || !okB) {
@@ -489,8 +500,7 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
           u[n][e] = valid ? u[n][e] : -INFINITY;
         }
     }
-    // ---- the lazy running max (the rows' tile maxima over the quad)
-    float tA_ = -INFINITY, tB_ = -INFINITY;
+    float tA_ = -INFINITY, tB_ = -INFINITY;   // the rows' tile maxima over the quad
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       tA_ = fmaxf(tA_, fmaxf(u[n][0], u[n][1]));
@@ -501,18 +511,14 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       tA_ = fmaxf(tA_, __shfl_xor_sync(0xffffffffu, tA_, o));
       tB_ = fmaxf(tB_, __shfl_xor_sync(0xffffffffu, tB_, o));
     }
-    if (__any_sync(0xffffffffu, tA_ > LAZY || tB_ > LAZY) || s == 0) {
-      const float tmA = tA_ + mA, tmB = tB_ + mB;
-      const bool upA = tmA > -INFINITY && (s == 0 || tmA > mA + LAZY);
-      const bool upB = tmB > -INFINITY && (s == 0 || tmB > mB + LAZY);
-      const float dA = upA ? mA - tmA : 0.f, dB = upB ? mB - tmB : 0.f;
-      const float cA = fast_exp2(dA), cB = fast_exp2(dB);
-      mA = upA ? tmA : mA;
-      mB = upB ? tmB : mB;
-      lA *= cA;
-      lB *= cB;
-      bA *= cA;
-      bB *= cB;
+    uint32_t pf[4][4];   // P as fp16 A fragments of the four 16-key k-steps
+    float scA = 0.f, scB = 0.f, biasA = 0.f, biasB = 0.f;
+    if constexpr (EXACT) {
+      // ---- exact running max; P' = fp16(p v_scale 4096)
+      const float mnA = fmaxf(mA, tA_), mnB = fmaxf(mB, tB_);
+      const float cA = mA == -INFINITY ? 0.f : fast_exp2(mA - mnA), cB = mB == -INFINITY ? 0.f : fast_exp2(mB - mnB);
+      mA = mnA;
+      mB = mnB;
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
         acc[j][0] *= cA;
@@ -520,62 +526,104 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
         acc[j][2] *= cB;
         acc[j][3] *= cB;
       }
+      float psA = 0.f, psB = 0.f;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-        u[n][0] += dA;
-        u[n][1] += dA;
-        u[n][2] += dB;
-        u[n][3] += dB;
+        const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + 2 * D + 4) * kPScale;
+        const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + 2 * D + 4) * kPScale;
+        float pv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mn = e < 2 ? mnA : mnB;
+          pv[e] = mn == -INFINITY ? 0.f : fast_exp2(u[n][e] - mn);
+          if (e < 2) psA += pv[e];
+          else psB += pv[e];
+        }
+        pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(pv[0] * vs0, pv[1] * vs1);
+        pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(pv[2] * vs0, pv[3] * vs1);
       }
-    }
-    // ---- P' = 2^u v_scale, l += 2^u; u8 against the row's largest P' of the tile
-    float pmA = 0.f, pmB = 0.f;
+      lA = lA * cA + psA;
+      lB = lB * cB + psB;
+    } else {
+      // ---- the lazy running max
+      if (__any_sync(0xffffffffu, tA_ > LAZY || tB_ > LAZY) || s == 0) {
+        const float tmA = tA_ + mA, tmB = tB_ + mB;
+        const bool upA = tmA > -INFINITY && (s == 0 || tmA > mA + LAZY);
+        const bool upB = tmB > -INFINITY && (s == 0 || tmB > mB + LAZY);
+        const float dA = upA ? mA - tmA : 0.f, dB = upB ? mB - tmB : 0.f;
+        const float cA = fast_exp2(dA), cB = fast_exp2(dB);
+        mA = upA ? tmA : mA;
+        mB = upB ? tmB : mB;
+        lA *= cA;
+        lB *= cB;
+        bA *= cA;
+        bB *= cB;
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + 2 * D + 4);
-      const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + 2 * D + 4);
+        for (int j = 0; j < NJ; ++j) {
+          acc[j][0] *= cA;
+          acc[j][1] *= cA;
+          acc[j][2] *= cB;
+          acc[j][3] *= cB;
+        }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float ex = fast_exp2(u[n][e]);
-        if (e < 2) lA += ex;
-        else lB += ex;
-        u[n][e] = ex * ((e & 1) ? vs1 : vs0);   // u now holds P'
+        for (int n = 0; n < 8; ++n) {
+          u[n][0] += dA;
+          u[n][1] += dA;
+          u[n][2] += dB;
+          u[n][3] += dB;
+        }
       }
-      pmA = fmaxf(pmA, fmaxf(u[n][0], u[n][1]));
-      pmB = fmaxf(pmB, fmaxf(u[n][2], u[n][3]));
-    }
+      // ---- P' = 2^u v_scale, l += 2^u; u8 against the row's largest P' of the tile
+      float pmA = 0.f, pmB = 0.f;
 #pragma unroll
-    for (int o = 1; o <= 2; o <<= 1) {
-      pmA = fmaxf(pmA, __shfl_xor_sync(0xffffffffu, pmA, o));
-      pmB = fmaxf(pmB, __shfl_xor_sync(0xffffffffu, pmB, o));
-    }
-    const float invA = 255.f * __frcp_rn(fmaxf(pmA, 1e-30f)), invB = 255.f * __frcp_rn(fmaxf(pmB, 1e-30f));
-    const float scA = pmA * (1.f / 255.f), scB = pmB * (1.f / 255.f);
-    int qsumA = 0, qsumB = 0;
-    uint32_t pf[4][4];   // the u8 probabilities as fp16 A fragments of the four 16-key k-steps
+      for (int n = 0; n < 8; ++n) {
+        const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + 2 * D + 4);
+        const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + 2 * D + 4);
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      float qv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float x = fminf(u[n][e] * (e < 2 ? invA : invB), 255.f);
-        const int q = (int)(__float_as_uint(x + 12582912.f) & 0xffu);   // nearest even, in [0, 255]
-        qv[e] = (float)q;
-        if (e < 2) qsumA += q;
-        else qsumB += q;
+        for (int e = 0; e < 4; ++e) {
+          const float ex = fast_exp2(u[n][e]);
+          if (e < 2) lA += ex;
+          else lB += ex;
+          u[n][e] = ex * ((e & 1) ? vs1 : vs0);   // u now holds P'
+        }
+        pmA = fmaxf(pmA, fmaxf(u[n][0], u[n][1]));
+        pmB = fmaxf(pmB, fmaxf(u[n][2], u[n][3]));
       }
-      pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(qv[0], qv[1]);
-      pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(qv[2], qv[3]);
-    }
-    bA = fmaf((float)qsumA, 128.f * scA, bA);
-    bB = fmaf((float)qsumB, 128.f * scB, bB);
 #pragma unroll
-    for (int o = 1; o <= 2; o <<= 1) {
-      qsumA += __shfl_xor_sync(0xffffffffu, qsumA, o);
-      qsumB += __shfl_xor_sync(0xffffffffu, qsumB, o);
+      for (int o = 1; o <= 2; o <<= 1) {
+        pmA = fmaxf(pmA, __shfl_xor_sync(0xffffffffu, pmA, o));
+        pmB = fmaxf(pmB, __shfl_xor_sync(0xffffffffu, pmB, o));
+      }
+      const float invA = 255.f * __frcp_rn(fmaxf(pmA, 1e-30f)), invB = 255.f * __frcp_rn(fmaxf(pmB, 1e-30f));
+      scA = pmA * (1.f / 255.f);
+      scB = pmB * (1.f / 255.f);
+      int qsumA = 0, qsumB = 0;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        float qv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = fminf(u[n][e] * (e < 2 ? invA : invB), 255.f);
+          const int q = (int)(__float_as_uint(x + 12582912.f) & 0xffu);   // nearest even, in [0, 255]
+          qv[e] = (float)q;
+          if (e < 2) qsumA += q;
+          else qsumB += q;
+        }
+        pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(qv[0], qv[1]);
+        pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(qv[2], qv[3]);
+      }
+      bA = fmaf((float)qsumA, 128.f * scA, bA);
+      bB = fmaf((float)qsumB, 128.f * scB, bB);
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        qsumA += __shfl_xor_sync(0xffffffffu, qsumA, o);
+        qsumB += __shfl_xor_sync(0xffffffffu, qsumB, o);
+      }
+      biasA = 128.f * (float)qsumA;   // the + 128 of every V byte
+      biasB = 128.f * (float)qsumB;
     }
-    const float biasA = 128.f * (float)qsumA, biasB = 128.f * (float)qsumB;   // the + 128 of every V byte
-    // ---- PV in passes of 32 dims: dot = sum_k q_k v_k exactly, then acc = fma(dot + 128 sum q, sc, acc)
+    // ---- PV in passes of 32 dims. Int8-PV: dot = sum_k q_k v_k exactly, then acc = fma(dot + 128 sum q, sc, acc);
+    // exact: the fp16 P' x V straight into acc.
     constexpr int NP = NJ / 4;   // passes; a pass covers 4 n-tiles (one V word per key)
 #pragma unroll
     for (int half = 0; half < NP; ++half) {
@@ -592,15 +640,18 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
         const uint32_t w0 = v0[half], w1 = v1[half], w8 = v8[half], w9 = v9[half];
 #pragma unroll
         for (int by = 0; by < 4; ++by)
-          mma_f16_16816(dot[by], pf[kk], s8pair_to_f16x2(w0, w1, by), s8pair_to_f16x2(w8, w9, by));
+          mma_f16_16816(EXACT ? acc[4 * half + by] : dot[by], pf[kk], s8pair_to_f16x2(w0, w1, by),
+                        s8pair_to_f16x2(w8, w9, by));
       }
+      if constexpr (!EXACT) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int jn = 4 * half + j;
-        acc[jn][0] = fmaf(dot[j][0] + biasA, scA, acc[jn][0]);
-        acc[jn][1] = fmaf(dot[j][1] + biasA, scA, acc[jn][1]);
-        acc[jn][2] = fmaf(dot[j][2] + biasB, scB, acc[jn][2]);
-        acc[jn][3] = fmaf(dot[j][3] + biasB, scB, acc[jn][3]);
+        for (int j = 0; j < 4; ++j) {
+          const int jn = 4 * half + j;
+          acc[jn][0] = fmaf(dot[j][0] + biasA, scA, acc[jn][0]);
+          acc[jn][1] = fmaf(dot[j][1] + biasA, scA, acc[jn][1]);
+          acc[jn][2] = fmaf(dot[j][2] + biasB, scB, acc[jn][2]);
+          acc[jn][3] = fmaf(dot[j][3] + biasB, scB, acc[jn][3]);
+        }
       }
     }
     __syncthreads();   // every warp is done with this buffer before the copy of tile s + 2 lands in it
@@ -616,14 +667,15 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     if (!(half ? okB : okA)) continue;
-    const float bias = half ? bB : bA;
+    // int8-PV: acc - bias; exact: acc / 4096 (P' carried the 4096)
+    const float bias = EXACT ? 0.f : (half ? bB : bA), mul = EXACT ? 1.f / kPScale : 1.f;
     float* dst = a.part + ((half ? rowB : rowA) * nz + z) * (D + 2);
 #pragma unroll
     for (int jn = 0; jn < NJ; jn += 2) {
       *reinterpret_cast<float2*>(dst + NJ * (2 * tig) + jn) =
-          make_float2(acc[jn][2 * half] - bias, acc[jn + 1][2 * half] - bias);
+          make_float2((acc[jn][2 * half] - bias) * mul, (acc[jn + 1][2 * half] - bias) * mul);
       *reinterpret_cast<float2*>(dst + NJ * (2 * tig + 1) + jn) =
-          make_float2(acc[jn][2 * half + 1] - bias, acc[jn + 1][2 * half + 1] - bias);
+          make_float2((acc[jn][2 * half + 1] - bias) * mul, (acc[jn + 1][2 * half + 1] - bias) * mul);
     }
     if (tig == 0) {
       dst[D] = ntiles > 0 ? (half ? mB : mA) : -INFINITY;

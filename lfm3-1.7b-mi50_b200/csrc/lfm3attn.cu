@@ -880,7 +880,7 @@ int lfm3a_prefill_i8_splits(int tokens, int q_heads, int context, int window, in
 }
 
 int lfm3a_prefill_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int tokens, int q_heads, int context,
-                               int window, void* out, void* workspace, size_t workspace_bytes, int splits,
+                               int window, int exact, void* out, void* workspace, size_t workspace_bytes, int splits,
                                void* stream) {
   int rc = check_view(kv);
   if (rc != LFM3A_OK) return rc;
@@ -909,8 +909,10 @@ int lfm3a_prefill_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, in
   a.kscale = (1.f / sqrtf((float)D)) * kLog2e;
   const cudaStream_t st = as_stream(stream);
   const dim3 grid(a.qtiles, H, splits);
-  if (D == 128) launch_pdl(prefill_i8rec_kernel<128>, grid, 256, 0, st, a);
-  else launch_pdl(prefill_i8rec_kernel<64>, grid, 256, 0, st, a);
+  if (D == 128 && exact) launch_pdl(prefill_i8rec_kernel<128, true>, grid, 256, 0, st, a);
+  else if (D == 128) launch_pdl(prefill_i8rec_kernel<128, false>, grid, 256, 0, st, a);
+  else if (exact) launch_pdl(prefill_i8rec_kernel<64, true>, grid, 256, 0, st, a);
+  else launch_pdl(prefill_i8rec_kernel<64, false>, grid, 256, 0, st, a);
   rc = check_launch("prefill_i8rec_kernel");
   if (rc != LFM3A_OK) return rc;
   return launch_combine(a.part, tokens * q_heads, splits, D, D + 2, (int64_t)splits * (D + 2), nullptr,

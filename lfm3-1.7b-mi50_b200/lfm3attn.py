@@ -85,7 +85,7 @@ SIGNATURES = {
     "lfm3a_verify_round": (_I, [ctypes.POINTER(KvView), _P, _P, _I64, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _SZ, _I,
                                 _P]),
     "lfm3a_prefill_i8_splits": (_I, [_I, _I, _I, _I, _I]),
-    "lfm3a_prefill_attention_i8": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
+    "lfm3a_prefill_attention_i8": (_I, [ctypes.POINTER(KvView), _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
     "lfm3a_verify_round_host": (_I, [ctypes.POINTER(KvView), _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _SZ,
                                      _I, _P, _I]),
     "lfm3a_ring_table": (_I, [_I, _I, _P]),
@@ -337,9 +337,10 @@ class LayerCache:
         return out
 
     def prefill_i8(self, qbuf, tokens: int, q_heads: int, context: int, window: int = 0, out=None, workspace=None,
-                   splits: int = 0, stream=None):
-        """Prefill attention over this MODE_I8REC cache with the reference's arithmetic (prefill_attn.hip:212-505):
-        qbuf = quantize_q(q) of the tokens (appended at context ..); returns fp16 [tokens][q_heads][head_dim]."""
+                   splits: int = 0, stream=None, exact: bool = False):
+        """Prefill attention over this MODE_I8REC cache with the reference's arithmetic (prefill_attn.hip:212-505;
+        exact: prefill_attn_exact.hip:173-344): qbuf = quantize_q(q) of the tokens (appended at context ..);
+        returns fp16 [tokens][q_heads][head_dim]."""
         import torch
 
         d = self.head_dim
@@ -352,7 +353,8 @@ class LayerCache:
                                     device=qbuf.device)
         ws_bytes = workspace.numel() * workspace.element_size()
         _check(lib().lfm3a_prefill_attention_i8(ctypes.byref(self.view), _ptr(qbuf), tokens, q_heads, context, window,
-                                                _ptr(out), _ptr(workspace), ws_bytes, splits, _stream(stream)))
+                                                int(exact), _ptr(out), _ptr(workspace), ws_bytes, splits,
+                                                _stream(stream)))
         return out
 
     def verify_i8(self, qbuf, m: int, q_heads: int, ctx_len: int, window: int = 0, gate=None, out=None,

@@ -563,6 +563,104 @@ void orc_prefill_i8rec(const uint32_t* qbuf, int tokens, int q_heads, int kv_hea
   }
 }
 
+// The exact prefill over the int8 records (kernels/prefill_attn_exact.hip:173-344, the --exact-attention option):
+// per (token, head) row, tiles of 64 keys from kbegin / 64 * 64 (kbegin from the row's 32-token block and the window,
+// which gives the same result as the reference's 16-token blocks: fully masked tiles change nothing);
+//   s = sum_g float(dot_g) qs_g (from 0, groups in order), s = s * k_scale (1 / sqrt(D)) log2 e, masked keys -inf
+//   (:247-285);
+//   exact running max per tile: mn = max(m, tile max), corr = 2^(m - mn) (0 while m is -inf), l = l corr + sum p,
+//   acc *= corr, p = 2^(s - mn) (:287-302);
+//   P' = fp16(p * v_scale * 4096), acc += P' * float(v) in fp32 (:303-331);
+//   out = acc / (l * 4096) (:333-344).
+// exp2f in place of the reference's degree-4 polynomial (~1e-4 relative; within the fp16 rounding of P').
+// Key splits (an extension: the reference's exact kernel does not split): as orc_prefill_i8rec's, each split's
+// partial (acc / 4096, m, l) merged as there.
+void orc_prefill_i8rec_exact(const uint32_t* qbuf, int tokens, int q_heads, int kv_heads, int head_dim,
+                             const uint8_t* rec, int context, int window, int splits, float* out) {
+  const int D = head_dim, G = q_heads / kv_heads, R = 2 * D + 8, NG = D / 32, qrow = D / 4 + D / 32;
+  constexpr int KT = 64, QT = 32;
+  constexpr float PSCALE = 4096.f;
+  const float kscale = (1.f / sqrtf((float)D)) * LOG2E;
+  const int nz = std::max(1, splits);
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int row = 0; row < tokens * q_heads; ++row) {
+    const int t = row / q_heads, qh = row % q_heads, h = qh / G;
+    const int t0 = t / QT * QT, ntok = std::min(QT, tokens - t0);
+    const int qpos = context + t, qfirst = context + t0, kend = context + t0 + ntok;
+    const int kbegin = window > 0 ? std::max(0, qfirst - window + 1) : 0;
+    const int kt_begin = kbegin / KT * KT, all_tiles = (kend - kt_begin + KT - 1) / KT;
+    const int8_t* q8 = reinterpret_cast<const int8_t*>(qbuf + (size_t)row * qrow);
+    float qs[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int g = 0; g < NG; ++g) memcpy(&qs[g], qbuf + (size_t)row * qrow + D / 4 + g, 4);
+    std::vector<float> pacc((size_t)nz * D), pm(nz), pl(nz);
+    for (int z = 0; z < nz; ++z) {
+      const int tile_lo = all_tiles * z / nz, ntiles = all_tiles * (z + 1) / nz - tile_lo;
+      float m = -INFINITY, l = 0.f;
+      std::vector<float> acc(D, 0.f);
+      for (int s = 0; s < ntiles; ++s) {
+        const int k0 = kt_begin + (tile_lo + s) * KT;
+        float sc[KT];
+        float mx = -INFINITY;
+        for (int kk = 0; kk < KT; ++kk) {
+          const int kpos = k0 + kk;
+          const bool valid = kpos <= qpos && kpos >= kbegin && (window == 0 || kpos > qpos - window);
+          if (!valid) {
+            sc[kk] = -INFINITY;
+            continue;
+          }
+          const uint8_t* r = rec + ((size_t)kpos * kv_heads + h) * R;
+          const int8_t* k8 = reinterpret_cast<const int8_t*>(r);
+          float ks;
+          memcpy(&ks, r + D, 4);
+          float v = 0.f;
+          for (int g = 0; g < NG; ++g) {
+            int dot = 0;
+            for (int d = 32 * g; d < 32 * g + 32; ++d) dot += (int)q8[d] * (int)k8[d];
+            v = fmaf((float)dot, qs[g], v);
+          }
+          sc[kk] = v * (ks * kscale);
+          mx = fmaxf(mx, sc[kk]);
+        }
+        const float mn = fmaxf(m, mx);
+        const float corr = m == -INFINITY ? 0.f : exp2f(m - mn);
+        m = mn;
+        float ps = 0.f;
+        float pr[KT];
+        for (int kk = 0; kk < KT; ++kk) {
+          pr[kk] = sc[kk] == -INFINITY ? 0.f : exp2f(sc[kk] - mn);
+          ps += pr[kk];
+        }
+        l = l * corr + ps;
+        for (int e = 0; e < D; ++e) acc[e] *= corr;
+        for (int kk = 0; kk < KT; ++kk) {
+          if (pr[kk] == 0.f) continue;
+          const uint8_t* r = rec + ((size_t)(k0 + kk) * kv_heads + h) * R;
+          float vs;
+          memcpy(&vs, r + 2 * D + 4, 4);
+          const float p16 = r16(pr[kk] * (vs * PSCALE));
+          const int8_t* v8 = reinterpret_cast<const int8_t*>(r + D + 4);
+          for (int e = 0; e < D; ++e) acc[e] += p16 * (float)v8[e];
+        }
+      }
+      for (int e = 0; e < D; ++e) pacc[(size_t)z * D + e] = acc[e] * (1.f / PSCALE);
+      pm[z] = ntiles > 0 ? m : -INFINITY;
+      pl[z] = l;
+    }
+    float mxz = -INFINITY;
+    for (int z = 0; z < nz; ++z) mxz = fmaxf(mxz, pm[z]);
+    float lt = 0.f;
+    std::vector<float> a(D, 0.f);
+    for (int z = 0; z < nz; ++z) {
+      if (pm[z] == -INFINITY) continue;
+      const float w = exp2f(pm[z] - mxz);
+      lt = fmaf(w, pl[z], lt);
+      for (int e = 0; e < D; ++e) a[e] = fmaf(w, pacc[(size_t)z * D + e], a[e]);
+    }
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    for (int e = 0; e < D; ++e) out[(size_t)row * D + e] = a[e] * inv;
+  }
+}
+
 // The verify partial of one cache shard (keys [kv_begin, kv_end) of the sequence, K/V indexed by global
 // position): per row [acc[D] (unnormalised, at the shard's max), max, sum], as lfm3a_verify_partial leaves
 // it for the cross-GPU merge.

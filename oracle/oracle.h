@@ -73,6 +73,11 @@ void orc_verify_i8rec(const uint32_t* qbuf, int m, int q_heads, int kv_heads, in
  * with the bias taken back, the split merge): out fp32 [tokens * q_heads][head_dim]. */
 void orc_prefill_i8rec(const uint32_t* qbuf, int tokens, int q_heads, int kv_heads, int head_dim, const uint8_t* rec,
                        int context, int window, int splits, float* out);
+/* The exact prefill over the int8 records (kernels/prefill_attn_exact.hip:173-344: exact running max,
+ * P' = fp16(p * v_scale * 4096) x V in fp32, out = acc / (l * 4096)), with the same blocks and splits as
+ * orc_prefill_i8rec. */
+void orc_prefill_i8rec_exact(const uint32_t* qbuf, int tokens, int q_heads, int kv_heads, int head_dim,
+                             const uint8_t* rec, int context, int window, int splits, float* out);
 
 /* Verify attention over the cache (drafts already appended at ctx_len..ctx_len+m-1), restating the
  * split-KV page partition, exact running max, fp16 P and the log-sum-exp combine with the optional

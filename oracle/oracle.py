@@ -31,6 +31,7 @@ _SIGS = {
     "orc_quantize_q": (None, [_P, ctypes.c_int64, _I, _I, _I, _P]),
     "orc_verify_i8rec": (None, [_P, _I, _I, _I, _I, _P, _I, _I, _P, _I, _P]),
     "orc_prefill_i8rec": (None, [_P, _I, _I, _I, _I, _P, _I, _I, _I, _P]),
+    "orc_prefill_i8rec_exact": (None, [_P, _I, _I, _I, _I, _P, _I, _I, _I, _P]),
     "orc_verify_partial": (None, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _I, _I, _P]),
     "orc_combine": (None, [_P, _I, _I, _I, _P, _P]),
     "orc_attention_f64": (None, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P]),
@@ -179,16 +180,18 @@ def verify_i8rec(qbuf, m: int, q_heads: int, rec, ctx_len: int, window: int = 0,
     return out
 
 
-def prefill_i8rec(qbuf, tokens: int, q_heads: int, rec, context: int, window: int = 0, splits: int = 1) -> np.ndarray:
-    """prefill_attn.hip:212-505 over int8 records rec [context + tokens][kv_heads][2 * head_dim + 8] uint8 with the
-    query rows qbuf (quantize_q of the tokens) -> out [tokens][q_heads][head_dim] float32."""
+def prefill_i8rec(qbuf, tokens: int, q_heads: int, rec, context: int, window: int = 0, splits: int = 1,
+                  exact: bool = False) -> np.ndarray:
+    """prefill_attn.hip:212-505 (exact: prefill_attn_exact.hip:173-344) over int8 records
+    rec [context + tokens][kv_heads][2 * head_dim + 8] uint8 with the query rows qbuf (quantize_q of the tokens)
+    -> out [tokens][q_heads][head_dim] float32."""
     rec = np.ascontiguousarray(rec, dtype=np.uint8)
     kvh, rb = rec.shape[1], rec.shape[2]
     d = (rb - 8) // 2
     qbuf = np.ascontiguousarray(qbuf, dtype=np.uint32)
     out = np.empty((tokens, q_heads, d), dtype=np.float32)
-    lib().orc_prefill_i8rec(qbuf.ctypes.data, tokens, q_heads, kvh, d, rec.ctypes.data, context, window, splits,
-                            out.ctypes.data)
+    fn = lib().orc_prefill_i8rec_exact if exact else lib().orc_prefill_i8rec
+    fn(qbuf.ctypes.data, tokens, q_heads, kvh, d, rec.ctypes.data, context, window, splits, out.ctypes.data)
     return out
 
 

@@ -128,14 +128,14 @@ def test_verify_i8_published_case(la, orc, synth, cuda):
 TOL_PREFILL = 2e-2   # against the oracle's restatement: u8 roundings that flip with the exponentials' last bits
 
 
-def run_prefill_i8(la, orc, synth, cuda, seed, context, tokens, q_heads, kv_heads, d, window=0, splits=1):
+def run_prefill_i8(la, orc, synth, cuda, seed, context, tokens, q_heads, kv_heads, d, window=0, splits=1, exact=False):
     n = context + tokens
     case = synth.prefill_case(seed, n, q_heads=q_heads, kv_heads=kv_heads, head_dim=d)
     rope_np = la.rope_table(1e6, 0.5 if d == 128 else 1.0, d, n + 1)
     cache = la.LayerCache(la.MODE_I8REC, kv_heads, d, n + 64, device=cuda)
     cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0, rope=dev(rope_np.view(np.float16), cuda))
     qbuf = la.quantize_q(dev(case["Q"][context:], cuda))
-    out = cache.prefill_i8(qbuf, tokens, q_heads, context, window=window, splits=splits)
+    out = cache.prefill_i8(qbuf, tokens, q_heads, context, window=window, splits=splits, exact=exact)
     la.sync()
     rec = cache.logical(n)["rec"]
     assert np.array_equal(rec, orc.kv_append_i8rec(case["K"], case["V"], 0, rope=rope_np.view(np.float16)))
@@ -143,7 +143,7 @@ def run_prefill_i8(la, orc, synth, cuda, seed, context, tokens, q_heads, kv_head
     got = out.float().cpu().numpy()
     if splits <= 0:
         splits = la.lib().lfm3a_prefill_i8_splits(tokens, q_heads, context, window, 0)
-    want = orc.prefill_i8rec(qb, tokens, q_heads, rec, context, window=window, splits=splits)
+    want = orc.prefill_i8rec(qb, tokens, q_heads, rec, context, window=window, splits=splits, exact=exact)
     return got, want, splits
 
 
@@ -166,3 +166,20 @@ def test_prefill_i8_reference_geometry(la, orc, synth, cuda, context, tokens, wi
 def test_prefill_i8_benchmark_geometry(la, orc, synth, cuda):
     got, want, _ = run_prefill_i8(la, orc, synth, cuda, 1100, 150, 40, 32, 8, 64)
     assert rel_err(got, want) < TOL_PREFILL
+
+
+@pytest.mark.parametrize("context,tokens,window,splits", [(0, 70, 0, 1), (300, 33, 100, 1), (3000, 96, 0, 3),
+                                                          (5000, 64, 0, 0), (129, 1, 0, 1)])
+def test_prefill_i8_exact_reference_geometry(la, orc, synth, cuda, context, tokens, window, splits):
+    """The exact variant over the records (prefill_attn_exact.hip:173-344: exact running max, fp16 P' = p v_scale
+    4096 x V) against the oracle's restatement with the same blocks and splits, within the two-rounding bar of the
+    fp16 probabilities (4e-3 of the RMS beyond half an fp16 ulp); the oracle itself is held to exact fp64 attention
+    over the same int8 values in test_oracle_math.py."""
+    got, want, _ = run_prefill_i8(la, orc, synth, cuda, 1200 + tokens + context, context, tokens, 16, 4, 128,
+                                  window, splits, exact=True)
+    assert rel_err(got, want) < TOL_PAIR
+
+
+def test_prefill_i8_exact_benchmark_geometry(la, orc, synth, cuda):
+    got, want, _ = run_prefill_i8(la, orc, synth, cuda, 1300, 150, 40, 32, 8, 64, exact=True)
+    assert rel_err(got, want) < TOL_PAIR

@@ -129,3 +129,19 @@ def test_prefill_i8rec_matches_fp64(orc, synth, d, context, tokens, window):
     assert float(np.mean(np.abs(got - want))) / rms < 5e-3
     split = orc.prefill_i8rec(qbuf, tokens, qh, rec, context, window=window, splits=3)
     assert rel_err(split, got) < 1e-2
+
+
+@pytest.mark.parametrize("d,context,tokens,window", [(128, 200, 40, 0), (128, 300, 33, 100), (64, 150, 40, 0)])
+def test_prefill_i8rec_exact_matches_fp64(orc, synth, d, context, tokens, window):
+    """The restated exact prefill over the records (prefill_attn_exact.hip:173-344: exact running max, fp16
+    P' = p * v_scale * 4096) against exact attention over the same int8 values: within 4e-3 of the RMS (the fp16
+    probabilities), and the same within 3e-3 whatever the key splits (each split rounds its P' to fp16 against
+    its own running maximum)."""
+    qh, kvh = (16, 4) if d == 128 else (32, 8)
+    case, rec = records_case(orc, synth, 600 + tokens + context, context + tokens, qh, kvh, d)
+    qbuf = orc.quantize_q(case["Q"][context:])
+    got = orc.prefill_i8rec(qbuf, tokens, qh, rec, context, window=window, exact=True)
+    want = f64_prefill_over_records(orc, qbuf, rec, tokens, qh, context, window)
+    assert rel_err(got, want) < 4e-3
+    split = orc.prefill_i8rec(qbuf, tokens, qh, rec, context, window=window, splits=3, exact=True)
+    assert rel_err(split, got) < 3e-3
