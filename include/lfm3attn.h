@@ -303,13 +303,13 @@ int lfm3a_prefill_attention(const lfm3a_kv_view* kv, const void* q, int tokens, 
 
 /* lfm3a_prefill_attention with the glue around it fused (the reference launches q_norm_rope,
  * kernels/ops.hip:202-210, before it and gate_mul, ops.hip:254-264, after it; Go calls
- * internal/model/prefill.go:449-511). q: raw query projections, row (t, qh) at q + t * q_stride + qh * 64
- * (q_stride in halves, a multiple of 8). q_norm: fp16 [64] RMS weights (eps 1e-5) or NULL; rope: a table
- * of lfm3a_rope_table, row context + t, or NULL; the row is normalised, then rotated, each step rounded to
- * fp16 as q_norm_rope does. gate: fp16 logits at gate + t * gate_stride + qh, or NULL: the output row is
- * fp16(fp16(attention) * fp16(sigmoid(logit))), as gate_mul rounds. out stays [tokens][q_heads][64].
- * The fused glue is head_dim 64 only (LFM3A_ENOTSUP at 128); with all three NULL any q_stride works at either
- * head_dim. */
+ * internal/model/prefill.go:449-511). q: raw query projections, row (t, qh) at q + t * q_stride + qh * head_dim
+ * (q_stride in halves, a multiple of 8). q_norm: fp16 [head_dim] RMS weights (eps 1e-5) or NULL; rope: a table
+ * of lfm3a_rope_table, row context + t, or NULL; the row is normalised, then rotated (pairs d, d + head_dim / 2),
+ * each step rounded to fp16 as q_norm_rope does; at head_dim 128 the sum of squares follows the reference's
+ * wave_sum order (ops.hip:24-30). gate: fp16 logits at gate + t * gate_stride + qh, or NULL: the output row is
+ * fp16(fp16(attention) * fp16(sigmoid(logit))), as gate_mul rounds. out stays [tokens][q_heads][head_dim].
+ * head_dim 64 or 128. */
 int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_t q_stride, const void* q_norm,
                                   const void* rope, const void* gate, int64_t gate_stride, int tokens, int q_heads,
                                   int context, int window, int exact, void* out, void* workspace,

@@ -47,7 +47,11 @@ struct AppendArgs {
 };
 
 // Lane l of a warp holds the RoPE pairs (l + 32 j, l + 32 j + D/2), j < D/64 (kernels/ops.hip:186-200
-// with 64-lane waves). Every rounding step is explicit so the result is bit-identical to the oracle.
+// with 64-lane waves). Every rounding step is explicit so the result is bit-identical to the oracle. The k-norm's sum
+// of squares at head_dim 128 is the reference's wave_sum (ops.hip:24-30): its lane L holds the pair (L, L + 64) and
+// its 64 lanes add as a pairwise tree in natural order; here lane l holds its lanes l and l + 32, so an ascending
+// butterfly (l ^ 1, l ^ 2, .. l ^ 16) adds each half's 32 the same way, then the halves are added. At head_dim 64
+// (no reference code) lane l holds (l, l + 32), added by a descending butterfly.
 template <int D>
 __device__ __forceinline__ void norm_rope_pairs(const AppendArgs& a, const __half* ks, int pos, int lane, float (&ra)[D / 64],
                                                 float (&rb)[D / 64]) {
@@ -59,14 +63,21 @@ __device__ __forceinline__ void norm_rope_pairs(const AppendArgs& a, const __hal
     x1[j] = __half2float(ks[lane + 32 * j + HALF]);
   }
   if (a.knorm) {
-    float acc = 0.f;
+    float acc;
+    if constexpr (J == 2) {
+      float h0 = __fadd_rn(__fmul_rn(x0[0], x0[0]), __fmul_rn(x1[0], x1[0]));
+      float h1 = __fadd_rn(__fmul_rn(x0[1], x0[1]), __fmul_rn(x1[1], x1[1]));
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const float term = __fadd_rn(__fmul_rn(x0[j], x0[j]), __fmul_rn(x1[j], x1[j]));
-      acc = j == 0 ? term : __fadd_rn(acc, term);
+      for (int o = 1; o <= 16; o <<= 1) {
+        h0 = __fadd_rn(h0, __shfl_xor_sync(0xffffffffu, h0, o));
+        h1 = __fadd_rn(h1, __shfl_xor_sync(0xffffffffu, h1, o));
+      }
+      acc = __fadd_rn(h0, h1);
+    } else {
+      acc = __fadd_rn(__fmul_rn(x0[0], x0[0]), __fmul_rn(x1[0], x1[0]));
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
     }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
     const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)D), 1e-5f)));
 #pragma unroll
     for (int j = 0; j < J; ++j) {

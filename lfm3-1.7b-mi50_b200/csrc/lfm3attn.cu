@@ -647,8 +647,6 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
   const int D = L.head_dim;
   if (L.mode != LFM3A_MODE_F16 || (D != 64 && D != 128))
     return fail(LFM3A_ENOTSUP, "prefill attention needs MODE_F16, head_dim 64 or 128");
-  if (D == 128 && (q_norm || rope || gate))
-    return fail(LFM3A_ENOTSUP, "the fused q-norm / RoPE / gate needs head_dim 64");
   if (q_heads != 4 * L.kv_heads) return fail(LFM3A_ENOTSUP, "prefill attention needs 4 query heads per kv head");
   if (!q || !out || tokens < 0 || context < 0 || window < 0) return fail(LFM3A_EINVAL, "bad prefill arguments");
   if (q_stride < (int64_t)q_heads * D || q_stride % 8 != 0)
@@ -669,9 +667,9 @@ int lfm3a_prefill_attention_fused(const lfm3a_kv_view* kv, const void* q, int64_
   rc = launch_combine(part, tokens * q_heads, splits, D, D + 2, (int64_t)splits * (D + 2), nullptr,
                       static_cast<__half*>(out), nullptr, st);
   if (rc != LFM3A_OK || !gate) return rc;
-  const int64_t groups = (int64_t)tokens * q_heads * 8;
+  const int64_t groups = (int64_t)tokens * q_heads * (D / 8);
   launch_pdl(prefill_gate_kernel, (unsigned)((groups + 255) / 256), 256, 0, st, static_cast<__half*>(out),
-             static_cast<const __half*>(gate), gate_stride, tokens * q_heads, q_heads);
+             static_cast<const __half*>(gate), gate_stride, tokens * q_heads, q_heads, D / 8);
   return check_launch("prefill_gate_kernel");
 }
 

@@ -105,35 +105,56 @@ __device__ __forceinline__ void load_q_row(const PrefillArgs& a, uint8_t* sQ, in
     for (int c = 0; c < D / 8; ++c) dst[c * 8] = row_ok ? src[c] : zero;
     return;
   }
-  static_assert(!GLUE || D == 64, "the fused q-norm / RoPE serves head_dim 64");
+  constexpr int NC = D / 16;   // 8-dim chunks of a half: chunk c pairs dims 8c .. 8c + 7 with D/2 + 8c .. D/2 + 8c + 7
   float inv = 1.f;
   if (a.q_norm) {
-    float v[32];
+    float ss;
+    if constexpr (D == 128) {
+      // The reference's wave_sum over the 64 pairs (d, d + 64) (ops.hip:24-30,186-200): a pairwise tree in natural
+      // order, chunk c holding the 8 leaves 8c .. 8c + 7.
+      float e[NC];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float lo[8], hi[8];
-      unpack8(row_ok ? src[c] : zero, lo);
-      unpack8(row_ok ? src[c + 4] : zero, hi);
+      for (int c = 0; c < NC; ++c) {
+        float lo[8], hi[8], x[8];
+        unpack8(row_ok ? src[c] : zero, lo);
+        unpack8(row_ok ? src[c + NC] : zero, hi);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[8 * c + i] = __fadd_rn(__fmul_rn(lo[i], lo[i]), __fmul_rn(hi[i], hi[i]));
+        for (int i = 0; i < 8; ++i) x[i] = __fadd_rn(__fmul_rn(lo[i], lo[i]), __fmul_rn(hi[i], hi[i]));
+        e[c] = __fadd_rn(__fadd_rn(__fadd_rn(x[0], x[1]), __fadd_rn(x[2], x[3])),
+                         __fadd_rn(__fadd_rn(x[4], x[5]), __fadd_rn(x[6], x[7])));
+      }
+      ss = __fadd_rn(__fadd_rn(__fadd_rn(e[0], e[1]), __fadd_rn(e[2], e[3])),
+                     __fadd_rn(__fadd_rn(e[4], e[5]), __fadd_rn(e[6], e[7])));
+    } else {
+      // head_dim 64 (no reference code): pairs (d, d + 32) as 32 lanes added by a descending butterfly
+      float v[32];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        float lo[8], hi[8];
+        unpack8(row_ok ? src[c] : zero, lo);
+        unpack8(row_ok ? src[c + NC] : zero, hi);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[8 * c + i] = __fadd_rn(__fmul_rn(lo[i], lo[i]), __fmul_rn(hi[i], hi[i]));
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+        for (int l = 0; l < o; ++l) v[l] = __fadd_rn(v[l], v[l + o]);
+      ss = v[0];
     }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1)
-#pragma unroll
-      for (int l = 0; l < o; ++l) v[l] = __fadd_rn(v[l], v[l + o]);
-    inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v[0], 64.f), 1e-5f)));
+    inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
   }
   const uint4* w4 = reinterpret_cast<const uint4*>(a.q_norm);
-  const uint4* cs4 = a.rope ? reinterpret_cast<const uint4*>(a.rope + (int64_t)(a.context + tok) * 64) : nullptr;
+  const uint4* cs4 = a.rope ? reinterpret_cast<const uint4*>(a.rope + (int64_t)(a.context + tok) * D) : nullptr;
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < NC; ++c) {
     float lo[8], hi[8];
     unpack8(row_ok ? src[c] : zero, lo);
-    unpack8(row_ok ? src[c + 4] : zero, hi);
+    unpack8(row_ok ? src[c + NC] : zero, hi);
     if (a.q_norm) {
       float wl[8], wh[8];
       unpack8(w4[c], wl);
-      unpack8(w4[c + 4], wh);
+      unpack8(w4[c + NC], wh);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         lo[i] = r16f(__fmul_rn(__fmul_rn(lo[i], inv), wl[i]));
@@ -143,7 +164,7 @@ __device__ __forceinline__ void load_q_row(const PrefillArgs& a, uint8_t* sQ, in
     if (cs4) {
       float cv[8], sv[8];
       unpack8(cs4[c], cv);
-      unpack8(cs4[c + 4], sv);
+      unpack8(cs4[c + NC], sv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float a1 = lo[i], b1 = hi[i];
@@ -152,7 +173,7 @@ __device__ __forceinline__ void load_q_row(const PrefillArgs& a, uint8_t* sQ, in
       }
     }
     dst[c * 8] = row_ok ? pack8(lo) : zero;
-    dst[(c + 4) * 8] = row_ok ? pack8(hi) : zero;
+    dst[(c + NC) * 8] = row_ok ? pack8(hi) : zero;
   }
 }
 
@@ -175,14 +196,15 @@ __device__ __forceinline__ uint4 out_pack8(const uint32_t* rr, float inv, __half
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// In-place output gate for split chunks (the combine leaves fp16(acc / l) in out): 8 halves per thread.
+// In-place output gate for split chunks (the combine leaves fp16(acc / l) in out): 8 halves per thread, a row's
+// head_dim / 8 groups.
 __global__ __launch_bounds__(256) void prefill_gate_kernel(__half* out, const __half* gate, int64_t gate_stride,
-                                                           int rows, int q_heads) {
+                                                           int rows, int q_heads, int groups_per_row) {
   pdl_wait();
   pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // 8-half group
-  if (i >= (int64_t)rows * 8) return;
-  const int row = (int)(i >> 3), tok = row / q_heads, qh = row - tok * q_heads;
+  if (i >= (int64_t)rows * groups_per_row) return;
+  const int row = (int)(i / groups_per_row), tok = row / q_heads, qh = row - tok * q_heads;
   const float g = __half2float(gate[(int64_t)tok * gate_stride + qh]);
   const __half2 g2 = __float2half2_rn(__fdiv_rn(1.f, __fadd_rn(1.f, expf(-g))));
   uint4 v = reinterpret_cast<uint4*>(out)[i];
@@ -895,7 +917,7 @@ __global__ __launch_bounds__(PfLayout<D, I8>::kThreads, PfLayout<D, I8>::kBlocks
 }
 
 inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, int head_dim, cudaStream_t st) {
-  static std::atomic<bool> done[12][64];   // per device: set once the attributes are (see ensure_smem)
+  static std::atomic<bool> done[16][64];   // per device: set once the attributes are (see ensure_smem)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LFM3A_ECUDA;
   const dim3 grid(a.qtiles, a.g.kv_heads, a.splits);
@@ -911,14 +933,20 @@ inline int launch_prefill_kernel(const PrefillArgs& a, bool i8, int head_dim, cu
     return true;
   };
   bool ok;
-  if (head_dim == 128) {   // the reference model's geometry: no fused glue
-    if (glue) return LFM3A_ENOTSUP;
+  if (head_dim == 128) {   // the reference model's geometry
     using LI = PfLayout<128, true>;
     using LE = PfLayout<128, false>;
-    if (i8) ok = split ? run(prefill_kernel<128, true, true, false>, LI::kRequest, LI::kThreads, 11)
-                       : run(prefill_kernel<128, true, false, false>, LI::kRequest, LI::kThreads, 10);
-    else ok = split ? run(prefill_kernel<128, false, true, false>, LE::kRequest, LE::kThreads, 9)
-                    : run(prefill_kernel<128, false, false, false>, LE::kRequest, LE::kThreads, 8);
+    if (i8) {
+      if (split) ok = glue ? run(prefill_kernel<128, true, true, true>, LI::kRequest, LI::kThreads, 15)
+                           : run(prefill_kernel<128, true, true, false>, LI::kRequest, LI::kThreads, 11);
+      else ok = glue ? run(prefill_kernel<128, true, false, true>, LI::kRequest, LI::kThreads, 14)
+                     : run(prefill_kernel<128, true, false, false>, LI::kRequest, LI::kThreads, 10);
+    } else {
+      if (split) ok = glue ? run(prefill_kernel<128, false, true, true>, LE::kRequest, LE::kThreads, 13)
+                           : run(prefill_kernel<128, false, true, false>, LE::kRequest, LE::kThreads, 9);
+      else ok = glue ? run(prefill_kernel<128, false, false, true>, LE::kRequest, LE::kThreads, 12)
+                     : run(prefill_kernel<128, false, false, false>, LE::kRequest, LE::kThreads, 8);
+    }
   } else {
     using LI = PfLayout<64, true>;
     using LE = PfLayout<64, false>;

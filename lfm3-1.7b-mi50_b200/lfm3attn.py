@@ -419,7 +419,7 @@ class LayerCache:
     def prefill(self, q, context: int, window: int = 0, exact: bool = False, out=None, workspace=None, stream=None,
                 q_norm=None, rope=None, gate=None, q_heads: int | None = None):
         """Causal prefill attention of q at positions context... q: [T][q_heads][head_dim] fp16, or with
-        q_heads given any [T][>= q_heads * head_dim] row-strided view of raw projections. q_norm (fp16 [64]),
+        q_heads given any [T][>= q_heads * head_dim] row-strided view of raw projections. q_norm (fp16 [head_dim]),
         rope (a rope_table on the device) and gate (fp16 logits [T][>= q_heads], row-strided) fuse the
         reference's q_norm_rope and gate_mul around the attention."""
         import torch

@@ -33,23 +33,32 @@ float lane_tree_sum(float* v) {
   return v[0];
 }
 
+// The sum of squares of a head for its RMS norm. Head_dim 128, the reference's own (ops.hip:186-200 norm_rotate with
+// wave_sum, :24-30): lane L of its 64-lane wave holds the RoPE pair (L, L + 64), x_L = a^2 + b^2 (two products, one
+// sum), and wave_sum's quad swaps, row-half and row mirrors and the final (0 + 16) + (32 + 48) add the 64 lanes as a
+// pairwise tree in natural order: ((x0 + x1) + (x2 + x3)) + ... Head_dim 64 (no reference code; this library's
+// convention): lane l of 32 holds (l, l + 32), summed by a butterfly v[l] + v[l ^ o], o = 16 .. 1.
+float head_sum_squares(const float* x, int D) {
+  const int half = D / 2;
+  if (D == 128) {
+    float v[64];
+    for (int l = 0; l < 64; ++l) v[l] = x[l] * x[l] + x[l + half] * x[l + half];
+    for (int n = 32; n >= 1; n >>= 1)
+      for (int k = 0; k < n; ++k) v[k] = v[2 * k] + v[2 * k + 1];
+    return v[0];
+  }
+  float lanes[32];
+  for (int l = 0; l < 32; ++l) lanes[l] = x[l] * x[l] + x[l + half] * x[l + half];
+  return lane_tree_sum(lanes);
+}
+
 // RMS k-norm + RoPE of one head, ops.hip:193-200. x: [D] fp32 values of fp16 inputs, out: [D] fp32
-// values of the stored fp16 results. Lane l of the kernel holds pairs (l + 32 j, l + 32 j + D/2).
+// values of the stored fp16 results.
 void norm_rope_head(const float* x, int D, const uint16_t* rope_row, const uint16_t* knorm, float* out) {
-  const int half = D / 2, J = D / 64;
+  const int half = D / 2;
   float a1[128], b1[128];
   if (knorm) {
-    float lanes[32];
-    for (int l = 0; l < 32; ++l) {
-      float acc = 0.f;
-      for (int j = 0; j < J; ++j) {
-        const float a = x[l + 32 * j], b = x[l + 32 * j + half];
-        const float term = a * a + b * b;   // two products, one sum (no contraction)
-        acc = j == 0 ? term : acc + term;
-      }
-      lanes[l] = acc;
-    }
-    const float ss = lane_tree_sum(lanes);
+    const float ss = head_sum_squares(x, D);
     const float inv = 1.f / sqrtf(ss / (float)D + 1e-5f);
     for (int i = 0; i < half; ++i) {
       a1[i] = r16(x[i] * inv * orc_f16_to_f32(knorm[i]));

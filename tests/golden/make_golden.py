@@ -58,12 +58,19 @@ def norm_rope(k, pos0, rope, knorm):
     a = np.stack([x[..., 32 * j:32 * j + 32] for j in range(J)], axis=-2)                 # [n][h][J][32]
     b = np.stack([x[..., half + 32 * j:half + 32 * j + 32] for j in range(J)], axis=-2)
     if knorm is not None:
-        lanes = a[..., 0, :] * a[..., 0, :] + b[..., 0, :] * b[..., 0, :]
-        for j in range(1, J):
-            lanes = lanes + (a[..., j, :] * a[..., j, :] + b[..., j, :] * b[..., j, :])
-        for o in (16, 8, 4, 2, 1):
-            lanes = lanes + lanes[..., np.arange(32) ^ o]
-        ss = lanes[..., 0]
+        if d == 128:
+            # ops.hip:186-200, 24-30: lane L of a 64-lane wave holds (L, L + 64); wave_sum adds the 64 lanes' a^2 + b^2
+            # as a pairwise tree in natural order.
+            v = x[..., :half] * x[..., :half] + x[..., half:] * x[..., half:]                 # [n][h][64]
+            while v.shape[-1] > 1:
+                v = v[..., 0::2] + v[..., 1::2]
+            ss = v[..., 0]
+        else:
+            # head_dim 64 (no reference code): lane l of 32 holds (l, l + 32), butterfly o = 16 .. 1.
+            lanes = a[..., 0, :] * a[..., 0, :] + b[..., 0, :] * b[..., 0, :]
+            for o in (16, 8, 4, 2, 1):
+                lanes = lanes + lanes[..., np.arange(32) ^ o]
+            ss = lanes[..., 0]
         inv = f32(1.0) / np.sqrt(ss / f32(d) + f32(1e-5))
         w = knorm.astype(f32)
         wa = np.stack([w[32 * j:32 * j + 32] for j in range(J)])
@@ -259,6 +266,24 @@ def main():
     table128 = rope_rows(1e6, 0.5, 128, np.arange(48))
     g["rec_k"], g["rec_v"], g["knorm128"] = k128, v128, knorm128
     g["rec"] = i8_records(norm_rope(k128, 40, table128, knorm128), v128)
+
+    # The k-norm's sum of squares at head_dim 128 in the reference's order (a pairwise tree over its 64 lanes): rows
+    # picked so that 16 of them round to other fp16 outputs under the butterfly order of a 32-lane warp (lane l
+    # holding dims l, l + 32, l + 64, l + 96, o = 16 .. 1), and 16 that do not.
+    s = synth.Stream(104)
+    cand = s.normal_f16((16384, 1, 128))
+    want = norm_rope(cand, 0, None, knorm128)
+    x = cand[:, 0].astype(f32)
+    lanes = (x[:, 0:32] * x[:, 0:32] + x[:, 64:96] * x[:, 64:96]) + (x[:, 32:64] * x[:, 32:64] + x[:, 96:] * x[:, 96:])
+    for o in (16, 8, 4, 2, 1):
+        lanes = lanes + lanes[:, np.arange(32) ^ o]
+    inv = f32(1.0) / np.sqrt(lanes[:, 0] / f32(128) + f32(1e-5))
+    other = f16((x * inv[:, None]) * knorm128.astype(f32))
+    differs = np.any(other != want[:, 0], axis=1)
+    assert differs.sum() >= 16
+    pick = np.concatenate([np.nonzero(differs)[0][:16], np.nonzero(~differs)[0][:16]])
+    g["knorm_order_in"] = cand[pick]
+    g["knorm_order_out"] = want[pick]
 
     # int8 V per 64-token block: 100 tokens (one full block, one partial), a zero head to hit the floor.
     s = synth.Stream(102)

@@ -102,6 +102,21 @@ def test_i8_records_reference_geometry(la, orc, synth, cuda):
     assert np.array_equal(got, want)
 
 
+def test_append_head_dim_128_norm_order(la, cuda):
+    """The append's k-norm at head_dim 128 sums its squares in the reference's order (wave_sum, a pairwise tree over
+    the 64 pairs d, d + 64): the golden rows, half of which round differently under a 32-lane butterfly, come out
+    bit for bit."""
+    import pathlib
+
+    g = np.load(pathlib.Path(__file__).resolve().parent / "golden" / "golden.npz")
+    k = g["knorm_order_in"]
+    cache = la.LayerCache(la.MODE_F16, 1, 128, k.shape[0] + 64, device=cuda)
+    cache.append(dev(k, cuda), dev(k, cuda), 0, k_norm=dev(g["knorm128"], cuda))
+    la.sync()
+    got = cache.logical(k.shape[0])["K"]
+    assert np.array_equal(got, g["knorm_order_out"].view(np.uint16))
+
+
 def test_quantize_p_bitexact(la, orc, synth, cuda):
     s = synth.Stream(14)
     p = np.abs(s.normal(4096 * 64)).astype(np.float32).reshape(4096, 64)

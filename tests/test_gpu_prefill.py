@@ -142,6 +142,37 @@ def test_prefill_fused_glue(la, orc, synth, cuda, context, T, exact):
     assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3
 
 
+@pytest.mark.parametrize("exact", [True, False])
+@pytest.mark.parametrize("context,T", [(37, 100), (20000, 64)])
+def test_prefill_fused_glue_head_dim_128(la, orc, synth, cuda, context, T, exact):
+    """The fused glue at the reference model's geometry (16/4/128, RoPE over half the dims): q_norm_rope with the
+    reference's own sum-of-squares order (its wave_sum over the pairs d, d + 64) inside the kernel's Q load gives
+    bit for bit the plain call on the oracle's q_norm_rope output; the gate as at head_dim 64. (20000, 64) runs
+    split along the keys, the gate applied after the combine."""
+    case = synth.prefill_case(190 + T, context + T, q_heads=16, kv_heads=4, head_dim=128)
+    cache = la.LayerCache(la.MODE_F16, 4, 128, context + T + 64, device=cuda)
+    cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
+    s = synth.Stream(195)
+    width = 16 * 128 + 2 * 128 + 48   # a projection row: the 16 query heads, then other columns
+    f = s.normal_f16((T, width))
+    qnorm = (1.0 + 0.25 * s.normal_f16((128,)).astype(np.float32)).astype(np.float16)
+    table = orc.rope_table(1e6, 0.5, 128, context + T + 1)
+    gate = s.normal_f16((T, 24))
+    fd, qn_d, rope_d = dev(f, cuda), dev(qnorm, cuda), dev(table.view(np.float16), cuda)
+    fused = cache.prefill(fd[:, :16 * 128], context, exact=exact, q_norm=qn_d, rope=rope_d, q_heads=16)
+    gated = cache.prefill(fd[:, :16 * 128], context, exact=exact, q_norm=qn_d, rope=rope_d, gate=dev(gate, cuda),
+                          q_heads=16)
+    q_ref = orc.q_norm_rope(f, 16, 128, context, qnorm=qnorm, rope=table)
+    plain = cache.prefill(dev(q_ref, cuda), context, exact=exact)
+    la.sync()
+    plain_np = plain.cpu().numpy()
+    assert np.array_equal(fused.cpu().numpy().view(np.uint16), plain_np.view(np.uint16))
+    want = orc.gate_mul(plain_np, gate)
+    got = gated.cpu().numpy()
+    ulps = np.abs(got.view(np.int16).astype(np.int32) - want.view(np.int16).astype(np.int32))
+    assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3
+
+
 # ---------------------------------------------------------------- the reference model's geometry
 # 16 query heads, 4 kv heads, head_dim 128 (internal/model/engine.go:22-40). The exact kernel runs two CTAs per
 # SM there, as at head_dim 64; the int8-PV kernel one, so its key splits follow lfm3a_prefill_splits with half the
@@ -210,11 +241,17 @@ def test_prefill_head_dim_128_sampled_rows(la, orc, synth, cuda):
     assert rel_err(i8.float().cpu().numpy(), emu, rows) < TOL_I8
 
 
-def test_prefill_head_dim_128_refuses_glue(la, synth, cuda):
+def test_prefill_head_dim_128_gate_only(la, orc, synth, cuda):
+    """The gate alone at head_dim 128 (a plain Q): gate_mul of the plain call's output, within one fp16 ulp where
+    the device's and the host's expf round the sigmoid differently."""
     case = synth.prefill_case(121, 64, q_heads=16, kv_heads=4, head_dim=128)
     cache = la.LayerCache(la.MODE_F16, 4, 128, 128, device=cuda)
     cache.append(dev(case["K"], cuda), dev(case["V"], cuda), 0)
-    gate = dev(synth.Stream(122).normal_f16((64, 16)), cuda)
-    with pytest.raises(la.LFM3AError) as e:
-        cache.prefill(dev(case["Q"], cuda), 0, exact=True, gate=gate)
-    assert e.value.code == la.ENOTSUP
+    gate = synth.Stream(122).normal_f16((64, 16))
+    gated = cache.prefill(dev(case["Q"], cuda), 0, exact=True, gate=dev(gate, cuda))
+    plain = cache.prefill(dev(case["Q"], cuda), 0, exact=True)
+    la.sync()
+    want = orc.gate_mul(plain.cpu().numpy(), gate)
+    got = gated.cpu().numpy()
+    ulps = np.abs(got.view(np.int16).astype(np.int32) - want.view(np.int16).astype(np.int32))
+    assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3

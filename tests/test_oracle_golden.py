@@ -55,6 +55,13 @@ def test_append_i8_records(orc, g):
     assert np.array_equal(rec, g["rec"])
 
 
+def test_append_head_dim_128_norm_order(orc, g):
+    """The k-norm's sum of squares at head_dim 128 follows the reference's wave_sum (a pairwise tree over its 64
+    lanes, ops.hip:24-30,186-200): the fixture's first 16 rows round differently under a 32-lane butterfly."""
+    k, _ = orc.kv_append_f16(g["knorm_order_in"], g["knorm_order_in"], 0, knorm=g["knorm128"])
+    assert np.array_equal(bits(k), bits(g["knorm_order_out"]))
+
+
 def test_v8_blocks(orc, g):
     v8, sc = orc.quantize_v8(g["v8_in"], 100)
     assert np.array_equal(v8, g["v8"])
