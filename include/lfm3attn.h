@@ -205,7 +205,9 @@ int lfm3a_verify_round(const lfm3a_kv_view* kv, const void* k, const void* v, in
  * end-to-end leg of the benchmark): copies host_in, the drafts' q then k then v (fp16 [m][q_heads][head_dim],
  * [m][kv_heads][head_dim], [m][kv_heads][head_dim], contiguous), into dev_in (device, 16-byte aligned, as many
  * bytes), runs lfm3a_verify_round on them (out: device fp16 [m][q_heads][head_dim]), then copies out into
- * host_out, all on stream. host_in and host_out should be pinned. timeout_ms > 0: returns once the stream is
+ * host_out, all on stream. host_in and host_out should be pinned; when host_out is pinned memory mapped into the
+ * device's address space (cudaHostAlloc, or cudaHostRegister, on a unified address space) the round writes its
+ * output there directly and out is not written. timeout_ms > 0: returns once the stream is
  * done, LFM3A_ETIMEOUT after timeout_ms; 0: waits for the stream without a limit (cudaStreamSynchronize); < 0:
  * returns at once (the caller waits, e.g. after queueing the rollback). A kernel that gave up a bounded wait is
  * reported by the next lfm3a_sync. No reference counterpart: the reference's drafts are produced on the GPU. */

@@ -588,12 +588,23 @@ int lfm3a_verify_round_host(const lfm3a_kv_view* kv, const void* host_in, void* 
   const cudaStream_t st = as_stream(stream);
   cudaError_t e = cudaMemcpyAsync(dev_in, host_in, qb + 2 * kb, cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (drafts to the device)");
+  // Pinned host memory mapped into the device's address space (cudaHostAlloc / cudaHostRegister on a unified
+  // address space) takes the output straight from the kernel that writes it: no device-to-host copy.
+  void* out_dev = out;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, host_out) == cudaSuccess && attr.type == cudaMemoryTypeHost &&
+      attr.devicePointer != nullptr && aligned16(attr.devicePointer))
+    out_dev = attr.devicePointer;
+  else
+    cudaGetLastError();
   const char* d = static_cast<const char*>(dev_in);
-  rc = lfm3a_verify_round(kv, d + qb, d + qb + kb, 0, rope, k_norm, d, m, q_heads, ctx_len, window, gate, out,
+  rc = lfm3a_verify_round(kv, d + qb, d + qb + kb, 0, rope, k_norm, d, m, q_heads, ctx_len, window, gate, out_dev,
                           workspace, workspace_bytes, splits, stream);
   if (rc != LFM3A_OK) return rc;
-  e = cudaMemcpyAsync(host_out, out, qb, cudaMemcpyDeviceToHost, st);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (output to the host)");
+  if (out_dev == out) {
+    e = cudaMemcpyAsync(host_out, out, qb, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (output to the host)");
+  }
   if (timeout_ms < 0) return LFM3A_OK;
   if (timeout_ms == 0) {
     e = cudaStreamSynchronize(st);
