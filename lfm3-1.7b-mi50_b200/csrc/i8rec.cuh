@@ -361,7 +361,8 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
 //       even, saturated), bias += sum(q) 128 sc with sc = max P' / 255 (:298-317);
 //   PV  the exact sum_k q_k v_k from mma.m16n8k16 on fp16 (u8 and int8 are exact there, the fp32 sums of
 //       products stay below 2^24), plus 128 sum(q): the reference's u8 x (v + 128) dot, then
-//       acc = fma(that, sc, acc) (:320-350);
+//       acc = fma(that, sc, acc) (:320-350). The tile's V is made fp16 once, by the whole CTA, into a key-major
+//       shared tile, and the MMAs' B fragments come from it by ldmatrix.trans;
 //   the split's partial: acc - bias, m (-inf without tiles), l, merged by the combine kernel (:489-505).
 // EXACT: the --exact-attention kernel over the same bytes (prefill_attn_exact.hip:173-344): s = sum_g float(dot_g) qs_g
 // from 0, times k_scale (1 / sqrt(D)) log2 e; an exact running max per tile (corr = 2^(m - mn), l = l corr + sum p);
@@ -375,6 +376,25 @@ struct PrefillI8Args {
   float kscale;           // (1 / sqrt(D)) log2(e)
 };
 
+// Four 8x8 fp16 matrices, transposed on the way out: lane L gives the address of row L % 8 of matrix L / 8; each
+// thread receives, per matrix, the elements (rows 2 (t % 4), 2 (t % 4) + 1; column t / 4): the B fragment of an
+// m16n8k16 MMA from a key-major (row = key) tile.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// A prefill tile's V as fp16, key-major, rows padded by 16 bytes so the eight rows an ldmatrix reads fall in
+// distinct banks.
+template <int D>
+struct PfI8Smem {
+  static constexpr int kRec = 2 * D + 8, kTile = 64 * kRec;   // a tile of 64 records
+  static constexpr int kVRow = D + 8;                         // halves per fp16 V row
+  static constexpr int kOffV = 2 * kTile;                     // after the two record buffers
+  static constexpr int kBytes = kOffV + 64 * kVRow * 2;
+};
+
 __device__ __forceinline__ void cp_async8(void* smem_dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
 }
@@ -386,10 +406,13 @@ __device__ __forceinline__ void cp_async_wait() {
 
 template <int D, bool EXACT>
 __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) {
+  using SM = PfI8Smem<D>;
   constexpr int REC = 2 * D + 8, NG = D / 32, NJ = D / 8, KT = 64, QT = 32, CH = REC / 8;
   constexpr float LAZY = 8.f, MAGIC_F = 12582912.f;
   constexpr int MAGIC_I = 0x4B400000;
-  __shared__ __align__(16) uint8_t tiles[2][KT * REC];
+  extern __shared__ __align__(16) uint8_t pf_smem[];
+  uint8_t (*tiles)[KT * REC] = reinterpret_cast<uint8_t (*)[KT * REC]>(pf_smem);
+  __half* vh = reinterpret_cast<__half*>(pf_smem + SM::kOffV);   // [KT][kVRow]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const int h = blockIdx.y, z = blockIdx.z, nz = a.splits, H = a.g.kv_heads;
   const int t0 = (a.qtiles - 1 - blockIdx.x) * QT, ntok = min(QT, a.T - t0);
@@ -462,6 +485,20 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
     __syncthreads();
     const uint8_t* tl = tiles[s & 1];
     const int k0 = kt_first + s * KT;
+    // The tile's V made fp16 once (the previous tile's PV is done: the barrier that ended it): a word of four
+    // int8 dims per step, 0x64NN - 1152 with NN = v + 128 giving v exactly.
+    for (int idx = threadIdx.x; idx < KT * (D / 4); idx += blockDim.x) {
+      const int key = idx / (D / 4), w = idx - key * (D / 4);
+      const uint32_t x = *reinterpret_cast<const uint32_t*>(tl + key * REC + D + 4 + 4 * w) ^ 0x80808080u;
+      const uint32_t plo = __byte_perm(x, 0x64646464u, 0x4140u), phi = __byte_perm(x, 0x64646464u, 0x4342u);
+      __half2 lo = *reinterpret_cast<const __half2*>(&plo);
+      __half2 hi = *reinterpret_cast<const __half2*>(&phi);
+      lo = __hsub2(lo, __floats2half2_rn(1152.f, 1152.f));
+      hi = __hsub2(hi, __floats2half2_rn(1152.f, 1152.f));
+      *reinterpret_cast<uint2*>(vh + key * SM::kVRow + 4 * w) =
+          make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    }
+    __syncthreads();
     // ---- QK: 8 n-tiles of 8 keys; C fragment (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1)
     float u[8][4];
 #pragma unroll
@@ -622,31 +659,32 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       biasA = 128.f * (float)qsumA;   // the + 128 of every V byte
       biasB = 128.f * (float)qsumB;
     }
-    // ---- PV in passes of 32 dims. Int8-PV: dot = sum_k q_k v_k exactly, then acc = fma(dot + 128 sum q, sc, acc);
-    // exact: the fp16 P' x V straight into acc.
-    constexpr int NP = NJ / 4;   // passes; a pass covers 4 n-tiles (one V word per key)
+    // ---- PV in passes of 32 dims (4 n-tiles of 8): B fragments by ldmatrix.trans from the fp16 V tile. Int8-PV:
+    // dot = sum_k q_k v_k exactly, then acc = fma(dot + 128 sum q, sc, acc); exact: the fp16 P' x V into acc.
+    constexpr int NP = NJ / 4;
+    // lane L addresses row L % 8 of matrix L / 8: keys + 8 (L / 8 & 1), dims + 8 (L / 16)
+    const uint32_t v_base = smem_u32(vh) + (uint32_t)(((lane & 7) + 8 * ((lane >> 3) & 1)) * SM::kVRow * 2 +
+                                                      8 * (lane >> 4) * 2);
 #pragma unroll
-    for (int half = 0; half < NP; ++half) {
+    for (int pass = 0; pass < NP; ++pass) {
       float dot[4][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) dot[j][0] = dot[j][1] = dot[j][2] = dot[j][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const int kb = 16 * kk + 2 * tig;
-        const uint32_t* v0 = reinterpret_cast<const uint32_t*>(tl + (kb + 0) * REC + D + 4 + NJ * gid);
-        const uint32_t* v1 = reinterpret_cast<const uint32_t*>(tl + (kb + 1) * REC + D + 4 + NJ * gid);
-        const uint32_t* v8 = reinterpret_cast<const uint32_t*>(tl + (kb + 8) * REC + D + 4 + NJ * gid);
-        const uint32_t* v9 = reinterpret_cast<const uint32_t*>(tl + (kb + 9) * REC + D + 4 + NJ * gid);
-        const uint32_t w0 = v0[half], w1 = v1[half], w8 = v8[half], w9 = v9[half];
 #pragma unroll
-        for (int by = 0; by < 4; ++by)
-          mma_f16_16816(EXACT ? acc[4 * half + by] : dot[by], pf[kk], s8pair_to_f16x2(w0, w1, by),
-                        s8pair_to_f16x2(w8, w9, by));
+        for (int jp = 0; jp < 2; ++jp) {   // n-tiles 4 pass + 2 jp, + 1
+          uint32_t b00, b01, b10, b11;
+          ldsm_x4_trans(v_base + (uint32_t)((16 * kk) * SM::kVRow * 2 + (32 * pass + 16 * jp) * 2), b00, b01, b10, b11);
+          const int j0 = 2 * jp;
+          mma_f16_16816(EXACT ? acc[4 * pass + j0] : dot[j0], pf[kk], b00, b01);
+          mma_f16_16816(EXACT ? acc[4 * pass + j0 + 1] : dot[j0 + 1], pf[kk], b10, b11);
+        }
       }
       if constexpr (!EXACT) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int jn = 4 * half + j;
+          const int jn = 4 * pass + j;
           acc[jn][0] = fmaf(dot[j][0] + biasA, scA, acc[jn][0]);
           acc[jn][1] = fmaf(dot[j][1] + biasA, scA, acc[jn][1]);
           acc[jn][2] = fmaf(dot[j][2] + biasB, scB, acc[jn][2]);
@@ -667,16 +705,13 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     if (!(half ? okB : okA)) continue;
-    // int8-PV: acc - bias; exact: acc / 4096 (P' carried the 4096)
+    // int8-PV: acc - bias; exact: acc / 4096 (P' carried the 4096). n-tile j holds dims 8 j + 2 tig, + 1.
     const float bias = EXACT ? 0.f : (half ? bB : bA), mul = EXACT ? 1.f / kPScale : 1.f;
     float* dst = a.part + ((half ? rowB : rowA) * nz + z) * (D + 2);
 #pragma unroll
-    for (int jn = 0; jn < NJ; jn += 2) {
-      *reinterpret_cast<float2*>(dst + NJ * (2 * tig) + jn) =
-          make_float2((acc[jn][2 * half] - bias) * mul, (acc[jn + 1][2 * half] - bias) * mul);
-      *reinterpret_cast<float2*>(dst + NJ * (2 * tig + 1) + jn) =
-          make_float2((acc[jn][2 * half + 1] - bias) * mul, (acc[jn + 1][2 * half + 1] - bias) * mul);
-    }
+    for (int jn = 0; jn < NJ; ++jn)
+      *reinterpret_cast<float2*>(dst + 8 * jn + 2 * tig) =
+          make_float2((acc[jn][2 * half] - bias) * mul, (acc[jn][2 * half + 1] - bias) * mul);
     if (tig == 0) {
       dst[D] = ntiles > 0 ? (half ? mB : mA) : -INFINITY;
       dst[D + 1] = half ? lB : lA;

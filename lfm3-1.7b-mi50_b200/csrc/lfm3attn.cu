@@ -918,10 +918,17 @@ int lfm3a_prefill_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, in
   a.kscale = (1.f / sqrtf((float)D)) * kLog2e;
   const cudaStream_t st = as_stream(stream);
   const dim3 grid(a.qtiles, H, splits);
-  if (D == 128 && exact) launch_pdl(prefill_i8rec_kernel<128, true>, grid, 256, 0, st, a);
-  else if (D == 128) launch_pdl(prefill_i8rec_kernel<128, false>, grid, 256, 0, st, a);
-  else if (exact) launch_pdl(prefill_i8rec_kernel<64, true>, grid, 256, 0, st, a);
-  else launch_pdl(prefill_i8rec_kernel<64, false>, grid, 256, 0, st, a);
+  static std::atomic<bool> pf_done[4][64];
+  auto run = [&](auto kernel, int bytes, std::atomic<bool>* done) {
+    const int r = ensure_smem(kernel, bytes, done);
+    if (r == LFM3A_OK) launch_pdl(kernel, grid, 256, (size_t)bytes, st, a);
+    return r;
+  };
+  if (D == 128 && exact) rc = run(prefill_i8rec_kernel<128, true>, PfI8Smem<128>::kBytes, pf_done[0]);
+  else if (D == 128) rc = run(prefill_i8rec_kernel<128, false>, PfI8Smem<128>::kBytes, pf_done[1]);
+  else if (exact) rc = run(prefill_i8rec_kernel<64, true>, PfI8Smem<64>::kBytes, pf_done[2]);
+  else rc = run(prefill_i8rec_kernel<64, false>, PfI8Smem<64>::kBytes, pf_done[3]);
+  if (rc != LFM3A_OK) return rc;
   rc = check_launch("prefill_i8rec_kernel");
   if (rc != LFM3A_OK) return rc;
   return launch_combine(a.part, tokens * q_heads, splits, D, D + 2, (int64_t)splits * (D + 2), nullptr,
