@@ -389,7 +389,10 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
 // distinct banks.
 template <int D>
 struct PfI8Smem {
-  static constexpr int kRec = 2 * D + 8, kTile = 64 * kRec;   // a tile of 64 records
+  // A record's 2 D + 8 bytes sit at a stride of 2 D + 32 in shared memory (72 words at D = 128, 40 at 64, both
+  // 8 mod 32): the four keys a half-warp's 8-byte K loads touch then fill 32 distinct banks (at 66 words the
+  // loads were 4-way conflicted).
+  static constexpr int kRec = 2 * D + 8, kSRec = kRec + 24, kTile = 64 * kSRec;   // a tile of 64 records
   static constexpr int kVRow = D + 8;                         // halves per fp16 V row
   static constexpr int kOffV = 2 * kTile;                     // after the two record buffers
   static constexpr int kBytes = kOffV + 64 * kVRow * 2;
@@ -407,11 +410,11 @@ __device__ __forceinline__ void cp_async_wait() {
 template <int D, bool EXACT>
 __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) {
   using SM = PfI8Smem<D>;
-  constexpr int REC = 2 * D + 8, NG = D / 32, NJ = D / 8, KT = 64, QT = 32, CH = REC / 8;
+  constexpr int REC = 2 * D + 8, SREC = SM::kSRec, NG = D / 32, NJ = D / 8, KT = 64, QT = 32, CH = REC / 8;
   constexpr float LAZY = 8.f, MAGIC_F = 12582912.f;
   constexpr int MAGIC_I = 0x4B400000;
   extern __shared__ __align__(16) uint8_t pf_smem[];
-  uint8_t (*tiles)[KT * REC] = reinterpret_cast<uint8_t (*)[KT * REC]>(pf_smem);
+  uint8_t (*tiles)[KT * SREC] = reinterpret_cast<uint8_t (*)[KT * SREC]>(pf_smem);
   __half* vh = reinterpret_cast<__half*>(pf_smem + SM::kOffV);   // [KT][kVRow]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const int h = blockIdx.y, z = blockIdx.z, nz = a.splits, H = a.g.kv_heads;
@@ -433,7 +436,7 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       const int key = min(k0 + kk, kend - 1);
       const char* src = a.g.pool + phys_block(a.g, key / kBlockTokens) * a.g.block_bytes +
                         ((int64_t)(key % kBlockTokens) * H + h) * REC + off;
-      cp_async8(dst + kk * REC + off, src);
+      cp_async8(dst + kk * SREC + off, src);
     }
     cp_async_commit();
   };
@@ -489,7 +492,7 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
     // int8 dims per step, 0x64NN - 1152 with NN = v + 128 giving v exactly.
     for (int idx = threadIdx.x; idx < KT * (D / 4); idx += blockDim.x) {
       const int key = idx / (D / 4), w = idx - key * (D / 4);
-      const uint32_t x = *reinterpret_cast<const uint32_t*>(tl + key * REC + D + 4 + 4 * w) ^ 0x80808080u;
+      const uint32_t x = *reinterpret_cast<const uint32_t*>(tl + key * SREC + D + 4 + 4 * w) ^ 0x80808080u;
       const uint32_t plo = __byte_perm(x, 0x64646464u, 0x4140u), phi = __byte_perm(x, 0x64646464u, 0x4342u);
       __half2 lo = *reinterpret_cast<const __half2*>(&plo);
       __half2 hi = *reinterpret_cast<const __half2*>(&phi);
@@ -503,7 +506,7 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
     float u[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-      const uint8_t* krec = tl + (8 * n + gid) * REC;
+      const uint8_t* krec = tl + (8 * n + gid) * SREC;
       float sv[4] = {EXACT ? 0.f : qcA, EXACT ? 0.f : qcA, EXACT ? 0.f : qcB, EXACT ? 0.f : qcB};
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
@@ -516,8 +519,8 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
           sv[e] = fmaf(d, e < 2 ? qsA[g] : qsB[g], sv[e]);
         }
       }
-      const float ks0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + D) * a.kscale;
-      const float ks1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + D) * a.kscale;
+      const float ks0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * SREC + D) * a.kscale;
+      const float ks1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * SREC + D) * a.kscale;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float ks = (e & 1) ? ks1 : ks0;
@@ -566,8 +569,8 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       float psA = 0.f, psB = 0.f;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-        const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + 2 * D + 4) * kPScale;
-        const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + 2 * D + 4) * kPScale;
+        const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * SREC + 2 * D + 4) * kPScale;
+        const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * SREC + 2 * D + 4) * kPScale;
         float pv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -614,8 +617,8 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       float pmA = 0.f, pmB = 0.f;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-        const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * REC + 2 * D + 4);
-        const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * REC + 2 * D + 4);
+        const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * SREC + 2 * D + 4);
+        const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * SREC + 2 * D + 4);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float ex = fast_exp2(u[n][e]);

@@ -23,8 +23,8 @@
 using namespace lfm3a;
 
 // Split partials of lfm3a_verify_attention_static: one fixed array per device, loaded with the module, so that
-// entry point allocates nothing. 16 MiB holds m * q_heads * splits * 66 floats for, e.g., 16 tokens x 32 query
-// heads x 121 splits.
+// entry point allocates nothing. 16 MiB holds m * q_heads * splits * (head_dim + 2) floats for, e.g., 16 tokens x
+// 32 query heads x 121 splits at head_dim 64.
 static __device__ __align__(256) float g_verify_scratch[LFM3A_VERIFY_SCRATCH_BYTES / sizeof(float)];
 
 namespace {
@@ -540,7 +540,7 @@ int lfm3a_verify_attention_static(const lfm3a_kv_view* kv, const void* q, int m,
                             nullptr, scratch[dev], LFM3A_VERIFY_SCRATCH_BYTES, splits, as_stream(stream));
   if (rc == LFM3A_EWORKSPACE)
     return fail(rc, "verify partials exceed the " + std::to_string(LFM3A_VERIFY_SCRATCH_BYTES >> 20) +
-                        " MiB static scratch (m * q_heads * splits * 66 floats); pass fewer splits or call "
+                        " MiB static scratch (m * q_heads * splits * (head_dim + 2) floats); pass fewer splits or call "
                         "lfm3a_verify_attention with a workspace");
   return rc;
 }
