@@ -407,6 +407,20 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// acc rows A (fragment elements 0, 1) times cA and rows B (2, 3) times cB, two elements per instruction.
+template <int NJ>
+__device__ __forceinline__ void scale_acc(float (&acc)[NJ][4], float cA, float cB) {
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const float2 a = fmul2(make_float2(acc[j][0], acc[j][1]), make_float2(cA, cA));
+    const float2 b = fmul2(make_float2(acc[j][2], acc[j][3]), make_float2(cB, cB));
+    acc[j][0] = a.x;
+    acc[j][1] = a.y;
+    acc[j][2] = b.x;
+    acc[j][3] = b.y;
+  }
+}
+
 template <int D, bool EXACT>
 __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) {
   using SM = PfI8Smem<D>;
@@ -431,11 +445,17 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
   auto load = [&](int s) {   // tile s of the split into buffer s & 1; keys past the end read the last key's record
     const int k0 = kt_first + s * KT;
     uint8_t* dst = tiles[s & 1];
+    // The tile's 64 keys lie in two blocks of the table (k0 is a multiple of 64); a tile that ends inside the
+    // first one reads only that one.
+    const int blk0 = k0 / kBlockTokens;
+    const char* base0 = a.g.pool + phys_block(a.g, blk0) * a.g.block_bytes + (int64_t)h * REC;
+    const char* base1 = kend - 1 >= k0 + kBlockTokens ? a.g.pool + phys_block(a.g, blk0 + 1) * a.g.block_bytes +
+                                                            (int64_t)h * REC
+                                                      : base0;
     for (int c = threadIdx.x; c < KT * CH; c += blockDim.x) {
       const int kk = c / CH, off = (c - kk * CH) * 8;
       const int key = min(k0 + kk, kend - 1);
-      const char* src = a.g.pool + phys_block(a.g, key / kBlockTokens) * a.g.block_bytes +
-                        ((int64_t)(key % kBlockTokens) * H + h) * REC + off;
+      const char* src = (key / kBlockTokens == blk0 ? base0 : base1) + (int64_t)(key % kBlockTokens) * H * REC + off;
       cp_async8(dst + kk * SREC + off, src);
     }
     cp_async_commit();
@@ -507,25 +527,33 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const uint8_t* krec = tl + (8 * n + gid) * SREC;
-      float sv[4] = {EXACT ? 0.f : qcA, EXACT ? 0.f : qcA, EXACT ? 0.f : qcB, EXACT ? 0.f : qcB};
+      // The C fragment's pairs (e 0, 1: row A) and (e 2, 3: row B) go through packed fp32 arithmetic (one issued
+      // instruction per two scores, each lane rounded as the scalar form).
+      float2 svA = make_float2(EXACT ? 0.f : qcA, EXACT ? 0.f : qcA);
+      float2 svB = make_float2(EXACT ? 0.f : qcB, EXACT ? 0.f : qcB);
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
         int d4[4] = {MAGIC_I, MAGIC_I, MAGIC_I, MAGIC_I};
         const uint2 kb = *reinterpret_cast<const uint2*>(krec + 32 * g + 8 * tig);
         mma_s8_16832(d4, qa[g], kb.x, kb.y);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float d = EXACT ? __int_as_float(d4[e]) - MAGIC_F : __int_as_float(d4[e]);   // exact: float(dot)
-          sv[e] = fmaf(d, e < 2 ? qsA[g] : qsB[g], sv[e]);
+        float2 dA = make_float2(__int_as_float(d4[0]), __int_as_float(d4[1]));
+        float2 dB = make_float2(__int_as_float(d4[2]), __int_as_float(d4[3]));
+        if (EXACT) {   // float(dot)
+          dA = fadd2(dA, make_float2(-MAGIC_F, -MAGIC_F));
+          dB = fadd2(dB, make_float2(-MAGIC_F, -MAGIC_F));
         }
+        svA = ffma2(dA, make_float2(qsA[g], qsA[g]), svA);
+        svB = ffma2(dB, make_float2(qsB[g], qsB[g]), svB);
       }
       const float ks0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * SREC + D) * a.kscale;
       const float ks1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * SREC + D) * a.kscale;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float ks = (e & 1) ? ks1 : ks0;
-        u[n][e] = EXACT ? sv[e] * ks : fmaf(sv[e], ks, -(e < 2 ? mA : mB));
-      }
+      const float2 ks = make_float2(ks0, ks1);
+      const float2 uA = EXACT ? fmul2(svA, ks) : ffma2(svA, ks, make_float2(-mA, -mA));
+      const float2 uB = EXACT ? fmul2(svB, ks) : ffma2(svB, ks, make_float2(-mB, -mB));
+      u[n][0] = uA.x;
+      u[n][1] = uA.y;
+      u[n][2] = uB.x;
+      u[n][3] = uB.y;
     }
     const bool interior = k0 + KT - 1 <= qfirst && k0 >= kbegin && (a.window == 0 || k0 > qlast - a.window);
     if (!interior || !okB) {
@@ -559,13 +587,7 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       const float cA = mA == -INFINITY ? 0.f : fast_exp2(mA - mnA), cB = mB == -INFINITY ? 0.f : fast_exp2(mB - mnB);
       mA = mnA;
       mB = mnB;
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        acc[j][0] *= cA;
-        acc[j][1] *= cA;
-        acc[j][2] *= cB;
-        acc[j][3] *= cB;
-      }
+      scale_acc(acc, cA, cB);
       float psA = 0.f, psB = 0.f;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
@@ -579,8 +601,10 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
           if (e < 2) psA += pv[e];
           else psB += pv[e];
         }
-        pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(pv[0] * vs0, pv[1] * vs1);
-        pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(pv[2] * vs0, pv[3] * vs1);
+        const float2 vs = make_float2(vs0, vs1);
+        const float2 pA = fmul2(make_float2(pv[0], pv[1]), vs), pB = fmul2(make_float2(pv[2], pv[3]), vs);
+        pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(pA.x, pA.y);
+        pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(pB.x, pB.y);
       }
       lA = lA * cA + psA;
       lB = lB * cB + psB;
@@ -598,13 +622,7 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
         lB *= cB;
         bA *= cA;
         bB *= cB;
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          acc[j][0] *= cA;
-          acc[j][1] *= cA;
-          acc[j][2] *= cB;
-          acc[j][3] *= cB;
-        }
+        scale_acc(acc, cA, cB);
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           u[n][0] += dA;
@@ -619,13 +637,20 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       for (int n = 0; n < 8; ++n) {
         const float vs0 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig) * SREC + 2 * D + 4);
         const float vs1 = *reinterpret_cast<const float*>(tl + (8 * n + 2 * tig + 1) * SREC + 2 * D + 4);
+        float ex[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float ex = fast_exp2(u[n][e]);
-          if (e < 2) lA += ex;
-          else lB += ex;
-          u[n][e] = ex * ((e & 1) ? vs1 : vs0);   // u now holds P'
+          ex[e] = fast_exp2(u[n][e]);
+          if (e < 2) lA += ex[e];
+          else lB += ex[e];
         }
+        // u now holds P'
+        const float2 vs = make_float2(vs0, vs1);
+        const float2 pA = fmul2(make_float2(ex[0], ex[1]), vs), pB = fmul2(make_float2(ex[2], ex[3]), vs);
+        u[n][0] = pA.x;
+        u[n][1] = pA.y;
+        u[n][2] = pB.x;
+        u[n][3] = pB.y;
         pmA = fmaxf(pmA, fmaxf(u[n][0], u[n][1]));
         pmB = fmaxf(pmB, fmaxf(u[n][2], u[n][3]));
       }
@@ -637,30 +662,32 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       const float invA = 255.f * __frcp_rn(fmaxf(pmA, 1e-30f)), invB = 255.f * __frcp_rn(fmaxf(pmB, 1e-30f));
       scA = pmA * (1.f / 255.f);
       scB = pmB * (1.f / 255.f);
-      int qsumA = 0, qsumB = 0;
+      // q = rne(P' x 255 / max P'): P' <= max P' keeps the product at most 255 (1 + 3 2^-24), which rounds to 255,
+      // so the reference's saturation never binds. Adding 1.5 2^23 rounds to the nearest even integer and
+      // subtracting it again leaves that integer exactly; the per-thread sums of q (at most 32 x 255) are exact in
+      // fp32.
+      const float2 mag = make_float2(MAGIC_F, MAGIC_F), nmag = make_float2(-MAGIC_F, -MAGIC_F);
+      const float2 iA = make_float2(invA, invA), iB = make_float2(invB, invB);
+      float2 qsA2 = make_float2(0.f, 0.f), qsB2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-        float qv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x = fminf(u[n][e] * (e < 2 ? invA : invB), 255.f);
-          const int q = (int)(__float_as_uint(x + 12582912.f) & 0xffu);   // nearest even, in [0, 255]
-          qv[e] = (float)q;
-          if (e < 2) qsumA += q;
-          else qsumB += q;
-        }
-        pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(qv[0], qv[1]);
-        pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(qv[2], qv[3]);
+        const float2 qA = fadd2(fadd2(fmul2(make_float2(u[n][0], u[n][1]), iA), mag), nmag);
+        const float2 qB = fadd2(fadd2(fmul2(make_float2(u[n][2], u[n][3]), iB), mag), nmag);
+        qsA2 = fadd2(qsA2, qA);
+        qsB2 = fadd2(qsB2, qB);
+        pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(qA.x, qA.y);
+        pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(qB.x, qB.y);
       }
-      bA = fmaf((float)qsumA, 128.f * scA, bA);
-      bB = fmaf((float)qsumB, 128.f * scB, bB);
+      float qsumA = qsA2.x + qsA2.y, qsumB = qsB2.x + qsB2.y;
+      bA = fmaf(qsumA, 128.f * scA, bA);
+      bB = fmaf(qsumB, 128.f * scB, bB);
 #pragma unroll
       for (int o = 1; o <= 2; o <<= 1) {
         qsumA += __shfl_xor_sync(0xffffffffu, qsumA, o);
         qsumB += __shfl_xor_sync(0xffffffffu, qsumB, o);
       }
-      biasA = 128.f * (float)qsumA;   // the + 128 of every V byte
-      biasB = 128.f * (float)qsumB;
+      biasA = 128.f * qsumA;   // the + 128 of every V byte
+      biasB = 128.f * qsumB;
     }
     // ---- PV in passes of 32 dims (4 n-tiles of 8): B fragments by ldmatrix.trans from the fp16 V tile. Int8-PV:
     // dot = sum_k q_k v_k exactly, then acc = fma(dot + 128 sum q, sc, acc); exact: the fp16 P' x V into acc.
@@ -688,10 +715,14 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int jn = 4 * pass + j;
-          acc[jn][0] = fmaf(dot[j][0] + biasA, scA, acc[jn][0]);
-          acc[jn][1] = fmaf(dot[j][1] + biasA, scA, acc[jn][1]);
-          acc[jn][2] = fmaf(dot[j][2] + biasB, scB, acc[jn][2]);
-          acc[jn][3] = fmaf(dot[j][3] + biasB, scB, acc[jn][3]);
+          const float2 tA = fadd2(make_float2(dot[j][0], dot[j][1]), make_float2(biasA, biasA));
+          const float2 tB = fadd2(make_float2(dot[j][2], dot[j][3]), make_float2(biasB, biasB));
+          const float2 aA = ffma2(tA, make_float2(scA, scA), make_float2(acc[jn][0], acc[jn][1]));
+          const float2 aB = ffma2(tB, make_float2(scB, scB), make_float2(acc[jn][2], acc[jn][3]));
+          acc[jn][0] = aA.x;
+          acc[jn][1] = aA.y;
+          acc[jn][2] = aB.x;
+          acc[jn][3] = aB.y;
         }
       }
     }
