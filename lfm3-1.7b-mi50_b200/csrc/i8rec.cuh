@@ -98,6 +98,20 @@ __device__ __forceinline__ uint32_t s8pair_to_f16x2(uint32_t wk, uint32_t wk1, i
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// acc rows A (fragment elements 0, 1) times cA and rows B (2, 3) times cB, two elements per instruction.
+template <int NJ>
+__device__ __forceinline__ void scale_acc(float (&acc)[NJ][4], float cA, float cB) {
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const float2 a = fmul2(make_float2(acc[j][0], acc[j][1]), make_float2(cA, cA));
+    const float2 b = fmul2(make_float2(acc[j][2], acc[j][3]), make_float2(cB, cB));
+    acc[j][0] = a.x;
+    acc[j][1] = a.y;
+    acc[j][2] = b.x;
+    acc[j][3] = b.y;
+  }
+}
+
 // MAXW: the most warps the instantiation launches with, which sets the register cap (65536 / (32 MAXW)). At head_dim
 // 128 a thread holds 64 accumulators; the 12-warp instance (up to 12 tokens at 4 kv heads: the reference verifies
 // at most 9) gets 170 registers and does not spill, the 16-warp one serves 13-16 tokens at 128.
@@ -188,7 +202,10 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
       // fragment is (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1) of the n-tile. Each dot
       // accumulates onto the bits of 1.5 * 2^23 (|dot| <= 32 * 127 * 128 < 2^22): read as fp32 that is
       // 1.5 * 2^23 + dot exactly, so one FADD converts it (no I2F on the XU pipe).
-      float pair[NG / 2][4];
+      // The fragment's row pairs (e 0, 1: row A; e 2, 3: row B) go through packed fp32 arithmetic, each lane
+      // rounded as the scalar form.
+      const float2 nmag = make_float2(-12582912.f, -12582912.f);
+      float2 pairA[NG / 2], pairB[NG / 2];
 #pragma unroll
       for (int g2 = 0; g2 < NG / 2; ++g2) {
         int d0[4] = {0x4B400000, 0x4B400000, 0x4B400000, 0x4B400000};
@@ -197,20 +214,24 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
         const uint2 k1 = *reinterpret_cast<const uint2*>(krec + 64 * g2 + 32 + 8 * tig);
         mma_s8_16832(d0, qa[2 * g2], k0.x, k0.y);
         mma_s8_16832(d1, qa[2 * g2 + 1], k1.x, k1.y);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float* qs = e < 2 ? qsA : qsB;
-          const float f0 = __int_as_float(d0[e]) - 12582912.f, f1 = __int_as_float(d1[e]) - 12582912.f;
-          pair[g2][e] = fmaf(f1, qs[2 * g2 + 1], f0 * qs[2 * g2]);
-        }
+        const float2 fA0 = fadd2(make_float2(__int_as_float(d0[0]), __int_as_float(d0[1])), nmag);
+        const float2 fA1 = fadd2(make_float2(__int_as_float(d1[0]), __int_as_float(d1[1])), nmag);
+        const float2 fB0 = fadd2(make_float2(__int_as_float(d0[2]), __int_as_float(d0[3])), nmag);
+        const float2 fB1 = fadd2(make_float2(__int_as_float(d1[2]), __int_as_float(d1[3])), nmag);
+        pairA[g2] = ffma2(fA1, make_float2(qsA[2 * g2 + 1], qsA[2 * g2 + 1]),
+                          fmul2(fA0, make_float2(qsA[2 * g2], qsA[2 * g2])));
+        pairB[g2] = ffma2(fB1, make_float2(qsB[2 * g2 + 1], qsB[2 * g2 + 1]),
+                          fmul2(fB0, make_float2(qsB[2 * g2], qsB[2 * g2])));
       }
       const float ksc0 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig) * H + h) * REC + D);
       const float ksc1 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig + 1) * H + h) * REC + D);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float v = NG == 4 ? pair[0][e] + pair[NG / 2 - 1][e] : pair[0][e];
-        s[n][e] = v * ((e & 1) ? ksc1 : ksc0);
-      }
+      const float2 ks = make_float2(ksc0, ksc1);
+      const float2 sA = fmul2(NG == 4 ? fadd2(pairA[0], pairA[NG / 2 - 1]) : pairA[0], ks);
+      const float2 sB = fmul2(NG == 4 ? fadd2(pairB[0], pairB[NG / 2 - 1]) : pairB[0], ks);
+      s[n][0] = sA.x;
+      s[n][1] = sA.y;
+      s[n][2] = sB.x;
+      s[n][3] = sB.y;
     }
     // ---- masks (edge pages only) and the page maximum of each row
     const bool interior = k0 >= a.start && k0 + kBlockTokens <= a.ctx_len && (a.window == 0 || k0 > qlast - a.window);
@@ -246,13 +267,7 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
       mB = nB;
       lA *= cA;
       lB *= cB;
-#pragma unroll
-      for (int jn = 0; jn < NJ; ++jn) {
-        acc[jn][0] *= cA;
-        acc[jn][1] *= cA;
-        acc[jn][2] *= cB;
-        acc[jn][3] *= cB;
-      }
+      scale_acc(acc, cA, cB);
     }
     // ---- P = fp16(p (vs 4096)) as the A fragments of two 16-key k-steps
     uint32_t pf[2][4];
@@ -266,8 +281,10 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
       lA += p0 + p1;
       lB += p2 + p3;
       // n-tiles 2 kk and 2 kk + 1 are k-step kk: a0/a1 from the first, a2/a3 from the second
-      pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(p0 * vs0, p1 * vs1);
-      pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(p2 * vs0, p3 * vs1);
+      const float2 vs = make_float2(vs0, vs1);
+      const float2 PA = fmul2(make_float2(p0, p1), vs), PB = fmul2(make_float2(p2, p3), vs);
+      pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(PA.x, PA.y);
+      pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(PB.x, PB.y);
     }
     // ---- PV: per k-step, the V bytes of keys 16 kk + 2 tig (+1, +8, +9) at dims [NJ gid, NJ gid + NJ)
 #pragma unroll
@@ -405,20 +422,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// acc rows A (fragment elements 0, 1) times cA and rows B (2, 3) times cB, two elements per instruction.
-template <int NJ>
-__device__ __forceinline__ void scale_acc(float (&acc)[NJ][4], float cA, float cB) {
-#pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    const float2 a = fmul2(make_float2(acc[j][0], acc[j][1]), make_float2(cA, cA));
-    const float2 b = fmul2(make_float2(acc[j][2], acc[j][3]), make_float2(cB, cB));
-    acc[j][0] = a.x;
-    acc[j][1] = a.y;
-    acc[j][2] = b.x;
-    acc[j][3] = b.y;
-  }
 }
 
 template <int D, bool EXACT>
