@@ -16,8 +16,10 @@
 //       NN = v + 128 are 1152 + v; one subtraction);
 //   partial acc / 4096, max, sum per (row, split) (:2100-2120).
 // Within a 32-dim group the order of the dims is free (the dot is exact), so each thread reads 8 contiguous dims
-// of a key; the output dims are permuted the same way for V (thread column c of n-tile j holds dim (D / 8) c + j)
-// and put back in order when the partial is written.
+// of a key. Within a 16-key k-step the order of the keys is free too (QK's columns and PV's rows follow the same
+// map, verify_key_of), and the output dims are permuted for V (column c of n-tile j holds dim
+// 4 c + 32 (j / 4) + j % 4, put back in order when the partial is written): with both, the 4-byte V loads of a
+// warp and its key-scale loads fall in distinct shared-memory banks (a page's records sit 8 mod 32 words apart).
 #pragma once
 #include "common.cuh"
 #include "kv.cuh"
@@ -112,6 +114,15 @@ __device__ __forceinline__ void scale_acc(float (&acc)[NJ][4], float cA, float c
   }
 }
 
+// Key (0..15) of a 16-key k-step behind k-row r = 8 c + 2 t + b of the PV (and behind column r of QK n-tile
+// 2 kk + c): ((t + 2 b) mod 4) + 4 (2 c + b). For each (b, c) the four t get keys of distinct residues mod 4, which
+// spreads the PV's V loads (rows 2 tig + b + 8 c) over the banks; QK's columns 0..3 (and 4..7) also get distinct
+// residues, so its 8-byte K loads stay conflict-free. A bijection on 0..15.
+__device__ __forceinline__ int verify_key_of(int r) {
+  const int t = (r >> 1) & 3, b = r & 1, c = r >> 3;
+  return ((t + 2 * b) & 3) + 4 * (2 * c + b);
+}
+
 // MAXW: the most warps the instantiation launches with, which sets the register cap (65536 / (32 MAXW)). At head_dim
 // 128 a thread holds 64 accumulators; the 12-warp instance (up to 12 tokens at 4 kv heads: the reference verifies
 // at most 9) gets 170 registers and does not spill, the 16-warp one serves 13-16 tokens at 128.
@@ -197,7 +208,9 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
     float s[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
-      const uint8_t* krec = page + ((8 * n + gid) * H + h) * REC;   // key 8 n + gid of this kv head
+      // Column col of n-tile n is key 16 (n / 2) + verify_key_of(8 (n % 2) + col) of the page.
+      const int kn = 16 * (n >> 1), cn = 8 * (n & 1);
+      const uint8_t* krec = page + ((kn + verify_key_of(cn + gid)) * H + h) * REC;
       // Groups in pairs, each pair folded as soon as its two dots are out (fewer registers live): the C
       // fragment is (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1) of the n-tile. Each dot
       // accumulates onto the bits of 1.5 * 2^23 (|dot| <= 32 * 127 * 128 < 2^22): read as fp32 that is
@@ -223,8 +236,9 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
         pairB[g2] = ffma2(fB1, make_float2(qsB[2 * g2 + 1], qsB[2 * g2 + 1]),
                           fmul2(fB0, make_float2(qsB[2 * g2], qsB[2 * g2])));
       }
-      const float ksc0 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig) * H + h) * REC + D);
-      const float ksc1 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig + 1) * H + h) * REC + D);
+      const float ksc0 = *reinterpret_cast<const float*>(page + ((kn + verify_key_of(cn + 2 * tig)) * H + h) * REC + D);
+      const float ksc1 =
+          *reinterpret_cast<const float*>(page + ((kn + verify_key_of(cn + 2 * tig + 1)) * H + h) * REC + D);
       const float2 ks = make_float2(ksc0, ksc1);
       const float2 sA = fmul2(NG == 4 ? fadd2(pairA[0], pairA[NG / 2 - 1]) : pairA[0], ks);
       const float2 sB = fmul2(NG == 4 ? fadd2(pairB[0], pairB[NG / 2 - 1]) : pairB[0], ks);
@@ -240,7 +254,7 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
       for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int kpos = k0 + 8 * n + 2 * tig + (e & 1);
+          const int kpos = k0 + 16 * (n >> 1) + verify_key_of(8 * (n & 1) + 2 * tig + (e & 1));
           const int qpos = e < 2 ? qposA : qposB;
           const bool rok = e < 2 ? okA : okB;
           bool valid;
@@ -273,9 +287,13 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
     uint32_t pf[2][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
-      const float vs0 = *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig) * H + h) * REC + 2 * D + 4) * kPScale;
+      const int kn = 16 * (n >> 1), cn = 8 * (n & 1);
+      const float vs0 =
+          *reinterpret_cast<const float*>(page + ((kn + verify_key_of(cn + 2 * tig)) * H + h) * REC + 2 * D + 4) *
+          kPScale;
       const float vs1 =
-          *reinterpret_cast<const float*>(page + ((8 * n + 2 * tig + 1) * H + h) * REC + 2 * D + 4) * kPScale;
+          *reinterpret_cast<const float*>(page + ((kn + verify_key_of(cn + 2 * tig + 1)) * H + h) * REC + 2 * D + 4) *
+          kPScale;
       const float p0 = fast_exp2(s[n][0] - mA), p1 = fast_exp2(s[n][1] - mA);
       const float p2 = fast_exp2(s[n][2] - mB), p3 = fast_exp2(s[n][3] - mB);
       lA += p0 + p1;
@@ -286,21 +304,24 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
       pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(PA.x, PA.y);
       pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(PB.x, PB.y);
     }
-    // ---- PV: per k-step, the V bytes of keys 16 kk + 2 tig (+1, +8, +9) at dims [NJ gid, NJ gid + NJ)
+    // ---- PV: per k-step, the V bytes of the keys behind k-rows 2 tig (+1, +8, +9); word w of column gid holds
+    // dims 4 gid + 32 w .. + 3
 #pragma unroll
     for (int kk = 0; kk < 2; ++kk) {
-      const int kb = 16 * kk + 2 * tig;
-      const uint8_t* v0 = page + ((kb + 0) * H + h) * REC + D + 4 + NJ * gid;
-      const uint8_t* v1 = page + ((kb + 1) * H + h) * REC + D + 4 + NJ * gid;
-      const uint8_t* v8 = page + ((kb + 8) * H + h) * REC + D + 4 + NJ * gid;
-      const uint8_t* v9 = page + ((kb + 9) * H + h) * REC + D + 4 + NJ * gid;
+      const uint8_t* vrow = page + h * REC + D + 4 + 4 * gid;
+      const uint8_t* v0 = vrow + (16 * kk + verify_key_of(2 * tig)) * H * REC;
+      const uint8_t* v1 = vrow + (16 * kk + verify_key_of(2 * tig + 1)) * H * REC;
+      const uint8_t* v8 = vrow + (16 * kk + verify_key_of(2 * tig + 8)) * H * REC;
+      const uint8_t* v9 = vrow + (16 * kk + verify_key_of(2 * tig + 9)) * H * REC;
 #pragma unroll
       for (int w = 0; w < NJ / 4; ++w) {
-        const uint32_t w0 = reinterpret_cast<const uint32_t*>(v0)[w], w1 = reinterpret_cast<const uint32_t*>(v1)[w];
-        const uint32_t w8 = reinterpret_cast<const uint32_t*>(v8)[w], w9 = reinterpret_cast<const uint32_t*>(v9)[w];
+        const uint32_t w0 = reinterpret_cast<const uint32_t*>(v0)[8 * w];
+        const uint32_t w1 = reinterpret_cast<const uint32_t*>(v1)[8 * w];
+        const uint32_t w8 = reinterpret_cast<const uint32_t*>(v8)[8 * w];
+        const uint32_t w9 = reinterpret_cast<const uint32_t*>(v9)[8 * w];
 #pragma unroll
         for (int by = 0; by < 4; ++by) {
-          const int jn = 4 * w + by;   // n-tile: its column gid holds dim NJ gid + jn
+          const int jn = 4 * w + by;   // n-tile: its column gid holds dim 4 gid + 32 w + by
           mma_f16_16816(acc[jn], pf[kk], s8pair_to_f16x2(w0, w1, by), s8pair_to_f16x2(w8, w9, by));
         }
       }
@@ -339,13 +360,15 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
       const bool rok = half ? okB : okA;
       if (!rok) continue;
       float* dst = a.part + ((int64_t)(half ? rowB : rowA) * a.splits + split) * (D + 2);
-      // C fragment columns 2 tig, 2 tig + 1 of n-tile jn hold dims NJ (2 tig) + jn and NJ (2 tig + 1) + jn: the
-      // thread's 2 NJ dims of the row are contiguous, stored in 8-byte pairs (a row starts 8-byte aligned).
+      // C fragment columns 2 tig, 2 tig + 1 of n-tile jn = 4 w + by hold dims 8 tig + 32 w + by and
+      // 8 tig + 4 + 32 w + by: per w the thread's 8 dims of the row are contiguous, stored in 8-byte pairs (a row
+      // starts 8-byte aligned).
 #pragma unroll
       for (int jn = 0; jn < NJ; jn += 2) {
-        *reinterpret_cast<float2*>(dst + NJ * (2 * tig) + jn) =
+        const int dim = 8 * tig + 32 * (jn >> 2) + (jn & 3);
+        *reinterpret_cast<float2*>(dst + dim) =
             make_float2(acc[jn][2 * half] * (1.f / kPScale), acc[jn + 1][2 * half] * (1.f / kPScale));
-        *reinterpret_cast<float2*>(dst + NJ * (2 * tig + 1) + jn) =
+        *reinterpret_cast<float2*>(dst + dim + 4) =
             make_float2(acc[jn][2 * half + 1] * (1.f / kPScale), acc[jn + 1][2 * half + 1] * (1.f / kPScale));
       }
       if (tig == 0) {
