@@ -83,6 +83,13 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4]
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// u8 A (P) x s8 B (V) -> s32, k = 32.
+__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -534,8 +541,38 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
     __syncthreads();
     const uint8_t* tl = tiles[s & 1];
     const int k0 = kt_first + s * KT;
-    // The tile's V made fp16 once (the previous tile's PV is done: the barrier that ended it): a word of four
-    // int8 dims per step, 0x64NN - 1152 with NN = v + 128 giving v exactly.
+    // The tile's V, once per CTA (the previous tile's PV is done: the barrier that ended it).
+    if constexpr (!EXACT) {
+      // Int8-PV: V stays int8, transposed to [dim][64 keys] so that a u8 x s8 MMA's B fragment (four keys at one
+      // dim) is one word. The keys of a 32-key k-step sit in the order the thread's P bytes come in: position
+      // 16 t + 8 h + 4 ks + j of a dim's 64-byte row holds key 32 ks + 16 h + 8 (j / 2) + 2 t + j % 2 (the C
+      // fragment's keys 2 t, 2 t + 1 of n-tiles 4 ks + 2 h + j / 2). The row's four 16-byte chunks (one per t) are
+      // swizzled by (dim / 4) % 4 and the four words of a chunk (one per (h, ks)) by (dim / 16) % 4, so that the
+      // transposing stores of a warp spread over the banks; the reads stay one conflict-free 16-byte load per
+      // n-tile, whose word order is known at compile time.
+      uint8_t* vt = pf_smem + SM::kOffV;
+      if (threadIdx.x < 8 * (D / 4)) {
+        const int w = threadIdx.x % (D / 4), th = threadIdx.x / (D / 4), t = th & 3, hh = th >> 2;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint8_t* r0 = tl + (32 * ks + 16 * hh + 2 * t) * SREC + D + 4 + 4 * w;
+          const uint32_t k0 = *reinterpret_cast<const uint32_t*>(r0);
+          const uint32_t k1 = *reinterpret_cast<const uint32_t*>(r0 + SREC);
+          const uint32_t k2 = *reinterpret_cast<const uint32_t*>(r0 + 8 * SREC);
+          const uint32_t k3 = *reinterpret_cast<const uint32_t*>(r0 + 9 * SREC);
+          const uint32_t lo01 = __byte_perm(k0, k1, 0x5140u), hi01 = __byte_perm(k0, k1, 0x7362u);
+          const uint32_t lo23 = __byte_perm(k2, k3, 0x5140u), hi23 = __byte_perm(k2, k3, 0x7362u);
+          const uint32_t o[4] = {__byte_perm(lo01, lo23, 0x5410u), __byte_perm(lo01, lo23, 0x7632u),
+                                 __byte_perm(hi01, hi23, 0x5410u), __byte_perm(hi01, hi23, 0x7632u)};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int dim = 4 * w + i, chunk = t ^ ((dim >> 2) & 3), word = (2 * hh + ks) ^ ((dim >> 4) & 3);
+            *reinterpret_cast<uint32_t*>(vt + dim * 64 + 16 * chunk + 4 * word) = o[i];
+          }
+        }
+      }
+    } else {
+    // Exact: made fp16, a word of four int8 dims per step, 0x64NN - 1152 with NN = v + 128 giving v exactly.
     for (int idx = threadIdx.x; idx < KT * (D / 4); idx += blockDim.x) {
       const int key = idx / (D / 4), w = idx - key * (D / 4);
       const uint32_t x = *reinterpret_cast<const uint32_t*>(tl + key * SREC + D + 4 + 4 * w) ^ 0x80808080u;
@@ -546,6 +583,7 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       hi = __hsub2(hi, __floats2half2_rn(1152.f, 1152.f));
       *reinterpret_cast<uint2*>(vh + key * SM::kVRow + 4 * w) =
           make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    }
     }
     __syncthreads();
     // ---- QK: 8 n-tiles of 8 keys; C fragment (rA, key 2 tig), (rA, 2 tig + 1), (rB, 2 tig), (rB, 2 tig + 1)
@@ -605,7 +643,8 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       tA_ = fmaxf(tA_, __shfl_xor_sync(0xffffffffu, tA_, o));
       tB_ = fmaxf(tB_, __shfl_xor_sync(0xffffffffu, tB_, o));
     }
-    uint32_t pf[4][4];   // P as fp16 A fragments of the four 16-key k-steps
+    uint32_t pf[4][4];   // exact: P as fp16 A fragments of the four 16-key k-steps
+    uint32_t p8[2][4];   // int8-PV: q as u8 A fragments of the two 32-key k-steps
     float scA = 0.f, scB = 0.f, biasA = 0.f, biasB = 0.f;
     if constexpr (EXACT) {
       // ---- exact running max; P' = fp16(p v_scale 4096)
@@ -689,22 +728,30 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       scA = pmA * (1.f / 255.f);
       scB = pmB * (1.f / 255.f);
       // q = rne(P' x 255 / max P'): P' <= max P' keeps the product at most 255 (1 + 3 2^-24), which rounds to 255,
-      // so the reference's saturation never binds. Adding 1.5 2^23 rounds to the nearest even integer and
-      // subtracting it again leaves that integer exactly; the per-thread sums of q (at most 32 x 255) are exact in
-      // fp32.
-      const float2 mag = make_float2(MAGIC_F, MAGIC_F), nmag = make_float2(-MAGIC_F, -MAGIC_F);
+      // so the reference's saturation never binds. Adding 1.5 2^23 rounds to the nearest even integer, which is
+      // then the low byte of the sum's bits. A fragment word: the bytes of n-tiles 2 i, 2 i + 1 (keys 2 tig,
+      // 2 tig + 1 of each), the order the transposed V tile keeps its keys in.
+      const float2 mag = make_float2(MAGIC_F, MAGIC_F);
       const float2 iA = make_float2(invA, invA), iB = make_float2(invB, invB);
-      float2 qsA2 = make_float2(0.f, 0.f), qsB2 = make_float2(0.f, 0.f);
+      uint32_t pkA[8], pkB[8];
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-        const float2 qA = fadd2(fadd2(fmul2(make_float2(u[n][0], u[n][1]), iA), mag), nmag);
-        const float2 qB = fadd2(fadd2(fmul2(make_float2(u[n][2], u[n][3]), iB), mag), nmag);
-        qsA2 = fadd2(qsA2, qA);
-        qsB2 = fadd2(qsB2, qB);
-        pf[n >> 1][(n & 1) * 2 + 0] = pack_half2(qA.x, qA.y);
-        pf[n >> 1][(n & 1) * 2 + 1] = pack_half2(qB.x, qB.y);
+        const float2 rA = fadd2(fmul2(make_float2(u[n][0], u[n][1]), iA), mag);
+        const float2 rB = fadd2(fmul2(make_float2(u[n][2], u[n][3]), iB), mag);
+        pkA[n] = __byte_perm(__float_as_uint(rA.x), __float_as_uint(rA.y), 0x0040u);
+        pkB[n] = __byte_perm(__float_as_uint(rB.x), __float_as_uint(rB.y), 0x0040u);
       }
-      float qsumA = qsA2.x + qsA2.y, qsumB = qsB2.x + qsB2.y;
+      unsigned qiA = 0u, qiB = 0u;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        p8[ks][0] = __byte_perm(pkA[4 * ks], pkA[4 * ks + 1], 0x5410u);
+        p8[ks][1] = __byte_perm(pkB[4 * ks], pkB[4 * ks + 1], 0x5410u);
+        p8[ks][2] = __byte_perm(pkA[4 * ks + 2], pkA[4 * ks + 3], 0x5410u);
+        p8[ks][3] = __byte_perm(pkB[4 * ks + 2], pkB[4 * ks + 3], 0x5410u);
+        qiA = __dp4a(p8[ks][0], 0x01010101u, __dp4a(p8[ks][2], 0x01010101u, qiA));
+        qiB = __dp4a(p8[ks][1], 0x01010101u, __dp4a(p8[ks][3], 0x01010101u, qiB));
+      }
+      float qsumA = (float)qiA, qsumB = (float)qiB;   // at most 32 x 255: exact
       bA = fmaf(qsumA, 128.f * scA, bA);
       bB = fmaf(qsumB, 128.f * scB, bB);
 #pragma unroll
@@ -715,17 +762,40 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
       biasA = 128.f * qsumA;   // the + 128 of every V byte
       biasB = 128.f * qsumB;
     }
-    // ---- PV in passes of 32 dims (4 n-tiles of 8): B fragments by ldmatrix.trans from the fp16 V tile. Int8-PV:
-    // dot = sum_k q_k v_k exactly, then acc = fma(dot + 128 sum q, sc, acc); exact: the fp16 P' x V into acc.
+    if constexpr (!EXACT) {
+      // ---- PV: per n-tile (dims 8 jn .. 8 jn + 7) one 16-byte load of the transposed tile gives the B words of
+      // both k-steps; dot = sum_k q_k v_k exactly in s32, accumulated onto the bits of 1.5 2^23 (|dot| <=
+      // 64 x 255 x 128 < 2^22), so (bits as fp32) + (128 sum q - 1.5 2^23) is dot + 128 sum q exactly; then
+      // acc = fma(that, sc, acc).
+      const uint8_t* vt = pf_smem + SM::kOffV;
+      const float2 bbA = make_float2(biasA - MAGIC_F, biasA - MAGIC_F), bbB = make_float2(biasB - MAGIC_F, biasB - MAGIC_F);
+#pragma unroll
+      for (int jn = 0; jn < NJ; ++jn) {
+        const int dim = 8 * jn + gid;
+        const uint4 bw = *reinterpret_cast<const uint4*>(vt + dim * 64 + 16 * (tig ^ ((dim >> 2) & 3)));
+        const uint32_t wv[4] = {bw.x, bw.y, bw.z, bw.w};
+        const int xs = (jn >> 1) & 3;   // (dim / 16) % 4: the chunk's word order
+        int d[4] = {MAGIC_I, MAGIC_I, MAGIC_I, MAGIC_I};
+        mma_u8s8_16832(d, p8[0], wv[0 ^ xs], wv[2 ^ xs]);   // k-step 0: b0 (h 0), b1 (h 1)
+        mma_u8s8_16832(d, p8[1], wv[1 ^ xs], wv[3 ^ xs]);   // k-step 1
+        const float2 tA = fadd2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), bbA);
+        const float2 tB = fadd2(make_float2(__int_as_float(d[2]), __int_as_float(d[3])), bbB);
+        const float2 aA = ffma2(tA, make_float2(scA, scA), make_float2(acc[jn][0], acc[jn][1]));
+        const float2 aB = ffma2(tB, make_float2(scB, scB), make_float2(acc[jn][2], acc[jn][3]));
+        acc[jn][0] = aA.x;
+        acc[jn][1] = aA.y;
+        acc[jn][2] = aB.x;
+        acc[jn][3] = aB.y;
+      }
+    } else {
+    // ---- PV in passes of 32 dims (4 n-tiles of 8): B fragments by ldmatrix.trans from the fp16 V tile: the fp16
+    // P' x V into acc.
     constexpr int NP = NJ / 4;
     // lane L addresses row L % 8 of matrix L / 8: keys + 8 (L / 8 & 1), dims + 8 (L / 16)
     const uint32_t v_base = smem_u32(vh) + (uint32_t)(((lane & 7) + 8 * ((lane >> 3) & 1)) * SM::kVRow * 2 +
                                                       8 * (lane >> 4) * 2);
 #pragma unroll
     for (int pass = 0; pass < NP; ++pass) {
-      float dot[4][4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) dot[j][0] = dot[j][1] = dot[j][2] = dot[j][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
@@ -733,24 +803,11 @@ __global__ __launch_bounds__(256, 1) void prefill_i8rec_kernel(PrefillI8Args a) 
           uint32_t b00, b01, b10, b11;
           ldsm_x4_trans(v_base + (uint32_t)((16 * kk) * SM::kVRow * 2 + (32 * pass + 16 * jp) * 2), b00, b01, b10, b11);
           const int j0 = 2 * jp;
-          mma_f16_16816(EXACT ? acc[4 * pass + j0] : dot[j0], pf[kk], b00, b01);
-          mma_f16_16816(EXACT ? acc[4 * pass + j0 + 1] : dot[j0 + 1], pf[kk], b10, b11);
+          mma_f16_16816(acc[4 * pass + j0], pf[kk], b00, b01);
+          mma_f16_16816(acc[4 * pass + j0 + 1], pf[kk], b10, b11);
         }
       }
-      if constexpr (!EXACT) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int jn = 4 * pass + j;
-          const float2 tA = fadd2(make_float2(dot[j][0], dot[j][1]), make_float2(biasA, biasA));
-          const float2 tB = fadd2(make_float2(dot[j][2], dot[j][3]), make_float2(biasB, biasB));
-          const float2 aA = ffma2(tA, make_float2(scA, scA), make_float2(acc[jn][0], acc[jn][1]));
-          const float2 aB = ffma2(tB, make_float2(scB, scB), make_float2(acc[jn][2], acc[jn][3]));
-          acc[jn][0] = aA.x;
-          acc[jn][1] = aA.y;
-          acc[jn][2] = aB.x;
-          acc[jn][3] = aB.y;
-        }
-      }
+    }
     }
     __syncthreads();   // every warp is done with this buffer before the copy of tile s + 2 lands in it
   }
