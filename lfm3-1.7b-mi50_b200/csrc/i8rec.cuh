@@ -406,15 +406,15 @@ __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args
 //   the lazy running max (m from 0; on the split's first tile, or when a row's u passes 8) (:274-297);
 //   e = 2^u, P' = e v_scale, l += e, P' to u8 against the row's largest P' of the tile (round to nearest
 //       even, saturated), bias += sum(q) 128 sc with sc = max P' / 255 (:298-317);
-//   PV  the exact sum_k q_k v_k from mma.m16n8k16 on fp16 (u8 and int8 are exact there, the fp32 sums of
-//       products stay below 2^24), plus 128 sum(q): the reference's u8 x (v + 128) dot, then
-//       acc = fma(that, sc, acc) (:320-350). The tile's V is made fp16 once, by the whole CTA, into a key-major
-//       shared tile, and the MMAs' B fragments come from it by ldmatrix.trans;
+//   PV  the exact sum_k q_k v_k from mma.m16n8k32 u8 x s8 -> s32, plus 128 sum(q): the reference's u8 x (v + 128)
+//       dot, then acc = fma(that, sc, acc) (:320-350). The tile's int8 V is transposed once, by the whole CTA,
+//       into a dim-major shared tile whose words are the MMAs' B operands;
 //   the split's partial: acc - bias, m (-inf without tiles), l, merged by the combine kernel (:489-505).
 // EXACT: the --exact-attention kernel over the same bytes (prefill_attn_exact.hip:173-344): s = sum_g float(dot_g) qs_g
 // from 0, times k_scale (1 / sqrt(D)) log2 e; an exact running max per tile (corr = 2^(m - mn), l = l corr + sum p);
-// P' = fp16(p v_scale 4096) times V's int8 made fp16, accumulated in fp32 by the MMAs across tiles (no per-tile fold);
-// the partial acc / 4096, m, l.
+// P' = fp16(p v_scale 4096) times V's int8 made fp16 (once per tile, by the whole CTA, into a key-major shared tile
+// read by ldmatrix.trans), accumulated in fp32 by mma.m16n8k16 across tiles (no per-tile fold); the partial
+// acc / 4096, m, l.
 struct PrefillI8Args {
   KvGeom g;
   const uint32_t* qbuf;   // [tokens * q_heads][D / 4 + D / 32] (quantize_q rows)
