@@ -131,8 +131,9 @@ __device__ __forceinline__ int verify_key_of(int r) {
 }
 
 // MAXW: the most warps the instantiation launches with, which sets the register cap (65536 / (32 MAXW)). At head_dim
-// 128 a thread holds 64 accumulators; the 12-warp instance (up to 12 tokens at 4 kv heads: the reference verifies
-// at most 9) gets 170 registers and does not spill, the 16-warp one serves 13-16 tokens at 128.
+// 128 a thread holds 64 accumulators; the 8-warp instance (up to 8 tokens at 4 kv heads) may use 255 registers
+// (it takes 180, and the extra room over the 12-warp cap of 170 buys the scheduler more loads and MMAs in flight),
+// the 12-warp one (9-12 tokens: the reference verifies at most 9) does not spill, the 16-warp one serves 13-16.
 template <int D, int MAXW>
 __global__ __launch_bounds__(32 * MAXW, 1) void verify_i8rec_kernel(VerifyI8Args a) {
   constexpr int REC = 2 * D + 8, NG = D / 32, NJ = D / 8;   // record bytes, 32-dim groups, output n-tiles

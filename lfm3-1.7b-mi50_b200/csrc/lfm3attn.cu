@@ -858,12 +858,16 @@ int lfm3a_verify_attention_i8(const lfm3a_kv_view* kv, const uint32_t* qbuf, int
     return fail(LFM3A_EWORKSPACE, "verify workspace too small");
   a.part = static_cast<float*>(workspace);
   const size_t smem = (size_t)stages * page_bytes + 256;
-  static std::atomic<bool> done[3][64];
+  static std::atomic<bool> done[4][64];
   const cudaStream_t st = as_stream(stream);
   // The limit is set once, to the most any geometry's ring asks for (220 KiB and the barriers).
   constexpr int kRingLimit = 220 * 1024 + 256;
   const int threads = 32 * H * mtiles;
-  if (D == 128 && H * mtiles <= 12) {
+  if (D == 128 && H * mtiles <= 8) {
+    rc = ensure_smem(verify_i8rec_kernel<128, 8>, kRingLimit, done[3]);
+    if (rc != LFM3A_OK) return rc;
+    launch_pdl(verify_i8rec_kernel<128, 8>, a.splits, threads, smem, st, a);
+  } else if (D == 128 && H * mtiles <= 12) {
     rc = ensure_smem(verify_i8rec_kernel<128, 12>, kRingLimit, done[2]);
     if (rc != LFM3A_OK) return rc;
     launch_pdl(verify_i8rec_kernel<128, 12>, a.splits, threads, smem, st, a);
